@@ -1,0 +1,203 @@
+/*
+ * zilla_b200.h -- C-ABI of libzilla_b200.so, the B200 (sm_100a) backend for
+ * ZillaPHP's training hot path.
+ *
+ * Part 1 declares, with byte-identical signatures, every function that
+ * ZillaPHP's CudaBackend binds through PHP FFI
+ * (src/Hardware/CUDA/CudaBackend.php:51-95), so an FFI::cdef of that block
+ * resolves against this library unchanged.  Part 2 adds entry points the
+ * reference does not have (Adam, the fused training step, the data-parallel
+ * runner, error reporting); they are additive and the reference's cdef
+ * block does not need them.
+ *
+ * Conventions (kept from the reference):
+ *   - Device memory lives in a handle registry (native/cuda/buffer_registry.cu:
+ *     20-128): slots 1..8191, lowest free slot reused, 4-byte elements.
+ *     Argmax indices (int32) and class targets (float-coded) share the
+ *     float buffer type, as native/cuda/pooling_batched.cu:69 and
+ *     native/cuda/training_ops.cu:7-9 do.
+ *   - int-returning functions return 0 on success, -1 on an invalid handle,
+ *     failed allocation or upload/download beyond capacity (as the reference),
+ *     -2 on invalid sizes/arguments, -3 when a CUDA launch or call failed
+ *     (the reference never reports launch failures; this library does).
+ *   - All *_dev work is enqueued on one library stream per device; upload and
+ *     download are synchronous with respect to it, so a download returns
+ *     finished data (native/cuda/buffer_registry.cu:88,107).
+ *   - Single-threaded caller (PHP); the registry is not thread-safe.
+ */
+#ifndef ZILLA_B200_H
+#define ZILLA_B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ===================================================================== *
+ * Part 1 -- the reference's CUDA C-ABI
+ * ===================================================================== */
+
+/* ---- host-pointer helpers (PCIe round trip per call) ---- */
+/* native/cuda/matmul.cu:93-144: C[M,N] = A[M,K] @ B[K,N], row-major host arrays. */
+void matmul_f32(const float *A, const float *B, float *C, int M, int K, int N);
+/* native/cuda/elementwise.cu:71-148: elementwise ops on host arrays. */
+void relu_f32_cuda(const float *X, float *Y, int N);
+void add_f32_cuda(const float *A, const float *B, float *C, int N);
+void sub_f32_cuda(const float *A, const float *B, float *C, int N);
+void mul_f32_cuda(const float *A, const float *B, float *C, int N);
+void div_f32_cuda(const float *A, const float *B, float *C, int N);
+/* native/cuda/audio.cu:31-39: periodic-free Hann window 0.5-0.5cos(2 pi i/(N-1)). */
+void hann_window_cuda(float *w, int N);
+/* native/cuda/audio.cu:125-188: |rFFT| of Hann-windowed frames, output [nBins, nFrames].
+ * Audio preprocessing, off the training path; kept so the reference's cdef resolves. */
+void stft_magnitude_cuda(const float *input, int inputLen, const float *window, int fftSize,
+                         int hopSize, float *output, int *outNBins, int *outNFrames);
+
+/* ---- persistent buffer registry: native/cuda/buffer_registry.cu:39-128 ---- */
+int zilla_buffer_alloc(unsigned long n_floats);
+void zilla_buffer_free(int id);
+int zilla_buffer_upload(int id, const float *host, unsigned long n_floats);
+int zilla_buffer_download(int id, float *host, unsigned long n_floats);
+void zilla_sync(void);
+float *zilla_buffer_ptr(int id);
+
+/* ---- device ops: native/cuda/device_ops.cu:44-149 ---- */
+int matmul_dev(int a_id, int b_id, int c_id, int M, int K, int N);   /* C = A @ B */
+int add_dev(int a_id, int b_id, int c_id, int n);
+int sub_dev(int a_id, int b_id, int c_id, int n);
+int mul_dev(int a_id, int b_id, int c_id, int n);
+int div_dev(int a_id, int b_id, int c_id, int n);
+int relu_dev(int x_id, int y_id, int n);
+
+/* ---- training ops: native/cuda/training_ops.cu:42-288 ---- */
+int add_bias_dev(int x_id, int b_id, int B, int C);                 /* :42-56   X[i,c] += b[c] */
+int relu_fwd_dev(int x_id, int y_id, int mask_id, int n);           /* :62-78   y, float mask */
+int relu_bwd_dev(int dy_id, int mask_id, int dx_id, int n);         /* :84-98   dx = dy*mask */
+int softmax_ce_dev(int logits_id, int targets_id, int dlogits_id,   /* :110-163 loss += sum -log p_t */
+                   int loss_id, int B, int C);                      /*          dZ = (p-onehot)/B  */
+int bias_grad_dev(int dy_id, int db_id, int B, int C);              /* :169-184 db = column sums  */
+int sgd_update_dev(int w_id, int dw_id, float lr, int n);           /* :190-203 W -= lr dW        */
+int zero_dev(int id, int n);                                        /* :209-220 */
+int matmul_tn_dev(int a_id, int b_id, int c_id, int M, int K, int N); /* :233-251 C = A^T B, A [K,M] */
+int matmul_nt_dev(int a_id, int b_id, int c_id, int M, int K, int N); /* :258-276 C = A B^T, B [N,K] */
+int copy_dev(int src_id, int dst_id, int n);                        /* :282-288 */
+
+/* ---- per-sample conv / pool: native/cuda/conv2d.cu:71-259, native/cuda/pooling.cu:67-124 ---- */
+int conv2d_fwd_dev(int input_id, int weight_id, int bias_id, int output_id, int C, int H, int W,
+                   int outC, int outH, int outW, int kH, int kW, int stride, int padding);
+int conv2d_bwd_dev(int input_id, int weight_id, int gradOut_id, int gradInput_id,
+                   int gradWeight_id, int gradBias_id, int C, int H, int W, int outC, int outH,
+                   int outW, int kH, int kW, int stride, int padding);
+int maxpool2d_fwd_dev(int input_id, int output_id, int argmax_id, int C, int H, int W,
+                      int outH, int outW, int kH, int kW, int stride);
+int maxpool2d_bwd_dev(int gradOut_id, int argmax_id, int gradInput_id, int C, int outH, int outW);
+
+/* ---- batched conv / pool: native/cuda/conv2d_batched.cu:69-271,
+ *      native/cuda/pooling_batched.cu:61-116 ---- */
+int conv2d_batched_fwd_dev(int input_id, int weight_id, int bias_id, int output_id, int B, int C,
+                           int H, int W, int outC, int outH, int outW, int kH, int kW, int stride,
+                           int padding);
+int conv2d_batched_bwd_dev(int input_id, int weight_id, int gradOut_id, int gradInput_id,
+                           int gradWeight_id, int gradBias_id, int B, int C, int H, int W,
+                           int outC, int outH, int outW, int kH, int kW, int stride, int padding);
+int maxpool2d_batched_fwd_dev(int input_id, int output_id, int argmax_id, int B, int C, int H,
+                              int W, int outH, int outW, int kH, int kW, int stride);
+int maxpool2d_batched_bwd_dev(int gradOut_id, int argmax_id, int gradInput_id, int B, int C,
+                              int outH, int outW);
+
+/* ---- attention primitives: native/cuda/attention.cu:83-251 ---- */
+int softmax_rows_fwd_dev(int x_id, int y_id, int N, int M);
+int softmax_rows_bwd_dev(int P_id, int dP_id, int dS_id, int N, int M);
+int causal_mask_dev(int x_id, int N, int M, float maskValue);
+int scale_dev(int x_id, float s, int n);
+int causal_softmax_dev(int x_id, int N, int M, float maskValue);
+
+/* ===================================================================== *
+ * Part 2 -- additive entry points (no counterpart in the reference's cdef)
+ * ===================================================================== */
+
+/* Last error of this library as text ("" when none); the code of the last
+ * failing call.  The reference only prints to stderr. */
+const char *zilla_last_error(void);
+int zilla_last_status(void);
+/* Use the given cudaStream_t (as void*) for all following device work;
+ * NULL restores the library's own stream. */
+int zilla_set_stream(void *stream);
+/* Number of kernel launches this library issued so far (instrumentation). */
+unsigned long long zilla_launch_count(void);
+
+/* Adam (src/Optim/Adam.php:36-62) over one flat tensor of n floats, fused in
+ * one kernel: m = b1 m + (1-b1) g; v = b2 v + (1-b2) g^2;
+ * w -= lr (m/(1-b1^t)) / (sqrt(v/(1-b2^t)) + eps).  t is the 1-based step.
+ * The reference has no native Adam (it runs in PHP). */
+int adam_update_dev(int w_id, int g_id, int m_id, int v_id, float lr, float beta1, float beta2,
+                    float eps, int t, int n);
+
+/* ---- fused training step (replaces the ~30 per-op FFI calls of
+ *      examples/mnist_cnn_gpu_v2.php:183-264 with one call) ----
+ *
+ * A "net" is a Sequential of layers given as int[4] rows {kind, a, b, c}:
+ *   1 Conv2D 3x3 stride 1 (a = in channels, b = out channels, c = padding)
+ *   2 ReLU
+ *   3 MaxPool2D 2x2 stride 2
+ *   4 Linear (a = in features, b = out features; W stored [in, out] as
+ *     src/NN/Layers/Linear.php:14)
+ * followed by softmax cross-entropy on the last layer's output.
+ * Parameters are one flat float buffer in Sequential::parameters() order
+ * (src/NN/Sequential.php:32-39): [W, b] per Conv2D/Linear layer, Conv2D W
+ * in [outC, inC, 3, 3] (src/NN/Layers/Conv2D.php:25-44).
+ *
+ * precision: 0 = fp32 CUDA-core kernels everywhere (matches the reference
+ *            within 1e-4 normwise);
+ *            1 = bf16 tcgen05 tensor cores with fp32 accumulation for the
+ *            dense conv and Linear contractions, fp32 master weights and
+ *            fp32 optimizer state (larger, stated tolerance).
+ * Returns a net id > 0, or a negative status. */
+int zilla_net_create(const int *layers, int n_layers, int batch, int in_c, int in_h, int in_w,
+                     int precision);
+int zilla_net_destroy(int net);
+/* Number of floats in the flat parameter buffer. */
+long zilla_net_param_count(int net);
+/* Registry handles of the flat parameter and gradient buffers (persistent
+ * device tensors owned by the net; do not free). */
+int zilla_net_params_id(int net);
+int zilla_net_grads_id(int net);
+/* Registry handle of the int32 argmax (global flat index, GPU batched
+ * convention of native/cuda/pooling_batched.cu:39-52) of layer `layer`
+ * (a MaxPool2D layer), materialised on request; 0 if unavailable. */
+int zilla_net_argmax_id(int net, int layer);
+/* Set optimizer: 1 = SGD (lr), 2 = Adam (lr, beta1, beta2, eps). */
+int zilla_net_set_optimizer(int net, int kind, float lr, float beta1, float beta2, float eps);
+/* One training step on device-resident inputs: x_id [batch, in_c*in_h*in_w],
+ * y_id [batch] float-coded labels.  Writes the softmax_ce loss SUM over the
+ * batch into loss_id[0] (softmax_ce_dev semantics, loss zeroed first),
+ * leaves gradients in the grads buffer and updates the parameters.
+ * update = 0 computes gradients only. */
+int zilla_net_step(int net, int x_id, int y_id, int loss_id, int update);
+/* Same step from host arrays: copies x/y host->device, runs the step and
+ * copies the loss sum back (the end-to-end path). */
+int zilla_net_step_host(int net, const float *x, const float *y, float *loss_sum, int update);
+
+/* Device timing of the step's segments (instrumentation).  With profiling
+ * enabled, zilla_net_step records a CUDA event after each kernel group;
+ * zilla_net_timings then returns, for the last step, up to max_segments
+ * durations in ms and their labels ('\n'-separated) and the segment count. */
+int zilla_net_profile(int net, int enable);
+int zilla_net_timings(int net, char *labels, int labels_len, float *ms, int max_segments);
+
+/* ---- data-parallel runner (one process per GPU, NCCL over NVLink) ----
+ * zilla_dp_unique_id writes a 128-byte NCCL unique id (rank 0 creates it,
+ * the host distributes it, e.g. through a file or a store).
+ * zilla_dp_attach joins `net` to a communicator of `world` ranks: each step
+ * then sums the flat gradient buffer over ranks (one ncclAllReduce on the
+ * library stream, the scalar loss riding in the same buffer) and scales by
+ * 1/world before the identical optimizer update on every rank.  The per-rank
+ * batch is the net's batch; the global batch is world * batch. */
+int zilla_dp_unique_id(unsigned char *id128);
+int zilla_dp_attach(int net, int rank, int world, const unsigned char *id128);
+int zilla_dp_detach(int net);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ZILLA_B200_H */

@@ -1,0 +1,259 @@
+// conv_pool_f32.cu -- exact-fp32 contractions and pooling behind the
+// reference's entry points:
+//   matmul_dev / matmul_tn_dev / matmul_nt_dev (native/cuda/device_ops.cu:44-75,
+//     native/cuda/training_ops.cu:233-276; cuBLAS SGEMM there, a tiled
+//     CUDA-core GEMM here, no TF32),
+//   matmul_f32 (native/cuda/matmul.cu:93-144, host pointers),
+//   conv2d_batched_fwd_dev / conv2d_batched_bwd_dev
+//     (native/cuda/conv2d_batched.cu:69-271) and the per-sample
+//     conv2d_fwd_dev / conv2d_bwd_dev (native/cuda/conv2d.cu:71-259) as
+//     implicit GEMMs on NCHW tensors (no im2col buffer),
+//   maxpool2d_batched_fwd_dev / _bwd_dev (native/cuda/pooling_batched.cu:
+//     61-116) and maxpool2d_fwd_dev / _bwd_dev (native/cuda/pooling.cu:67-124).
+#include "conv_pool_f32.cuh"
+
+using namespace zb;
+
+namespace zb {
+
+namespace {
+float *g_ws = nullptr;
+size_t g_ws_cap = 0;
+}  // namespace
+
+float *gemm_workspace(size_t floats) {
+    if (floats > g_ws_cap) {
+        if (g_ws) {
+            cudaStreamSynchronize(stream());
+            cudaFree(g_ws);
+        }
+        g_ws = nullptr;
+        g_ws_cap = 0;
+        if (cudaMalloc((void **)&g_ws, floats * sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        g_ws_cap = floats;
+    }
+    return g_ws;
+}
+
+// ---------------------------------------------------------------- pooling
+// native/cuda/pooling_batched.cu:21-59: max from -1e30 with strict '>' in
+// (kh, kw) order (first maximum wins); argmax = flat index into the whole
+// [B, C, H, W] input, stored as int32 bits in the float buffer.
+__global__ void maxpool_fwd_kernel(const float *__restrict__ in, float *__restrict__ out,
+                                   int *__restrict__ arg, int B, int C, int H, int W, int oH,
+                                   int oW, int kH, int kW, int s) {
+    const long long total = (long long)B * C * oH * oW;
+    for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const int ow = (int)(idx % oW);
+        const int oh = (int)((idx / oW) % oH);
+        const long long bc = idx / ((long long)oW * oH);
+        const long long base = bc * H * W;
+        float best = -1e30f;
+        long long at = base;
+        for (int kh = 0; kh < kH; ++kh) {
+            const int ih = oh * s + kh;
+            for (int kw = 0; kw < kW; ++kw) {
+                const int iw = ow * s + kw;
+                if (ih >= H || iw >= W) continue;
+                const float v = in[base + (long long)ih * W + iw];
+                if (v > best) { best = v; at = base + (long long)ih * W + iw; }
+            }
+        }
+        out[idx] = best;
+        arg[idx] = (int)at;
+    }
+}
+
+// dX[argmax] += dY (caller zeroes dX, native/cuda/pooling_batched.cu:87-98).
+// Windows that do not overlap (stride >= kernel) give every input element at
+// most one source, so the add is a plain read-modify-write; overlapping
+// windows use atomics.  Indices outside dX are skipped and reported.
+template <bool kAtomic>
+__global__ void maxpool_bwd_kernel(const float *__restrict__ gout, const int *__restrict__ arg,
+                                   float *__restrict__ gin, long long total, long long n_in,
+                                   int *__restrict__ err) {
+    for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const long long t = arg[idx];
+        if (t < 0 || t >= n_in) {
+            if (err) atomicCAS(err, 0, 0x504f4f4c);  // "POOL": index out of range
+            continue;
+        }
+        if (kAtomic) atomicAdd(gin + t, gout[idx]);
+        else gin[t] += gout[idx];
+    }
+}
+
+}  // namespace zb
+
+namespace {
+
+int conv_fwd(int in_id, int w_id, int b_id, int out_id, int B, int C, int H, int W, int oC,
+             int oH, int oW, int kH, int kW, int stride, int pad, const char *name) {
+    float *x = ptr(in_id), *w = ptr(w_id), *b = ptr(b_id), *y = ptr(out_id);
+    if (!x || !w || !b || !y) return fail(kBadHandle, "%s: invalid handle", name);
+    if (B < 0 || C <= 0 || H <= 0 || W <= 0 || oC <= 0 || kH <= 0 || kW <= 0 || stride <= 0 ||
+        pad < 0)
+        return fail(kBadArg, "%s: bad sizes", name);
+    if (oH != (H + 2 * pad - kH) / stride + 1 || oW != (W + 2 * pad - kW) / stride + 1)
+        return fail(kBadArg, "%s: output size mismatch", name);
+    if (capacity(in_id) < (size_t)B * C * H * W || capacity(out_id) < (size_t)B * oC * oH * oW ||
+        capacity(w_id) < (size_t)oC * C * kH * kW || capacity(b_id) < (size_t)oC)
+        return fail(kBadHandle, "%s: buffer smaller than the shape", name);
+    ConvFwdF32 p(x, w, b, y, B, C, H, W, oC, oH, oW, kH, kW, stride, pad, false);
+    return run_simt_gemm(p, 1, name);
+}
+
+int conv_bwd(int in_id, int w_id, int go_id, int gi_id, int gw_id, int gb_id, int B, int C, int H,
+             int W, int oC, int oH, int oW, int kH, int kW, int stride, int pad, const char *name) {
+    float *x = ptr(in_id), *w = ptr(w_id), *go = ptr(go_id), *gi = ptr(gi_id), *gw = ptr(gw_id),
+          *gb = ptr(gb_id);
+    if (!x || !w || !go || !gi || !gw || !gb) return fail(kBadHandle, "%s: invalid handle", name);
+    if (B < 0 || C <= 0 || H <= 0 || W <= 0 || oC <= 0 || kH <= 0 || kW <= 0 || stride <= 0 ||
+        pad < 0)
+        return fail(kBadArg, "%s: bad sizes", name);
+    if (oH != (H + 2 * pad - kH) / stride + 1 || oW != (W + 2 * pad - kW) / stride + 1)
+        return fail(kBadArg, "%s: output size mismatch", name);
+    if (capacity(in_id) < (size_t)B * C * H * W || capacity(gi_id) < (size_t)B * C * H * W ||
+        capacity(go_id) < (size_t)B * oC * oH * oW || capacity(w_id) < (size_t)oC * C * kH * kW ||
+        capacity(gw_id) < (size_t)oC * C * kH * kW || capacity(gb_id) < (size_t)oC)
+        return fail(kBadHandle, "%s: buffer smaller than the shape", name);
+    ConvDgradF32 pd(go, w, gi, nullptr, B, C, H, W, oC, oH, oW, kH, kW, stride, pad);
+    int rc = run_simt_gemm(pd, 1, name);
+    if (rc) return rc;
+    ConvWgradF32 pw(x, go, gw, gb, B, C, H, W, oC, oH, oW, kH, kW, stride, pad);
+    return run_simt_gemm(pw, 0, name);
+}
+
+int pool_fwd(int in_id, int out_id, int arg_id, int B, int C, int H, int W, int oH, int oW,
+             int kH, int kW, int s, const char *name) {
+    float *x = ptr(in_id), *y = ptr(out_id), *a = ptr(arg_id);
+    if (!x || !y || !a) return fail(kBadHandle, "%s: invalid handle", name);
+    if (B < 0 || C <= 0 || H <= 0 || W <= 0 || oH <= 0 || oW <= 0 || kH <= 0 || kW <= 0 || s <= 0)
+        return fail(kBadArg, "%s: bad sizes", name);
+    if ((oH - 1) * s + kH > H || (oW - 1) * s + kW > W)
+        return fail(kBadArg, "%s: window exceeds the input", name);
+    const long long no = (long long)B * C * oH * oW;
+    if (capacity(in_id) < (size_t)B * C * H * W || capacity(out_id) < (size_t)no ||
+        capacity(arg_id) < (size_t)no)
+        return fail(kBadHandle, "%s: buffer smaller than the shape", name);
+    if ((long long)B * C * H * W > 0x7fffffffLL)
+        return fail(kBadArg, "%s: input too large for int32 argmax", name);
+    if (!no) return kOk;
+    maxpool_fwd_kernel<<<grid_for(no, 256), 256, 0, stream()>>>(x, y, (int *)a, B, C, H, W, oH, oW,
+                                                                kH, kW, s);
+    ZB_LAUNCH_CHECK(name);
+    return kOk;
+}
+
+int pool_bwd(int go_id, int arg_id, int gi_id, long long total, bool overlap, const char *name) {
+    float *go = ptr(go_id), *a = ptr(arg_id), *gi = ptr(gi_id);
+    if (!go || !a || !gi) return fail(kBadHandle, "%s: invalid handle", name);
+    if (total < 0) return fail(kBadArg, "%s: bad sizes", name);
+    if (capacity(go_id) < (size_t)total || capacity(arg_id) < (size_t)total)
+        return fail(kBadHandle, "%s: buffer smaller than the shape", name);
+    if (!total) return kOk;
+    const long long n_in = (long long)capacity(gi_id);
+    if (overlap)
+        maxpool_bwd_kernel<true><<<grid_for(total, 256), 256, 0, stream()>>>(go, (const int *)a, gi, total, n_in, device_error_word());
+    else
+        maxpool_bwd_kernel<false><<<grid_for(total, 256), 256, 0, stream()>>>(go, (const int *)a, gi, total, n_in, device_error_word());
+    ZB_LAUNCH_CHECK(name);
+    return kOk;
+}
+
+int matmul_any(int a_id, int b_id, int c_id, int M, int K, int N, int variant, const char *name) {
+    float *A = ptr(a_id), *B = ptr(b_id), *Cm = ptr(c_id);
+    if (!A || !B || !Cm) return fail(kBadHandle, "%s: invalid handle", name);
+    if (M < 0 || K < 0 || N < 0) return fail(kBadArg, "%s: negative size", name);
+    if (capacity(a_id) < (size_t)M * K || capacity(b_id) < (size_t)K * N ||
+        capacity(c_id) < (size_t)M * N)
+        return fail(kBadHandle, "%s: buffer smaller than the shape", name);
+    if (variant == 0) return run_simt_gemm(GemmNN(A, B, Cm, M, N, K), 0, name);
+    if (variant == 1) return run_simt_gemm(GemmTN(A, B, Cm, M, N, K), 0, name);
+    return run_simt_gemm(GemmNT(A, B, Cm, M, N, K), 0, name);
+}
+
+// Host-pointer staging for matmul_f32.
+float *g_hm = nullptr;
+size_t g_hm_cap = 0;
+
+}  // namespace
+
+extern "C" {
+
+int matmul_dev(int a, int b, int c, int M, int K, int N) { return matmul_any(a, b, c, M, K, N, 0, "matmul_dev"); }
+int matmul_tn_dev(int a, int b, int c, int M, int K, int N) { return matmul_any(a, b, c, M, K, N, 1, "matmul_tn_dev"); }
+int matmul_nt_dev(int a, int b, int c, int M, int K, int N) { return matmul_any(a, b, c, M, K, N, 2, "matmul_nt_dev"); }
+
+void matmul_f32(const float *A, const float *B, float *Cm, int M, int K, int N) {
+    if (M <= 0 || N <= 0 || K < 0) return;
+    const size_t na = (size_t)M * K, nb = (size_t)K * N, nc = (size_t)M * N;
+    const size_t need = na + nb + nc;
+    if (need > g_hm_cap) {
+        if (g_hm) cudaFree(g_hm);
+        g_hm = nullptr;
+        g_hm_cap = 0;
+        if (cudaMalloc((void **)&g_hm, need * sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            fail(kBadHandle, "matmul_f32: staging allocation failed");
+            return;
+        }
+        g_hm_cap = need;
+    }
+    float *dA = g_hm, *dB = g_hm + na, *dC = g_hm + na + nb;
+    if (na) cudaMemcpyAsync(dA, A, na * sizeof(float), cudaMemcpyHostToDevice, stream());
+    if (nb) cudaMemcpyAsync(dB, B, nb * sizeof(float), cudaMemcpyHostToDevice, stream());
+    if (run_simt_gemm(GemmNN(dA, dB, dC, M, N, K), 0, "matmul_f32")) return;
+    cudaMemcpyAsync(Cm, dC, nc * sizeof(float), cudaMemcpyDeviceToHost, stream());
+    if (cudaStreamSynchronize(stream()) != cudaSuccess) check_cuda("matmul_f32");
+}
+
+int conv2d_batched_fwd_dev(int in, int w, int b, int out, int B, int C, int H, int W, int oC,
+                           int oH, int oW, int kH, int kW, int stride, int pad) {
+    return conv_fwd(in, w, b, out, B, C, H, W, oC, oH, oW, kH, kW, stride, pad, "conv2d_batched_fwd_dev");
+}
+
+int conv2d_batched_bwd_dev(int in, int w, int go, int gi, int gw, int gb, int B, int C, int H,
+                           int W, int oC, int oH, int oW, int kH, int kW, int stride, int pad) {
+    return conv_bwd(in, w, go, gi, gw, gb, B, C, H, W, oC, oH, oW, kH, kW, stride, pad, "conv2d_batched_bwd_dev");
+}
+
+int conv2d_fwd_dev(int in, int w, int b, int out, int C, int H, int W, int oC, int oH, int oW,
+                   int kH, int kW, int stride, int pad) {
+    return conv_fwd(in, w, b, out, 1, C, H, W, oC, oH, oW, kH, kW, stride, pad, "conv2d_fwd_dev");
+}
+
+int conv2d_bwd_dev(int in, int w, int go, int gi, int gw, int gb, int C, int H, int W, int oC,
+                   int oH, int oW, int kH, int kW, int stride, int pad) {
+    return conv_bwd(in, w, go, gi, gw, gb, 1, C, H, W, oC, oH, oW, kH, kW, stride, pad, "conv2d_bwd_dev");
+}
+
+int maxpool2d_batched_fwd_dev(int in, int out, int arg, int B, int C, int H, int W, int oH,
+                              int oW, int kH, int kW, int s) {
+    return pool_fwd(in, out, arg, B, C, H, W, oH, oW, kH, kW, s, "maxpool2d_batched_fwd_dev");
+}
+
+int maxpool2d_batched_bwd_dev(int go, int arg, int gi, int B, int C, int oH, int oW) {
+    // The ABI carries no kernel/stride; pooling windows written by this
+    // library's forward never overlap when stride >= kernel, but the
+    // signature cannot tell, so overlapping-safe atomics are used unless the
+    // index set is known to be collision-free (the fused step uses its own
+    // gather kernels).
+    return pool_bwd(go, arg, gi, (long long)B * C * oH * oW, true, "maxpool2d_batched_bwd_dev");
+}
+
+int maxpool2d_fwd_dev(int in, int out, int arg, int C, int H, int W, int oH, int oW, int kH,
+                      int kW, int s) {
+    return pool_fwd(in, out, arg, 1, C, H, W, oH, oW, kH, kW, s, "maxpool2d_fwd_dev");
+}
+
+int maxpool2d_bwd_dev(int go, int arg, int gi, int C, int oH, int oW) {
+    return pool_bwd(go, arg, gi, (long long)C * oH * oW, true, "maxpool2d_bwd_dev");
+}
+
+}  // extern "C"

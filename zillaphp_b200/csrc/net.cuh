@@ -1,0 +1,81 @@
+// net.cuh -- the fused training step ("net") shared between the fp32
+// CUDA-core engine and the bf16 tcgen05 engine.
+#pragma once
+
+#include <vector>
+
+#include "common.cuh"
+#include "optim.cuh"
+
+#ifdef ZB_HAVE_NCCL
+#include <nccl.h>
+#endif
+
+namespace zb {
+
+enum LayerKind { kConv = 1, kRelu = 2, kPool = 3, kLinear = 4 };
+
+// A stage is one launch group of the step: a conv or linear layer with the
+// ReLU that follows it fused in, a max-pool, or a stand-alone ReLU.
+struct Stage {
+    int kind = 0;          // LayerKind of the main layer
+    int layer = 0;         // index of the main layer in the user's list
+    bool relu = false;     // a ReLU follows and is fused into this stage
+    int C = 0, H = 0, W = 0;      // input shape per sample
+    int oC = 0, oH = 0, oW = 0;   // output shape per sample
+    int pad = 0;
+    long long in_n = 0, out_n = 0;  // per-sample sizes
+    long long poff = 0, pn_w = 0, pn_b = 0;  // offsets into the flat parameter buffer
+    float *out = nullptr;  // [B, out_n] fp32 activations (engine 0) / NCHW mirror
+    float *gin = nullptr;  // gradient w.r.t. the stage input [B, in_n] (masked by the
+                           // previous stage's ReLU when that one is fused)
+    int *arg = nullptr;    // max-pool argmax (global flat index, int32)
+    int arg_id = 0;        // registry handle exported on request
+};
+
+struct TcEngine;  // bf16 tensor-core engine (tc_net.cu)
+
+struct Net {
+    int id = 0;
+    int B = 0, inC = 0, inH = 0, inW = 0, classes = 0;
+    int precision = 0;
+    std::vector<int> spec;
+    std::vector<Stage> st;
+    long long nparams = 0;
+    int params_id = 0, grads_id = 0;  // registry handles (grads has nparams + 1 floats: loss last)
+    float *params = nullptr, *grads = nullptr;
+    float *m = nullptr, *v = nullptr;  // Adam state
+    float *dlogits = nullptr;
+    double *row_loss = nullptr;
+    float *xin = nullptr, *yin = nullptr, *loss_dev = nullptr;  // staging for step_host
+    int opt = 1;
+    float lr = 0.01f, b1 = 0.9f, b2 = 0.999f, eps = 1e-8f;
+    int t = 0;
+    // data parallel
+    int rank = 0, world = 1;
+#ifdef ZB_HAVE_NCCL
+    ncclComm_t comm = nullptr;
+#endif
+    TcEngine *tc = nullptr;
+    // per-segment device timing (zilla_net_profile / zilla_net_timings)
+    bool profile = false;
+    std::vector<cudaEvent_t> ev_pool;
+    std::vector<const char *> ev_label;   // label of the segment ending at event i
+    int ev_used = 0;
+};
+
+// Records the end of a timed segment named `label` (no-op unless profiling).
+void prof_mark(Net &n, const char *label);
+
+Net *net_get(int id);
+// fp32 engine pieces used by both engines
+int fp32_forward(Net &n, const float *x);
+int fp32_backward(Net &n, const float *x);
+int loss_and_dlogits(Net &n, const float *logits, const float *y, float *loss_out);
+// bf16 engine (tc_net.cu)
+int tc_create(Net &n);
+void tc_destroy(Net &n);
+int tc_step(Net &n, const float *x, const float *y, float *loss_out);
+int tc_sync_params(Net &n);   // refresh the bf16 operand copies from the fp32 master
+
+}  // namespace zb

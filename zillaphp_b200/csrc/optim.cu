@@ -1,0 +1,97 @@
+// optim.cu -- fused Adam over one flat parameter buffer.
+//
+// The reference runs Adam in PHP doubles, one element at a time
+// (src/Optim/Adam.php:36-62).  Here parameters, first and second moments are
+// fp32 device buffers updated by one vectorised grid-stride kernel:
+//   m = b1 m + (1-b1) g;  v = b2 v + (1-b2) g^2;
+//   w -= lr * (m / bc1) / (sqrt(v / bc2) + eps),  bc = 1 - b^t (host, double)
+// keeping the reference's placement of eps (after the square root).
+#include <math.h>
+
+#include "common.cuh"
+#include "optim.cuh"
+
+namespace zb {
+
+__device__ __forceinline__ void adam_one(float &w, float g, float &m, float &v, const AdamArgs &a) {
+    g *= a.grad_scale;
+    m = a.b1 * m + a.one_minus_b1 * g;
+    v = a.b2 * v + a.one_minus_b2 * g * g;
+    w -= a.lr * (m * a.inv_bc1) / (sqrtf(v * a.inv_bc2) + a.eps);
+}
+
+__global__ void adam_kernel(float *__restrict__ w, const float *__restrict__ g,
+                            float *__restrict__ m, float *__restrict__ v, long long n, AdamArgs a) {
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    const long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool vec = ((((uintptr_t)w) | ((uintptr_t)g) | ((uintptr_t)m) | ((uintptr_t)v)) & 15) == 0;
+    long long tail = 0;
+    if (vec) {
+        const long long n4 = n >> 2;
+        for (long long i = i0; i < n4; i += stride) {
+            float4 W = reinterpret_cast<float4 *>(w)[i];
+            const float4 G = reinterpret_cast<const float4 *>(g)[i];
+            float4 M = reinterpret_cast<float4 *>(m)[i];
+            float4 V = reinterpret_cast<float4 *>(v)[i];
+            adam_one(W.x, G.x, M.x, V.x, a);
+            adam_one(W.y, G.y, M.y, V.y, a);
+            adam_one(W.z, G.z, M.z, V.z, a);
+            adam_one(W.w, G.w, M.w, V.w, a);
+            reinterpret_cast<float4 *>(w)[i] = W;
+            reinterpret_cast<float4 *>(m)[i] = M;
+            reinterpret_cast<float4 *>(v)[i] = V;
+        }
+        tail = n4 << 2;
+    }
+    for (long long i = tail + i0; i < n; i += stride) adam_one(w[i], g[i], m[i], v[i], a);
+}
+
+__global__ void sgd_scaled_kernel(float *__restrict__ w, const float *__restrict__ g, float lr,
+                                  float scale, long long n) {
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        w[i] -= lr * (g[i] * scale);
+}
+
+int launch_sgd(float *w, const float *g, float lr, float grad_scale, long long n) {
+    if (n <= 0) return kOk;
+    sgd_scaled_kernel<<<grid_for(n, 256, 4), 256, 0, stream()>>>(w, g, lr, grad_scale, n);
+    ZB_LAUNCH_CHECK("sgd_update");
+    return kOk;
+}
+
+AdamArgs make_adam_args(float lr, float b1, float b2, float eps, int t, float grad_scale) {
+    AdamArgs a;
+    a.lr = lr;
+    a.b1 = b1;
+    a.b2 = b2;
+    a.one_minus_b1 = (float)(1.0 - (double)b1);
+    a.one_minus_b2 = (float)(1.0 - (double)b2);
+    a.inv_bc1 = (float)(1.0 / (1.0 - pow((double)b1, (double)t)));
+    a.inv_bc2 = (float)(1.0 / (1.0 - pow((double)b2, (double)t)));
+    a.eps = eps;
+    a.grad_scale = grad_scale;
+    return a;
+}
+
+int launch_adam(float *w, const float *g, float *m, float *v, long long n, const AdamArgs &a) {
+    if (n <= 0) return kOk;
+    adam_kernel<<<grid_for(n / 4 + 1, 256, 4), 256, 0, stream()>>>(w, g, m, v, n, a);
+    ZB_LAUNCH_CHECK("adam_update");
+    return kOk;
+}
+
+}  // namespace zb
+
+using namespace zb;
+
+extern "C" int adam_update_dev(int w_id, int g_id, int m_id, int v_id, float lr, float beta1,
+                               float beta2, float eps, int t, int n) {
+    float *w = ptr(w_id), *g = ptr(g_id), *m = ptr(m_id), *v = ptr(v_id);
+    if (!w || !g || !m || !v) return fail(kBadHandle, "adam_update_dev: invalid handle");
+    if (n < 0 || t < 1) return fail(kBadArg, "adam_update_dev: bad n or t");
+    if (capacity(w_id) < (size_t)n || capacity(g_id) < (size_t)n || capacity(m_id) < (size_t)n ||
+        capacity(v_id) < (size_t)n)
+        return fail(kBadHandle, "adam_update_dev: buffer smaller than n");
+    return launch_adam(w, g, m, v, n, make_adam_args(lr, beta1, beta2, eps, t, 1.0f));
+}

@@ -1,0 +1,109 @@
+"""Python handle on the fused training step of libzilla_b200.so (zilla_net_*)."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import native
+from .configs import ADAM, Workload
+
+
+class Net:
+    """A Sequential trained by one C call per step (zilla_net_step)."""
+
+    def __init__(self, workload: Workload, batch: int | None = None, precision: int | None = None):
+        self.w = workload
+        self.lib = native.load()
+        self.batch = batch if batch is not None else workload.batch
+        self.precision = workload.precision if precision is None else precision
+        spec = np.ascontiguousarray(np.asarray(workload.layers, np.int32).ravel())
+        c, h, wd = workload.in_shape
+        self.id = self.lib.zilla_net_create(spec.ctypes.data_as(native.IP), len(workload.layers), self.batch,
+                                            c, h, wd, self.precision)
+        if self.id <= 0:
+            raise RuntimeError(f"zilla_net_create failed: {native.last_error()}")
+        self.nparams = int(self.lib.zilla_net_param_count(self.id))
+        b1, b2, eps = workload.adam
+        self._check(self.lib.zilla_net_set_optimizer(self.id, workload.optimizer, workload.lr, b1, b2, eps))
+        self.params_id = self.lib.zilla_net_params_id(self.id)
+        self.grads_id = self.lib.zilla_net_grads_id(self.id)
+
+    def _check(self, rc: int) -> None:
+        if rc != 0:
+            raise RuntimeError(f"libzilla_b200 call failed ({rc}): {native.last_error()}")
+
+    # ---- parameters
+    def set_params(self, p: np.ndarray) -> None:
+        p = np.ascontiguousarray(p, np.float32)
+        assert p.size == self.nparams
+        self._check(self.lib.zilla_buffer_upload(self.params_id, p.ctypes.data_as(native.FP), p.size))
+
+    def params(self) -> np.ndarray:
+        out = np.empty(self.nparams, np.float32)
+        self._check(self.lib.zilla_buffer_download(self.params_id, out.ctypes.data_as(native.FP), self.nparams))
+        return out
+
+    def grads(self) -> np.ndarray:
+        out = np.empty(self.nparams + 1, np.float32)
+        self._check(self.lib.zilla_buffer_download(self.grads_id, out.ctypes.data_as(native.FP), self.nparams + 1))
+        return out[: self.nparams]
+
+    def argmax(self, layer: int, n: int) -> np.ndarray:
+        i = self.lib.zilla_net_argmax_id(self.id, layer)
+        if i <= 0:
+            raise RuntimeError("no argmax for that layer")
+        out = np.empty(n, np.float32)
+        self._check(self.lib.zilla_buffer_download(i, out.ctypes.data_as(native.FP), n))
+        return out.view(np.int32)
+
+    # ---- steps
+    def step_host(self, x: np.ndarray, y: np.ndarray, update: bool = True) -> float:
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.ascontiguousarray(y, np.float32)
+        loss = C.c_float(0.0)
+        self._check(self.lib.zilla_net_step_host(self.id, x.ctypes.data_as(native.FP), y.ctypes.data_as(native.FP),
+                                                 C.byref(loss), int(update)))
+        return float(loss.value)
+
+    def step_dev(self, x_id: int, y_id: int, loss_id: int, update: bool = True) -> None:
+        self._check(self.lib.zilla_net_step(self.id, x_id, y_id, loss_id, int(update)))
+
+    def profile(self, enable: bool = True) -> None:
+        self._check(self.lib.zilla_net_profile(self.id, int(enable)))
+
+    def timings(self) -> list[tuple[str, float]]:
+        """(label, ms) of each kernel group of the last profiled step."""
+        labels = C.create_string_buffer(8192)
+        ms = np.zeros(256, np.float32)
+        k = self.lib.zilla_net_timings(self.id, labels, 8192, ms.ctypes.data_as(native.FP), 256)
+        if k < 0:
+            raise RuntimeError(native.last_error())
+        names = labels.value.decode().split("\n")[:k]
+        return list(zip(names, ms[:k].tolist()))
+
+    def dp_attach(self, rank: int, world: int, uid: bytes) -> None:
+        self._check(self.lib.zilla_dp_attach(self.id, rank, world, uid))
+
+    def close(self) -> None:
+        if getattr(self, "id", 0) > 0:
+            self.lib.zilla_net_destroy(self.id)
+            self.id = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def dp_unique_id() -> bytes:
+    lib = native.load()
+    buf = C.create_string_buffer(128)
+    if lib.zilla_dp_unique_id(buf) != 0:
+        raise RuntimeError(native.last_error())
+    return buf.raw
+
+
+def is_adam(w: Workload) -> bool:
+    return w.optimizer == ADAM

@@ -142,7 +142,57 @@ def stage_work(w: configs.Workload, batch: int) -> list[dict]:
     return out
 
 
-def roofline(w, batch, seg_times: list[tuple[str, float]], steps: int, pk: dict, pk_kind: str):
+def tc_work(w: configs.Workload, b: int) -> list[dict]:
+    """Kernel groups of the tensor-core engine in execution order (the labels
+    zilla_net_timings reports): algorithmic FLOPs (2*M*N*K per contraction)
+    and compulsory bytes (bf16 activations, u8 pool codes, fp32 parameters)."""
+    L = list(w.layers)
+    c, h, wd = w.in_shape
+    out = [{"label": "pack", "flops": 0, "bytes": 4 * configs.param_count(w)}]
+    convs, lin = [], []
+    i = 0
+    while i < len(L):
+        kind, a, o, p = L[i]
+        if kind == configs.CONV:
+            oh, ow = h + 2 * p - 2, wd + 2 * p - 2
+            pool = i + 2 < len(L) and L[i + 2][0] == configs.POOL
+            convs.append((a, o, h, wd, oh, ow, pool))
+            c, h, wd = o, (oh // 2 if pool else oh), (ow // 2 if pool else ow)
+            i += 3 if pool else 2
+        elif kind == configs.LINEAR:
+            lin.append((a, o))
+            i += 2 if (i + 1 < len(L) and L[i + 1][0] == configs.RELU) else 1
+        else:
+            i += 1
+    for k, (a, o, ih, iw, oh, ow, pool) in enumerate(convs):
+        f = 2 * b * oh * ow * o * a * 9
+        inb = b * ih * iw * a * (4 if k == 0 else 2)
+        outb = b * (oh // 2) * (ow // 2) * o * 3 if pool else b * oh * ow * o * 2
+        out.append({"label": "conv_fwd", "flops": f, "bytes": inb + outb, "name": f"conv{k + 1} fwd"})
+    (F, HD), (_, NC) = lin[0], lin[-1]
+    out.append({"label": "linear_fwd", "flops": 2 * b * F * HD, "bytes": 2 * (b * (F + HD) + F * HD),
+                "name": "fc1 fwd"})
+    out.append({"label": "softmax_ce", "flops": 6 * b * HD * NC, "bytes": 4 * b * HD, "name": "head"})
+    out.append({"label": "linear_bwd", "flops": 4 * b * F * HD, "bytes": 2 * (2 * b * F + 2 * b * HD + F * HD) + 4 * F * HD,
+                "name": "fc1 dX+dW"})
+    for k in range(len(convs) - 1, -1, -1):
+        a, o, ih, iw, oh, ow, pool = convs[k]
+        if k > 0:
+            out.append({"label": "pool_bwd", "flops": 0, "bytes": b * ((oh // 2) * (ow // 2) * o * 3 + oh * ow * o * 2),
+                        "name": f"unpool{k + 1}"})
+            f = 2 * 2 * b * oh * ow * o * a * 9
+            out.append({"label": "conv_bwd", "flops": f, "bytes": b * (oh * ow * o * 2 * 2 + ih * iw * a * 2 * 2),
+                        "name": f"conv{k + 1} dX+dW"})
+        else:
+            out.append({"label": "conv_bwd", "flops": 2 * b * oh * ow * o * a * 9,
+                        "bytes": b * (oh * ow * o * 2 + ih * iw * 4), "name": "conv1 dW"})
+    n = configs.param_count(w)
+    out.append({"label": "adam" if w.optimizer == configs.ADAM else "sgd", "flops": 0,
+                "bytes": (28 if w.optimizer == configs.ADAM else 12) * n, "name": "optimizer"})
+    return out
+
+
+def roofline(w, batch, seg_times: list[tuple[str, float]], steps: int, pk: dict, pk_kind: str, precision: int = 0):
     """Dominant kernel group: the label with the largest total time; matched to
     its algorithmic work in execution order."""
     # assign each measured segment to the work item of the same label, in order
@@ -151,6 +201,8 @@ def roofline(w, batch, seg_times: list[tuple[str, float]], steps: int, pk: dict,
     bwd = [x for x in work if x["label"].endswith("_bwd")][::-1]
     tail = [x for x in work if not x["label"].endswith(("_fwd", "_bwd"))]
     order = fwd + [t for t in tail if t["label"] == "softmax_ce"] + bwd + [t for t in tail if t["label"] != "softmax_ce"]
+    if precision == 1:
+        order = tc_work(w, batch)
     per_step = [s for s in seg_times if s[0] != "allreduce"]
     nseg = len(order)
     agg = {}
@@ -163,7 +215,7 @@ def roofline(w, batch, seg_times: list[tuple[str, float]], steps: int, pk: dict,
     k_dom = max(agg, key=lambda k: sum(agg[k]))
     item = order[k_dom]
     ms = sum(agg[k_dom]) / len(agg[k_dom])
-    breakdown = {f"{order[k]['label']}#{k}": round(sum(v) / len(v), 4) for k, v in sorted(agg.items())}
+    breakdown = {f"{order[k].get('name', order[k]['label'])}#{k}": round(sum(v) / len(v), 4) for k, v in sorted(agg.items())}
     if item["flops"] > 0:
         achieved = item["flops"] / (ms * 1e-3) / 1e12
         peak = pk.get("bf16_tflops_sustained" if ms > 50 else "bf16_tflops", 1590.0)
@@ -173,7 +225,7 @@ def roofline(w, batch, seg_times: list[tuple[str, float]], steps: int, pk: dict,
         peak = pk.get("hbm_gbs", 6650.0)
         r = {"bound": "hbm", "unit": "GB/s", "achieved": round(achieved, 1), "peak": peak}
     r["frac"] = round(r["achieved"] / r["peak"], 5)
-    r["kernel"] = f"{item['label']} (group {k_dom} of the step)"
+    r["kernel"] = f"{item.get('name', item['label'])} (group {k_dom} of the step)"
     r["ms_per_launch"] = round(ms, 4)
     r["peak_source"] = pk_kind
     r["traffic"] = None
@@ -330,7 +382,7 @@ def main():
 
     if rank == 0:
         pk, pk_kind = peaks()
-        roof, breakdown = roofline(w, b, segs, args.steps, pk, pk_kind)
+        roof, breakdown = roofline(w, b, segs, args.steps, pk, pk_kind, precision)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             r = cpu_reference(w, sample=64, min_seconds=10.0, max_steps=50)

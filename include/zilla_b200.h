@@ -183,6 +183,15 @@ int zilla_net_step_host(int net, const float *x, const float *y, float *loss_sum
  * durations in ms and their labels ('\n'-separated) and the segment count. */
 int zilla_net_profile(int net, int enable);
 int zilla_net_timings(int net, char *labels, int labels_len, float *ms, int max_segments);
+/* Diagnostics.  zilla_net_inspect returns the element count of the engine's
+ * intermediate tensor `index` (0 past the last one), writes its name and,
+ * when host != NULL, copies up to n_floats elements widened to float (bf16
+ * activations, u8 pool codes).  Precision 1 only.  zilla_net_device_status
+ * synchronises and reports a kernel-side error (a bounded wait that expired
+ * or an index out of range) as -3 with the code in zilla_last_error(). */
+int zilla_net_inspect(int net, int index, char *name, int name_len, float *host,
+                      unsigned long n_floats);
+int zilla_net_device_status(int net);
 
 /* ---- data-parallel runner (one process per GPU, NCCL over NVLink) ----
  * zilla_dp_unique_id writes a 128-byte NCCL unique id (rank 0 creates it,

@@ -37,7 +37,7 @@ def test_fp32_step_matches_oracle(name, batch):
         gl = net.step_host(x, y)
         assert abs(gl - rl) / abs(rl) < 1e-5, (step, gl, rl)
         assert npref.normwise(net.grads(), ref.grads) < 1e-4
-        assert npref.normwise(net.params(), ref.params) < 1e-5
+        assert npref.normwise(net.params(), ref.params) < 1e-4
         if step == 0:
             # pool argmax bit-exact (same forward bits on both sides)
             shape = (1,) + tuple(w.in_shape)

@@ -1,0 +1,114 @@
+"""The bf16 tcgen05 engine (precision 1) against the CPU oracle (GPU).
+
+Tolerances (bf16 operands, fp32 accumulation and fp32 master weights):
+  packed bf16 weights           exact (round-to-nearest of the fp32 master)
+  activations per layer         normwise <= 2e-2
+  loss                          relative <= 1e-2
+  gradients per parameter block normwise <= 5e-2
+  weights after one Adam step   normwise <= 1e-2
+The tensor-core path is also deterministic: two identical steps give
+bit-identical gradients.
+"""
+import numpy as np
+import pytest
+
+import npref
+import oracle
+from zillaphp_b200 import configs, synthetic
+from zillaphp_b200.net import Net
+
+pytestmark = pytest.mark.gpu
+
+B = 16
+
+
+def bf16_round(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).float().numpy()
+
+
+def nchw_to_nhwc(a, Bn, C, H, W):
+    return a.reshape(Bn, C, H, W).transpose(0, 2, 3, 1).ravel()
+
+
+def blocks(w):
+    off, out = 0, []
+    for li, (kind, a, b, _) in enumerate(w.layers):
+        if kind == configs.CONV:
+            out += [(f"L{li}.W", off, b * a * 9), (f"L{li}.b", off + b * a * 9, b)]
+            off += b * a * 9 + b
+        elif kind == configs.LINEAR:
+            out += [(f"L{li}.W", off, a * b), (f"L{li}.b", off + a * b, b)]
+            off += a * b + b
+    return out
+
+
+@pytest.fixture(scope="module")
+def large_step():
+    w = configs.CNN_LARGE
+    p0 = synthetic.init_params(w, seed=21)
+    x, y = synthetic.batch(w, B, seed=21)
+    ref = oracle.StepModel(w.spec(), B, w.in_shape)
+    ref.params[:] = p0
+    rl = ref.step(x, y, w.optimizer, w.lr)
+    net = Net(w, batch=B, precision=1)
+    net.set_params(p0)
+    gl = net.step_host(x, y)
+    net.device_status()
+    views = net.inspect()
+    out = dict(w=w, p0=p0, x=x, y=y, ref=ref, rl=rl, net=net, gl=gl, views=views,
+               grads=net.grads(), params=net.params())
+    yield out
+    net.close()
+
+
+def test_packed_weights_exact(large_step):
+    v, p0 = large_step["views"], large_step["p0"]
+    W2 = p0[320:320 + 64 * 32 * 9].reshape(64, 32, 9)
+    assert np.array_equal(v["conv2.wf"], bf16_round(W2.transpose(2, 0, 1)).ravel())        # [t][co][ci]
+    assert np.array_equal(v["conv2.wd"], bf16_round(W2[:, :, ::-1].transpose(2, 1, 0)).ravel())  # [t][ci][co]
+
+
+def test_forward_activations(large_step):
+    s, ref, v = large_step, large_step["ref"], large_step["views"]
+    errs = {}
+    # layer outputs of the oracle (NCHW fp32): 1 relu(conv1), 4 pool(conv2), 7 pool(conv3), 9 relu(fc1)
+    c1 = nchw_to_nhwc(ref.output(1, B * 32 * 28 * 28), B, 32, 28, 28)
+    errs["conv1"] = npref.normwise(v["conv1.out"], c1)
+    p2 = nchw_to_nhwc(ref.output(4, B * 64 * 14 * 14), B, 64, 14, 14)
+    errs["conv2"] = npref.normwise(v["conv2.out"], p2)
+    p3 = nchw_to_nhwc(ref.output(7, B * 128 * 7 * 7), B, 128, 7, 7)
+    errs["conv3"] = npref.normwise(v["conv3.out"], p3)
+    errs["fc1"] = npref.normwise(v["hidden.out"], ref.output(9, B * 256))
+    print("forward normwise errors:", errs)
+    assert all(e < 2e-2 for e in errs.values()), errs
+    # argmax agreement of the fused pool epilogue with the oracle (codes vs channel-local argmax)
+    am = ref.argmax(4, B * 64 * 14 * 14).reshape(B, 64, 14, 14)
+    oh = np.arange(14)[:, None]; ow = np.arange(14)[None, :]
+    pos = (am // 28 - 2 * oh) * 2 + (am % 28 - 2 * ow)
+    code = v["conv2.code"].reshape(B, 14, 14, 64).transpose(0, 3, 1, 2).astype(np.int64) & 3
+    agree = float((code == pos).mean())
+    print("pool2 argmax agreement", agree)
+    assert agree > 0.97
+
+
+def test_loss_grads_update(large_step):
+    s = large_step
+    w, ref = s["w"], s["ref"]
+    assert abs(s["gl"] - s["rl"]) / abs(s["rl"]) < 1e-2, (s["gl"], s["rl"])
+    errs = {name: npref.normwise(s["grads"][o:o + n], ref.grads[o:o + n]) for name, o, n in blocks(w)}
+    print("gradient normwise errors:", errs)
+    assert all(e < 5e-2 for e in errs.values()), errs
+    assert npref.normwise(s["params"], ref.params) < 1e-2
+
+
+def test_deterministic():
+    w = configs.CNN_LARGE
+    p0 = synthetic.init_params(w, seed=4)
+    x, y = synthetic.batch(w, 128, seed=4)
+    a, b = Net(w, batch=128, precision=1), Net(w, batch=128, precision=1)
+    a.set_params(p0); b.set_params(p0)
+    la, lb = a.step_host(x, y, update=False), b.step_host(x, y, update=False)
+    assert la == lb
+    assert np.array_equal(a.grads(), b.grads())
+    a.close(); b.close()

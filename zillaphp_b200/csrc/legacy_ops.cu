@@ -76,7 +76,7 @@ __global__ void sgd_kernel(float *__restrict__ w, const float *__restrict__ g, f
                            long long n) {
     const long long stride = (long long)gridDim.x * blockDim.x;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-        w[i] -= lr * g[i];
+        w[i] = __fsub_rn(w[i], __fmul_rn(lr, g[i]));   // no FMA: the CPU rounds the product
 }
 
 __global__ void scale_kernel(float *__restrict__ x, float s, long long n) {

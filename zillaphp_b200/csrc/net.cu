@@ -495,6 +495,24 @@ int zilla_net_step_host(int id, const float *x, const float *y, float *loss_sum,
     return check_cuda("zilla_net_step_host");
 }
 
+int zilla_net_inspect(int id, int index, char *name, int name_len, float *host, unsigned long n_floats) {
+    Net *n = net_get(id);
+    if (!n) return fail(kBadHandle, "zilla_net_inspect: unknown net %d", id);
+    if (n->precision != 1) return 0;
+    int rc = read_and_clear_device_error();
+    if (rc) return fail(kCudaError, "zilla_net_inspect: device error word 0x%x", rc);
+    return tc_inspect(*n, index, name, name_len, host, n_floats);
+}
+
+int zilla_net_device_status(int id) {
+    Net *n = net_get(id);
+    if (!n) return fail(kBadHandle, "zilla_net_device_status: unknown net %d", id);
+    cudaStreamSynchronize(stream());
+    int code = read_and_clear_device_error();
+    if (code) return fail(kCudaError, "device error word 0x%x (bounded wait expired or bad index)", code);
+    return check_cuda("zilla_net_device_status");
+}
+
 int zilla_net_profile(int id, int enable) {
     Net *n = net_get(id);
     if (!n) return fail(kBadHandle, "zilla_net_profile: unknown net %d", id);

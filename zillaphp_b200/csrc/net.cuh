@@ -77,5 +77,6 @@ int tc_create(Net &n);
 void tc_destroy(Net &n);
 int tc_step(Net &n, const float *x, const float *y, float *loss_out);
 int tc_sync_params(Net &n);   // refresh the bf16 operand copies from the fp32 master
+int tc_inspect(Net &n, int index, char *name, int name_len, float *host, unsigned long n_floats);
 
 }  // namespace zb

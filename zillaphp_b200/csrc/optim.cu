@@ -50,7 +50,7 @@ __global__ void sgd_scaled_kernel(float *__restrict__ w, const float *__restrict
                                   float scale, long long n) {
     const long long stride = (long long)gridDim.x * blockDim.x;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-        w[i] -= lr * (g[i] * scale);
+        w[i] = __fsub_rn(w[i], __fmul_rn(lr, __fmul_rn(g[i], scale)));   // as sgd_update_dev: no FMA
 }
 
 int launch_sgd(float *w, const float *g, float lr, float grad_scale, long long n) {

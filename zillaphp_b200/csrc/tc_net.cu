@@ -1,16 +1,974 @@
 // tc_net.cu -- bf16 tcgen05 engine of the fused training step (precision 1).
+//
+// Network shape handled (the reference's CNN family, src/NN):
+//   Conv2D(1 -> C1, 3x3) + ReLU [+ MaxPool]        CUDA cores (K = 9)
+//   { Conv2D(Cin -> Cout, 3x3, pad 1) + ReLU + MaxPool }*   tcgen05 implicit GEMM
+//   [ Linear(F -> Hd) + ReLU ]                       tcgen05 GEMM
+//   Linear(Hd -> classes) + softmax cross-entropy    fused head (CUDA cores)
+// Activations are NHWC bf16; parameters, gradients and Adam state stay fp32
+// (master weights); bf16 operand copies of the weights are packed at the
+// start of each step.  The flat parameter / gradient layout and all
+// semantics are those of the fp32 engine (net.cu).
+//
+// Step (large CNN, 8192 x 1x28x28):
+//   pack -> conv1 -> conv2(+pool) -> conv3(+pool) -> fc1 -> head(fc2, CE, dZ)
+//   -> fc1 dX, fc1 dW -> unpool3 -> conv3 dX, conv3 dW -> unpool2
+//   -> conv2 dX (x ReLU mask of conv1) , conv2 dW -> conv1 dW -> Adam/SGD
+#include <math.h>
+#include <string.h>
+
+#include <string>
+#include <vector>
+
 #include "net.cuh"
+#include "tc_conv.cuh"
+#include "tc_gemm.cuh"
+#include "tc_wgrad.cuh"
 
 namespace zb {
 
-struct TcEngine {};
+using tc::ConvTcParams;
+using tc::GemmTcParams;
+using tc::WgradTcParams;
+
+// ====================================================================== host: TMA maps
+namespace tc {
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+}
+
+int make_tmap_bf16(CUtensorMap *map, const void *base, int rank, const uint64_t *dims, const uint64_t *strides,
+                   const uint32_t *box, Swizzle sw) {
+    if (!g_encode) {
+        cudaDriverEntryPointQueryResult q;
+        void *fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn) {
+            cudaGetLastError();
+            return fail(kCudaError, "cuTensorMapEncodeTiled unavailable");
+        }
+        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    cuuint64_t gd[5], gs[4];
+    cuuint32_t bx[5], es[5];
+    for (int i = 0; i < rank; ++i) { gd[i] = dims[i]; bx[i] = box[i]; es[i] = 1; }
+    for (int i = 0; i < rank - 1; ++i) gs[i] = strides[i];
+    CUtensorMapSwizzle s = sw == kSw128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                           : sw == kSw64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                           : sw == kSw32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                         : CU_TENSOR_MAP_SWIZZLE_NONE;
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void *>(base), gd, gs,
+                          bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, s, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(kCudaError, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return kOk;
+}
+}  // namespace tc
+
+namespace {
+
+using bf16 = __nv_bfloat16;
+
+// ====================================================================== SIMT kernels
+// Packs fp32 master weights into the bf16 operand layouts of the tensor-core
+// kernels.  Jobs: 0 conv fwd  dst[t][co][ci] = W[co][ci][t]
+//                 1 conv dgrad dst[t][ci][co] = W[co][ci][8-t]
+//                 2 linear W^T  dst[n][k]     = W[perm(k)][n]   (K-major forward B)
+//                 3 linear W    dst[k][n]     = W[perm(k)][n]   (K-major dgrad B)
+// perm maps an NHWC flatten index of the previous activation to the NCHW
+// flatten index of the reference (src/Tensor/Tensor.php:958-981).
+struct PackJob {
+    int kind;
+    const float *src;
+    bf16 *dst;
+    int a, b;          // conv: COUT, CIN;  linear: IN (K), OUT (N)
+    int C, H, W;       // linear: geometry of the flattened activation (NHWC order)
+    long long n;       // elements
+};
+constexpr int kMaxPack = 8;
+struct PackJobs {
+    PackJob j[kMaxPack];
+    int count;
+};
+
+__device__ __forceinline__ int nhwc_to_nchw(int k, int C, int H, int W) {
+    const int c = k % C, hw = k / C;
+    return c * H * W + hw;
+}
+
+__global__ void pack_kernel(PackJobs jobs) {
+    for (int ji = 0; ji < jobs.count; ++ji) {
+        const PackJob J = jobs.j[ji];
+        for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < J.n;
+             i += (long long)gridDim.x * blockDim.x) {
+            float v;
+            if (J.kind == 0) {          // i = (t*COUT + co)*CIN + ci
+                const int ci = (int)(i % J.b), r = (int)(i / J.b), co = r % J.a, t = r / J.a;
+                v = J.src[((size_t)co * J.b + ci) * 9 + t];
+            } else if (J.kind == 1) {   // i = (t*CIN + ci)*COUT + co
+                const int co = (int)(i % J.a), r = (int)(i / J.a), ci = r % J.b, t = r / J.b;
+                v = J.src[((size_t)co * J.b + ci) * 9 + (8 - t)];
+            } else if (J.kind == 2) {   // i = n*K + k
+                const int k = (int)(i % J.a), n = (int)(i / J.a);
+                v = J.src[(size_t)nhwc_to_nchw(k, J.C, J.H, J.W) * J.b + n];
+            } else {                    // i = k*N + n
+                const int n = (int)(i % J.b), k = (int)(i / J.b);
+                v = J.src[(size_t)nhwc_to_nchw(k, J.C, J.H, J.W) * J.b + n];
+            }
+            J.dst[i] = __float2bfloat16_rn(v);
+        }
+    }
+}
+
+// First conv (CIN = 1, 3x3, stride 1, pad P) + bias + ReLU on CUDA cores,
+// NHWC bf16 output; with `pool`, 2x2 max-pool + codes instead (same rules as
+// the tensor-core epilogue).  One thread per output (or pooled) pixel, all
+// COUT channels.  The tap sum follows the reference order (bias first, then
+// kh, kw ascending).
+template <int COUT, bool POOL>
+__global__ void conv_first_fwd_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                                      const float *__restrict__ bias, bf16 *__restrict__ out,
+                                      uint8_t *__restrict__ code, int B, int H, int W, int pad) {
+    __shared__ float sw[COUT * 9], sb[COUT];
+    for (int i = threadIdx.x; i < COUT * 9; i += blockDim.x) sw[i] = w[i];
+    for (int i = threadIdx.x; i < COUT; i += blockDim.x) sb[i] = bias[i];
+    __syncthreads();
+    const int oH = H + 2 * pad - 2, oW = W + 2 * pad - 2;
+    const int pH = POOL ? oH / 2 : oH, pW = POOL ? oW / 2 : oW;
+    const long long total = (long long)B * pH * pW;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int pw = (int)(i % pW), ph = (int)((i / pW) % pH), b = (int)(i / ((long long)pW * pH));
+        const float *xb = x + (size_t)b * H * W;
+        constexpr int NP = POOL ? 4 : 1;
+        float patch[NP][9];
+#pragma unroll
+        for (int q = 0; q < NP; ++q) {
+            const int oh = POOL ? 2 * ph + (q >> 1) : ph, ow = POOL ? 2 * pw + (q & 1) : pw;
+#pragma unroll
+            for (int t = 0; t < 9; ++t) {
+                const int ih = oh - pad + t / 3, iw = ow - pad + t % 3;
+                patch[q][t] = ((unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W) ? xb[ih * W + iw] : 0.0f;
+            }
+        }
+        const size_t o = (size_t)i * COUT;
+#pragma unroll 4
+        for (int c0 = 0; c0 < COUT; c0 += 8) {
+            float best[8];
+            int pos[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int co = c0 + e;
+#pragma unroll
+                for (int q = 0; q < NP; ++q) {
+                    float acc = sb[co];
+#pragma unroll
+                    for (int t = 0; t < 9; ++t) acc = __fadd_rn(acc, __fmul_rn(patch[q][t], sw[co * 9 + t]));
+                    acc = acc > 0.0f ? acc : 0.0f;
+                    if (q == 0 || acc > best[e]) { best[e] = acc; pos[e] = q; }
+                }
+            }
+            uint4 pk;
+            __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h2[e] = __floats2bfloat162_rn(best[2 * e], best[2 * e + 1]);
+            *reinterpret_cast<uint4 *>(out + o + c0) = pk;
+            if (POOL) {
+                uint2 cp;
+                uint8_t *cb = reinterpret_cast<uint8_t *>(&cp);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) cb[e] = (uint8_t)(pos[e] | (best[e] > 0.0f ? 4 : 0));
+                *reinterpret_cast<uint2 *>(code + o + c0) = cp;
+            }
+        }
+    }
+}
+
+// First-conv weight and bias gradient: dW[co][t] = sum_p dC[p][co] x[p + t],
+// db[co] = sum_p dC[p][co].  Thread (pixel slot, co); per-block partials
+// [block][COUT][10] summed later in block order.
+template <int COUT>
+__global__ void conv_first_wgrad_kernel(const bf16 *__restrict__ dC, const float *__restrict__ x,
+                                        float *__restrict__ partial, int B, int H, int W, int pad) {
+    constexpr int SLOTS = 256 / COUT;
+    const int co = threadIdx.x % COUT, slot = threadIdx.x / COUT;
+    const int oH = H + 2 * pad - 2, oW = W + 2 * pad - 2;
+    const long long total = (long long)B * oH * oW;
+    float acc[10];
+#pragma unroll
+    for (int t = 0; t < 10; ++t) acc[t] = 0.0f;
+    for (long long p = (long long)blockIdx.x * SLOTS + slot; p < total; p += (long long)gridDim.x * SLOTS) {
+        const float g = __bfloat162float(dC[(size_t)p * COUT + co]);
+        const int ow = (int)(p % oW), oh = (int)((p / oW) % oH), b = (int)(p / ((long long)oW * oH));
+        const float *xb = x + (size_t)b * H * W;
+#pragma unroll
+        for (int t = 0; t < 9; ++t) {
+            const int ih = oh - pad + t / 3, iw = ow - pad + t % 3;
+            const float xv = ((unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W) ? xb[ih * W + iw] : 0.0f;
+            acc[t] = fmaf(g, xv, acc[t]);
+        }
+        acc[9] += g;
+    }
+    __shared__ float red[256][11];
+#pragma unroll
+    for (int t = 0; t < 10; ++t) red[threadIdx.x][t] = acc[t];
+    __syncthreads();
+    if (slot == 0) {
+        for (int s = 1; s < SLOTS; ++s)
+#pragma unroll
+            for (int t = 0; t < 10; ++t) acc[t] += red[s * COUT + co][t];
+        float *dst = partial + (size_t)blockIdx.x * COUT * 10 + co * 10;
+#pragma unroll
+        for (int t = 0; t < 10; ++t) dst[t] = acc[t];
+    }
+}
+
+// Max-pool + ReLU backward as a gather: dC[b,h,w,c] = dP[b,h/2,w/2,c] when the
+// window's code points at (h,w) and the maximum was positive, else 0
+// (positions outside every window, floor pooling, get 0).  Also the bias
+// gradient partials sum_p dC[p][c] per block.  Thread = 8 channels of one
+// pixel (16-byte loads / stores).
+__global__ void unpool_kernel(const bf16 *__restrict__ dP, const uint8_t *__restrict__ code, bf16 *__restrict__ dC,
+                              float *__restrict__ bias_partial, int B, int H, int W, int C) {
+    const int G = C / 8;                   // channel groups
+    const int slots = blockDim.x / G;
+    const int g = threadIdx.x % G, slot = threadIdx.x / G;
+    const int Ho = H / 2, Wo = W / 2;
+    const long long total = (long long)B * H * W;
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+    if (slot < slots) {
+        for (long long p = (long long)blockIdx.x * slots + slot; p < total; p += (long long)gridDim.x * slots) {
+            const int w = (int)(p % W), h = (int)((p / W) % H), b = (int)(p / ((long long)W * H));
+            uint4 outv = make_uint4(0, 0, 0, 0);
+            if ((h >> 1) < Ho && (w >> 1) < Wo) {
+                const size_t o = (((size_t)b * Ho + (h >> 1)) * Wo + (w >> 1)) * C + g * 8;
+                const uint2 cv = *reinterpret_cast<const uint2 *>(code + o);
+                const uint4 dv = *reinterpret_cast<const uint4 *>(dP + o);
+                const uint8_t *cb = reinterpret_cast<const uint8_t *>(&cv);
+                const bf16 *db = reinterpret_cast<const bf16 *>(&dv);
+                bf16 *ob = reinterpret_cast<bf16 *>(&outv);
+                const int pos = ((h & 1) << 1) | (w & 1);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const bool hit = (cb[e] & 3) == pos && (cb[e] & 4);
+                    const float v = hit ? __bfloat162float(db[e]) : 0.0f;
+                    ob[e] = __float2bfloat16_rn(v);
+                    acc[e] += v;
+                }
+            }
+            *reinterpret_cast<uint4 *>(dC + (size_t)p * C + g * 8) = outv;
+        }
+    }
+    extern __shared__ float red[];   // [blockDim.x][8]
+#pragma unroll
+    for (int e = 0; e < 8; ++e) red[threadIdx.x * 8 + e] = acc[e];
+    __syncthreads();
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const int gg = c / 8, e = c % 8;
+        float s = 0.0f;
+        for (int sl = 0; sl < slots; ++sl) s += red[(sl * G + gg) * 8 + e];
+        bias_partial[(size_t)blockIdx.x * C + c] = s;
+    }
+}
+
+// Head: last Linear (Hd -> NC, NC <= 32) + softmax cross-entropy + the start
+// of the backward, one warp per row:
+//   z = a W + b;  loss_r = -log softmax(z)[y];  dz = (p - onehot)/B
+//   dA = dz W^T times (a > 0) (ReLU of the previous Linear) -> bf16
+// Block partials (fixed warp order): dW [Hd][NC], db [NC], dbPrev [Hd].
+template <int HD, int NC>
+__global__ void __launch_bounds__(256) head_kernel(const bf16 *__restrict__ a, const float *__restrict__ Wt,
+                                                   const float *__restrict__ bias, const float *__restrict__ y,
+                                                   bf16 *__restrict__ dA, double *__restrict__ row_loss,
+                                                   float *__restrict__ partial, int B, float invB) {
+    constexpr int KPL = HD / 32;   // inputs per lane
+    __shared__ float sW[HD * NC];
+    __shared__ float sAcc[HD * NC + NC + HD];
+    for (int i = threadIdx.x; i < HD * NC; i += blockDim.x) sW[i] = Wt[i];
+    for (int i = threadIdx.x; i < HD * NC + NC + HD; i += blockDim.x) sAcc[i] = 0.0f;
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float gW[KPL][NC], gB[NC], gP[KPL];
+#pragma unroll
+    for (int j = 0; j < KPL; ++j) {
+        gP[j] = 0.0f;
+#pragma unroll
+        for (int n = 0; n < NC; ++n) gW[j][n] = 0.0f;
+    }
+#pragma unroll
+    for (int n = 0; n < NC; ++n) gB[n] = 0.0f;
+    for (int r = blockIdx.x * 8 + warp; r < B; r += gridDim.x * 8) {
+        float av[KPL];
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) av[j] = __bfloat162float(a[(size_t)r * HD + lane + 32 * j]);
+        float z[NC];
+#pragma unroll
+        for (int n = 0; n < NC; ++n) {
+            float s = 0.0f;
+#pragma unroll
+            for (int j = 0; j < KPL; ++j) s = fmaf(av[j], sW[(lane + 32 * j) * NC + n], s);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            z[n] = s + bias[n];
+        }
+        float mx = z[0];
+#pragma unroll
+        for (int n = 1; n < NC; ++n) mx = fmaxf(mx, z[n]);
+        float se = 0.0f;
+#pragma unroll
+        for (int n = 0; n < NC; ++n) se += expf(z[n] - mx);
+        const int t = (int)y[r];
+        float dz[NC];
+#pragma unroll
+        for (int n = 0; n < NC; ++n) {
+            const float p = expf(z[n] - mx) / se;
+            dz[n] = (p - (n == t ? 1.0f : 0.0f)) * invB;
+            gB[n] += dz[n];
+        }
+        if (lane == 0) {
+            float pt = 0.0f;
+#pragma unroll
+            for (int n = 0; n < NC; ++n) if (n == t) pt = expf(z[n] - mx) / se;
+            row_loss[r] = -(double)logf(pt);
+        }
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) {
+            const int k = lane + 32 * j;
+            float g = 0.0f;
+#pragma unroll
+            for (int n = 0; n < NC; ++n) {
+                g = fmaf(dz[n], sW[k * NC + n], g);
+                gW[j][n] = fmaf(av[j], dz[n], gW[j][n]);
+            }
+            g = av[j] > 0.0f ? g : 0.0f;
+            gP[j] += g;
+            dA[(size_t)r * HD + k] = __float2bfloat16_rn(g);
+        }
+    }
+    for (int wv = 0; wv < 8; ++wv) {   // fixed warp order
+        if (warp == wv) {
+#pragma unroll
+            for (int j = 0; j < KPL; ++j) {
+                const int k = lane + 32 * j;
+#pragma unroll
+                for (int n = 0; n < NC; ++n) sAcc[k * NC + n] += gW[j][n];
+                sAcc[HD * NC + NC + k] += gP[j];
+            }
+            if (lane == 0)
+#pragma unroll
+                for (int n = 0; n < NC; ++n) sAcc[HD * NC + n] += gB[n];
+        }
+        __syncthreads();
+    }
+    float *dst = partial + (size_t)blockIdx.x * (HD * NC + NC + HD);
+    for (int i = threadIdx.x; i < HD * NC + NC + HD; i += blockDim.x) dst[i] = sAcc[i];
+}
+
+// Sums partial[s][i] over s in order and scatters into the gradient layout.
+// map 0: dst[i];  1 conv (M=COUT rows, N = 9*CIN, n = tap*CIN + ci) -> dst[(co*CIN+ci)*9+tap]
+//        2 conv (M = 9*CIN rows (tap*CIN+ci), N = COUT)  -> same dst layout
+//        3 linear (M = F rows in NHWC order, N = OUT)    -> dst[nchw(m)*OUT + n]
+//        4 head partial [HD*NC | NC | HD] -> dW5, db5, db4 (three destinations)
+//        5 first conv [COUT][10] -> dW1[co*9+t], db1[co]
+struct ReduceArgs {
+    const float *partial;
+    int splits;
+    long long n;       // elements per partial
+    int map, M, N, CIN, C, H, W;
+    float *dst, *dst2, *dst3;
+};
+
+__global__ void reduce_partials_kernel(ReduceArgs r) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < r.n;
+         i += (long long)gridDim.x * blockDim.x) {
+        float s = 0.0f;
+        for (int k = 0; k < r.splits; ++k) s += r.partial[(size_t)k * r.n + i];
+        const int m = (int)(i / r.N), n = (int)(i % r.N);
+        switch (r.map) {
+        case 0: r.dst[i] = s; break;
+        case 1: { const int tap = n / r.CIN, ci = n % r.CIN; r.dst[((size_t)m * r.CIN + ci) * 9 + tap] = s; break; }
+        case 2: { const int tap = m / r.CIN, ci = m % r.CIN; r.dst[((size_t)n * r.CIN + ci) * 9 + tap] = s; break; }
+        case 3: { const int c = m % r.C, hw = m / r.C; r.dst[((size_t)c * r.H * r.W + hw) * r.N + n] = s; break; }
+        case 4: {
+            const long long hdnc = (long long)r.M * r.N;
+            if (i < hdnc) r.dst[i] = s;
+            else if (i < hdnc + r.N) r.dst2[i - hdnc] = s;
+            else r.dst3[i - hdnc - r.N] = s;
+            break;
+        }
+        case 5: { const int co = (int)(i / 10), t = (int)(i % 10); if (t < 9) r.dst[co * 9 + t] = s; else r.dst2[co] = s; break; }
+        }
+    }
+}
+
+__global__ void loss_sum_kernel(const double *__restrict__ row_loss, int B, float *__restrict__ loss) {
+    __shared__ double part[256];
+    const int per = (B + blockDim.x - 1) / blockDim.x;
+    const int b0 = threadIdx.x * per, b1 = min(B, b0 + per);
+    double acc = 0.0;
+    for (int r = b0; r < b1; ++r) acc += row_loss[r];
+    part[threadIdx.x] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double tot = 0.0;
+        for (int i = 0; i < (int)blockDim.x; ++i) tot += part[i];
+        *loss = (float)tot;
+    }
+}
+
+}  // namespace
+
+// ====================================================================== engine
+using bf16 = __nv_bfloat16;
+
+struct ConvLayer {   // a tensor-core conv stage (conv + ReLU + pool)
+    int si;          // stage index
+    int CIN, COUT, H, W, R, tpi;
+    bf16 *wf = nullptr, *wd = nullptr;   // packed fwd / dgrad weights
+    bf16 *out = nullptr;                 // pooled output [B, H/2, W/2, COUT]
+    uint8_t *code = nullptr;
+    bf16 *dP = nullptr;                  // gradient w.r.t. the pooled output
+    bf16 *dC = nullptr;                  // gradient w.r.t. the conv output [B, H, W, COUT]
+    ConvTcParams fwd{}, dgrad{};
+    WgradTcParams wg{};
+    int wg_mode = 0, wg_grid = 0, wg_smem = 0;
+    float *wg_partial = nullptr;
+    float *bias_partial = nullptr;
+    int unpool_grid = 0;
+};
+
+struct TcEngine {
+    int B = 0;
+    // first conv
+    int c1_si = 0, C1 = 0, H0 = 0, W0 = 0, pad1 = 0, H1 = 0, W1 = 0;
+    bool c1_pool = false;
+    bf16 *a1 = nullptr;        // first conv output (pooled if c1_pool)
+    uint8_t *code1 = nullptr;
+    bf16 *dC1 = nullptr;       // gradient w.r.t. the first conv output [B, oH, oW, C1]
+    bf16 *dP1 = nullptr;       // gradient w.r.t. its pooled output (c1_pool)
+    float *c1_partial = nullptr;
+    int c1_wgrad_grid = 0;
+    float *c1_bias_partial = nullptr;
+    int c1_unpool_grid = 0;
+    std::vector<ConvLayer> convs;
+    // flattened activation geometry (NHWC) feeding the first Linear
+    int fC = 0, fH = 0, fW = 0, F = 0;
+    // hidden Linear (tensor cores) and head
+    bool has_hidden = false;
+    int hid_si = 0, HD = 0, head_si = 0, NC = 0;
+    bf16 *wT = nullptr, *wP = nullptr;   // hidden Linear packed W^T [HD][F], W [F][HD]
+    bf16 *a_hid = nullptr;               // [B][HD]
+    bf16 *dZ_hid = nullptr;              // [B][HD]
+    bf16 *dflat = nullptr;               // gradient w.r.t. the flattened activation [B][F]
+    GemmTcParams fc_fwd{}, fc_dgrad{};
+    WgradTcParams fc_wg{};
+    int fc_wg_grid = 0, fc_wg_smem = 0;
+    float *fc_partial = nullptr;
+    float *head_partial = nullptr;
+    int head_grid = 0;
+    double *row_loss = nullptr;
+    PackJobs pack{};
+    std::vector<void *> allocs;
+    // named intermediate tensors (zilla_net_inspect)
+    struct View { std::string name; const void *p; size_t n; int kind; };   // kind 0 bf16, 1 u8, 2 f32
+    std::vector<View> views;
+};
+
+namespace {
+
+template <class T>
+int dalloc(TcEngine &e, T **p, size_t count) {
+    if (cudaMalloc((void **)p, (count ? count : 1) * sizeof(T)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(kBadHandle, "tc engine: cudaMalloc of %zu bytes failed", count * sizeof(T));
+    }
+    e.allocs.push_back((void *)*p);
+    return kOk;
+}
+
+// ---------------------------------------------------------------- conv dispatch
+template <int CIN, int COUT, int EPI, int NS>
+int launch_conv(const ConvTcParams &p) {
+    using S = tc::ConvTcShape<CIN, COUT, NS, EPI == tc::kEpiPool>;
+    auto kern = tc::conv_tc_kernel<CIN, COUT, EPI, NS>;
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM) != cudaSuccess)
+            return check_cuda("conv_tc smem attribute");
+        attr = true;
+    }
+    // resident CTAs per SM: shared memory (227 KB) and TMEM (512 columns) bound it
+    int per_sm = (227 * 1024) / S::SMEM;
+    if (per_sm > (int)(512 / S::TMEM_COLS)) per_sm = 512 / S::TMEM_COLS;
+    if (per_sm < 1) per_sm = 1;
+    if (per_sm > 2) per_sm = 2;
+    const int slots = sm_count() * per_sm;
+    const int grid = p.num_tiles < slots ? p.num_tiles : slots;
+    kern<<<grid, 192, S::SMEM, stream()>>>(p);
+    ZB_LAUNCH_CHECK("conv_tc");
+    return kOk;
+}
+
+bool conv_shape_supported(int cin, int cout) {
+    return (cin == 32 && cout == 64) || (cin == 64 && cout == 128) || (cin == 16 && cout == 32);
+}
+
+int run_conv_fwd(const ConvLayer &L) {
+    if (L.CIN == 32 && L.COUT == 64) return launch_conv<32, 64, tc::kEpiPool, 6>(L.fwd);
+    if (L.CIN == 64 && L.COUT == 128) return launch_conv<64, 128, tc::kEpiPool, 3>(L.fwd);
+    if (L.CIN == 16 && L.COUT == 32) return launch_conv<16, 32, tc::kEpiPool, 8>(L.fwd);
+    return fail(kBadArg, "tc engine: no forward conv kernel for %d->%d", L.CIN, L.COUT);
+}
+
+int run_conv_dgrad(const ConvLayer &L) {
+    // dgrad convolves dY (COUT channels) into CIN outputs
+    if (L.CIN == 32 && L.COUT == 64) return launch_conv<64, 32, tc::kEpiDgrad, 6>(L.dgrad);
+    if (L.CIN == 64 && L.COUT == 128) return launch_conv<128, 64, tc::kEpiDgrad, 2>(L.dgrad);
+    if (L.CIN == 16 && L.COUT == 32) return launch_conv<32, 32, tc::kEpiDgrad, 8>(L.dgrad);
+    return fail(kBadArg, "tc engine: no dgrad conv kernel for %d->%d", L.CIN, L.COUT);
+}
+
+template <int MODE>
+int launch_wgrad(const WgradTcParams &p, int grid, int smem) {
+    auto kern = tc::wgrad_tc_kernel<MODE>;
+    static int attr = 0;
+    if (attr < smem) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return check_cuda("wgrad_tc smem attribute");
+        attr = smem;
+    }
+    kern<<<grid, 192, smem, stream()>>>(p);
+    ZB_LAUNCH_CHECK("wgrad_tc");
+    return kOk;
+}
+
+int run_wgrad(const WgradTcParams &p, int mode, int grid, int smem) {
+    if (mode == tc::kWgLinear) return launch_wgrad<tc::kWgLinear>(p, grid, smem);
+    if (mode == tc::kWgConvCo) return launch_wgrad<tc::kWgConvCo>(p, grid, smem);
+    return launch_wgrad<tc::kWgConvTap>(p, grid, smem);
+}
+
+template <int BN, int EPI, int NS>
+int launch_gemm(const GemmTcParams &p) {
+    using S = tc::GemmTcShape<BN, NS>;
+    auto kern = tc::gemm_tc_kernel<BN, EPI, NS>;
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM) != cudaSuccess)
+            return check_cuda("gemm_tc smem attribute");
+        attr = true;
+    }
+    const int tiles = p.m_tiles * p.n_tiles;
+    kern<<<tiles < sm_count() ? tiles : sm_count(), 192, S::SMEM, stream()>>>(p);
+    ZB_LAUNCH_CHECK("gemm_tc");
+    return kOk;
+}
+
+int reduce(const ReduceArgs &r) {
+    reduce_partials_kernel<<<grid_for(r.n, 256, 4), 256, 0, stream()>>>(r);
+    ZB_LAUNCH_CHECK("reduce_partials");
+    return kOk;
+}
+
+// ---------------------------------------------------------------- building
+int nhwc_map(CUtensorMap *m, const bf16 *base, int C, int W, int H, int B, int box_c, int box_w, int box_h) {
+    const uint64_t dims[4] = {(uint64_t)C, (uint64_t)W, (uint64_t)H, (uint64_t)B};
+    const uint64_t strides[3] = {(uint64_t)C * 2, (uint64_t)C * W * 2, (uint64_t)C * W * H * 2};
+    const uint32_t box[4] = {(uint32_t)box_c, (uint32_t)box_w, (uint32_t)box_h, 1};
+    const int rowb = box_c * 2;
+    return tc::make_tmap_bf16(m, base, 4, dims, strides, box,
+                              rowb == 128 ? tc::kSw128 : rowb == 64 ? tc::kSw64 : tc::kSw32);
+}
+
+int tc_build(Net &n, TcEngine &e) {
+    const int B = n.B;
+    e.B = B;
+    auto &st = n.st;
+    size_t i = 0;
+    // first conv: 1 input channel, CUDA cores
+    if (st.empty() || st[0].kind != kConv || st[0].C != 1 || !st[0].relu)
+        return fail(kBadArg, "tc engine: the first layer must be Conv2D(1 -> C) + ReLU");
+    e.c1_si = 0;
+    e.C1 = st[0].oC; e.H0 = st[0].H; e.W0 = st[0].W; e.pad1 = st[0].pad;
+    e.H1 = st[0].oH; e.W1 = st[0].oW;
+    if (e.C1 != 16 && e.C1 != 32) return fail(kBadArg, "tc engine: first conv must have 16 or 32 outputs");
+    i = 1;
+    e.c1_pool = i < st.size() && st[i].kind == kPool;
+    int C = e.C1, H = e.H1, W = e.W1;
+    if (e.c1_pool) { H = st[i].oH; W = st[i].oW; ++i; }
+    int rc;
+    if ((rc = dalloc(e, &e.a1, (size_t)B * H * W * C))) return rc;
+    if ((rc = dalloc(e, &e.dC1, (size_t)B * e.H1 * e.W1 * C))) return rc;
+    if (e.c1_pool) {
+        if ((rc = dalloc(e, &e.code1, (size_t)B * H * W * C))) return rc;
+        if ((rc = dalloc(e, &e.dP1, (size_t)B * H * W * C))) return rc;
+    }
+    // tensor-core conv stages
+    const bf16 *prev = e.a1;
+    while (i < st.size() && st[i].kind == kConv) {
+        Stage &s = st[i];
+        if (!s.relu || s.pad != 1 || i + 1 >= st.size() || st[i + 1].kind != kPool)
+            return fail(kBadArg, "tc engine: inner convs must be Conv2D(pad 1) + ReLU + MaxPool");
+        if (!conv_shape_supported(s.C, s.oC)) return fail(kBadArg, "tc engine: conv %d->%d not supported", s.C, s.oC);
+        ConvLayer L;
+        L.si = (int)i; L.CIN = s.C; L.COUT = s.oC; L.H = s.H; L.W = s.W;
+        if (L.W > 64) return fail(kBadArg, "tc engine: image width %d > 64", L.W);
+        L.R = (128 / L.W) & ~1;
+        L.tpi = (L.H + L.R - 1) / L.R;
+        const int Ho = L.H / 2, Wo = L.W / 2;
+        if ((rc = dalloc(e, &L.wf, (size_t)9 * L.CIN * L.COUT))) return rc;
+        if ((rc = dalloc(e, &L.wd, (size_t)9 * L.CIN * L.COUT))) return rc;
+        if ((rc = dalloc(e, &L.out, (size_t)B * Ho * Wo * L.COUT))) return rc;
+        if ((rc = dalloc(e, &L.code, (size_t)B * Ho * Wo * L.COUT))) return rc;
+        if ((rc = dalloc(e, &L.dP, (size_t)B * Ho * Wo * L.COUT))) return rc;
+        if ((rc = dalloc(e, &L.dC, (size_t)B * L.H * L.W * L.COUT))) return rc;
+        // forward: input = prev activations (CIN channels)
+        ConvTcParams &f = L.fwd;
+        const int chunk_f = L.CIN > 64 ? 64 : L.CIN;
+        if ((rc = nhwc_map(&f.in_map, prev, L.CIN, L.W, L.H, B, chunk_f, L.W, L.R))) return rc;
+        {
+            const uint64_t dims[3] = {(uint64_t)L.CIN, (uint64_t)L.COUT, 9};
+            const uint64_t strides[2] = {(uint64_t)L.CIN * 2, (uint64_t)L.CIN * L.COUT * 2};
+            const uint32_t box[3] = {(uint32_t)chunk_f, (uint32_t)L.COUT, 1};
+            if ((rc = tc::make_tmap_bf16(&f.w_map, L.wf, 3, dims, strides, box,
+                                         chunk_f * 2 == 128 ? tc::kSw128 : chunk_f * 2 == 64 ? tc::kSw64 : tc::kSw32)))
+                return rc;
+        }
+        f.B = B; f.H = L.H; f.W = L.W; f.R = L.R; f.tiles_per_img = L.tpi; f.num_tiles = B * L.tpi;
+        f.bias = n.params + s.poff + s.pn_w;
+        f.out = L.out; f.code = L.code; f.mask = nullptr; f.err = device_error_word();
+        // dgrad: input = dC (COUT channels), output CIN channels, masked by prev > 0
+        ConvTcParams &d = L.dgrad;
+        const int chunk_d = L.COUT > 64 ? 64 : L.COUT;
+        if ((rc = nhwc_map(&d.in_map, L.dC, L.COUT, L.W, L.H, B, chunk_d, L.W, L.R))) return rc;
+        {
+            const uint64_t dims[3] = {(uint64_t)L.COUT, (uint64_t)L.CIN, 9};
+            const uint64_t strides[2] = {(uint64_t)L.COUT * 2, (uint64_t)L.CIN * L.COUT * 2};
+            const uint32_t box[3] = {(uint32_t)chunk_d, (uint32_t)L.CIN, 1};
+            if ((rc = tc::make_tmap_bf16(&d.w_map, L.wd, 3, dims, strides, box,
+                                         chunk_d * 2 == 128 ? tc::kSw128 : chunk_d * 2 == 64 ? tc::kSw64 : tc::kSw32)))
+                return rc;
+        }
+        d.B = B; d.H = L.H; d.W = L.W; d.R = L.R; d.tiles_per_img = L.tpi; d.num_tiles = B * L.tpi;
+        d.bias = nullptr; d.code = nullptr; d.err = device_error_word();
+        // output of dgrad: gradient w.r.t. the previous activation
+        const bool prev_is_first = L.si == (e.c1_pool ? 2 : 1);
+        if (prev_is_first) {
+            d.out = e.c1_pool ? e.dP1 : e.dC1;
+            d.mask = e.c1_pool ? nullptr : e.a1;   // ReLU of conv1 (pooled: handled by unpool codes)
+        } else {
+            d.out = e.convs.back().dP;
+            d.mask = nullptr;                      // handled by that layer's unpool codes
+        }
+        // weight gradient
+        WgradTcParams &g = L.wg;
+        g.K_total = B; g.H = L.H; g.W = L.W; g.R = L.R; g.tiles_per_img = L.tpi;
+        g.kstage_rows = L.R * L.W; g.err = device_error_word();
+        if (L.COUT == 128 && L.CIN == 64) {
+            L.wg_mode = tc::kWgConvCo;
+            if ((rc = nhwc_map(&g.a_map, L.dC, L.COUT, L.W, L.H, B, 64, L.W, L.R))) return rc;
+            if ((rc = nhwc_map(&g.b_map, prev, L.CIN, L.W, L.H, B, 64, L.W, L.R))) return rc;
+            g.m_tiles = 3; g.M = L.COUT; g.N = 9 * L.CIN;
+            g.splits = (sm_count() / 3) > 0 ? sm_count() / 3 : 1;
+            L.wg_smem = tc::WgradTcShape<tc::kWgConvCo>::smem(g.kstage_rows);
+        } else if (L.CIN == 32 && L.COUT == 64) {
+            L.wg_mode = tc::kWgConvTap;
+            if ((rc = nhwc_map(&g.a_map, prev, L.CIN, L.W, L.H, B, 32, L.W, L.R))) return rc;
+            if ((rc = nhwc_map(&g.b_map, L.dC, L.COUT, L.W, L.H, B, 64, L.W, L.R))) return rc;
+            g.m_tiles = 1; g.M = 9 * L.CIN; g.N = L.COUT;
+            g.splits = sm_count();
+            L.wg_smem = tc::WgradTcShape<tc::kWgConvTap>::smem(g.kstage_rows);
+        } else {
+            return fail(kBadArg, "tc engine: no weight-gradient kernel for %d->%d", L.CIN, L.COUT);
+        }
+        if (g.splits > B) g.splits = B;
+        g.mode = L.wg_mode;
+        L.wg_grid = g.m_tiles * g.splits;
+        if ((rc = dalloc(e, &L.wg_partial, (size_t)g.splits * g.M * g.N))) return rc;
+        L.wg.partial = L.wg_partial;
+        L.unpool_grid = sm_count() * 4;
+        if ((rc = dalloc(e, &L.bias_partial, (size_t)L.unpool_grid * L.COUT))) return rc;
+        e.convs.push_back(L);
+        prev = L.out;
+        C = L.COUT; H = Ho; W = Wo;
+        i += 2;
+    }
+    e.fC = C; e.fH = H; e.fW = W; e.F = C * H * W;
+    // Linear layers
+    if (i < st.size() && st[i].kind == kLinear && st[i].relu) {
+        Stage &s = st[i];
+        e.has_hidden = true;
+        e.hid_si = (int)i;
+        e.HD = s.oC;
+        if (e.F % 64 || e.HD % 64 || e.HD > 256)
+            return fail(kBadArg, "tc engine: hidden Linear %d->%d not supported", e.F, e.HD);
+        if ((rc = dalloc(e, &e.wT, (size_t)e.F * e.HD))) return rc;
+        if ((rc = dalloc(e, &e.wP, (size_t)e.F * e.HD))) return rc;
+        if ((rc = dalloc(e, &e.a_hid, (size_t)B * e.HD))) return rc;
+        if ((rc = dalloc(e, &e.dZ_hid, (size_t)B * e.HD))) return rc;
+        if ((rc = dalloc(e, &e.dflat, (size_t)B * e.F))) return rc;
+        // forward: A = flattened activation [B][F], B = W^T [HD][F]
+        GemmTcParams &g = e.fc_fwd;
+        {
+            const uint64_t da[2] = {(uint64_t)e.F, (uint64_t)B}, sa[1] = {(uint64_t)e.F * 2};
+            const uint32_t ba[2] = {64, 128};
+            if ((rc = tc::make_tmap_bf16(&g.a_map, prev, 2, da, sa, ba, tc::kSw128))) return rc;
+            const uint64_t db[2] = {(uint64_t)e.F, (uint64_t)e.HD}, sb[1] = {(uint64_t)e.F * 2};
+            const uint32_t bb[2] = {64, (uint32_t)e.HD};
+            if ((rc = tc::make_tmap_bf16(&g.b_map, e.wT, 2, db, sb, bb, tc::kSw128))) return rc;
+        }
+        g.M = B; g.N = e.HD; g.K = e.F; g.m_tiles = (B + 127) / 128; g.n_tiles = 1;
+        g.bias = n.params + s.poff + s.pn_w; g.out = e.a_hid; g.err = device_error_word();
+        // input gradient: A = dZ [B][HD], B = W [F][HD] -> dflat [B][F], N tile 224/256/128
+        GemmTcParams &dg = e.fc_dgrad;
+        int bn = 0;
+        for (int cand : {256, 224, 192, 160, 128, 96, 64})
+            if (e.F % cand == 0) { bn = cand; break; }
+        if (bn != 224 && bn != 256 && bn != 128) return fail(kBadArg, "tc engine: Linear input size %d", e.F);
+        {
+            const uint64_t da[2] = {(uint64_t)e.HD, (uint64_t)B}, sa[1] = {(uint64_t)e.HD * 2};
+            const uint32_t ba[2] = {64, 128};
+            if ((rc = tc::make_tmap_bf16(&dg.a_map, e.dZ_hid, 2, da, sa, ba, tc::kSw128))) return rc;
+            const uint64_t db[2] = {(uint64_t)e.HD, (uint64_t)e.F}, sb[1] = {(uint64_t)e.HD * 2};
+            const uint32_t bb[2] = {64, (uint32_t)bn};
+            if ((rc = tc::make_tmap_bf16(&dg.b_map, e.wP, 2, db, sb, bb, tc::kSw128))) return rc;
+        }
+        dg.M = B; dg.N = e.F; dg.K = e.HD; dg.m_tiles = (B + 127) / 128; dg.n_tiles = e.F / bn;
+        dg.bias = nullptr; dg.out = e.dflat; dg.err = device_error_word();
+        // weight gradient: A = flattened activation (MN-major), B = dZ
+        WgradTcParams &w = e.fc_wg;
+        {
+            const uint64_t da[2] = {(uint64_t)e.F, (uint64_t)B}, sa[1] = {(uint64_t)e.F * 2};
+            const uint32_t ba[2] = {64, 64};
+            if ((rc = tc::make_tmap_bf16(&w.a_map, prev, 2, da, sa, ba, tc::kSw128))) return rc;
+            const uint64_t db[2] = {(uint64_t)e.HD, (uint64_t)B}, sb[1] = {(uint64_t)e.HD * 2};
+            const uint32_t bb[2] = {64, 64};
+            if ((rc = tc::make_tmap_bf16(&w.b_map, e.dZ_hid, 2, db, sb, bb, tc::kSw128))) return rc;
+        }
+        if (e.HD != 256) return fail(kBadArg, "tc engine: hidden Linear width must be 256");
+        w.mode = tc::kWgLinear; w.K_total = B; w.m_tiles = e.F / 128; w.M = e.F; w.N = e.HD;
+        if (e.F % 128) return fail(kBadArg, "tc engine: Linear input %d not a multiple of 128", e.F);
+        w.splits = (sm_count() + w.m_tiles - 1) / w.m_tiles;
+        if (w.splits > (B + 63) / 64) w.splits = (B + 63) / 64;
+        w.kstage_rows = 64; w.err = device_error_word();
+        e.fc_wg_grid = w.m_tiles * w.splits;
+        e.fc_wg_smem = tc::WgradTcShape<tc::kWgLinear>::smem(64);
+        if ((rc = dalloc(e, &e.fc_partial, (size_t)w.splits * e.F * e.HD))) return rc;
+        w.partial = e.fc_partial;
+        ++i;
+    }
+    if (i + 1 != st.size() || st[i].kind != kLinear || st[i].relu)
+        return fail(kBadArg, "tc engine: the network must end with Linear(-> classes)");
+    e.head_si = (int)i;
+    e.NC = st[i].oC;
+    if (!e.has_hidden) return fail(kBadArg, "tc engine: a hidden Linear + ReLU before the classifier is required");
+    if (e.HD != 256 || e.NC != 10) return fail(kBadArg, "tc engine: head %d->%d not supported", e.HD, e.NC);
+    e.head_grid = sm_count() * 2;
+    if ((rc = dalloc(e, &e.head_partial, (size_t)e.head_grid * (e.HD * e.NC + e.NC + e.HD)))) return rc;
+    if ((rc = dalloc(e, &e.row_loss, (size_t)B))) return rc;
+    e.c1_wgrad_grid = sm_count() * 2;
+    if ((rc = dalloc(e, &e.c1_partial, (size_t)e.c1_wgrad_grid * e.C1 * 10))) return rc;
+    // diagnostics
+    e.views.push_back({"conv1.out", e.a1, (size_t)B * (e.c1_pool ? (e.H1 / 2) * (e.W1 / 2) : e.H1 * e.W1) * e.C1, 0});
+    e.views.push_back({"conv1.dC", e.dC1, (size_t)B * e.H1 * e.W1 * e.C1, 0});
+    for (size_t k = 0; k < e.convs.size(); ++k) {
+        const ConvLayer &L = e.convs[k];
+        const std::string pre = "conv" + std::to_string(k + 2);
+        const size_t np = (size_t)B * (L.H / 2) * (L.W / 2) * L.COUT;
+        e.views.push_back({pre + ".out", L.out, np, 0});
+        e.views.push_back({pre + ".code", L.code, np, 1});
+        e.views.push_back({pre + ".dP", L.dP, np, 0});
+        e.views.push_back({pre + ".dC", L.dC, (size_t)B * L.H * L.W * L.COUT, 0});
+        e.views.push_back({pre + ".wf", L.wf, (size_t)9 * L.CIN * L.COUT, 0});
+        e.views.push_back({pre + ".wd", L.wd, (size_t)9 * L.CIN * L.COUT, 0});
+    }
+    e.views.push_back({"hidden.out", e.a_hid, (size_t)B * e.HD, 0});
+    e.views.push_back({"hidden.dZ", e.dZ_hid, (size_t)B * e.HD, 0});
+    e.views.push_back({"flat.d", e.dflat, (size_t)B * e.F, 0});
+    e.views.push_back({"hidden.wT", e.wT, (size_t)e.F * e.HD, 0});
+    e.views.push_back({"hidden.wP", e.wP, (size_t)e.F * e.HD, 0});
+    // weight packing jobs
+    PackJobs &pj = e.pack;
+    pj.count = 0;
+    for (auto &L : e.convs) {
+        const Stage &s = st[L.si];
+        pj.j[pj.count++] = {0, n.params + s.poff, L.wf, L.COUT, L.CIN, 0, 0, 0, (long long)9 * L.CIN * L.COUT};
+        pj.j[pj.count++] = {1, n.params + s.poff, L.wd, L.COUT, L.CIN, 0, 0, 0, (long long)9 * L.CIN * L.COUT};
+    }
+    {
+        const Stage &s = st[e.hid_si];
+        pj.j[pj.count++] = {2, n.params + s.poff, e.wT, e.F, e.HD, e.fC, e.fH, e.fW, (long long)e.F * e.HD};
+        pj.j[pj.count++] = {3, n.params + s.poff, e.wP, e.F, e.HD, e.fC, e.fH, e.fW, (long long)e.F * e.HD};
+    }
+    return kOk;
+}
+
+int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out) {
+    const int B = e.B;
+    auto &st = n.st;
+    int rc;
+    // ---- pack bf16 operands from the fp32 master
+    pack_kernel<<<sm_count() * 4, 256, 0, stream()>>>(e.pack);
+    ZB_LAUNCH_CHECK("pack");
+    prof_mark(n, "pack");
+    // ---- forward
+    const Stage &s1 = st[e.c1_si];
+    const float *w1 = n.params + s1.poff, *b1 = w1 + s1.pn_w;
+    {
+        const long long pix = (long long)B * (e.c1_pool ? (e.H1 / 2) * (e.W1 / 2) : e.H1 * e.W1);
+        const int grid = grid_for(pix, 128, 8);
+        if (e.C1 == 32 && !e.c1_pool) conv_first_fwd_kernel<32, false><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, nullptr, B, e.H0, e.W0, e.pad1);
+        else if (e.C1 == 32) conv_first_fwd_kernel<32, true><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
+        else if (!e.c1_pool) conv_first_fwd_kernel<16, false><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, nullptr, B, e.H0, e.W0, e.pad1);
+        else conv_first_fwd_kernel<16, true><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
+        ZB_LAUNCH_CHECK("conv_first_fwd");
+        prof_mark(n, "conv_fwd");
+    }
+    for (auto &L : e.convs) {
+        if ((rc = run_conv_fwd(L))) return rc;
+        prof_mark(n, "conv_fwd");
+    }
+    if ((rc = launch_gemm<256, tc::kGemmBiasRelu, 4>(e.fc_fwd))) return rc;
+    prof_mark(n, "linear_fwd");
+    // ---- head: classifier, loss, start of the backward
+    const Stage &sh = st[e.head_si];
+    float *gW5 = n.grads + sh.poff, *gb5 = gW5 + sh.pn_w;
+    const Stage &sd = st[e.hid_si];
+    float *gW4 = n.grads + sd.poff, *gb4 = gW4 + sd.pn_w;
+    head_kernel<256, 10><<<e.head_grid, 256, 0, stream()>>>(e.a_hid, n.params + sh.poff, n.params + sh.poff + sh.pn_w,
+                                                           y, e.dZ_hid, e.row_loss, e.head_partial, B, 1.0f / (float)B);
+    ZB_LAUNCH_CHECK("head");
+    loss_sum_kernel<<<1, 256, 0, stream()>>>(e.row_loss, B, loss_out);
+    ZB_LAUNCH_CHECK("loss_sum");
+    {
+        ReduceArgs r{e.head_partial, e.head_grid, (long long)e.HD * e.NC + e.NC + e.HD, 4, e.HD, e.NC, 0, 0, 0, 0,
+                     gW5, gb5, gb4};
+        if ((rc = reduce(r))) return rc;
+    }
+    prof_mark(n, "softmax_ce");
+    // ---- hidden Linear backward
+    {   // dflat = dZ W^T
+        const int bn = e.F / e.fc_dgrad.n_tiles;
+        rc = bn == 224 ? launch_gemm<224, tc::kGemmStore, 4>(e.fc_dgrad)
+             : bn == 256 ? launch_gemm<256, tc::kGemmStore, 4>(e.fc_dgrad)
+                         : launch_gemm<128, tc::kGemmStore, 4>(e.fc_dgrad);
+        if (rc) return rc;
+    }
+    if ((rc = run_wgrad(e.fc_wg, tc::kWgLinear, e.fc_wg_grid, e.fc_wg_smem))) return rc;
+    {
+        ReduceArgs r{e.fc_partial, e.fc_wg.splits, (long long)e.F * e.HD, 3, e.F, e.HD, 0, e.fC, e.fH, e.fW,
+                     gW4, nullptr, nullptr};
+        if ((rc = reduce(r))) return rc;
+    }
+    prof_mark(n, "linear_bwd");
+    // ---- conv stages backward (last to first)
+    const bf16 *dpooled = e.dflat;   // gradient w.r.t. the last pooled output
+    for (int li = (int)e.convs.size() - 1; li >= 0; --li) {
+        ConvLayer &L = e.convs[li];
+        const Stage &s = st[L.si];
+        const bf16 *dP = (li == (int)e.convs.size() - 1) ? dpooled : L.dP;
+        const int G = L.COUT / 8, slots = 256 / G;
+        unpool_kernel<<<L.unpool_grid, slots * G, slots * G * 8 * sizeof(float), stream()>>>(
+            dP, L.code, L.dC, L.bias_partial, B, L.H, L.W, L.COUT);
+        ZB_LAUNCH_CHECK("unpool");
+        {
+            ReduceArgs r{L.bias_partial, L.unpool_grid, (long long)L.COUT, 0, 1, L.COUT, 0, 0, 0, 0,
+                         n.grads + s.poff + s.pn_w, nullptr, nullptr};
+            if ((rc = reduce(r))) return rc;
+        }
+        prof_mark(n, "pool_bwd");
+        if ((rc = run_conv_dgrad(L))) return rc;
+        if ((rc = run_wgrad(L.wg, L.wg_mode, L.wg_grid, L.wg_smem))) return rc;
+        {
+            ReduceArgs r{L.wg_partial, L.wg.splits, (long long)L.wg.M * L.wg.N,
+                         L.wg_mode == tc::kWgConvCo ? 1 : 2, L.wg.M, L.wg.N, L.CIN, 0, 0, 0,
+                         n.grads + s.poff, nullptr, nullptr};
+            if ((rc = reduce(r))) return rc;
+        }
+        prof_mark(n, "conv_bwd");
+    }
+    // ---- first conv backward (dC1 written by the next conv's dgrad, masked)
+    if (e.c1_pool) {
+        const int G = e.C1 / 8, slots = 256 / G;
+        unpool_kernel<<<sm_count() * 4, slots * G, slots * G * 8 * sizeof(float), stream()>>>(
+            e.dP1, e.code1, e.dC1, e.c1_partial /*scratch*/, B, e.H1, e.W1, e.C1);
+        ZB_LAUNCH_CHECK("unpool first");
+    }
+    if (e.C1 == 32) conv_first_wgrad_kernel<32><<<e.c1_wgrad_grid, 256, 0, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
+    else conv_first_wgrad_kernel<16><<<e.c1_wgrad_grid, 256, 0, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
+    ZB_LAUNCH_CHECK("conv_first_wgrad");
+    {
+        ReduceArgs r{e.c1_partial, e.c1_wgrad_grid, (long long)e.C1 * 10, 5, e.C1, 10, 0, 0, 0, 0,
+                     n.grads + s1.poff, n.grads + s1.poff + s1.pn_w, nullptr};
+        if ((rc = reduce(r))) return rc;
+    }
+    prof_mark(n, "conv_bwd");
+    return kOk;
+}
+
+}  // namespace
 
 int tc_create(Net &n) {
-    (void)n;
-    return fail(kBadArg, "zilla_net_create: precision 1 (tcgen05) engine not built yet");
+    TcEngine *e = new TcEngine();
+    int rc = tc_build(n, *e);
+    if (rc) {
+        for (void *p : e->allocs) cudaFree(p);
+        delete e;
+        return rc;
+    }
+    n.tc = e;
+    return kOk;
 }
-void tc_destroy(Net &n) { n.tc = nullptr; }
-int tc_step(Net &n, const float *, const float *, float *) { (void)n; return kBadArg; }
-int tc_sync_params(Net &n) { (void)n; return kOk; }
+
+void tc_destroy(Net &n) {
+    if (!n.tc) return;
+    cudaStreamSynchronize(stream());
+    for (void *p : n.tc->allocs) cudaFree(p);
+    delete n.tc;
+    n.tc = nullptr;
+}
+
+int tc_step(Net &n, const float *x, const float *y, float *loss_out) {
+    if (!n.tc) return fail(kBadArg, "tc engine missing");
+    int rc = tc_run(n, *n.tc, x, y, loss_out);
+    if (rc) return rc;
+    return kOk;
+}
+
+int tc_sync_params(Net &n) {
+    (void)n;
+    return kOk;
+}
+
+__global__ void widen_kernel(const void *src, int kind, float *dst, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        if (kind == 0) dst[i] = __bfloat162float(reinterpret_cast<const bf16 *>(src)[i]);
+        else if (kind == 1) dst[i] = (float)reinterpret_cast<const uint8_t *>(src)[i];
+        else dst[i] = reinterpret_cast<const float *>(src)[i];
+    }
+}
+
+int tc_inspect(Net &n, int index, char *name, int name_len, float *host, unsigned long n_floats) {
+    if (!n.tc || index < 0 || index >= (int)n.tc->views.size()) return 0;
+    const auto &v = n.tc->views[index];
+    if (name && name_len > 0) {
+        strncpy(name, v.name.c_str(), (size_t)name_len - 1);
+        name[name_len - 1] = 0;
+    }
+    if (host && n_floats) {
+        const size_t cnt = n_floats < v.n ? n_floats : v.n;
+        float *tmp = nullptr;
+        if (cudaMalloc((void **)&tmp, cnt * sizeof(float)) != cudaSuccess) { cudaGetLastError(); return kBadHandle; }
+        widen_kernel<<<grid_for((long long)cnt, 256, 4), 256, 0, stream()>>>(v.p, v.kind, tmp, cnt);
+        cudaMemcpyAsync(host, tmp, cnt * sizeof(float), cudaMemcpyDeviceToHost, stream());
+        cudaStreamSynchronize(stream());
+        cudaFree(tmp);
+        int rc = check_cuda("zilla_net_inspect");
+        if (rc) return rc;
+    }
+    return (int)v.n;
+}
 
 }  // namespace zb

@@ -83,6 +83,8 @@ SIGNATURES: dict[str, tuple] = {
     "zilla_net_step_host": (I, [I, FP, FP, FP, I]),
     "zilla_net_profile": (I, [I, I]),
     "zilla_net_timings": (I, [I, C.c_char_p, I, FP, I]),
+    "zilla_net_inspect": (I, [I, I, C.c_char_p, I, FP, UL]),
+    "zilla_net_device_status": (I, [I]),
     "zilla_dp_unique_id": (I, [C.c_char_p]),
     "zilla_dp_attach": (I, [I, I, I, C.c_char_p]),
     "zilla_dp_detach": (I, [I]),

@@ -82,6 +82,25 @@ class Net:
         names = labels.value.decode().split("\n")[:k]
         return list(zip(names, ms[:k].tolist()))
 
+    def device_status(self) -> None:
+        """Raises if a kernel recorded an error (expired bounded wait, bad index)."""
+        self._check(self.lib.zilla_net_device_status(self.id))
+
+    def inspect(self) -> dict[str, np.ndarray]:
+        """Intermediate tensors of the tensor-core engine (diagnostics), by name."""
+        out, i = {}, 0
+        while True:
+            name = C.create_string_buffer(64)
+            n = self.lib.zilla_net_inspect(self.id, i, name, 64, None, 0)
+            if n <= 0:
+                break
+            buf = np.empty(n, np.float32)
+            self._check(0 if self.lib.zilla_net_inspect(self.id, i, name, 64, buf.ctypes.data_as(native.FP), n) == n
+                        else -3)
+            out[name.value.decode()] = buf
+            i += 1
+        return out
+
     def dp_attach(self, rank: int, world: int, uid: bytes) -> None:
         self._check(self.lib.zilla_dp_attach(self.id, rank, world, uid))
 

@@ -269,8 +269,13 @@ def main():
     ap.add_argument("--workload", default="large_cnn", choices=sorted(configs.WORKLOADS))
     ap.add_argument("--precision", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="global batch override (small cases for ncu captures; default: the workload's)")
     args = ap.parse_args()
     w = configs.WORKLOADS[args.workload]
+    if args.batch:
+        import dataclasses
+        w = dataclasses.replace(w, batch=args.batch)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -304,7 +309,10 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     lib = native.load()
-    stream = torch.cuda.current_stream()
+    # one non-default stream shared by the library and the timing events
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    assert stream.cuda_stream != 0
     lib.zilla_set_stream(stream.cuda_stream)
 
     precision = w.precision if args.precision is None else args.precision

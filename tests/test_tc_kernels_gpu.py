@@ -1,0 +1,157 @@
+"""Kernel-level parity of the bf16 tcgen05 engine (GPU).
+
+Every contraction of the large-CNN step is recomputed in float64 from the
+engine's own inputs (its bf16 intermediates, read through zilla_net_inspect),
+so the only remaining difference is fp32 accumulation / bf16 output rounding:
+  bf16 outputs (activation gradients)     normwise <= 1e-2
+  fp32 outputs (weight / bias gradients)  normwise <= 2e-3
+  unpool routing (argmax + ReLU codes)    exact
+End-to-end differences against the fp32 oracle come on top of this from
+ReLU-mask and max-pool decisions that bf16 rounding flips near ties; those
+are checked in test_tc_gpu.py.
+"""
+import numpy as np
+import pytest
+
+import npref
+from zillaphp_b200 import configs, synthetic
+from zillaphp_b200.net import Net
+
+pytestmark = pytest.mark.gpu
+B = 16
+
+
+def bf16(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).float().numpy().astype(np.float64)
+
+
+def shift(x, dh, dw):
+    """x[b, h + dh - 1, w + dw - 1, c] with zero padding (NHWC)."""
+    Bn, H, W, C = x.shape
+    xp = np.pad(x, ((0, 0), (1, 1), (1, 1), (0, 0)))
+    return xp[:, dh:dh + H, dw:dw + W, :]
+
+
+def conv_fwd(x, Wt):           # Wt [co][ci][3][3]
+    return sum(np.einsum("bhwc,oc->bhwo", shift(x, dh, dw), Wt[:, :, dh, dw]) for dh in range(3) for dw in range(3))
+
+
+def conv_dgrad(dy, Wt):        # dx[b,i,j,ci] = sum dy[b, i-dh+1, j-dw+1, co] W[co,ci,dh,dw]
+    return sum(np.einsum("bhwo,oc->bhwc", shift(dy, 2 - dh, 2 - dw), Wt[:, :, dh, dw])
+               for dh in range(3) for dw in range(3))
+
+
+def conv_wgrad(x, dy):         # dW[co,ci,dh,dw]
+    out = np.zeros((dy.shape[3], x.shape[3], 3, 3))
+    for dh in range(3):
+        for dw in range(3):
+            out[:, :, dh, dw] = np.einsum("bhwo,bhwc->oc", dy, shift(x, dh, dw))
+    return out
+
+
+def unpool(dp, code, H, W):
+    Bn, Ho, Wo, C = dp.shape
+    out = np.zeros((Bn, H, W, C))
+    for ph in (0, 1):
+        for pw in (0, 1):
+            hit = ((code & 3) == (ph * 2 + pw)) & ((code & 4) != 0)
+            out[:, ph:2 * Ho:2, pw:2 * Wo:2, :] = np.where(hit, dp, 0.0)
+    return out
+
+
+@pytest.fixture(scope="module")
+def step():
+    w = configs.CNN_LARGE
+    p0 = synthetic.init_params(w, seed=33)
+    x, y = synthetic.batch(w, B, seed=33)
+    net = Net(w, batch=B, precision=1)
+    net.set_params(p0)
+    net.step_host(x, y, update=False)
+    net.device_status()
+    v = {k: a.astype(np.float64) for k, a in net.inspect().items()}
+    g = net.grads().astype(np.float64)
+    net.close()
+    # parameter views (Sequential order)
+    P = {}
+    off = 0
+    for li, (kind, a, b, _) in enumerate(w.layers):
+        if kind == configs.CONV:
+            P[f"W{li}"] = (off, (b, a, 3, 3)); off += b * a * 9
+            P[f"b{li}"] = (off, (b,)); off += b
+        elif kind == configs.LINEAR:
+            P[f"W{li}"] = (off, (a, b)); off += a * b
+            P[f"b{li}"] = (off, (b,)); off += b
+    par = {k: p0[o:o + int(np.prod(s))].reshape(s).astype(np.float64) for k, (o, s) in P.items()}
+    grd = {k: g[o:o + int(np.prod(s))].reshape(s) for k, (o, s) in P.items()}
+    return dict(x=x.astype(np.float64).reshape(B, 28, 28, 1), y=y.astype(int), v=v, par=par, grd=grd)
+
+
+def check(name, got, ref, tol):
+    e = npref.normwise(got, ref)
+    print(f"{name}: normwise {e:.2e}")
+    assert e < tol, (name, e)
+
+
+def test_head(step):
+    v, par, grd = step["v"], step["par"], step["grd"]
+    a4 = v["hidden.out"].reshape(B, 256)
+    z = a4 @ par["W10"] + par["b10"]
+    p = np.exp(z - z.max(1, keepdims=True)); p /= p.sum(1, keepdims=True)
+    dz = p.copy(); dz[np.arange(B), step["y"]] -= 1; dz /= B
+    da = (dz @ par["W10"].T) * (a4 > 0)
+    check("head dA (bf16)", v["hidden.dZ"].reshape(B, 256), da, 1e-2)
+    check("dW fc2", grd["W10"], a4.T @ dz, 2e-3)
+    check("db fc2", grd["b10"], dz.sum(0), 2e-3)
+    check("db fc1", grd["b8"], da.sum(0), 2e-3)
+
+
+def test_fc1_backward(step):
+    v, par, grd = step["v"], step["par"], step["grd"]
+    dz4 = v["hidden.dZ"].reshape(B, 256)
+    p3 = v["conv3.out"].reshape(B, 7 * 7 * 128)                      # NHWC flatten
+    perm = np.arange(6272).reshape(128, 7, 7).transpose(1, 2, 0).ravel()   # NHWC pos -> NCHW row
+    W4 = bf16(par["W8"])                                             # [6272 (NCHW), 256]
+    check("fc1 dX (bf16)", v["flat.d"].reshape(B, 6272), dz4 @ W4[perm].T, 1e-2)
+    dW = np.zeros((6272, 256)); dW[perm] = p3.T @ dz4
+    check("fc1 dW", grd["W8"], dW, 2e-3)
+
+
+def test_conv_backward(step):
+    v, par, grd = step["v"], step["par"], step["grd"]
+    p2 = v["conv2.out"].reshape(B, 14, 14, 64)
+    a1 = v["conv1.out"].reshape(B, 28, 28, 32)
+    code3 = v["conv3.code"].reshape(B, 7, 7, 128).astype(np.int64)
+    code2 = v["conv2.code"].reshape(B, 14, 14, 64).astype(np.int64)
+    dC3 = unpool(v["flat.d"].reshape(B, 7, 7, 128), code3, 14, 14)
+    assert np.array_equal(v["conv3.dC"].reshape(B, 14, 14, 128), dC3), "unpool3 routing"
+    check("db conv3", grd["b5"], dC3.sum((0, 1, 2)), 2e-3)
+    check("conv3 dX (bf16)", v["conv2.dP"].reshape(B, 14, 14, 64), conv_dgrad(dC3, bf16(par["W5"])), 1e-2)
+    check("conv3 dW", grd["W5"], conv_wgrad(p2, dC3), 2e-3)
+    dC2 = unpool(v["conv2.dP"].reshape(B, 14, 14, 64), code2, 28, 28)
+    assert np.array_equal(v["conv2.dC"].reshape(B, 28, 28, 64), dC2), "unpool2 routing"
+    check("db conv2", grd["b2"], dC2.sum((0, 1, 2)), 2e-3)
+    check("conv2 dX*mask (bf16)", v["conv1.dC"].reshape(B, 28, 28, 32),
+          conv_dgrad(dC2, bf16(par["W2"])) * (a1 > 0), 1e-2)
+    check("conv2 dW", grd["W2"], conv_wgrad(a1, dC2), 2e-3)
+    dC1 = v["conv1.dC"].reshape(B, 28, 28, 32)
+    check("conv1 dW", grd["W0"], conv_wgrad(step["x"], dC1), 2e-3)
+    check("db conv1", grd["b0"], dC1.sum((0, 1, 2)), 2e-3)
+
+
+def test_forward_kernels(step):
+    v, par = step["v"], step["par"]
+    a1 = np.maximum(conv_fwd(step["x"], par["W0"]) + par["b0"], 0)
+    check("conv1 fwd (bf16)", v["conv1.out"].reshape(B, 28, 28, 32), a1, 1e-2)
+    a1b = v["conv1.out"].reshape(B, 28, 28, 32)
+    c2 = np.maximum(conv_fwd(a1b, bf16(par["W2"])) + par["b2"], 0)
+    win = np.stack([c2[:, dh::2, dw::2, :] for dh in (0, 1) for dw in (0, 1)], -1)
+    check("conv2 fwd+pool (bf16)", v["conv2.out"].reshape(B, 14, 14, 64), win.max(-1), 1e-2)
+    p2 = v["conv2.out"].reshape(B, 14, 14, 64)
+    c3 = np.maximum(conv_fwd(p2, bf16(par["W5"])) + par["b5"], 0)
+    win = np.stack([c3[:, dh::2, dw::2, :] for dh in (0, 1) for dw in (0, 1)], -1)
+    check("conv3 fwd+pool (bf16)", v["conv3.out"].reshape(B, 7, 7, 128), win.max(-1), 1e-2)
+    p3 = v["conv3.out"].reshape(B, 6272)
+    perm = np.arange(6272).reshape(128, 7, 7).transpose(1, 2, 0).ravel()
+    a4 = np.maximum(p3 @ bf16(par["W8"])[perm] + par["b8"], 0)
+    check("fc1 fwd (bf16)", v["hidden.out"].reshape(B, 256), a4, 1e-2)

@@ -31,7 +31,7 @@ __global__ void __launch_bounds__(kGThreads) simt_gemm_kernel(P p, float *__rest
     __shared__ float Bs[kGBK][kGBN + 4];
     const int tid = threadIdx.x;
     const int tx = tid & 15, ty = tid >> 4;
-    const int m0 = blockIdx.y * kGBM, n0 = blockIdx.x * kGBN;
+    const int m0 = blockIdx.x * kGBM, n0 = blockIdx.y * kGBN;   // M tiles on x (up to 2^31-1)
     const int kb = blockIdx.z * k_per_split;
     const int ke = min(p.K, kb + k_per_split);
 
@@ -145,7 +145,8 @@ int run_simt_gemm(const P &p, int splits, const char *what) {
         ws = gemm_workspace((size_t)splits * p.M * p.N);
         if (!ws) return fail(kBadHandle, "%s: split-K workspace allocation failed", what);
     }
-    dim3 grid((p.N + kGBN - 1) / kGBN, (p.M + kGBM - 1) / kGBM, splits);
+    if ((p.N + kGBN - 1) / kGBN > 65535 || splits > 65535) return fail(kBadArg, "%s: N too large", what);
+    dim3 grid((p.M + kGBM - 1) / kGBM, (p.N + kGBN - 1) / kGBN, splits);
     simt_gemm_kernel<P><<<grid, kGThreads, 0, stream()>>>(p, ws, kps);
     ZB_LAUNCH_CHECK(what);
     if (splits > 1) {

@@ -123,7 +123,8 @@ __global__ void pack_kernel(PackJobs jobs) {
 // First conv (CIN = 1, 3x3, stride 1, pad P) + bias + ReLU on CUDA cores,
 // NHWC bf16 output; with `pool`, 2x2 max-pool + codes instead (same rules as
 // the tensor-core epilogue).  One thread per output (or pooled) pixel, all
-// COUT channels.  The tap sum follows the reference order (bias first, then
+// COUT channels.  The tap sum runs in the reference order with fused
+// multiply-adds (the output is rounded to bf16 anyway) (bias first, then
 // kh, kw ascending).
 template <int COUT, bool POOL>
 __global__ void conv_first_fwd_kernel(const float *__restrict__ x, const float *__restrict__ w,
@@ -163,7 +164,7 @@ __global__ void conv_first_fwd_kernel(const float *__restrict__ x, const float *
                 for (int q = 0; q < NP; ++q) {
                     float acc = sb[co];
 #pragma unroll
-                    for (int t = 0; t < 9; ++t) acc = __fadd_rn(acc, __fmul_rn(patch[q][t], sw[co * 9 + t]));
+                    for (int t = 0; t < 9; ++t) acc = fmaf(patch[q][t], sw[co * 9 + t], acc);
                     acc = acc > 0.0f ? acc : 0.0f;
                     if (q == 0 || acc > best[e]) { best[e] = acc; pos[e] = q; }
                 }
@@ -185,31 +186,45 @@ __global__ void conv_first_fwd_kernel(const float *__restrict__ x, const float *
 }
 
 // First-conv weight and bias gradient: dW[co][t] = sum_p dC[p][co] x[p + t],
-// db[co] = sum_p dC[p][co].  Thread (pixel slot, co); per-block partials
-// [block][COUT][10] summed later in block order.
+// db[co] = sum_p dC[p][co].  A block walks whole images: the image (with a
+// zero halo) is staged in shared memory, thread (pixel lane, co) reads one
+// bf16 of dC per pixel (a warp reads a pixel's 32 channels, 64 contiguous
+// bytes) and keeps 10 accumulators.  Per-block partials [block][COUT][10]
+// are summed later in block order.  Dynamic shared memory: (H+2p)(W+2p) floats.
 template <int COUT>
-__global__ void conv_first_wgrad_kernel(const bf16 *__restrict__ dC, const float *__restrict__ x,
-                                        float *__restrict__ partial, int B, int H, int W, int pad) {
+__global__ void __launch_bounds__(256) conv_first_wgrad_kernel(const bf16 *__restrict__ dC,
+                                                               const float *__restrict__ x,
+                                                               float *__restrict__ partial, int B, int H, int W,
+                                                               int pad) {
     constexpr int SLOTS = 256 / COUT;
+    extern __shared__ float xs[];
     const int co = threadIdx.x % COUT, slot = threadIdx.x / COUT;
     const int oH = H + 2 * pad - 2, oW = W + 2 * pad - 2;
-    const long long total = (long long)B * oH * oW;
+    const int PH = H + 2 * pad, PW = W + 2 * pad;
     float acc[10];
 #pragma unroll
     for (int t = 0; t < 10; ++t) acc[t] = 0.0f;
-    for (long long p = (long long)blockIdx.x * SLOTS + slot; p < total; p += (long long)gridDim.x * SLOTS) {
-        const float g = __bfloat162float(dC[(size_t)p * COUT + co]);
-        const int ow = (int)(p % oW), oh = (int)((p / oW) % oH), b = (int)(p / ((long long)oW * oH));
+    for (int b = blockIdx.x; b < B; b += gridDim.x) {
+        __syncthreads();
         const float *xb = x + (size_t)b * H * W;
-#pragma unroll
-        for (int t = 0; t < 9; ++t) {
-            const int ih = oh - pad + t / 3, iw = ow - pad + t % 3;
-            const float xv = ((unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W) ? xb[ih * W + iw] : 0.0f;
-            acc[t] = fmaf(g, xv, acc[t]);
+        for (int i = threadIdx.x; i < PH * PW; i += blockDim.x) {
+            const int ih = i / PW - pad, iw = i % PW - pad;
+            xs[i] = ((unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W) ? xb[ih * W + iw] : 0.0f;
         }
-        acc[9] += g;
+        __syncthreads();
+        const bf16 *gb = dC + (size_t)b * oH * oW * COUT + co;
+#pragma unroll 4
+        for (int p = slot; p < oH * oW; p += SLOTS) {
+            const int oh = p / oW, ow = p - oh * oW;
+            const float g = __bfloat162float(gb[(size_t)p * COUT]);
+            const float *xr = xs + oh * PW + ow;
+#pragma unroll
+            for (int t = 0; t < 9; ++t) acc[t] = fmaf(g, xr[(t / 3) * PW + (t % 3)], acc[t]);
+            acc[9] += g;
+        }
     }
-    __shared__ float red[256][11];
+    __syncthreads();
+    float (*red)[11] = reinterpret_cast<float (*)[11]>(xs);   // reuse: 256 x 11 floats
 #pragma unroll
     for (int t = 0; t < 10; ++t) red[threadIdx.x][t] = acc[t];
     __syncthreads();
@@ -896,8 +911,13 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
             e.dP1, e.code1, e.dC1, e.c1_partial /*scratch*/, B, e.H1, e.W1, e.C1);
         ZB_LAUNCH_CHECK("unpool first");
     }
-    if (e.C1 == 32) conv_first_wgrad_kernel<32><<<e.c1_wgrad_grid, 256, 0, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
-    else conv_first_wgrad_kernel<16><<<e.c1_wgrad_grid, 256, 0, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
+    {
+        const int padded = (e.H0 + 2 * e.pad1) * (e.W0 + 2 * e.pad1);
+        const size_t smem = (size_t)(padded > 256 * 11 ? padded : 256 * 11) * sizeof(float);
+        if (smem > 48 * 1024) return fail(kBadArg, "tc engine: first-conv image too large for the weight-gradient kernel");
+        if (e.C1 == 32) conv_first_wgrad_kernel<32><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
+        else conv_first_wgrad_kernel<16><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
+    }
     ZB_LAUNCH_CHECK("conv_first_wgrad");
     {
         ReduceArgs r{e.c1_partial, e.c1_wgrad_grid, (long long)e.C1 * 10, 5, e.C1, 10, 0, 0, 0, 0,

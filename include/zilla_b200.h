@@ -132,6 +132,22 @@ unsigned long long zilla_launch_count(void);
 int adam_update_dev(int w_id, int g_id, int m_id, int v_id, float lr, float beta1, float beta2,
                     float eps, int t, int n);
 
+/* softmax_ce_dev for callers that cannot let a library allocate device memory
+ * (code under a caller-owned memory pool or budget, or a host that only hands
+ * over device pointers it already owns).  No counterpart in the reference.
+ * Same arithmetic and the same outputs as softmax_ce_dev, on raw device
+ * pointers and the caller's stream (NULL = the legacy default stream): dlogits
+ * = (softmax - onehot)/B, and the loss SUM over the rows is ADDED to *loss (the
+ * caller zeroes it).  It calls no cudaMalloc, cudaFree or allocating library
+ * routine: its per-row scratch is a file-scope static device array of 65536
+ * doubles (512 KB on every GPU that loads the library, held until exit), so
+ * B > 65536 is rejected with -2.  The first call on a device looks the array
+ * up with cudaGetSymbolAddress; make that first call before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU (other
+ * streams, other host threads) race and must be serialised by the caller. */
+int softmax_ce_noalloc(const float *logits, const float *targets, float *dlogits, float *loss,
+                       int B, int C, void *stream);
+
 /* ---- fused training step (replaces the ~30 per-op FFI calls of
  *      examples/mnist_cnn_gpu_v2.php:183-264 with one call) ----
  *

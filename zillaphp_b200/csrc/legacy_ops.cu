@@ -343,6 +343,55 @@ int launch_bias_grad(const float *dy, float *db, int B, int C) {
 
 }  // namespace zb
 
+// ---------------------------------------------------------------- allocation-free softmax-CE
+// softmax_ce_dev needs B doubles of scratch for its per-row losses and takes them from a
+// buffer the library allocates with cudaMalloc on first use.  Some callers cannot let a
+// library allocate device memory: code running under a caller-owned memory pool or budget,
+// or a caller that only hands over device pointers it already owns.  softmax_ce_noalloc
+// serves them: the per-row scratch is this fixed file-scope device array instead, reserved
+// when the library is loaded, so a call allocates nothing.  Every GPU that loads the
+// library holds the array (512 KB) until the process exits.
+namespace {
+
+constexpr int kNoAllocMaxRows = 65536;                                 // rows per call
+static __device__ __align__(256) double g_noalloc_row_loss[kNoAllocMaxRows];
+
+constexpr int kMaxDevices = 64;
+double *g_noalloc_ptr[kMaxDevices] = {};   // device address of the array, per device
+
+}  // namespace
+
+extern "C" int softmax_ce_noalloc(const float *logits, const float *targets, float *dlogits,
+                                  float *loss, int B, int C, void *stream_handle) {
+    if (!logits || !targets || !dlogits || !loss)
+        return fail(kBadHandle, "softmax_ce_noalloc: null device pointer");
+    if (B < 0 || C <= 0) return fail(kBadArg, "softmax_ce_noalloc: bad sizes B=%d C=%d", B, C);
+    if (B > kNoAllocMaxRows)
+        return fail(kBadArg, "softmax_ce_noalloc: B=%d exceeds the %d rows of its static scratch",
+                    B, kNoAllocMaxRows);
+    if (B == 0) return kOk;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+        return check_cuda("softmax_ce_noalloc: cudaGetDevice");
+    if (!g_noalloc_ptr[dev]) {   // set-up, once per device, with that device current
+        double *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress((void **)&p, g_noalloc_row_loss);
+        if (e != cudaSuccess || !p) {
+            cudaGetLastError();
+            return fail(kCudaError, "softmax_ce_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+        }
+        g_noalloc_ptr[dev] = p;
+    }
+    cudaStream_t s = (cudaStream_t)stream_handle;
+    // every row slot read by the sum is written first by the row kernel: nothing to clear
+    softmax_ce_rows_kernel<<<grid_for((long long)B * 32, kThreads), kThreads, 0, s>>>(
+        logits, targets, dlogits, g_noalloc_ptr[dev], B, C);
+    ZB_LAUNCH_CHECK("softmax_ce_noalloc");
+    sum_rows_into_loss_kernel<<<1, kThreads, 0, s>>>(g_noalloc_ptr[dev], B, loss);
+    ZB_LAUNCH_CHECK("softmax_ce_noalloc(sum)");
+    return kOk;
+}
+
 extern "C" {
 
 // ---- device_ops.cu:81-149 ----

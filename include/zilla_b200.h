@@ -124,6 +124,10 @@ int zilla_last_status(void);
 int zilla_set_stream(void *stream);
 /* Number of kernel launches this library issued so far (instrumentation). */
 unsigned long long zilla_launch_count(void);
+/* Synchronises the library stream and reports (then clears) a kernel-side
+ * error: -3 when a kernel skipped an out-of-range index (e.g. an argmax
+ * outside dX in maxpool2d_*_bwd_dev) or a bounded wait expired, else 0. */
+int zilla_check_device(void);
 
 /* Adam (src/Optim/Adam.php:36-62) over one flat tensor of n floats, fused in
  * one kernel: m = b1 m + (1-b1) g; v = b2 v + (1-b2) g^2;

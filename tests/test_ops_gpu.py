@@ -127,6 +127,8 @@ def test_maxpool_backward_rejects_out_of_range_argmax(be):
     be.maxPool2dBatchedBwdDev(igo, ia, igi, 1, 1, 2, 2)
     got = get(be, igi, 8)
     assert got.tolist() == [1, 0, 0, 1, 0, 0, 0, 1]          # index 1000000 skipped
+    assert be.ffi.zilla_check_device() == -3                 # ... and reported
+    assert be.ffi.zilla_check_device() == 0                  # read-and-clear
 
 
 @pytest.mark.parametrize("M,K,N", [(64, 784, 128), (64, 128, 10), (7, 33, 5), (300, 257, 65), (1, 1, 1)])

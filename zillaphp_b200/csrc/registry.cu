@@ -188,4 +188,11 @@ int zilla_set_stream(void *s) {
 
 unsigned long long zilla_launch_count(void) { return g_launches; }
 
+int zilla_check_device(void) {
+    cudaStreamSynchronize(stream());
+    const int code = read_and_clear_device_error();
+    if (code) return fail(kCudaError, "device error word 0x%x (bounded wait expired or index out of range)", code);
+    return check_cuda("zilla_check_device");
+}
+
 }  // extern "C"

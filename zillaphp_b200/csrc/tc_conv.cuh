@@ -57,7 +57,8 @@ struct ConvTcShape {
     static constexpr int ASTAGE = NCH * ABLK;
     static constexpr int BBLK = COUT * ROWB;
     static constexpr int BTOTAL = 9 * NCH * BBLK;
-    static constexpr int STAGE_F = 33;                     // padded fp32 staging row
+    static constexpr int STAGE_F = 36;   // fp32 staging row pitch: 144 B, 16-byte aligned and
+                                         // conflict-free for 128-bit accesses of 8 rows
     static constexpr int POOL_STAGE = POOL ? 128 * STAGE_F * 4 : 0;
     static constexpr uint32_t TMEM_COLS = (2 * COUT <= 32) ? 32 : (2 * COUT <= 64) ? 64 : (2 * COUT <= 128) ? 128 : (2 * COUT <= 256) ? 256 : 512;
     static constexpr int BAR_BYTES = 256;
@@ -208,29 +209,49 @@ __global__ void __launch_bounds__(192, 1) conv_tc_kernel(const __grid_constant__
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&acc_empty[acc]);
                     }
+                    // bias + ReLU, the row's 32 channels as eight 16-byte stores
+                    float4 *srow = reinterpret_cast<float4 *>(stage + row * S::STAGE_F);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float x = v[j] + __ldg(p.bias + 32 * cc + j);
-                        stage[row * S::STAGE_F + j] = x > 0.0f ? x : 0.0f;
+                    for (int k = 0; k < 8; ++k) {
+                        float4 t;
+                        t.x = fmaxf(v[4 * k + 0] + __ldg(p.bias + 32 * cc + 4 * k + 0), 0.0f);
+                        t.y = fmaxf(v[4 * k + 1] + __ldg(p.bias + 32 * cc + 4 * k + 1), 0.0f);
+                        t.z = fmaxf(v[4 * k + 2] + __ldg(p.bias + 32 * cc + 4 * k + 2), 0.0f);
+                        t.w = fmaxf(v[4 * k + 3] + __ldg(p.bias + 32 * cc + 4 * k + 3), 0.0f);
+                        srow[k] = t;
                     }
                     named_bar_sync(1, 128);
-                    for (int idx = ep_tid; idx < nwin * 32; idx += 128) {
-                        const int wi = idx >> 5, j = idx & 31;
+                    // thread = (window, channel octet): four pixels x 8 channels
+                    for (int idx = ep_tid; idx < nwin * 4; idx += 128) {
+                        const int wi = idx >> 2, o = idx & 3;
                         const int pr = wi / Wo, pc = wi - pr * Wo;
                         const int ho = (h0 >> 1) + pr;
                         if (ho >= Ho) continue;
                         const int r0 = (2 * pr) * p.W + 2 * pc;
-                        const float v00 = stage[r0 * S::STAGE_F + j], v01 = stage[(r0 + 1) * S::STAGE_F + j];
-                        const float v10 = stage[(r0 + p.W) * S::STAGE_F + j], v11 = stage[(r0 + p.W + 1) * S::STAGE_F + j];
-                        // first maximum in (kh, kw) order
-                        float best = v00;
-                        int pos = 0;
-                        if (v01 > best) { best = v01; pos = 1; }
-                        if (v10 > best) { best = v10; pos = 2; }
-                        if (v11 > best) { best = v11; pos = 3; }
-                        const size_t o = (((size_t)b * Ho + ho) * Wo + pc) * COUT + 32 * cc + j;
-                        p.out[o] = __float2bfloat16_rn(best);
-                        p.code[o] = (uint8_t)(pos | (best > 0.0f ? 4 : 0));
+                        const int rr[4] = {r0, r0 + 1, r0 + p.W, r0 + p.W + 1};
+                        float best[8];
+                        int pos[8];
+#pragma unroll
+                        for (int q4 = 0; q4 < 4; ++q4) {   // (kh, kw) order: first maximum wins
+                            const float4 *src = reinterpret_cast<const float4 *>(stage + rr[q4] * S::STAGE_F + 8 * o);
+                            const float4 lo = src[0], hi = src[1];
+                            const float vv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                if (q4 == 0 || vv[e] > best[e]) { best[e] = vv[e]; pos[e] = q4; }
+                            }
+                        }
+                        uint4 pk;
+                        __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) h2[e] = __floats2bfloat162_rn(best[2 * e], best[2 * e + 1]);
+                        uint2 cd;
+                        uint8_t *cb = reinterpret_cast<uint8_t *>(&cd);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) cb[e] = (uint8_t)(pos[e] | (best[e] > 0.0f ? 4 : 0));
+                        const size_t o8 = (((size_t)b * Ho + ho) * Wo + pc) * COUT + 32 * cc + 8 * o;
+                        *reinterpret_cast<uint4 *>(p.out + o8) = pk;
+                        *reinterpret_cast<uint2 *>(p.code + o8) = cd;
                     }
                     named_bar_sync(1, 128);
                 }

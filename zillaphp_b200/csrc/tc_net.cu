@@ -185,25 +185,90 @@ __global__ void conv_first_fwd_kernel(const float *__restrict__ x, const float *
     }
 }
 
+// First conv without a following pool: thread = (4 consecutive output pixels
+// of a row, 8-channel octet).  The octet's 72 weights and 8 biases live in
+// registers, the 3x6 input window in registers, 288 FMAs per thread, four
+// 16-byte stores.  The octet of a thread is fixed across its grid-stride loop
+// (the stride is a multiple of the octet count).
+template <int COUT>
+__global__ void __launch_bounds__(256) conv_first_fwd_rows_kernel(const float *__restrict__ x,
+                                                                  const float *__restrict__ w,
+                                                                  const float *__restrict__ bias,
+                                                                  bf16 *__restrict__ out, int B, int H, int W,
+                                                                  int pad) {
+    constexpr int NQ = COUT / 8;
+    const int oH = H + 2 * pad - 2, oW = W + 2 * pad - 2;
+    const int ngrp = (oW + 3) / 4;
+    const long long total = (long long)B * oH * ngrp * NQ;
+    const long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int q = (int)(i0 % NQ);
+    float wr[8][9], br[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        br[e] = __ldg(bias + 8 * q + e);
+#pragma unroll
+        for (int t = 0; t < 9; ++t) wr[e][t] = __ldg(w + (8 * q + e) * 9 + t);
+    }
+    for (long long i = i0; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const long long gi = i / NQ;
+        const int grp = (int)(gi % ngrp);
+        const long long r = gi / ngrp;
+        const int oh = (int)(r % oH);
+        const long long b = r / oH;
+        const int ow0 = grp * 4;
+        const float *xb = x + (size_t)b * H * W;
+        float xv[3][6];
+#pragma unroll
+        for (int dh = 0; dh < 3; ++dh)
+#pragma unroll
+            for (int k = 0; k < 6; ++k) {
+                const int ih = oh - pad + dh, iw = ow0 - pad + k;
+                xv[dh][k] = ((unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W) ? __ldg(xb + ih * W + iw) : 0.0f;
+            }
+#pragma unroll
+        for (int px = 0; px < 4; ++px) {
+            if (ow0 + px >= oW) break;
+            uint4 pk;
+            __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
+#pragma unroll
+            for (int e2 = 0; e2 < 4; ++e2) {
+                float a0 = br[2 * e2], a1 = br[2 * e2 + 1];
+#pragma unroll
+                for (int t = 0; t < 9; ++t) {
+                    a0 = fmaf(xv[t / 3][px + t % 3], wr[2 * e2][t], a0);
+                    a1 = fmaf(xv[t / 3][px + t % 3], wr[2 * e2 + 1][t], a1);
+                }
+                h2[e2] = __floats2bfloat162_rn(a0 > 0.0f ? a0 : 0.0f, a1 > 0.0f ? a1 : 0.0f);
+            }
+            *reinterpret_cast<uint4 *>(out + (((size_t)b * oH + oh) * oW + ow0 + px) * COUT + 8 * q) = pk;
+        }
+    }
+}
+
 // First-conv weight and bias gradient: dW[co][t] = sum_p dC[p][co] x[p + t],
 // db[co] = sum_p dC[p][co].  A block walks whole images: the image (with a
-// zero halo) is staged in shared memory, thread (pixel lane, co) reads one
-// bf16 of dC per pixel (a warp reads a pixel's 32 channels, 64 contiguous
-// bytes) and keeps 10 accumulators.  Per-block partials [block][COUT][10]
-// are summed later in block order.  Dynamic shared memory: (H+2p)(W+2p) floats.
+// zero halo) is staged in shared memory; thread (pixel lane, channel octet)
+// loads 8 bf16 of dC per pixel as one 16-byte load (a warp reads 8 pixels x
+// 32 channels = 512 contiguous bytes) and keeps 8 x 10 accumulators.  Lanes
+// of a warp that share an octet are combined by shuffles, warps in fixed order
+// through shared memory: per-block partials [block][COUT][10], summed later
+// in block order.  Dynamic shared memory: max((H+2p)(W+2p), 8*4*80) floats.
 template <int COUT>
 __global__ void __launch_bounds__(256) conv_first_wgrad_kernel(const bf16 *__restrict__ dC,
                                                                const float *__restrict__ x,
                                                                float *__restrict__ partial, int B, int H, int W,
                                                                int pad) {
-    constexpr int SLOTS = 256 / COUT;
+    constexpr int NQ = COUT / 8;            // channel octets per pixel
+    constexpr int LANES = 256 / NQ;         // pixel lanes per block
     extern __shared__ float xs[];
-    const int co = threadIdx.x % COUT, slot = threadIdx.x / COUT;
-    const int oH = H + 2 * pad - 2, oW = W + 2 * pad - 2;
+    const int q = threadIdx.x % NQ, pl = threadIdx.x / NQ;
+    const int oH = H + 2 * pad - 2, oW = W + 2 * pad - 2, P = oH * oW;
     const int PH = H + 2 * pad, PW = W + 2 * pad;
-    float acc[10];
+    float acc[8][10];
 #pragma unroll
-    for (int t = 0; t < 10; ++t) acc[t] = 0.0f;
+    for (int e = 0; e < 8; ++e)
+#pragma unroll
+        for (int t = 0; t < 10; ++t) acc[e][t] = 0.0f;
     for (int b = blockIdx.x; b < B; b += gridDim.x) {
         __syncthreads();
         const float *xb = x + (size_t)b * H * W;
@@ -212,68 +277,111 @@ __global__ void __launch_bounds__(256) conv_first_wgrad_kernel(const bf16 *__res
             xs[i] = ((unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W) ? xb[ih * W + iw] : 0.0f;
         }
         __syncthreads();
-        const bf16 *gb = dC + (size_t)b * oH * oW * COUT + co;
-#pragma unroll 4
-        for (int p = slot; p < oH * oW; p += SLOTS) {
-            const int oh = p / oW, ow = p - oh * oW;
-            const float g = __bfloat162float(gb[(size_t)p * COUT]);
-            const float *xr = xs + oh * PW + ow;
+        const bf16 *gb = dC + (size_t)b * P * COUT + 8 * q;
+        for (int p = pl; p < P; p += LANES) {
+            const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(gb + (size_t)p * COUT));
+            const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+            float g[8];
 #pragma unroll
-            for (int t = 0; t < 9; ++t) acc[t] = fmaf(g, xr[(t / 3) * PW + (t % 3)], acc[t]);
-            acc[9] += g;
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = __bfloat1622float2(h2[k]);
+                g[2 * k] = f.x;
+                g[2 * k + 1] = f.y;
+            }
+            const int oh = p / oW, ow = p - oh * oW;
+            const float *xr = xs + oh * PW + ow;
+            float xv[9];
+#pragma unroll
+            for (int t = 0; t < 9; ++t) xv[t] = xr[(t / 3) * PW + (t % 3)];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+#pragma unroll
+                for (int t = 0; t < 9; ++t) acc[e][t] = fmaf(g[e], xv[t], acc[e][t]);
+                acc[e][9] += g[e];
+            }
         }
     }
+    // lanes of a warp with the same octet: lane = pixel-slot * NQ + q
+#pragma unroll
+    for (int off = NQ; off < 32; off <<= 1)
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+#pragma unroll
+            for (int t = 0; t < 10; ++t) acc[e][t] += __shfl_xor_sync(0xffffffffu, acc[e][t], off);
     __syncthreads();
-    float (*red)[11] = reinterpret_cast<float (*)[11]>(xs);   // reuse: 256 x 11 floats
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float *red = xs;   // [8 warps][NQ][80]
+    if (lane < NQ)
 #pragma unroll
-    for (int t = 0; t < 10; ++t) red[threadIdx.x][t] = acc[t];
+        for (int e = 0; e < 8; ++e)
+#pragma unroll
+            for (int t = 0; t < 10; ++t) red[(warp * NQ + lane) * 80 + e * 10 + t] = acc[e][t];
     __syncthreads();
-    if (slot == 0) {
-        for (int s = 1; s < SLOTS; ++s)
-#pragma unroll
-            for (int t = 0; t < 10; ++t) acc[t] += red[s * COUT + co][t];
-        float *dst = partial + (size_t)blockIdx.x * COUT * 10 + co * 10;
-#pragma unroll
-        for (int t = 0; t < 10; ++t) dst[t] = acc[t];
+    for (int i = threadIdx.x; i < COUT * 10; i += blockDim.x) {   // i = co*10 + t, co = 8q + e
+        const int co = i / 10, t = i % 10, qq = co / 8, e = co % 8;
+        float s = 0.0f;
+        for (int wv = 0; wv < 8; ++wv) s += red[(wv * NQ + qq) * 80 + e * 10 + t];
+        partial[(size_t)blockIdx.x * COUT * 10 + i] = s;
     }
 }
 
 // Max-pool + ReLU backward as a gather: dC[b,h,w,c] = dP[b,h/2,w/2,c] when the
-// window's code points at (h,w) and the maximum was positive, else 0
-// (positions outside every window, floor pooling, get 0).  Also the bias
-// gradient partials sum_p dC[p][c] per block.  Thread = 8 channels of one
-// pixel (16-byte loads / stores).
+// window's code points at (h,w) and its maximum was positive, else 0.  One
+// thread per (window, 8-channel octet): one 16-byte load of dP and one 8-byte
+// load of the codes, four 16-byte stores (a warp writes whole contiguous
+// 2-pixel row segments).  Rows / columns outside every window (floor pooling
+// of an odd size) are zero-filled.  Bias-gradient partials sum_p dC[p][c] =
+// sum over windows of dP * [max > 0], per block (fixed combine order).
 __global__ void unpool_kernel(const bf16 *__restrict__ dP, const uint8_t *__restrict__ code, bf16 *__restrict__ dC,
                               float *__restrict__ bias_partial, int B, int H, int W, int C) {
-    const int G = C / 8;                   // channel groups
+    const int G = C / 8;                   // channel octets
     const int slots = blockDim.x / G;
     const int g = threadIdx.x % G, slot = threadIdx.x / G;
     const int Ho = H / 2, Wo = W / 2;
-    const long long total = (long long)B * H * W;
+    const long long windows = (long long)B * Ho * Wo;
     float acc[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
     if (slot < slots) {
-        for (long long p = (long long)blockIdx.x * slots + slot; p < total; p += (long long)gridDim.x * slots) {
-            const int w = (int)(p % W), h = (int)((p / W) % H), b = (int)(p / ((long long)W * H));
-            uint4 outv = make_uint4(0, 0, 0, 0);
-            if ((h >> 1) < Ho && (w >> 1) < Wo) {
-                const size_t o = (((size_t)b * Ho + (h >> 1)) * Wo + (w >> 1)) * C + g * 8;
-                const uint2 cv = *reinterpret_cast<const uint2 *>(code + o);
-                const uint4 dv = *reinterpret_cast<const uint4 *>(dP + o);
-                const uint8_t *cb = reinterpret_cast<const uint8_t *>(&cv);
-                const bf16 *db = reinterpret_cast<const bf16 *>(&dv);
-                bf16 *ob = reinterpret_cast<bf16 *>(&outv);
-                const int pos = ((h & 1) << 1) | (w & 1);
+        for (long long wi = (long long)blockIdx.x * slots + slot; wi < windows; wi += (long long)gridDim.x * slots) {
+            const int pw = (int)(wi % Wo);
+            const long long r = wi / Wo;
+            const int ph = (int)(r % Ho);
+            const long long b = r / Ho;
+            const size_t o = (size_t)wi * C + g * 8;
+            const uint2 cv = __ldg(reinterpret_cast<const uint2 *>(code + o));
+            const uint4 dv = __ldg(reinterpret_cast<const uint4 *>(dP + o));
+            const uint8_t *cb = reinterpret_cast<const uint8_t *>(&cv);
+            const bf16 *db = reinterpret_cast<const bf16 *>(&dv);
+            uint4 outv[4];
+            const unsigned short *du = reinterpret_cast<const unsigned short *>(db);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const bool hit = (cb[e] & 3) == pos && (cb[e] & 4);
-                    const float v = hit ? __bfloat162float(db[e]) : 0.0f;
-                    ob[e] = __float2bfloat16_rn(v);
-                    acc[e] += v;
-                }
+            for (int k = 0; k < 4; ++k) {
+                unsigned short *ou = reinterpret_cast<unsigned short *>(&outv[k]);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ou[e] = (cb[e] & 7) == (4 | k) ? du[e] : (unsigned short)0;
             }
-            *reinterpret_cast<uint4 *>(dC + (size_t)p * C + g * 8) = outv;
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+                if (cb[e] & 4) acc[e] += __bfloat162float(db[e]);
+            bf16 *row0 = dC + (((size_t)b * H + 2 * ph) * W + 2 * pw) * C + g * 8;
+            *reinterpret_cast<uint4 *>(row0) = outv[0];
+            *reinterpret_cast<uint4 *>(row0 + C) = outv[1];
+            *reinterpret_cast<uint4 *>(row0 + (size_t)W * C) = outv[2];
+            *reinterpret_cast<uint4 *>(row0 + (size_t)W * C + C) = outv[3];
+        }
+        // zero the last row / column that no window covers (odd H or W)
+        if ((H & 1) || (W & 1)) {
+            const int extra = ((H & 1) ? W : 0) + ((W & 1) ? H - (H & 1) : 0);
+            const long long total = (long long)B * extra;
+            for (long long i = (long long)blockIdx.x * slots + slot; i < total; i += (long long)gridDim.x * slots) {
+                const long long b = i / extra;
+                const int k = (int)(i % extra);
+                int h, w;
+                if ((H & 1) && k < W) { h = H - 1; w = k; }
+                else { h = k - ((H & 1) ? W : 0); w = W - 1; }
+                *reinterpret_cast<uint4 *>(dC + (((size_t)b * H + h) * W + w) * C + g * 8) = make_uint4(0, 0, 0, 0);
+            }
         }
     }
     extern __shared__ float red[];   // [blockDim.x][8]
@@ -395,11 +503,33 @@ struct ReduceArgs {
     float *dst, *dst2, *dst3;
 };
 
-__global__ void reduce_partials_kernel(ReduceArgs r) {
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < r.n;
-         i += (long long)gridDim.x * blockDim.x) {
+__device__ void r_store(const ReduceArgs &r, long long i, float s);
+
+// Block = 32 consecutive elements x 8 split lanes: lane l sums the splits
+// l, l+8, l+16, ... in order (coalesced 128-byte rows), then lane sums are
+// combined in lane order: a fixed order, so the result is deterministic.
+__global__ void __launch_bounds__(256) reduce_partials_kernel(ReduceArgs r) {
+    __shared__ float part[8][33];
+    const int el = threadIdx.x & 31, sl = threadIdx.x >> 5;
+    for (long long base = (long long)blockIdx.x * 32; base < r.n; base += (long long)gridDim.x * 32) {
+        const long long i = base + el;
         float s = 0.0f;
-        for (int k = 0; k < r.splits; ++k) s += r.partial[(size_t)k * r.n + i];
+        if (i < r.n)
+            for (int k = sl; k < r.splits; k += 8) s += r.partial[(size_t)k * r.n + i];
+        part[sl][el] = s;
+        __syncthreads();
+        if (sl == 0 && i < r.n) {
+            s = part[0][el];
+#pragma unroll
+            for (int l = 1; l < 8; ++l) s += part[l][el];
+            r_store(r, i, s);
+        }
+        __syncthreads();
+    }
+}
+
+__device__ void r_store(const ReduceArgs &r, long long i, float s) {
+    {
         const int m = (int)(i / r.N), n = (int)(i % r.N);
         switch (r.map) {
         case 0: r.dst[i] = s; break;
@@ -582,7 +712,7 @@ int launch_gemm(const GemmTcParams &p) {
 }
 
 int reduce(const ReduceArgs &r) {
-    reduce_partials_kernel<<<grid_for(r.n, 256, 4), 256, 0, stream()>>>(r);
+    reduce_partials_kernel<<<grid_for(r.n, 32, 8), 256, 0, stream()>>>(r);   // 32 elements per block
     ZB_LAUNCH_CHECK("reduce_partials");
     return kOk;
 }
@@ -834,9 +964,11 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
     {
         const long long pix = (long long)B * (e.c1_pool ? (e.H1 / 2) * (e.W1 / 2) : e.H1 * e.W1);
         const int grid = grid_for(pix, 128, 8);
-        if (e.C1 == 32 && !e.c1_pool) conv_first_fwd_kernel<32, false><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, nullptr, B, e.H0, e.W0, e.pad1);
+        const long long items = (long long)B * e.H1 * ((e.W1 + 3) / 4) * (e.C1 / 8);
+        const int grid_rows = grid_for(items, 256, 8);
+        if (e.C1 == 32 && !e.c1_pool) conv_first_fwd_rows_kernel<32><<<grid_rows, 256, 0, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
         else if (e.C1 == 32) conv_first_fwd_kernel<32, true><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
-        else if (!e.c1_pool) conv_first_fwd_kernel<16, false><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, nullptr, B, e.H0, e.W0, e.pad1);
+        else if (!e.c1_pool) conv_first_fwd_rows_kernel<16><<<grid_rows, 256, 0, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
         else conv_first_fwd_kernel<16, true><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
         ZB_LAUNCH_CHECK("conv_first_fwd");
         prof_mark(n, "conv_fwd");
@@ -913,7 +1045,7 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
     }
     {
         const int padded = (e.H0 + 2 * e.pad1) * (e.W0 + 2 * e.pad1);
-        const size_t smem = (size_t)(padded > 256 * 11 ? padded : 256 * 11) * sizeof(float);
+        const size_t smem = (size_t)(padded > 8 * 4 * 80 ? padded : 8 * 4 * 80) * sizeof(float);
         if (smem > 48 * 1024) return fail(kBadArg, "tc engine: first-conv image too large for the weight-gradient kernel");
         if (e.C1 == 32) conv_first_wgrad_kernel<32><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
         else conv_first_wgrad_kernel<16><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);

@@ -47,16 +47,21 @@ struct ConvTcParams {
     int *err;
 };
 
-template <int CIN, int COUT, int NS, bool POOL>
+// SB ("stream B"): instead of keeping all 9 taps of packed weights resident,
+// each pipeline stage carries its tap's weight slice next to the activation
+// box.  For wide layers (64 -> 128) the resident weights would take 147 KB
+// and leave room for only two or three stages.
+template <int CIN, int COUT, int NS, bool POOL, bool SB = false>
 struct ConvTcShape {
     static constexpr int CHUNK = CIN > 64 ? 64 : CIN;
     static constexpr int NCH = CIN / CHUNK;
     static constexpr int ROWB = CHUNK * 2;
     static constexpr Swizzle SW = ROWB == 128 ? kSw128 : (ROWB == 64 ? kSw64 : kSw32);
     static constexpr int ABLK = 128 * ROWB;
-    static constexpr int ASTAGE = NCH * ABLK;
     static constexpr int BBLK = COUT * ROWB;
-    static constexpr int BTOTAL = 9 * NCH * BBLK;
+    static constexpr int AONLY = NCH * ABLK;                       // activation part of a stage
+    static constexpr int ASTAGE = AONLY + (SB ? NCH * BBLK : 0);   // whole stage
+    static constexpr int BTOTAL = SB ? 0 : 9 * NCH * BBLK;          // resident weights
     static constexpr int STAGE_F = 36;   // fp32 staging row pitch: 144 B, 16-byte aligned and
                                          // conflict-free for 128-bit accesses of 8 rows
     static constexpr int POOL_STAGE = POOL ? 128 * STAGE_F * 4 : 0;
@@ -67,9 +72,9 @@ struct ConvTcShape {
     static_assert(CIN <= 64 || CIN % 64 == 0, "CIN above 64 must be a multiple of 64");
 };
 
-template <int CIN, int COUT, int EPI, int NS>
+template <int CIN, int COUT, int EPI, int NS, bool SB = false>
 __global__ void __launch_bounds__(192, 1) conv_tc_kernel(const __grid_constant__ ConvTcParams p) {
-    using S = ConvTcShape<CIN, COUT, NS, EPI == kEpiPool>;
+    using S = ConvTcShape<CIN, COUT, NS, EPI == kEpiPool, SB>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -110,10 +115,13 @@ __global__ void __launch_bounds__(192, 1) conv_tc_kernel(const __grid_constant__
         if (elect_one()) {
             prefetch_tmap(&p.in_map);
             prefetch_tmap(&p.w_map);
-            mbar_arrive_expect_tx(wbar, S::BTOTAL);
-            for (int t = 0; t < 9; ++t)
-                for (int j = 0; j < S::NCH; ++j)
-                    tma_load_3d(sB + (t * S::NCH + j) * S::BBLK, &p.w_map, wbar, j * S::CHUNK, 0, t);
+            if constexpr (!SB) {
+                mbar_arrive_expect_tx(wbar, S::BTOTAL);
+                for (int t = 0; t < 9; ++t)
+                    for (int j = 0; j < S::NCH; ++j)
+                        tma_load_3d(sB + (t * S::NCH + j) * S::BBLK, &p.w_map, wbar, j * S::CHUNK, 0, t);
+            }
+            const uint32_t stage_tx = box_bytes * S::NCH + (SB ? S::NCH * S::BBLK : 0);
             int s = 0;
             uint32_t ph = 0;
             for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
@@ -121,12 +129,16 @@ __global__ void __launch_bounds__(192, 1) conv_tc_kernel(const __grid_constant__
                 const int h0 = (tile - b * p.tiles_per_img) * p.R;
                 for (int tap = 0; tap < 9; ++tap) {
                     if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err, kErrEmptyWait)) break;
-                    mbar_arrive_expect_tx(&full[s], box_bytes * S::NCH);
+                    mbar_arrive_expect_tx(&full[s], stage_tx);
                     armed[s] = (int)ph + 1;
                     const int dh = tap / 3, dw = tap - 3 * dh;
                     for (int j = 0; j < S::NCH; ++j)
                         tma_load_4d(sA + s * S::ASTAGE + j * S::ABLK, &p.in_map, &full[s], j * S::CHUNK, dw - 1,
                                     h0 + dh - 1, b);
+                    if constexpr (SB)
+                        for (int j = 0; j < S::NCH; ++j)
+                            tma_load_3d(sA + s * S::ASTAGE + S::AONLY + j * S::BBLK, &p.w_map, &full[s],
+                                        j * S::CHUNK, 0, tap);
                     if (++s == NS) { s = 0; ph ^= 1u; }
                 }
             }
@@ -134,13 +146,14 @@ __global__ void __launch_bounds__(192, 1) conv_tc_kernel(const __grid_constant__
                 for (int i = 0; i < NS; ++i)
                     if (armed[i] && !mbar_wait_drain(&full[i], (uint32_t)(armed[i] - 1)))
                         atomicCAS(p.err, 0, kErrDrain);
+                if (!SB && !mbar_wait_drain(wbar, 0)) atomicCAS(p.err, 0, kErrDrain);
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (elect_one()) {
             bool issued = false;
-            if (mbar_wait(wbar, 0, abort_flag, p.err, kErrFullWait)) {
+            if (SB || mbar_wait(wbar, 0, abort_flag, p.err, kErrFullWait)) {
                 int s = 0, acc = 0;
                 uint32_t ph = 0, acc_ph = 0;
                 const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
@@ -158,8 +171,9 @@ __global__ void __launch_bounds__(192, 1) conv_tc_kernel(const __grid_constant__
                             for (int k = 0; k < S::CHUNK / 16; ++k) {
                                 const uint64_t ad = smem_desc(sA0 + s * S::ASTAGE + j * S::ABLK + k * 32, 16,
                                                               8 * S::ROWB, S::SW);
-                                const uint64_t bd = smem_desc(sB0 + (tap * S::NCH + j) * S::BBLK + k * 32, 16,
-                                                              8 * S::ROWB, S::SW);
+                                const uint32_t bsrc = SB ? sA0 + s * S::ASTAGE + S::AONLY + j * S::BBLK
+                                                         : sB0 + (tap * S::NCH + j) * S::BBLK;
+                                const uint64_t bd = smem_desc(bsrc + k * 32, 16, 8 * S::ROWB, S::SW);
                                 mma_bf16(d, ad, bd, IDESC, (tap | j | k) != 0);
                             }
                         issued = true;

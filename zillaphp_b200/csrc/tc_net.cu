@@ -634,10 +634,10 @@ int dalloc(TcEngine &e, T **p, size_t count) {
 }
 
 // ---------------------------------------------------------------- conv dispatch
-template <int CIN, int COUT, int EPI, int NS>
+template <int CIN, int COUT, int EPI, int NS, bool SB = false>
 int launch_conv(const ConvTcParams &p) {
-    using S = tc::ConvTcShape<CIN, COUT, NS, EPI == tc::kEpiPool>;
-    auto kern = tc::conv_tc_kernel<CIN, COUT, EPI, NS>;
+    using S = tc::ConvTcShape<CIN, COUT, NS, EPI == tc::kEpiPool, SB>;
+    auto kern = tc::conv_tc_kernel<CIN, COUT, EPI, NS, SB>;
     static bool attr = false;
     if (!attr) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM) != cudaSuccess)
@@ -662,15 +662,15 @@ bool conv_shape_supported(int cin, int cout) {
 
 int run_conv_fwd(const ConvLayer &L) {
     if (L.CIN == 32 && L.COUT == 64) return launch_conv<32, 64, tc::kEpiPool, 6>(L.fwd);
-    if (L.CIN == 64 && L.COUT == 128) return launch_conv<64, 128, tc::kEpiPool, 3>(L.fwd);
+    if (L.CIN == 64 && L.COUT == 128) return launch_conv<64, 128, tc::kEpiPool, 6, true>(L.fwd);
     if (L.CIN == 16 && L.COUT == 32) return launch_conv<16, 32, tc::kEpiPool, 8>(L.fwd);
     return fail(kBadArg, "tc engine: no forward conv kernel for %d->%d", L.CIN, L.COUT);
 }
 
 int run_conv_dgrad(const ConvLayer &L) {
     // dgrad convolves dY (COUT channels) into CIN outputs
-    if (L.CIN == 32 && L.COUT == 64) return launch_conv<64, 32, tc::kEpiDgrad, 6>(L.dgrad);
-    if (L.CIN == 64 && L.COUT == 128) return launch_conv<128, 64, tc::kEpiDgrad, 2>(L.dgrad);
+    if (L.CIN == 32 && L.COUT == 64) return launch_conv<64, 32, tc::kEpiDgrad, 4>(L.dgrad);
+    if (L.CIN == 64 && L.COUT == 128) return launch_conv<128, 64, tc::kEpiDgrad, 4, true>(L.dgrad);
     if (L.CIN == 16 && L.COUT == 32) return launch_conv<32, 32, tc::kEpiDgrad, 8>(L.dgrad);
     return fail(kBadArg, "tc engine: no dgrad conv kernel for %d->%d", L.CIN, L.COUT);
 }
@@ -913,7 +913,7 @@ int tc_build(Net &n, TcEngine &e) {
     e.head_grid = sm_count() * 2;
     if ((rc = dalloc(e, &e.head_partial, (size_t)e.head_grid * (e.HD * e.NC + e.NC + e.HD)))) return rc;
     if ((rc = dalloc(e, &e.row_loss, (size_t)B))) return rc;
-    e.c1_wgrad_grid = sm_count() * 2;
+    e.c1_wgrad_grid = sm_count() * 6;   // several blocks per SM: each walks whole images
     if ((rc = dalloc(e, &e.c1_partial, (size_t)e.c1_wgrad_grid * e.C1 * 10))) return rc;
     // diagnostics
     e.views.push_back({"conv1.out", e.a1, (size_t)B * (e.c1_pool ? (e.H1 / 2) * (e.W1 / 2) : e.H1 * e.W1) * e.C1, 0});

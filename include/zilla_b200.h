@@ -213,6 +213,25 @@ int zilla_net_inspect(int net, int index, char *name, int name_len, float *host,
                       unsigned long n_floats);
 int zilla_net_device_status(int net);
 
+/* ---- fused Transformer language-model step (fp32) ----
+ * Replaces TransformerLM::forwardBatch + the autograd backward + the
+ * optimizer (src/Transformers/TransformerLM.php:77-116, trained as in
+ * examples/train_shakespeare.php:104-124) with one call.  Pre-LN blocks
+ * (src/Transformers/TransformerBlock.php:28-33): causal multi-head attention
+ * (head dimension 32, src/Attention/MultiHeadAttention.php:41-80), FFN with
+ * ReLU, LayerNorm eps 1e-5; final LayerNorm and Linear head; loss is
+ * softmax_ce_dev's (sum over the batch*seq rows, gradients of the mean).
+ * Parameters follow TransformerLM::parameters() (TransformerLM.php:158-170):
+ * token table [vocab, dim], position table [max_seq, dim], final LN (g, b),
+ * head (W [dim, vocab], b), then per block Wq bq Wk bk Wv bv Wo bo,
+ * W1 [dim, ffn] b1, W2 [ffn, dim] b2, ln1 (g, b), ln2 (g, b).
+ * The returned id is a net: zilla_net_set_optimizer / zilla_net_step /
+ * zilla_net_step_host / zilla_net_params_id / zilla_dp_attach all apply,
+ * with x = batch*seq token ids and y = batch*seq next-token ids, both as
+ * floats.  seq <= 176 (one (sequence, head) of the attention backward is
+ * held in shared memory).  Returns a net id > 0, or a negative status. */
+int zilla_lm_create(int vocab, int dim, int heads, int layers, int max_seq, int ffn, int batch, int seq);
+
 /* ---- data-parallel runner (one process per GPU, NCCL over NVLink) ----
  * zilla_dp_unique_id writes a 128-byte NCCL unique id (rank 0 creates it,
  * the host distributes it, e.g. through a file or a store).

@@ -81,9 +81,23 @@ def test_net_spec_validation(lib):
     assert lib.zilla_net_destroy(12345) == -1
 
 
+def test_lm_create_validation(lib):
+    ok = (65, 128, 4, 2, 128, 512, 64, 128)
+    def create(**kw):
+        args = dict(zip(("vocab", "dim", "heads", "layers", "max_seq", "ffn", "batch", "seq"), ok))
+        args.update(kw)
+        return lib.zilla_lm_create(*args.values())
+    assert create(heads=8) == -2                # head dimension 16: only 32 is built
+    assert create(seq=129) == -2                # longer than the position table
+    assert create(max_seq=512, seq=200) == -2   # attention backward tile beyond shared memory
+    assert create(vocab=0) == -2
+    assert create(batch=0) == -2
+
+
 def test_workload_param_counts():
     assert configs.param_count(configs.CNN_LARGE) == 1_701_130
     assert configs.param_count(configs.AUDIO_CNN) == 97_036
     assert configs.param_count(configs.MLP) == 101_770
     assert configs.param_count(configs.CNN_SMALL) == 13_610
+    assert configs.lm_param_count(configs.TRANSFORMER_LM) == 429_889
     assert abs(configs.flops_per_sample(configs.CNN_LARGE) * 8192 / 1e9 - 1507.0) < 1.0

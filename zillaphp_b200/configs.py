@@ -65,6 +65,51 @@ AUDIO_CNN = Workload(
 WORKLOADS = {w.name: w for w in (MLP, CNN_SMALL, CNN_LARGE, AUDIO_CNN)}
 
 
+@dataclass(frozen=True)
+class LmWorkload:
+    """A decoder-only Transformer LM (src/Transformers/TransformerLM.php)."""
+    name: str
+    vocab: int
+    dim: int
+    heads: int
+    layers: int
+    max_seq: int
+    ffn: int
+    batch: int                 # sequences per step
+    seq: int                   # tokens per sequence
+    lr: float
+    optimizer: int = ADAM
+    adam: tuple = field(default=(0.9, 0.999, 1e-8))
+    notes: str = ""
+
+    @property
+    def rows(self) -> int:
+        return self.batch * self.seq
+
+
+TRANSFORMER_LM = LmWorkload(
+    "char_transformer_lm", vocab=65, dim=128, heads=4, layers=2, max_seq=128, ffn=512, batch=64, seq=128, lr=3e-4,
+    notes="vocab 65, d 128, 4 heads (head dim 32), 2 pre-LN blocks, FFN 512 ReLU, learned positions, "
+          "seq 128, batch 64, causal attention, cross-entropy, Adam 3e-4; fp32")
+
+
+def lm_param_count(w: LmWorkload) -> int:
+    D, F = w.dim, w.ffn
+    per_block = 4 * (D * D + D) + D * F + F + F * D + D + 4 * D
+    return w.vocab * D + w.max_seq * D + 2 * D + D * w.vocab + w.vocab + w.layers * per_block
+
+
+def lm_flops_per_token(w: LmWorkload) -> float:
+    """Algorithmic FLOPs of one training step per token: 3x the forward's
+    2*M*N*K for every projection, FFN and head GEMM, plus the causal
+    attention contractions (q k^T and P v over the T(T+1)/2 kept scores,
+    three contractions' worth each in the backward)."""
+    D, F, V, T = w.dim, w.ffn, w.vocab, w.seq
+    dense = w.layers * (4 * D * D + 2 * D * F) + D * V
+    attn = w.layers * 2 * D * (T + 1) / 2        # per token: QK^T and PV over ~T/2 keys
+    return 2 * 3 * dense + 2 * 3 * attn
+
+
 def param_count(w: Workload) -> int:
     n = 0
     c, h, wd = w.in_shape

@@ -1,0 +1,601 @@
+// lm_net.cu -- the fused training step of ZillaPHP's decoder-only Transformer
+// language model (fp32, CUDA cores): one C call per step for
+// TransformerLM::forwardBatch + the autograd backward + the optimizer
+// (src/Transformers/TransformerLM.php:77-116, TransformerBlock.php:28-33,
+// src/Attention/MultiHeadAttention.php:41-80, src/NN/Layers/FeedForward.php,
+// src/Tensor/Tensor.php:636-735 LayerNorm, src/NN/Layers/Embedding.php:35-56).
+//
+// Rows are the B*T tokens of the batch.  Per block (pre-LN):
+//   h1 = LN1(x); [q|k|v] = h1 [Wq|Wk|Wv] + [bq|bk|bv]  (one GEMM, N = 3D)
+//   per (sequence, head): P = softmax(maskfill(q k^T / sqrt(dh), -1e9 on future keys)); o = P v
+//   xm = x + o Wo + bo                                  (residual fused in the GEMM store)
+//   h2 = LN2(xm); f = relu(h2 W1 + b1); x' = xm + f W2 + b2
+// then hf = LNf(x), logits = hf Wh + bh, softmax cross-entropy (softmax_ce_dev
+// semantics: loss sum, dlogits / rows).  Attention runs per sequence: the
+// reference's block-diagonal batch mask only adds -1e9 entries, whose softmax
+// weight is exactly zero.  Every reduction has a fixed order (deterministic).
+#include <math.h>
+#include <string.h>
+
+#include <vector>
+
+#include "conv_pool_f32.cuh"
+#include "net.cuh"
+
+namespace zb {
+
+int launch_softmax_ce(const float *z, const float *y, float *dz, double *row_loss, float *loss,
+                      int B, int C, bool zero_first);
+
+struct LmEngine {
+    int V = 0, D = 0, H = 0, L = 0, T = 0, F = 0, Bs = 0, Ts = 0, N = 0;
+    long long o_tok = 0, o_pos = 0, o_lnf_g = 0, o_lnf_b = 0, o_head_W = 0, o_head_b = 0;
+    struct Blk {
+        long long qW, qb, kW, kb, vW, vb, oW, ob, f1W, f1b, f2W, f2b, ln1g, ln1b, ln2g, ln2b;
+    };
+    std::vector<Blk> blk;
+    // saved forward tensors (per block) and the final ones
+    std::vector<float *> x, h1, xh1, inv1, qkv, P, att, xm, h2, xh2, inv2, f1;
+    float *hf = nullptr, *xhf = nullptr, *invf = nullptr, *logits = nullptr;
+    // gradients
+    float *g = nullptr, *gm = nullptr, *dh = nullptr, *df1 = nullptr, *datt = nullptr, *dqkv = nullptr;
+    float *ln_partial = nullptr;   // [ln_blocks][2D]
+    int ln_blocks = 0;
+    std::vector<void *> allocs;
+};
+
+namespace {
+
+// ---------------------------------------------------------------- GEMM problems
+// Y[m, n] = sum_k X[m*ldx + k] W_s[k*sw + (n - s*sw)] + b_s[n - s*sw]  (s = n / sw)
+//           [+ R[m*ldy + n]] [relu]
+struct LinFwd {
+    const float *X, *R;
+    const float *W[3], *Bv[3];
+    float *Y;
+    int M, N, K, ldx, ldy, sw;
+    bool relu;
+    static constexpr bool kAMFast = false, kBNFast = true, kExactOrder = false;
+    __device__ float init(int, int) const { return 0.0f; }
+    __device__ float a(int m, int k) const { return X[(size_t)m * ldx + k]; }
+    __device__ float b(int k, int n) const { const int s = n / sw; return W[s][(size_t)k * sw + (n - s * sw)]; }
+    __device__ void store(int m, int n, float v) const {
+        const int s = n / sw;
+        float o = v + Bv[s][n - s * sw];
+        if (R) o += R[(size_t)m * ldy + n];
+        if (relu) o = o > 0.0f ? o : 0.0f;
+        Y[(size_t)m * ldy + n] = o;
+    }
+};
+
+// dX[m, j] = sum_n dY[m*ldy + n] W_s[j*sw + (n - s*sw)]  [* (mask[m*ldx + j] > 0)]
+struct LinDgrad {
+    const float *dY, *mask;
+    const float *W[3];
+    float *dX;
+    int M, N, K, ldx, ldy, sw;   // N = in features, K = out features (all segments)
+    static constexpr bool kAMFast = false, kBNFast = false, kExactOrder = false;
+    __device__ float init(int, int) const { return 0.0f; }
+    __device__ float a(int m, int k) const { return dY[(size_t)m * ldy + k]; }
+    __device__ float b(int k, int n) const { const int s = k / sw; return W[s][(size_t)n * sw + (k - s * sw)]; }
+    __device__ void store(int m, int n, float v) const {
+        const size_t at = (size_t)m * ldx + n;
+        if (mask && !(mask[at] > 0.0f)) v = 0.0f;
+        dX[at] = v;
+    }
+};
+
+// dW_s[j*sw + (n - s*sw)] = sum_m X[m*ldx + j] dY[m*ldy + n]   (M = in, N = out, K = rows)
+struct LinWgrad {
+    const float *X, *dY;
+    float *dW[3];
+    int M, N, K, ldx, ldy, sw;
+    static constexpr bool kAMFast = true, kBNFast = true, kExactOrder = false;
+    __device__ float init(int, int) const { return 0.0f; }
+    __device__ float a(int m, int k) const { return X[(size_t)k * ldx + m]; }
+    __device__ float b(int k, int n) const { return dY[(size_t)k * ldy + n]; }
+    __device__ void store(int m, int n, float v) const {
+        const int s = n / sw;
+        dW[s][(size_t)m * sw + (n - s * sw)] = v;
+    }
+};
+
+// ---------------------------------------------------------------- kernels
+__global__ void embed_fwd_kernel(const float *__restrict__ tokens, const float *__restrict__ tok,
+                                 const float *__restrict__ pos, float *__restrict__ x, int N, int Ts, int D, int V,
+                                 int *__restrict__ err) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (long long)N * D;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / D), d = (int)(i % D);
+        int id = (int)tokens[r];
+        if (id < 0 || id >= V) {   // Embedding::forward throws OutOfRange; record and use row 0
+            if (err) atomicCAS(err, 0, 0x454d4244);   // "EMBD"
+            id = 0;
+        }
+        x[i] = tok[(size_t)id * D + d] + pos[(size_t)(r % Ts) * D + d];
+    }
+}
+
+// LayerNorm forward, one warp per row (D a multiple of 32, <= 1024):
+// mean, biased variance, invstd = 1/sqrt(var + eps); y = xhat*g + b.
+__global__ void ln_fwd_kernel(const float *__restrict__ x, const float *__restrict__ gam,
+                              const float *__restrict__ bet, float *__restrict__ y, float *__restrict__ xhat,
+                              float *__restrict__ inv, int N, int D, float eps) {
+    const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < N; r += gridDim.x * warps) {
+        const float *xr = x + (size_t)r * D;
+        float s = 0.0f;
+        for (int j = lane; j < D; j += 32) s += xr[j];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float mean = s / D;
+        float q = 0.0f;
+        for (int j = lane; j < D; j += 32) { const float d0 = xr[j] - mean; q += d0 * d0; }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+        const float is = 1.0f / sqrtf(q / D + eps);
+        for (int j = lane; j < D; j += 32) {
+            const float xh = (xr[j] - mean) * is;
+            xhat[(size_t)r * D + j] = xh;
+            y[(size_t)r * D + j] = xh * gam[j] + bet[j];
+        }
+        if (lane == 0) inv[r] = is;
+    }
+}
+
+// LayerNorm backward (src/Tensor/Tensor.php:691-712): gx = g*gamma,
+// dx = inv/D (D gx - sum gx - xhat sum(gx xhat)); out = R + dx.  Per-block
+// partial sums of g*xhat (dgamma) and g (dbeta), warps combined in order.
+__global__ void ln_bwd_kernel(const float *__restrict__ gout, const float *__restrict__ xhat,
+                              const float *__restrict__ inv, const float *__restrict__ gam,
+                              const float *__restrict__ R, float *__restrict__ out,
+                              float *__restrict__ partial, int N, int D) {
+    extern __shared__ float red[];   // [warps][2D]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    float *mine = red + (size_t)warp * 2 * D;
+    for (int j = lane; j < 2 * D; j += 32) mine[j] = 0.0f;
+    __syncwarp();
+    for (int r = blockIdx.x * warps + warp; r < N; r += gridDim.x * warps) {
+        const float *g = gout + (size_t)r * D, *xh = xhat + (size_t)r * D;
+        float s1 = 0.0f, s2 = 0.0f;
+        for (int j = lane; j < D; j += 32) {
+            const float gx = g[j] * gam[j];
+            s1 += gx;
+            s2 += gx * xh[j];
+            mine[j] += g[j] * xh[j];
+            mine[D + j] += g[j];
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+            s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        }
+        const float is = inv[r];
+        for (int j = lane; j < D; j += 32) {
+            const float gx = g[j] * gam[j];
+            float d = is / D * (D * gx - s1 - xh[j] * s2);
+            if (R) d += R[(size_t)r * D + j];
+            out[(size_t)r * D + j] = d;
+        }
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < 2 * D; j += blockDim.x) {
+        float s = 0.0f;
+        for (int w = 0; w < warps; ++w) s += red[(size_t)w * 2 * D + j];
+        partial[(size_t)blockIdx.x * 2 * D + j] = s;
+    }
+}
+
+// Sum of per-block partials [blocks][2D] into gamma / beta gradients.
+__global__ void sum_ln_partials_kernel(const float *__restrict__ partial, int blocks, int D,
+                                       float *__restrict__ dg, float *__restrict__ db) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < 2 * D; j += gridDim.x * blockDim.x) {
+        float s = 0.0f;
+        for (int b = 0; b < blocks; ++b) s += partial[(size_t)b * 2 * D + j];
+        if (j < D) dg[j] = s;
+        else db[j - D] = s;
+    }
+}
+
+// Column sums over rows with a row stride: out_s[c] = sum_r dY[r*ld + s*sw + c].
+__global__ void colsum_kernel(const float *__restrict__ dY, int rows, int ld, int sw, float *o0, float *o1,
+                              float *o2) {
+    __shared__ float part[8][33];
+    const int col = blockIdx.x * 32 + threadIdx.x;
+    float acc = 0.0f;
+    if (col < ld)
+        for (int r = threadIdx.y; r < rows; r += 8) acc += dY[(size_t)r * ld + col];
+    part[threadIdx.y][threadIdx.x] = acc;
+    __syncthreads();
+    if (threadIdx.y == 0 && col < ld) {
+        float s = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s += part[k][threadIdx.x];
+        const int seg = col / sw, c = col - seg * sw;
+        float *o = seg == 0 ? o0 : seg == 1 ? o1 : o2;
+        o[c] = s;
+    }
+}
+
+// Causal attention forward for one (sequence, head, block of 32 query rows),
+// head dim DH: S = q k^T * scale with -1e9 on future keys, P = row softmax
+// (written out for the backward), o = P v into the head's columns.
+template <int DH>
+__global__ void __launch_bounds__(128) attn_fwd_kernel(const float *__restrict__ qkv, float *__restrict__ P,
+                                                       float *__restrict__ out, int Ts, int H, int D, float scale) {
+    extern __shared__ float sm[];
+    const int bh = blockIdx.x, b = bh / H, h = bh % H;
+    const int i0 = blockIdx.y * 32;
+    const int rows = min(32, Ts - i0);
+    const int keys = min(Ts, i0 + 32);   // causal: keys after the last query row are never used
+    float *Ks = sm, *Vs = Ks + (size_t)Ts * (DH + 1), *Qs = Vs + (size_t)Ts * (DH + 1), *S = Qs + 32 * (DH + 1);
+    const size_t ld = 3 * (size_t)D;
+    const float *base = qkv + (size_t)b * Ts * ld + h * DH;
+    for (int i = threadIdx.x; i < keys * DH; i += blockDim.x) {
+        const int j = i / DH, d = i % DH;
+        Ks[j * (DH + 1) + d] = base[(size_t)j * ld + D + d];
+        Vs[j * (DH + 1) + d] = base[(size_t)j * ld + 2 * D + d];
+    }
+    for (int i = threadIdx.x; i < rows * DH; i += blockDim.x) {
+        const int r = i / DH, d = i % DH;
+        Qs[r * (DH + 1) + d] = base[(size_t)(i0 + r) * ld + d];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < rows * keys; i += blockDim.x) {
+        const int r = i / keys, j = i % keys;
+        float s;
+        if (j > i0 + r) {
+            s = -1e9f;                      // maskedFill(-1e9)
+        } else {
+            s = 0.0f;
+#pragma unroll
+            for (int d = 0; d < DH; ++d) s += Qs[r * (DH + 1) + d] * Ks[j * (DH + 1) + d];
+            s *= scale;
+        }
+        S[r * Ts + j] = s;
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int r = warp; r < rows; r += 4) {
+        float mx = -INFINITY;
+        for (int j = lane; j < keys; j += 32) mx = fmaxf(mx, S[r * Ts + j]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float sum = 0.0f;
+        for (int j = lane; j < keys; j += 32) {
+            const float e = expf(S[r * Ts + j] - mx);
+            S[r * Ts + j] = e;
+            sum += e;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        float *prow = P + ((size_t)bh * Ts + i0 + r) * Ts;
+        for (int j = lane; j < Ts; j += 32) {
+            const float p = j < keys ? S[r * Ts + j] / sum : 0.0f;
+            if (j < keys) S[r * Ts + j] = p;
+            prow[j] = p;
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < rows * DH; i += blockDim.x) {
+        const int r = i / DH, d = i % DH;
+        float o = 0.0f;
+        for (int j = 0; j <= i0 + r; ++j) o += S[r * Ts + j] * Vs[j * (DH + 1) + d];
+        out[((size_t)b * Ts + i0 + r) * D + h * DH + d] = o;
+    }
+}
+
+// Attention backward for one (sequence, head):
+//   dV = P^T dO;  dP = dO V^T;  dS = P (dP - rowsum(dP P)) * scale  (softmax and
+//   maskedFill backward: masked entries have P = 0);  dQ = dS K;  dK = dS^T Q.
+template <int DH>
+__global__ void __launch_bounds__(256) attn_bwd_kernel(const float *__restrict__ qkv, const float *__restrict__ P,
+                                                       const float *__restrict__ dO, float *__restrict__ dqkv,
+                                                       int Ts, int H, int D, float scale) {
+    extern __shared__ float sm[];
+    const int bh = blockIdx.x, b = bh / H, h = bh % H;
+    const int LD = DH + 1;
+    float *Qs = sm, *Ks = Qs + Ts * LD, *Vs = Ks + Ts * LD, *Os = Vs + Ts * LD, *S = Os + Ts * LD;   // S: [Ts][Ts+1]
+    const int SL = Ts + 1;
+    const size_t ld = 3 * (size_t)D;
+    const float *base = qkv + (size_t)b * Ts * ld + h * DH;
+    for (int i = threadIdx.x; i < Ts * DH; i += blockDim.x) {
+        const int j = i / DH, d = i % DH;
+        Qs[j * LD + d] = base[(size_t)j * ld + d];
+        Ks[j * LD + d] = base[(size_t)j * ld + D + d];
+        Vs[j * LD + d] = base[(size_t)j * ld + 2 * D + d];
+        Os[j * LD + d] = dO[((size_t)b * Ts + j) * D + h * DH + d];
+    }
+    const float *Pb = P + (size_t)bh * Ts * Ts;
+    for (int i = threadIdx.x; i < Ts * Ts; i += blockDim.x) S[(i / Ts) * SL + (i % Ts)] = Pb[i];
+    __syncthreads();
+    float *gb = dqkv + (size_t)b * Ts * ld + h * DH;
+    // dV[j][d] = sum_{i >= j} P[i][j] dO[i][d]
+    for (int i = threadIdx.x; i < Ts * DH; i += blockDim.x) {
+        const int j = i / DH, d = i % DH;
+        float s = 0.0f;
+        for (int r = j; r < Ts; ++r) s += S[r * SL + j] * Os[r * LD + d];
+        gb[(size_t)j * ld + 2 * D + d] = s;
+    }
+    __syncthreads();
+    // dS in place, one warp per row
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    for (int r = warp; r < Ts; r += warps) {
+        float dot = 0.0f;
+        float dp[8];   // Ts <= 256: at most 8 columns per lane
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const int j = lane + 32 * c;
+            dp[c] = 0.0f;
+            if (j <= r && j < Ts) {
+                float s = 0.0f;
+#pragma unroll
+                for (int d = 0; d < DH; ++d) s += Os[r * LD + d] * Vs[j * LD + d];
+                dp[c] = s;
+                dot += s * S[r * SL + j];
+            }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const int j = lane + 32 * c;
+            if (j < Ts) S[r * SL + j] = j <= r ? S[r * SL + j] * (dp[c] - dot) * scale : 0.0f;
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < Ts * DH; i += blockDim.x) {
+        const int r = i / DH, d = i % DH;
+        float sq = 0.0f, sk = 0.0f;
+        for (int j = 0; j <= r; ++j) sq += S[r * SL + j] * Ks[j * LD + d];          // dQ[r]
+        for (int q = r; q < Ts; ++q) sk += S[q * SL + r] * Qs[q * LD + d];         // dK[r]
+        gb[(size_t)r * ld + d] = sq;
+        gb[(size_t)r * ld + D + d] = sk;
+    }
+}
+
+// dTok[v][d] = sum over rows with token v of g[row][d] (row order); dPos[t][d]
+// = sum over sequences of g[b*T + t][d].
+__global__ void embed_bwd_kernel(const float *__restrict__ g, const float *__restrict__ tokens,
+                                 float *__restrict__ dtok, float *__restrict__ dpos, int N, int Ts, int D, int V,
+                                 int Tmax) {
+    const int Bs = N / Ts;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (long long)(V + Tmax) * D;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int row = (int)(i / D), d = (int)(i % D);
+        float s = 0.0f;
+        if (row < V) {
+            for (int r = 0; r < N; ++r)
+                if ((int)tokens[r] == row) s += g[(size_t)r * D + d];
+            dtok[(size_t)row * D + d] = s;
+        } else {
+            const int t = row - V;
+            if (t < Ts)
+                for (int bq = 0; bq < Bs; ++bq) s += g[((size_t)bq * Ts + t) * D + d];
+            dpos[(size_t)t * D + d] = s;   // positions >= T were not used: zero
+        }
+    }
+}
+
+template <class T>
+int lalloc(LmEngine &e, T **p, size_t count) {
+    if (cudaMalloc((void **)p, (count ? count : 1) * sizeof(T)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(kBadHandle, "lm: cudaMalloc of %zu bytes failed", count * sizeof(T));
+    }
+    e.allocs.push_back((void *)*p);
+    return kOk;
+}
+
+int ln_fwd(const float *x, const float *g, const float *b, float *y, float *xh, float *inv, int N, int D) {
+    ln_fwd_kernel<<<grid_for((long long)N * 32, 256, 8), 256, 0, stream()>>>(x, g, b, y, xh, inv, N, D, 1e-5f);
+    ZB_LAUNCH_CHECK("lm layernorm");
+    return kOk;
+}
+
+int ln_bwd(LmEngine &e, const float *gout, const float *xh, const float *inv, const float *gam, const float *R,
+           float *out, float *dg, float *db) {
+    const int warps = 8;
+    ln_bwd_kernel<<<e.ln_blocks, warps * 32, (size_t)warps * 2 * e.D * sizeof(float), stream()>>>(
+        gout, xh, inv, gam, R, out, e.ln_partial, e.N, e.D);
+    ZB_LAUNCH_CHECK("lm layernorm backward");
+    sum_ln_partials_kernel<<<(2 * e.D + 255) / 256, 256, 0, stream()>>>(e.ln_partial, e.ln_blocks, e.D, dg, db);
+    ZB_LAUNCH_CHECK("lm layernorm partials");
+    return kOk;
+}
+
+int colsum(const float *dY, int rows, int ld, int sw, float *o0, float *o1 = nullptr, float *o2 = nullptr) {
+    colsum_kernel<<<(ld + 31) / 32, dim3(32, 8), 0, stream()>>>(dY, rows, ld, sw, o0, o1, o2);
+    ZB_LAUNCH_CHECK("lm column sums");
+    return kOk;
+}
+
+int lm_build(Net &n, LmEngine &e) {
+    const int D = e.D, N = e.N, F = e.F, L = e.L, V = e.V;
+    long long off = 0;
+    auto take = [&](long long cnt) { const long long o = off; off += cnt; return o; };
+    e.o_tok = take((long long)V * D);
+    e.o_pos = take((long long)e.T * D);
+    e.o_lnf_g = take(D);
+    e.o_lnf_b = take(D);
+    e.o_head_W = take((long long)D * V);
+    e.o_head_b = take(V);
+    for (int l = 0; l < L; ++l) {
+        LmEngine::Blk b;
+        b.qW = take((long long)D * D); b.qb = take(D);
+        b.kW = take((long long)D * D); b.kb = take(D);
+        b.vW = take((long long)D * D); b.vb = take(D);
+        b.oW = take((long long)D * D); b.ob = take(D);
+        b.f1W = take((long long)D * F); b.f1b = take(F);
+        b.f2W = take((long long)F * D); b.f2b = take(D);
+        b.ln1g = take(D); b.ln1b = take(D); b.ln2g = take(D); b.ln2b = take(D);
+        e.blk.push_back(b);
+    }
+    n.nparams = off;
+    int rc;
+    const size_t ND = (size_t)N * D;
+    e.x.resize(L + 1);
+    for (auto *v : {&e.h1, &e.xh1, &e.inv1, &e.qkv, &e.P, &e.att, &e.xm, &e.h2, &e.xh2, &e.inv2, &e.f1})
+        v->resize(L);
+    for (int l = 0; l <= L; ++l)
+        if ((rc = lalloc(e, &e.x[l], ND))) return rc;
+    for (int l = 0; l < L; ++l) {
+        if ((rc = lalloc(e, &e.h1[l], ND)) || (rc = lalloc(e, &e.xh1[l], ND)) || (rc = lalloc(e, &e.inv1[l], N)) ||
+            (rc = lalloc(e, &e.qkv[l], 3 * ND)) || (rc = lalloc(e, &e.P[l], (size_t)e.Bs * e.H * e.Ts * e.Ts)) ||
+            (rc = lalloc(e, &e.att[l], ND)) || (rc = lalloc(e, &e.xm[l], ND)) || (rc = lalloc(e, &e.h2[l], ND)) ||
+            (rc = lalloc(e, &e.xh2[l], ND)) || (rc = lalloc(e, &e.inv2[l], N)) ||
+            (rc = lalloc(e, &e.f1[l], (size_t)N * F)))
+            return rc;
+    }
+    if ((rc = lalloc(e, &e.hf, ND)) || (rc = lalloc(e, &e.xhf, ND)) || (rc = lalloc(e, &e.invf, N)) ||
+        (rc = lalloc(e, &e.logits, (size_t)N * V)) || (rc = lalloc(e, &e.g, ND)) || (rc = lalloc(e, &e.gm, ND)) ||
+        (rc = lalloc(e, &e.dh, ND)) || (rc = lalloc(e, &e.df1, (size_t)N * F)) || (rc = lalloc(e, &e.datt, ND)) ||
+        (rc = lalloc(e, &e.dqkv, 3 * ND)))
+        return rc;
+    e.ln_blocks = sm_count() * 2;
+    if ((rc = lalloc(e, &e.ln_partial, (size_t)e.ln_blocks * 2 * D))) return rc;
+    return kOk;
+}
+
+int attn_smem_fwd(int Ts, int dh) { return (int)((2 * (size_t)Ts * (dh + 1) + 32 * (dh + 1) + 32 * (size_t)Ts) * sizeof(float)); }
+int attn_smem_bwd(int Ts, int dh) { return (int)((4 * (size_t)Ts * (dh + 1) + (size_t)Ts * (Ts + 1)) * sizeof(float)); }
+
+}  // namespace
+
+void lm_destroy(Net &n) {
+    if (!n.lm) return;
+    cudaStreamSynchronize(stream());
+    for (void *p : n.lm->allocs) cudaFree(p);
+    delete n.lm;
+    n.lm = nullptr;
+}
+
+int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) {
+    LmEngine &e = *n.lm;
+    const int D = e.D, N = e.N, F = e.F, V = e.V, L = e.L;
+    const float *Pm = n.params;
+    float *G = n.grads;
+    const float scale = 1.0f / sqrtf((float)(D / e.H));
+    int rc;
+    // ---- forward
+    embed_fwd_kernel<<<grid_for((long long)N * D, 256, 8), 256, 0, stream()>>>(
+        tokens, Pm + e.o_tok, Pm + e.o_pos, e.x[0], N, e.Ts, D, V, device_error_word());
+    ZB_LAUNCH_CHECK("lm embedding");
+    prof_mark(n, "embed");
+    for (int l = 0; l < L; ++l) {
+        const auto &b = e.blk[l];
+        if ((rc = ln_fwd(e.x[l], Pm + b.ln1g, Pm + b.ln1b, e.h1[l], e.xh1[l], e.inv1[l], N, D))) return rc;
+        LinFwd qkv{e.h1[l], nullptr, {Pm + b.qW, Pm + b.kW, Pm + b.vW}, {Pm + b.qb, Pm + b.kb, Pm + b.vb},
+                   e.qkv[l], N, 3 * D, D, D, 3 * D, D, false};
+        if ((rc = run_simt_gemm(qkv, 1, "lm qkv"))) return rc;
+        attn_fwd_kernel<32><<<dim3(e.Bs * e.H, (e.Ts + 31) / 32), 128, attn_smem_fwd(e.Ts, 32), stream()>>>(
+            e.qkv[l], e.P[l], e.att[l], e.Ts, e.H, D, scale);
+        ZB_LAUNCH_CHECK("lm attention");
+        LinFwd o{e.att[l], e.x[l], {Pm + b.oW, nullptr, nullptr}, {Pm + b.ob, nullptr, nullptr}, e.xm[l],
+                 N, D, D, D, D, D, false};
+        if ((rc = run_simt_gemm(o, 1, "lm out proj"))) return rc;
+        if ((rc = ln_fwd(e.xm[l], Pm + b.ln2g, Pm + b.ln2b, e.h2[l], e.xh2[l], e.inv2[l], N, D))) return rc;
+        LinFwd f1{e.h2[l], nullptr, {Pm + b.f1W, nullptr, nullptr}, {Pm + b.f1b, nullptr, nullptr}, e.f1[l],
+                  N, F, D, D, F, F, true};
+        if ((rc = run_simt_gemm(f1, 1, "lm fc1"))) return rc;
+        LinFwd f2{e.f1[l], e.xm[l], {Pm + b.f2W, nullptr, nullptr}, {Pm + b.f2b, nullptr, nullptr}, e.x[l + 1],
+                  N, D, F, F, D, D, false};
+        if ((rc = run_simt_gemm(f2, 1, "lm fc2"))) return rc;
+        prof_mark(n, "block_fwd");
+    }
+    if ((rc = ln_fwd(e.x[L], Pm + e.o_lnf_g, Pm + e.o_lnf_b, e.hf, e.xhf, e.invf, N, D))) return rc;
+    LinFwd head{e.hf, nullptr, {Pm + e.o_head_W, nullptr, nullptr}, {Pm + e.o_head_b, nullptr, nullptr}, e.logits,
+                N, V, D, D, V, V, false};
+    if ((rc = run_simt_gemm(head, 1, "lm head"))) return rc;
+    if ((rc = launch_softmax_ce(e.logits, targets, n.dlogits, n.row_loss, loss_out, N, V, true))) return rc;
+    prof_mark(n, "head_ce");
+    // ---- backward
+    {
+        LinWgrad wg{e.hf, n.dlogits, {G + e.o_head_W, nullptr, nullptr}, D, V, N, D, V, V};
+        if ((rc = run_simt_gemm(wg, 0, "lm head dW"))) return rc;
+        if ((rc = colsum(n.dlogits, N, V, V, G + e.o_head_b))) return rc;
+        LinDgrad dg{n.dlogits, nullptr, {Pm + e.o_head_W, nullptr, nullptr}, e.dh, N, D, V, D, V, V};
+        if ((rc = run_simt_gemm(dg, 1, "lm head dX"))) return rc;
+        if ((rc = ln_bwd(e, e.dh, e.xhf, e.invf, Pm + e.o_lnf_g, nullptr, e.g, G + e.o_lnf_g, G + e.o_lnf_b))) return rc;
+    }
+    prof_mark(n, "head_bwd");
+    for (int l = L - 1; l >= 0; --l) {
+        const auto &b = e.blk[l];
+        // FFN
+        LinWgrad w2{e.f1[l], e.g, {G + b.f2W, nullptr, nullptr}, F, D, N, F, D, D};
+        if ((rc = run_simt_gemm(w2, 0, "lm fc2 dW"))) return rc;
+        if ((rc = colsum(e.g, N, D, D, G + b.f2b))) return rc;
+        LinDgrad d2{e.g, e.f1[l], {Pm + b.f2W, nullptr, nullptr}, e.df1, N, F, D, F, D, D};
+        if ((rc = run_simt_gemm(d2, 1, "lm fc2 dX"))) return rc;
+        LinWgrad w1{e.h2[l], e.df1, {G + b.f1W, nullptr, nullptr}, D, F, N, D, F, F};
+        if ((rc = run_simt_gemm(w1, 0, "lm fc1 dW"))) return rc;
+        if ((rc = colsum(e.df1, N, F, F, G + b.f1b))) return rc;
+        LinDgrad d1{e.df1, nullptr, {Pm + b.f1W, nullptr, nullptr}, e.dh, N, D, F, D, F, F};
+        if ((rc = run_simt_gemm(d1, 1, "lm fc1 dX"))) return rc;
+        if ((rc = ln_bwd(e, e.dh, e.xh2[l], e.inv2[l], Pm + b.ln2g, e.g, e.gm, G + b.ln2g, G + b.ln2b))) return rc;
+        // attention
+        LinWgrad wo{e.att[l], e.gm, {G + b.oW, nullptr, nullptr}, D, D, N, D, D, D};
+        if ((rc = run_simt_gemm(wo, 0, "lm out dW"))) return rc;
+        if ((rc = colsum(e.gm, N, D, D, G + b.ob))) return rc;
+        LinDgrad dout{e.gm, nullptr, {Pm + b.oW, nullptr, nullptr}, e.datt, N, D, D, D, D, D};
+        if ((rc = run_simt_gemm(dout, 1, "lm out dX"))) return rc;
+        attn_bwd_kernel<32><<<e.Bs * e.H, 256, attn_smem_bwd(e.Ts, 32), stream()>>>(e.qkv[l], e.P[l], e.datt,
+                                                                                  e.dqkv, e.Ts, e.H, D, scale);
+        ZB_LAUNCH_CHECK("lm attention backward");
+        LinWgrad wq{e.h1[l], e.dqkv, {G + b.qW, G + b.kW, G + b.vW}, D, 3 * D, N, D, 3 * D, D};
+        if ((rc = run_simt_gemm(wq, 0, "lm qkv dW"))) return rc;
+        if ((rc = colsum(e.dqkv, N, 3 * D, D, G + b.qb, G + b.kb, G + b.vb))) return rc;
+        LinDgrad dq{e.dqkv, nullptr, {Pm + b.qW, Pm + b.kW, Pm + b.vW}, e.dh, N, D, 3 * D, D, 3 * D, D};
+        if ((rc = run_simt_gemm(dq, 1, "lm qkv dX"))) return rc;
+        if ((rc = ln_bwd(e, e.dh, e.xh1[l], e.inv1[l], Pm + b.ln1g, e.gm, e.g, G + b.ln1g, G + b.ln1b))) return rc;
+        prof_mark(n, "block_bwd");
+    }
+    embed_bwd_kernel<<<grid_for((long long)(V + e.T) * D, 128, 8), 128, 0, stream()>>>(
+        e.g, tokens, G + e.o_tok, G + e.o_pos, N, e.Ts, D, V, e.T);
+    ZB_LAUNCH_CHECK("lm embedding backward");
+    prof_mark(n, "embed_bwd");
+    return kOk;
+}
+
+}  // namespace zb
+
+using namespace zb;
+
+extern "C" int zilla_lm_create(int vocab, int dim, int heads, int layers, int max_seq, int ffn, int batch,
+                               int seq) {
+    if (vocab <= 0 || dim <= 0 || heads <= 0 || layers <= 0 || ffn <= 0 || batch <= 0 || seq <= 0)
+        return fail(kBadArg, "zilla_lm_create: bad arguments");
+    if (dim % heads || dim / heads != 32)
+        return fail(kBadArg, "zilla_lm_create: head dimension must be 32 (dim %d, heads %d)", dim, heads);
+    if (dim % 32 || dim > 1024) return fail(kBadArg, "zilla_lm_create: dim must be a multiple of 32, <= 1024");
+    if (seq > max_seq) return fail(kBadArg, "zilla_lm_create: sequence length %d exceeds max %d", seq, max_seq);
+    if (attn_smem_bwd(seq, 32) > 227 * 1024)   // one (sequence, head) of the backward lives in shared memory
+        return fail(kBadArg, "zilla_lm_create: sequence length %d above the supported 176", seq);
+    if (layers > 64) return fail(kBadArg, "zilla_lm_create: too many layers");
+    Net *n = new Net();
+    LmEngine *e = new LmEngine();
+    e->V = vocab; e->D = dim; e->H = heads; e->L = layers; e->T = max_seq; e->F = ffn;
+    e->Bs = batch; e->Ts = seq; e->N = batch * seq;
+    n->lm = e;
+    n->B = e->N;
+    n->classes = vocab;
+    n->precision = 0;
+    int rc = lm_build(*n, *e);
+    n->x_floats = e->N;
+    n->y_floats = e->N;
+    if (!rc) rc = net_alloc_common(*n, (long long)e->N * vocab, e->N);
+    if (!rc) {
+        const int fs = attn_smem_fwd(seq, 32), bs = attn_smem_bwd(seq, 32);
+        if (cudaFuncSetAttribute(attn_fwd_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, fs) != cudaSuccess ||
+            cudaFuncSetAttribute(attn_bwd_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bs) != cudaSuccess ||
+            cudaFuncSetAttribute(ln_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 8 * 2 * dim * (int)sizeof(float)) != cudaSuccess)
+            rc = check_cuda("zilla_lm_create: attention shared memory");
+    }
+    if (!rc) rc = check_cuda("zilla_lm_create");
+    if (rc) {
+        net_free(n);
+        return rc;
+    }
+    return net_register(n);
+}

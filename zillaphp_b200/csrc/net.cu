@@ -179,6 +179,7 @@ void free_net(Net *n) {
     if (!n) return;
     cudaStreamSynchronize(stream());
     if (n->tc) tc_destroy(*n);
+    if (n->lm) lm_destroy(*n);
     for (auto &s : n->st) {
         if (s.out) cudaFree(s.out);
         if (s.gin) cudaFree(s.gin);
@@ -210,6 +211,39 @@ void prof_mark(Net &n, const char *label) {
     n.ev_label[n.ev_used] = label;
     cudaEventRecord(n.ev_pool[n.ev_used], stream());
     n.ev_used += 1;
+}
+
+int net_register(Net *n) {
+    n->id = g_next_net++;
+    g_nets[n->id] = n;
+    return n->id;
+}
+
+void net_free(Net *n) { free_net(n); }
+
+// Flat parameter / gradient buffers (registry handles; gradients carry the
+// loss sum in one extra slot), Adam moments, dlogits [classes_rows], per-row
+// loss and host-step staging for x_floats / y_floats inputs.
+int net_alloc_common(Net &n, long long classes_rows, long long rows) {
+    n.params_id = zilla_buffer_alloc((unsigned long)(n.nparams > 0 ? n.nparams : 1));
+    n.grads_id = zilla_buffer_alloc((unsigned long)n.nparams + 1);
+    if (n.params_id <= 0 || n.grads_id <= 0) return kBadHandle;
+    n.params = ptr(n.params_id);
+    n.grads = ptr(n.grads_id);
+    const size_t pbytes = (size_t)(n.nparams + 1) * sizeof(float);
+    int rc = alloc_dev((void **)&n.m, pbytes);
+    if (!rc) rc = alloc_dev((void **)&n.v, pbytes);
+    if (!rc) rc = alloc_dev((void **)&n.dlogits, (size_t)classes_rows * sizeof(float));
+    if (!rc) rc = alloc_dev((void **)&n.row_loss, (size_t)rows * sizeof(double));
+    if (!rc) rc = alloc_dev((void **)&n.xin, (size_t)n.x_floats * sizeof(float));
+    if (!rc) rc = alloc_dev((void **)&n.yin, (size_t)n.y_floats * sizeof(float));
+    if (!rc) rc = alloc_dev((void **)&n.loss_dev, sizeof(float));
+    if (rc) return rc;
+    cudaMemsetAsync(n.params, 0, pbytes - sizeof(float), stream());
+    cudaMemsetAsync(n.grads, 0, pbytes, stream());
+    cudaMemsetAsync(n.m, 0, pbytes, stream());
+    cudaMemsetAsync(n.v, 0, pbytes, stream());
+    return check_cuda("net_alloc_common");
 }
 
 Net *net_get(int id) {
@@ -345,7 +379,9 @@ static int run_step(Net &n, const float *x, const float *y, int update) {
     float *loss_slot = n.grads + n.nparams;
     int rc;
     prof_mark(n, "start");
-    if (n.precision == 1) {
+    if (n.lm) {
+        rc = lm_step(n, x, y, loss_slot);
+    } else if (n.precision == 1) {
         rc = tc_step(n, x, y, loss_slot);
     } else {
         rc = fp32_forward(n, x);
@@ -381,24 +417,10 @@ int zilla_net_create(const int *layers, int n_layers, int batch, int in_c, int i
     n->spec.assign(layers, layers + 4 * n_layers);
     int rc = build_stages(*n);
     if (rc) { delete n; return rc; }
-    n->params_id = zilla_buffer_alloc((unsigned long)(n->nparams > 0 ? n->nparams : 1));
-    n->grads_id = zilla_buffer_alloc((unsigned long)n->nparams + 1);
-    if (n->params_id <= 0 || n->grads_id <= 0) { free_net(n); return kBadHandle; }
-    n->params = ptr(n->params_id);
-    n->grads = ptr(n->grads_id);
-    const size_t pbytes = (size_t)(n->nparams + 1) * sizeof(float);
-    rc = alloc_dev((void **)&n->m, pbytes);
-    if (!rc) rc = alloc_dev((void **)&n->v, pbytes);
-    if (!rc) rc = alloc_dev((void **)&n->dlogits, (size_t)batch * n->classes * sizeof(float));
-    if (!rc) rc = alloc_dev((void **)&n->row_loss, (size_t)batch * sizeof(double));
-    if (!rc) rc = alloc_dev((void **)&n->xin, (size_t)batch * in_c * in_h * in_w * sizeof(float));
-    if (!rc) rc = alloc_dev((void **)&n->yin, (size_t)batch * sizeof(float));
-    if (!rc) rc = alloc_dev((void **)&n->loss_dev, sizeof(float));
+    n->x_floats = (long long)batch * in_c * in_h * in_w;
+    n->y_floats = batch;
+    rc = net_alloc_common(*n, (long long)batch * n->classes, batch);
     if (rc) { free_net(n); return rc; }
-    cudaMemsetAsync(n->params, 0, pbytes - sizeof(float), stream());
-    cudaMemsetAsync(n->grads, 0, pbytes, stream());
-    cudaMemsetAsync(n->m, 0, pbytes, stream());
-    cudaMemsetAsync(n->v, 0, pbytes, stream());
     if (precision == 0) {
         for (size_t i = 0; i < n->st.size(); ++i) {
             Stage &s = n->st[i];
@@ -422,9 +444,7 @@ int zilla_net_create(const int *layers, int n_layers, int batch, int in_c, int i
     }
     if (!rc) rc = check_cuda("zilla_net_create");
     if (rc) { free_net(n); return rc; }
-    n->id = g_next_net++;
-    g_nets[n->id] = n;
-    return n->id;
+    return net_register(n);
 }
 
 int zilla_net_destroy(int id) {
@@ -471,9 +491,9 @@ int zilla_net_step(int id, int x_id, int y_id, int loss_id, int update) {
     if (!n) return fail(kBadHandle, "zilla_net_step: unknown net %d", id);
     float *x = ptr(x_id), *y = ptr(y_id), *loss = ptr(loss_id);
     if (!x || !y || !loss) return fail(kBadHandle, "zilla_net_step: invalid handle");
-    if (capacity(x_id) < (size_t)n->B * n->st[0].in_n || capacity(y_id) < (size_t)n->B)
+    if (capacity(x_id) < (size_t)n->x_floats || capacity(y_id) < (size_t)n->y_floats)
         return fail(kBadHandle, "zilla_net_step: input buffers smaller than the batch");
-    if (n->precision == 0 && n->st[0].C == 0) return kBadArg;
+
     int rc = run_step(*n, x, y, update);
     if (rc) return rc;
     cudaMemcpyAsync(loss, n->grads + n->nparams, sizeof(float), cudaMemcpyDeviceToDevice, stream());
@@ -484,8 +504,8 @@ int zilla_net_step_host(int id, const float *x, const float *y, float *loss_sum,
     Net *n = net_get(id);
     if (!n) return fail(kBadHandle, "zilla_net_step_host: unknown net %d", id);
     if (!x || !y) return fail(kBadArg, "zilla_net_step_host: null input");
-    cudaMemcpyAsync(n->xin, x, (size_t)n->B * n->st[0].in_n * sizeof(float), cudaMemcpyHostToDevice, stream());
-    cudaMemcpyAsync(n->yin, y, (size_t)n->B * sizeof(float), cudaMemcpyHostToDevice, stream());
+    cudaMemcpyAsync(n->xin, x, (size_t)n->x_floats * sizeof(float), cudaMemcpyHostToDevice, stream());
+    cudaMemcpyAsync(n->yin, y, (size_t)n->y_floats * sizeof(float), cudaMemcpyHostToDevice, stream());
     int rc = run_step(*n, n->xin, n->yin, update);
     if (rc) return rc;
     if (loss_sum) {

@@ -34,6 +34,7 @@ struct Stage {
 };
 
 struct TcEngine;  // bf16 tensor-core engine (tc_net.cu)
+struct LmEngine;  // Transformer language-model engine (lm_net.cu)
 
 struct Net {
     int id = 0;
@@ -57,6 +58,8 @@ struct Net {
     ncclComm_t comm = nullptr;
 #endif
     TcEngine *tc = nullptr;
+    LmEngine *lm = nullptr;
+    long long x_floats = 0, y_floats = 0;   // per-step input sizes (floats)
     // per-segment device timing (zilla_net_profile / zilla_net_timings)
     bool profile = false;
     std::vector<cudaEvent_t> ev_pool;
@@ -78,5 +81,12 @@ void tc_destroy(Net &n);
 int tc_step(Net &n, const float *x, const float *y, float *loss_out);
 int tc_sync_params(Net &n);   // refresh the bf16 operand copies from the fp32 master
 int tc_inspect(Net &n, int index, char *name, int name_len, float *host, unsigned long n_floats);
+// language-model engine (lm_net.cu)
+void lm_destroy(Net &n);
+int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out);
+// registry helpers shared by the engines (net.cu)
+int net_register(Net *n);             // assigns the id, returns it
+void net_free(Net *n);                // releases everything a Net holds
+int net_alloc_common(Net &n, long long classes_rows, long long rows);   // params, grads, Adam, staging
 
 }  // namespace zb

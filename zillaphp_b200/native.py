@@ -87,6 +87,7 @@ SIGNATURES: dict[str, tuple] = {
     "zilla_net_timings": (I, [I, C.c_char_p, I, FP, I]),
     "zilla_net_inspect": (I, [I, I, C.c_char_p, I, FP, UL]),
     "zilla_net_device_status": (I, [I]),
+    "zilla_lm_create": (I, [I] * 8),
     "zilla_dp_unique_id": (I, [C.c_char_p]),
     "zilla_dp_attach": (I, [I, I, I, C.c_char_p]),
     "zilla_dp_detach": (I, [I]),

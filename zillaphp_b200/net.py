@@ -6,7 +6,7 @@ import ctypes as C
 import numpy as np
 
 from . import native
-from .configs import ADAM, Workload
+from .configs import ADAM, LmWorkload, Workload
 
 
 class Net:
@@ -114,6 +114,29 @@ class Net:
             self.close()
         except Exception:
             pass
+
+
+class LM(Net):
+    """A Transformer language model trained by one C call per step
+    (zilla_lm_create + zilla_net_step): x and y are the batch*seq token ids
+    and next-token ids, as floats."""
+
+    def __init__(self, workload: LmWorkload, batch: int | None = None, seq: int | None = None):
+        self.w = workload
+        self.lib = native.load()
+        self.batch = batch if batch is not None else workload.batch
+        self.seq = seq if seq is not None else workload.seq
+        self.precision = 0
+        w = workload
+        self.id = self.lib.zilla_lm_create(w.vocab, w.dim, w.heads, w.layers, w.max_seq, w.ffn, self.batch,
+                                           self.seq)
+        if self.id <= 0:
+            raise RuntimeError(f"zilla_lm_create failed: {native.last_error()}")
+        self.nparams = int(self.lib.zilla_net_param_count(self.id))
+        b1, b2, eps = w.adam
+        self._check(self.lib.zilla_net_set_optimizer(self.id, w.optimizer, w.lr, b1, b2, eps))
+        self.params_id = self.lib.zilla_net_params_id(self.id)
+        self.grads_id = self.lib.zilla_net_grads_id(self.id)
 
 
 def dp_unique_id() -> bytes:

@@ -5,6 +5,11 @@ against the float64 oracle restatement of TransformerLM training
 Tolerances (fp32 device arithmetic against float64):
   loss sum            relative 1e-5
   gradients           1e-4 normwise over the whole flat buffer, 1e-3 per tensor
+                      (a tensor's error is taken relative to its own largest
+                      entry, floored at 1e-4 of the whole buffer's: the key-bias
+                      gradient is analytically zero -- a bias on every key shifts
+                      a score row by a constant, which softmax ignores -- so
+                      both sides hold only rounding noise there)
   updated parameters  the oracle's Adam applied to the device's own gradients,
                       1e-6 absolute (the update kernel is checked apart from the
                       gradient error that Adam's sign-like first step amplifies)
@@ -35,14 +40,12 @@ def oracle_step(w, flat, tok, tgt, batch, seq, **kw):
 
 def per_tensor(w, got, ref):
     worst, off = ("", 0.0), 0
+    floor = 1e-4 * np.max(np.abs(ref))
     for name, shape in synthetic.lm_layout(w):
         n = int(np.prod(shape))
         a, b = got[off:off + n], ref[off:off + n]
         off += n
-        if np.linalg.norm(b) == 0:
-            assert np.all(a == 0), name
-            continue
-        e = npref.normwise(a, b)
+        e = float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), floor))
         if e > worst[1]:
             worst = (name, e)
     return worst

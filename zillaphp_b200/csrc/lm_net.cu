@@ -40,6 +40,7 @@ struct LmEngine {
     // gradients
     float *g = nullptr, *gm = nullptr, *dh = nullptr, *df1 = nullptr, *datt = nullptr, *dqkv = nullptr;
     float *ln_partial = nullptr;   // [ln_blocks][2D]
+    float *emb_partial = nullptr;  // [row chunks][V][D]
     int ln_blocks = 0;
     std::vector<void *> allocs;
 };
@@ -354,19 +355,40 @@ __global__ void __launch_bounds__(256) attn_bwd_kernel(const float *__restrict__
     }
 }
 
-// dTok[v][d] = sum over rows with token v of g[row][d] (row order); dPos[t][d]
-// = sum over sequences of g[b*T + t][d].
-__global__ void embed_bwd_kernel(const float *__restrict__ g, const float *__restrict__ tokens,
+// Embedding backward (the one-hot matmul's gradient, src/NN/Layers/Embedding.php:35-56),
+// in two fixed-order passes.  Pass 1: for each chunk of kEmbChunk rows,
+// part[chunk][v][d] = sum over the chunk's rows with token v of g[row][d].
+constexpr int kEmbChunk = 256;
+
+__global__ void __launch_bounds__(256) embed_tok_partial_kernel(const float *__restrict__ g,
+                                                                const float *__restrict__ tokens,
+                                                                float *__restrict__ part, int N, int D, int V) {
+    __shared__ int ids[kEmbChunk];
+    const int r0 = blockIdx.y * kEmbChunk;
+    const int rows = min(kEmbChunk, N - r0);
+    for (int k = threadIdx.x; k < rows; k += blockDim.x) ids[k] = (int)tokens[r0 + k];
+    __syncthreads();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= V * D) return;
+    const int v = i / D, d = i % D;
+    float s = 0.0f;
+    for (int k = 0; k < rows; ++k)
+        if (ids[k] == v) s += g[(size_t)(r0 + k) * D + d];
+    part[((size_t)blockIdx.y * V + v) * D + d] = s;
+}
+
+// Pass 2: dTok[v][d] = sum of the chunk partials in chunk order; dPos[t][d] =
+// sum over sequences of g[b*T + t][d] (positions >= T are unused: zero).
+__global__ void embed_bwd_kernel(const float *__restrict__ g, const float *__restrict__ part,
                                  float *__restrict__ dtok, float *__restrict__ dpos, int N, int Ts, int D, int V,
-                                 int Tmax) {
+                                 int Tmax, int chunks) {
     const int Bs = N / Ts;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (long long)(V + Tmax) * D;
          i += (long long)gridDim.x * blockDim.x) {
         const int row = (int)(i / D), d = (int)(i % D);
         float s = 0.0f;
         if (row < V) {
-            for (int r = 0; r < N; ++r)
-                if ((int)tokens[r] == row) s += g[(size_t)r * D + d];
+            for (int c = 0; c < chunks; ++c) s += part[((size_t)c * V + row) * D + d];
             dtok[(size_t)row * D + d] = s;
         } else {
             const int t = row - V;
@@ -454,6 +476,7 @@ int lm_build(Net &n, LmEngine &e) {
         return rc;
     e.ln_blocks = sm_count() * 2;
     if ((rc = lalloc(e, &e.ln_partial, (size_t)e.ln_blocks * 2 * D))) return rc;
+    if ((rc = lalloc(e, &e.emb_partial, (size_t)((N + kEmbChunk - 1) / kEmbChunk) * V * D))) return rc;
     return kOk;
 }
 
@@ -488,9 +511,11 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
         LinFwd qkv{e.h1[l], nullptr, {Pm + b.qW, Pm + b.kW, Pm + b.vW}, {Pm + b.qb, Pm + b.kb, Pm + b.vb},
                    e.qkv[l], N, 3 * D, D, D, 3 * D, D, false};
         if ((rc = run_simt_gemm(qkv, 1, "lm qkv"))) return rc;
+        prof_mark(n, "ln1_qkv");
         attn_fwd_kernel<32><<<dim3(e.Bs * e.H, (e.Ts + 31) / 32), 128, attn_smem_fwd(e.Ts, 32), stream()>>>(
             e.qkv[l], e.P[l], e.att[l], e.Ts, e.H, D, scale);
         ZB_LAUNCH_CHECK("lm attention");
+        prof_mark(n, "attn_fwd");
         LinFwd o{e.att[l], e.x[l], {Pm + b.oW, nullptr, nullptr}, {Pm + b.ob, nullptr, nullptr}, e.xm[l],
                  N, D, D, D, D, D, false};
         if ((rc = run_simt_gemm(o, 1, "lm out proj"))) return rc;
@@ -501,7 +526,7 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
         LinFwd f2{e.f1[l], e.xm[l], {Pm + b.f2W, nullptr, nullptr}, {Pm + b.f2b, nullptr, nullptr}, e.x[l + 1],
                   N, D, F, F, D, D, false};
         if ((rc = run_simt_gemm(f2, 1, "lm fc2"))) return rc;
-        prof_mark(n, "block_fwd");
+        prof_mark(n, "oproj_ln2_ffn");
     }
     if ((rc = ln_fwd(e.x[L], Pm + e.o_lnf_g, Pm + e.o_lnf_b, e.hf, e.xhf, e.invf, N, D))) return rc;
     LinFwd head{e.hf, nullptr, {Pm + e.o_head_W, nullptr, nullptr}, {Pm + e.o_head_b, nullptr, nullptr}, e.logits,
@@ -533,6 +558,7 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
         LinDgrad d1{e.df1, nullptr, {Pm + b.f1W, nullptr, nullptr}, e.dh, N, D, F, D, F, F};
         if ((rc = run_simt_gemm(d1, 1, "lm fc1 dX"))) return rc;
         if ((rc = ln_bwd(e, e.dh, e.xh2[l], e.inv2[l], Pm + b.ln2g, e.g, e.gm, G + b.ln2g, G + b.ln2b))) return rc;
+        prof_mark(n, "ffn_ln2_bwd");
         // attention
         LinWgrad wo{e.att[l], e.gm, {G + b.oW, nullptr, nullptr}, D, D, N, D, D, D};
         if ((rc = run_simt_gemm(wo, 0, "lm out dW"))) return rc;
@@ -542,16 +568,21 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
         attn_bwd_kernel<32><<<e.Bs * e.H, 256, attn_smem_bwd(e.Ts, 32), stream()>>>(e.qkv[l], e.P[l], e.datt,
                                                                                   e.dqkv, e.Ts, e.H, D, scale);
         ZB_LAUNCH_CHECK("lm attention backward");
+        prof_mark(n, "oproj_attn_bwd");
         LinWgrad wq{e.h1[l], e.dqkv, {G + b.qW, G + b.kW, G + b.vW}, D, 3 * D, N, D, 3 * D, D};
         if ((rc = run_simt_gemm(wq, 0, "lm qkv dW"))) return rc;
         if ((rc = colsum(e.dqkv, N, 3 * D, D, G + b.qb, G + b.kb, G + b.vb))) return rc;
         LinDgrad dq{e.dqkv, nullptr, {Pm + b.qW, Pm + b.kW, Pm + b.vW}, e.dh, N, D, 3 * D, D, 3 * D, D};
         if ((rc = run_simt_gemm(dq, 1, "lm qkv dX"))) return rc;
         if ((rc = ln_bwd(e, e.dh, e.xh1[l], e.inv1[l], Pm + b.ln1g, e.gm, e.g, G + b.ln1g, G + b.ln1b))) return rc;
-        prof_mark(n, "block_bwd");
+        prof_mark(n, "qkv_ln1_bwd");
     }
-    embed_bwd_kernel<<<grid_for((long long)(V + e.T) * D, 128, 8), 128, 0, stream()>>>(
-        e.g, tokens, G + e.o_tok, G + e.o_pos, N, e.Ts, D, V, e.T);
+    const int chunks = (N + kEmbChunk - 1) / kEmbChunk;
+    embed_tok_partial_kernel<<<dim3((V * D + 255) / 256, chunks), 256, 0, stream()>>>(e.g, tokens, e.emb_partial,
+                                                                                    N, D, V);
+    ZB_LAUNCH_CHECK("lm embedding backward (partials)");
+    embed_bwd_kernel<<<grid_for((long long)(V + e.T) * D, 256, 8), 256, 0, stream()>>>(
+        e.g, e.emb_partial, G + e.o_tok, G + e.o_pos, N, e.Ts, D, V, e.T, chunks);
     ZB_LAUNCH_CHECK("lm embedding backward");
     prof_mark(n, "embed_bwd");
     return kOk;

@@ -28,9 +28,7 @@ import ctypes
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 import numpy as np
@@ -54,52 +52,68 @@ def peaks() -> tuple[dict, str]:
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled every 2 ms through
+    NVML (read-only queries) on a background thread during the timed region;
+    timed regions are tens of milliseconds, too short for nvidia-smi's loop."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "hw_power_brake_slowdown": 0x80, "sw_power_cap": 0x4}
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
-        self.path = None
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self.err = None
+        self._stop = None
+        self._thread = None
 
     def start(self):
-        fd, self.path = tempfile.mkstemp(suffix=".csv")
-        os.close(fd)
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        import threading
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            h = None
+            try:
+                import torch
+                uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+                h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001
+            self.err = f"NVML unavailable: {e}"
+            return
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    for name, bit in self.REASONS.items():
+                        if r & bit:
+                            self.reasons.add(name)
+                except Exception as e:  # noqa: BLE001
+                    self.err = str(e)
+                    return
+                self._stop.wait(0.002)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
+        time.sleep(0.01)    # first samples before the timed region starts
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9:
-                    continue
-                try:
-                    sm.append(float(parts[1]))
-                    mx.append(float(parts[2]))
-                except ValueError:
-                    continue
-                for nm, v in zip(names, parts[5:9]):
-                    if v.lower() == "active":
-                        reasons.add(nm)
-        os.unlink(self.path)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if self._thread is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err or "not sampled"], "samples": 0}
+        self._stop.set()
+        self._thread.join(timeout=2)
+        sm = self.samples
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+               "reasons": sorted(self.reasons), "samples": len(sm), "source": "NVML, 2 ms polling"}
+        if sm:
+            out["sm_mhz_min"] = min(sm)
+        return out
 
 
 # ------------------------------------------------------------------ work model

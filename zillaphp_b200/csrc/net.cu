@@ -175,6 +175,15 @@ int alloc_dev(void **p, size_t bytes) {
     return kOk;
 }
 
+void dp_release_streams(Net &n) {
+    if (n.comm_stream) { cudaStreamSynchronize(n.comm_stream); cudaStreamDestroy(n.comm_stream); }
+    if (n.ev_ready) cudaEventDestroy(n.ev_ready);
+    if (n.ev_done) cudaEventDestroy(n.ev_done);
+    n.comm_stream = nullptr;
+    n.ev_ready = n.ev_done = nullptr;
+    n.ar_lo = -1;
+}
+
 void free_net(Net *n) {
     if (!n) return;
     cudaStreamSynchronize(stream());
@@ -194,6 +203,7 @@ void free_net(Net *n) {
 #ifdef ZB_HAVE_NCCL
     if (n->comm) ncclCommDestroy(n->comm);
 #endif
+    dp_release_streams(*n);
     for (auto e : n->ev_pool) cudaEventDestroy(e);
     delete n;
 }
@@ -354,16 +364,43 @@ int fp32_backward(Net &n, const float *x) {
     return kOk;
 }
 
-// Sum of gradients (and the loss slot) over the data-parallel ranks.
-static int allreduce_grads(Net &n) {
-    if (n.world <= 1) return kOk;
+// All-reduce (sum) of grads[lo, hi) on the comm stream, after everything
+// enqueued so far on the library stream.
+static int allreduce_range(Net &n, long long lo, long long hi) {
 #ifdef ZB_HAVE_NCCL
-    ncclResult_t r = ncclAllReduce(n.grads, n.grads, (size_t)n.nparams + 1, ncclFloat, ncclSum, n.comm, stream());
+    if (hi <= lo) return kOk;
+    if (cudaEventRecord(n.ev_ready, stream()) != cudaSuccess ||
+        cudaStreamWaitEvent(n.comm_stream, n.ev_ready, 0) != cudaSuccess)
+        return check_cuda("net: all-reduce ordering");
+    ncclResult_t r = ncclAllReduce(n.grads + lo, n.grads + lo, (size_t)(hi - lo), ncclFloat, ncclSum, n.comm,
+                                   n.comm_stream);
     if (r != ncclSuccess) return fail(kCudaError, "net: ncclAllReduce failed: %s", ncclGetErrorString(r));
     return kOk;
 #else
+    (void)n; (void)lo; (void)hi;
     return fail(kBadArg, "net: built without NCCL");
 #endif
+}
+
+int dp_bucket_ready(Net &n, long long off) {
+    if (n.world <= 1 || n.ar_lo >= 0) return kOk;
+    n.ar_lo = off;
+    return allreduce_range(n, off, n.nparams + 1);
+}
+
+// Sum of gradients (and the loss slot) over the data-parallel ranks: the part
+// not started early by dp_bucket_ready, then the library stream waits for the
+// comm stream.  Every rank issues the same calls in the same order.
+static int allreduce_grads(Net &n) {
+    if (n.world <= 1) return kOk;
+    const long long hi = n.ar_lo >= 0 ? n.ar_lo : n.nparams + 1;
+    n.ar_lo = -1;
+    int rc = allreduce_range(n, 0, hi);
+    if (rc) return rc;
+    if (cudaEventRecord(n.ev_done, n.comm_stream) != cudaSuccess ||
+        cudaStreamWaitEvent(stream(), n.ev_done, 0) != cudaSuccess)
+        return check_cuda("net: all-reduce completion");
+    return kOk;
 }
 
 static int optimizer_step(Net &n) {
@@ -589,6 +626,15 @@ int zilla_dp_attach(int id, int rank, int world, const unsigned char *id128) {
         n->comm = nullptr;
         return fail(kCudaError, "zilla_dp_attach: ncclCommInitRank failed: %s", ncclGetErrorString(r));
     }
+    if (!n->comm_stream &&
+        (cudaStreamCreateWithFlags(&n->comm_stream, cudaStreamNonBlocking) != cudaSuccess ||
+         cudaEventCreateWithFlags(&n->ev_ready, cudaEventDisableTiming) != cudaSuccess ||
+         cudaEventCreateWithFlags(&n->ev_done, cudaEventDisableTiming) != cudaSuccess)) {
+        dp_release_streams(*n);
+        ncclCommDestroy(n->comm);
+        n->comm = nullptr;
+        return check_cuda("zilla_dp_attach: comm stream");
+    }
     n->rank = rank;
     n->world = world;
     return kOk;
@@ -604,6 +650,7 @@ int zilla_dp_detach(int id) {
 #ifdef ZB_HAVE_NCCL
     if (n->comm) {
         cudaStreamSynchronize(stream());
+        dp_release_streams(*n);
         ncclCommDestroy(n->comm);
         n->comm = nullptr;
     }

@@ -57,6 +57,9 @@ struct Net {
 #ifdef ZB_HAVE_NCCL
     ncclComm_t comm = nullptr;
 #endif
+    cudaStream_t comm_stream = nullptr;        // all-reduce stream (data parallel)
+    cudaEvent_t ev_ready = nullptr, ev_done = nullptr;
+    long long ar_lo = -1;                      // grads [ar_lo, nparams] already launched this step
     TcEngine *tc = nullptr;
     LmEngine *lm = nullptr;
     long long x_floats = 0, y_floats = 0;   // per-step input sizes (floats)
@@ -84,6 +87,10 @@ int tc_inspect(Net &n, int index, char *name, int name_len, float *host, unsigne
 // language-model engine (lm_net.cu)
 void lm_destroy(Net &n);
 int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out);
+// Data parallel: grads[off .. nparams] (the loss slot included) are final for
+// this step; starts their all-reduce on the comm stream so that it overlaps
+// the rest of the backward.  No-op on one rank.
+int dp_bucket_ready(Net &n, long long off);
 // registry helpers shared by the engines (net.cu)
 int net_register(Net *n);             // assigns the id, returns it
 void net_free(Net *n);                // releases everything a Net holds

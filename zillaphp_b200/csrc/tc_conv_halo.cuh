@@ -1,0 +1,377 @@
+// tc_conv_halo.cuh -- implicit-GEMM 3x3 (stride 1, pad 1) convolution on
+// tcgen05 with one halo tile per output tile.
+//
+// D[pixel, n] = sum_{tap, c} IN[pixel + tap offset, c] * Wt[tap][n][c]
+//   forward:        IN = activations x (NHWC bf16), Wt[tap][co][ci] = W[co][ci][tap]
+//   input gradient: IN = dY (NHWC bf16),            Wt[tap][ci][co] = W[co][ci][8 - tap]
+// (the input gradient of a stride-1, pad-1 3x3 conv is the same convolution
+// of dY with the flipped, channel-transposed kernel).
+//
+// Output tile: R image rows of one image.  Its input, rows h0-1 .. h0+R and
+// columns -1 .. W (Wp = W + 2 wide, zero outside the image: TMA's
+// out-of-bounds fill is the padding), is loaded ONCE per tile, in 8-channel
+// groups: group g holds the HR = (R+2)*Wp halo pixels as 16-byte rows,
+//     smem[g][rr * Wp + cc][8 channels]        (rr, cc halo coordinates).
+// That is the canonical K-major no-swizzle UMMA layout (8-row core matrices of
+// 16-byte rows, SBO = 128 B between 8-row groups, LBO = the group pitch
+// between the two 8-channel halves of a K16 step), so MMA row i can be the
+// output pixel (i / Wp, i % Wp) for every tap at once: tap (dh, dw) is the
+// same descriptor started dh*Wp + dw rows further on.  Rows with
+// i % Wp >= W or i / Wp >= R are padding of the M = 128 tile; they read
+// halo rows that feed only those discarded outputs.
+// Compared with one shifted TMA box per tap, the L2 -> SM traffic per tile
+// falls from 9 boxes to (R+2)/R of one, which is what let the pipeline keep
+// the tensor pipe fed.
+//
+// The packed weights of all 9 taps stay resident in shared memory
+// (K-major, 128/64-byte swizzle).  KS > 1 splits a tile's channels over KS
+// pipeline stages (wide inputs: 128 channels of dY).
+//
+// Warp roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer and TMEM
+// owner, warps 2-9 epilogue in two groups of four: group g = (warp - 2) / 4
+// takes the 32-channel accumulator chunks g, g + 2, ... of TMEM lane quarter
+// warp % 4.  The epilogue is latency-bound (TMEM loads, staging, barriers,
+// stores), so eight warps per CTA keep the tensor pipe fed.  The pool
+// epilogue stages bias + ReLU rows (bf16, all channels) in shared memory and
+// then pools with consecutive threads on consecutive channel octets of
+// adjacent windows, so each warp's stores are contiguous.  Accumulators are
+// double-buffered in TMEM so the epilogue of tile i overlaps the MMAs of tile
+// i+1.  Epilogues:
+//   kEpiPool : relu(acc + bias), 2x2/2 max-pool with the reference tie rule
+//              (first maximum in (kh, kw) order, native/cpu/zilla_cpu.c:215-224)
+//              on the bf16-rounded values (rounding is monotonic, so the
+//              pooled value equals the rounded fp32 maximum), pooled bf16
+//              NHWC out + a code byte per output
+//              (window position 0..3 | (max > 0) << 2).
+//   kEpiStore: relu(acc + bias) -> bf16 NHWC.
+//   kEpiDgrad: acc [* (mask > 0)] -> bf16 NHWC.
+#pragma once
+
+#include "tc_common.cuh"
+#include "tc_conv.cuh"
+
+namespace zb {
+namespace tc {
+
+struct ConvHaloParams {
+    CUtensorMap in_map;   // 4D {CIN, W, H, B} bf16, box {8, W + 2, R + 2, 1}, no swizzle
+    CUtensorMap w_map;    // 3D {CIN, COUT, 9} bf16, box {chunk, COUT, 1}
+    int B, H, W, R, Wp, HR, region, stage_bytes, tiles_per_img, num_tiles;
+    const float *bias;          // [COUT] (forward)
+    __nv_bfloat16 *out;         // pooled [B, H/2, W/2, COUT] or full [B, H, W, COUT]
+    uint8_t *code;              // [B, H/2, W/2, COUT] (kEpiPool)
+    const __nv_bfloat16 *mask;  // [B, H, W, COUT] or null (kEpiDgrad)
+    int *err;
+};
+
+template <int CIN, int COUT, int NS, int KS, bool POOL>
+struct ConvHaloShape {
+    static constexpr int CHUNK = CIN > 64 ? 64 : CIN;   // weight K chunk
+    static constexpr int NCH = CIN / CHUNK;
+    static constexpr int ROWB = CHUNK * 2;
+    static constexpr Swizzle SW = ROWB == 128 ? kSw128 : (ROWB == 64 ? kSw64 : kSw32);
+    static constexpr int BBLK = COUT * ROWB;
+    static constexpr int BTOTAL = 9 * NCH * BBLK;
+    static constexpr int SC = CIN / KS;   // channels per stage
+    static constexpr int NC8 = SC / 8;    // 8-channel groups per stage
+    // pool staging: bf16 rows of all COUT channels, pitch COUT + 8 (an odd
+    // number of 16-byte units: conflict-free 16-byte accesses), double-buffered
+    // when it fits next to the resident weights
+    static constexpr int SP = COUT + 8;
+    static constexpr int SBUF_BYTES = 128 * SP * 2;
+    static constexpr int NSBUF = (BTOTAL + 2 * SBUF_BYTES <= 150 * 1024) ? 2 : 1;
+    static constexpr int POOL_STAGE = POOL ? NSBUF * SBUF_BYTES : 0;
+    static constexpr int BIAS_BYTES = POOL ? COUT * 4 : 0;
+    static constexpr uint32_t TMEM_COLS = (2 * COUT <= 32) ? 32 : (2 * COUT <= 64) ? 64 : (2 * COUT <= 128) ? 128 : (2 * COUT <= 256) ? 256 : 512;
+    static constexpr int SLACK = 1024;    // the last stage's padding rows may be read past its end
+    static constexpr int BAR_BYTES = 256;
+    // group pitch: HR rows of 16 B rounded to 128 B (TMA destination alignment)
+    static __host__ __device__ int region(int HR) { return (HR * 16 + 127) / 128 * 128; }
+    static __host__ __device__ int stage_bytes(int HR) { return (NC8 * region(HR) + 1023) / 1024 * 1024; }
+    static __host__ __device__ int smem(int HR) {
+        return 1024 + BTOTAL + NS * stage_bytes(HR) + SLACK + POOL_STAGE + BIAS_BYTES + BAR_BYTES;
+    }
+    static_assert(CIN % 16 == 0 && SC % 16 == 0 && COUT % 32 == 0 && COUT <= 256, "unsupported conv channels");
+    static_assert(CIN <= 64 || CIN % 64 == 0, "CIN above 64 must be a multiple of 64");
+    static_assert(SC % CHUNK == 0 || CHUNK % SC == 0, "stage channels and weight chunks must nest");
+};
+
+template <int CIN, int COUT, int EPI, int NS, int KS>
+__global__ void __launch_bounds__(320, 2) conv_halo_kernel(const __grid_constant__ ConvHaloParams p) {
+    using S = ConvHaloShape<CIN, COUT, NS, KS, EPI == kEpiPool>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t *base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    uint8_t *sB = base;
+    uint8_t *sA = sB + S::BTOTAL;
+    const int STAGE = p.stage_bytes;
+    float *stage = reinterpret_cast<float *>(sA + NS * STAGE + S::SLACK);
+    float *sbias = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(stage) + S::POOL_STAGE);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(sbias) + S::BIAS_BYTES);
+    uint64_t *full = bars;               // [NS]
+    uint64_t *empty = bars + NS;         // [NS]
+    uint64_t *acc_full = bars + 2 * NS;  // [2]
+    uint64_t *acc_empty = acc_full + 2;  // [2]
+    uint64_t *wbar = acc_empty + 2;
+    uint64_t *drain = wbar + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    int *armed = const_cast<int *>(abort_flag) + 1;   // [NS] parity+1 of the latest arm (0 = never)
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr uint32_t IDESC = idesc_bf16(128, COUT, false, false);
+
+    // Rows of the stages that TMA never writes (group padding, the slack) are
+    // zeroed once so that the discarded accumulator rows stay finite.
+    for (int i = threadIdx.x; i < (NS * STAGE + S::SLACK) / 16; i += blockDim.x)
+        *reinterpret_cast<uint4 *>(sA + 16 * i) = make_uint4(0, 0, 0, 0);
+    if constexpr (EPI == kEpiPool)
+        for (int i = threadIdx.x; i < COUT; i += blockDim.x) sbias[i] = p.bias[i];
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NS; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); armed[i] = 0; }
+        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 8); }
+        mbar_init(wbar, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (elect_one()) {
+            prefetch_tmap(&p.in_map);
+            prefetch_tmap(&p.w_map);
+            mbar_arrive_expect_tx(wbar, S::BTOTAL);
+            for (int t = 0; t < 9; ++t)
+                for (int j = 0; j < S::NCH; ++j)
+                    tma_load_3d(sB + (t * S::NCH + j) * S::BBLK, &p.w_map, wbar, j * S::CHUNK, 0, t);
+            const uint32_t stage_tx = (uint32_t)(S::NC8 * p.HR * 16);
+            int s = 0;
+            uint32_t ph = 0;
+            for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
+                const int b = tile / p.tiles_per_img;
+                const int h0 = (tile - b * p.tiles_per_img) * p.R;
+                for (int kb = 0; kb < KS; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err, kErrEmptyWait)) break;
+                    mbar_arrive_expect_tx(&full[s], stage_tx);
+                    armed[s] = (int)ph + 1;
+                    uint8_t *dst = sA + s * STAGE;
+                    for (int g = 0; g < S::NC8; ++g)
+                        tma_load_4d(dst + g * p.region, &p.in_map, &full[s], kb * S::SC + 8 * g, -1, h0 - 1, b);
+                    if (++s == NS) { s = 0; ph ^= 1u; }
+                }
+            }
+            if (*abort_flag) {   // let every copy this thread started land before exit
+                for (int i = 0; i < NS; ++i)
+                    if (armed[i] && !mbar_wait_drain(&full[i], (uint32_t)(armed[i] - 1)))
+                        atomicCAS(p.err, 0, kErrDrain);
+                if (!mbar_wait_drain(wbar, 0)) atomicCAS(p.err, 0, kErrDrain);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (elect_one()) {
+            bool issued = false;
+            if (mbar_wait(wbar, 0, abort_flag, p.err, kErrFullWait)) {
+                int s = 0, acc = 0;
+                uint32_t ph = 0, acc_ph = 0;
+                const uint32_t lbo = (uint32_t)p.region;
+                // Descriptors are built once; an MMA's operands differ only in the
+                // start-address field (bits 0-13, 16-byte units), so each one is a
+                // single add.  Offsets stay below 256 KB: no carry out of the field.
+                const uint64_t adesc0 = smem_desc(smem_u32(sA), lbo, 128, kSwNone);
+                const uint64_t bdesc0 = smem_desc(smem_u32(sB), 16, 8 * S::ROWB, S::SW);
+                const uint32_t row16 = (uint32_t)p.Wp;          // one halo row, in 16-byte units
+                const uint32_t half16 = lbo >> 4;               // next 8 channels, in 16-byte units
+                for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
+                    if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1u, abort_flag, p.err, kErrAccWait)) break;
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + (uint32_t)(acc * COUT);
+                    bool ok = true;
+                    for (int kb = 0; kb < KS; ++kb) {
+                        if (!mbar_wait(&full[s], ph, abort_flag, p.err, kErrFullWait)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint64_t a_stage = adesc0 + (uint64_t)((uint32_t)(s * STAGE) >> 4);
+                        const uint64_t b_kb = bdesc0 + (uint64_t)((uint32_t)(kb * S::SC / S::CHUNK * S::BBLK) >> 4);
+#pragma unroll
+                        for (int tap = 0; tap < 9; ++tap) {
+                            const int dh = tap / 3, dw = tap - 3 * dh;
+                            const uint64_t a_tap = a_stage + (uint64_t)(dh * row16 + dw);
+#pragma unroll
+                            for (int k = 0; k < S::SC / 16; ++k) {
+                                // K16 step k: channels kb*SC + 16k.. (groups 2k, 2k+1 of the stage)
+                                constexpr int KPC = S::CHUNK / 16;   // K16 steps per weight chunk
+                                const uint32_t boff = (uint32_t)((tap * S::NCH + (k / KPC)) * S::BBLK + (k % KPC) * 32);
+                                mma_bf16(d, a_tap + (uint64_t)(2 * k * half16), b_kb + (uint64_t)(boff >> 4), IDESC,
+                                         (kb | tap | k) != 0);
+                            }
+                        }
+                        issued = true;
+                        mma_commit(&empty[s]);
+                        if (++s == NS) { s = 0; ph ^= 1u; }
+                    }
+                    if (!ok) break;
+                    mma_commit(&acc_full[acc]);
+                    if (++acc == 2) { acc = 0; acc_ph ^= 1u; }
+                }
+            }
+            if (issued) {   // wait for every MMA this thread issued before TMEM is freed
+                mma_commit(drain);
+                if (!mbar_wait_drain(drain, 0)) atomicCAS(p.err, 0, kErrDrain);
+            }
+        }
+    } else {
+        // ------------------------------------------------ epilogue (warps 2..9)
+        const int q = warp & 3;                 // TMEM lane quarter
+        const int grp = (warp - 2) >> 2;        // warp group: chunks grp, grp + 2, ...
+        const int row = q * 32 + lane;          // accumulator row: pixel (row / Wp, row % Wp) of the tile
+        const int etid = threadIdx.x - 64;      // 0..255
+        const int r = row / p.Wp, c = row - r * p.Wp;
+        const bool in_tile = (r < p.R) && (c < p.W);
+        constexpr int NCC = COUT / 32;
+        constexpr int OCT = COUT / 8;           // channel octets per pixel
+        const int Wo = p.W >> 1, Ho = p.H >> 1;
+        const int nitems = (p.R >> 1) * Wo * OCT;
+        __nv_bfloat16 *sbuf = reinterpret_cast<__nv_bfloat16 *>(stage);
+        int acc = 0, sb = 0;
+        uint32_t acc_ph = 0;
+        // All eight epilogue warps leave the tile loop together: the abort flag
+        // is only consulted right after their common named barrier, so a warp
+        // can never wait at a barrier that another epilogue warp has left.
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+            const int b = tile / p.tiles_per_img;
+            const int h0 = (tile - b * p.tiles_per_img) * p.R;
+            mbar_wait(&acc_full[acc], acc_ph, abort_flag, p.err, kErrAccWait);
+            named_bar_sync(1, 256);
+            if (*abort_flag) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * COUT);
+            const int h = h0 + r;
+            const bool pix_ok = in_tile && (h < p.H);
+            if (grp >= NCC) {   // no chunk for this group (COUT = 32)
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            }
+            if constexpr (EPI == kEpiPool) {
+                __nv_bfloat16 *buf = sbuf + sb * 128 * S::SP;
+#pragma unroll 1
+                for (int cc = grp; cc < NCC; cc += 2) {
+                    float v[32];
+                    tmem_ld32(taddr + 32 * cc, v);
+                    if (cc + 2 >= NCC) {   // this group's last chunk: the accumulator is free
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                    }
+                    // bias + ReLU -> bf16, the row's 32 channels as four 16-byte stores
+                    uint4 *srow = reinterpret_cast<uint4 *>(buf + row * S::SP + 32 * cc);
+                    const float4 *bias4 = reinterpret_cast<const float4 *>(sbias + 32 * cc);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float4 b0 = bias4[2 * k], b1 = bias4[2 * k + 1];
+                        uint4 pk;
+                        __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
+                        h2[0] = __floats2bfloat162_rn(fmaxf(v[8 * k + 0] + b0.x, 0.0f), fmaxf(v[8 * k + 1] + b0.y, 0.0f));
+                        h2[1] = __floats2bfloat162_rn(fmaxf(v[8 * k + 2] + b0.z, 0.0f), fmaxf(v[8 * k + 3] + b0.w, 0.0f));
+                        h2[2] = __floats2bfloat162_rn(fmaxf(v[8 * k + 4] + b1.x, 0.0f), fmaxf(v[8 * k + 5] + b1.y, 0.0f));
+                        h2[3] = __floats2bfloat162_rn(fmaxf(v[8 * k + 6] + b1.z, 0.0f), fmaxf(v[8 * k + 7] + b1.w, 0.0f));
+                        srow[k] = pk;
+                    }
+                }
+                named_bar_sync(2, 256);
+                // thread = (window, channel octet), octets fastest: four pixels x 8 channels
+                for (int idx = etid; idx < nitems; idx += 256) {
+                    const int wi = idx / OCT, o = idx - wi * OCT;
+                    const int pr = wi / Wo, pc = wi - pr * Wo;
+                    const int ho = (h0 >> 1) + pr;
+                    if (ho >= Ho) continue;
+                    const int r0 = (2 * pr) * p.Wp + 2 * pc;
+                    const int rr[4] = {r0, r0 + 1, r0 + p.Wp, r0 + p.Wp + 1};
+                    float best[8];
+                    int pos[8];
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {   // (kh, kw) order: first maximum wins
+                        uint4 raw8 = *reinterpret_cast<const uint4 *>(buf + rr[q4] * S::SP + 8 * o);
+                        const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&raw8);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 f = __bfloat1622float2(h2[e]);
+                            if (q4 == 0 || f.x > best[2 * e]) { best[2 * e] = f.x; pos[2 * e] = q4; }
+                            if (q4 == 0 || f.y > best[2 * e + 1]) { best[2 * e + 1] = f.y; pos[2 * e + 1] = q4; }
+                        }
+                    }
+                    uint4 pk;
+                    __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) h2[e] = __floats2bfloat162_rn(best[2 * e], best[2 * e + 1]);
+                    uint2 cd;
+                    uint8_t *cb = reinterpret_cast<uint8_t *>(&cd);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) cb[e] = (uint8_t)(pos[e] | (best[e] > 0.0f ? 4 : 0));
+                    const size_t o8 = (((size_t)b * Ho + ho) * Wo + pc) * COUT + 8 * o;
+                    *reinterpret_cast<uint4 *>(p.out + o8) = pk;
+                    *reinterpret_cast<uint2 *>(p.code + o8) = cd;
+                }
+                // A staging buffer is rewritten only after the next tile's
+                // opening barrier, which every thread reaches after its pooling.
+                if constexpr (S::NSBUF == 2) sb ^= 1;
+            } else {
+#pragma unroll 1
+                for (int cc = grp; cc < NCC; cc += 2) {
+                    float v[32];
+                    tmem_ld32(taddr + 32 * cc, v);
+                    if (cc + 2 >= NCC) {   // this group's last chunk: the accumulator is free
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                    }
+                    if (!pix_ok) continue;
+                    const size_t o = (((size_t)b * p.H + h) * p.W + c) * COUT + 32 * cc;
+                    if constexpr (EPI == kEpiStore) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const float x = v[j] + __ldg(p.bias + 32 * cc + j);
+                            v[j] = x > 0.0f ? x : 0.0f;
+                        }
+                    } else if (p.mask) {
+                        const uint4 *mk = reinterpret_cast<const uint4 *>(p.mask + o);
+#pragma unroll
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            uint4 m = __ldg(mk + q4);
+                            const __nv_bfloat16 *mb = reinterpret_cast<const __nv_bfloat16 *>(&m);
+#pragma unroll
+                            for (int e = 0; e < 8; ++e)
+                                if (!(__bfloat162float(mb[e]) > 0.0f)) v[q4 * 8 + e] = 0.0f;
+                        }
+                    }
+                    uint4 *dst = reinterpret_cast<uint4 *>(p.out + o);
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        uint4 pk;
+                        __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) h2[e] = __floats2bfloat162_rn(v[q4 * 8 + 2 * e], v[q4 * 8 + 2 * e + 1]);
+                        dst[q4] = pk;
+                    }
+                }
+            }
+            if (++acc == 2) { acc = 0; acc_ph ^= 1u; }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, S::TMEM_COLS);
+}
+
+}  // namespace tc
+}  // namespace zb

@@ -9,6 +9,9 @@
 // Epilogues:
 //   kGemmBiasRelu: bf16 relu(acc + bias[n])        (Linear forward + ReLU)
 //   kGemmStore   : bf16 acc                       (Linear input gradient)
+//   kGemmPartial : fp32 acc of one K split into partial[split][M][N]; the
+//                  splits are summed in split order by a separate pass
+//                  (small batches: few M tiles, so K is split to fill the SMs)
 #pragma once
 
 #include "tc_common.cuh"
@@ -16,15 +19,17 @@
 namespace zb {
 namespace tc {
 
-enum GemmEpi { kGemmBiasRelu = 0, kGemmStore = 1 };
+enum GemmEpi { kGemmBiasRelu = 0, kGemmStore = 1, kGemmPartial = 2 };
 
 struct GemmTcParams {
     CUtensorMap a_map;   // 2D {K, M} bf16, box {64, 128}
     CUtensorMap b_map;   // 2D {K, N} bf16, box {64, BN}
     int M, N, K;         // N % BN == 0, K % 64 == 0
     int m_tiles, n_tiles;
+    int ksplit, kper;    // K splits (1 unless kGemmPartial) and 64-wide k steps per split
     const float *bias;   // [N]
     __nv_bfloat16 *out;  // [M][N]
+    float *partial;      // kGemmPartial: [ksplit][M][N]
     int *err;
 };
 
@@ -53,7 +58,8 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr uint32_t IDESC = idesc_bf16(128, BN, false, false);
-    const int num_tiles = p.m_tiles * p.n_tiles;
+    const int mn_tiles = p.m_tiles * p.n_tiles;
+    const int num_tiles = mn_tiles * p.ksplit;
     const int ksteps = p.K / 64;
 
     if (threadIdx.x == 0) {
@@ -76,8 +82,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
             int s = 0;
             uint32_t ph = 0;
             for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-                const int mt = tile % p.m_tiles, nt = tile / p.m_tiles;
-                for (int k = 0; k < ksteps; ++k) {
+                const int mn = tile % mn_tiles, ks = tile / mn_tiles;
+                const int mt = mn % p.m_tiles, nt = mn / p.m_tiles;
+                const int kb = ks * p.kper, ke = min(ksteps, kb + p.kper);
+                for (int k = kb; k < ke; ++k) {
                     if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err, kErrEmptyWait)) break;
                     mbar_arrive_expect_tx(&full[s], S::STAGE);
                     armed[s] = (int)ph + 1;
@@ -102,14 +110,16 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * BN);
                 bool ok = true;
-                for (int k = 0; k < ksteps; ++k) {
+                const int ks = tile / mn_tiles;
+                const int kb = ks * p.kper, ke = min(ksteps, kb + p.kper);
+                for (int k = kb; k < ke; ++k) {
                     if (!mbar_wait(&full[s], ph, abort_flag, p.err, kErrFullWait)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a0 = s0 + s * S::STAGE, b0 = a0 + S::ABYTES;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
                         mma_bf16(d, smem_desc(a0 + kk * 32, 16, 1024, kSw128), smem_desc(b0 + kk * 32, 16, 1024, kSw128),
-                                 IDESC, (k | kk) != 0);
+                                 IDESC, (k > kb) || kk != 0);
                     issued = true;
                     mma_commit(&empty[s]);
                     if (++s == NS) { s = 0; ph ^= 1u; }
@@ -129,7 +139,8 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         int acc = 0;
         uint32_t acc_ph = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            const int mt = tile % p.m_tiles, nt = tile / p.m_tiles;
+            const int mn = tile % mn_tiles, ks = tile / mn_tiles;
+            const int mt = mn % p.m_tiles, nt = mn / p.m_tiles;
             mbar_wait(&acc_full[acc], acc_ph, abort_flag, p.err, kErrAccWait);
             named_bar_sync(1, 128);
             if (*abort_flag) break;
@@ -147,6 +158,12 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                 }
                 if (m >= p.M) continue;
                 const int n0 = nt * BN + 32 * cc;
+                if constexpr (EPI == kGemmPartial) {
+                    float4 *dstf = reinterpret_cast<float4 *>(p.partial + ((size_t)ks * p.M + m) * p.N + n0);
+#pragma unroll
+                    for (int q4 = 0; q4 < 8; ++q4) dstf[q4] = make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+                    continue;
+                }
                 if constexpr (EPI == kGemmBiasRelu) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {

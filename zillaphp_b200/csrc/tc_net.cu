@@ -22,12 +22,14 @@
 
 #include "net.cuh"
 #include "tc_conv.cuh"
+#include "tc_conv_halo.cuh"
 #include "tc_gemm.cuh"
 #include "tc_wgrad.cuh"
 
 namespace zb {
 
 using tc::ConvTcParams;
+using tc::ConvHaloParams;
 using tc::GemmTcParams;
 using tc::WgradTcParams;
 
@@ -96,27 +98,51 @@ __device__ __forceinline__ int nhwc_to_nchw(int k, int C, int H, int W) {
     return c * H * W + hw;
 }
 
+// bf16 conv weights in the tensor-core layouts (32-bit index math; the conv
+// weights are < 2^31 elements):
+//   kind 0 (forward): dst[(t*COUT + co)*CIN + ci] = W[co][ci][t]
+//   kind 1 (dgrad)  : dst[(t*CIN + ci)*COUT + co] = W[co][ci][8 - t]   (flipped, transposed)
 __global__ void pack_kernel(PackJobs jobs) {
     for (int ji = 0; ji < jobs.count; ++ji) {
         const PackJob J = jobs.j[ji];
-        for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < J.n;
-             i += (long long)gridDim.x * blockDim.x) {
+        const int n = (int)J.n;
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
             float v;
-            if (J.kind == 0) {          // i = (t*COUT + co)*CIN + ci
-                const int ci = (int)(i % J.b), r = (int)(i / J.b), co = r % J.a, t = r / J.a;
-                v = J.src[((size_t)co * J.b + ci) * 9 + t];
-            } else if (J.kind == 1) {   // i = (t*CIN + ci)*COUT + co
-                const int co = (int)(i % J.a), r = (int)(i / J.a), ci = r % J.b, t = r / J.b;
-                v = J.src[((size_t)co * J.b + ci) * 9 + (8 - t)];
-            } else if (J.kind == 2) {   // i = n*K + k
-                const int k = (int)(i % J.a), n = (int)(i / J.a);
-                v = J.src[(size_t)nhwc_to_nchw(k, J.C, J.H, J.W) * J.b + n];
-            } else {                    // i = k*N + n
-                const int n = (int)(i % J.b), k = (int)(i / J.b);
-                v = J.src[(size_t)nhwc_to_nchw(k, J.C, J.H, J.W) * J.b + n];
+            if (J.kind == 0) {
+                const int ci = i % J.b, r = i / J.b, co = r % J.a, t = r / J.a;
+                v = J.src[(co * J.b + ci) * 9 + t];
+            } else {
+                const int co = i % J.a, r = i / J.a, ci = r % J.b, t = r / J.b;
+                v = J.src[(co * J.b + ci) * 9 + (8 - t)];
             }
             J.dst[i] = __float2bfloat16_rn(v);
         }
+    }
+}
+
+// The two bf16 copies of the hidden Linear weight W [F][N] (row-major over
+// NCHW features; k' is the NHWC feature index of the conv output):
+//   wP[k'][n] = W[nchw(k')][n]   (input-gradient GEMM operand)
+//   wT[n][k'] = W[nchw(k')][n]   (forward GEMM operand, K-major)
+// W is read once, in 32 x 32 tiles through shared memory, so the fp32 reads
+// and both bf16 writes are coalesced.
+__global__ void __launch_bounds__(256) pack_fc_kernel(const float *__restrict__ W, bf16 *__restrict__ wP,
+                                                      bf16 *__restrict__ dst, int F, int N, int C, int H, int Wd) {
+    __shared__ float tile[32][33];
+    const int k0 = blockIdx.x * 32, n0 = blockIdx.y * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8
+    for (int r = ty; r < 32; r += 8) {
+        const int k = k0 + r;
+        if (k < F && n0 + tx < N) {
+            const float v = W[(size_t)nhwc_to_nchw(k, C, H, Wd) * N + n0 + tx];
+            tile[r][tx] = v;
+            wP[(size_t)k * N + n0 + tx] = __float2bfloat16_rn(v);
+        }
+    }
+    __syncthreads();
+    for (int r = ty; r < 32; r += 8) {
+        const int n = n0 + r;
+        if (n < N && k0 + tx < F) dst[(size_t)n * F + k0 + tx] = __float2bfloat16_rn(tile[tx][r]);
     }
 }
 
@@ -501,6 +527,8 @@ struct ReduceArgs {
     long long n;       // elements per partial
     int map, M, N, CIN, C, H, W;
     float *dst, *dst2, *dst3;
+    const float *bias;             // map 6
+    __nv_bfloat16 *out_bf16;       // map 6
 };
 
 __device__ void r_store(const ReduceArgs &r, long long i, float s);
@@ -528,6 +556,54 @@ __global__ void __launch_bounds__(256) reduce_partials_kernel(ReduceArgs r) {
     }
 }
 
+// Many splits of a short vector (bias and small weight gradients: hundreds of
+// partials of <= 64K floats): block = 8 consecutive elements x 32 split lanes;
+// lane l sums splits l, l+32, ... in order, then the 32 lane sums of each
+// element are added in lane order (fixed order: deterministic).
+__global__ void __launch_bounds__(256) reduce_deep_kernel(ReduceArgs r) {
+    __shared__ float part[32][9];
+    const int el = threadIdx.x & 7, sl = threadIdx.x >> 3;
+    for (long long base = (long long)blockIdx.x * 8; base < r.n; base += (long long)gridDim.x * 8) {
+        const long long i = base + el;
+        float s0 = 0.0f, s1 = 0.0f;
+        if (i < r.n) {
+            int k = sl;
+            for (; k + 32 < r.splits; k += 64) {   // two independent chains per lane
+                s0 += r.partial[(size_t)k * r.n + i];
+                s1 += r.partial[(size_t)(k + 32) * r.n + i];
+            }
+            if (k < r.splits) s0 += r.partial[(size_t)k * r.n + i];
+        }
+        part[sl][el] = s0 + s1;
+        __syncthreads();
+        if (sl == 0 && i < r.n) {
+            float s = part[0][el];
+#pragma unroll
+            for (int l = 1; l < 32; ++l) s += part[l][el];
+            r_store(r, i, s);
+        }
+        __syncthreads();
+    }
+}
+
+// Few splits of a long vector (the Linear weight gradient): each thread owns
+// 4 consecutive elements and adds the splits in order with 16-byte loads.
+__global__ void __launch_bounds__(256) reduce_wide_kernel(ReduceArgs r) {
+    const long long n4 = r.n >> 2;
+    for (long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x; q < n4;
+         q += (long long)gridDim.x * blockDim.x) {
+        float4 s = reinterpret_cast<const float4 *>(r.partial)[q];
+        for (int k = 1; k < r.splits; ++k) {
+            const float4 v = reinterpret_cast<const float4 *>(r.partial + (size_t)k * r.n)[q];
+            s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+        }
+        r_store(r, 4 * q, s.x);
+        r_store(r, 4 * q + 1, s.y);
+        r_store(r, 4 * q + 2, s.z);
+        r_store(r, 4 * q + 3, s.w);
+    }
+}
+
 __device__ void r_store(const ReduceArgs &r, long long i, float s) {
     {
         const int m = (int)(i / r.N), n = (int)(i % r.N);
@@ -544,6 +620,7 @@ __device__ void r_store(const ReduceArgs &r, long long i, float s) {
             break;
         }
         case 5: { const int co = (int)(i / 10), t = (int)(i % 10); if (t < 9) r.dst[co * 9 + t] = s; else r.dst2[co] = s; break; }
+        case 6: { const float x = s + r.bias[n]; r.out_bf16[i] = __float2bfloat16_rn(x > 0.0f ? x : 0.0f); break; }
         }
     }
 }
@@ -577,6 +654,8 @@ struct ConvLayer {   // a tensor-core conv stage (conv + ReLU + pool)
     bf16 *dP = nullptr;                  // gradient w.r.t. the pooled output
     bf16 *dC = nullptr;                  // gradient w.r.t. the conv output [B, H, W, COUT]
     ConvTcParams fwd{}, dgrad{};
+    bool halo = false;                   // halo-tile kernels (R * (W + 2) <= 128)
+    ConvHaloParams hfwd{}, hdgrad{};
     WgradTcParams wg{};
     int wg_mode = 0, wg_grid = 0, wg_smem = 0;
     float *wg_partial = nullptr;
@@ -611,6 +690,7 @@ struct TcEngine {
     WgradTcParams fc_wg{};
     int fc_wg_grid = 0, fc_wg_smem = 0;
     float *fc_partial = nullptr;
+    float *fc_fwd_partial = nullptr;   // [ksplit][B][HD] when the forward splits K
     float *head_partial = nullptr;
     int head_grid = 0;
     double *row_loss = nullptr;
@@ -660,7 +740,39 @@ bool conv_shape_supported(int cin, int cout) {
     return (cin == 32 && cout == 64) || (cin == 64 && cout == 128) || (cin == 16 && cout == 32);
 }
 
+template <int CIN, int COUT, int EPI, int NS, int KS>
+int launch_halo(const ConvHaloParams &p0) {
+    using S = tc::ConvHaloShape<CIN, COUT, NS, KS, EPI == tc::kEpiPool>;
+    auto kern = tc::conv_halo_kernel<CIN, COUT, EPI, NS, KS>;
+    ConvHaloParams p = p0;
+    p.region = S::region(p.HR);
+    p.stage_bytes = S::stage_bytes(p.HR);
+    const int smem = S::smem(p.HR);
+    if (smem > 227 * 1024) return fail(kBadArg, "conv_halo: %d bytes of shared memory needed", smem);
+    static int attr = 0;
+    if (attr < smem) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return check_cuda("conv_halo smem attribute");
+        attr = smem;
+    }
+    // resident CTAs per SM: shared memory (228 KB, 1 KB reserved per CTA) and TMEM (512 columns)
+    int per_sm = (228 * 1024) / (smem + 1024);
+    if (per_sm > (int)(512 / S::TMEM_COLS)) per_sm = 512 / S::TMEM_COLS;
+    if (per_sm < 1) per_sm = 1;
+    if (per_sm > 2) per_sm = 2;
+    const int slots = sm_count() * per_sm;
+    const int grid = p.num_tiles < slots ? p.num_tiles : slots;
+    kern<<<grid, 320, smem, stream()>>>(p);
+    ZB_LAUNCH_CHECK("conv_halo");
+    return kOk;
+}
+
 int run_conv_fwd(const ConvLayer &L) {
+    if (L.halo) {
+        if (L.CIN == 32 && L.COUT == 64) return launch_halo<32, 64, tc::kEpiPool, 3, 1>(L.hfwd);
+        if (L.CIN == 64 && L.COUT == 128) return launch_halo<64, 128, tc::kEpiPool, 2, 1>(L.hfwd);
+        if (L.CIN == 16 && L.COUT == 32) return launch_halo<16, 32, tc::kEpiPool, 6, 1>(L.hfwd);
+    }
     if (L.CIN == 32 && L.COUT == 64) return launch_conv<32, 64, tc::kEpiPool, 6>(L.fwd);
     if (L.CIN == 64 && L.COUT == 128) return launch_conv<64, 128, tc::kEpiPool, 6, true>(L.fwd);
     if (L.CIN == 16 && L.COUT == 32) return launch_conv<16, 32, tc::kEpiPool, 8>(L.fwd);
@@ -669,6 +781,11 @@ int run_conv_fwd(const ConvLayer &L) {
 
 int run_conv_dgrad(const ConvLayer &L) {
     // dgrad convolves dY (COUT channels) into CIN outputs
+    if (L.halo) {
+        if (L.CIN == 32 && L.COUT == 64) return launch_halo<64, 32, tc::kEpiDgrad, 3, 1>(L.hdgrad);
+        if (L.CIN == 64 && L.COUT == 128) return launch_halo<128, 64, tc::kEpiDgrad, 3, 2>(L.hdgrad);
+        if (L.CIN == 16 && L.COUT == 32) return launch_halo<32, 32, tc::kEpiDgrad, 4, 1>(L.hdgrad);
+    }
     if (L.CIN == 32 && L.COUT == 64) return launch_conv<64, 32, tc::kEpiDgrad, 4>(L.dgrad);
     if (L.CIN == 64 && L.COUT == 128) return launch_conv<128, 64, tc::kEpiDgrad, 4, true>(L.dgrad);
     if (L.CIN == 16 && L.COUT == 32) return launch_conv<32, 32, tc::kEpiDgrad, 8>(L.dgrad);
@@ -705,14 +822,20 @@ int launch_gemm(const GemmTcParams &p) {
             return check_cuda("gemm_tc smem attribute");
         attr = true;
     }
-    const int tiles = p.m_tiles * p.n_tiles;
+    const int tiles = p.m_tiles * p.n_tiles * p.ksplit;
     kern<<<tiles < sm_count() ? tiles : sm_count(), 192, S::SMEM, stream()>>>(p);
     ZB_LAUNCH_CHECK("gemm_tc");
     return kOk;
 }
 
 int reduce(const ReduceArgs &r) {
-    reduce_partials_kernel<<<grid_for(r.n, 32, 8), 256, 0, stream()>>>(r);   // 32 elements per block
+    if (r.splits >= 32 && r.n <= 131072) {
+        reduce_deep_kernel<<<grid_for(r.n, 8, 16), 256, 0, stream()>>>(r);            // 8 elements per block
+    } else if (r.n % 4 == 0 && r.n >= 65536 && r.splits <= 16) {
+        reduce_wide_kernel<<<grid_for(r.n / 4, 256, 8), 256, 0, stream()>>>(r);
+    } else {
+        reduce_partials_kernel<<<grid_for(r.n, 32, 8), 256, 0, stream()>>>(r);       // 32 elements per block
+    }
     ZB_LAUNCH_CHECK("reduce_partials");
     return kOk;
 }
@@ -725,6 +848,22 @@ int nhwc_map(CUtensorMap *m, const bf16 *base, int C, int W, int H, int B, int b
     const int rowb = box_c * 2;
     return tc::make_tmap_bf16(m, base, 4, dims, strides, box,
                               rowb == 128 ? tc::kSw128 : rowb == 64 ? tc::kSw64 : tc::kSw32);
+}
+
+// 4D NHWC map whose box is one halo tile of 8 channels: {8, W + 2, R + 2, 1},
+// no swizzle (the halo kernel's K-major interleaved operand layout).
+int halo_map(CUtensorMap *m, const bf16 *base, int C, int W, int H, int B, int R) {
+    const uint64_t dims[4] = {(uint64_t)C, (uint64_t)W, (uint64_t)H, (uint64_t)B};
+    const uint64_t strides[3] = {(uint64_t)C * 2, (uint64_t)C * W * 2, (uint64_t)C * W * H * 2};
+    const uint32_t box[4] = {8, (uint32_t)(W + 2), (uint32_t)(R + 2), 1};
+    return tc::make_tmap_bf16(m, base, 4, dims, strides, box, tc::kSwNone);
+}
+
+void halo_params(ConvHaloParams &h, const ConvTcParams &t, int R, int W) {
+    h.w_map = t.w_map;
+    h.B = t.B; h.H = t.H; h.W = t.W; h.R = R; h.Wp = W + 2; h.HR = (R + 2) * (W + 2);
+    h.tiles_per_img = t.tiles_per_img; h.num_tiles = t.num_tiles;
+    h.bias = t.bias; h.out = t.out; h.code = t.code; h.mask = t.mask; h.err = t.err;
 }
 
 int tc_build(Net &n, TcEngine &e) {
@@ -807,6 +946,14 @@ int tc_build(Net &n, TcEngine &e) {
             d.out = e.convs.back().dP;
             d.mask = nullptr;                      // handled by that layer's unpool codes
         }
+        // halo-tile variants of the forward and input-gradient convolutions
+        L.halo = L.R >= 2 && L.R * (L.W + 2) <= 128 && L.W + 2 <= 256 && L.R + 2 <= 256;
+        if (L.halo) {
+            halo_params(L.hfwd, f, L.R, L.W);
+            halo_params(L.hdgrad, d, L.R, L.W);
+            if ((rc = halo_map(&L.hfwd.in_map, prev, L.CIN, L.W, L.H, B, L.R))) return rc;
+            if ((rc = halo_map(&L.hdgrad.in_map, L.dC, L.COUT, L.W, L.H, B, L.R))) return rc;
+        }
         // weight gradient
         WgradTcParams &g = L.wg;
         g.K_total = B; g.H = L.H; g.W = L.W; g.R = L.R; g.tiles_per_img = L.tpi;
@@ -861,11 +1008,25 @@ int tc_build(Net &n, TcEngine &e) {
             const uint32_t ba[2] = {64, 128};
             if ((rc = tc::make_tmap_bf16(&g.a_map, prev, 2, da, sa, ba, tc::kSw128))) return rc;
             const uint64_t db[2] = {(uint64_t)e.F, (uint64_t)e.HD}, sb[1] = {(uint64_t)e.F * 2};
-            const uint32_t bb[2] = {64, (uint32_t)e.HD};
+            const uint32_t bb[2] = {64, 128};
             if ((rc = tc::make_tmap_bf16(&g.b_map, e.wT, 2, db, sb, bb, tc::kSw128))) return rc;
         }
-        g.M = B; g.N = e.HD; g.K = e.F; g.m_tiles = (B + 127) / 128; g.n_tiles = 1;
+        // 128-wide N tiles; when the batch gives fewer tiles than SMs, split K
+        // so that the tiles fill the SMs (fp32 partials, summed in split order)
+        g.M = B; g.N = e.HD; g.K = e.F; g.m_tiles = (B + 127) / 128; g.n_tiles = e.HD / 128;
+        {
+            const int ksteps = e.F / 64, mn = g.m_tiles * g.n_tiles;
+            int ks = sm_count() / mn;
+            if (ks < 1) ks = 1;
+            if (ks > ksteps) ks = ksteps;
+            g.kper = (ksteps + ks - 1) / ks;
+            g.ksplit = (ksteps + g.kper - 1) / g.kper;   // every split has at least one k step
+        }
         g.bias = n.params + s.poff + s.pn_w; g.out = e.a_hid; g.err = device_error_word();
+        if (g.ksplit > 1) {
+            if ((rc = dalloc(e, &e.fc_fwd_partial, (size_t)g.ksplit * B * e.HD))) return rc;
+            g.partial = e.fc_fwd_partial;
+        }
         // input gradient: A = dZ [B][HD], B = W [F][HD] -> dflat [B][F], N tile 224/256/128
         GemmTcParams &dg = e.fc_dgrad;
         int bn = 0;
@@ -881,6 +1042,7 @@ int tc_build(Net &n, TcEngine &e) {
             if ((rc = tc::make_tmap_bf16(&dg.b_map, e.wP, 2, db, sb, bb, tc::kSw128))) return rc;
         }
         dg.M = B; dg.N = e.F; dg.K = e.HD; dg.m_tiles = (B + 127) / 128; dg.n_tiles = e.F / bn;
+        dg.ksplit = 1; dg.kper = e.HD / 64;
         dg.bias = nullptr; dg.out = e.dflat; dg.err = device_error_word();
         // weight gradient: A = flattened activation (MN-major), B = dZ
         WgradTcParams &w = e.fc_wg;
@@ -895,7 +1057,8 @@ int tc_build(Net &n, TcEngine &e) {
         if (e.HD != 256) return fail(kBadArg, "tc engine: hidden Linear width must be 256");
         w.mode = tc::kWgLinear; w.K_total = B; w.m_tiles = e.F / 128; w.M = e.F; w.N = e.HD;
         if (e.F % 128) return fail(kBadArg, "tc engine: Linear input %d not a multiple of 128", e.F);
-        w.splits = (sm_count() + w.m_tiles - 1) / w.m_tiles;
+        w.splits = sm_count() / w.m_tiles;   // one wave: one CTA per SM fits
+        if (w.splits < 1) w.splits = 1;
         if (w.splits > (B + 63) / 64) w.splits = (B + 63) / 64;
         w.kstage_rows = 64; w.err = device_error_word();
         e.fc_wg_grid = w.m_tiles * w.splits;
@@ -910,7 +1073,10 @@ int tc_build(Net &n, TcEngine &e) {
     e.NC = st[i].oC;
     if (!e.has_hidden) return fail(kBadArg, "tc engine: a hidden Linear + ReLU before the classifier is required");
     if (e.HD != 256 || e.NC != 10) return fail(kBadArg, "tc engine: head %d->%d not supported", e.HD, e.NC);
-    e.head_grid = sm_count() * 2;
+    // at least 4 rows per warp: the block set-up (W staging, partial write) is
+    // the fixed cost, and fewer blocks also means fewer partials to sum
+    e.head_grid = (B + 31) / 32;
+    if (e.head_grid > sm_count() * 2) e.head_grid = sm_count() * 2;
     if ((rc = dalloc(e, &e.head_partial, (size_t)e.head_grid * (e.HD * e.NC + e.NC + e.HD)))) return rc;
     if ((rc = dalloc(e, &e.row_loss, (size_t)B))) return rc;
     e.c1_wgrad_grid = sm_count() * 6;   // several blocks per SM: each walks whole images
@@ -934,18 +1100,13 @@ int tc_build(Net &n, TcEngine &e) {
     e.views.push_back({"flat.d", e.dflat, (size_t)B * e.F, 0});
     e.views.push_back({"hidden.wT", e.wT, (size_t)e.F * e.HD, 0});
     e.views.push_back({"hidden.wP", e.wP, (size_t)e.F * e.HD, 0});
-    // weight packing jobs
+    // conv weight packing jobs (the hidden Linear weight has its own kernel)
     PackJobs &pj = e.pack;
     pj.count = 0;
     for (auto &L : e.convs) {
         const Stage &s = st[L.si];
         pj.j[pj.count++] = {0, n.params + s.poff, L.wf, L.COUT, L.CIN, 0, 0, 0, (long long)9 * L.CIN * L.COUT};
         pj.j[pj.count++] = {1, n.params + s.poff, L.wd, L.COUT, L.CIN, 0, 0, 0, (long long)9 * L.CIN * L.COUT};
-    }
-    {
-        const Stage &s = st[e.hid_si];
-        pj.j[pj.count++] = {2, n.params + s.poff, e.wT, e.F, e.HD, e.fC, e.fH, e.fW, (long long)e.F * e.HD};
-        pj.j[pj.count++] = {3, n.params + s.poff, e.wP, e.F, e.HD, e.fC, e.fH, e.fW, (long long)e.F * e.HD};
     }
     return kOk;
 }
@@ -955,8 +1116,14 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
     auto &st = n.st;
     int rc;
     // ---- pack bf16 operands from the fp32 master
-    pack_kernel<<<sm_count() * 4, 256, 0, stream()>>>(e.pack);
+    pack_kernel<<<sm_count(), 256, 0, stream()>>>(e.pack);
     ZB_LAUNCH_CHECK("pack");
+    {
+        const float *W4 = n.params + st[e.hid_si].poff;
+        pack_fc_kernel<<<dim3((e.F + 31) / 32, (e.HD + 31) / 32), 256, 0, stream()>>>(
+            W4, e.wP, e.wT, e.F, e.HD, e.fC, e.fH, e.fW);
+        ZB_LAUNCH_CHECK("pack transpose");
+    }
     prof_mark(n, "pack");
     // ---- forward
     const Stage &s1 = st[e.c1_si];
@@ -977,7 +1144,14 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
         if ((rc = run_conv_fwd(L))) return rc;
         prof_mark(n, "conv_fwd");
     }
-    if ((rc = launch_gemm<256, tc::kGemmBiasRelu, 4>(e.fc_fwd))) return rc;
+    if (e.fc_fwd.ksplit > 1) {
+        if ((rc = launch_gemm<128, tc::kGemmPartial, 6>(e.fc_fwd))) return rc;
+        ReduceArgs r{e.fc_fwd_partial, e.fc_fwd.ksplit, (long long)B * e.HD, 6, B, e.HD, 0, 0, 0, 0,
+                     nullptr, nullptr, nullptr, e.fc_fwd.bias, e.a_hid};
+        if ((rc = reduce(r))) return rc;
+    } else if ((rc = launch_gemm<128, tc::kGemmBiasRelu, 6>(e.fc_fwd))) {
+        return rc;
+    }
     prof_mark(n, "linear_fwd");
     // ---- head: classifier, loss, start of the backward
     const Stage &sh = st[e.head_si];
@@ -1009,6 +1183,9 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
                      gW4, nullptr, nullptr};
         if ((rc = reduce(r))) return rc;
     }
+    // hidden + classifier Linear gradients and the loss are final: their
+    // all-reduce (the bulk of the gradient bytes) overlaps the conv backward
+    if ((rc = dp_bucket_ready(n, st[e.hid_si].poff))) return rc;
     prof_mark(n, "linear_bwd");
     // ---- conv stages backward (last to first)
     const bf16 *dpooled = e.dflat;   // gradient w.r.t. the last pooled output

@@ -56,6 +56,15 @@ struct WgradTcShape {
     static __host__ __device__ int smem(int kr) { return 1024 + NS * stage(kr) + 256; }
 };
 
+// 32 consecutive fp32 partial values of one row (16-byte aligned) as eight
+// 16-byte stores; zeros for a CTA whose K slice was empty.
+__device__ __forceinline__ void store_row32(float *dst, const float (&v)[32], bool zero) {
+    float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+        d4[q] = zero ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(192, 1) wgrad_tc_kernel(const __grid_constant__ WgradTcParams p) {
     using S = WgradTcShape<MODE>;
@@ -205,18 +214,14 @@ __global__ void __launch_bounds__(192, 1) wgrad_tc_kernel(const __grid_constant_
                 for (int cc = 0; cc < 8; ++cc) {
                     float v[32];
                     tmem_ld32(taddr + 32 * cc, v);
-                    if (m < p.M)
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) part[(size_t)m * p.N + 32 * cc + j] = empty_slice ? 0.0f : v[j];
+                    if (m < p.M) store_row32(part + (size_t)m * p.N + 32 * cc, v, empty_slice);
                 }
             } else if constexpr (MODE == kWgConvCo) {
 #pragma unroll 1
                 for (int cc = 0; cc < 6; ++cc) {
                     float v[32];
                     tmem_ld32(taddr + 32 * cc, v);
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        part[(size_t)row * p.N + mt * 192 + 32 * cc + j] = empty_slice ? 0.0f : v[j];
+                    store_row32(part + (size_t)row * p.N + mt * 192 + 32 * cc, v, empty_slice);
                 }
             } else {
 #pragma unroll 1
@@ -226,9 +231,7 @@ __global__ void __launch_bounds__(192, 1) wgrad_tc_kernel(const __grid_constant_
                     for (int cc = 0; cc < 2; ++cc) {
                         float v[32];
                         tmem_ld32(taddr + t * 64 + 32 * cc, v);
-                        if (m < p.M)
-#pragma unroll
-                            for (int j = 0; j < 32; ++j) part[(size_t)m * p.N + 32 * cc + j] = empty_slice ? 0.0f : v[j];
+                        if (m < p.M) store_row32(part + (size_t)m * p.N + 32 * cc, v, empty_slice);
                     }
                 }
             }

@@ -211,23 +211,59 @@ __global__ void conv_first_fwd_kernel(const float *__restrict__ x, const float *
     }
 }
 
-// First conv without a following pool: thread = (4 consecutive output pixels
-// of a row, 8-channel octet).  The octet's 72 weights and 8 biases live in
-// registers, the 3x6 input window in registers, 288 FMAs per thread, four
-// 16-byte stores.  The octet of a thread is fixed across its grid-stride loop
-// (the stride is a multiple of the octet count).
+// Zero-padded image staging for the first-conv kernels: each of the 256
+// threads owns up to kStageRegs elements of the (H+2p) x (W+2p) padded image;
+// their source offsets (-1 = padding) are fixed per thread, and the next
+// image is loaded into registers while the current one is being used, so the
+// global-load latency overlaps the compute.
+constexpr int kStageRegs = 4;
+
+struct ImageStager {
+    int off[kStageRegs];
+    float v[kStageRegs];
+    __device__ void init(int H, int W, int pad) {
+        const int PW = W + 2 * pad, PH = H + 2 * pad;
+#pragma unroll
+        for (int k = 0; k < kStageRegs; ++k) {
+            const int i = threadIdx.x + k * 256;
+            const int ih = i / PW - pad, iw = i % PW - pad;
+            off[k] = (i < PH * PW && (unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W) ? ih * W + iw
+                     : (i < PH * PW ? -1 : -2);
+        }
+    }
+    __device__ void load(const float *__restrict__ xb) {
+#pragma unroll
+        for (int k = 0; k < kStageRegs; ++k) v[k] = off[k] >= 0 ? __ldg(xb + off[k]) : 0.0f;
+    }
+    __device__ void store(float *xs) const {
+#pragma unroll
+        for (int k = 0; k < kStageRegs; ++k)
+            if (off[k] != -2) xs[threadIdx.x + k * 256] = v[k];
+    }
+};
+
+// First conv without a following pool.  A block walks whole images: the
+// zero-padded image is staged in shared memory; thread = (column, pair of
+// output rows, 8-channel octet), octets fastest, so for each of its two rows
+// a warp writes 8 consecutive pixels x COUT bf16 as one contiguous run.  The
+// two pixels share 6 of their 12 inputs and give two independent FMA chains;
+// the octet's 72 weights and 8 biases live in registers.  Coordinates
+// advance incrementally (no division in the loop).
 template <int COUT>
-__global__ void __launch_bounds__(256) conv_first_fwd_rows_kernel(const float *__restrict__ x,
-                                                                  const float *__restrict__ w,
-                                                                  const float *__restrict__ bias,
-                                                                  bf16 *__restrict__ out, int B, int H, int W,
-                                                                  int pad) {
+__global__ void __launch_bounds__(256) conv_first_fwd_img_kernel(const float *__restrict__ x,
+                                                                 const float *__restrict__ w,
+                                                                 const float *__restrict__ bias,
+                                                                 bf16 *__restrict__ out, int B, int H, int W,
+                                                                 int pad) {
     constexpr int NQ = COUT / 8;
+    constexpr int LANES = 256 / NQ;
+    extern __shared__ float xs[];
+    const int q = threadIdx.x % NQ, pl = threadIdx.x / NQ;
     const int oH = H + 2 * pad - 2, oW = W + 2 * pad - 2;
-    const int ngrp = (oW + 3) / 4;
-    const long long total = (long long)B * oH * ngrp * NQ;
-    const long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    const int q = (int)(i0 % NQ);
+    const int PW = W + 2 * pad, PH = H + 2 * pad;
+    const int nrp = (oH + 1) / 2;            // row pairs
+    const int NP = nrp * oW;                 // (row pair, column) items per image
+    const int step_r = LANES / oW, step_c = LANES % oW;
     float wr[8][9], br[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -235,38 +271,44 @@ __global__ void __launch_bounds__(256) conv_first_fwd_rows_kernel(const float *_
 #pragma unroll
         for (int t = 0; t < 9; ++t) wr[e][t] = __ldg(w + (8 * q + e) * 9 + t);
     }
-    for (long long i = i0; i < total; i += (long long)gridDim.x * blockDim.x) {
-        const long long gi = i / NQ;
-        const int grp = (int)(gi % ngrp);
-        const long long r = gi / ngrp;
-        const int oh = (int)(r % oH);
-        const long long b = r / oH;
-        const int ow0 = grp * 4;
-        const float *xb = x + (size_t)b * H * W;
-        float xv[3][6];
+    ImageStager stg;
+    stg.init(H, W, pad);
+    if (blockIdx.x < B) stg.load(x + (size_t)blockIdx.x * H * W);
+    for (int b = blockIdx.x; b < B; b += gridDim.x) {
+        __syncthreads();
+        stg.store(xs);
+        __syncthreads();
+        if (b + (int)gridDim.x < B) stg.load(x + (size_t)(b + gridDim.x) * H * W);
+        bf16 *ob = out + (size_t)b * oH * oW * COUT + 8 * q;
+        int rp = pl / oW, ow = pl - (pl / oW) * oW;
+        for (int it = pl; it < NP; it += LANES) {
+            const int oh = 2 * rp;
+            const float *xr = xs + oh * PW + ow;   // rows oh .. oh + 3 of the padded image
+            float xv[4][3];
 #pragma unroll
-        for (int dh = 0; dh < 3; ++dh)
+            for (int r = 0; r < 4; ++r)
 #pragma unroll
-            for (int k = 0; k < 6; ++k) {
-                const int ih = oh - pad + dh, iw = ow0 - pad + k;
-                xv[dh][k] = ((unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W) ? __ldg(xb + ih * W + iw) : 0.0f;
-            }
+                for (int k = 0; k < 3; ++k) xv[r][k] = (oh + r < PH) ? xr[r * PW + k] : 0.0f;
 #pragma unroll
-        for (int px = 0; px < 4; ++px) {
-            if (ow0 + px >= oW) break;
-            uint4 pk;
-            __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
+            for (int dr = 0; dr < 2; ++dr) {
+                if (oh + dr >= oH) break;
+                uint4 pk;
+                __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
 #pragma unroll
-            for (int e2 = 0; e2 < 4; ++e2) {
-                float a0 = br[2 * e2], a1 = br[2 * e2 + 1];
+                for (int e2 = 0; e2 < 4; ++e2) {
+                    float a0 = br[2 * e2], a1 = br[2 * e2 + 1];
 #pragma unroll
-                for (int t = 0; t < 9; ++t) {
-                    a0 = fmaf(xv[t / 3][px + t % 3], wr[2 * e2][t], a0);
-                    a1 = fmaf(xv[t / 3][px + t % 3], wr[2 * e2 + 1][t], a1);
+                    for (int t = 0; t < 9; ++t) {
+                        a0 = fmaf(xv[dr + t / 3][t % 3], wr[2 * e2][t], a0);
+                        a1 = fmaf(xv[dr + t / 3][t % 3], wr[2 * e2 + 1][t], a1);
+                    }
+                    h2[e2] = __floats2bfloat162_rn(a0 > 0.0f ? a0 : 0.0f, a1 > 0.0f ? a1 : 0.0f);
                 }
-                h2[e2] = __floats2bfloat162_rn(a0 > 0.0f ? a0 : 0.0f, a1 > 0.0f ? a1 : 0.0f);
+                *reinterpret_cast<uint4 *>(ob + ((size_t)(oh + dr) * oW + ow) * COUT) = pk;
             }
-            *reinterpret_cast<uint4 *>(out + (((size_t)b * oH + oh) * oW + ow0 + px) * COUT + 8 * q) = pk;
+            rp += step_r;
+            ow += step_c;
+            if (ow >= oW) { ow -= oW; ++rp; }
         }
     }
 }
@@ -275,10 +317,11 @@ __global__ void __launch_bounds__(256) conv_first_fwd_rows_kernel(const float *_
 // db[co] = sum_p dC[p][co].  A block walks whole images: the image (with a
 // zero halo) is staged in shared memory; thread (pixel lane, channel octet)
 // loads 8 bf16 of dC per pixel as one 16-byte load (a warp reads 8 pixels x
-// 32 channels = 512 contiguous bytes) and keeps 8 x 10 accumulators.  Lanes
-// of a warp that share an octet are combined by shuffles, warps in fixed order
-// through shared memory: per-block partials [block][COUT][10], summed later
-// in block order.  Dynamic shared memory: max((H+2p)(W+2p), 8*4*80) floats.
+// 32 channels = 512 contiguous bytes), four pixels' loads in flight at once,
+// and keeps 8 x 10 accumulators.  Lanes of a warp that share an octet are
+// combined by shuffles, warps in fixed order through shared memory: per-block
+// partials [block][COUT][10], summed later in block order.  Dynamic shared
+// memory: max((H+2p)(W+2p), 8*4*80) floats.
 template <int COUT>
 __global__ void __launch_bounds__(256) conv_first_wgrad_kernel(const bf16 *__restrict__ dC,
                                                                const float *__restrict__ x,
@@ -286,44 +329,58 @@ __global__ void __launch_bounds__(256) conv_first_wgrad_kernel(const bf16 *__res
                                                                int pad) {
     constexpr int NQ = COUT / 8;            // channel octets per pixel
     constexpr int LANES = 256 / NQ;         // pixel lanes per block
+    constexpr int U = 4;                    // pixels per thread in flight
     extern __shared__ float xs[];
     const int q = threadIdx.x % NQ, pl = threadIdx.x / NQ;
     const int oH = H + 2 * pad - 2, oW = W + 2 * pad - 2, P = oH * oW;
     const int PH = H + 2 * pad, PW = W + 2 * pad;
+    const int step_h = LANES / oW, step_w = LANES % oW;
     float acc[8][10];
 #pragma unroll
     for (int e = 0; e < 8; ++e)
 #pragma unroll
         for (int t = 0; t < 10; ++t) acc[e][t] = 0.0f;
+    ImageStager stg;
+    stg.init(H, W, pad);
+    if (blockIdx.x < B) stg.load(x + (size_t)blockIdx.x * H * W);
     for (int b = blockIdx.x; b < B; b += gridDim.x) {
         __syncthreads();
-        const float *xb = x + (size_t)b * H * W;
-        for (int i = threadIdx.x; i < PH * PW; i += blockDim.x) {
-            const int ih = i / PW - pad, iw = i % PW - pad;
-            xs[i] = ((unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W) ? xb[ih * W + iw] : 0.0f;
-        }
+        stg.store(xs);
         __syncthreads();
+        if (b + (int)gridDim.x < B) stg.load(x + (size_t)(b + gridDim.x) * H * W);
         const bf16 *gb = dC + (size_t)b * P * COUT + 8 * q;
-        for (int p = pl; p < P; p += LANES) {
-            const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(gb + (size_t)p * COUT));
-            const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
-            float g[8];
+        int oh = pl / oW, ow = pl - (pl / oW) * oW;
+        for (int p0 = pl; p0 < P; p0 += U * LANES) {
+            uint4 raw[U];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float2 f = __bfloat1622float2(h2[k]);
-                g[2 * k] = f.x;
-                g[2 * k + 1] = f.y;
+            for (int u = 0; u < U; ++u) {
+                const int p = p0 + u * LANES;
+                raw[u] = p < P ? __ldg(reinterpret_cast<const uint4 *>(gb + (size_t)p * COUT)) : make_uint4(0, 0, 0, 0);
             }
-            const int oh = p / oW, ow = p - oh * oW;
-            const float *xr = xs + oh * PW + ow;
-            float xv[9];
 #pragma unroll
-            for (int t = 0; t < 9; ++t) xv[t] = xr[(t / 3) * PW + (t % 3)];
+            for (int u = 0; u < U; ++u) {
+                if (p0 + u * LANES >= P) break;
+                const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&raw[u]);
+                float g[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
+                for (int k = 0; k < 4; ++k) {
+                    const float2 f = __bfloat1622float2(h2[k]);
+                    g[2 * k] = f.x;
+                    g[2 * k + 1] = f.y;
+                }
+                const float *xr = xs + oh * PW + ow;
+                float xv[9];
 #pragma unroll
-                for (int t = 0; t < 9; ++t) acc[e][t] = fmaf(g[e], xv[t], acc[e][t]);
-                acc[e][9] += g[e];
+                for (int t = 0; t < 9; ++t) xv[t] = xr[(t / 3) * PW + (t % 3)];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+#pragma unroll
+                    for (int t = 0; t < 9; ++t) acc[e][t] = fmaf(g[e], xv[t], acc[e][t]);
+                    acc[e][9] += g[e];
+                }
+                oh += step_h;
+                ow += step_w;
+                if (ow >= oW) { ow -= oW; ++oh; }
             }
         }
     }
@@ -878,6 +935,9 @@ int tc_build(Net &n, TcEngine &e) {
     e.C1 = st[0].oC; e.H0 = st[0].H; e.W0 = st[0].W; e.pad1 = st[0].pad;
     e.H1 = st[0].oH; e.W1 = st[0].oW;
     if (e.C1 != 16 && e.C1 != 32) return fail(kBadArg, "tc engine: first conv must have 16 or 32 outputs");
+    if ((e.H0 + 2 * e.pad1) * (e.W0 + 2 * e.pad1) > kStageRegs * 256)
+        return fail(kBadArg, "tc engine: first-conv image too large (padded %d x %d)", e.H0 + 2 * e.pad1,
+                    e.W0 + 2 * e.pad1);
     i = 1;
     e.c1_pool = i < st.size() && st[i].kind == kPool;
     int C = e.C1, H = e.H1, W = e.W1;
@@ -1079,7 +1139,8 @@ int tc_build(Net &n, TcEngine &e) {
     if (e.head_grid > sm_count() * 2) e.head_grid = sm_count() * 2;
     if ((rc = dalloc(e, &e.head_partial, (size_t)e.head_grid * (e.HD * e.NC + e.NC + e.HD)))) return rc;
     if ((rc = dalloc(e, &e.row_loss, (size_t)B))) return rc;
-    e.c1_wgrad_grid = sm_count() * 6;   // several blocks per SM: each walks whole images
+    e.c1_wgrad_grid = sm_count() * 2;   // the resident blocks (two per SM): each walks whole images
+    if (e.c1_wgrad_grid > B) e.c1_wgrad_grid = B;
     if ((rc = dalloc(e, &e.c1_partial, (size_t)e.c1_wgrad_grid * e.C1 * 10))) return rc;
     // diagnostics
     e.views.push_back({"conv1.out", e.a1, (size_t)B * (e.c1_pool ? (e.H1 / 2) * (e.W1 / 2) : e.H1 * e.W1) * e.C1, 0});
@@ -1131,11 +1192,14 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
     {
         const long long pix = (long long)B * (e.c1_pool ? (e.H1 / 2) * (e.W1 / 2) : e.H1 * e.W1);
         const int grid = grid_for(pix, 128, 8);
-        const long long items = (long long)B * e.H1 * ((e.W1 + 3) / 4) * (e.C1 / 8);
-        const int grid_rows = grid_for(items, 256, 8);
-        if (e.C1 == 32 && !e.c1_pool) conv_first_fwd_rows_kernel<32><<<grid_rows, 256, 0, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
+        const size_t xsm = (size_t)(e.H0 + 2 * e.pad1) * (e.W0 + 2 * e.pad1) * sizeof(float);
+        const int gimg = B < sm_count() * 4 ? B : sm_count() * 4;
+        if ((e.H0 + 2 * e.pad1) * (e.W0 + 2 * e.pad1) > kStageRegs * 256)
+            return fail(kBadArg, "tc engine: first-conv image too large (padded %d x %d)", e.H0 + 2 * e.pad1,
+                        e.W0 + 2 * e.pad1);
+        if (e.C1 == 32 && !e.c1_pool) conv_first_fwd_img_kernel<32><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
         else if (e.C1 == 32) conv_first_fwd_kernel<32, true><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
-        else if (!e.c1_pool) conv_first_fwd_rows_kernel<16><<<grid_rows, 256, 0, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
+        else if (!e.c1_pool) conv_first_fwd_img_kernel<16><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
         else conv_first_fwd_kernel<16, true><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
         ZB_LAUNCH_CHECK("conv_first_fwd");
         prof_mark(n, "conv_fwd");

@@ -194,16 +194,35 @@ def tc_work(w: configs.Workload, b: int) -> list[dict]:
         if k > 0:
             out.append({"label": "pool_bwd", "flops": 0, "bytes": b * ((oh // 2) * (ow // 2) * o * 3 + oh * ow * o * 2),
                         "name": f"unpool{k + 1}"})
-            f = 2 * 2 * b * oh * ow * o * a * 9
-            out.append({"label": "conv_bwd", "flops": f, "bytes": b * (oh * ow * o * 2 * 2 + ih * iw * a * 2 * 2),
-                        "name": f"conv{k + 1} dX+dW"})
+            f = 2 * b * oh * ow * o * a * 9
+            # input gradient: reads dY, writes dX (plus the ReLU mask of conv1's output for conv2)
+            out.append({"label": "conv_dgrad", "flops": f,
+                        "bytes": b * (oh * ow * o * 2 + ih * iw * a * 2 * (2 if k == 1 else 1)),
+                        "name": f"conv{k + 1} dX"})
+            out.append({"label": "conv_wgrad", "flops": f, "bytes": b * (oh * ow * o * 2 + ih * iw * a * 2),
+                        "name": f"conv{k + 1} dW"})
         else:
-            out.append({"label": "conv_bwd", "flops": 2 * b * oh * ow * o * a * 9,
+            out.append({"label": "conv_wgrad", "flops": 2 * b * oh * ow * o * a * 9,
                         "bytes": b * (oh * ow * o * 2 + ih * iw * 4), "name": "conv1 dW"})
     n = configs.param_count(w)
     out.append({"label": "adam" if w.optimizer == configs.ADAM else "sgd", "flops": 0,
                 "bytes": (28 if w.optimizer == configs.ADAM else 12) * n, "name": "optimizer"})
     return out
+
+
+# DRAM bytes (read + write) per sample of the tensor-core kernels, from one
+# `ncu --set full` capture at batch 2048 (dram__bytes_read.sum +
+# dram__bytes_write.sum divided by 2048); per-sample work is fixed and these
+# kernels have no cross-sample reuse, so a launch's traffic scales with its
+# sample count.
+NCU_DRAM_BYTES_PER_SAMPLE = {
+    "conv2 fwd": (102.861056e6 + 39.156736e6) / 2048,
+    "conv3 fwd": (51.557632e6 + 5.623296e6) / 2048,
+    "conv3 dX": (102.938112e6 + 22.401024e6) / 2048,
+    "conv2 dX": (308.345344e6 + 84.106496e6) / 2048,
+    "conv3 dW": (154.178048e6 + 4.386560e6) / 2048,
+    "conv2 dW": (308.313856e6 + 5.590528e6) / 2048,
+}
 
 
 def roofline(w, batch, seg_times: list[tuple[str, float]], steps: int, pk: dict, pk_kind: str, precision: int = 0):
@@ -242,7 +261,11 @@ def roofline(w, batch, seg_times: list[tuple[str, float]], steps: int, pk: dict,
     r["kernel"] = f"{item.get('name', item['label'])} (group {k_dom} of the step)"
     r["ms_per_launch"] = round(ms, 4)
     r["peak_source"] = pk_kind
-    r["traffic"] = None
+    per_sample = NCU_DRAM_BYTES_PER_SAMPLE.get(item.get("name", "")) if precision == 1 else None
+    r["traffic"] = round(per_sample * batch) if per_sample else None
+    if per_sample:
+        r["traffic_unit"] = "bytes per launch (ncu DRAM read + write, batch 2048 capture scaled by samples)"
+        r["algorithmic_bytes"] = item["bytes"]
     return r, breakdown
 
 

@@ -1268,6 +1268,7 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
         }
         prof_mark(n, "pool_bwd");
         if ((rc = run_conv_dgrad(L))) return rc;
+        prof_mark(n, "conv_dgrad");
         if ((rc = run_wgrad(L.wg, L.wg_mode, L.wg_grid, L.wg_smem))) return rc;
         {
             ReduceArgs r{L.wg_partial, L.wg.splits, (long long)L.wg.M * L.wg.N,
@@ -1275,7 +1276,7 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
                          n.grads + s.poff, nullptr, nullptr};
             if ((rc = reduce(r))) return rc;
         }
-        prof_mark(n, "conv_bwd");
+        prof_mark(n, "conv_wgrad");
     }
     // ---- first conv backward (dC1 written by the next conv's dgrad, masked)
     if (e.c1_pool) {
@@ -1297,7 +1298,7 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
                      n.grads + s1.poff, n.grads + s1.poff + s1.pn_w, nullptr};
         if ((rc = reduce(r))) return rc;
     }
-    prof_mark(n, "conv_bwd");
+    prof_mark(n, "conv_wgrad");
     return kOk;
 }
 

@@ -56,7 +56,9 @@ namespace tc {
 struct ConvHaloParams {
     CUtensorMap in_map;   // 4D {CIN, W, H, B} bf16, box {8, W + 2, R + 2, 1}, no swizzle
     CUtensorMap w_map;    // 3D {CIN, COUT, 9} bf16, box {chunk, COUT, 1}
+    CUtensorMap out_map;  // kEpiDgrad: 4D {COUT, W, H, B} bf16, box {COUT, W, R, 1}, swizzle = row bytes
     int B, H, W, R, Wp, HR, region, stage_bytes, tiles_per_img, num_tiles;
+    int out_tile_bytes;   // kEpiDgrad: one staged output tile (R * W * COUT * 2, 1024-aligned)
     const float *bias;          // [COUT] (forward)
     __nv_bfloat16 *out;         // pooled [B, H/2, W/2, COUT] or full [B, H, W, COUT]
     uint8_t *code;              // [B, H/2, W/2, COUT] (kEpiPool)
@@ -88,15 +90,18 @@ struct ConvHaloShape {
     // group pitch: HR rows of 16 B rounded to 128 B (TMA destination alignment)
     static __host__ __device__ int region(int HR) { return (HR * 16 + 127) / 128 * 128; }
     static __host__ __device__ int stage_bytes(int HR) { return (NC8 * region(HR) + 1023) / 1024 * 1024; }
-    static __host__ __device__ int smem(int HR) {
-        return 1024 + BTOTAL + NS * stage_bytes(HR) + SLACK + POOL_STAGE + BIAS_BYTES + BAR_BYTES;
+    // kEpiDgrad: staged output tiles for the TMA store (one or two buffers)
+    static __host__ __device__ int out_tile_bytes(int R, int W) { return (R * W * COUT * 2 + 1023) / 1024 * 1024; }
+    static __host__ __device__ int smem(int HR, int out_total) {
+        const int epi = POOL_STAGE > out_total ? POOL_STAGE : out_total;
+        return 1024 + BTOTAL + NS * stage_bytes(HR) + SLACK + epi + BIAS_BYTES + BAR_BYTES;
     }
     static_assert(CIN % 16 == 0 && SC % 16 == 0 && COUT % 32 == 0 && COUT <= 256, "unsupported conv channels");
     static_assert(CIN <= 64 || CIN % 64 == 0, "CIN above 64 must be a multiple of 64");
     static_assert(SC % CHUNK == 0 || CHUNK % SC == 0, "stage channels and weight chunks must nest");
 };
 
-template <int CIN, int COUT, int EPI, int NS, int KS>
+template <int CIN, int COUT, int EPI, int NS, int KS, int OB = 2>
 __global__ void __launch_bounds__(320, 2) conv_halo_kernel(const __grid_constant__ ConvHaloParams p) {
     using S = ConvHaloShape<CIN, COUT, NS, KS, EPI == kEpiPool>;
     extern __shared__ uint8_t smem_raw[];
@@ -105,8 +110,9 @@ __global__ void __launch_bounds__(320, 2) conv_halo_kernel(const __grid_constant
     uint8_t *sB = base;
     uint8_t *sA = sB + S::BTOTAL;
     const int STAGE = p.stage_bytes;
-    float *stage = reinterpret_cast<float *>(sA + NS * STAGE + S::SLACK);
-    float *sbias = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(stage) + S::POOL_STAGE);
+    float *stage = reinterpret_cast<float *>(sA + NS * STAGE + S::SLACK);   // epilogue staging
+    const int EPI_BYTES = EPI == kEpiPool ? S::POOL_STAGE : (EPI == kEpiDgrad ? OB * p.out_tile_bytes : 0);
+    float *sbias = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(stage) + EPI_BYTES);
     uint64_t *bars = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(sbias) + S::BIAS_BYTES);
     uint64_t *full = bars;               // [NS]
     uint64_t *empty = bars + NS;         // [NS]
@@ -148,6 +154,7 @@ __global__ void __launch_bounds__(320, 2) conv_halo_kernel(const __grid_constant
         if (elect_one()) {
             prefetch_tmap(&p.in_map);
             prefetch_tmap(&p.w_map);
+            if (EPI == kEpiDgrad) prefetch_tmap(&p.out_map);
             mbar_arrive_expect_tx(wbar, S::BTOTAL);
             for (int t = 0; t < 9; ++t)
                 for (int j = 0; j < S::NCH; ++j)
@@ -249,8 +256,12 @@ __global__ void __launch_bounds__(320, 2) conv_halo_kernel(const __grid_constant
             const int b = tile / p.tiles_per_img;
             const int h0 = (tile - b * p.tiles_per_img) * p.R;
             mbar_wait(&acc_full[acc], acc_ph, abort_flag, p.err, kErrAccWait);
+            // the TMA store that last read this tile's staging buffer (two tiles
+            // ago) has finished reading before anyone writes it again
+            if (EPI == kEpiDgrad && etid == 0) bulk_wait_read<OB - 1>();
             named_bar_sync(1, 256);
             if (*abort_flag) break;
+
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * COUT);
             const int h = h0 + r;
@@ -333,6 +344,38 @@ __global__ void __launch_bounds__(320, 2) conv_halo_kernel(const __grid_constant
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&acc_empty[acc]);
                     }
+                    if constexpr (EPI == kEpiDgrad) {
+                        if (!in_tile) continue;   // rows past H are clipped by the TMA store
+                        if (p.mask && pix_ok) {
+                            const uint4 *mk = reinterpret_cast<const uint4 *>(
+                                p.mask + (((size_t)b * p.H + h) * p.W + c) * COUT + 32 * cc);
+#pragma unroll
+                            for (int q4 = 0; q4 < 4; ++q4) {
+                                uint4 m = __ldg(mk + q4);
+                                const __nv_bfloat16 *mb = reinterpret_cast<const __nv_bfloat16 *>(&m);
+#pragma unroll
+                                for (int e = 0; e < 8; ++e)
+                                    if (!(__bfloat162float(mb[e]) > 0.0f)) v[q4 * 8 + e] = 0.0f;
+                            }
+                        }
+                        // staging tile [R][W][COUT] bf16 with the TMA store's swizzle
+                        // (16-byte chunk index XOR (offset >> 7) within the row span)
+                        constexpr int RB = COUT * 2;
+                        constexpr uint32_t SWM = RB == 128 ? 7u : RB == 64 ? 3u : 1u;
+                        uint8_t *tile_buf = reinterpret_cast<uint8_t *>(stage) + sb * p.out_tile_bytes;
+                        const uint32_t base_off = (uint32_t)((r * p.W + c) * RB + 64 * cc);
+#pragma unroll
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            uint4 pk;
+                            __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                h2[e] = __floats2bfloat162_rn(v[q4 * 8 + 2 * e], v[q4 * 8 + 2 * e + 1]);
+                            const uint32_t o = base_off + 16 * q4;
+                            *reinterpret_cast<uint4 *>(tile_buf + (o ^ (((o >> 7) & SWM) << 4))) = pk;
+                        }
+                        continue;
+                    }
                     if (!pix_ok) continue;
                     const size_t o = (((size_t)b * p.H + h) * p.W + c) * COUT + 32 * cc;
                     if constexpr (EPI == kEpiStore) {
@@ -362,9 +405,19 @@ __global__ void __launch_bounds__(320, 2) conv_halo_kernel(const __grid_constant
                         dst[q4] = pk;
                     }
                 }
+                if constexpr (EPI == kEpiDgrad) {
+                    fence_proxy_async_smem();
+                    named_bar_sync(2, 256);
+                    if (etid == 0) {
+                        tma_store_4d(&p.out_map, reinterpret_cast<uint8_t *>(stage) + sb * p.out_tile_bytes, 0, 0, h0, b);
+                        bulk_commit();
+                    }
+                    if (OB == 2) sb ^= 1;
+                }
             }
             if (++acc == 2) { acc = 0; acc_ph ^= 1u; }
         }
+        if (EPI == kEpiDgrad && etid == 0) bulk_wait_all();   // stores complete before exit
     }
 
     tc_fence_before();

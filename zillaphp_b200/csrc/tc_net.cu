@@ -25,6 +25,7 @@
 #include "tc_conv_halo.cuh"
 #include "tc_gemm.cuh"
 #include "tc_wgrad.cuh"
+#include "tc_wgrad_halo.cuh"
 
 namespace zb {
 
@@ -32,6 +33,7 @@ using tc::ConvTcParams;
 using tc::ConvHaloParams;
 using tc::GemmTcParams;
 using tc::WgradTcParams;
+using tc::WgradHaloParams;
 
 // ====================================================================== host: TMA maps
 namespace tc {
@@ -713,6 +715,10 @@ struct ConvLayer {   // a tensor-core conv stage (conv + ReLU + pool)
     ConvTcParams fwd{}, dgrad{};
     bool halo = false;                   // halo-tile kernels (R * (W + 2) <= 128)
     ConvHaloParams hfwd{}, hdgrad{};
+    bool wg_halo = false;                // halo-tile weight gradient
+    WgradHaloParams whalo{};
+    int whalo_grid = 0;
+    float *whalo_partial = nullptr;
     WgradTcParams wg{};
     int wg_mode = 0, wg_grid = 0, wg_smem = 0;
     float *wg_partial = nullptr;
@@ -794,17 +800,18 @@ int launch_conv(const ConvTcParams &p) {
 }
 
 bool conv_shape_supported(int cin, int cout) {
-    return (cin == 32 && cout == 64) || (cin == 64 && cout == 128) || (cin == 16 && cout == 32);
+    return (cin == 32 && cout == 64) || (cin == 64 && cout == 128);
 }
 
-template <int CIN, int COUT, int EPI, int NS, int KS>
+template <int CIN, int COUT, int EPI, int NS, int KS, int OB = 2>
 int launch_halo(const ConvHaloParams &p0) {
     using S = tc::ConvHaloShape<CIN, COUT, NS, KS, EPI == tc::kEpiPool>;
-    auto kern = tc::conv_halo_kernel<CIN, COUT, EPI, NS, KS>;
+    auto kern = tc::conv_halo_kernel<CIN, COUT, EPI, NS, KS, OB>;
     ConvHaloParams p = p0;
     p.region = S::region(p.HR);
     p.stage_bytes = S::stage_bytes(p.HR);
-    const int smem = S::smem(p.HR);
+    p.out_tile_bytes = EPI == tc::kEpiDgrad ? S::out_tile_bytes(p.R, p.W) : 0;
+    const int smem = S::smem(p.HR, OB * p.out_tile_bytes);
     if (smem > 227 * 1024) return fail(kBadArg, "conv_halo: %d bytes of shared memory needed", smem);
     static int attr = 0;
     if (attr < smem) {
@@ -828,25 +835,48 @@ int run_conv_fwd(const ConvLayer &L) {
     if (L.halo) {
         if (L.CIN == 32 && L.COUT == 64) return launch_halo<32, 64, tc::kEpiPool, 3, 1>(L.hfwd);
         if (L.CIN == 64 && L.COUT == 128) return launch_halo<64, 128, tc::kEpiPool, 2, 1>(L.hfwd);
-        if (L.CIN == 16 && L.COUT == 32) return launch_halo<16, 32, tc::kEpiPool, 6, 1>(L.hfwd);
     }
     if (L.CIN == 32 && L.COUT == 64) return launch_conv<32, 64, tc::kEpiPool, 6>(L.fwd);
     if (L.CIN == 64 && L.COUT == 128) return launch_conv<64, 128, tc::kEpiPool, 6, true>(L.fwd);
-    if (L.CIN == 16 && L.COUT == 32) return launch_conv<16, 32, tc::kEpiPool, 8>(L.fwd);
     return fail(kBadArg, "tc engine: no forward conv kernel for %d->%d", L.CIN, L.COUT);
 }
 
 int run_conv_dgrad(const ConvLayer &L) {
     // dgrad convolves dY (COUT channels) into CIN outputs
     if (L.halo) {
-        if (L.CIN == 32 && L.COUT == 64) return launch_halo<64, 32, tc::kEpiDgrad, 3, 1>(L.hdgrad);
-        if (L.CIN == 64 && L.COUT == 128) return launch_halo<128, 64, tc::kEpiDgrad, 3, 2>(L.hdgrad);
-        if (L.CIN == 16 && L.COUT == 32) return launch_halo<32, 32, tc::kEpiDgrad, 4, 1>(L.hdgrad);
+        if (L.CIN == 32 && L.COUT == 64) return launch_halo<64, 32, tc::kEpiDgrad, 2, 1, 2>(L.hdgrad);
+        if (L.CIN == 64 && L.COUT == 128) return launch_halo<128, 64, tc::kEpiDgrad, 3, 2, 1>(L.hdgrad);
     }
     if (L.CIN == 32 && L.COUT == 64) return launch_conv<64, 32, tc::kEpiDgrad, 4>(L.dgrad);
     if (L.CIN == 64 && L.COUT == 128) return launch_conv<128, 64, tc::kEpiDgrad, 4, true>(L.dgrad);
-    if (L.CIN == 16 && L.COUT == 32) return launch_conv<32, 32, tc::kEpiDgrad, 8>(L.dgrad);
     return fail(kBadArg, "tc engine: no dgrad conv kernel for %d->%d", L.CIN, L.COUT);
+}
+
+template <int CIN, int COUT, int NGRP, int NS>
+int launch_wgrad_halo(const WgradHaloParams &p0, int grid) {
+    using S = tc::WgradHaloShape<CIN, COUT, NGRP, NS>;
+    auto kern = tc::wgrad_halo_kernel<CIN, COUT, NGRP, NS>;
+    WgradHaloParams p = p0;
+    p.dy_region = S::dy_region(p.R, p.Wp);
+    p.x_region = S::x_region(p.HR);
+    p.stage_bytes = S::stage_bytes(p.R, p.Wp, p.HR);
+    const int smem = S::smem(p.R, p.Wp, p.HR);
+    if (smem > 227 * 1024) return fail(kBadArg, "wgrad_halo: %d bytes of shared memory needed", smem);
+    static int attr = 0;
+    if (attr < smem) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return check_cuda("wgrad_halo smem attribute");
+        attr = smem;
+    }
+    kern<<<grid, 192, smem, stream()>>>(p);
+    ZB_LAUNCH_CHECK("wgrad_halo");
+    return kOk;
+}
+
+int run_wgrad_halo(const ConvLayer &L) {
+    if (L.CIN == 32 && L.COUT == 64) return launch_wgrad_halo<32, 64, 1, 6>(L.whalo, L.whalo_grid);
+    if (L.CIN == 64 && L.COUT == 128) return launch_wgrad_halo<64, 128, 2, 4>(L.whalo, L.whalo_grid);
+    return fail(kBadArg, "tc engine: no halo weight-gradient kernel for %d->%d", L.CIN, L.COUT);
 }
 
 template <int MODE>
@@ -1013,6 +1043,38 @@ int tc_build(Net &n, TcEngine &e) {
             halo_params(L.hdgrad, d, L.R, L.W);
             if ((rc = halo_map(&L.hfwd.in_map, prev, L.CIN, L.W, L.H, B, L.R))) return rc;
             if ((rc = halo_map(&L.hdgrad.in_map, L.dC, L.COUT, L.W, L.H, B, L.R))) return rc;
+            // input-gradient output [B, H, W, CIN] written by TMA stores of R-row tiles
+            const uint64_t od[4] = {(uint64_t)L.CIN, (uint64_t)L.W, (uint64_t)L.H, (uint64_t)B};
+            const uint64_t os[3] = {(uint64_t)L.CIN * 2, (uint64_t)L.CIN * L.W * 2, (uint64_t)L.CIN * L.W * L.H * 2};
+            const uint32_t ob[4] = {(uint32_t)L.CIN, (uint32_t)L.W, (uint32_t)L.R, 1};
+            const int rb = L.CIN * 2;
+            if (rb != 32 && rb != 64 && rb != 128) return fail(kBadArg, "tc engine: input-gradient row of %d bytes", rb);
+            if ((rc = tc::make_tmap_bf16(&L.hdgrad.out_map, L.hdgrad.out, 4, od, os, ob,
+                                         rb == 128 ? tc::kSw128 : rb == 64 ? tc::kSw64 : tc::kSw32)))
+                return rc;
+
+        }
+        // halo-tile weight gradient: D[co][tap*CIN + ci], column groups x image slices
+        // (only for 32 -> 64: at 64 -> 128 the per-tap kernel's single N = 192 MMA per K step
+        // reads dY from shared memory once, where the halo kernel reads it once per tap)
+        L.wg_halo = L.halo && L.CIN == 32 && L.COUT == 64;
+        if (L.wg_halo) {
+            WgradHaloParams &w = L.whalo;
+            const int ngrp = L.COUT == 128 ? 2 : 1;
+            w.B = B; w.H = L.H; w.W = L.W; w.R = L.R; w.Wp = L.W + 2; w.HR = (L.R + 2) * (L.W + 2);
+            w.tiles_per_img = L.tpi;
+            w.splits = sm_count() / ngrp;
+            if (w.splits > B) w.splits = B;
+            if (w.splits < 1) w.splits = 1;
+            w.err = device_error_word();
+            L.whalo_grid = w.splits * ngrp;
+            const uint64_t dd[4] = {(uint64_t)L.COUT, (uint64_t)L.W, (uint64_t)L.H, (uint64_t)B};
+            const uint64_t ds[3] = {(uint64_t)L.COUT * 2, (uint64_t)L.COUT * L.W * 2, (uint64_t)L.COUT * L.W * L.H * 2};
+            const uint32_t db[4] = {8, (uint32_t)(L.W + 2), (uint32_t)L.R, 1};
+            if ((rc = tc::make_tmap_bf16(&w.dy_map, L.dC, 4, dd, ds, db, tc::kSwNone))) return rc;
+            if ((rc = halo_map(&w.x_map, prev, L.CIN, L.W, L.H, B, L.R))) return rc;
+            if ((rc = dalloc(e, &L.whalo_partial, (size_t)w.splits * L.COUT * 9 * L.CIN))) return rc;
+            w.partial = L.whalo_partial;
         }
         // weight gradient
         WgradTcParams &g = L.wg;
@@ -1269,8 +1331,13 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
         prof_mark(n, "pool_bwd");
         if ((rc = run_conv_dgrad(L))) return rc;
         prof_mark(n, "conv_dgrad");
-        if ((rc = run_wgrad(L.wg, L.wg_mode, L.wg_grid, L.wg_smem))) return rc;
-        {
+        if (L.wg_halo) {
+            if ((rc = run_wgrad_halo(L))) return rc;
+            ReduceArgs r{L.whalo_partial, L.whalo.splits, (long long)L.COUT * 9 * L.CIN, 1, L.COUT, 9 * L.CIN,
+                         L.CIN, 0, 0, 0, n.grads + s.poff, nullptr, nullptr};
+            if ((rc = reduce(r))) return rc;
+        } else {
+            if ((rc = run_wgrad(L.wg, L.wg_mode, L.wg_grid, L.wg_smem))) return rc;
             ReduceArgs r{L.wg_partial, L.wg.splits, (long long)L.wg.M * L.wg.N,
                          L.wg_mode == tc::kWgConvCo ? 1 : 2, L.wg.M, L.wg.N, L.CIN, 0, 0, 0,
                          n.grads + s.poff, nullptr, nullptr};

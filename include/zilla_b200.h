@@ -145,10 +145,11 @@ int adam_update_dev(int w_id, int g_id, int m_id, int v_id, float lr, float beta
  * caller zeroes it).  It calls no cudaMalloc, cudaFree or allocating library
  * routine: its per-row scratch is a file-scope static device array of 65536
  * doubles (512 KB on every GPU that loads the library, held until exit), so
- * B > 65536 is rejected with -2.  The first call on a device looks the array
- * up with cudaGetSymbolAddress.  All calls share the array: calls that
- * overlap on the GPU (other streams, other host threads) race and must be
- * serialised by the caller. */
+ * B > 65536 is rejected with -2.  The first call on a device does the
+ * set-up: it looks the array's device address up with cudaGetSymbolAddress,
+ * so make that first call on each device before any stream capture.  All
+ * calls share the array: calls that overlap on the GPU (other streams, other
+ * host threads) race and must be serialised by the caller. */
 int softmax_ce_noalloc(const float *logits, const float *targets, float *dlogits, float *loss,
                        int B, int C, void *stream);
 

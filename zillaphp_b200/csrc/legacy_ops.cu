@@ -350,7 +350,9 @@ int launch_bias_grad(const float *dy, float *db, int B, int C) {
 // or a caller that only hands over device pointers it already owns.  softmax_ce_noalloc
 // serves them: the per-row scratch is this fixed file-scope device array instead, reserved
 // when the library is loaded, so a call allocates nothing.  Every GPU that loads the
-// library holds the array (512 KB) until the process exits.
+// library holds the array (512 KB) until the process exits.  The first call on a device
+// does the set-up (cudaGetSymbolAddress with that device current); callers make that
+// first call before any stream capture.
 namespace {
 
 constexpr int kNoAllocMaxRows = 65536;                                 // rows per call

@@ -213,6 +213,15 @@ __global__ void conv_first_fwd_kernel(const float *__restrict__ x, const float *
     }
 }
 
+// Packed two-lane fp32 FMA (sm_100): d = a * b + c per lane, each lane
+// rounded exactly as fmaf.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    uint64_t ra = *reinterpret_cast<uint64_t *>(&a), rb = *reinterpret_cast<uint64_t *>(&b),
+             rc = *reinterpret_cast<uint64_t *>(&c), rd;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rd) : "l"(ra), "l"(rb), "l"(rc));
+    return *reinterpret_cast<float2 *>(&rd);
+}
+
 // Zero-padded image staging for the first-conv kernels: each of the 256
 // threads owns up to kStageRegs elements of the (H+2p) x (W+2p) padded image;
 // their source offsets (-1 = padding) are fixed per thread, and the next
@@ -252,7 +261,7 @@ struct ImageStager {
 // the octet's 72 weights and 8 biases live in registers.  Coordinates
 // advance incrementally (no division in the loop).
 template <int COUT>
-__global__ void __launch_bounds__(256) conv_first_fwd_img_kernel(const float *__restrict__ x,
+__global__ void __launch_bounds__(256, 2) conv_first_fwd_img_kernel(const float *__restrict__ x,
                                                                  const float *__restrict__ w,
                                                                  const float *__restrict__ bias,
                                                                  bf16 *__restrict__ out, int B, int H, int W,
@@ -266,12 +275,13 @@ __global__ void __launch_bounds__(256) conv_first_fwd_img_kernel(const float *__
     const int nrp = (oH + 1) / 2;            // row pairs
     const int NP = nrp * oW;                 // (row pair, column) items per image
     const int step_r = LANES / oW, step_c = LANES % oW;
-    float wr[8][9], br[8];
+    float2 wr2[4][9], br2[4];   // channel pairs (2k, 2k + 1) of the octet
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        br[e] = __ldg(bias + 8 * q + e);
+    for (int k = 0; k < 4; ++k) {
+        br2[k] = make_float2(__ldg(bias + 8 * q + 2 * k), __ldg(bias + 8 * q + 2 * k + 1));
 #pragma unroll
-        for (int t = 0; t < 9; ++t) wr[e][t] = __ldg(w + (8 * q + e) * 9 + t);
+        for (int t = 0; t < 9; ++t)
+            wr2[k][t] = make_float2(__ldg(w + (8 * q + 2 * k) * 9 + t), __ldg(w + (8 * q + 2 * k + 1) * 9 + t));
     }
     ImageStager stg;
     stg.init(H, W, pad);
@@ -298,13 +308,13 @@ __global__ void __launch_bounds__(256) conv_first_fwd_img_kernel(const float *__
                 __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
 #pragma unroll
                 for (int e2 = 0; e2 < 4; ++e2) {
-                    float a0 = br[2 * e2], a1 = br[2 * e2 + 1];
+                    float2 a = br2[e2];
 #pragma unroll
                     for (int t = 0; t < 9; ++t) {
-                        a0 = fmaf(xv[dr + t / 3][t % 3], wr[2 * e2][t], a0);
-                        a1 = fmaf(xv[dr + t / 3][t % 3], wr[2 * e2 + 1][t], a1);
+                        const float xt = xv[dr + t / 3][t % 3];
+                        a = ffma2(make_float2(xt, xt), wr2[e2][t], a);
                     }
-                    h2[e2] = __floats2bfloat162_rn(a0 > 0.0f ? a0 : 0.0f, a1 > 0.0f ? a1 : 0.0f);
+                    h2[e2] = __floats2bfloat162_rn(a.x > 0.0f ? a.x : 0.0f, a.y > 0.0f ? a.y : 0.0f);
                 }
                 *reinterpret_cast<uint4 *>(ob + ((size_t)(oh + dr) * oW + ow) * COUT) = pk;
             }
@@ -325,7 +335,7 @@ __global__ void __launch_bounds__(256) conv_first_fwd_img_kernel(const float *__
 // partials [block][COUT][10], summed later in block order.  Dynamic shared
 // memory: max((H+2p)(W+2p), 8*4*80) floats.
 template <int COUT>
-__global__ void __launch_bounds__(256) conv_first_wgrad_kernel(const bf16 *__restrict__ dC,
+__global__ void __launch_bounds__(256, 2) conv_first_wgrad_kernel(const bf16 *__restrict__ dC,
                                                                const float *__restrict__ x,
                                                                float *__restrict__ partial, int B, int H, int W,
                                                                int pad) {
@@ -337,11 +347,11 @@ __global__ void __launch_bounds__(256) conv_first_wgrad_kernel(const bf16 *__res
     const int oH = H + 2 * pad - 2, oW = W + 2 * pad - 2, P = oH * oW;
     const int PH = H + 2 * pad, PW = W + 2 * pad;
     const int step_h = LANES / oW, step_w = LANES % oW;
-    float acc[8][10];
+    float2 acc2[4][10];   // channel pairs (2k, 2k + 1); t = 9 is the bias sum
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
+    for (int k = 0; k < 4; ++k)
 #pragma unroll
-        for (int t = 0; t < 10; ++t) acc[e][t] = 0.0f;
+        for (int t = 0; t < 10; ++t) acc2[k][t] = make_float2(0.0f, 0.0f);
     ImageStager stg;
     stg.init(H, W, pad);
     if (blockIdx.x < B) stg.load(x + (size_t)blockIdx.x * H * W);
@@ -363,22 +373,18 @@ __global__ void __launch_bounds__(256) conv_first_wgrad_kernel(const bf16 *__res
             for (int u = 0; u < U; ++u) {
                 if (p0 + u * LANES >= P) break;
                 const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&raw[u]);
-                float g[8];
+                float2 g2[4];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float2 f = __bfloat1622float2(h2[k]);
-                    g[2 * k] = f.x;
-                    g[2 * k + 1] = f.y;
-                }
+                for (int k = 0; k < 4; ++k) g2[k] = __bfloat1622float2(h2[k]);
                 const float *xr = xs + oh * PW + ow;
                 float xv[9];
 #pragma unroll
                 for (int t = 0; t < 9; ++t) xv[t] = xr[(t / 3) * PW + (t % 3)];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
+                for (int k = 0; k < 4; ++k) {
 #pragma unroll
-                    for (int t = 0; t < 9; ++t) acc[e][t] = fmaf(g[e], xv[t], acc[e][t]);
-                    acc[e][9] += g[e];
+                    for (int t = 0; t < 9; ++t) acc2[k][t] = ffma2(g2[k], make_float2(xv[t], xv[t]), acc2[k][t]);
+                    acc2[k][9] = ffma2(g2[k], make_float2(1.0f, 1.0f), acc2[k][9]);
                 }
                 oh += step_h;
                 ow += step_w;
@@ -390,17 +396,23 @@ __global__ void __launch_bounds__(256) conv_first_wgrad_kernel(const bf16 *__res
 #pragma unroll
     for (int off = NQ; off < 32; off <<= 1)
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
+        for (int k = 0; k < 4; ++k)
 #pragma unroll
-            for (int t = 0; t < 10; ++t) acc[e][t] += __shfl_xor_sync(0xffffffffu, acc[e][t], off);
+            for (int t = 0; t < 10; ++t) {
+                acc2[k][t].x += __shfl_xor_sync(0xffffffffu, acc2[k][t].x, off);
+                acc2[k][t].y += __shfl_xor_sync(0xffffffffu, acc2[k][t].y, off);
+            }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float *red = xs;   // [8 warps][NQ][80]
     if (lane < NQ)
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
+        for (int k = 0; k < 4; ++k)
 #pragma unroll
-            for (int t = 0; t < 10; ++t) red[(warp * NQ + lane) * 80 + e * 10 + t] = acc[e][t];
+            for (int t = 0; t < 10; ++t) {
+                red[(warp * NQ + lane) * 80 + (2 * k) * 10 + t] = acc2[k][t].x;
+                red[(warp * NQ + lane) * 80 + (2 * k + 1) * 10 + t] = acc2[k][t].y;
+            }
     __syncthreads();
     for (int i = threadIdx.x; i < COUT * 10; i += blockDim.x) {   // i = co*10 + t, co = 8q + e
         const int co = i / 10, t = i % 10, qq = co / 8, e = co % 8;

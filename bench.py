@@ -195,6 +195,11 @@ def tc_work(w: configs.Workload, b: int) -> list[dict]:
             out.append({"label": "pool_bwd", "flops": 0, "bytes": b * ((oh // 2) * (ow // 2) * o * 3 + oh * ow * o * 2),
                         "name": f"unpool{k + 1}"})
             f = 2 * b * oh * ow * o * a * 9
+            if (a, o) == (32, 64):
+                # one kernel for both: reads dY and X once, writes dX
+                out.append({"label": "conv_bwd", "flops": 2 * f,
+                            "bytes": b * (oh * ow * o * 2 + ih * iw * a * 2 * 2), "name": f"conv{k + 1} dX+dW"})
+                continue
             # input gradient: reads dY, writes dX (plus the ReLU mask of conv1's output for conv2)
             out.append({"label": "conv_dgrad", "flops": f,
                         "bytes": b * (oh * ow * o * 2 + ih * iw * a * 2 * (2 if k == 1 else 1)),

@@ -1,0 +1,304 @@
+// tc_conv_bwd_fused.cuh -- the whole backward of a 3x3 (stride 1, pad 1) conv
+// whose input is a ReLU output, in one tcgen05 kernel: per tile it loads the
+// dY halo tile and the X halo tile ONCE and runs both contractions on them.
+//
+//   input gradient  dX[pixel][ci] = (X > 0) * sum_{tap, co} dY[pixel - tap][co] Wd[tap][ci][co]
+//   weight gradient dW[co][tap][ci] = sum_pixels dY[pixel][co] X[pixel + tap][ci]
+//
+// Tile: R image rows of one image with R * Wp = 128, Wp >= W + 2 (W = 28:
+// Wp = 32, R = 4).  Both halo tiles hold rows h0-1 .. h0+R and columns
+// -1 .. Wp-2 as 8-channel groups of 16-byte rows (zero outside the image), the
+// canonical no-swizzle UMMA layout, which serves as
+//   * K-major A of the input gradient (M = 128 output pixels i = r*Wp + c,
+//     K = dY channels; tap (dh, dw) starts dh*Wp + dw rows further on), and
+//   * MN-major A / B of the weight gradient (K = the 128 pixel rows
+//     k = r*Wp + c; dY starts Wp + 1 rows in, X starts dh*Wp + dw rows in).
+// With R * Wp = 128 every K row past the tile (c >= W) reads a zero halo column
+// of dY, so the padding adds nothing, and every row read lies inside the tile.
+// The ReLU mask of the input gradient comes from the X tile already in shared
+// memory, so a stage is released only when both its MMAs and the epilogue's
+// mask reads are done (two arrivals).
+//
+// TMEM: the input gradient in two 128 x CX accumulators (double-buffered: the
+// epilogue of tile i overlaps the MMAs of tile i+1), the weight gradient in one
+// 64-row x 9*CX accumulator that stays for the CTA's whole run (M = CY = 64:
+// rows 16q .. 16q+15 in lanes 32q .. 32q+15).  At the end each CTA writes its
+// weight-gradient partial [cta][CY][9*CX]; a second kernel sums them in CTA
+// order (deterministic).
+//
+// Warp roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer and TMEM
+// owner, warps 2-9 epilogue (input gradient: staged bf16 tile + TMA store, as
+// conv_halo_kernel's kEpiDgrad; weight gradient partial at the end).  Every
+// wait is bounded (tc_common.cuh).
+#pragma once
+
+#include "tc_common.cuh"
+
+namespace zb {
+namespace tc {
+
+struct ConvBwdFusedParams {
+    CUtensorMap dy_map;   // 4D {CY, W, H, B} bf16, box {8, Wp, R + 2, 1}, no swizzle
+    CUtensorMap x_map;    // 4D {CX, W, H, B} bf16, box {8, Wp, R + 2, 1}, no swizzle
+    CUtensorMap w_map;    // 3D {CY, CX, 9} bf16 (flipped, transposed kernel), box {CY, CX, 1}, 128B swizzle
+    CUtensorMap out_map;  // 4D {CX, W, H, B} bf16, box {CX, W, R, 1}, swizzle = CX * 2 bytes
+    int B, H, W, R, Wp, tiles_per_img, num_tiles;
+    int region, stage_bytes, out_tile_bytes;   // set by the launcher
+    float *partial;       // [gridDim.x][CY][9 * CX]
+    int *err;
+};
+
+template <int CX, int CY, int NS>
+struct ConvBwdFusedShape {
+    static constexpr int NTOT = 9 * CX;
+    static constexpr int DYG = CY / 8, XG = CX / 8;
+    static constexpr int WROWB = CY * 2;                 // dgrad weight row: 128 B (CY = 64)
+    static constexpr int WBLK = CX * WROWB;              // one tap
+    static constexpr int WTOTAL = 9 * WBLK;
+    static constexpr uint32_t TMEM_COLS = 512;           // 2 * CX + NTOT <= 512
+    static constexpr int WG_COL0 = 2 * CX;                // weight-gradient columns start
+    static constexpr int SLACK = 1024;
+    static constexpr int BAR_BYTES = 256;
+    static __host__ __device__ int region(int R, int Wp) { return ((R + 2) * Wp * 16 + 127) / 128 * 128; }
+    static __host__ __device__ int stage_bytes(int R, int Wp) { return ((DYG + XG) * region(R, Wp) + 1023) / 1024 * 1024; }
+    static __host__ __device__ int out_tile_bytes(int R, int W) { return (R * W * CX * 2 + 1023) / 1024 * 1024; }
+    static __host__ __device__ int smem(int R, int Wp, int W) {
+        return 1024 + WTOTAL + NS * stage_bytes(R, Wp) + SLACK + 2 * out_tile_bytes(R, W) + BAR_BYTES;
+    }
+    static_assert(CY == 64 && CX == 32, "built for the 32 -> 64 conv: M = 64 weight gradient, N = 32 input gradient");
+    static_assert(2 * CX + NTOT <= 512, "TMEM columns");
+};
+
+template <int CX, int CY, int NS>
+__global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_constant__ ConvBwdFusedParams p) {
+    using S = ConvBwdFusedShape<CX, CY, NS>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t *base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    uint8_t *sW = base;
+    uint8_t *sA = sW + S::WTOTAL;
+    const int STAGE = p.stage_bytes;
+    uint8_t *outbuf = sA + NS * STAGE + S::SLACK;   // [2] staged input-gradient tiles
+    uint64_t *bars = reinterpret_cast<uint64_t *>(outbuf + 2 * p.out_tile_bytes);
+    uint64_t *full = bars;               // [NS]
+    uint64_t *empty = bars + NS;         // [NS]: MMA commit + epilogue mask release
+    uint64_t *acc_full = bars + 2 * NS;  // [2]
+    uint64_t *acc_empty = acc_full + 2;  // [2]
+    uint64_t *wbar = acc_empty + 2;
+    uint64_t *wg_full = wbar + 1;
+    uint64_t *drain = wg_full + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    int *armed = const_cast<int *>(abort_flag) + 1;   // [NS]
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr uint32_t IDESC_DX = idesc_bf16(128, CX, false, false);
+    constexpr uint32_t IDESC_DW = idesc_bf16(CY, CX, true, true);
+    const int my_tiles = p.num_tiles > (int)blockIdx.x ? (p.num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+
+    for (int i = threadIdx.x; i < (NS * STAGE + S::SLACK) / 16; i += blockDim.x)
+        *reinterpret_cast<uint4 *>(sA + 16 * i) = make_uint4(0, 0, 0, 0);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NS; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 2); armed[i] = 0; }
+        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 8); }
+        mbar_init(wbar, 1);
+        mbar_init(wg_full, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (elect_one()) {
+            prefetch_tmap(&p.dy_map);
+            prefetch_tmap(&p.x_map);
+            prefetch_tmap(&p.w_map);
+            prefetch_tmap(&p.out_map);
+            mbar_arrive_expect_tx(wbar, S::WTOTAL);
+            for (int t = 0; t < 9; ++t) tma_load_3d(sW + t * S::WBLK, &p.w_map, wbar, 0, 0, t);
+            const uint32_t tx = (uint32_t)((S::DYG + S::XG) * (p.R + 2) * p.Wp * 16);
+            int s = 0;
+            uint32_t ph = 0;
+            for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
+                const int b = tile / p.tiles_per_img;
+                const int h0 = (tile - b * p.tiles_per_img) * p.R;
+                if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err, kErrEmptyWait)) break;
+                mbar_arrive_expect_tx(&full[s], tx);
+                armed[s] = (int)ph + 1;
+                uint8_t *st = sA + s * STAGE;
+                for (int g = 0; g < S::DYG; ++g)
+                    tma_load_4d(st + g * p.region, &p.dy_map, &full[s], 8 * g, -1, h0 - 1, b);
+                for (int g = 0; g < S::XG; ++g)
+                    tma_load_4d(st + (S::DYG + g) * p.region, &p.x_map, &full[s], 8 * g, -1, h0 - 1, b);
+                if (++s == NS) { s = 0; ph ^= 1u; }
+            }
+            if (*abort_flag) {
+                for (int i = 0; i < NS; ++i)
+                    if (armed[i] && !mbar_wait_drain(&full[i], (uint32_t)(armed[i] - 1))) atomicCAS(p.err, 0, kErrDrain);
+                if (!mbar_wait_drain(wbar, 0)) atomicCAS(p.err, 0, kErrDrain);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (elect_one()) {
+            bool issued = false;
+            if (mbar_wait(wbar, 0, abort_flag, p.err, kErrFullWait)) {
+                int s = 0, acc = 0;
+                uint32_t ph = 0, acc_ph = 0;
+                const uint32_t lbo = (uint32_t)p.region, reg16 = lbo >> 4;
+                // descriptors differ only in the start address (16-byte units)
+                const uint64_t dx_a0 = smem_desc(smem_u32(sA), lbo, 128, kSwNone);          // K-major dY
+                const uint64_t dx_b0 = smem_desc(smem_u32(sW), 16, 8 * S::WROWB, kSw128);   // weights
+                const uint64_t dw_a0 = smem_desc(smem_u32(sA), 128, lbo, kSwNone);          // MN-major dY
+                const uint64_t dw_b0 = smem_desc(smem_u32(sA) + (uint32_t)(S::DYG * p.region), 128, lbo, kSwNone);
+                const uint32_t wp = (uint32_t)p.Wp;
+                int n = 0;
+                for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x, ++n) {
+                    if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1u, abort_flag, p.err, kErrAccWait)) break;
+                    if (!mbar_wait(&full[s], ph, abort_flag, p.err, kErrFullWait)) break;
+                    tc_fence_after();
+                    const uint64_t st16 = (uint64_t)((uint32_t)(s * STAGE) >> 4);
+                    // input gradient: 9 taps x CY/16 K16 steps into acc
+                    const uint32_t d = tmem_base + (uint32_t)(acc * CX);
+#pragma unroll
+                    for (int tap = 0; tap < 9; ++tap) {
+                        const int dh = tap / 3, dw = tap - 3 * dh;
+                        const uint64_t a_tap = dx_a0 + st16 + (uint64_t)(dh * wp + dw);
+#pragma unroll
+                        for (int k = 0; k < CY / 16; ++k)
+                            mma_bf16(d, a_tap + (uint64_t)(2 * k * reg16),
+                                     dx_b0 + (uint64_t)((uint32_t)(tap * S::WBLK + k * 32) >> 4), IDESC_DX,
+                                     (tap | k) != 0);
+                    }
+                    mma_commit(&acc_full[acc]);
+                    if (++acc == 2) { acc = 0; acc_ph ^= 1u; }
+                    // weight gradient: 8 K16 steps (128 pixel rows) x 9 taps
+                    const uint64_t a_dy = dw_a0 + st16 + (uint64_t)(wp + 1);
+#pragma unroll 1
+                    for (int k = 0; k < 8; ++k) {
+#pragma unroll
+                        for (int tap = 0; tap < 9; ++tap) {
+                            const int dh = tap / 3, dw = tap - 3 * dh;
+                            mma_bf16(tmem_base + (uint32_t)(S::WG_COL0 + tap * CX), a_dy + (uint64_t)(16 * k),
+                                     dw_b0 + st16 + (uint64_t)(dh * wp + dw + 16 * k), IDESC_DW, (n | k) != 0);
+                        }
+                    }
+                    issued = true;
+                    mma_commit(&empty[s]);
+                    if (++s == NS) { s = 0; ph ^= 1u; }
+                }
+            }
+            if (issued) mma_commit(wg_full);
+            else mbar_arrive(wg_full);   // nothing accumulated: release the partial writer
+            if (issued) {
+                mma_commit(drain);
+                if (!mbar_wait_drain(drain, 0)) atomicCAS(p.err, 0, kErrDrain);
+            }
+        }
+    } else {
+        // ------------------------------------------------ epilogue (warps 2..9)
+        const int q = warp & 3;
+        const int grp = (warp - 2) >> 2;
+        const int row = q * 32 + lane;          // input-gradient row: pixel (row / Wp, row % Wp)
+        const int etid = threadIdx.x - 64;      // 0..255
+        const int r = row / p.Wp, c = row - r * p.Wp;
+        const bool in_tile = (r < p.R) && (c < p.W);
+        constexpr int RB = CX * 2;              // output row bytes
+        constexpr uint32_t SWM = RB == 128 ? 7u : RB == 64 ? 3u : 1u;
+        int acc = 0, sb = 0, s = 0;
+        uint32_t acc_ph = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+            const int b = tile / p.tiles_per_img;
+            const int h0 = (tile - b * p.tiles_per_img) * p.R;
+            mbar_wait(&acc_full[acc], acc_ph, abort_flag, p.err, kErrAccWait);
+            if (etid == 0) bulk_wait_read<1>();   // the store that last read staging buffer sb
+            named_bar_sync(1, 256);
+            if (*abort_flag) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * CX);
+            if (grp == 0) {   // CX = 32: one 32-column chunk, taken by the first group
+                float v[32];
+                tmem_ld32(taddr, v);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                if (in_tile) {
+                    // ReLU mask: X > 0 at the same pixel, from the X halo tile of this stage
+                    const uint8_t *xs = sA + s * STAGE + S::DYG * p.region + ((r + 1) * p.Wp + c + 1) * 16;
+#pragma unroll
+                    for (int g = 0; g < S::XG; ++g) {
+                        const uint4 m = *reinterpret_cast<const uint4 *>(xs + g * p.region);
+                        const __nv_bfloat16 *mb = reinterpret_cast<const __nv_bfloat16 *>(&m);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            if (!(__bfloat162float(mb[e]) > 0.0f)) v[g * 8 + e] = 0.0f;
+                    }
+                    uint8_t *tile_buf = outbuf + sb * p.out_tile_bytes;
+                    const uint32_t base_off = (uint32_t)((r * p.W + c) * RB);
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        uint4 pk;
+                        __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            h2[e] = __floats2bfloat162_rn(v[q4 * 8 + 2 * e], v[q4 * 8 + 2 * e + 1]);
+                        const uint32_t o = base_off + 16 * q4;
+                        *reinterpret_cast<uint4 *>(tile_buf + (o ^ (((o >> 7) & SWM) << 4))) = pk;
+                    }
+                }
+            } else {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            }
+            fence_proxy_async_smem();
+            named_bar_sync(2, 256);
+            if (etid == 0) {
+                mbar_arrive(&empty[s]);   // this stage's mask reads are done
+                tma_store_4d(&p.out_map, outbuf + sb * p.out_tile_bytes, 0, 0, h0, b);
+                bulk_commit();
+            }
+            sb ^= 1;
+            if (++s == NS) s = 0;
+            if (++acc == 2) { acc = 0; acc_ph ^= 1u; }
+        }
+        if (etid == 0) bulk_wait_all();   // stores complete before exit
+        // weight-gradient partial of this CTA: rows co, columns (tap, ci)
+        mbar_wait(wg_full, 0, abort_flag, p.err, kErrAccWait);
+        named_bar_sync(1, 256);
+        if (!*abort_flag) {
+            tc_fence_after();
+            const int m = q * 16 + lane;   // M = 64: lanes 32q .. 32q + 15
+            const bool row_ok = lane < 16;
+            float *part = p.partial + ((size_t)blockIdx.x * CY + (row_ok ? m : 0)) * S::NTOT;
+            const uint32_t waddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)S::WG_COL0;
+            const bool empty_cta = my_tiles == 0;
+#pragma unroll 1
+            for (int cc = grp; cc < S::NTOT / 32; cc += 2) {
+                float v[32];
+                tmem_ld32(waddr + 32 * cc, v);
+                if (!row_ok) continue;
+                float4 *d4 = reinterpret_cast<float4 *>(part + 32 * cc);
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    d4[j] = empty_cta ? make_float4(0.0f, 0.0f, 0.0f, 0.0f)
+                                      : make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, S::TMEM_COLS);
+}
+
+}  // namespace tc
+}  // namespace zb

@@ -26,6 +26,7 @@
 #include "tc_gemm.cuh"
 #include "tc_wgrad.cuh"
 #include "tc_wgrad_halo.cuh"
+#include "tc_conv_bwd_fused.cuh"
 
 namespace zb {
 
@@ -34,6 +35,7 @@ using tc::ConvHaloParams;
 using tc::GemmTcParams;
 using tc::WgradTcParams;
 using tc::WgradHaloParams;
+using tc::ConvBwdFusedParams;
 
 // ====================================================================== host: TMA maps
 namespace tc {
@@ -727,6 +729,10 @@ struct ConvLayer {   // a tensor-core conv stage (conv + ReLU + pool)
     ConvTcParams fwd{}, dgrad{};
     bool halo = false;                   // halo-tile kernels (R * (W + 2) <= 128)
     ConvHaloParams hfwd{}, hdgrad{};
+    bool fused_bwd = false;              // input + weight gradient in one kernel (32 -> 64)
+    ConvBwdFusedParams fbwd{};
+    int fbwd_grid = 0;
+    float *fbwd_partial = nullptr;
     bool wg_halo = false;                // halo-tile weight gradient
     WgradHaloParams whalo{};
     int whalo_grid = 0;
@@ -882,6 +888,26 @@ int launch_wgrad_halo(const WgradHaloParams &p0, int grid) {
     }
     kern<<<grid, 192, smem, stream()>>>(p);
     ZB_LAUNCH_CHECK("wgrad_halo");
+    return kOk;
+}
+
+int run_conv_bwd_fused(const ConvLayer &L) {
+    using S = tc::ConvBwdFusedShape<32, 64, 3>;
+    auto kern = tc::conv_bwd_fused_kernel<32, 64, 3>;
+    ConvBwdFusedParams p = L.fbwd;
+    p.region = S::region(p.R, p.Wp);
+    p.stage_bytes = S::stage_bytes(p.R, p.Wp);
+    p.out_tile_bytes = S::out_tile_bytes(p.R, p.W);
+    const int smem = S::smem(p.R, p.Wp, p.W);
+    if (smem > 227 * 1024) return fail(kBadArg, "conv_bwd_fused: %d bytes of shared memory needed", smem);
+    static int attr = 0;
+    if (attr < smem) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return check_cuda("conv_bwd_fused smem attribute");
+        attr = smem;
+    }
+    kern<<<L.fbwd_grid, 320, smem, stream()>>>(p);
+    ZB_LAUNCH_CHECK("conv_bwd_fused");
     return kOk;
 }
 
@@ -1069,7 +1095,30 @@ int tc_build(Net &n, TcEngine &e) {
         // halo-tile weight gradient: D[co][tap*CIN + ci], column groups x image slices
         // (only for 32 -> 64: at 64 -> 128 the per-tap kernel's single N = 192 MMA per K step
         // reads dY from shared memory once, where the halo kernel reads it once per tap)
-        L.wg_halo = L.halo && L.CIN == 32 && L.COUT == 64;
+        // whole backward of a 32 -> 64 conv on a ReLU output in one kernel: tiles of 4 rows
+        // with a 32-pixel halo row (4 x 32 = 128 K rows), the input's ReLU mask from its tile
+        L.fused_bwd = L.halo && L.CIN == 32 && L.COUT == 64 && L.W + 2 <= 32 && d.mask == prev;
+        if (L.fused_bwd) {
+            ConvBwdFusedParams &f = L.fbwd;
+            f.B = B; f.H = L.H; f.W = L.W; f.Wp = 32; f.R = 128 / f.Wp;
+            f.tiles_per_img = (L.H + f.R - 1) / f.R;
+            f.num_tiles = B * f.tiles_per_img;
+            f.err = device_error_word();
+            const uint32_t hb[4] = {8, (uint32_t)f.Wp, (uint32_t)(f.R + 2), 1};
+            const uint64_t dd[4] = {(uint64_t)L.COUT, (uint64_t)L.W, (uint64_t)L.H, (uint64_t)B};
+            const uint64_t ds[3] = {(uint64_t)L.COUT * 2, (uint64_t)L.COUT * L.W * 2, (uint64_t)L.COUT * L.W * L.H * 2};
+            if ((rc = tc::make_tmap_bf16(&f.dy_map, L.dC, 4, dd, ds, hb, tc::kSwNone))) return rc;
+            const uint64_t xd[4] = {(uint64_t)L.CIN, (uint64_t)L.W, (uint64_t)L.H, (uint64_t)B};
+            const uint64_t xs[3] = {(uint64_t)L.CIN * 2, (uint64_t)L.CIN * L.W * 2, (uint64_t)L.CIN * L.W * L.H * 2};
+            if ((rc = tc::make_tmap_bf16(&f.x_map, prev, 4, xd, xs, hb, tc::kSwNone))) return rc;
+            f.w_map = d.w_map;   // {COUT, CIN, 9}, box {64, CIN, 1}, 128-byte swizzle
+            const uint32_t ob[4] = {(uint32_t)L.CIN, (uint32_t)L.W, (uint32_t)f.R, 1};
+            if ((rc = tc::make_tmap_bf16(&f.out_map, d.out, 4, xd, xs, ob, tc::kSw64))) return rc;
+            L.fbwd_grid = f.num_tiles < sm_count() ? f.num_tiles : sm_count();
+            if ((rc = dalloc(e, &L.fbwd_partial, (size_t)L.fbwd_grid * L.COUT * 9 * L.CIN))) return rc;
+            f.partial = L.fbwd_partial;
+        }
+        L.wg_halo = !L.fused_bwd && L.halo && L.CIN == 32 && L.COUT == 64;
         if (L.wg_halo) {
             WgradHaloParams &w = L.whalo;
             const int ngrp = L.COUT == 128 ? 2 : 1;
@@ -1341,6 +1390,14 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
             if ((rc = reduce(r))) return rc;
         }
         prof_mark(n, "pool_bwd");
+        if (L.fused_bwd) {
+            if ((rc = run_conv_bwd_fused(L))) return rc;
+            ReduceArgs r{L.fbwd_partial, L.fbwd_grid, (long long)L.COUT * 9 * L.CIN, 1, L.COUT, 9 * L.CIN,
+                         L.CIN, 0, 0, 0, n.grads + s.poff, nullptr, nullptr};
+            if ((rc = reduce(r))) return rc;
+            prof_mark(n, "conv_bwd");
+            continue;
+        }
         if ((rc = run_conv_dgrad(L))) return rc;
         prof_mark(n, "conv_dgrad");
         if (L.wg_halo) {

@@ -189,12 +189,23 @@ def tc_work(w: configs.Workload, b: int) -> list[dict]:
     out.append({"label": "softmax_ce", "flops": 6 * b * HD * NC, "bytes": 4 * b * HD, "name": "head"})
     out.append({"label": "linear_bwd", "flops": 4 * b * F * HD, "bytes": 2 * (2 * b * F + 2 * b * HD + F * HD) + 4 * F * HD,
                 "name": "fc1 dX+dW"})
+    # the first conv's weight gradient is taken inside the next conv's fused
+    # backward when that one is 32 -> 64 on the unpooled, same-size first-conv output
+    a0, o0, ih0, iw0, oh0, ow0, pool0 = convs[0]
+    c1_fused = (len(convs) > 1 and convs[1][:2] == (32, 64) and o0 == 32 and not pool0 and (oh0, ow0) == (ih0, iw0)
+                and convs[1][3] + 2 <= 32 and (4 * convs[1][3]) % 16 == 0)
     for k in range(len(convs) - 1, -1, -1):
         a, o, ih, iw, oh, ow, pool = convs[k]
         if k > 0:
             out.append({"label": "pool_bwd", "flops": 0, "bytes": b * ((oh // 2) * (ow // 2) * o * 3 + oh * ow * o * 2),
                         "name": f"unpool{k + 1}"})
             f = 2 * b * oh * ow * o * a * 9
+            if (a, o) == (32, 64) and k == 1 and c1_fused:
+                # one kernel: reads dY, X and the first conv's fp32 input; dX stays on chip
+                out.append({"label": "conv_bwd", "flops": 2 * f + 2 * b * oh0 * ow0 * o0 * 9,
+                            "bytes": b * (oh * ow * o * 2 + ih * iw * a * 2 + ih0 * iw0 * 4),
+                            "name": f"conv{k + 1} dX+dW, conv1 dW"})
+                break
             if (a, o) == (32, 64):
                 # one kernel for both: reads dY and X once, writes dX
                 out.append({"label": "conv_bwd", "flops": 2 * f,

@@ -30,6 +30,18 @@
 // owner, warps 2-9 epilogue (input gradient: staged bf16 tile + TMA store, as
 // conv_halo_kernel's kEpiDgrad; weight gradient partial at the end).  Every
 // wait is bounded (tc_common.cuh).
+//
+// C1 (X is the ReLU output of a first conv with one input channel, 3x3, pad 1):
+// that conv's weight gradient dW1[co][t] = sum_p dX[p][co] x[p + t] is taken here
+// too, from the masked dX tile, so dX never goes to global memory.  The staged
+// dX tile (rows = the R*W pixels, 64 bytes of 32 channels, 64-byte swizzle) is
+// an MN-major UMMA operand with K = pixels; the second epilogue warp group
+// builds the matching im2col tile of x (rows = pixels, 64 bf16: x_hi of the 9
+// taps, 1.0 for the bias, x_lo of the 9 taps at 16.., with x = x_hi + x_lo so the
+// fp32 input keeps its precision; 128-byte swizzle).  One elected epilogue
+// thread issues the R*W/16 MMAs D1[64][32] += im2col^T dX per tile (M = 64, N =
+// 32); at the end D1's hi rows (+ bias) and lo rows go out as two [32][10]
+// partials per CTA, which the deterministic split reduction adds.
 #pragma once
 
 #include "tc_common.cuh"
@@ -45,10 +57,13 @@ struct ConvBwdFusedParams {
     int B, H, W, R, Wp, tiles_per_img, num_tiles;
     int region, stage_bytes, out_tile_bytes;   // set by the launcher
     float *partial;       // [gridDim.x][CY][9 * CX]
+    const float *x0;      // C1: the first conv's input [B, H, W] fp32
+    float *c1_partial;    // C1: [gridDim.x * 2][CX][10] (9 taps, bias; x_hi and x_lo halves)
+    int x9_bytes;         // C1: one im2col tile (R * W rows of 128 B, 1024-aligned)
     int *err;
 };
 
-template <int CX, int CY, int NS>
+template <int CX, int CY, int NS, bool C1 = false>
 struct ConvBwdFusedShape {
     static constexpr int NTOT = 9 * CX;
     static constexpr int DYG = CY / 8, XG = CX / 8;
@@ -57,29 +72,32 @@ struct ConvBwdFusedShape {
     static constexpr int WTOTAL = 9 * WBLK;
     static constexpr uint32_t TMEM_COLS = 512;           // 2 * CX + NTOT <= 512
     static constexpr int WG_COL0 = 2 * CX;                // weight-gradient columns start
+    static constexpr int C1_COL0 = WG_COL0 + 9 * CX;      // first-conv weight-gradient columns (C1)
     static constexpr int SLACK = 1024;
     static constexpr int BAR_BYTES = 256;
     static __host__ __device__ int region(int R, int Wp) { return ((R + 2) * Wp * 16 + 127) / 128 * 128; }
     static __host__ __device__ int stage_bytes(int R, int Wp) { return ((DYG + XG) * region(R, Wp) + 1023) / 1024 * 1024; }
     static __host__ __device__ int out_tile_bytes(int R, int W) { return (R * W * CX * 2 + 1023) / 1024 * 1024; }
+    static __host__ __device__ int x9_bytes(int R, int W) { return C1 ? (R * W * 128 + 1023) / 1024 * 1024 : 0; }
     static __host__ __device__ int smem(int R, int Wp, int W) {
-        return 1024 + WTOTAL + NS * stage_bytes(R, Wp) + SLACK + 2 * out_tile_bytes(R, W) + BAR_BYTES;
+        return 1024 + WTOTAL + NS * stage_bytes(R, Wp) + SLACK + 2 * (out_tile_bytes(R, W) + x9_bytes(R, W)) + BAR_BYTES;
     }
     static_assert(CY == 64 && CX == 32, "built for the 32 -> 64 conv: M = 64 weight gradient, N = 32 input gradient");
-    static_assert(2 * CX + NTOT <= 512, "TMEM columns");
+    static_assert(2 * CX + NTOT + (C1 ? CX : 0) <= 512, "TMEM columns");
 };
 
-template <int CX, int CY, int NS>
+template <int CX, int CY, int NS, bool C1 = false>
 __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_constant__ ConvBwdFusedParams p) {
-    using S = ConvBwdFusedShape<CX, CY, NS>;
+    using S = ConvBwdFusedShape<CX, CY, NS, C1>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
     uint8_t *sW = base;
     uint8_t *sA = sW + S::WTOTAL;
     const int STAGE = p.stage_bytes;
-    uint8_t *outbuf = sA + NS * STAGE + S::SLACK;   // [2] staged input-gradient tiles
-    uint64_t *bars = reinterpret_cast<uint64_t *>(outbuf + 2 * p.out_tile_bytes);
+    uint8_t *outbuf = sA + NS * STAGE + S::SLACK;   // [2] staged input-gradient tiles (+ im2col tiles, C1)
+    const int OBUF = p.out_tile_bytes + (C1 ? p.x9_bytes : 0);   // one buffer: [dX tile][im2col tile]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(outbuf + 2 * OBUF);
     uint64_t *full = bars;               // [NS]
     uint64_t *empty = bars + NS;         // [NS]: MMA commit + epilogue mask release
     uint64_t *acc_full = bars + 2 * NS;  // [2]
@@ -87,7 +105,8 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
     uint64_t *wbar = acc_empty + 2;
     uint64_t *wg_full = wbar + 1;
     uint64_t *drain = wg_full + 1;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    uint64_t *c1_done = drain + 1;       // [2] (C1): the first-conv MMAs reading buffer i finished
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(c1_done + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     int *armed = const_cast<int *>(abort_flag) + 1;   // [NS]
 
@@ -106,6 +125,8 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
         mbar_init(wbar, 1);
         mbar_init(wg_full, 1);
         mbar_init(drain, 1);
+        mbar_init(&c1_done[0], 1);
+        mbar_init(&c1_done[1], 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -213,13 +234,38 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
         const bool in_tile = (r < p.R) && (c < p.W);
         constexpr int RB = CX * 2;              // output row bytes
         constexpr uint32_t SWM = RB == 128 ? 7u : RB == 64 ? 3u : 1u;
-        int acc = 0, sb = 0, s = 0;
+        int acc = 0, sb = 0, s = 0, n = 0;
         uint32_t acc_ph = 0;
-        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+        uint32_t c1_ph[2] = {0u, 0u};
+        int c1_pending[2] = {0, 0};   // (elected thread) commits on c1_done[i] not yet waited for
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++n) {
             const int b = tile / p.tiles_per_img;
             const int h0 = (tile - b * p.tiles_per_img) * p.R;
+            // C1: the second group loads the 9 taps of the first conv's input at pixel
+            // (h0 + r, c) before the accumulator wait (zero outside the image)
+            float xt[9];
+            if (C1 && grp == 1) {
+                const int h = h0 + r;
+#pragma unroll
+                for (int t = 0; t < 9; ++t) {
+                    const int ih = h + t / 3 - 1, iw = c + t % 3 - 1;
+                    xt[t] = (in_tile && h < p.H && (unsigned)ih < (unsigned)p.H && (unsigned)iw < (unsigned)p.W)
+                                ? __ldg(p.x0 + ((size_t)b * p.H + ih) * p.W + iw)
+                                : 0.0f;
+                }
+            }
             mbar_wait(&acc_full[acc], acc_ph, abort_flag, p.err, kErrAccWait);
-            if (etid == 0) bulk_wait_read<1>();   // the store that last read staging buffer sb
+            if (etid == 0) {
+                if (C1) {   // the first-conv MMAs that last read buffer sb are done
+                    if (c1_pending[sb]) {
+                        mbar_wait(&c1_done[sb], c1_ph[sb], abort_flag, p.err, kErrAccWait);
+                        c1_ph[sb] ^= 1u;
+                        c1_pending[sb] = 0;
+                    }
+                } else {
+                    bulk_wait_read<1>();   // the store that last read staging buffer sb
+                }
+            }
             named_bar_sync(1, 256);
             if (*abort_flag) break;
             tc_fence_after();
@@ -241,7 +287,7 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
                         for (int e = 0; e < 8; ++e)
                             if (!(__bfloat162float(mb[e]) > 0.0f)) v[g * 8 + e] = 0.0f;
                     }
-                    uint8_t *tile_buf = outbuf + sb * p.out_tile_bytes;
+                    uint8_t *tile_buf = outbuf + sb * OBUF;
                     const uint32_t base_off = (uint32_t)((r * p.W + c) * RB);
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
@@ -258,19 +304,63 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                if (C1 && in_tile) {
+                    // im2col row of the first conv's input for pixel (h0 + r, c): x_hi of the
+                    // 9 taps, 1.0 (bias), x_lo at 16..24; zero rows past the image
+                    const int h = h0 + r;
+                    __nv_bfloat16 vals[32];
+#pragma unroll
+                    for (int t = 0; t < 9; ++t) {
+                        const __nv_bfloat16 hi = __float2bfloat16_rn(xt[t]);
+                        vals[t] = hi;
+                        vals[16 + t] = __float2bfloat16_rn(xt[t] - __bfloat162float(hi));
+                    }
+                    vals[9] = __float2bfloat16_rn(h < p.H ? 1.0f : 0.0f);
+#pragma unroll
+                    for (int t = 10; t < 16; ++t) vals[t] = __float2bfloat16_rn(0.0f);
+#pragma unroll
+                    for (int t = 25; t < 32; ++t) vals[t] = __float2bfloat16_rn(0.0f);
+                    uint8_t *x9 = outbuf + sb * OBUF + p.out_tile_bytes;
+                    const uint32_t k = (uint32_t)(r * p.W + c);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {   // 128-byte row, 16-byte chunk j XOR (k & 7)
+                        uint4 pk = make_uint4(0, 0, 0, 0);
+                        if (j < 4) pk = *reinterpret_cast<const uint4 *>(&vals[8 * j]);
+                        *reinterpret_cast<uint4 *>(x9 + k * 128 + ((j ^ (k & 7)) << 4)) = pk;
+                    }
+                }
             }
             fence_proxy_async_smem();
             named_bar_sync(2, 256);
             if (etid == 0) {
                 mbar_arrive(&empty[s]);   // this stage's mask reads are done
-                tma_store_4d(&p.out_map, outbuf + sb * p.out_tile_bytes, 0, 0, h0, b);
-                bulk_commit();
+                if (C1) {
+                    // D1[64][CX] += im2col^T (MN-major, 128-byte swizzle) x dX (MN-major, 64-byte swizzle)
+                    tc_fence_after();
+                    constexpr uint32_t IDESC_C1 = idesc_bf16(64, CX, true, true);
+                    const uint32_t xa = smem_u32(outbuf + sb * OBUF + p.out_tile_bytes);
+                    const uint32_t db = smem_u32(outbuf + sb * OBUF);
+                    const int ksteps = (p.R * p.W) / 16;
+                    for (int k = 0; k < ksteps; ++k)
+                        mma_bf16(tmem_base + (uint32_t)S::C1_COL0, smem_desc(xa + k * 2048, 16, 1024, kSw128),
+                                 smem_desc(db + k * 1024, 16, 512, kSw64), IDESC_C1, (n | k) != 0);
+                    mma_commit(&c1_done[sb]);
+                    c1_pending[sb] = 1;
+                } else {
+                    tma_store_4d(&p.out_map, outbuf + sb * p.out_tile_bytes, 0, 0, h0, b);
+                    bulk_commit();
+                }
             }
             sb ^= 1;
             if (++s == NS) s = 0;
             if (++acc == 2) { acc = 0; acc_ph ^= 1u; }
         }
-        if (etid == 0) bulk_wait_all();   // stores complete before exit
+        if (etid == 0) {
+            bulk_wait_all();   // stores complete before exit
+            if (C1)            // and every first-conv MMA finished before D1 is read or TMEM freed
+                for (int i = 0; i < 2; ++i)
+                    if (c1_pending[i] && !mbar_wait_drain(&c1_done[i], c1_ph[i])) atomicCAS(p.err, 0, kErrDrain);
+        }
         // weight-gradient partial of this CTA: rows co, columns (tap, ci)
         mbar_wait(wg_full, 0, abort_flag, p.err, kErrAccWait);
         named_bar_sync(1, 256);
@@ -291,6 +381,18 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
                 for (int j = 0; j < 8; ++j)
                     d4[j] = empty_cta ? make_float4(0.0f, 0.0f, 0.0f, 0.0f)
                                       : make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            }
+            if (C1 && grp == 0 && (q == 0 || q == 1)) {
+                // D1 rows 16q + lane sit in lanes 32q + lane: quarter 0 holds the x_hi taps and
+                // the bias (rows 0..9), quarter 1 the x_lo taps (rows 16..24; row 25 is zero).
+                // Each writes its own [CX][10] slice; the reduction adds the two.
+                float v[32];
+                tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)S::C1_COL0, v);
+                if (lane < 10) {
+                    float *c1p = p.c1_partial + ((size_t)blockIdx.x * 2 + q) * CX * 10;
+#pragma unroll
+                    for (int co = 0; co < CX; ++co) c1p[co * 10 + lane] = empty_cta ? 0.0f : v[co];
+                }
             }
         }
     }

@@ -733,6 +733,7 @@ struct ConvLayer {   // a tensor-core conv stage (conv + ReLU + pool)
     ConvBwdFusedParams fbwd{};
     int fbwd_grid = 0;
     float *fbwd_partial = nullptr;
+    bool fbwd_c1 = false;                // the first conv's weight gradient taken in the same kernel
     bool wg_halo = false;                // halo-tile weight gradient
     WgradHaloParams whalo{};
     int whalo_grid = 0;
@@ -755,6 +756,7 @@ struct TcEngine {
     bf16 *dP1 = nullptr;       // gradient w.r.t. its pooled output (c1_pool)
     float *c1_partial = nullptr;
     int c1_wgrad_grid = 0;
+    bool c1_fused = false;     // first conv's weight gradient from the next conv's backward kernel
     float *c1_bias_partial = nullptr;
     int c1_unpool_grid = 0;
     std::vector<ConvLayer> convs;
@@ -891,13 +893,18 @@ int launch_wgrad_halo(const WgradHaloParams &p0, int grid) {
     return kOk;
 }
 
-int run_conv_bwd_fused(const ConvLayer &L) {
-    using S = tc::ConvBwdFusedShape<32, 64, 3>;
-    auto kern = tc::conv_bwd_fused_kernel<32, 64, 3>;
+template <bool C1>
+int launch_conv_bwd_fused(const ConvLayer &L, const float *x0) {
+    using S = tc::ConvBwdFusedShape<32, 64, 3, C1>;
+    auto kern = tc::conv_bwd_fused_kernel<32, 64, 3, C1>;
     ConvBwdFusedParams p = L.fbwd;
     p.region = S::region(p.R, p.Wp);
     p.stage_bytes = S::stage_bytes(p.R, p.Wp);
     p.out_tile_bytes = S::out_tile_bytes(p.R, p.W);
+    p.x9_bytes = S::x9_bytes(p.R, p.W);
+    p.x0 = x0;
+    if (C1 && (!x0 || !p.c1_partial || (p.R * p.W) % 16 != 0))
+        return fail(kBadArg, "conv_bwd_fused: first-conv weight gradient not set up");
     const int smem = S::smem(p.R, p.Wp, p.W);
     if (smem > 227 * 1024) return fail(kBadArg, "conv_bwd_fused: %d bytes of shared memory needed", smem);
     static int attr = 0;
@@ -909,6 +916,10 @@ int run_conv_bwd_fused(const ConvLayer &L) {
     kern<<<L.fbwd_grid, 320, smem, stream()>>>(p);
     ZB_LAUNCH_CHECK("conv_bwd_fused");
     return kOk;
+}
+
+int run_conv_bwd_fused(const ConvLayer &L, const float *x0) {
+    return L.fbwd_c1 ? launch_conv_bwd_fused<true>(L, x0) : launch_conv_bwd_fused<false>(L, nullptr);
 }
 
 int run_wgrad_halo(const ConvLayer &L) {
@@ -1117,6 +1128,11 @@ int tc_build(Net &n, TcEngine &e) {
             L.fbwd_grid = f.num_tiles < sm_count() ? f.num_tiles : sm_count();
             if ((rc = dalloc(e, &L.fbwd_partial, (size_t)L.fbwd_grid * L.COUT * 9 * L.CIN))) return rc;
             f.partial = L.fbwd_partial;
+            // the masked input gradient is the first conv's output gradient (3x3, pad 1, one
+            // input channel, same size): its weight gradient is taken from the staged tile
+            L.fbwd_c1 = !e.c1_pool && e.C1 == L.CIN && e.pad1 == 1 && e.H1 == e.H0 && e.W1 == e.W0 &&
+                        (f.R * f.W) % 16 == 0;
+            e.c1_fused = L.fbwd_c1;
         }
         L.wg_halo = !L.fused_bwd && L.halo && L.CIN == 32 && L.COUT == 64;
         if (L.wg_halo) {
@@ -1264,10 +1280,15 @@ int tc_build(Net &n, TcEngine &e) {
     if ((rc = dalloc(e, &e.row_loss, (size_t)B))) return rc;
     e.c1_wgrad_grid = sm_count() * 2;   // the resident blocks (two per SM): each walks whole images
     if (e.c1_wgrad_grid > B) e.c1_wgrad_grid = B;
+    if (e.c1_fused) {   // two partials (x_hi and x_lo products) per fused-kernel CTA
+        e.c1_wgrad_grid = 2 * e.convs.front().fbwd_grid;
+        e.convs.front().fbwd.c1_partial = nullptr;
+    }
     if ((rc = dalloc(e, &e.c1_partial, (size_t)e.c1_wgrad_grid * e.C1 * 10))) return rc;
+    if (e.c1_fused) e.convs.front().fbwd.c1_partial = e.c1_partial;
     // diagnostics
     e.views.push_back({"conv1.out", e.a1, (size_t)B * (e.c1_pool ? (e.H1 / 2) * (e.W1 / 2) : e.H1 * e.W1) * e.C1, 0});
-    e.views.push_back({"conv1.dC", e.dC1, (size_t)B * e.H1 * e.W1 * e.C1, 0});
+    if (!e.c1_fused) e.views.push_back({"conv1.dC", e.dC1, (size_t)B * e.H1 * e.W1 * e.C1, 0});
     for (size_t k = 0; k < e.convs.size(); ++k) {
         const ConvLayer &L = e.convs[k];
         const std::string pre = "conv" + std::to_string(k + 2);
@@ -1391,10 +1412,15 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
         }
         prof_mark(n, "pool_bwd");
         if (L.fused_bwd) {
-            if ((rc = run_conv_bwd_fused(L))) return rc;
+            if ((rc = run_conv_bwd_fused(L, x))) return rc;
             ReduceArgs r{L.fbwd_partial, L.fbwd_grid, (long long)L.COUT * 9 * L.CIN, 1, L.COUT, 9 * L.CIN,
                          L.CIN, 0, 0, 0, n.grads + s.poff, nullptr, nullptr};
             if ((rc = reduce(r))) return rc;
+            if (L.fbwd_c1) {
+                ReduceArgs r1{e.c1_partial, e.c1_wgrad_grid, (long long)e.C1 * 10, 5, e.C1, 10, 0, 0, 0, 0,
+                              n.grads + s1.poff, n.grads + s1.poff + s1.pn_w, nullptr};
+                if ((rc = reduce(r1))) return rc;
+            }
             prof_mark(n, "conv_bwd");
             continue;
         }
@@ -1415,6 +1441,7 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
         prof_mark(n, "conv_wgrad");
     }
     // ---- first conv backward (dC1 written by the next conv's dgrad, masked)
+    if (e.c1_fused) return kOk;   // taken by the next conv's fused backward kernel
     if (e.c1_pool) {
         const int G = e.C1 / 8, slots = 256 / G;
         unpool_kernel<<<sm_count() * 4, slots * G, slots * G * 8 * sizeof(float), stream()>>>(

@@ -246,6 +246,43 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// relu(a + ba), relu(b + bb) rounded to bf16 and packed, a in the low half:
+// one packed fp32 add (each lane rounded like a scalar add) and one
+// conversion whose .relu clamps negative results to zero, which equals
+// rounding relu(x) since rounding is monotonic and keeps zero.
+__device__ __forceinline__ uint32_t bias_relu_bf16x2(float a, float b, float ba, float bb) {
+    uint64_t x, y, s;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a), "f"(b));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(ba), "f"(bb));
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(s) : "l"(x), "l"(y));
+    float lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(s));
+    uint32_t d;
+    asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+
+// One step of a running 2x2 max-pool over bf16x2 words: where the candidate c
+// is strictly greater (the first maximum wins ties), the lane's position
+// becomes q; best becomes the lane-wise maximum.
+__device__ __forceinline__ void pool_step_bf16x2(uint32_t &best, uint32_t &pos, uint32_t c, uint32_t q) {
+    const __nv_bfloat162 cb = *reinterpret_cast<const __nv_bfloat162 *>(&c);
+    __nv_bfloat162 bb = *reinterpret_cast<const __nv_bfloat162 *>(&best);
+    const uint32_t m = __hgt2_mask(cb, bb);
+    bb = __hmax2(bb, cb);
+    best = *reinterpret_cast<const uint32_t *>(&bb);
+    pos = (pos & ~m) | (q * 0x00010001u & m);
+}
+
+// Pool codes of two bf16x2 words of ReLU outputs: per channel a byte
+// pos | 4 when the maximum is positive (non-zero magnitude bits), packed in
+// channel order.
+__device__ __forceinline__ uint32_t pool_codes(uint32_t best0, uint32_t pos0, uint32_t best1, uint32_t pos1) {
+    const uint32_t nz0 = (((best0 & 0x7FFF7FFFu) + 0x7FFF7FFFu) & 0x80008000u) >> 13;
+    const uint32_t nz1 = (((best1 & 0x7FFF7FFFu) + 0x7FFF7FFFu) & 0x80008000u) >> 13;
+    return __byte_perm(pos0 | nz0, pos1 | nz1, 0x6420);
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }

@@ -236,8 +236,8 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
         constexpr uint32_t SWM = RB == 128 ? 7u : RB == 64 ? 3u : 1u;
         int acc = 0, sb = 0, s = 0, n = 0;
         uint32_t acc_ph = 0;
-        uint32_t c1_ph[2] = {0u, 0u};
-        int c1_pending[2] = {0, 0};   // (elected thread) commits on c1_done[i] not yet waited for
+        // (elected thread, C1) bit i: a commit on c1_done[i] not yet waited for; bit 2 + i: its parity
+        uint32_t c1_state = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++n) {
             const int b = tile / p.tiles_per_img;
             const int h0 = (tile - b * p.tiles_per_img) * p.R;
@@ -257,10 +257,9 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
             mbar_wait(&acc_full[acc], acc_ph, abort_flag, p.err, kErrAccWait);
             if (etid == 0) {
                 if (C1) {   // the first-conv MMAs that last read buffer sb are done
-                    if (c1_pending[sb]) {
-                        mbar_wait(&c1_done[sb], c1_ph[sb], abort_flag, p.err, kErrAccWait);
-                        c1_ph[sb] ^= 1u;
-                        c1_pending[sb] = 0;
+                    if ((c1_state >> sb) & 1u) {
+                        mbar_wait(&c1_done[sb], (c1_state >> (2 + sb)) & 1u, abort_flag, p.err, kErrAccWait);
+                        c1_state ^= (4u << sb) | (1u << sb);
                     }
                 } else {
                     bulk_wait_read<1>();   // the store that last read staging buffer sb
@@ -345,7 +344,7 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
                         mma_bf16(tmem_base + (uint32_t)S::C1_COL0, smem_desc(xa + k * 2048, 16, 1024, kSw128),
                                  smem_desc(db + k * 1024, 16, 512, kSw64), IDESC_C1, (n | k) != 0);
                     mma_commit(&c1_done[sb]);
-                    c1_pending[sb] = 1;
+                    c1_state |= 1u << sb;
                 } else {
                     tma_store_4d(&p.out_map, outbuf + sb * p.out_tile_bytes, 0, 0, h0, b);
                     bulk_commit();
@@ -359,7 +358,8 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
             bulk_wait_all();   // stores complete before exit
             if (C1)            // and every first-conv MMA finished before D1 is read or TMEM freed
                 for (int i = 0; i < 2; ++i)
-                    if (c1_pending[i] && !mbar_wait_drain(&c1_done[i], c1_ph[i])) atomicCAS(p.err, 0, kErrDrain);
+                    if (((c1_state >> i) & 1u) && !mbar_wait_drain(&c1_done[i], (c1_state >> (2 + i)) & 1u))
+                        atomicCAS(p.err, 0, kErrDrain);
         }
         // weight-gradient partial of this CTA: rows co, columns (tap, ci)
         mbar_wait(wg_full, 0, abort_flag, p.err, kErrAccWait);

@@ -282,19 +282,17 @@ __global__ void __launch_bounds__(320, 2) conv_halo_kernel(const __grid_constant
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&acc_empty[acc]);
                     }
-                    // bias + ReLU -> bf16, the row's 32 channels as four 16-byte stores
+                    // bias + ReLU -> bf16 (packed add, converting clamp), the row's 32
+                    // channels as four 16-byte stores
                     uint4 *srow = reinterpret_cast<uint4 *>(buf + row * S::SP + 32 * cc);
                     const float4 *bias4 = reinterpret_cast<const float4 *>(sbias + 32 * cc);
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
                         const float4 b0 = bias4[2 * k], b1 = bias4[2 * k + 1];
-                        uint4 pk;
-                        __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
-                        h2[0] = __floats2bfloat162_rn(fmaxf(v[8 * k + 0] + b0.x, 0.0f), fmaxf(v[8 * k + 1] + b0.y, 0.0f));
-                        h2[1] = __floats2bfloat162_rn(fmaxf(v[8 * k + 2] + b0.z, 0.0f), fmaxf(v[8 * k + 3] + b0.w, 0.0f));
-                        h2[2] = __floats2bfloat162_rn(fmaxf(v[8 * k + 4] + b1.x, 0.0f), fmaxf(v[8 * k + 5] + b1.y, 0.0f));
-                        h2[3] = __floats2bfloat162_rn(fmaxf(v[8 * k + 6] + b1.z, 0.0f), fmaxf(v[8 * k + 7] + b1.w, 0.0f));
-                        srow[k] = pk;
+                        srow[k] = make_uint4(bias_relu_bf16x2(v[8 * k + 0], v[8 * k + 1], b0.x, b0.y),
+                                             bias_relu_bf16x2(v[8 * k + 2], v[8 * k + 3], b0.z, b0.w),
+                                             bias_relu_bf16x2(v[8 * k + 4], v[8 * k + 5], b1.x, b1.y),
+                                             bias_relu_bf16x2(v[8 * k + 6], v[8 * k + 7], b1.z, b1.w));
                     }
                 }
                 named_bar_sync(2, 256);
@@ -306,29 +304,22 @@ __global__ void __launch_bounds__(320, 2) conv_halo_kernel(const __grid_constant
                     if (ho >= Ho) continue;
                     const int r0 = (2 * pr) * p.Wp + 2 * pc;
                     const int rr[4] = {r0, r0 + 1, r0 + p.Wp, r0 + p.Wp + 1};
-                    float best[8];
-                    int pos[8];
+                    uint4 px[4];
 #pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {   // (kh, kw) order: first maximum wins
-                        uint4 raw8 = *reinterpret_cast<const uint4 *>(buf + rr[q4] * S::SP + 8 * o);
-                        const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&raw8);
+                    for (int q4 = 0; q4 < 4; ++q4) px[q4] = *reinterpret_cast<const uint4 *>(buf + rr[q4] * S::SP + 8 * o);
+                    // (kh, kw) order, bf16x2 lanes: first maximum wins
+                    uint32_t best[4] = {px[0].x, px[0].y, px[0].z, px[0].w}, pos[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float2 f = __bfloat1622float2(h2[e]);
-                            if (q4 == 0 || f.x > best[2 * e]) { best[2 * e] = f.x; pos[2 * e] = q4; }
-                            if (q4 == 0 || f.y > best[2 * e + 1]) { best[2 * e + 1] = f.y; pos[2 * e + 1] = q4; }
-                        }
+                    for (int q4 = 1; q4 < 4; ++q4) {
+                        pool_step_bf16x2(best[0], pos[0], px[q4].x, (uint32_t)q4);
+                        pool_step_bf16x2(best[1], pos[1], px[q4].y, (uint32_t)q4);
+                        pool_step_bf16x2(best[2], pos[2], px[q4].z, (uint32_t)q4);
+                        pool_step_bf16x2(best[3], pos[3], px[q4].w, (uint32_t)q4);
                     }
-                    uint4 pk;
-                    __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) h2[e] = __floats2bfloat162_rn(best[2 * e], best[2 * e + 1]);
-                    uint2 cd;
-                    uint8_t *cb = reinterpret_cast<uint8_t *>(&cd);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) cb[e] = (uint8_t)(pos[e] | (best[e] > 0.0f ? 4 : 0));
+                    const uint2 cd = make_uint2(pool_codes(best[0], pos[0], best[1], pos[1]),
+                                                pool_codes(best[2], pos[2], best[3], pos[3]));
                     const size_t o8 = (((size_t)b * Ho + ho) * Wo + pc) * COUT + 8 * o;
-                    *reinterpret_cast<uint4 *>(p.out + o8) = pk;
+                    *reinterpret_cast<uint4 *>(p.out + o8) = make_uint4(best[0], best[1], best[2], best[3]);
                     *reinterpret_cast<uint2 *>(p.code + o8) = cd;
                 }
                 // A staging buffer is rewritten only after the next tile's

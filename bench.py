@@ -197,14 +197,19 @@ def tc_work(w: configs.Workload, b: int) -> list[dict]:
     for k in range(len(convs) - 1, -1, -1):
         a, o, ih, iw, oh, ow, pool = convs[k]
         if k > 0:
-            out.append({"label": "pool_bwd", "flops": 0, "bytes": b * ((oh // 2) * (ow // 2) * o * 3 + oh * ow * o * 2),
-                        "name": f"unpool{k + 1}"})
+            # the 32 -> 64 fused backward builds dY from the pooled gradient and the codes itself
+            up = (a, o) == (32, 64) and k == 1 and not pool0 and iw + 2 <= 32 and pool and oh % 2 == 0 and ow % 2 == 0
+            if not up:
+                out.append({"label": "pool_bwd", "flops": 0,
+                            "bytes": b * ((oh // 2) * (ow // 2) * o * 3 + oh * ow * o * 2), "name": f"unpool{k + 1}"})
             f = 2 * b * oh * ow * o * a * 9
             if (a, o) == (32, 64) and k == 1 and c1_fused:
-                # one kernel: reads dY, X and the first conv's fp32 input; dX stays on chip
+                # one kernel: reads the pooled dY and its codes (or dY), X and the first conv's
+                # fp32 input; dY and dX stay on chip
+                dy_bytes = (oh // 2) * (ow // 2) * o * 3 if up else oh * ow * o * 2
                 out.append({"label": "conv_bwd", "flops": 2 * f + 2 * b * oh0 * ow0 * o0 * 9,
-                            "bytes": b * (oh * ow * o * 2 + ih * iw * a * 2 + ih0 * iw0 * 4),
-                            "name": f"conv{k + 1} dX+dW, conv1 dW"})
+                            "bytes": b * (dy_bytes + ih * iw * a * 2 + ih0 * iw0 * 4),
+                            "name": f"{'unpool2+' if up else ''}conv{k + 1} dX+dW, conv1 dW"})
                 break
             if (a, o) == (32, 64):
                 # one kernel for both: reads dY and X once, writes dX

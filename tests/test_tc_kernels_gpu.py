@@ -129,7 +129,8 @@ def test_conv_backward(step):
     check("conv3 dX (bf16)", v["conv2.dP"].reshape(B, 14, 14, 64), conv_dgrad(dC3, bf16(par["W5"])), 1e-2)
     check("conv3 dW", grd["W5"], conv_wgrad(p2, dC3), 2e-3)
     dC2 = unpool(v["conv2.dP"].reshape(B, 14, 14, 64), code2, 28, 28)
-    assert np.array_equal(v["conv2.dC"].reshape(B, 28, 28, 64), dC2), "unpool2 routing"
+    if "conv2.dC" in v:   # else dC2 is built on chip by conv2's backward kernel from dP2 and the codes
+        assert np.array_equal(v["conv2.dC"].reshape(B, 28, 28, 64), dC2), "unpool2 routing"
     check("db conv2", grd["b2"], dC2.sum((0, 1, 2)), 2e-3)
     dC1_ref = conv_dgrad(dC2, bf16(par["W2"])) * (a1 > 0)
     if "conv1.dC" in v:   # input gradient of conv2 written to global memory

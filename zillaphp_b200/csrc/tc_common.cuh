@@ -283,6 +283,16 @@ __device__ __forceinline__ uint32_t pool_codes(uint32_t best0, uint32_t pos0, ui
     return __byte_perm(pos0 | nz0, pos1 | nz1, 0x6420);
 }
 
+// Max-unpool of 8 channels: the lanes of pv whose code (a nibble of sel_lo for
+// channels 0-3, sel_hi for 4-7; codes 0..7) selects a 0xFF byte of the table
+// (0, tab), zero elsewhere.  tab = 0xFF << 8q keeps the channels routed to
+// window position q (code 4 | q); tab = ~0 keeps every routed channel.
+__device__ __forceinline__ uint4 unpool_select(uint4 pv, uint32_t sel_lo, uint32_t sel_hi, uint32_t tab) {
+    const uint32_t m_lo = __byte_perm(0u, tab, sel_lo), m_hi = __byte_perm(0u, tab, sel_hi);
+    return make_uint4(pv.x & __byte_perm(m_lo, 0u, 0x1100), pv.y & __byte_perm(m_lo, 0u, 0x3322),
+                      pv.z & __byte_perm(m_hi, 0u, 0x1100), pv.w & __byte_perm(m_hi, 0u, 0x3322));
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }

@@ -42,6 +42,20 @@
 // thread issues the R*W/16 MMAs D1[64][32] += im2col^T dX per tile (M = 64, N =
 // 32); at the end D1's hi rows (+ bias) and lo rows go out as two [32][10]
 // partials per CTA, which the deterministic split reduction adds.
+//
+// UP (dY is the max-unpool of the pooled gradient dP [B, H/2, W/2, CY] by the
+// pool codes [B, H/2, W/2, CY], byte = window position | 4 when routed): four
+// more warps (10-13) build each stage's dY halo tile in shared memory from dP
+// and the codes instead of a TMA load of dY, so dY never exists in global
+// memory.  Work item = (pooled row of the halo, pooled column, 8-channel
+// octet): one 16-byte dP load and one 8-byte code load give the 2 or 4
+// 16-byte chunks of its 2x2 window that lie in the halo rows; a channel keeps
+// its value at the position its code names and is zero at the other three.
+// The halo columns outside the image are never written (zero since the
+// start).  The dY octet pitch is the row block plus 16 bytes so that the
+// octets of one pixel fall in different shared-memory banks.  The builders
+// also sum the routed values of the tile's own pooled rows per channel: the
+// bias gradient of this conv, one [CY] partial per CTA.
 #pragma once
 
 #include "tc_common.cuh"
@@ -60,11 +74,16 @@ struct ConvBwdFusedParams {
     const float *x0;      // C1: the first conv's input [B, H, W] fp32
     float *c1_partial;    // C1: [gridDim.x * 2][CX][10] (9 taps, bias; x_hi and x_lo halves)
     int x9_bytes;         // C1: one im2col tile (R * W rows of 128 B, 1024-aligned)
+    const __nv_bfloat16 *dp;   // UP: pooled gradient [B, H/2, W/2, CY]
+    const uint8_t *code;       // UP: pool codes [B, H/2, W/2, CY]
+    float *bias_partial;       // UP: [gridDim.x * 4][CY] (one slice per builder warp)
+    int dy_region, x_off;      // dY octet pitch, offset of the X octets in a stage (set by the launcher)
     int *err;
 };
 
-template <int CX, int CY, int NS, bool C1 = false>
+template <int CX, int CY, int NS, bool C1 = false, bool UP = false>
 struct ConvBwdFusedShape {
+    static constexpr int THREADS = UP ? 448 : 320;
     static constexpr int NTOT = 9 * CX;
     static constexpr int DYG = CY / 8, XG = CX / 8;
     static constexpr int WROWB = CY * 2;                 // dgrad weight row: 128 B (CY = 64)
@@ -76,7 +95,9 @@ struct ConvBwdFusedShape {
     static constexpr int SLACK = 1024;
     static constexpr int BAR_BYTES = 256;
     static __host__ __device__ int region(int R, int Wp) { return ((R + 2) * Wp * 16 + 127) / 128 * 128; }
-    static __host__ __device__ int stage_bytes(int R, int Wp) { return ((DYG + XG) * region(R, Wp) + 1023) / 1024 * 1024; }
+    static __host__ __device__ int dy_region(int R, int Wp) { return region(R, Wp) + (UP ? 16 : 0); }
+    static __host__ __device__ int x_off(int R, int Wp) { return (DYG * dy_region(R, Wp) + 127) / 128 * 128; }
+    static __host__ __device__ int stage_bytes(int R, int Wp) { return (x_off(R, Wp) + XG * region(R, Wp) + 1023) / 1024 * 1024; }
     static __host__ __device__ int out_tile_bytes(int R, int W) { return (R * W * CX * 2 + 1023) / 1024 * 1024; }
     static __host__ __device__ int x9_bytes(int R, int W) { return C1 ? (R * W * 128 + 1023) / 1024 * 1024 : 0; }
     static __host__ __device__ int smem(int R, int Wp, int W) {
@@ -86,9 +107,9 @@ struct ConvBwdFusedShape {
     static_assert(2 * CX + NTOT + (C1 ? CX : 0) <= 512, "TMEM columns");
 };
 
-template <int CX, int CY, int NS, bool C1 = false>
-__global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_constant__ ConvBwdFusedParams p) {
-    using S = ConvBwdFusedShape<CX, CY, NS, C1>;
+template <int CX, int CY, int NS, bool C1 = false, bool UP = false>
+__global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const __grid_constant__ ConvBwdFusedParams p) {
+    using S = ConvBwdFusedShape<CX, CY, NS, C1, UP>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -120,7 +141,8 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < NS; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 2); armed[i] = 0; }
+        // full: the TMA transaction arrival (+ one per builder warp, UP)
+        for (int i = 0; i < NS; ++i) { mbar_init(&full[i], UP ? 5 : 1); mbar_init(&empty[i], 2); armed[i] = 0; }
         for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 8); }
         mbar_init(wbar, 1);
         mbar_init(wg_full, 1);
@@ -139,13 +161,13 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (elect_one()) {
-            prefetch_tmap(&p.dy_map);
+            if (!UP) prefetch_tmap(&p.dy_map);
             prefetch_tmap(&p.x_map);
             prefetch_tmap(&p.w_map);
             prefetch_tmap(&p.out_map);
             mbar_arrive_expect_tx(wbar, S::WTOTAL);
             for (int t = 0; t < 9; ++t) tma_load_3d(sW + t * S::WBLK, &p.w_map, wbar, 0, 0, t);
-            const uint32_t tx = (uint32_t)((S::DYG + S::XG) * (p.R + 2) * p.Wp * 16);
+            const uint32_t tx = (uint32_t)(((UP ? 0 : S::DYG) + S::XG) * (p.R + 2) * p.Wp * 16);
             int s = 0;
             uint32_t ph = 0;
             for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
@@ -155,10 +177,11 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
                 mbar_arrive_expect_tx(&full[s], tx);
                 armed[s] = (int)ph + 1;
                 uint8_t *st = sA + s * STAGE;
-                for (int g = 0; g < S::DYG; ++g)
-                    tma_load_4d(st + g * p.region, &p.dy_map, &full[s], 8 * g, -1, h0 - 1, b);
+                if (!UP)
+                    for (int g = 0; g < S::DYG; ++g)
+                        tma_load_4d(st + g * p.dy_region, &p.dy_map, &full[s], 8 * g, -1, h0 - 1, b);
                 for (int g = 0; g < S::XG; ++g)
-                    tma_load_4d(st + (S::DYG + g) * p.region, &p.x_map, &full[s], 8 * g, -1, h0 - 1, b);
+                    tma_load_4d(st + p.x_off + g * p.region, &p.x_map, &full[s], 8 * g, -1, h0 - 1, b);
                 if (++s == NS) { s = 0; ph ^= 1u; }
             }
             if (*abort_flag) {
@@ -174,12 +197,12 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
             if (mbar_wait(wbar, 0, abort_flag, p.err, kErrFullWait)) {
                 int s = 0, acc = 0;
                 uint32_t ph = 0, acc_ph = 0;
-                const uint32_t lbo = (uint32_t)p.region, reg16 = lbo >> 4;
+                const uint32_t lbo = (uint32_t)p.dy_region, reg16 = lbo >> 4;
                 // descriptors differ only in the start address (16-byte units)
                 const uint64_t dx_a0 = smem_desc(smem_u32(sA), lbo, 128, kSwNone);          // K-major dY
                 const uint64_t dx_b0 = smem_desc(smem_u32(sW), 16, 8 * S::WROWB, kSw128);   // weights
                 const uint64_t dw_a0 = smem_desc(smem_u32(sA), 128, lbo, kSwNone);          // MN-major dY
-                const uint64_t dw_b0 = smem_desc(smem_u32(sA) + (uint32_t)(S::DYG * p.region), 128, lbo, kSwNone);
+                const uint64_t dw_b0 = smem_desc(smem_u32(sA) + (uint32_t)p.x_off, 128, (uint32_t)p.region, kSwNone);
                 const uint32_t wp = (uint32_t)p.Wp;
                 int n = 0;
                 for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x, ++n) {
@@ -223,6 +246,85 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
                 mma_commit(drain);
                 if (!mbar_wait_drain(drain, 0)) atomicCAS(p.err, 0, kErrDrain);
             }
+        }
+    } else if (UP && warp >= 10) {
+        // ------------------------------------------------ dY builders (warps 10..13, UP)
+        const int bt = threadIdx.x - 320;   // 0..127
+        const int g = bt & 7;               // channel octet of every item of this thread
+        const int Ho = p.H >> 1, Wo = p.W >> 1;
+        const int nitems = 4 * Wo * 8;      // 4 pooled rows cover the R + 2 = 6 halo rows
+        float bsum[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) bsum[e] = 0.0f;
+        int s = 0;
+        uint32_t ph = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
+            const int b = tile / p.tiles_per_img;
+            const int h0 = (tile - b * p.tiles_per_img) * p.R;
+            // this tile's dP and code loads go out before the stage wait
+            uint4 pv[4];
+            uint2 cd[4];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const int i = bt + 128 * m;
+                const int wi = i >> 3, prow = wi / Wo, pw = wi - prow * Wo;
+                const int phr = (h0 >> 1) - 1 + prow;   // pooled row
+                pv[m] = make_uint4(0, 0, 0, 0);
+                cd[m] = make_uint2(0, 0);
+                if (i < nitems && (unsigned)phr < (unsigned)Ho) {
+                    const size_t o = (((size_t)b * Ho + phr) * Wo + pw) * CY + 8 * g;
+                    pv[m] = __ldg(reinterpret_cast<const uint4 *>(p.dp + o));
+                    cd[m] = __ldg(reinterpret_cast<const uint2 *>(p.code + o));
+                }
+            }
+            if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err, kErrEmptyWait)) break;
+            uint8_t *st = sA + s * STAGE + g * p.dy_region;
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const int i = bt + 128 * m;
+                if (i >= nitems) continue;
+                const int wi = i >> 3, prow = wi / Wo, pw = wi - prow * Wo;
+                // selector nibbles = the 8 codes (values 0..7)
+                const uint32_t t0 = cd[m].x | (cd[m].x >> 4), t1 = cd[m].y | (cd[m].y >> 4);
+                const uint32_t sel0 = (t0 & 0xFFu) | ((t0 >> 8) & 0xFF00u);
+                const uint32_t sel1 = (t1 & 0xFFu) | ((t1 >> 8) & 0xFF00u);
+                // halo row of the window's top image row: 2 * pooled row - (h0 - 1)
+                const int hr0 = 2 * prow - 1;
+#pragma unroll
+                for (int kh = 0; kh < 2; ++kh) {
+                    const int hr = hr0 + kh;
+                    if (hr < 0 || hr > p.R + 1) continue;
+                    uint8_t *rowp = st + (hr * p.Wp + 2 * pw + 1) * 16;
+#pragma unroll
+                    for (int kw = 0; kw < 2; ++kw)
+                        *reinterpret_cast<uint4 *>(rowp + kw * 16) =
+                            unpool_select(pv[m], sel0, sel1, 0xFFu << (8 * (2 * kh + kw)));
+                }
+                if (prow == 1 || prow == 2) {   // the tile's own pooled rows: bias-gradient sums
+                    const uint4 r4 = unpool_select(pv[m], sel0, sel1, 0xFFFFFFFFu);   // any code >= 4
+                    const uint32_t w[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        bsum[2 * e] += __uint_as_float(w[e] << 16);
+                        bsum[2 * e + 1] += __uint_as_float(w[e] & 0xFFFF0000u);
+                    }
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[s]);
+            if (++s == NS) { s = 0; ph ^= 1u; }
+        }
+        // bias-gradient partial of this CTA: the 16 threads of each octet, in a fixed order
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            bsum[e] += __shfl_xor_sync(0xffffffffu, bsum[e], 8);
+            bsum[e] += __shfl_xor_sync(0xffffffffu, bsum[e], 16);
+        }
+        if (lane < 8) {   // lane = octet: one [CY] slice per builder warp, summed by the split reduction
+            float *bp = p.bias_partial + ((size_t)blockIdx.x * 4 + (warp - 10)) * CY + 8 * lane;
+            reinterpret_cast<float4 *>(bp)[0] = make_float4(bsum[0], bsum[1], bsum[2], bsum[3]);
+            reinterpret_cast<float4 *>(bp)[1] = make_float4(bsum[4], bsum[5], bsum[6], bsum[7]);
         }
     } else {
         // ------------------------------------------------ epilogue (warps 2..9)
@@ -277,7 +379,7 @@ __global__ void __launch_bounds__(320, 1) conv_bwd_fused_kernel(const __grid_con
                 if (lane == 0) mbar_arrive(&acc_empty[acc]);
                 if (in_tile) {
                     // ReLU mask: X > 0 at the same pixel, from the X halo tile of this stage
-                    const uint8_t *xs = sA + s * STAGE + S::DYG * p.region + ((r + 1) * p.Wp + c + 1) * 16;
+                    const uint8_t *xs = sA + s * STAGE + p.x_off + ((r + 1) * p.Wp + c + 1) * 16;
 #pragma unroll
                     for (int g = 0; g < S::XG; ++g) {
                         const uint4 m = *reinterpret_cast<const uint4 *>(xs + g * p.region);

@@ -734,6 +734,8 @@ struct ConvLayer {   // a tensor-core conv stage (conv + ReLU + pool)
     int fbwd_grid = 0;
     float *fbwd_partial = nullptr;
     bool fbwd_c1 = false;                // the first conv's weight gradient taken in the same kernel
+    bool fbwd_up = false;                // dY built in the kernel from dP and the pool codes (no unpool)
+    float *fbwd_bias_partial = nullptr;  // fbwd_up: [fbwd_grid * 4][COUT]
     bool wg_halo = false;                // halo-tile weight gradient
     WgradHaloParams whalo{};
     int whalo_grid = 0;
@@ -893,13 +895,18 @@ int launch_wgrad_halo(const WgradHaloParams &p0, int grid) {
     return kOk;
 }
 
-template <bool C1>
-int launch_conv_bwd_fused(const ConvLayer &L, const float *x0) {
-    using S = tc::ConvBwdFusedShape<32, 64, 3, C1>;
-    auto kern = tc::conv_bwd_fused_kernel<32, 64, 3, C1>;
+template <bool C1, bool UP>
+int launch_conv_bwd_fused(const ConvLayer &L, const float *x0, const bf16 *dp) {
+    using S = tc::ConvBwdFusedShape<32, 64, 3, C1, UP>;
+    auto kern = tc::conv_bwd_fused_kernel<32, 64, 3, C1, UP>;
     ConvBwdFusedParams p = L.fbwd;
     p.region = S::region(p.R, p.Wp);
+    p.dy_region = S::dy_region(p.R, p.Wp);
+    p.x_off = S::x_off(p.R, p.Wp);
     p.stage_bytes = S::stage_bytes(p.R, p.Wp);
+    p.dp = dp;
+    if (UP && (!dp || !p.code || !p.bias_partial || p.R != 4 || p.H % 2 || p.W % 2 || 4 * (p.W / 2) * 8 > 512))
+        return fail(kBadArg, "conv_bwd_fused: unpool inputs not set up");
     p.out_tile_bytes = S::out_tile_bytes(p.R, p.W);
     p.x9_bytes = S::x9_bytes(p.R, p.W);
     p.x0 = x0;
@@ -913,13 +920,15 @@ int launch_conv_bwd_fused(const ConvLayer &L, const float *x0) {
             return check_cuda("conv_bwd_fused smem attribute");
         attr = smem;
     }
-    kern<<<L.fbwd_grid, 320, smem, stream()>>>(p);
+    kern<<<L.fbwd_grid, S::THREADS, smem, stream()>>>(p);
     ZB_LAUNCH_CHECK("conv_bwd_fused");
     return kOk;
 }
 
-int run_conv_bwd_fused(const ConvLayer &L, const float *x0) {
-    return L.fbwd_c1 ? launch_conv_bwd_fused<true>(L, x0) : launch_conv_bwd_fused<false>(L, nullptr);
+int run_conv_bwd_fused(const ConvLayer &L, const float *x0, const bf16 *dp) {
+    if (L.fbwd_c1)
+        return L.fbwd_up ? launch_conv_bwd_fused<true, true>(L, x0, dp) : launch_conv_bwd_fused<true, false>(L, x0, nullptr);
+    return L.fbwd_up ? launch_conv_bwd_fused<false, true>(L, nullptr, dp) : launch_conv_bwd_fused<false, false>(L, nullptr, nullptr);
 }
 
 int run_wgrad_halo(const ConvLayer &L) {
@@ -1133,6 +1142,14 @@ int tc_build(Net &n, TcEngine &e) {
             L.fbwd_c1 = !e.c1_pool && e.C1 == L.CIN && e.pad1 == 1 && e.H1 == e.H0 && e.W1 == e.W0 &&
                         (f.R * f.W) % 16 == 0;
             e.c1_fused = L.fbwd_c1;
+            // dY = max-unpool of the pooled gradient: built from dP and the codes inside the
+            // kernel (even H and W, even tile rows; 4 pooled rows x W/2 x 8 octets <= 512 items)
+            L.fbwd_up = L.H % 2 == 0 && L.W % 2 == 0 && f.R % 2 == 0 && f.R == 4 && 4 * (L.W / 2) * 8 <= 512;
+            if (L.fbwd_up) {
+                if ((rc = dalloc(e, &L.fbwd_bias_partial, (size_t)L.fbwd_grid * 4 * L.COUT))) return rc;
+                f.code = L.code;
+                f.bias_partial = L.fbwd_bias_partial;
+            }
         }
         L.wg_halo = !L.fused_bwd && L.halo && L.CIN == 32 && L.COUT == 64;
         if (L.wg_halo) {
@@ -1296,7 +1313,7 @@ int tc_build(Net &n, TcEngine &e) {
         e.views.push_back({pre + ".out", L.out, np, 0});
         e.views.push_back({pre + ".code", L.code, np, 1});
         e.views.push_back({pre + ".dP", L.dP, np, 0});
-        e.views.push_back({pre + ".dC", L.dC, (size_t)B * L.H * L.W * L.COUT, 0});
+        if (!L.fbwd_up) e.views.push_back({pre + ".dC", L.dC, (size_t)B * L.H * L.W * L.COUT, 0});
         e.views.push_back({pre + ".wf", L.wf, (size_t)9 * L.CIN * L.COUT, 0});
         e.views.push_back({pre + ".wd", L.wd, (size_t)9 * L.CIN * L.COUT, 0});
     }
@@ -1401,21 +1418,26 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
         ConvLayer &L = e.convs[li];
         const Stage &s = st[L.si];
         const bf16 *dP = (li == (int)e.convs.size() - 1) ? dpooled : L.dP;
-        const int G = L.COUT / 8, slots = 256 / G;
-        unpool_kernel<<<L.unpool_grid, slots * G, slots * G * 8 * sizeof(float), stream()>>>(
-            dP, L.code, L.dC, L.bias_partial, B, L.H, L.W, L.COUT);
-        ZB_LAUNCH_CHECK("unpool");
-        {
+        if (!(L.fused_bwd && L.fbwd_up)) {
+            const int G = L.COUT / 8, slots = 256 / G;
+            unpool_kernel<<<L.unpool_grid, slots * G, slots * G * 8 * sizeof(float), stream()>>>(
+                dP, L.code, L.dC, L.bias_partial, B, L.H, L.W, L.COUT);
+            ZB_LAUNCH_CHECK("unpool");
             ReduceArgs r{L.bias_partial, L.unpool_grid, (long long)L.COUT, 0, 1, L.COUT, 0, 0, 0, 0,
                          n.grads + s.poff + s.pn_w, nullptr, nullptr};
             if ((rc = reduce(r))) return rc;
+            prof_mark(n, "pool_bwd");
         }
-        prof_mark(n, "pool_bwd");
         if (L.fused_bwd) {
-            if ((rc = run_conv_bwd_fused(L, x))) return rc;
+            if ((rc = run_conv_bwd_fused(L, x, dP))) return rc;
             ReduceArgs r{L.fbwd_partial, L.fbwd_grid, (long long)L.COUT * 9 * L.CIN, 1, L.COUT, 9 * L.CIN,
                          L.CIN, 0, 0, 0, n.grads + s.poff, nullptr, nullptr};
             if ((rc = reduce(r))) return rc;
+            if (L.fbwd_up) {
+                ReduceArgs rb{L.fbwd_bias_partial, 4 * L.fbwd_grid, (long long)L.COUT, 0, 1, L.COUT, 0, 0, 0, 0,
+                              n.grads + s.poff + s.pn_w, nullptr, nullptr};
+                if ((rc = reduce(rb))) return rc;
+            }
             if (L.fbwd_c1) {
                 ReduceArgs r1{e.c1_partial, e.c1_wgrad_grid, (long long)e.C1 * 10, 5, e.C1, 10, 0, 0, 0, 0,
                               n.grads + s1.poff, n.grads + s1.poff + s1.pn_w, nullptr};

@@ -237,12 +237,11 @@ def tc_work(w: configs.Workload, b: int) -> list[dict]:
 # kernels have no cross-sample reuse, so a launch's traffic scales with its
 # sample count.
 NCU_DRAM_BYTES_PER_SAMPLE = {
-    "conv2 fwd": (102.861056e6 + 39.156736e6) / 2048,
-    "conv3 fwd": (51.557632e6 + 5.623296e6) / 2048,
-    "conv3 dX": (102.938112e6 + 22.401024e6) / 2048,
-    "conv2 dX": (308.345344e6 + 84.106496e6) / 2048,
+    "conv2 fwd": (102.822912e6 + 39.685632e6) / 2048,
+    "conv3 fwd": (51.557376e6 + 4.843264e6) / 2048,
+    "conv3 dX": (102.936064e6 + 24.424704e6) / 2048,
     "conv3 dW": (154.178048e6 + 4.386560e6) / 2048,
-    "conv2 dW": (308.313856e6 + 5.590528e6) / 2048,
+    "unpool2+conv2 dX+dW, conv1 dW": (186.347264e6 + 3.699712e6) / 2048,
 }
 
 

@@ -137,6 +137,14 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, const void 
         : "memory");
 }
 
+// Untiled bulk copy shared -> global (no multicast): both addresses 16-byte
+// aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_store(void *gdst, const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(src)),
+                 "r"(bytes)
+                 : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Waits until at most N committed bulk groups of this thread still read shared memory.
@@ -259,6 +267,13 @@ __device__ __forceinline__ uint32_t bias_relu_bf16x2(float a, float b, float ba,
     asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(s));
     uint32_t d;
     asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+
+// relu(a), relu(b) rounded to bf16 and packed, a in the low half.
+__device__ __forceinline__ uint32_t relu_bf16x2(float a, float b) {
+    uint32_t d;
+    asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(b), "f"(a));
     return d;
 }
 

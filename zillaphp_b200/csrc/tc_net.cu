@@ -27,6 +27,7 @@
 #include "tc_wgrad.cuh"
 #include "tc_wgrad_halo.cuh"
 #include "tc_conv_bwd_fused.cuh"
+#include "tc_conv_first.cuh"
 
 namespace zb {
 
@@ -1358,7 +1359,14 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
         if ((e.H0 + 2 * e.pad1) * (e.W0 + 2 * e.pad1) > kStageRegs * 256)
             return fail(kBadArg, "tc engine: first-conv image too large (padded %d x %d)", e.H0 + 2 * e.pad1,
                         e.W0 + 2 * e.pad1);
-        if (e.C1 == 32 && !e.c1_pool) conv_first_fwd_img_kernel<32><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
+        const bool same = e.pad1 == 1 && e.H1 == e.H0 && e.W1 == e.W0;   // 3x3, pad 1
+        if (e.C1 == 32 && !e.c1_pool && same) {
+            // tensor cores: one 128 x 32 x 32 MMA per 128 output pixels
+            const long long tiles = (pix + 127) / 128;
+            const int g = tiles < (long long)sm_count() * 8 ? (int)tiles : sm_count() * 8;
+            tc::conv_first_tc_kernel<32><<<g, 128, tc::ConvFirstTcShape<32>::SMEM, stream()>>>(
+                x, w1, b1, e.a1, B, e.H0, e.W0, device_error_word());
+        } else if (e.C1 == 32 && !e.c1_pool) conv_first_fwd_img_kernel<32><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
         else if (e.C1 == 32) conv_first_fwd_kernel<32, true><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
         else if (!e.c1_pool) conv_first_fwd_img_kernel<16><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
         else conv_first_fwd_kernel<16, true><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);

@@ -197,8 +197,13 @@ def tc_work(w: configs.Workload, b: int) -> list[dict]:
     for k in range(len(convs) - 1, -1, -1):
         a, o, ih, iw, oh, ow, pool = convs[k]
         if k > 0:
-            # the 32 -> 64 fused backward builds dY from the pooled gradient and the codes itself
-            up = (a, o) == (32, 64) and k == 1 and not pool0 and iw + 2 <= 32 and pool and oh % 2 == 0 and ow % 2 == 0
+            # the 32 -> 64 fused backward, and the 64 -> 128 input- and weight-gradient kernels on
+            # halo tiles, build dY from the pooled gradient and the codes themselves
+            r = (128 // ow) & ~1
+            up = pool and oh % 2 == 0 and ow % 2 == 0 and (
+                ((a, o) == (32, 64) and k == 1 and not pool0 and iw + 2 <= 32) or
+                ((a, o) == (64, 128) and r >= 2 and r * (ow + 2) <= 128 and r * ow <= 128
+                 and (r // 2 + 2) * (ow // 2) * 8 <= 512))
             if not up:
                 out.append({"label": "pool_bwd", "flops": 0,
                             "bytes": b * ((oh // 2) * (ow // 2) * o * 3 + oh * ow * o * 2), "name": f"unpool{k + 1}"})
@@ -216,12 +221,15 @@ def tc_work(w: configs.Workload, b: int) -> list[dict]:
                 out.append({"label": "conv_bwd", "flops": 2 * f,
                             "bytes": b * (oh * ow * o * 2 + ih * iw * a * 2 * 2), "name": f"conv{k + 1} dX+dW"})
                 continue
-            # input gradient: reads dY, writes dX (plus the ReLU mask of conv1's output for conv2)
+            # input gradient: reads dY (or the pooled dY and its codes), writes dX (plus the
+            # ReLU mask of conv1's output for conv2)
+            dy_bytes = (oh // 2) * (ow // 2) * o * 3 if up else oh * ow * o * 2
+            pre = f"unpool{k + 1}+" if up else ""
             out.append({"label": "conv_dgrad", "flops": f,
-                        "bytes": b * (oh * ow * o * 2 + ih * iw * a * 2 * (2 if k == 1 else 1)),
-                        "name": f"conv{k + 1} dX"})
-            out.append({"label": "conv_wgrad", "flops": f, "bytes": b * (oh * ow * o * 2 + ih * iw * a * 2),
-                        "name": f"conv{k + 1} dW"})
+                        "bytes": b * (dy_bytes + ih * iw * a * 2 * (2 if k == 1 else 1)),
+                        "name": f"{pre}conv{k + 1} dX"})
+            out.append({"label": "conv_wgrad", "flops": f, "bytes": b * (dy_bytes + ih * iw * a * 2),
+                        "name": f"{pre}conv{k + 1} dW"})
         else:
             out.append({"label": "conv_wgrad", "flops": 2 * b * oh * ow * o * a * 9,
                         "bytes": b * (oh * ow * o * 2 + ih * iw * 4), "name": "conv1 dW"})

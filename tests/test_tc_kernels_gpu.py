@@ -124,7 +124,8 @@ def test_conv_backward(step):
     code3 = v["conv3.code"].reshape(B, 7, 7, 128).astype(np.int64)
     code2 = v["conv2.code"].reshape(B, 14, 14, 64).astype(np.int64)
     dC3 = unpool(v["flat.d"].reshape(B, 7, 7, 128), code3, 14, 14)
-    assert np.array_equal(v["conv3.dC"].reshape(B, 14, 14, 128), dC3), "unpool3 routing"
+    if "conv3.dC" in v:   # else conv3's backward kernels build dC3 on chip from dP3 and the codes
+        assert np.array_equal(v["conv3.dC"].reshape(B, 14, 14, 128), dC3), "unpool3 routing"
     check("db conv3", grd["b5"], dC3.sum((0, 1, 2)), 2e-3)
     check("conv3 dX (bf16)", v["conv2.dP"].reshape(B, 14, 14, 64), conv_dgrad(dC3, bf16(par["W5"])), 1e-2)
     check("conv3 dW", grd["W5"], conv_wgrad(p2, dC3), 2e-3)

@@ -45,6 +45,18 @@
 //              (window position 0..3 | (max > 0) << 2).
 //   kEpiStore: relu(acc + bias) -> bf16 NHWC.
 //   kEpiDgrad: acc [* (mask > 0)] -> bf16 NHWC.
+//
+// UP (input gradient whose dY is the max-unpool of a pooled gradient dP
+// [B, H/2, W/2, CIN] by the pool codes): four more warps (10-13) build each
+// stage's halo octets from dP and the codes instead of a TMA load of dY (the
+// same construction as the fused conv2 backward: one 16-byte dP load and one
+// 8-byte code load per (pooled row, pooled column, octet) item, the channel's
+// value at the window position its code names, zero at the other three; the
+// halo columns outside the image stay zero from the start).  The octet pitch
+// is the row block plus 16 bytes so a pixel's octets fall in different banks.
+// The builders also sum the routed values of the tile's own pooled rows: the
+// bias gradient of the conv whose dY this is, one [CIN] slice per builder
+// warp and CTA.
 #pragma once
 
 #include "tc_common.cuh"
@@ -63,6 +75,9 @@ struct ConvHaloParams {
     __nv_bfloat16 *out;         // pooled [B, H/2, W/2, COUT] or full [B, H, W, COUT]
     uint8_t *code;              // [B, H/2, W/2, COUT] (kEpiPool)
     const __nv_bfloat16 *mask;  // [B, H, W, COUT] or null (kEpiDgrad)
+    const __nv_bfloat16 *dp;    // UP: pooled gradient [B, H/2, W/2, CIN]
+    const uint8_t *up_code;     // UP: its pool codes
+    float *up_bias_partial;     // UP: [gridDim.x * 4][CIN]
     int *err;
 };
 
@@ -90,19 +105,23 @@ struct ConvHaloShape {
     // group pitch: HR rows of 16 B rounded to 128 B (TMA destination alignment)
     static __host__ __device__ int region(int HR) { return (HR * 16 + 127) / 128 * 128; }
     static __host__ __device__ int stage_bytes(int HR) { return (NC8 * region(HR) + 1023) / 1024 * 1024; }
+    // UP: octets written by threads, pitch + 16 bytes (no TMA alignment needed)
+    static __host__ __device__ int region_up(int HR) { return region(HR) + 16; }
+    static __host__ __device__ int stage_bytes_up(int HR) { return (NC8 * region_up(HR) + 1023) / 1024 * 1024; }
     // kEpiDgrad: staged output tiles for the TMA store (one or two buffers)
     static __host__ __device__ int out_tile_bytes(int R, int W) { return (R * W * COUT * 2 + 1023) / 1024 * 1024; }
-    static __host__ __device__ int smem(int HR, int out_total) {
+    // dynamic shared memory for stages of `stage` bytes (stage_bytes or stage_bytes_up)
+    static __host__ __device__ int smem(int stage, int out_total) {
         const int epi = POOL_STAGE > out_total ? POOL_STAGE : out_total;
-        return 1024 + BTOTAL + NS * stage_bytes(HR) + SLACK + epi + BIAS_BYTES + BAR_BYTES;
+        return 1024 + BTOTAL + NS * stage + SLACK + epi + BIAS_BYTES + BAR_BYTES;
     }
     static_assert(CIN % 16 == 0 && SC % 16 == 0 && COUT % 32 == 0 && COUT <= 256, "unsupported conv channels");
     static_assert(CIN <= 64 || CIN % 64 == 0, "CIN above 64 must be a multiple of 64");
     static_assert(SC % CHUNK == 0 || CHUNK % SC == 0, "stage channels and weight chunks must nest");
 };
 
-template <int CIN, int COUT, int EPI, int NS, int KS, int OB = 2>
-__global__ void __launch_bounds__(320, 2) conv_halo_kernel(const __grid_constant__ ConvHaloParams p) {
+template <int CIN, int COUT, int EPI, int NS, int KS, int OB = 2, bool UP = false>
+__global__ void __launch_bounds__(UP ? 448 : 320, UP ? 1 : 2) conv_halo_kernel(const __grid_constant__ ConvHaloParams p) {
     using S = ConvHaloShape<CIN, COUT, NS, KS, EPI == kEpiPool>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -136,7 +155,8 @@ __global__ void __launch_bounds__(320, 2) conv_halo_kernel(const __grid_constant
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < NS; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); armed[i] = 0; }
+        // full: the TMA transaction arrival, or one arrival per builder warp (UP)
+        for (int i = 0; i < NS; ++i) { mbar_init(&full[i], UP ? 4 : 1); mbar_init(&empty[i], 1); armed[i] = 0; }
         for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 8); }
         mbar_init(wbar, 1);
         mbar_init(drain, 1);
@@ -152,7 +172,7 @@ __global__ void __launch_bounds__(320, 2) conv_halo_kernel(const __grid_constant
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (elect_one()) {
-            prefetch_tmap(&p.in_map);
+            if (!UP) prefetch_tmap(&p.in_map);
             prefetch_tmap(&p.w_map);
             if (EPI == kEpiDgrad) prefetch_tmap(&p.out_map);
             mbar_arrive_expect_tx(wbar, S::BTOTAL);
@@ -162,7 +182,7 @@ __global__ void __launch_bounds__(320, 2) conv_halo_kernel(const __grid_constant
             const uint32_t stage_tx = (uint32_t)(S::NC8 * p.HR * 16);
             int s = 0;
             uint32_t ph = 0;
-            for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
+            for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag && !UP; tile += gridDim.x) {
                 const int b = tile / p.tiles_per_img;
                 const int h0 = (tile - b * p.tiles_per_img) * p.R;
                 for (int kb = 0; kb < KS; ++kb) {
@@ -232,6 +252,103 @@ __global__ void __launch_bounds__(320, 2) conv_halo_kernel(const __grid_constant
             if (issued) {   // wait for every MMA this thread issued before TMEM is freed
                 mma_commit(drain);
                 if (!mbar_wait_drain(drain, 0)) atomicCAS(p.err, 0, kErrDrain);
+            }
+        }
+    } else if (UP && warp >= 10) {
+        // ------------------------------------------------ dY builders (warps 10..13, UP)
+        const int bt = threadIdx.x - 320;   // 0..127
+        const int g = bt & (S::NC8 - 1);    // octet (within a stage) of every item of this thread
+        const int Ho = p.H >> 1, Wo = p.W >> 1;
+        const int PR = (p.R >> 1) + 2;      // pooled rows covering the R + 2 halo rows
+        const int nitems = PR * Wo * S::NC8;
+        float bsum[KS][8];
+#pragma unroll
+        for (int kb = 0; kb < KS; ++kb)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) bsum[kb][e] = 0.0f;
+        // this thread's dP and code loads of stage kb of `tile` (zero past the image / the tiles)
+        auto load_stage = [&](int tile, int kb, uint4 (&pv)[4], uint2 (&cd)[4]) {
+            const int b = tile / p.tiles_per_img;
+            const int h0 = (tile - b * p.tiles_per_img) * p.R;
+            const int ch = (kb * S::NC8 + g) * 8;
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const int i = bt + 128 * m;
+                const int wi = i / S::NC8, prow = wi / Wo, pw = wi - prow * Wo;
+                const int phr = (h0 >> 1) - 1 + prow;
+                pv[m] = make_uint4(0, 0, 0, 0);
+                cd[m] = make_uint2(0, 0);
+                if (tile < p.num_tiles && i < nitems && (unsigned)phr < (unsigned)Ho) {
+                    const size_t o = (((size_t)b * Ho + phr) * Wo + pw) * CIN + ch;
+                    pv[m] = __ldg(reinterpret_cast<const uint4 *>(p.dp + o));
+                    cd[m] = __ldg(reinterpret_cast<const uint2 *>(p.up_code + o));
+                }
+            }
+        };
+        int s = 0;
+        uint32_t ph = 0;
+        uint4 pv[4], pvn[4];
+        uint2 cd[4], cdn[4];
+        load_stage(blockIdx.x, 0, pv, cd);
+        for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
+#pragma unroll
+            for (int kb = 0; kb < KS; ++kb) {
+                // the next stage's loads go out first: their latency overlaps this stage
+                if (kb + 1 < KS) load_stage(tile, kb + 1, pvn, cdn);
+                else load_stage(tile + gridDim.x, 0, pvn, cdn);
+                if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err, kErrEmptyWait)) break;
+                uint8_t *st = sA + s * STAGE + g * p.region;
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    const int i = bt + 128 * m;
+                    if (i >= nitems) continue;
+                    const int wi = i / S::NC8, prow = wi / Wo, pw = wi - prow * Wo;
+                    const uint32_t t0 = cd[m].x | (cd[m].x >> 4), t1 = cd[m].y | (cd[m].y >> 4);
+                    const uint32_t sel0 = (t0 & 0xFFu) | ((t0 >> 8) & 0xFF00u);
+                    const uint32_t sel1 = (t1 & 0xFFu) | ((t1 >> 8) & 0xFF00u);
+                    const int hr0 = 2 * prow - 1;   // halo row of the window's top image row
+#pragma unroll
+                    for (int kh = 0; kh < 2; ++kh) {
+                        const int hr = hr0 + kh;
+                        if (hr < 0 || hr > p.R + 1) continue;
+                        uint8_t *rowp = st + (hr * p.Wp + 2 * pw + 1) * 16;
+#pragma unroll
+                        for (int kw = 0; kw < 2; ++kw)
+                            *reinterpret_cast<uint4 *>(rowp + kw * 16) =
+                                unpool_select(pv[m], sel0, sel1, 0xFFu << (8 * (2 * kh + kw)));
+                    }
+                    if (prow >= 1 && prow <= (p.R >> 1)) {   // the tile's own pooled rows
+                        const uint4 r4 = unpool_select(pv[m], sel0, sel1, 0xFFFFFFFFu);
+                        const uint32_t w[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            bsum[kb][2 * e] += __uint_as_float(w[e] << 16);
+                            bsum[kb][2 * e + 1] += __uint_as_float(w[e] & 0xFFFF0000u);
+                        }
+                    }
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[s]);
+                if (++s == NS) { s = 0; ph ^= 1u; }
+#pragma unroll
+                for (int m = 0; m < 4; ++m) { pv[m] = pvn[m]; cd[m] = cdn[m]; }
+            }
+        }
+        // bias-gradient partial: the lanes of each octet in a fixed order, one slice per warp
+#pragma unroll
+        for (int kb = 0; kb < KS; ++kb)
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+                for (int off = S::NC8; off < 32; off <<= 1)
+                    bsum[kb][e] += __shfl_xor_sync(0xffffffffu, bsum[kb][e], off);
+        if (lane < S::NC8) {
+            float *bp = p.up_bias_partial + ((size_t)blockIdx.x * 4 + (warp - 10)) * CIN;
+#pragma unroll
+            for (int kb = 0; kb < KS; ++kb) {
+                float4 *d4 = reinterpret_cast<float4 *>(bp + (kb * S::NC8 + lane) * 8);
+                d4[0] = make_float4(bsum[kb][0], bsum[kb][1], bsum[kb][2], bsum[kb][3]);
+                d4[1] = make_float4(bsum[kb][4], bsum[kb][5], bsum[kb][6], bsum[kb][7]);
             }
         }
     } else {

@@ -737,6 +737,9 @@ struct ConvLayer {   // a tensor-core conv stage (conv + ReLU + pool)
     bool fbwd_c1 = false;                // the first conv's weight gradient taken in the same kernel
     bool fbwd_up = false;                // dY built in the kernel from dP and the pool codes (no unpool)
     float *fbwd_bias_partial = nullptr;  // fbwd_up: [fbwd_grid * 4][COUT]
+    bool up = false;                     // conv3 path: dgrad + weight gradient build dY from dP and codes
+    int up_grid = 0;                     // up: CTAs of the input-gradient kernel
+    float *up_bias_partial = nullptr;    // up: [up_grid * 4][COUT]
     bool wg_halo = false;                // halo-tile weight gradient
     WgradHaloParams whalo{};
     int whalo_grid = 0;
@@ -826,15 +829,17 @@ bool conv_shape_supported(int cin, int cout) {
     return (cin == 32 && cout == 64) || (cin == 64 && cout == 128);
 }
 
-template <int CIN, int COUT, int EPI, int NS, int KS, int OB = 2>
-int launch_halo(const ConvHaloParams &p0) {
+template <int CIN, int COUT, int EPI, int NS, int KS, int OB = 2, bool UP = false>
+int launch_halo(const ConvHaloParams &p0, int up_grid = 0) {
     using S = tc::ConvHaloShape<CIN, COUT, NS, KS, EPI == tc::kEpiPool>;
-    auto kern = tc::conv_halo_kernel<CIN, COUT, EPI, NS, KS, OB>;
+    auto kern = tc::conv_halo_kernel<CIN, COUT, EPI, NS, KS, OB, UP>;
     ConvHaloParams p = p0;
-    p.region = S::region(p.HR);
-    p.stage_bytes = S::stage_bytes(p.HR);
+    p.region = UP ? S::region_up(p.HR) : S::region(p.HR);
+    p.stage_bytes = UP ? S::stage_bytes_up(p.HR) : S::stage_bytes(p.HR);
+    if (UP && (!p.dp || !p.up_code || !p.up_bias_partial || up_grid < 1))
+        return fail(kBadArg, "conv_halo: unpool inputs not set up");
     p.out_tile_bytes = EPI == tc::kEpiDgrad ? S::out_tile_bytes(p.R, p.W) : 0;
-    const int smem = S::smem(p.HR, OB * p.out_tile_bytes);
+    const int smem = S::smem(p.stage_bytes, OB * p.out_tile_bytes);
     if (smem > 227 * 1024) return fail(kBadArg, "conv_halo: %d bytes of shared memory needed", smem);
     static int attr = 0;
     if (attr < smem) {
@@ -848,8 +853,8 @@ int launch_halo(const ConvHaloParams &p0) {
     if (per_sm < 1) per_sm = 1;
     if (per_sm > 2) per_sm = 2;
     const int slots = sm_count() * per_sm;
-    const int grid = p.num_tiles < slots ? p.num_tiles : slots;
-    kern<<<grid, 320, smem, stream()>>>(p);
+    const int grid = UP ? up_grid : (p.num_tiles < slots ? p.num_tiles : slots);
+    kern<<<grid, UP ? 448 : 320, smem, stream()>>>(p);
     ZB_LAUNCH_CHECK("conv_halo");
     return kOk;
 }
@@ -864,8 +869,13 @@ int run_conv_fwd(const ConvLayer &L) {
     return fail(kBadArg, "tc engine: no forward conv kernel for %d->%d", L.CIN, L.COUT);
 }
 
-int run_conv_dgrad(const ConvLayer &L) {
+int run_conv_dgrad(const ConvLayer &L, const bf16 *dp) {
     // dgrad convolves dY (COUT channels) into CIN outputs
+    if (L.up) {   // dY built in the kernel from the pooled gradient and the codes
+        ConvHaloParams p = L.hdgrad;
+        p.dp = dp;
+        return launch_halo<128, 64, tc::kEpiDgrad, 3, 2, 1, true>(p, L.up_grid);
+    }
     if (L.halo) {
         if (L.CIN == 32 && L.COUT == 64) return launch_halo<64, 32, tc::kEpiDgrad, 2, 1, 2>(L.hdgrad);
         if (L.CIN == 64 && L.COUT == 128) return launch_halo<128, 64, tc::kEpiDgrad, 3, 2, 1>(L.hdgrad);
@@ -938,24 +948,31 @@ int run_wgrad_halo(const ConvLayer &L) {
     return fail(kBadArg, "tc engine: no halo weight-gradient kernel for %d->%d", L.CIN, L.COUT);
 }
 
-template <int MODE>
+template <int MODE, bool UP = false>
 int launch_wgrad(const WgradTcParams &p, int grid, int smem) {
-    auto kern = tc::wgrad_tc_kernel<MODE>;
+    auto kern = tc::wgrad_tc_kernel<MODE, UP>;
     static int attr = 0;
     if (attr < smem) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
             return check_cuda("wgrad_tc smem attribute");
         attr = smem;
     }
-    kern<<<grid, 192, smem, stream()>>>(p);
+    if (UP && (!p.dp || !p.up_code)) return fail(kBadArg, "wgrad_tc: unpool inputs not set up");
+    kern<<<grid, UP ? 320 : 192, smem, stream()>>>(p);
     ZB_LAUNCH_CHECK("wgrad_tc");
     return kOk;
 }
 
-int run_wgrad(const WgradTcParams &p, int mode, int grid, int smem) {
-    if (mode == tc::kWgLinear) return launch_wgrad<tc::kWgLinear>(p, grid, smem);
-    if (mode == tc::kWgConvCo) return launch_wgrad<tc::kWgConvCo>(p, grid, smem);
-    return launch_wgrad<tc::kWgConvTap>(p, grid, smem);
+// dp: the pooled gradient when the conv-co kernel builds dY itself (null: dY from the a map)
+int run_wgrad(const WgradTcParams &p0, int mode, int grid, int smem, const bf16 *dp = nullptr) {
+    if (mode == tc::kWgLinear) return launch_wgrad<tc::kWgLinear>(p0, grid, smem);
+    if (mode == tc::kWgConvCo) {
+        if (!dp) return launch_wgrad<tc::kWgConvCo>(p0, grid, smem);
+        WgradTcParams p = p0;
+        p.dp = dp;
+        return launch_wgrad<tc::kWgConvCo, true>(p, grid, smem);
+    }
+    return launch_wgrad<tc::kWgConvTap>(p0, grid, smem);
 }
 
 template <int BN, int EPI, int NS>
@@ -1195,6 +1212,17 @@ int tc_build(Net &n, TcEngine &e) {
         if (g.splits > B) g.splits = B;
         g.mode = L.wg_mode;
         L.wg_grid = g.m_tiles * g.splits;
+        // 64 -> 128 on halo tiles: both backward kernels build dY = unpool(dP, codes) themselves
+        // (even H, W and R; the builders' items fit 4 rounds of 128 threads)
+        L.up = L.halo && L.wg_mode == tc::kWgConvCo && L.H % 2 == 0 && L.W % 2 == 0 && L.R % 2 == 0 &&
+               L.R * L.W <= 128 && ((L.R / 2) + 2) * (L.W / 2) * 8 <= 512 && (L.R / 2) * (L.W / 2) * 16 <= 512;
+        if (L.up) {
+            L.up_grid = L.hdgrad.num_tiles < sm_count() ? L.hdgrad.num_tiles : sm_count();
+            if ((rc = dalloc(e, &L.up_bias_partial, (size_t)L.up_grid * 4 * L.COUT))) return rc;
+            L.hdgrad.up_code = L.code;
+            L.hdgrad.up_bias_partial = L.up_bias_partial;
+            g.up_code = L.code;
+        }
         if ((rc = dalloc(e, &L.wg_partial, (size_t)g.splits * g.M * g.N))) return rc;
         L.wg.partial = L.wg_partial;
         L.unpool_grid = sm_count() * 4;
@@ -1314,7 +1342,7 @@ int tc_build(Net &n, TcEngine &e) {
         e.views.push_back({pre + ".out", L.out, np, 0});
         e.views.push_back({pre + ".code", L.code, np, 1});
         e.views.push_back({pre + ".dP", L.dP, np, 0});
-        if (!L.fbwd_up) e.views.push_back({pre + ".dC", L.dC, (size_t)B * L.H * L.W * L.COUT, 0});
+        if (!L.fbwd_up && !L.up) e.views.push_back({pre + ".dC", L.dC, (size_t)B * L.H * L.W * L.COUT, 0});
         e.views.push_back({pre + ".wf", L.wf, (size_t)9 * L.CIN * L.COUT, 0});
         e.views.push_back({pre + ".wd", L.wd, (size_t)9 * L.CIN * L.COUT, 0});
     }
@@ -1426,7 +1454,7 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
         ConvLayer &L = e.convs[li];
         const Stage &s = st[L.si];
         const bf16 *dP = (li == (int)e.convs.size() - 1) ? dpooled : L.dP;
-        if (!(L.fused_bwd && L.fbwd_up)) {
+        if (!(L.fused_bwd && L.fbwd_up) && !L.up) {
             const int G = L.COUT / 8, slots = 256 / G;
             unpool_kernel<<<L.unpool_grid, slots * G, slots * G * 8 * sizeof(float), stream()>>>(
                 dP, L.code, L.dC, L.bias_partial, B, L.H, L.W, L.COUT);
@@ -1454,7 +1482,12 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
             prof_mark(n, "conv_bwd");
             continue;
         }
-        if ((rc = run_conv_dgrad(L))) return rc;
+        if ((rc = run_conv_dgrad(L, dP))) return rc;
+        if (L.up) {   // bias gradient from the dgrad kernel's builders
+            ReduceArgs rb{L.up_bias_partial, 4 * L.up_grid, (long long)L.COUT, 0, 1, L.COUT, 0, 0, 0, 0,
+                          n.grads + s.poff + s.pn_w, nullptr, nullptr};
+            if ((rc = reduce(rb))) return rc;
+        }
         prof_mark(n, "conv_dgrad");
         if (L.wg_halo) {
             if ((rc = run_wgrad_halo(L))) return rc;
@@ -1462,7 +1495,7 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
                          L.CIN, 0, 0, 0, n.grads + s.poff, nullptr, nullptr};
             if ((rc = reduce(r))) return rc;
         } else {
-            if ((rc = run_wgrad(L.wg, L.wg_mode, L.wg_grid, L.wg_smem))) return rc;
+            if ((rc = run_wgrad(L.wg, L.wg_mode, L.wg_grid, L.wg_smem, L.up ? dP : nullptr))) return rc;
             ReduceArgs r{L.wg_partial, L.wg.splits, (long long)L.wg.M * L.wg.N,
                          L.wg_mode == tc::kWgConvCo ? 1 : 2, L.wg.M, L.wg.N, L.CIN, 0, 0, 0,
                          n.grads + s.poff, nullptr, nullptr};

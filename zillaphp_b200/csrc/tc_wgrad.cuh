@@ -18,6 +18,15 @@
 //               all 9 taps, box {32, W, R, 1} (64-byte swizzle), M tiles of
 //               4 taps; B = dY NHWC box {64 (=COUT), W, R, 1}; three
 //               accumulators of 128 x 64.  Partial [split][M = 9*CIN][N = COUT].
+//
+// UP (kWgConvCo whose dY is the max-unpool of a pooled gradient dP
+// [B, H/2, W/2, COUT] by the pool codes): four more warps (6-9) write the two
+// A boxes of each stage from dP and the codes (one 16-byte dP load and one
+// 8-byte code load per (pooled pixel, octet) item, the channel's value at the
+// window position its code names, zero elsewhere; rows = the stage's R x W
+// pixels, 128 B each with the 128-byte swizzle the TMA box would have), so dY
+// never exists in global memory; TMA loads only the three X boxes.  R is even
+// and tiles start on even rows, so every window lies inside one stage.
 #pragma once
 
 #include "tc_common.cuh"
@@ -37,6 +46,8 @@ struct WgradTcParams {
     int H, W, R, tiles_per_img;   // conv geometry (K-stage = R rows of one image)
     int kstage_rows;      // rows (pixels) per K-stage, multiple of 16 after zero padding
     float *partial;       // [splits][M][N]
+    const __nv_bfloat16 *dp;   // UP: pooled gradient [B, H/2, W/2, COUT]
+    const uint8_t *up_code;    // UP: its pool codes
     int *err;
 };
 
@@ -65,8 +76,9 @@ __device__ __forceinline__ void store_row32(float *dst, const float (&v)[32], bo
         d4[q] = zero ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(192, 1) wgrad_tc_kernel(const __grid_constant__ WgradTcParams p) {
+template <int MODE, bool UP = false>
+__global__ void __launch_bounds__(UP ? 320 : 192, 1) wgrad_tc_kernel(const __grid_constant__ WgradTcParams p) {
+    static_assert(!UP || MODE == kWgConvCo, "UP builds the dY boxes of kWgConvCo");
     using S = WgradTcShape<MODE>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -102,7 +114,8 @@ __global__ void __launch_bounds__(192, 1) wgrad_tc_kernel(const __grid_constant_
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < S::NS; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); armed[i] = 0; }
+        // full: the TMA transaction arrival (+ one per builder warp, UP)
+        for (int i = 0; i < S::NS; ++i) { mbar_init(&full[i], UP ? 5 : 1); mbar_init(&empty[i], 1); armed[i] = 0; }
         mbar_init(acc_full, 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -135,8 +148,9 @@ __global__ void __launch_bounds__(192, 1) wgrad_tc_kernel(const __grid_constant_
                     const int img = k0 + st / p.tiles_per_img;
                     const int h0 = (st % p.tiles_per_img) * p.R;
                     if constexpr (MODE == kWgConvCo) {
-                        mbar_arrive_expect_tx(&full[s], 2 * abox_bytes + 3 * bbox_bytes);
-                        for (int j = 0; j < 2; ++j) tma_load_4d(sa + j * ABOX, &p.a_map, &full[s], j * 64, 0, h0, img);
+                        mbar_arrive_expect_tx(&full[s], (UP ? 0 : 2 * abox_bytes) + 3 * bbox_bytes);
+                        if (!UP)
+                            for (int j = 0; j < 2; ++j) tma_load_4d(sa + j * ABOX, &p.a_map, &full[s], j * 64, 0, h0, img);
                         for (int j = 0; j < 3; ++j) {
                             const int tap = mt * 3 + j, dh = tap / 3, dw = tap % 3;
                             tma_load_4d(sb + j * BBOX, &p.b_map, &full[s], 0, dw - 1, h0 + dh - 1, img);
@@ -197,6 +211,63 @@ __global__ void __launch_bounds__(192, 1) wgrad_tc_kernel(const __grid_constant_
                 mma_commit(drain);
                 if (!mbar_wait_drain(drain, 0)) atomicCAS(p.err, 0, kErrDrain);
             }
+        }
+    } else if (UP && warp >= 6) {
+        // ------------------------------------------------ dY builders (warps 6..9, UP)
+        const int bt = threadIdx.x - 192;   // 0..127
+        const int o = bt & 15;              // channel octet (of 16) of every item of this thread
+        const int Ho = p.H >> 1, Wo = p.W >> 1;
+        const int nitems = (p.R >> 1) * Wo * 16;
+        // this thread's dP and code loads of stage st (zero past the image)
+        auto load_stage = [&](int st, uint4 (&pv)[4], uint2 (&cd)[4]) {
+            const int img = k0 + st / p.tiles_per_img;
+            const int h0 = (st % p.tiles_per_img) * p.R;
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const int i = bt + 128 * m;
+                const int wi = i >> 4, prow = wi / Wo, pw = wi - prow * Wo;
+                const int phr = (h0 >> 1) + prow;
+                pv[m] = make_uint4(0, 0, 0, 0);
+                cd[m] = make_uint2(0, 0);
+                if (st < nstages && i < nitems && phr < Ho) {
+                    const size_t off = (((size_t)img * Ho + phr) * Wo + pw) * 128 + 8 * o;
+                    pv[m] = __ldg(reinterpret_cast<const uint4 *>(p.dp + off));
+                    cd[m] = __ldg(reinterpret_cast<const uint2 *>(p.up_code + off));
+                }
+            }
+        };
+        int s = 0;
+        uint32_t ph = 0;
+        uint4 pv[4], pvn[4];
+        uint2 cd[4], cdn[4];
+        load_stage(0, pv, cd);
+        for (int st = 0; st < nstages && !*abort_flag; ++st) {
+            load_stage(st + 1, pvn, cdn);   // one stage ahead: its latency overlaps this stage
+            if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err, kErrEmptyWait)) break;
+            uint8_t *sa = sbase + s * STAGE + (o >> 3) * ABOX;   // box of channels 64 (o / 8) ..
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const int i = bt + 128 * m;
+                if (i >= nitems) continue;
+                const int wi = i >> 4, prow = wi / Wo, pw = wi - prow * Wo;
+                const uint32_t t0 = cd[m].x | (cd[m].x >> 4), t1 = cd[m].y | (cd[m].y >> 4);
+                const uint32_t sel0 = (t0 & 0xFFu) | ((t0 >> 8) & 0xFF00u);
+                const uint32_t sel1 = (t1 & 0xFFu) | ((t1 >> 8) & 0xFF00u);
+#pragma unroll
+                for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+                    for (int kw = 0; kw < 2; ++kw) {
+                        const int k = (2 * prow + kh) * p.W + 2 * pw + kw;   // stage pixel row
+                        *reinterpret_cast<uint4 *>(sa + k * 128 + (((o & 7) ^ (k & 7)) << 4)) =
+                            unpool_select(pv[m], sel0, sel1, 0xFFu << (8 * (2 * kh + kw)));
+                    }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[s]);
+            if (++s == S::NS) { s = 0; ph ^= 1u; }
+#pragma unroll
+            for (int m = 0; m < 4; ++m) { pv[m] = pvn[m]; cd[m] = cdn[m]; }
         }
     } else {
         const int q = warp & 3;

@@ -31,6 +31,31 @@ float *ptr(int id);
 // Capacity in floats of a registry handle (0 if invalid).
 size_t capacity(int id);
 
+// Programmatic dependent launch.  A kernel started by launch_pdl may begin
+// while the previous kernel on the stream is still running: it calls
+// griddep_wait() before its first global-memory access (read or write; only
+// shared memory, mbarrier and TMEM set-up come before), and griddep_launch()
+// at its start so that the next kernel's blocks can be scheduled, and run
+// their own set-up, as soon as SM resources free up.  Both are no-ops in a
+// kernel launched without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream();
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Grid size helper: enough blocks to cover n with `threads` each, capped to
 // a multiple of the SM count x `per_sm` (grid-stride loops cover the rest).
 int grid_for(long long n, int threads, int per_sm = 8);

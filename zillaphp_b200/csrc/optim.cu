@@ -22,6 +22,8 @@ __device__ __forceinline__ void adam_one(float &w, float g, float &m, float &v, 
 
 __global__ void adam_kernel(float *__restrict__ w, const float *__restrict__ g,
                             float *__restrict__ m, float *__restrict__ v, long long n, AdamArgs a) {
+    griddep_launch();
+    griddep_wait();
     const long long stride = (long long)gridDim.x * blockDim.x;
     const long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const bool vec = ((((uintptr_t)w) | ((uintptr_t)g) | ((uintptr_t)m) | ((uintptr_t)v)) & 15) == 0;
@@ -48,6 +50,8 @@ __global__ void adam_kernel(float *__restrict__ w, const float *__restrict__ g,
 
 __global__ void sgd_scaled_kernel(float *__restrict__ w, const float *__restrict__ g, float lr,
                                   float scale, long long n) {
+    griddep_launch();
+    griddep_wait();
     const long long stride = (long long)gridDim.x * blockDim.x;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
         w[i] = __fsub_rn(w[i], __fmul_rn(lr, __fmul_rn(g[i], scale)));   // as sgd_update_dev: no FMA
@@ -55,7 +59,7 @@ __global__ void sgd_scaled_kernel(float *__restrict__ w, const float *__restrict
 
 int launch_sgd(float *w, const float *g, float lr, float grad_scale, long long n) {
     if (n <= 0) return kOk;
-    sgd_scaled_kernel<<<grid_for(n, 256, 4), 256, 0, stream()>>>(w, g, lr, grad_scale, n);
+    launch_pdl(sgd_scaled_kernel, dim3(grid_for(n, 256, 4)), dim3(256), 0, w, g, lr, grad_scale, n);
     ZB_LAUNCH_CHECK("sgd_update");
     return kOk;
 }
@@ -76,7 +80,7 @@ AdamArgs make_adam_args(float lr, float b1, float b2, float eps, int t, float gr
 
 int launch_adam(float *w, const float *g, float *m, float *v, long long n, const AdamArgs &a) {
     if (n <= 0) return kOk;
-    adam_kernel<<<grid_for(n / 4 + 1, 256, 4), 256, 0, stream()>>>(w, g, m, v, n, a);
+    launch_pdl(adam_kernel, dim3(grid_for(n / 4 + 1, 256, 4)), dim3(256), 0, w, g, m, v, n, a);
     ZB_LAUNCH_CHECK("adam_update");
     return kOk;
 }

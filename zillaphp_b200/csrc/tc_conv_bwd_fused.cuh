@@ -109,6 +109,7 @@ struct ConvBwdFusedShape {
 
 template <int CX, int CY, int NS, bool C1 = false, bool UP = false>
 __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const __grid_constant__ ConvBwdFusedParams p) {
+    griddep_launch();
     using S = ConvBwdFusedShape<CX, CY, NS, C1, UP>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -157,6 +158,7 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    griddep_wait();   // everything below may touch global memory
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer

@@ -54,6 +54,8 @@ __global__ void __launch_bounds__(128, 8) conv_first_tc_kernel(const float *__re
                                                              __nv_bfloat16 *__restrict__ out, int B, int H, int W,
                                                              int *err) {
     using S = ConvFirstTcShape<CO>;
+    griddep_launch();
+    griddep_wait();
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *base = smem_raw + (((raw + 1023u) & ~1023u) - raw);

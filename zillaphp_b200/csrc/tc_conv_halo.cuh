@@ -122,6 +122,7 @@ struct ConvHaloShape {
 
 template <int CIN, int COUT, int EPI, int NS, int KS, int OB = 2, bool UP = false>
 __global__ void __launch_bounds__(UP ? 448 : 320, UP ? 1 : 2) conv_halo_kernel(const __grid_constant__ ConvHaloParams p) {
+    griddep_launch();
     using S = ConvHaloShape<CIN, COUT, NS, KS, EPI == kEpiPool>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -150,6 +151,7 @@ __global__ void __launch_bounds__(UP ? 448 : 320, UP ? 1 : 2) conv_halo_kernel(c
     // zeroed once so that the discarded accumulator rows stay finite.
     for (int i = threadIdx.x; i < (NS * STAGE + S::SLACK) / 16; i += blockDim.x)
         *reinterpret_cast<uint4 *>(sA + 16 * i) = make_uint4(0, 0, 0, 0);
+    griddep_wait();   // everything below may touch global memory
     if constexpr (EPI == kEpiPool)
         for (int i = threadIdx.x; i < COUT; i += blockDim.x) sbias[i] = p.bias[i];
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -45,6 +45,7 @@ struct GemmTcShape {
 
 template <int BN, int EPI, int NS>
 __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ GemmTcParams p) {
+    griddep_launch();
     using S = GemmTcShape<BN, NS>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -74,6 +75,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    griddep_wait();   // everything below may touch global memory
 
     if (warp == 0) {
         if (elect_one()) {

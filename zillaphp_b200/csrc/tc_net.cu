@@ -108,6 +108,8 @@ __device__ __forceinline__ int nhwc_to_nchw(int k, int C, int H, int W) {
 //   kind 0 (forward): dst[(t*COUT + co)*CIN + ci] = W[co][ci][t]
 //   kind 1 (dgrad)  : dst[(t*CIN + ci)*COUT + co] = W[co][ci][8 - t]   (flipped, transposed)
 __global__ void pack_kernel(PackJobs jobs) {
+    griddep_launch();
+    griddep_wait();
     for (int ji = 0; ji < jobs.count; ++ji) {
         const PackJob J = jobs.j[ji];
         const int n = (int)J.n;
@@ -134,6 +136,8 @@ __global__ void pack_kernel(PackJobs jobs) {
 __global__ void __launch_bounds__(256) pack_fc_kernel(const float *__restrict__ W, bf16 *__restrict__ wP,
                                                       bf16 *__restrict__ dst, int F, int N, int C, int H, int Wd) {
     __shared__ float tile[32][33];
+    griddep_launch();
+    griddep_wait();
     const int k0 = blockIdx.x * 32, n0 = blockIdx.y * 32;
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8
     for (int r = ty; r < 32; r += 8) {
@@ -509,6 +513,8 @@ __global__ void __launch_bounds__(256) head_kernel(const bf16 *__restrict__ a, c
     constexpr int KPL = HD / 32;   // inputs per lane
     __shared__ float sW[HD * NC];
     __shared__ float sAcc[HD * NC + NC + HD];
+    griddep_launch();
+    griddep_wait();
     for (int i = threadIdx.x; i < HD * NC; i += blockDim.x) sW[i] = Wt[i];
     for (int i = threadIdx.x; i < HD * NC + NC + HD; i += blockDim.x) sAcc[i] = 0.0f;
     __syncthreads();
@@ -611,6 +617,8 @@ __device__ void r_store(const ReduceArgs &r, long long i, float s);
 // l, l+8, l+16, ... in order (coalesced 128-byte rows), then lane sums are
 // combined in lane order: a fixed order, so the result is deterministic.
 __global__ void __launch_bounds__(256) reduce_partials_kernel(ReduceArgs r) {
+    griddep_launch();
+    griddep_wait();
     __shared__ float part[8][33];
     const int el = threadIdx.x & 31, sl = threadIdx.x >> 5;
     for (long long base = (long long)blockIdx.x * 32; base < r.n; base += (long long)gridDim.x * 32) {
@@ -635,6 +643,8 @@ __global__ void __launch_bounds__(256) reduce_partials_kernel(ReduceArgs r) {
 // lane l sums splits l, l+32, ... in order, then the 32 lane sums of each
 // element are added in lane order (fixed order: deterministic).
 __global__ void __launch_bounds__(256) reduce_deep_kernel(ReduceArgs r) {
+    griddep_launch();
+    griddep_wait();
     __shared__ float part[32][9];
     const int el = threadIdx.x & 7, sl = threadIdx.x >> 3;
     for (long long base = (long long)blockIdx.x * 8; base < r.n; base += (long long)gridDim.x * 8) {
@@ -663,6 +673,8 @@ __global__ void __launch_bounds__(256) reduce_deep_kernel(ReduceArgs r) {
 // Few splits of a long vector (the Linear weight gradient): each thread owns
 // 4 consecutive elements and adds the splits in order with 16-byte loads.
 __global__ void __launch_bounds__(256) reduce_wide_kernel(ReduceArgs r) {
+    griddep_launch();
+    griddep_wait();
     const long long n4 = r.n >> 2;
     for (long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x; q < n4;
          q += (long long)gridDim.x * blockDim.x) {
@@ -700,6 +712,8 @@ __device__ void r_store(const ReduceArgs &r, long long i, float s) {
 }
 
 __global__ void loss_sum_kernel(const double *__restrict__ row_loss, int B, float *__restrict__ loss) {
+    griddep_launch();
+    griddep_wait();
     __shared__ double part[256];
     const int per = (B + blockDim.x - 1) / blockDim.x;
     const int b0 = threadIdx.x * per, b1 = min(B, b0 + per);
@@ -854,7 +868,7 @@ int launch_halo(const ConvHaloParams &p0, int up_grid = 0) {
     if (per_sm > 2) per_sm = 2;
     const int slots = sm_count() * per_sm;
     const int grid = UP ? up_grid : (p.num_tiles < slots ? p.num_tiles : slots);
-    kern<<<grid, UP ? 448 : 320, smem, stream()>>>(p);
+    launch_pdl(kern, dim3(grid), dim3(UP ? 448 : 320), smem, p);
     ZB_LAUNCH_CHECK("conv_halo");
     return kOk;
 }
@@ -931,7 +945,7 @@ int launch_conv_bwd_fused(const ConvLayer &L, const float *x0, const bf16 *dp) {
             return check_cuda("conv_bwd_fused smem attribute");
         attr = smem;
     }
-    kern<<<L.fbwd_grid, S::THREADS, smem, stream()>>>(p);
+    launch_pdl(kern, dim3(L.fbwd_grid), dim3(S::THREADS), smem, p);
     ZB_LAUNCH_CHECK("conv_bwd_fused");
     return kOk;
 }
@@ -958,7 +972,7 @@ int launch_wgrad(const WgradTcParams &p, int grid, int smem) {
         attr = smem;
     }
     if (UP && (!p.dp || !p.up_code)) return fail(kBadArg, "wgrad_tc: unpool inputs not set up");
-    kern<<<grid, UP ? 320 : 192, smem, stream()>>>(p);
+    launch_pdl(kern, dim3(grid), dim3(UP ? 320 : 192), smem, p);
     ZB_LAUNCH_CHECK("wgrad_tc");
     return kOk;
 }
@@ -986,18 +1000,18 @@ int launch_gemm(const GemmTcParams &p) {
         attr = true;
     }
     const int tiles = p.m_tiles * p.n_tiles * p.ksplit;
-    kern<<<tiles < sm_count() ? tiles : sm_count(), 192, S::SMEM, stream()>>>(p);
+    launch_pdl(kern, dim3(tiles < sm_count() ? tiles : sm_count()), dim3(192), S::SMEM, p);
     ZB_LAUNCH_CHECK("gemm_tc");
     return kOk;
 }
 
 int reduce(const ReduceArgs &r) {
     if (r.splits >= 32 && r.n <= 131072) {
-        reduce_deep_kernel<<<grid_for(r.n, 8, 16), 256, 0, stream()>>>(r);            // 8 elements per block
+        launch_pdl(reduce_deep_kernel, dim3(grid_for(r.n, 8, 16)), dim3(256), 0, r);   // 8 elements per block
     } else if (r.n % 4 == 0 && r.n >= 65536 && r.splits <= 16) {
-        reduce_wide_kernel<<<grid_for(r.n / 4, 256, 8), 256, 0, stream()>>>(r);
+        launch_pdl(reduce_wide_kernel, dim3(grid_for(r.n / 4, 256, 8)), dim3(256), 0, r);
     } else {
-        reduce_partials_kernel<<<grid_for(r.n, 32, 8), 256, 0, stream()>>>(r);       // 32 elements per block
+        launch_pdl(reduce_partials_kernel, dim3(grid_for(r.n, 32, 8)), dim3(256), 0, r);   // 32 elements per block
     }
     ZB_LAUNCH_CHECK("reduce_partials");
     return kOk;
@@ -1367,12 +1381,12 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
     auto &st = n.st;
     int rc;
     // ---- pack bf16 operands from the fp32 master
-    pack_kernel<<<sm_count(), 256, 0, stream()>>>(e.pack);
+    launch_pdl(pack_kernel, dim3(sm_count()), dim3(256), 0, e.pack);
     ZB_LAUNCH_CHECK("pack");
     {
         const float *W4 = n.params + st[e.hid_si].poff;
-        pack_fc_kernel<<<dim3((e.F + 31) / 32, (e.HD + 31) / 32), 256, 0, stream()>>>(
-            W4, e.wP, e.wT, e.F, e.HD, e.fC, e.fH, e.fW);
+        launch_pdl(pack_fc_kernel, dim3((e.F + 31) / 32, (e.HD + 31) / 32), dim3(256), 0, W4, e.wP, e.wT, e.F, e.HD,
+                   e.fC, e.fH, e.fW);
         ZB_LAUNCH_CHECK("pack transpose");
     }
     prof_mark(n, "pack");
@@ -1392,8 +1406,8 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
             // tensor cores: one 128 x 32 x 32 MMA per 128 output pixels
             const long long tiles = (pix + 127) / 128;
             const int g = tiles < (long long)sm_count() * 8 ? (int)tiles : sm_count() * 8;
-            tc::conv_first_tc_kernel<32><<<g, 128, tc::ConvFirstTcShape<32>::SMEM, stream()>>>(
-                x, w1, b1, e.a1, B, e.H0, e.W0, device_error_word());
+            launch_pdl(tc::conv_first_tc_kernel<32>, dim3(g), dim3(128), tc::ConvFirstTcShape<32>::SMEM, x, w1, b1,
+                       e.a1, B, e.H0, e.W0, device_error_word());
         } else if (e.C1 == 32 && !e.c1_pool) conv_first_fwd_img_kernel<32><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
         else if (e.C1 == 32) conv_first_fwd_kernel<32, true><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
         else if (!e.c1_pool) conv_first_fwd_img_kernel<16><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
@@ -1419,10 +1433,10 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
     float *gW5 = n.grads + sh.poff, *gb5 = gW5 + sh.pn_w;
     const Stage &sd = st[e.hid_si];
     float *gW4 = n.grads + sd.poff, *gb4 = gW4 + sd.pn_w;
-    head_kernel<256, 10><<<e.head_grid, 256, 0, stream()>>>(e.a_hid, n.params + sh.poff, n.params + sh.poff + sh.pn_w,
-                                                           y, e.dZ_hid, e.row_loss, e.head_partial, B, 1.0f / (float)B);
+    launch_pdl(head_kernel<256, 10>, dim3(e.head_grid), dim3(256), 0, e.a_hid, n.params + sh.poff,
+               n.params + sh.poff + sh.pn_w, y, e.dZ_hid, e.row_loss, e.head_partial, B, 1.0f / (float)B);
     ZB_LAUNCH_CHECK("head");
-    loss_sum_kernel<<<1, 256, 0, stream()>>>(e.row_loss, B, loss_out);
+    launch_pdl(loss_sum_kernel, dim3(1), dim3(256), 0, e.row_loss, B, loss_out);
     ZB_LAUNCH_CHECK("loss_sum");
     {
         ReduceArgs r{e.head_partial, e.head_grid, (long long)e.HD * e.NC + e.NC + e.HD, 4, e.HD, e.NC, 0, 0, 0, 0,

@@ -78,6 +78,7 @@ __device__ __forceinline__ void store_row32(float *dst, const float (&v)[32], bo
 
 template <int MODE, bool UP = false>
 __global__ void __launch_bounds__(UP ? 320 : 192, 1) wgrad_tc_kernel(const __grid_constant__ WgradTcParams p) {
+    griddep_launch();
     static_assert(!UP || MODE == kWgConvCo, "UP builds the dY boxes of kWgConvCo");
     using S = WgradTcShape<MODE>;
     extern __shared__ uint8_t smem_raw[];
@@ -126,6 +127,7 @@ __global__ void __launch_bounds__(UP ? 320 : 192, 1) wgrad_tc_kernel(const __gri
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    griddep_wait();   // everything below may touch global memory
 
     if (warp == 0) {
         if (elect_one()) {

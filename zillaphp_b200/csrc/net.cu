@@ -187,6 +187,7 @@ void dp_release_streams(Net &n) {
 void free_net(Net *n) {
     if (!n) return;
     cudaStreamSynchronize(stream());
+    peer_release(*n);   // peers' stores into this rank ended with the last step's wait
     if (n->tc) tc_destroy(*n);
     if (n->lm) lm_destroy(*n);
     for (auto &s : n->st) {
@@ -383,7 +384,7 @@ static int allreduce_range(Net &n, long long lo, long long hi) {
 }
 
 int dp_bucket_ready(Net &n, long long off) {
-    if (n.world <= 1 || n.ar_lo >= 0) return kOk;
+    if (n.world <= 1 || n.ar_lo >= 0 || n.peer.in_step) return kOk;
     n.ar_lo = off;
     return allreduce_range(n, off, n.nparams + 1);
 }
@@ -413,8 +414,12 @@ static int optimizer_step(Net &n) {
 }
 
 static int run_step(Net &n, const float *x, const float *y, int update) {
-    float *loss_slot = n.grads + n.nparams;
     int rc;
+    // data parallel over peer memory: this step's gradients go to an exchange
+    // buffer, and one kernel sums the rank's slice over NVLink and updates it
+    const bool peer = n.peer.on && update;
+    if (peer && (rc = peer_step_begin(n))) return rc;
+    float *loss_slot = n.grads + n.nparams;
     prof_mark(n, "start");
     if (n.lm) {
         rc = lm_step(n, x, y, loss_slot);
@@ -426,7 +431,16 @@ static int run_step(Net &n, const float *x, const float *y, int update) {
         if (!rc) prof_mark(n, "softmax_ce");
         if (!rc) rc = fp32_backward(n, x);
     }
-    if (rc) return rc;
+    if (rc) {
+        if (peer) n.grads = n.peer.api_grads, n.peer.in_step = false;
+        return rc;
+    }
+    if (peer) {
+        rc = peer_step_end(n);
+        if (!rc) prof_mark(n, "allreduce");
+        if (!rc) prof_mark(n, n.opt == 2 ? "adam" : "sgd");
+        return rc;
+    }
     rc = allreduce_grads(n);
     if (rc) return rc;
     if (n.world > 1) prof_mark(n, "allreduce");
@@ -637,7 +651,8 @@ int zilla_dp_attach(int id, int rank, int world, const unsigned char *id128) {
     }
     n->rank = rank;
     n->world = world;
-    return kOk;
+    peer_release(*n);          // a re-attach starts from the NCCL path
+    return peer_attach(*n);    // collective: maps the peers' buffers when every rank can
 #else
     (void)id128;
     return fail(kBadArg, "zilla_dp_attach: built without NCCL");
@@ -649,6 +664,8 @@ int zilla_dp_detach(int id) {
     if (!n) return fail(kBadHandle, "zilla_dp_detach: unknown net %d", id);
 #ifdef ZB_HAVE_NCCL
     if (n->comm) {
+        int rc = peer_detach(*n);   // collective, before the communicator goes
+        if (rc) return rc;
         cudaStreamSynchronize(stream());
         dp_release_streams(*n);
         ncclCommDestroy(n->comm);

@@ -33,6 +33,25 @@ struct Stage {
     int arg_id = 0;        // registry handle exported on request
 };
 
+// Data-parallel exchange over NVLink peer memory (peer.cu): the ranks map
+// each other's gradient exchange buffers, parameters and flag words through
+// CUDA IPC; each rank owns a contiguous slice of the parameters.
+constexpr int kMaxPeers = 8;
+struct PeerState {
+    bool on = false;                       // attached with peer memory (else NCCL all-reduce)
+    bool in_step = false;                  // a peer step is between begin and end
+    float *ex[2] = {nullptr, nullptr};     // this rank's exchange gradient buffers (step parity)
+    unsigned long long *flags = nullptr;   // this rank's flag block: [0] gradients final, [8] slice written
+    unsigned int *done = nullptr;          // completion counter of the update kernel (local)
+    float *api_grads = nullptr;            // the registry gradient buffer
+    float *rex[2][kMaxPeers] = {};         // every rank's exchange buffers (own included)
+    float *rparams[kMaxPeers] = {};        // every rank's parameters
+    unsigned long long *rflags[kMaxPeers] = {};
+    std::vector<void *> opened;            // IPC mappings to close
+    unsigned long long step = 0;           // peer steps taken
+    long long lo = 0, hi = 0, chunk = 0;   // owned slice [lo, hi); slices of `chunk` floats
+};
+
 struct TcEngine;  // bf16 tensor-core engine (tc_net.cu)
 struct LmEngine;  // Transformer language-model engine (lm_net.cu)
 
@@ -60,6 +79,7 @@ struct Net {
     cudaStream_t comm_stream = nullptr;        // all-reduce stream (data parallel)
     cudaEvent_t ev_ready = nullptr, ev_done = nullptr;
     long long ar_lo = -1;                      // grads [ar_lo, nparams] already launched this step
+    PeerState peer;
     TcEngine *tc = nullptr;
     LmEngine *lm = nullptr;
     long long x_floats = 0, y_floats = 0;   // per-step input sizes (floats)
@@ -95,5 +115,12 @@ int dp_bucket_ready(Net &n, long long off);
 int net_register(Net *n);             // assigns the id, returns it
 void net_free(Net *n);                // releases everything a Net holds
 int net_alloc_common(Net &n, long long classes_rows, long long rows);   // params, grads, Adam, staging
+// peer.cu: set-up after the NCCL communicator exists (collective; stays on NCCL
+// when a rank cannot map every peer), the step hooks, and the release
+int peer_attach(Net &n);
+int peer_detach(Net &n);                   // collective: gathers the Adam state slices first
+void peer_release(Net &n);                 // local: unmaps and frees
+int peer_step_begin(Net &n);               // gradients of this step go to the exchange buffer
+int peer_step_end(Net &n);                 // exchange + update + wait for every rank's slice
 
 }  // namespace zb

@@ -13,13 +13,6 @@
 
 namespace zb {
 
-__device__ __forceinline__ void adam_one(float &w, float g, float &m, float &v, const AdamArgs &a) {
-    g *= a.grad_scale;
-    m = a.b1 * m + a.one_minus_b1 * g;
-    v = a.b2 * v + a.one_minus_b2 * g * g;
-    w -= a.lr * (m * a.inv_bc1) / (sqrtf(v * a.inv_bc2) + a.eps);
-}
-
 __global__ void adam_kernel(float *__restrict__ w, const float *__restrict__ g,
                             float *__restrict__ m, float *__restrict__ v, long long n, AdamArgs a) {
     griddep_launch();

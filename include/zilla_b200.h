@@ -233,14 +233,23 @@ int zilla_net_device_status(int net);
  * held in shared memory).  Returns a net id > 0, or a negative status. */
 int zilla_lm_create(int vocab, int dim, int heads, int layers, int max_seq, int ffn, int batch, int seq);
 
-/* ---- data-parallel runner (one process per GPU, NCCL over NVLink) ----
+/* ---- data-parallel runner (one process per GPU, NVLink) ----
  * zilla_dp_unique_id writes a 128-byte NCCL unique id (rank 0 creates it,
  * the host distributes it, e.g. through a file or a store).
- * zilla_dp_attach joins `net` to a communicator of `world` ranks: each step
- * then sums the flat gradient buffer over ranks (one ncclAllReduce on the
- * library stream, the scalar loss riding in the same buffer) and scales by
- * 1/world before the identical optimizer update on every rank.  The per-rank
- * batch is the net's batch; the global batch is world * batch. */
+ * zilla_dp_attach (collective) joins `net` to a communicator of `world`
+ * ranks.  The per-rank batch is the net's batch; the global batch is world *
+ * batch; gradients are scaled by 1/world before the update.  Two paths:
+ *   bf16 engine, every GPU able to map every peer (ZB_PEER_STEP unset or not
+ *   "0"): each rank owns a slice of the flat parameters; one kernel per step
+ *   sums its slice of all ranks' gradients over NVLink peer memory, updates
+ *   it and stores it into every rank's parameters.  After a step the
+ *   parameters are identical on every rank, the loss slot holds the summed
+ *   loss, and the gradient buffer holds the summed gradient of the rank's
+ *   own slice only (the rest is this rank's local gradient).
+ *   otherwise: the flat gradient buffer is summed with ncclAllReduce (the
+ *   loss riding in it) and every rank runs the identical update.
+ * zilla_dp_detach (collective) leaves the communicator; after a peer-memory
+ * attach it first gives every rank the whole Adam state. */
 int zilla_dp_unique_id(unsigned char *id128);
 int zilla_dp_attach(int net, int rank, int world, const unsigned char *id128);
 int zilla_dp_detach(int net);

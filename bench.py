@@ -245,11 +245,12 @@ def tc_work(w: configs.Workload, b: int) -> list[dict]:
 # kernels have no cross-sample reuse, so a launch's traffic scales with its
 # sample count.
 NCU_DRAM_BYTES_PER_SAMPLE = {
-    "conv2 fwd": (102.822912e6 + 39.685632e6) / 2048,
-    "conv3 fwd": (51.557376e6 + 4.843264e6) / 2048,
-    "conv3 dX": (102.936064e6 + 24.424704e6) / 2048,
-    "conv3 dW": (154.178048e6 + 4.386560e6) / 2048,
-    "unpool2+conv2 dX+dW, conv1 dW": (186.347264e6 + 3.699712e6) / 2048,
+    "conv1 fwd": (6.447104e6 + 44.127488e6) / 2048,
+    "conv2 fwd": (102.839040e6 + 40.105216e6) / 2048,
+    "conv3 fwd": (51.558912e6 + 7.517184e6) / 2048,
+    "unpool3+conv3 dX": (38.741504e6 + 8.715008e6) / 2048,
+    "unpool3+conv3 dW": (89.971456e6 + 3.796224e6) / 2048,
+    "unpool2+conv2 dX+dW, conv1 dW": (186.451712e6 + 4.156928e6) / 2048,
 }
 
 

@@ -504,7 +504,8 @@ __global__ void unpool_kernel(const bf16 *__restrict__ dP, const uint8_t *__rest
 // of the backward, one warp per row:
 //   z = a W + b;  loss_r = -log softmax(z)[y];  dz = (p - onehot)/B
 //   dA = dz W^T times (a > 0) (ReLU of the previous Linear) -> bf16
-// Block partials (fixed warp order): dW [Hd][NC], db [NC], dbPrev [Hd].
+// Block partials (fixed warp order): dW [Hd][NC], db [NC], dbPrev [Hd], and
+// the block's loss sum (one more element, summed by the same reduction).
 template <int HD, int NC>
 __global__ void __launch_bounds__(256) head_kernel(const bf16 *__restrict__ a, const float *__restrict__ Wt,
                                                    const float *__restrict__ bias, const float *__restrict__ y,
@@ -513,10 +514,13 @@ __global__ void __launch_bounds__(256) head_kernel(const bf16 *__restrict__ a, c
     constexpr int KPL = HD / 32;   // inputs per lane
     __shared__ float sW[HD * NC];
     __shared__ float sAcc[HD * NC + NC + HD];
+    __shared__ double sLoss;
     griddep_launch();
     griddep_wait();
     for (int i = threadIdx.x; i < HD * NC; i += blockDim.x) sW[i] = Wt[i];
     for (int i = threadIdx.x; i < HD * NC + NC + HD; i += blockDim.x) sAcc[i] = 0.0f;
+    if (threadIdx.x == 0) sLoss = 0.0;
+    double lsum = 0.0;   // lane 0: this warp's rows' loss
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float gW[KPL][NC], gB[NC], gP[KPL];
@@ -561,6 +565,7 @@ __global__ void __launch_bounds__(256) head_kernel(const bf16 *__restrict__ a, c
 #pragma unroll
             for (int n = 0; n < NC; ++n) if (n == t) pt = expf(z[n] - mx) / se;
             row_loss[r] = -(double)logf(pt);
+            lsum += -(double)logf(pt);
         }
 #pragma unroll
         for (int j = 0; j < KPL; ++j) {
@@ -585,21 +590,24 @@ __global__ void __launch_bounds__(256) head_kernel(const bf16 *__restrict__ a, c
                 for (int n = 0; n < NC; ++n) sAcc[k * NC + n] += gW[j][n];
                 sAcc[HD * NC + NC + k] += gP[j];
             }
-            if (lane == 0)
+            if (lane == 0) {
 #pragma unroll
                 for (int n = 0; n < NC; ++n) sAcc[HD * NC + n] += gB[n];
+                sLoss += lsum;
+            }
         }
         __syncthreads();
     }
-    float *dst = partial + (size_t)blockIdx.x * (HD * NC + NC + HD);
+    float *dst = partial + (size_t)blockIdx.x * (HD * NC + NC + HD + 1);
     for (int i = threadIdx.x; i < HD * NC + NC + HD; i += blockDim.x) dst[i] = sAcc[i];
+    if (threadIdx.x == 0) dst[HD * NC + NC + HD] = (float)sLoss;
 }
 
 // Sums partial[s][i] over s in order and scatters into the gradient layout.
 // map 0: dst[i];  1 conv (M=COUT rows, N = 9*CIN, n = tap*CIN + ci) -> dst[(co*CIN+ci)*9+tap]
 //        2 conv (M = 9*CIN rows (tap*CIN+ci), N = COUT)  -> same dst layout
 //        3 linear (M = F rows in NHWC order, N = OUT)    -> dst[nchw(m)*OUT + n]
-//        4 head partial [HD*NC | NC | HD] -> dW5, db5, db4 (three destinations)
+//        4 head partial [HD*NC | NC | HD | 1] -> dW5, db5, db4, loss (four destinations)
 //        5 first conv [COUT][10] -> dW1[co*9+t], db1[co]
 struct ReduceArgs {
     const float *partial;
@@ -609,6 +617,7 @@ struct ReduceArgs {
     float *dst, *dst2, *dst3;
     const float *bias;             // map 6
     __nv_bfloat16 *out_bf16;       // map 6
+    float *dst4;                   // map 4: the loss
 };
 
 __device__ void r_store(const ReduceArgs &r, long long i, float s);
@@ -670,6 +679,46 @@ __global__ void __launch_bounds__(256) reduce_deep_kernel(ReduceArgs r) {
     }
 }
 
+// Several independent deep reductions in one launch: blocks [start[j],
+// start[j+1]) run job j exactly as reduce_deep_kernel would.
+struct ReduceJobs {
+    ReduceArgs job[3];
+    int start[4];
+    int count;
+};
+
+__global__ void __launch_bounds__(256) reduce_multi_kernel(const __grid_constant__ ReduceJobs J) {
+    griddep_launch();
+    griddep_wait();
+    int j = 0;
+    while (j + 1 < J.count && (int)blockIdx.x >= J.start[j + 1]) ++j;
+    const ReduceArgs &r = J.job[j];
+    const int bx = (int)blockIdx.x - J.start[j], gx = J.start[j + 1] - J.start[j];
+    __shared__ float part[32][9];
+    const int el = threadIdx.x & 7, sl = threadIdx.x >> 3;
+    for (long long base = (long long)bx * 8; base < r.n; base += (long long)gx * 8) {
+        const long long i = base + el;
+        float s0 = 0.0f, s1 = 0.0f;
+        if (i < r.n) {
+            int k = sl;
+            for (; k + 32 < r.splits; k += 64) {
+                s0 += r.partial[(size_t)k * r.n + i];
+                s1 += r.partial[(size_t)(k + 32) * r.n + i];
+            }
+            if (k < r.splits) s0 += r.partial[(size_t)k * r.n + i];
+        }
+        part[sl][el] = s0 + s1;
+        __syncthreads();
+        if (sl == 0 && i < r.n) {
+            float s = part[0][el];
+#pragma unroll
+            for (int l = 1; l < 32; ++l) s += part[l][el];
+            r_store(r, i, s);
+        }
+        __syncthreads();
+    }
+}
+
 // Few splits of a long vector (the Linear weight gradient): each thread owns
 // 4 consecutive elements and adds the splits in order with 16-byte loads.
 __global__ void __launch_bounds__(256) reduce_wide_kernel(ReduceArgs r) {
@@ -702,7 +751,8 @@ __device__ void r_store(const ReduceArgs &r, long long i, float s) {
             const long long hdnc = (long long)r.M * r.N;
             if (i < hdnc) r.dst[i] = s;
             else if (i < hdnc + r.N) r.dst2[i - hdnc] = s;
-            else r.dst3[i - hdnc - r.N] = s;
+            else if (i < hdnc + r.N + r.M) r.dst3[i - hdnc - r.N] = s;
+            else *r.dst4 = s;
             break;
         }
         case 5: { const int co = (int)(i / 10), t = (int)(i % 10); if (t < 9) r.dst[co * 9 + t] = s; else r.dst2[co] = s; break; }
@@ -711,22 +761,6 @@ __device__ void r_store(const ReduceArgs &r, long long i, float s) {
     }
 }
 
-__global__ void loss_sum_kernel(const double *__restrict__ row_loss, int B, float *__restrict__ loss) {
-    griddep_launch();
-    griddep_wait();
-    __shared__ double part[256];
-    const int per = (B + blockDim.x - 1) / blockDim.x;
-    const int b0 = threadIdx.x * per, b1 = min(B, b0 + per);
-    double acc = 0.0;
-    for (int r = b0; r < b1; ++r) acc += row_loss[r];
-    part[threadIdx.x] = acc;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        double tot = 0.0;
-        for (int i = 0; i < (int)blockDim.x; ++i) tot += part[i];
-        *loss = (float)tot;
-    }
-}
 
 }  // namespace
 
@@ -1002,6 +1036,22 @@ int launch_gemm(const GemmTcParams &p) {
     const int tiles = p.m_tiles * p.n_tiles * p.ksplit;
     launch_pdl(kern, dim3(tiles < sm_count() ? tiles : sm_count()), dim3(192), S::SMEM, p);
     ZB_LAUNCH_CHECK("gemm_tc");
+    return kOk;
+}
+
+// Deep reductions (many splits, short vectors) of one phase in one launch.
+int reduce_multi(const ReduceArgs *jobs, int count) {
+    ReduceJobs J{};
+    J.count = count;
+    int total = 0;
+    for (int j = 0; j < count; ++j) {
+        J.job[j] = jobs[j];
+        J.start[j] = total;
+        total += grid_for(jobs[j].n, 8, 16);
+    }
+    J.start[count] = total;
+    launch_pdl(reduce_multi_kernel, dim3(total), dim3(256), 0, J);
+    ZB_LAUNCH_CHECK("reduce_multi");
     return kOk;
 }
 
@@ -1336,7 +1386,7 @@ int tc_build(Net &n, TcEngine &e) {
     // the fixed cost, and fewer blocks also means fewer partials to sum
     e.head_grid = (B + 31) / 32;
     if (e.head_grid > sm_count() * 2) e.head_grid = sm_count() * 2;
-    if ((rc = dalloc(e, &e.head_partial, (size_t)e.head_grid * (e.HD * e.NC + e.NC + e.HD)))) return rc;
+    if ((rc = dalloc(e, &e.head_partial, (size_t)e.head_grid * (e.HD * e.NC + e.NC + e.HD + 1)))) return rc;
     if ((rc = dalloc(e, &e.row_loss, (size_t)B))) return rc;
     e.c1_wgrad_grid = sm_count() * 2;   // the resident blocks (two per SM): each walks whole images
     if (e.c1_wgrad_grid > B) e.c1_wgrad_grid = B;
@@ -1436,11 +1486,10 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
     launch_pdl(head_kernel<256, 10>, dim3(e.head_grid), dim3(256), 0, e.a_hid, n.params + sh.poff,
                n.params + sh.poff + sh.pn_w, y, e.dZ_hid, e.row_loss, e.head_partial, B, 1.0f / (float)B);
     ZB_LAUNCH_CHECK("head");
-    launch_pdl(loss_sum_kernel, dim3(1), dim3(256), 0, e.row_loss, B, loss_out);
-    ZB_LAUNCH_CHECK("loss_sum");
-    {
-        ReduceArgs r{e.head_partial, e.head_grid, (long long)e.HD * e.NC + e.NC + e.HD, 4, e.HD, e.NC, 0, 0, 0, 0,
+    {   // fc2 dW, db, fc1 db and the loss sum (the blocks' partials, in block order)
+        ReduceArgs r{e.head_partial, e.head_grid, (long long)e.HD * e.NC + e.NC + e.HD + 1, 4, e.HD, e.NC, 0, 0, 0, 0,
                      gW5, gb5, gb4};
+        r.dst4 = loss_out;
         if ((rc = reduce(r))) return rc;
     }
     prof_mark(n, "softmax_ce");
@@ -1480,28 +1529,30 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
         }
         if (L.fused_bwd) {
             if ((rc = run_conv_bwd_fused(L, x, dP))) return rc;
-            ReduceArgs r{L.fbwd_partial, L.fbwd_grid, (long long)L.COUT * 9 * L.CIN, 1, L.COUT, 9 * L.CIN,
-                         L.CIN, 0, 0, 0, n.grads + s.poff, nullptr, nullptr};
-            if ((rc = reduce(r))) return rc;
-            if (L.fbwd_up) {
-                ReduceArgs rb{L.fbwd_bias_partial, 4 * L.fbwd_grid, (long long)L.COUT, 0, 1, L.COUT, 0, 0, 0, 0,
-                              n.grads + s.poff + s.pn_w, nullptr, nullptr};
-                if ((rc = reduce(rb))) return rc;
-            }
-            if (L.fbwd_c1) {
-                ReduceArgs r1{e.c1_partial, e.c1_wgrad_grid, (long long)e.C1 * 10, 5, e.C1, 10, 0, 0, 0, 0,
-                              n.grads + s1.poff, n.grads + s1.poff + s1.pn_w, nullptr};
-                if ((rc = reduce(r1))) return rc;
+            // the kernel's partials: conv2 dW, conv2 db (UP), conv1 dW + db (C1)
+            ReduceArgs jobs[3];
+            int nj = 0;
+            jobs[nj++] = ReduceArgs{L.fbwd_partial, L.fbwd_grid, (long long)L.COUT * 9 * L.CIN, 1, L.COUT, 9 * L.CIN,
+                                    L.CIN, 0, 0, 0, n.grads + s.poff, nullptr, nullptr};
+            if (L.fbwd_up)
+                jobs[nj++] = ReduceArgs{L.fbwd_bias_partial, 4 * L.fbwd_grid, (long long)L.COUT, 0, 1, L.COUT, 0, 0, 0, 0,
+                                        n.grads + s.poff + s.pn_w, nullptr, nullptr};
+            if (L.fbwd_c1)
+                jobs[nj++] = ReduceArgs{e.c1_partial, e.c1_wgrad_grid, (long long)e.C1 * 10, 5, e.C1, 10, 0, 0, 0, 0,
+                                        n.grads + s1.poff, n.grads + s1.poff + s1.pn_w, nullptr};
+            bool deep = true;   // every job has many splits of a short vector
+            for (int j = 0; j < nj; ++j) deep = deep && jobs[j].splits >= 32 && jobs[j].n <= 131072;
+            if (deep) {
+                if ((rc = reduce_multi(jobs, nj))) return rc;
+            } else {
+                for (int j = 0; j < nj; ++j)
+                    if ((rc = reduce(jobs[j]))) return rc;
             }
             prof_mark(n, "conv_bwd");
             continue;
         }
         if ((rc = run_conv_dgrad(L, dP))) return rc;
-        if (L.up) {   // bias gradient from the dgrad kernel's builders
-            ReduceArgs rb{L.up_bias_partial, 4 * L.up_grid, (long long)L.COUT, 0, 1, L.COUT, 0, 0, 0, 0,
-                          n.grads + s.poff + s.pn_w, nullptr, nullptr};
-            if ((rc = reduce(rb))) return rc;
-        }
+        // (up: the bias partials of the dgrad kernel's builders are summed with the weight gradient's)
         prof_mark(n, "conv_dgrad");
         if (L.wg_halo) {
             if ((rc = run_wgrad_halo(L))) return rc;
@@ -1510,10 +1561,22 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
             if ((rc = reduce(r))) return rc;
         } else {
             if ((rc = run_wgrad(L.wg, L.wg_mode, L.wg_grid, L.wg_smem, L.up ? dP : nullptr))) return rc;
-            ReduceArgs r{L.wg_partial, L.wg.splits, (long long)L.wg.M * L.wg.N,
-                         L.wg_mode == tc::kWgConvCo ? 1 : 2, L.wg.M, L.wg.N, L.CIN, 0, 0, 0,
-                         n.grads + s.poff, nullptr, nullptr};
-            if ((rc = reduce(r))) return rc;
+            ReduceArgs jobs[2];
+            jobs[0] = ReduceArgs{L.wg_partial, L.wg.splits, (long long)L.wg.M * L.wg.N,
+                                 L.wg_mode == tc::kWgConvCo ? 1 : 2, L.wg.M, L.wg.N, L.CIN, 0, 0, 0,
+                                 n.grads + s.poff, nullptr, nullptr};
+            const int nj = L.up ? 2 : 1;
+            if (L.up)   // the bias gradient from the dgrad kernel's builders
+                jobs[1] = ReduceArgs{L.up_bias_partial, 4 * L.up_grid, (long long)L.COUT, 0, 1, L.COUT, 0, 0, 0, 0,
+                                     n.grads + s.poff + s.pn_w, nullptr, nullptr};
+            bool deep = true;
+            for (int j = 0; j < nj; ++j) deep = deep && jobs[j].splits >= 32 && jobs[j].n <= 131072;
+            if (deep) {
+                if ((rc = reduce_multi(jobs, nj))) return rc;
+            } else {
+                for (int j = 0; j < nj; ++j)
+                    if ((rc = reduce(jobs[j]))) return rc;
+            }
         }
         prof_mark(n, "conv_wgrad");
     }

@@ -197,6 +197,19 @@ int zilla_net_step(int net, int x_id, int y_id, int loss_id, int update);
 /* Same step from host arrays: copies x/y host->device, runs the step and
  * copies the loss sum back (the end-to-end path). */
 int zilla_net_step_host(int net, const float *x, const float *y, float *loss_sum, int update);
+/* Staged host steps: the copy of the next batch runs during the current step.
+ * No reference counterpart (additive; the reference copies each batch with a
+ * blocking bufferUpload before its step, examples/mnist_cnn_gpu_v2.php:166-181).
+ * zilla_net_stage_host enqueues the host->device copy of x and y into the
+ * next of two device staging slots on the net's copy stream and returns at
+ * once (host memory should be pinned for the copy to be asynchronous; it must
+ * stay unchanged until the step that consumes it returns).  -2 when both
+ * slots already hold batches not yet stepped.
+ * zilla_net_step_staged runs the step on the oldest staged batch (-2 if none)
+ * and, when loss_sum is not null, returns after copying the loss sum back.
+ * Typical loop: stage(0); for k: stage(k+1); step_staged(k). */
+int zilla_net_stage_host(int net, const float *x, const float *y);
+int zilla_net_step_staged(int net, float *loss_sum, int update);
 
 /* Device timing of the step's segments (instrumentation).  With profiling
  * enabled, zilla_net_step records a CUDA event after each kernel group;

@@ -188,6 +188,16 @@ void free_net(Net *n) {
     if (!n) return;
     cudaStreamSynchronize(stream());
     peer_release(*n);   // peers' stores into this rank ended with the last step's wait
+    for (int k = 0; k < 2; ++k) {
+        if (n->sx[k]) cudaFree(n->sx[k]);
+        if (n->sy[k]) cudaFree(n->sy[k]);
+        if (n->ev_staged[k]) cudaEventDestroy(n->ev_staged[k]);
+        if (n->ev_consumed[k]) cudaEventDestroy(n->ev_consumed[k]);
+    }
+    if (n->copy_stream) {
+        cudaStreamSynchronize(n->copy_stream);
+        cudaStreamDestroy(n->copy_stream);
+    }
     if (n->tc) tc_destroy(*n);
     if (n->lm) lm_destroy(*n);
     for (auto &s : n->st) {
@@ -564,6 +574,52 @@ int zilla_net_step_host(int id, const float *x, const float *y, float *loss_sum,
         if (cudaStreamSynchronize(stream()) != cudaSuccess) return check_cuda("zilla_net_step_host");
     }
     return check_cuda("zilla_net_step_host");
+}
+
+int zilla_net_stage_host(int id, const float *x, const float *y) {
+    Net *n = net_get(id);
+    if (!n) return fail(kBadHandle, "zilla_net_stage_host: unknown net %d", id);
+    if (!x || !y) return fail(kBadArg, "zilla_net_stage_host: null input");
+    if (n->stage_count == 2) return fail(kBadArg, "zilla_net_stage_host: both slots hold batches not yet stepped");
+    if (!n->copy_stream) {   // first use: the copy stream, the two slots and their events
+        if (cudaStreamCreateWithFlags(&n->copy_stream, cudaStreamNonBlocking) != cudaSuccess)
+            return check_cuda("zilla_net_stage_host: copy stream");
+        for (int k = 0; k < 2; ++k) {
+            if (cudaMalloc((void **)&n->sx[k], (size_t)n->x_floats * sizeof(float)) != cudaSuccess ||
+                cudaMalloc((void **)&n->sy[k], (size_t)n->y_floats * sizeof(float)) != cudaSuccess ||
+                cudaEventCreateWithFlags(&n->ev_staged[k], cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&n->ev_consumed[k], cudaEventDisableTiming) != cudaSuccess)
+                return check_cuda("zilla_net_stage_host: staging slots");
+            cudaEventRecord(n->ev_consumed[k], stream());
+        }
+    }
+    const int k = n->stage_head;
+    // the step that last read this slot has finished before the copy overwrites it
+    cudaStreamWaitEvent(n->copy_stream, n->ev_consumed[k], 0);
+    cudaMemcpyAsync(n->sx[k], x, (size_t)n->x_floats * sizeof(float), cudaMemcpyHostToDevice, n->copy_stream);
+    cudaMemcpyAsync(n->sy[k], y, (size_t)n->y_floats * sizeof(float), cudaMemcpyHostToDevice, n->copy_stream);
+    cudaEventRecord(n->ev_staged[k], n->copy_stream);
+    n->stage_head ^= 1;
+    n->stage_count += 1;
+    return check_cuda("zilla_net_stage_host");
+}
+
+int zilla_net_step_staged(int id, float *loss_sum, int update) {
+    Net *n = net_get(id);
+    if (!n) return fail(kBadHandle, "zilla_net_step_staged: unknown net %d", id);
+    if (n->stage_count == 0) return fail(kBadArg, "zilla_net_step_staged: no batch staged");
+    const int k = n->stage_tail;
+    cudaStreamWaitEvent(stream(), n->ev_staged[k], 0);
+    int rc = run_step(*n, n->sx[k], n->sy[k], update);
+    cudaEventRecord(n->ev_consumed[k], stream());
+    n->stage_tail ^= 1;
+    n->stage_count -= 1;
+    if (rc) return rc;
+    if (loss_sum) {
+        cudaMemcpyAsync(loss_sum, n->grads + n->nparams, sizeof(float), cudaMemcpyDeviceToHost, stream());
+        if (cudaStreamSynchronize(stream()) != cudaSuccess) return check_cuda("zilla_net_step_staged");
+    }
+    return check_cuda("zilla_net_step_staged");
 }
 
 int zilla_net_inspect(int id, int index, char *name, int name_len, float *host, unsigned long n_floats) {

@@ -80,6 +80,11 @@ struct Net {
     cudaEvent_t ev_ready = nullptr, ev_done = nullptr;
     long long ar_lo = -1;                      // grads [ar_lo, nparams] already launched this step
     PeerState peer;
+    // staged host steps: two device input slots filled on a copy stream
+    cudaStream_t copy_stream = nullptr;
+    float *sx[2] = {nullptr, nullptr}, *sy[2] = {nullptr, nullptr};
+    cudaEvent_t ev_staged[2] = {nullptr, nullptr}, ev_consumed[2] = {nullptr, nullptr};
+    int stage_head = 0, stage_tail = 0, stage_count = 0;
     TcEngine *tc = nullptr;
     LmEngine *lm = nullptr;
     long long x_floats = 0, y_floats = 0;   // per-step input sizes (floats)

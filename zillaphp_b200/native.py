@@ -83,6 +83,8 @@ SIGNATURES: dict[str, tuple] = {
     "zilla_net_set_optimizer": (I, [I, I, F, F, F, F]),
     "zilla_net_step": (I, [I, I, I, I, I]),
     "zilla_net_step_host": (I, [I, FP, FP, FP, I]),
+    "zilla_net_stage_host": (I, [I, FP, FP]),
+    "zilla_net_step_staged": (I, [I, FP, I]),
     "zilla_net_profile": (I, [I, I]),
     "zilla_net_timings": (I, [I, C.c_char_p, I, FP, I]),
     "zilla_net_inspect": (I, [I, I, C.c_char_p, I, FP, UL]),

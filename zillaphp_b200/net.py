@@ -66,6 +66,24 @@ class Net:
                                                  C.byref(loss), int(update)))
         return float(loss.value)
 
+    def stage_host(self, x: np.ndarray, y: np.ndarray) -> None:
+        """Enqueue the host->device copy of the next batch (zilla_net_stage_host);
+        the arrays must stay alive and unchanged until its step_staged returns."""
+        self._staged = getattr(self, "_staged", [])
+        xa = x if (x.dtype == np.float32 and x.flags.c_contiguous) else np.ascontiguousarray(x, np.float32)
+        ya = y if (y.dtype == np.float32 and y.flags.c_contiguous) else np.ascontiguousarray(y, np.float32)
+        self._check(self.lib.zilla_net_stage_host(self.id, xa.ctypes.data_as(native.FP), ya.ctypes.data_as(native.FP)))
+        self._staged.append((xa, ya))   # keep the host buffers alive until their step
+
+    def step_staged(self, update: bool = True) -> float:
+        """Step on the oldest staged batch (zilla_net_step_staged); returns the loss sum."""
+        loss = C.c_float(0.0)
+        self._check(self.lib.zilla_net_step_staged(self.id, C.byref(loss), int(update)))
+        staged = getattr(self, "_staged", [])
+        if staged:
+            staged.pop(0)
+        return float(loss.value)
+
     def step_dev(self, x_id: int, y_id: int, loss_id: int, update: bool = True) -> None:
         self._check(self.lib.zilla_net_step(self.id, x_id, y_id, loss_id, int(update)))
 

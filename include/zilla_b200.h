@@ -211,6 +211,22 @@ int zilla_net_step_host(int net, const float *x, const float *y, float *loss_sum
 int zilla_net_stage_host(int net, const float *x, const float *y);
 int zilla_net_step_staged(int net, float *loss_sum, int update);
 
+/* Checkpoints: the net's parameters as a SafeTensors F32 file in the layout
+ * ModelSerializer::save writes through SafeTensorsSerializer::save
+ * (src/Serialization/ModelSerializer.php:56-69,
+ * src/Serialization/SafeTensorsSerializer.php:32-98): u64 little-endian
+ * header size, compact JSON header padded with spaces to 8 bytes, then the
+ * data; one tensor "param_i" per parameter in Module::parameters() order with
+ * its shape.  with_state != 0 also writes the Adam moments as "adam_m_i" /
+ * "adam_v_i" and the step count as __metadata__ "adam_t" (the reference keeps
+ * no optimizer state); it is rejected (-2) while the net is attached for
+ * data parallelism over peer memory (each rank holds a slice of the state).
+ * zilla_net_load reads such a file (or the reference's) into the net:
+ * param_i required with matching shapes and dtype F32, adam_* optional;
+ * -2 on a missing, malformed or mismatched file. */
+int zilla_net_save(int net, const char *path, int with_state);
+int zilla_net_load(int net, const char *path);
+
 /* Device timing of the step's segments (instrumentation).  With profiling
  * enabled, zilla_net_step records a CUDA event after each kernel group;
  * zilla_net_timings then returns, for the last step, up to max_segments

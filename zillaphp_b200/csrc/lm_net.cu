@@ -485,6 +485,26 @@ int attn_smem_bwd(int Ts, int dh) { return (int)((4 * (size_t)Ts * (dh + 1) + (s
 
 }  // namespace
 
+// Shapes of the LM's parameter tensors in buffer order (the order lm_build
+// lays them out in, which is TransformerLM::parameters() order).
+int lm_param_shapes(Net &n, std::vector<std::vector<long long>> &shapes) {
+    const LmEngine &e = *n.lm;
+    const long long V = e.V, D = e.D, F = e.F, T = e.T;
+    shapes = {{V, D}, {T, D}, {D}, {D}, {D, V}, {V}};
+    for (int l = 0; l < e.L; ++l) {
+        for (int k = 0; k < 4; ++k) {   // q, k, v, o: W [D, D], b [D]
+            shapes.push_back({D, D});
+            shapes.push_back({D});
+        }
+        shapes.push_back({D, F});
+        shapes.push_back({F});
+        shapes.push_back({F, D});
+        shapes.push_back({D});
+        for (int k = 0; k < 4; ++k) shapes.push_back({D});   // ln1 g, b; ln2 g, b
+    }
+    return kOk;
+}
+
 void lm_destroy(Net &n) {
     if (!n.lm) return;
     cudaStreamSynchronize(stream());

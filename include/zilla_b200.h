@@ -194,6 +194,13 @@ int zilla_net_set_optimizer(int net, int kind, float lr, float beta1, float beta
  * leaves gradients in the grads buffer and updates the parameters.
  * update = 0 computes gradients only. */
 int zilla_net_step(int net, int x_id, int y_id, int loss_id, int update);
+/* Evaluation (forward pass only, the same kernels as the step's forward):
+ * logits [batch, classes] fp32 into logits_id and, when y_id > 0 and
+ * loss_id > 0, the softmax_ce loss SUM into loss_id[0].  No gradients, no
+ * update.  Replaces the forward-only use of the layer stack in the
+ * reference's evaluation loops (examples/mnist_cnn_gpu_v2.php:284-373);
+ * not available for the language model (-2). */
+int zilla_net_forward(int net, int x_id, int y_id, int logits_id, int loss_id);
 /* Same step from host arrays: copies x/y host->device, runs the step and
  * copies the loss sum back (the end-to-end path). */
 int zilla_net_step_host(int net, const float *x, const float *y, float *loss_sum, int update);

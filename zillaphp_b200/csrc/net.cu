@@ -561,6 +561,33 @@ int zilla_net_step(int id, int x_id, int y_id, int loss_id, int update) {
     return check_cuda("zilla_net_step");
 }
 
+int zilla_net_forward(int id, int x_id, int y_id, int logits_id, int loss_id) {
+    Net *n = net_get(id);
+    if (!n) return fail(kBadHandle, "zilla_net_forward: unknown net %d", id);
+    if (n->lm) return fail(kBadArg, "zilla_net_forward: not available for the language model");
+    float *x = ptr(x_id), *logits = ptr(logits_id);
+    float *y = y_id > 0 ? ptr(y_id) : nullptr, *loss = loss_id > 0 ? ptr(loss_id) : nullptr;
+    if (!x || !logits || (y_id > 0 && !y) || (loss_id > 0 && !loss))
+        return fail(kBadHandle, "zilla_net_forward: invalid handle");
+    if (capacity(x_id) < (size_t)n->x_floats || capacity(logits_id) < (size_t)n->B * n->classes ||
+        (y && capacity(y_id) < (size_t)n->y_floats))
+        return fail(kBadHandle, "zilla_net_forward: buffers smaller than the batch");
+    if (loss && !y) return fail(kBadArg, "zilla_net_forward: a loss needs the targets");
+    int rc;
+    if (n->precision == 1) {
+        rc = tc_forward(*n, x, y, logits, loss);
+    } else {
+        rc = fp32_forward(*n, x);
+        if (!rc) {
+            cudaMemcpyAsync(logits, n->st.back().out, (size_t)n->B * n->classes * sizeof(float),
+                            cudaMemcpyDeviceToDevice, stream());
+            if (loss) rc = loss_and_dlogits(*n, n->st.back().out, y, loss);
+        }
+    }
+    if (rc) return rc;
+    return check_cuda("zilla_net_forward");
+}
+
 int zilla_net_step_host(int id, const float *x, const float *y, float *loss_sum, int update) {
     Net *n = net_get(id);
     if (!n) return fail(kBadHandle, "zilla_net_step_host: unknown net %d", id);

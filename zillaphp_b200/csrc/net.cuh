@@ -107,6 +107,7 @@ int loss_and_dlogits(Net &n, const float *logits, const float *y, float *loss_ou
 int tc_create(Net &n);
 void tc_destroy(Net &n);
 int tc_step(Net &n, const float *x, const float *y, float *loss_out);
+int tc_forward(Net &n, const float *x, const float *y, float *logits, float *loss_out);   // evaluation
 int tc_sync_params(Net &n);   // refresh the bf16 operand copies from the fp32 master
 int tc_inspect(Net &n, int index, char *name, int name_len, float *host, unsigned long n_floats);
 // language-model engine (lm_net.cu)

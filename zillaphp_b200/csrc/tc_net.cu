@@ -603,6 +603,65 @@ __global__ void __launch_bounds__(256) head_kernel(const bf16 *__restrict__ a, c
     if (threadIdx.x == 0) dst[HD * NC + NC + HD] = (float)sLoss;
 }
 
+// Forward-only classifier (evaluation): one warp per row, fp32 logits
+// z = a W + b with head_kernel's arithmetic, and (y given) the rows' loss
+// -log softmax(z)[y] summed per block in a fixed warp order into partial[block].
+template <int HD, int NC>
+__global__ void __launch_bounds__(256) head_fwd_kernel(const bf16 *__restrict__ a, const float *__restrict__ Wt,
+                                                       const float *__restrict__ bias, const float *__restrict__ y,
+                                                       float *__restrict__ logits, float *__restrict__ partial, int B) {
+    constexpr int KPL = HD / 32;
+    __shared__ float sW[HD * NC];
+    __shared__ double sLoss[8];
+    griddep_launch();
+    griddep_wait();
+    for (int i = threadIdx.x; i < HD * NC; i += blockDim.x) sW[i] = Wt[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    double lsum = 0.0;
+    for (int r = blockIdx.x * 8 + warp; r < B; r += gridDim.x * 8) {
+        float av[KPL];
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) av[j] = __bfloat162float(a[(size_t)r * HD + lane + 32 * j]);
+        float z[NC];
+#pragma unroll
+        for (int n = 0; n < NC; ++n) {
+            float s = 0.0f;
+#pragma unroll
+            for (int j = 0; j < KPL; ++j) s = fmaf(av[j], sW[(lane + 32 * j) * NC + n], s);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            z[n] = s + bias[n];
+        }
+        if (lane < NC) {
+            float zl = z[0];
+#pragma unroll
+            for (int n = 1; n < NC; ++n) if (lane == n) zl = z[n];
+            logits[(size_t)r * NC + lane] = zl;
+        }
+        if (y && lane == 0) {
+            float mx = z[0];
+#pragma unroll
+            for (int n = 1; n < NC; ++n) mx = fmaxf(mx, z[n]);
+            float se = 0.0f;
+#pragma unroll
+            for (int n = 0; n < NC; ++n) se += expf(z[n] - mx);
+            const int t = (int)y[r];
+            float pt = 0.0f;
+#pragma unroll
+            for (int n = 0; n < NC; ++n) if (n == t) pt = expf(z[n] - mx) / se;
+            lsum += -(double)logf(pt);
+        }
+    }
+    if (lane == 0) sLoss[warp] = lsum;
+    __syncthreads();
+    if (threadIdx.x == 0 && partial) {
+        double t = 0.0;
+        for (int w = 0; w < 8; ++w) t += sLoss[w];
+        partial[blockIdx.x] = (float)t;
+    }
+}
+
 // Sums partial[s][i] over s in order and scatters into the gradient layout.
 // map 0: dst[i];  1 conv (M=COUT rows, N = 9*CIN, n = tap*CIN + ci) -> dst[(co*CIN+ci)*9+tap]
 //        2 conv (M = 9*CIN rows (tap*CIN+ci), N = COUT)  -> same dst layout
@@ -1426,7 +1485,9 @@ int tc_build(Net &n, TcEngine &e) {
     return kOk;
 }
 
-int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out) {
+// One training step, or (logits_out != null) the forward pass only: logits
+// [B][classes] fp32 and, with y, the loss sum; no gradients, no update.
+int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out, float *logits_out = nullptr) {
     const int B = e.B;
     auto &st = n.st;
     int rc;
@@ -1478,6 +1539,18 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out)
         return rc;
     }
     prof_mark(n, "linear_fwd");
+    if (logits_out) {   // evaluation: classifier and loss only
+        const Stage &sf = st[e.head_si];
+        launch_pdl(head_fwd_kernel<256, 10>, dim3(e.head_grid), dim3(256), 0, e.a_hid, n.params + sf.poff,
+                   n.params + sf.poff + sf.pn_w, y, logits_out, (y && loss_out) ? e.head_partial : nullptr, B);
+        ZB_LAUNCH_CHECK("head forward");
+        if (y && loss_out) {
+            ReduceArgs r{e.head_partial, e.head_grid, 1, 0, 1, 1, 0, 0, 0, 0, loss_out, nullptr, nullptr};
+            if ((rc = reduce(r))) return rc;
+        }
+        prof_mark(n, "softmax_ce");
+        return kOk;
+    }
     // ---- head: classifier, loss, start of the backward
     const Stage &sh = st[e.head_si];
     float *gW5 = n.grads + sh.poff, *gb5 = gW5 + sh.pn_w;
@@ -1632,6 +1705,11 @@ int tc_step(Net &n, const float *x, const float *y, float *loss_out) {
     int rc = tc_run(n, *n.tc, x, y, loss_out);
     if (rc) return rc;
     return kOk;
+}
+
+int tc_forward(Net &n, const float *x, const float *y, float *logits, float *loss_out) {
+    if (!n.tc) return fail(kBadArg, "tc engine missing");
+    return tc_run(n, *n.tc, x, y, loss_out, logits);
 }
 
 int tc_sync_params(Net &n) {

@@ -84,6 +84,37 @@ class Net:
             staged.pop(0)
         return float(loss.value)
 
+    def forward(self, x: np.ndarray, y: np.ndarray | None = None) -> tuple[np.ndarray, float | None]:
+        """Evaluation through zilla_net_forward: (logits [batch, classes], loss sum or None)."""
+        lib, ids = self.lib, []
+
+        def dev(a: np.ndarray) -> int:
+            a = np.ascontiguousarray(a, np.float32)
+            i = lib.zilla_buffer_alloc(a.size)
+            if i <= 0:
+                raise RuntimeError(f"zilla_buffer_alloc failed: {native.last_error()}")
+            ids.append(i)
+            self._check(lib.zilla_buffer_upload(i, a.ctypes.data_as(native.FP), a.size))
+            return i
+
+        try:
+            xi = dev(x)
+            yi = dev(y) if y is not None else 0
+            li = dev(np.zeros(1, np.float32)) if y is not None else 0
+            lo = dev(np.zeros(self.batch * self.w.classes, np.float32))
+            self._check(lib.zilla_net_forward(self.id, xi, yi, lo, li))
+            logits = np.empty(self.batch * self.w.classes, np.float32)
+            self._check(lib.zilla_buffer_download(lo, logits.ctypes.data_as(native.FP), logits.size))
+            loss = None
+            if li:
+                l1 = np.empty(1, np.float32)
+                self._check(lib.zilla_buffer_download(li, l1.ctypes.data_as(native.FP), 1))
+                loss = float(l1[0])
+            return logits.reshape(self.batch, self.w.classes), loss
+        finally:
+            for i in ids:
+                lib.zilla_buffer_free(i)
+
     def step_dev(self, x_id: int, y_id: int, loss_id: int, update: bool = True) -> None:
         self._check(self.lib.zilla_net_step(self.id, x_id, y_id, loss_id, int(update)))
 

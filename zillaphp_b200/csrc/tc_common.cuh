@@ -128,6 +128,13 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
+// Tiled 2D TMA store shared -> global (no multicast); coordinates must be >= 0.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(c0),
+                 "r"(c1), "r"(smem_u32(src))
+                 : "memory");
+}
+
 // Tiled TMA store shared -> global (no multicast); coordinates must be >= 0.
 // Out-of-range box elements are not written.
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, const void *src, int c0, int c1, int c2, int c3) {

@@ -8,7 +8,11 @@
 //
 // Epilogues:
 //   kGemmBiasRelu: bf16 relu(acc + bias[n])        (Linear forward + ReLU)
-//   kGemmStore   : bf16 acc                       (Linear input gradient)
+//   kGemmStore   : bf16 acc                       (Linear input gradient): each
+//                  128 x 32 chunk is staged in shared memory with the 64-byte
+//                  swizzle and written by one TMA store (double-buffered), so
+//                  the output goes out as whole lines, not 16-byte pieces of
+//                  32 different rows per warp store
 //   kGemmPartial : fp32 acc of one K split into partial[split][M][N]; the
 //                  splits are summed in split order by a separate pass
 //                  (small batches: few M tiles, so K is split to fill the SMs)
@@ -24,6 +28,7 @@ enum GemmEpi { kGemmBiasRelu = 0, kGemmStore = 1, kGemmPartial = 2 };
 struct GemmTcParams {
     CUtensorMap a_map;   // 2D {K, M} bf16, box {64, 128}
     CUtensorMap b_map;   // 2D {K, N} bf16, box {64, BN}
+    CUtensorMap out_map; // kGemmStore: 2D {N, M} bf16, box {32, 128}, 64-byte swizzle
     int M, N, K;         // N % BN == 0, K % 64 == 0
     int m_tiles, n_tiles;
     int ksplit, kper;    // K splits (1 unless kGemmPartial) and 64-wide k steps per split
@@ -39,7 +44,8 @@ struct GemmTcShape {
     static constexpr int BBYTES = BN * 128;
     static constexpr int STAGE = ABYTES + BBYTES;
     static constexpr uint32_t TMEM_COLS = (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-    static constexpr int SMEM = 1024 + NS * STAGE + 256;
+    static constexpr int OUT_STAGE = 128 * 32 * 2;   // kGemmStore: one staged 128 x 32 chunk
+    static constexpr int SMEM = 1024 + NS * STAGE + 2 * OUT_STAGE + 256;
     static_assert(BN % 32 == 0 && BN <= 256, "BN");
 };
 
@@ -50,7 +56,8 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *sbase = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sbase + NS * S::STAGE);
+    uint8_t *sout = sbase + NS * S::STAGE;   // [2] staged output chunks (kGemmStore)
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sout + 2 * S::OUT_STAGE);
     uint64_t *full = bars, *empty = bars + NS, *acc_full = bars + 2 * NS, *acc_empty = acc_full + 2;
     uint64_t *drain = acc_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
@@ -81,6 +88,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         if (elect_one()) {
             prefetch_tmap(&p.a_map);
             prefetch_tmap(&p.b_map);
+            if (EPI == kGemmStore) prefetch_tmap(&p.out_map);
             int s = 0;
             uint32_t ph = 0;
             for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
@@ -138,7 +146,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
     } else {
         const int q = warp & 3;
         const int row = q * 32 + lane;
-        int acc = 0;
+        int acc = 0, sb = 0;
         uint32_t acc_ph = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             const int mn = tile % mn_tiles, ks = tile / mn_tiles;
@@ -158,8 +166,31 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&acc_empty[acc]);
                 }
-                if (m >= p.M) continue;
                 const int n0 = nt * BN + 32 * cc;
+                if constexpr (EPI == kGemmStore) {
+                    // every epilogue thread takes part (the barriers); the TMA store drops rows >= M
+                    if (threadIdx.x == 64) bulk_wait_read<1>();   // the store that last read this buffer
+                    named_bar_sync(1, 128);
+                    uint8_t *buf = sout + sb * S::OUT_STAGE;
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        uint4 pk;
+                        __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) h2[e] = __floats2bfloat162_rn(v[q4 * 8 + 2 * e], v[q4 * 8 + 2 * e + 1]);
+                        const uint32_t o = (uint32_t)(row * 64 + 16 * q4);   // 64-byte swizzle: 16-byte unit ^ (row / 2) % 4
+                        *reinterpret_cast<uint4 *>(buf + (o ^ (((o >> 7) & 3u) << 4))) = pk;
+                    }
+                    fence_proxy_async_smem();
+                    named_bar_sync(1, 128);
+                    if (threadIdx.x == 64) {
+                        tma_store_2d(&p.out_map, buf, n0, mt * 128);
+                        bulk_commit();
+                    }
+                    sb ^= 1;
+                    continue;
+                }
+                if (m >= p.M) continue;
                 if constexpr (EPI == kGemmPartial) {
                     float4 *dstf = reinterpret_cast<float4 *>(p.partial + ((size_t)ks * p.M + m) * p.N + n0);
 #pragma unroll
@@ -185,6 +216,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
             }
             if (++acc == 2) { acc = 0; acc_ph ^= 1u; }
         }
+        if (EPI == kGemmStore && threadIdx.x == 64) bulk_wait_all();   // stores complete before exit
     }
     tc_fence_before();
     __syncthreads();

@@ -1412,6 +1412,11 @@ int tc_build(Net &n, TcEngine &e) {
         dg.M = B; dg.N = e.F; dg.K = e.HD; dg.m_tiles = (B + 127) / 128; dg.n_tiles = e.F / bn;
         dg.ksplit = 1; dg.kper = e.HD / 64;
         dg.bias = nullptr; dg.out = e.dflat; dg.err = device_error_word();
+        {   // the epilogue's TMA store: 128 x 32 chunks of dflat [B][F], 64-byte swizzle
+            const uint64_t dd[2] = {(uint64_t)e.F, (uint64_t)B}, sd[1] = {(uint64_t)e.F * 2};
+            const uint32_t bd[2] = {32, 128};
+            if ((rc = tc::make_tmap_bf16(&dg.out_map, e.dflat, 2, dd, sd, bd, tc::kSw64))) return rc;
+        }
         // weight gradient: A = flattened activation (MN-major), B = dZ
         WgradTcParams &w = e.fc_wg;
         {

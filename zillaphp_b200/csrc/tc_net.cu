@@ -1446,9 +1446,10 @@ int tc_build(Net &n, TcEngine &e) {
     e.NC = st[i].oC;
     if (!e.has_hidden) return fail(kBadArg, "tc engine: a hidden Linear + ReLU before the classifier is required");
     if (e.HD != 256 || e.NC != 10) return fail(kBadArg, "tc engine: head %d->%d not supported", e.HD, e.NC);
-    // at least 4 rows per warp: the block set-up (W staging, partial write) is
-    // the fixed cost, and fewer blocks also means fewer partials to sum
-    e.head_grid = (B + 31) / 32;
+    // a row per warp up to two blocks per SM (small batches: the kernel is
+    // latency-bound, so more SMs), then more rows per warp (the block set-up,
+    // W staging and partial write, is the fixed cost; fewer partials to sum)
+    e.head_grid = (B + 7) / 8;
     if (e.head_grid > sm_count() * 2) e.head_grid = sm_count() * 2;
     if ((rc = dalloc(e, &e.head_partial, (size_t)e.head_grid * (e.HD * e.NC + e.NC + e.HD + 1)))) return rc;
     if ((rc = dalloc(e, &e.row_loss, (size_t)B))) return rc;

@@ -234,6 +234,16 @@ int zilla_net_step_staged(int net, float *loss_sum, int update);
 int zilla_net_save(int net, const char *path, int with_state);
 int zilla_net_load(int net, const char *path);
 
+/* Per-step CUDA graphs (no reference counterpart; the reference launches
+ * about 30 FFI calls per step, examples/mnist_cnn_gpu_v2.php:183-264).
+ * enable != 0: on one rank and without profiling, the first step for given
+ * inputs (x, y buffers and update flag) runs as is, the second is captured
+ * into a CUDA graph and launched, later ones replay it with the optimizer's
+ * arguments of the step; up to 16 input sets per net.  Results are those of
+ * the plain step, bit for bit.  zilla_net_set_optimizer drops the graphs.
+ * enable = 0 drops them and returns to plain launches. */
+int zilla_net_set_graph(int net, int enable);
+
 /* Device timing of the step's segments (instrumentation).  With profiling
  * enabled, zilla_net_step records a CUDA event after each kernel group;
  * zilla_net_timings then returns, for the last step, up to max_segments

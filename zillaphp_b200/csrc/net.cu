@@ -188,6 +188,7 @@ void free_net(Net *n) {
     if (!n) return;
     cudaStreamSynchronize(stream());
     peer_release(*n);   // peers' stores into this rank ended with the last step's wait
+    release_graphs(*n);
     for (int k = 0; k < 2; ++k) {
         if (n->sx[k]) cudaFree(n->sx[k]);
         if (n->sy[k]) cudaFree(n->sy[k]);
@@ -417,13 +418,97 @@ static int allreduce_grads(Net &n) {
 static int optimizer_step(Net &n) {
     const float scale = 1.0f / (float)n.world;
     n.t += 1;
-    if (n.opt == 2)
-        return launch_adam(n.params, n.grads, n.m, n.v, n.nparams,
-                           make_adam_args(n.lr, n.b1, n.b2, n.eps, n.t, scale));
-    return launch_sgd(n.params, n.grads, n.lr, scale, n.nparams);
+    const int rc = n.opt == 2 ? launch_adam(n.params, n.grads, n.m, n.v, n.nparams,
+                                            make_adam_args(n.lr, n.b1, n.b2, n.eps, n.t, scale))
+                              : launch_sgd(n.params, n.grads, n.lr, scale, n.nparams);
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (!rc && cudaStreamIsCapturing(stream(), &cs) == cudaSuccess && cs == cudaStreamCaptureStatusActive) {
+        // the node just captured: a replay gives it this step's Adam arguments
+        const cudaGraphNode_t *deps = nullptr;
+        size_t nd = 0;
+        if (cudaStreamGetCaptureInfo(stream(), &cs, nullptr, nullptr, &deps, &nd) == cudaSuccess && nd == 1)
+            n.captured_opt = deps[0];
+    }
+    return rc;
 }
 
+static int run_step_body(Net &n, const float *x, const float *y, int update);
+
+void release_graphs(Net &n) {
+    for (auto &g : n.graphs) {
+        if (g.exec) cudaGraphExecDestroy(g.exec);
+        if (g.graph) cudaGraphDestroy(g.graph);
+    }
+    n.graphs.clear();
+}
+
+// One step, replayed from a CUDA graph when enabled: the first call for a
+// (x, y, update) runs as is (lazy set-up happens outside any capture), the
+// second captures the step on the library stream and launches the graph,
+// later calls only refresh the optimizer's arguments and launch it.
 static int run_step(Net &n, const float *x, const float *y, int update) {
+    if (!n.graph_on || n.world > 1 || n.profile || n.peer.on) return run_step_body(n, x, y, update);
+    Net::StepGraph *g = nullptr;
+    for (auto &e : n.graphs)
+        if (e.x == x && e.y == y && e.update == update) g = &e;
+    if (!g) {
+        if (n.graphs.size() >= 16) return run_step_body(n, x, y, update);
+        n.graphs.emplace_back();
+        g = &n.graphs.back();
+        g->x = x; g->y = y; g->update = update;
+    }
+    if (g->runs++ == 0) return run_step_body(n, x, y, update);
+    if (!g->exec) {
+        const int t0 = n.t;
+        const unsigned long long l0 = zilla_launch_count();
+        n.captured_opt = nullptr;
+        if (cudaStreamBeginCapture(stream(), cudaStreamCaptureModeRelaxed) != cudaSuccess)
+            return check_cuda("net: graph capture");
+        int rc = run_step_body(n, x, y, update);
+        cudaGraph_t graph = nullptr;
+        const cudaError_t ce = cudaStreamEndCapture(stream(), &graph);
+        cudaGraphExec_t exec = nullptr;
+        if (!rc && ce == cudaSuccess && graph && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess &&
+            (!update || n.captured_opt)) {
+            g->graph = graph;
+            g->exec = exec;
+            g->opt_node = update ? n.captured_opt : nullptr;
+            g->nkern = (unsigned)(zilla_launch_count() - l0);
+            if (cudaGraphLaunch(exec, stream()) != cudaSuccess) return check_cuda("net: graph launch");
+            return check_cuda("net: graph");
+        }
+        // capture not possible: graphs off for this net, the step runs as is
+        if (exec) cudaGraphExecDestroy(exec);
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+        release_graphs(n);
+        n.graph_on = false;
+        n.t = t0;
+        if (rc) return rc;
+        return run_step_body(n, x, y, update);
+    }
+    if (update) {
+        n.t += 1;
+        if (n.opt == 2) {   // this step's Adam arguments (the bias corrections change with t)
+            float *w = n.params, *m = n.m, *v = n.v;
+            const float *gr = n.grads;
+            long long cnt = n.nparams;
+            AdamArgs a = make_adam_args(n.lr, n.b1, n.b2, n.eps, n.t, 1.0f);
+            void *args[6] = {&w, &gr, &m, &v, &cnt, &a};
+            cudaKernelNodeParams kp{};
+            if (cudaGraphKernelNodeGetParams(g->opt_node, &kp) != cudaSuccess) return check_cuda("net: graph node");
+            kp.kernelParams = args;
+            kp.extra = nullptr;
+            if (cudaGraphExecKernelNodeSetParams(g->exec, g->opt_node, &kp) != cudaSuccess)
+                return check_cuda("net: graph optimizer arguments");
+        }
+    }
+    if (cudaGraphLaunch(g->exec, stream()) != cudaSuccess) return check_cuda("net: graph launch");
+    count_launch(g->nkern);
+    return check_cuda("net: graph");
+}
+
+static int run_step_body(Net &n, const float *x, const float *y, int update) {
     int rc;
     // data parallel over peer memory: this step's gradients go to an exchange
     // buffer, and one kernel sums the rank's slice over NVLink and updates it
@@ -544,6 +629,7 @@ int zilla_net_set_optimizer(int id, int kind, float lr, float beta1, float beta2
     if (!n) return fail(kBadHandle, "zilla_net_set_optimizer: unknown net %d", id);
     if (kind != 1 && kind != 2) return fail(kBadArg, "zilla_net_set_optimizer: kind must be 1 (SGD) or 2 (Adam)");
     n->opt = kind; n->lr = lr; n->b1 = beta1; n->b2 = beta2; n->eps = eps;
+    release_graphs(*n);   // captured optimizer launches carry the old settings
     return kOk;
 }
 
@@ -665,6 +751,15 @@ int zilla_net_device_status(int id) {
     int code = read_and_clear_device_error();
     if (code) return fail(kCudaError, "device error word 0x%x (bounded wait expired or bad index)", code);
     return check_cuda("zilla_net_device_status");
+}
+
+int zilla_net_set_graph(int id, int enable) {
+    Net *n = net_get(id);
+    if (!n) return fail(kBadHandle, "zilla_net_set_graph: unknown net %d", id);
+    cudaStreamSynchronize(stream());
+    release_graphs(*n);
+    n->graph_on = enable != 0;
+    return kOk;
 }
 
 int zilla_net_profile(int id, int enable) {

@@ -85,6 +85,18 @@ struct Net {
     float *sx[2] = {nullptr, nullptr}, *sy[2] = {nullptr, nullptr};
     cudaEvent_t ev_staged[2] = {nullptr, nullptr}, ev_consumed[2] = {nullptr, nullptr};
     int stage_head = 0, stage_tail = 0, stage_count = 0;
+    // per-step CUDA graphs (zilla_net_set_graph): one per (x, y, update) on one rank
+    bool graph_on = false;
+    struct StepGraph {
+        const float *x = nullptr, *y = nullptr;
+        int update = 0, runs = 0;
+        cudaGraph_t graph = nullptr;          // kept: its optimizer node updates the exec
+        cudaGraphExec_t exec = nullptr;
+        cudaGraphNode_t opt_node = nullptr;   // the optimizer kernel (Adam's arguments change every step)
+        unsigned nkern = 0;                   // kernels per replay (launch counter)
+    };
+    std::vector<StepGraph> graphs;
+    cudaGraphNode_t captured_opt = nullptr;   // set by the optimizer launch while capturing
     TcEngine *tc = nullptr;
     LmEngine *lm = nullptr;
     long long x_floats = 0, y_floats = 0;   // per-step input sizes (floats)
@@ -121,6 +133,7 @@ int dp_bucket_ready(Net &n, long long off);
 int net_register(Net *n);             // assigns the id, returns it
 void net_free(Net *n);                // releases everything a Net holds
 int net_alloc_common(Net &n, long long classes_rows, long long rows);   // params, grads, Adam, staging
+void release_graphs(Net &n);          // the net's per-step CUDA graphs
 // peer.cu: set-up after the NCCL communicator exists (collective; stays on NCCL
 // when a rank cannot map every peer), the step hooks, and the release
 int peer_attach(Net &n);

@@ -85,6 +85,7 @@ SIGNATURES: dict[str, tuple] = {
     "zilla_net_step_host": (I, [I, FP, FP, FP, I]),
     "zilla_net_stage_host": (I, [I, FP, FP]),
     "zilla_net_forward": (I, [I, I, I, I, I]),
+    "zilla_net_set_graph": (I, [I, I]),
     "zilla_net_save": (I, [I, C.c_char_p, I]),
     "zilla_net_load": (I, [I, C.c_char_p]),
     "zilla_net_step_staged": (I, [I, FP, I]),

@@ -118,6 +118,10 @@ class Net:
     def step_dev(self, x_id: int, y_id: int, loss_id: int, update: bool = True) -> None:
         self._check(self.lib.zilla_net_step(self.id, x_id, y_id, loss_id, int(update)))
 
+    def set_graph(self, enable: bool = True) -> None:
+        """Replay the step from a CUDA graph (zilla_net_set_graph)."""
+        self._check(self.lib.zilla_net_set_graph(self.id, int(enable)))
+
     def profile(self, enable: bool = True) -> None:
         self._check(self.lib.zilla_net_profile(self.id, int(enable)))
 

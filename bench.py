@@ -672,6 +672,29 @@ def main_lm(args):
     if world > 1:
         dist.all_reduce(t2, op=dist.ReduceOp.MAX)
     e2e_value = batch * args.steps / (float(t2.item()) / 1e3)
+    gen = None
+    if world == 1:   # generation as Sampler::generate drives it: a prompt, then one token per call
+        prompt = xs_host[0].numpy()[: w.max_seq // 2]
+        new = w.max_seq - prompt.size
+
+        def generate():
+            net.cache_reset()
+            logits = net.forward_cached(prompt)
+            for _ in range(new):
+                logits = net.forward_cached([float(np.argmax(logits[-1]))])
+
+        generate()
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        generate()
+        g1.record(stream)
+        barrier()
+        gms = g0.elapsed_time(g1)
+        gen = {"prompt_tokens": int(prompt.size), "new_tokens": int(new), "ms_total": round(gms, 3),
+               "new_tokens_per_s": round(new / (gms / 1e3), 1),
+               "notes": "zilla_lm_forward_cached from host token ids, logits [rows, vocab] back to the host "
+                        "every call, greedy argmax on the host"}
     if rank == 0:
         work = lm_work(w, b)
         agg = {}
@@ -715,7 +738,7 @@ def main_lm(args):
             "gpu_launches": int(launches), "launches_per_step": per_step_launches,
             "roofline": roof,
             "segments_ms": {f"{work[k]['name']}#{k}": round(sum(v) / len(v), 4) for k, v in sorted(agg.items())},
-            "cpu_baseline": cpu, "clocks": clocks}))
+            "cpu_baseline": cpu, "clocks": clocks, "generation": gen}))
     net.close()
     lib.zilla_set_stream(None)
     if world > 1:

@@ -278,6 +278,24 @@ int zilla_net_device_status(int net);
  * floats.  seq <= 176 (one (sequence, head) of the attention backward is
  * held in shared memory).  Returns a net id > 0, or a negative status. */
 int zilla_lm_create(int vocab, int dim, int heads, int layers, int max_seq, int ffn, int batch, int seq);
+/* Generation with a K/V cache: TransformerLM::forwardWithCache
+ * (src/Transformers/TransformerLM.php:124-151), as driven by
+ * Sampler::generate (src/Generators/Sampler.php:35-100).  `count` token ids
+ * (host floats, truncated like Embedding's (int) cast) take positions
+ * len .. len+count-1, len = the cache length; each block appends their K and
+ * V rows to its cache (MultiHeadAttention::forwardWithCache,
+ * src/Attention/MultiHeadAttention.php:99-125) and every new row attends to
+ * all cached rows WITHOUT a causal mask (attendHeadCached, :127-137).  logits
+ * [count, vocab] fp32 are written to host memory (NULL skips the copy); the
+ * cache length then grows by count.  len + count > max_seq or a token id
+ * outside [0, vocab) returns kBadArg and leaves the cache unchanged (the
+ * reference throws RuntimeException / OutOfRangeException).  Uses the net's
+ * current parameters; independent of the training step's buffers. */
+int zilla_lm_forward_cached(int net, const float *tokens, int count, float *logits);
+/* TransformerLM::newCache (TransformerLM.php:153-156): cache length 0. */
+int zilla_lm_cache_reset(int net);
+/* KVCache::$length: the number of cached positions (>= 0), or a negative status. */
+int zilla_lm_cache_length(int net);
 
 /* ---- data-parallel runner (one process per GPU, NVLink) ----
  * zilla_dp_unique_id writes a 128-byte NCCL unique id (rank 0 creates it,

@@ -15,6 +15,8 @@ Follows the reference:
   loss                                softmax_ce_dev, native/cpu/training_ops.c:162-206
                                       (sum of -log p over rows; dlogits = (p - onehot) / rows)
   Adam                                src/Optim/Adam.php:36-62
+  TransformerLM::forwardWithCache     src/Transformers/TransformerLM.php:124-151 (generation;
+                                      forward_cached below: K/V cache, no causal mask)
 The batched block-diagonal mask of forwardBatch (src/Tensor/Tensor.php:619-634)
 is evaluated per sequence: masked scores are -1e9, whose softmax weight is
 exactly 0, so attention never crosses sequences.
@@ -183,3 +185,64 @@ def step(flat, tokens, targets, V, D, H, L, T, F, opt="adam", lr=3e-4, t=1, m=No
     else:
         new = w
     return loss, grads, new, m, v, logits
+
+
+def attention_cached(q, k, v, H):
+    """MultiHeadAttention::attendHeadCached per head (src/Attention/MultiHeadAttention.php:127-137),
+    heads concatenated: q [n, D] new rows, k, v [len, D] all cached rows; softmax of
+    (q k^T) / sqrt(head_dim) over every cached key -- no mask."""
+    D = q.shape[1]
+    dh = D // H
+    scale = 1.0 / np.sqrt(dh)
+    outs = []
+    for h in range(H):
+        cs = slice(h * dh, (h + 1) * dh)
+        s = q[:, cs] @ k[:, cs].T * scale
+        s = s - s.max(1, keepdims=True)
+        e = np.exp(s)
+        outs.append((e / e.sum(1, keepdims=True)) @ v[:, cs])
+    return np.concatenate(outs, 1)
+
+
+def forward_cached(flat, tokens, cache, V, D, H, L, T, F):
+    """TransformerLM::forwardWithCache (src/Transformers/TransformerLM.php:124-151)
+    in float64.  tokens: [n] ints for positions cache['len'] .. cache['len']+n-1;
+    cache: {'len': int, 'k': [L arrays [len, D]], 'v': [...]} (KVCache), updated
+    in place.  Per block (TransformerBlock.php:40-45): x += attn(ln1(x)) with the
+    new K/V rows appended to the layer's cache (MultiHeadAttention.php:99-125)
+    and every query row attending to ALL cached keys -- attendHeadCached
+    (MultiHeadAttention.php:127-137) applies no causal mask -- then
+    x += ffn(ln2(x)).  Returns logits [n, V]."""
+    n = len(tokens)
+    off = cache["len"]
+    if off + n > T:
+        raise RuntimeError(f"Sequence position {off + n} exceeds max {T}.")
+    P = unflatten(np.asarray(flat, np.float64), V, D, L, T, F)
+    ids = np.asarray(tokens, np.int64)
+    x = P["tok"][ids] + P["pos"][off:off + n]
+    for l in range(L):
+        pre = f"b{l}."
+        h1, _ = _ln(x, P[pre + "ln1.g"], P[pre + "ln1.b"])
+        q = h1 @ P[pre + "q.W"] + P[pre + "q.b"]
+        k = h1 @ P[pre + "k.W"] + P[pre + "k.b"]
+        vv = h1 @ P[pre + "v.W"] + P[pre + "v.b"]
+        if off:
+            k = np.concatenate([cache["k"][l], k])
+            vv = np.concatenate([cache["v"][l], vv])
+        if len(cache["k"]) <= l:
+            cache["k"].append(k)
+            cache["v"].append(vv)
+        else:
+            cache["k"][l], cache["v"][l] = k, vv
+        x = x + attention_cached(q, k, vv, H) @ P[pre + "o.W"] + P[pre + "o.b"]
+        h2, _ = _ln(x, P[pre + "ln2.g"], P[pre + "ln2.b"])
+        f1 = np.maximum(h2 @ P[pre + "fc1.W"] + P[pre + "fc1.b"], 0.0)
+        x = x + f1 @ P[pre + "fc2.W"] + P[pre + "fc2.b"]
+    cache["len"] = off + n
+    hf, _ = _ln(x, P["lnf.g"], P["lnf.b"])
+    return hf @ P["head.W"] + P["head.b"]
+
+
+def new_cache():
+    """TransformerLM::newCache (src/Transformers/TransformerLM.php:153-156)."""
+    return {"len": 0, "k": [], "v": []}

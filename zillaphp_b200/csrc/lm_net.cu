@@ -42,6 +42,12 @@ struct LmEngine {
     float *ln_partial = nullptr;   // [ln_blocks][2D]
     float *emb_partial = nullptr;  // [row chunks][V][D]
     int ln_blocks = 0;
+    // generation (TransformerLM::forwardWithCache): per-layer K/V caches
+    // [max_seq][D] and buffers for up to max_seq new rows, made on first use
+    std::vector<float *> kc, vc;
+    float *gx = nullptr, *gxm = nullptr, *gh = nullptr, *gxh = nullptr, *ginv = nullptr, *gqkv = nullptr,
+          *gatt = nullptr, *gf1 = nullptr, *glog = nullptr, *gtok = nullptr;
+    int cache_len = 0;
     std::vector<void *> allocs;
 };
 
@@ -104,7 +110,7 @@ struct LinWgrad {
 // ---------------------------------------------------------------- kernels
 __global__ void embed_fwd_kernel(const float *__restrict__ tokens, const float *__restrict__ tok,
                                  const float *__restrict__ pos, float *__restrict__ x, int N, int Ts, int D, int V,
-                                 int *__restrict__ err) {
+                                 int *__restrict__ err, int pos0 = 0) {
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (long long)N * D;
          i += (long long)gridDim.x * blockDim.x) {
         const int r = (int)(i / D), d = (int)(i % D);
@@ -113,7 +119,7 @@ __global__ void embed_fwd_kernel(const float *__restrict__ tokens, const float *
             if (err) atomicCAS(err, 0, 0x454d4244);   // "EMBD"
             id = 0;
         }
-        x[i] = tok[(size_t)id * D + d] + pos[(size_t)(r % Ts) * D + d];
+        x[i] = tok[(size_t)id * D + d] + pos[(size_t)(pos0 + r % Ts) * D + d];
     }
 }
 
@@ -284,6 +290,79 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const float *__restrict__
         for (int j = 0; j <= i0 + r; ++j) o += S[r * Ts + j] * Vs[j * (DH + 1) + d];
         out[((size_t)b * Ts + i0 + r) * D + h * DH + d] = o;
     }
+}
+
+// Generation: append the new rows' K and V (columns D..3D of qkv [rows][3D])
+// to one layer's caches [max_seq][D] at row `at` (Tensor::concatAlongRows of
+// MultiHeadAttention::forwardWithCache, src/Attention/MultiHeadAttention.php:105-112).
+__global__ void kv_append_kernel(const float *__restrict__ qkv, float *__restrict__ kc, float *__restrict__ vc,
+                                 int rows, int D, int at) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows * D; i += gridDim.x * blockDim.x) {
+        const int r = i / D, d = i % D;
+        kc[(size_t)(at + r) * D + d] = qkv[(size_t)r * 3 * D + D + d];
+        vc[(size_t)(at + r) * D + d] = qkv[(size_t)r * 3 * D + 2 * D + d];
+    }
+}
+
+// Generation attention for one (head, new row): scores against all `len`
+// cached keys, scaled by 1/sqrt(dh), row softmax, times the cached values --
+// attendHeadCached (src/Attention/MultiHeadAttention.php:127-137) applies NO
+// causal mask, so the rows of a multi-token prompt see each other both ways.
+// Shared memory: the len scores, 4 warps' partial outputs, the query row.
+// Fixed reduction order (deterministic).
+template <int DH>
+__global__ void __launch_bounds__(128) attn_cached_kernel(const float *__restrict__ qkv, const float *__restrict__ kc,
+                                                          const float *__restrict__ vc, float *__restrict__ out,
+                                                          int len, int D, float scale) {
+    extern __shared__ float sm[];
+    float *qs = sm, *part = qs + DH, *red = part + 4 * DH, *S = red + 8;
+    const int h = blockIdx.x, r = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x < DH) qs[threadIdx.x] = qkv[(size_t)r * 3 * D + h * DH + threadIdx.x];
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int j = threadIdx.x; j < len; j += blockDim.x) {
+        const float4 *k = reinterpret_cast<const float4 *>(kc + (size_t)j * D + h * DH);
+        float s = 0.0f;
+#pragma unroll
+        for (int c = 0; c < DH / 4; ++c) {
+            const float4 kv = k[c];
+            s += qs[4 * c] * kv.x;
+            s += qs[4 * c + 1] * kv.y;
+            s += qs[4 * c + 2] * kv.z;
+            s += qs[4 * c + 3] * kv.w;
+        }
+        s *= scale;
+        S[j] = s;
+        mx = fmaxf(mx, s);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    float sum = 0.0f;
+    for (int j = threadIdx.x; j < len; j += blockDim.x) {
+        const float e = expf(S[j] - mx);
+        S[j] = e;
+        sum += e;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) red[4 + warp] = sum;
+    __syncthreads();
+    sum = (red[4] + red[5]) + (red[6] + red[7]);
+    // o[d] = sum_j p_j v[j][d]: warp w takes keys w, w+4, ..., lane = d
+    for (int d0 = 0; d0 < DH; d0 += 32) {
+        float acc = 0.0f;
+        if (d0 + lane < DH)
+            for (int j = warp; j < len; j += 4) acc += (S[j] / sum) * vc[(size_t)j * D + h * DH + d0 + lane];
+        if (d0 + lane < DH) part[warp * DH + d0 + lane] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x < DH)
+        out[(size_t)r * D + h * DH + threadIdx.x] =
+            (part[threadIdx.x] + part[DH + threadIdx.x]) + (part[2 * DH + threadIdx.x] + part[3 * DH + threadIdx.x]);
 }
 
 // Attention backward for one (sequence, head):
@@ -608,6 +687,97 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
     return kOk;
 }
 
+namespace {
+
+int attn_smem_cached(int len) { return (int)((5 * 32 + 8 + (size_t)len) * sizeof(float)); }
+
+int lm_cache_alloc(LmEngine &e) {
+    if (!e.kc.empty()) return kOk;
+    const int T = e.T;
+    if (attn_smem_cached(T) > 227 * 1024)
+        return fail(kBadArg, "zilla_lm_forward_cached: max_seq %d above the supported 57900 for generation", T);
+    const size_t TD = (size_t)T * e.D;
+    int rc;
+    if ((rc = lalloc(e, &e.gx, TD)) || (rc = lalloc(e, &e.gxm, TD)) || (rc = lalloc(e, &e.gh, TD)) ||
+        (rc = lalloc(e, &e.gxh, TD)) || (rc = lalloc(e, &e.ginv, T)) || (rc = lalloc(e, &e.gqkv, 3 * TD)) ||
+        (rc = lalloc(e, &e.gatt, TD)) || (rc = lalloc(e, &e.gf1, (size_t)T * e.F)) ||
+        (rc = lalloc(e, &e.glog, (size_t)T * e.V)) || (rc = lalloc(e, &e.gtok, T)))
+        return rc;
+    std::vector<float *> kc(e.L), vc(e.L);
+    for (int l = 0; l < e.L; ++l)
+        if ((rc = lalloc(e, &kc[l], TD)) || (rc = lalloc(e, &vc[l], TD))) return rc;
+    if (cudaFuncSetAttribute(attn_cached_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             attn_smem_cached(T)) != cudaSuccess)
+        return check_cuda("zilla_lm_forward_cached: attention shared memory");
+    e.kc = kc;
+    e.vc = vc;
+    return kOk;
+}
+
+}  // namespace
+
+// TransformerLM::forwardWithCache (src/Transformers/TransformerLM.php:124-151):
+// `count` new tokens (host floats, Embedding's (int) cast) at positions
+// cache_len .. cache_len+count-1; per block TransformerBlock::forwardWithCache
+// (TransformerBlock.php:40-45) with the K/V rows appended to the layer's cache
+// and unmasked attention over all cached rows; logits [count, V] to the host.
+// The cache is unchanged when the call fails (the reference throws before it
+// advances the cache length).
+int lm_forward_cached(Net &n, const float *tokens, int count, float *logits) {
+    LmEngine &e = *n.lm;
+    const int D = e.D, F = e.F, V = e.V, L = e.L;
+    if (count <= 0 || !tokens) return fail(kBadArg, "zilla_lm_forward_cached: no tokens");
+    if (e.cache_len + count > e.T)
+        return fail(kBadArg, "zilla_lm_forward_cached: sequence position %d exceeds max %d", e.cache_len + count, e.T);
+    for (int i = 0; i < count; ++i) {   // Embedding::forward (src/NN/Layers/Embedding.php:44-48)
+        const float t = tokens[i];
+        if (!isfinite(t) || (int)t < 0 || (int)t >= V)
+            return fail(kBadArg, "zilla_lm_forward_cached: token id %g out of range [0, %d)", (double)t, V);
+    }
+    int rc;
+    if ((rc = lm_cache_alloc(e))) return rc;
+    const float *Pm = n.params;
+    const float scale = 1.0f / sqrtf((float)(D / e.H));
+    const int off = e.cache_len, len = off + count;
+    cudaMemcpyAsync(e.gtok, tokens, (size_t)count * sizeof(float), cudaMemcpyHostToDevice, stream());
+    embed_fwd_kernel<<<grid_for((long long)count * D, 256, 8), 256, 0, stream()>>>(
+        e.gtok, Pm + e.o_tok, Pm + e.o_pos, e.gx, count, count, D, V, device_error_word(), off);
+    ZB_LAUNCH_CHECK("lm generation embedding");
+    for (int l = 0; l < L; ++l) {
+        const auto &b = e.blk[l];
+        if ((rc = ln_fwd(e.gx, Pm + b.ln1g, Pm + b.ln1b, e.gh, e.gxh, e.ginv, count, D))) return rc;
+        LinFwd qkv{e.gh, nullptr, {Pm + b.qW, Pm + b.kW, Pm + b.vW}, {Pm + b.qb, Pm + b.kb, Pm + b.vb},
+                   e.gqkv, count, 3 * D, D, D, 3 * D, D, false};
+        if ((rc = run_simt_gemm(qkv, 1, "lm generation qkv"))) return rc;
+        kv_append_kernel<<<grid_for((long long)count * D, 256, 8), 256, 0, stream()>>>(e.gqkv, e.kc[l], e.vc[l],
+                                                                                     count, D, off);
+        ZB_LAUNCH_CHECK("lm generation kv append");
+        attn_cached_kernel<32><<<dim3(e.H, count), 128, attn_smem_cached(len), stream()>>>(
+            e.gqkv, e.kc[l], e.vc[l], e.gatt, len, D, scale);
+        ZB_LAUNCH_CHECK("lm generation attention");
+        LinFwd o{e.gatt, e.gx, {Pm + b.oW, nullptr, nullptr}, {Pm + b.ob, nullptr, nullptr}, e.gxm,
+                 count, D, D, D, D, D, false};
+        if ((rc = run_simt_gemm(o, 1, "lm generation out proj"))) return rc;
+        if ((rc = ln_fwd(e.gxm, Pm + b.ln2g, Pm + b.ln2b, e.gh, e.gxh, e.ginv, count, D))) return rc;
+        LinFwd f1{e.gh, nullptr, {Pm + b.f1W, nullptr, nullptr}, {Pm + b.f1b, nullptr, nullptr}, e.gf1,
+                  count, F, D, D, F, F, true};
+        if ((rc = run_simt_gemm(f1, 1, "lm generation fc1"))) return rc;
+        LinFwd f2{e.gf1, e.gxm, {Pm + b.f2W, nullptr, nullptr}, {Pm + b.f2b, nullptr, nullptr}, e.gx,
+                  count, D, F, F, D, D, false};
+        if ((rc = run_simt_gemm(f2, 1, "lm generation fc2"))) return rc;
+    }
+    if ((rc = ln_fwd(e.gx, Pm + e.o_lnf_g, Pm + e.o_lnf_b, e.gh, e.gxh, e.ginv, count, D))) return rc;
+    LinFwd head{e.gh, nullptr, {Pm + e.o_head_W, nullptr, nullptr}, {Pm + e.o_head_b, nullptr, nullptr}, e.glog,
+                count, V, D, D, V, V, false};
+    if ((rc = run_simt_gemm(head, 1, "lm generation head"))) return rc;
+    if (logits)
+        cudaMemcpyAsync(logits, e.glog, (size_t)count * V * sizeof(float), cudaMemcpyDeviceToHost, stream());
+    if (cudaStreamSynchronize(stream()) != cudaSuccess) return check_cuda("zilla_lm_forward_cached");
+    if ((rc = check_cuda("zilla_lm_forward_cached"))) return rc;
+    e.cache_len = len;
+    return kOk;
+}
+
 }  // namespace zb
 
 using namespace zb;
@@ -649,4 +819,23 @@ extern "C" int zilla_lm_create(int vocab, int dim, int heads, int layers, int ma
         return rc;
     }
     return net_register(n);
+}
+
+extern "C" int zilla_lm_cache_reset(int net) {
+    Net *n = net_get(net);
+    if (!n || !n->lm) return fail(kBadHandle, "zilla_lm_cache_reset: %d is not a language model", net);
+    n->lm->cache_len = 0;
+    return kOk;
+}
+
+extern "C" int zilla_lm_cache_length(int net) {
+    Net *n = net_get(net);
+    if (!n || !n->lm) return fail(kBadHandle, "zilla_lm_cache_length: %d is not a language model", net);
+    return n->lm->cache_len;
+}
+
+extern "C" int zilla_lm_forward_cached(int net, const float *tokens, int count, float *logits) {
+    Net *n = net_get(net);
+    if (!n || !n->lm) return fail(kBadHandle, "zilla_lm_forward_cached: %d is not a language model", net);
+    return lm_forward_cached(*n, tokens, count, logits);
 }

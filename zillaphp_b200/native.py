@@ -94,6 +94,9 @@ SIGNATURES: dict[str, tuple] = {
     "zilla_net_inspect": (I, [I, I, C.c_char_p, I, FP, UL]),
     "zilla_net_device_status": (I, [I]),
     "zilla_lm_create": (I, [I] * 8),
+    "zilla_lm_forward_cached": (I, [I, FP, I, FP]),
+    "zilla_lm_cache_reset": (I, [I]),
+    "zilla_lm_cache_length": (I, [I]),
     "zilla_dp_unique_id": (I, [C.c_char_p]),
     "zilla_dp_attach": (I, [I, I, I, C.c_char_p]),
     "zilla_dp_detach": (I, [I]),

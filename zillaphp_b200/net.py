@@ -191,6 +191,24 @@ class LM(Net):
         self.params_id = self.lib.zilla_net_params_id(self.id)
         self.grads_id = self.lib.zilla_net_grads_id(self.id)
 
+    def forward_cached(self, tokens) -> np.ndarray:
+        """TransformerLM::forwardWithCache: logits [len(tokens), vocab] for the
+        tokens at the next cache positions; the cache grows by len(tokens)."""
+        t = np.ascontiguousarray(tokens, np.float32).ravel()
+        out = np.empty((t.size, self.w.vocab), np.float32)
+        self._check(self.lib.zilla_lm_forward_cached(self.id, t.ctypes.data_as(native.FP), t.size,
+                                                     out.ctypes.data_as(native.FP)))
+        return out
+
+    def cache_reset(self) -> None:
+        self._check(self.lib.zilla_lm_cache_reset(self.id))
+
+    def cache_length(self) -> int:
+        n = int(self.lib.zilla_lm_cache_length(self.id))
+        if n < 0:
+            raise RuntimeError(native.last_error())
+        return n
+
 
 def dp_unique_id() -> bytes:
     lib = native.load()

@@ -255,9 +255,11 @@ NCU_DRAM_BYTES_PER_SAMPLE = {
 }
 
 
-def roofline(w, batch, seg_times: list[tuple[str, float]], steps: int, pk: dict, pk_kind: str, precision: int = 0):
+def roofline(w, batch, seg_times: list[tuple[str, float]], steps: int, pk: dict, pk_kind: str, precision: int = 0,
+             focus: tuple[int, list[float]] | None = None):
     """Dominant kernel group: the label with the largest total time; matched to
-    its algorithmic work in execution order."""
+    its algorithmic work in execution order.  With `focus` = (group, its
+    durations over the timed steps), that group's duration is taken from them."""
     # assign each measured segment to the work item of the same label, in order
     work = stage_work(w, batch)
     fwd = [x for x in work if x["label"].endswith("_fwd")]
@@ -276,8 +278,10 @@ def roofline(w, batch, seg_times: list[tuple[str, float]], steps: int, pk: dict,
     if not agg:
         return None, {}
     k_dom = max(agg, key=lambda k: sum(agg[k]))
-    item = order[k_dom]
     ms = sum(agg[k_dom]) / len(agg[k_dom])
+    if focus is not None and focus[1]:
+        k_dom, ms = focus[0], sum(focus[1]) / len(focus[1])
+    item = order[k_dom]
     breakdown = {f"{order[k].get('name', order[k]['label'])}#{k}": round(sum(v) / len(v), 4) for k, v in sorted(agg.items())}
     if item["flops"] > 0:
         achieved = item["flops"] / (ms * 1e-3) / 1e12
@@ -289,6 +293,7 @@ def roofline(w, batch, seg_times: list[tuple[str, float]], steps: int, pk: dict,
         r = {"bound": "hbm", "unit": "GB/s", "achieved": round(achieved, 1), "peak": peak}
     r["frac"] = round(r["achieved"] / r["peak"], 5)
     r["kernel"] = f"{item.get('name', item['label'])} (group {k_dom} of the step)"
+    r["group"] = k_dom
     r["ms_per_launch"] = round(ms, 4)
     r["peak_source"] = pk_kind
     per_sample = NCU_DRAM_BYTES_PER_SAMPLE.get(item.get("name", "")) if precision == 1 else None
@@ -461,8 +466,37 @@ def main():
         for s in range(2 * nb):
             net.step_dev(xs_dev[s % nb], ys_dev[s % nb], loss_id)
 
+    # ---- the step's segments (an untimed profiled pass): the breakdown and the
+    # dominant group, whose two boundaries alone carry events in the timed region
+    focus_seg, focus_label, breakdown_pass = None, None, []
+    if not args.graph:
+        net.profile(True)
+        for s in range(3):
+            net.step_dev(xs_dev[s % nb], ys_dev[s % nb], loss_id)
+        breakdown_pass = net.timings()
+        net.profile(False)
+        if rank == 0:
+            r0, _ = roofline(w, b, breakdown_pass, 3, {}, "", precision)
+            k_dom = r0["group"] if r0 else None
+        else:
+            k_dom = None
+        if world > 1:
+            obj = [k_dom]
+            dist.broadcast_object_list(obj, src=0)
+            k_dom = obj[0]
+        if k_dom is not None:   # index of that group in the unfiltered segment list of one step
+            seen = 0
+            for j, (lab, _) in enumerate(breakdown_pass):
+                if lab == "allreduce":
+                    continue
+                if seen == k_dom:
+                    focus_seg, focus_label = j, lab
+                    break
+                seen += 1
+
     # ---- device-resident timed region
-    net.profile(not args.graph)
+    if focus_seg is not None:
+        net.profile_segment(focus_seg)
     sampler = ClockSampler(local)
     sampler.start()
     barrier()
@@ -476,7 +510,7 @@ def main():
     clocks = sampler.stop()
     launches = lib.zilla_launch_count() - l0
     ms = e0.elapsed_time(e1)
-    segs = net.timings()
+    focus_ms = [t for lab, t in net.timings() if lab == focus_label] if focus_seg is not None else []
     net.profile(False)
     t = torch.tensor([ms], device="cuda")
     if world > 1:
@@ -507,7 +541,11 @@ def main():
 
     if rank == 0:
         pk, pk_kind = peaks()
-        roof, breakdown = roofline(w, b, segs, args.steps, pk, pk_kind, precision)
+        roof, breakdown = roofline(w, b, breakdown_pass, args.steps, pk, pk_kind, precision,
+                                   focus=(k_dom, focus_ms) if focus_seg is not None else None)
+        if roof and focus_seg is not None:
+            roof["timing"] = (f"CUDA events at the two boundaries of this group only, every timed step "
+                              f"({len(focus_ms)} launches); segments_ms from an untimed profiled pass of 3 steps")
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             r = cpu_reference(w, sample=64, min_seconds=10.0, max_steps=50)

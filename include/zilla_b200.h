@@ -249,6 +249,12 @@ int zilla_net_set_graph(int net, int enable);
  * zilla_net_timings then returns, for the last step, up to max_segments
  * durations in ms and their labels ('\n'-separated) and the segment count. */
 int zilla_net_profile(int net, int enable);
+/* Profiling of ONE segment: events only at the two boundaries of segment
+ * `segment` (its index in zilla_net_timings' list of a fully profiled step),
+ * so the step's other kernel boundaries carry no event.  zilla_net_timings
+ * then returns that segment's duration once per step.  zilla_net_profile
+ * (net, 0 or 1) ends it. */
+int zilla_net_profile_segment(int net, int segment);
 int zilla_net_timings(int net, char *labels, int labels_len, float *ms, int max_segments);
 /* Diagnostics.  zilla_net_inspect returns the element count of the engine's
  * intermediate tensor `index` (0 past the last one), writes its name and,

@@ -224,6 +224,14 @@ void free_net(Net *n) {
 
 void prof_mark(Net &n, const char *label) {
     if (!n.profile) return;
+    if (n.prof_focus >= 0) {
+        // Only the marks that bound segment prof_focus: the one before it is
+        // recorded as a "start" (zilla_net_timings skips the gap up to it), so
+        // every other kernel boundary of the step stays free of events.
+        const int idx = strcmp(label, "start") ? ++n.prof_idx : (n.prof_idx = 0);
+        if (idx == n.prof_focus) label = "start";
+        else if (idx != n.prof_focus + 1) return;
+    }
     if (n.ev_used >= (int)n.ev_pool.size()) {
         cudaEvent_t e;
         if (cudaEventCreate(&e) != cudaSuccess) { cudaGetLastError(); return; }
@@ -766,6 +774,18 @@ int zilla_net_profile(int id, int enable) {
     Net *n = net_get(id);
     if (!n) return fail(kBadHandle, "zilla_net_profile: unknown net %d", id);
     n->profile = enable != 0;
+    n->prof_focus = -1;
+    n->ev_used = 0;
+    return kOk;
+}
+
+int zilla_net_profile_segment(int id, int segment) {
+    Net *n = net_get(id);
+    if (!n) return fail(kBadHandle, "zilla_net_profile_segment: unknown net %d", id);
+    if (segment < 0) return fail(kBadArg, "zilla_net_profile_segment: segment %d", segment);
+    n->profile = true;
+    n->prof_focus = segment;
+    n->prof_idx = 0;
     n->ev_used = 0;
     return kOk;
 }

@@ -102,6 +102,8 @@ struct Net {
     long long x_floats = 0, y_floats = 0;   // per-step input sizes (floats)
     // per-segment device timing (zilla_net_profile / zilla_net_timings)
     bool profile = false;
+    int prof_focus = -1;   // >= 0: events only around this segment (zilla_net_profile_segment)
+    int prof_idx = 0;      // marks since the step's "start" mark
     std::vector<cudaEvent_t> ev_pool;
     std::vector<const char *> ev_label;   // label of the segment ending at event i
     int ev_used = 0;

@@ -90,6 +90,7 @@ SIGNATURES: dict[str, tuple] = {
     "zilla_net_load": (I, [I, C.c_char_p]),
     "zilla_net_step_staged": (I, [I, FP, I]),
     "zilla_net_profile": (I, [I, I]),
+    "zilla_net_profile_segment": (I, [I, I]),
     "zilla_net_timings": (I, [I, C.c_char_p, I, FP, I]),
     "zilla_net_inspect": (I, [I, I, C.c_char_p, I, FP, UL]),
     "zilla_net_device_status": (I, [I]),

@@ -125,6 +125,10 @@ class Net:
     def profile(self, enable: bool = True) -> None:
         self._check(self.lib.zilla_net_profile(self.id, int(enable)))
 
+    def profile_segment(self, segment: int) -> None:
+        """Time only segment `segment` of each step (zilla_net_profile_segment)."""
+        self._check(self.lib.zilla_net_profile_segment(self.id, segment))
+
     def timings(self) -> list[tuple[str, float]]:
         """(label, ms) of each kernel group of the last profiled step."""
         labels = C.create_string_buffer(8192)

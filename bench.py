@@ -376,6 +376,8 @@ def main():
     ap.add_argument("--graph", action="store_true",
                     help="replay each step from a CUDA graph (zilla_net_set_graph); the timed region then "
                          "runs without per-segment events, so no roofline")
+    ap.add_argument("--autograd", action="store_true",
+                    help="time the batched autograd bridge (Tensor/Sequential/Trainer, one device call per op)")
     ap.add_argument("--batch", type=int, default=None,
                     help="global batch override (small cases for ncu captures; default: the workload's)")
     args = ap.parse_args()
@@ -424,6 +426,8 @@ def main():
     assert stream.cuda_stream != 0
     lib.zilla_set_stream(stream.cuda_stream)
 
+    if args.autograd:
+        return main_autograd(args, w, stream, lib)
     precision = w.precision if args.precision is None else args.precision
     if w.batch % world:
         raise SystemExit("global batch must divide by the number of GPUs")
@@ -576,6 +580,56 @@ def main():
     lib.zilla_set_stream(None)
     if world > 1:
         dist.destroy_process_group()
+
+
+def main_autograd(args, w, stream, lib):
+    """One Trainer step of the batched autograd bridge per timed step: zeroGrad,
+    forward, CrossEntropy, backward, optimizer step, loss.item() (the host read
+    of Trainer::fitLoader), every op one device call (fp32 engine kernels)."""
+    import torch
+    from zillaphp_b200 import autograd as ag
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("--autograd runs on one GPU")
+    model = ag.sequential_from_spec(w.layers, w.in_shape)
+    model.load_flat(synthetic.init_params(w))
+    if w.optimizer == configs.ADAM:
+        b1, b2, eps = w.adam
+        opt = ag.Adam(model.parameters(), w.lr, b1, b2, eps)
+    else:
+        opt = ag.SGD(model.parameters(), w.lr)
+    trainer = ag.Trainer(model, opt, ag.CrossEntropy())
+    nb = 8
+    xs, ys = [], []
+    for j in range(nb):
+        x, y = synthetic.batch(w, w.batch, seed=1234, step=j)
+        xs.append(ag.Tensor.from_numpy(x.reshape((w.batch,) + tuple(w.in_shape))))
+        ys.append(ag.Tensor.from_numpy(y))
+    for s in range(args.warmup):
+        trainer.step(xs[s % nb], ys[s % nb])
+    sampler = ClockSampler(0)
+    sampler.start()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = lib.zilla_launch_count()
+    e0.record(stream)
+    for s in range(args.steps):
+        trainer.step(xs[s % nb], ys[s % nb])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    launches = lib.zilla_launch_count() - l0
+    ms = e0.elapsed_time(e1)
+    value = w.batch * args.steps / (ms / 1e3)
+    print(json.dumps({
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": w.name, "global_batch": w.batch, "path": "batched autograd bridge (Trainer.step)",
+                   "optimizer": "adam" if w.optimizer == configs.ADAM else "sgd",
+                   "l2": "8 distinct device-resident input batches rotated", "notes": w.notes},
+        "gpu_launches": int(launches), "launches_per_step": launches / args.steps,
+        "roofline": None, "cpu_baseline": None, "clocks": clocks}))
+    lib.zilla_set_stream(None)
 
 
 def lm_cpu_reference(w, batch: int, min_seconds: float, max_steps: int):

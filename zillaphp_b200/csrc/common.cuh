@@ -56,6 +56,28 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
     return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// Division by a divisor fixed at launch, as a multiply and a shift
+// (Granlund and Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994, Theorem 4.2 with N = 31): for 1 <= d < 2^31,
+// l = ceil(log2 d) and m = ceil(2^(31+l) / d), floor(n / d) equals
+// (n * m) >> (31 + l) for every 0 <= n < 2^31, and m < 2^32.  The index
+// arithmetic of the gather functors below stays in [0, 2^31).
+struct FastDiv {
+    unsigned d = 1, m = 0x80000000u;
+    int sh = 31;
+    FastDiv() = default;
+    explicit FastDiv(int div) {
+        d = div > 0 ? (unsigned)div : 1u;
+        int l = 0;
+        while ((1ull << l) < d) ++l;
+        sh = 31 + l;
+        m = (unsigned)(((1ull << sh) + d - 1) / d);
+    }
+    __host__ __device__ __forceinline__ int div(int n) const {
+        return (int)(((unsigned long long)(unsigned)n * m) >> sh);
+    }
+};
+
 // Grid size helper: enough blocks to cover n with `threads` each, capped to
 // a multiple of the SM count x `per_sm` (grid-stride loops cover the rest).
 int grid_for(long long n, int threads, int per_sm = 8);

@@ -47,6 +47,12 @@ struct GemmNT {
 
 struct ConvGeom {
     int B, C, H, W, oC, oH, oW, kH, kW, s, p;
+    // divisors of the index decompositions: output plane, output row, input
+    // plane, input row, taps, tap row
+    FastDiv f_ohw, f_ow, f_hw, f_w, f_kk, f_kw;
+    ConvGeom(int B_, int C_, int H_, int W_, int oC_, int oH_, int oW_, int kH_, int kW_, int s_, int p_)
+        : B(B_), C(C_), H(H_), W(W_), oC(oC_), oH(oH_), oW(oW_), kH(kH_), kW(kW_), s(s_), p(p_),
+          f_ohw(oH_ * oW_), f_ow(oW_), f_hw(H_ * W_), f_w(W_), f_kk(kH_ * kW_), f_kw(kW_) {}
 };
 
 // Forward: M = B*oH*oW output pixels, N = oC, K = C*kH*kW taps.
@@ -69,8 +75,8 @@ struct ConvFwdF32 {
           M(B * oH * oW), N(oC), K(C * kH * kW), relu(relu_) {}
     __device__ float a(int m, int k) const {
         const int hw = g.oH * g.oW, kk = g.kH * g.kW;
-        const int b = m / hw, r = m - b * hw, oh = r / g.oW, ow = r - oh * g.oW;
-        const int c = k / kk, t = k - c * kk, dh = t / g.kW, dw = t - dh * g.kW;
+        const int b = g.f_ohw.div(m), r = m - b * hw, oh = g.f_ow.div(r), ow = r - oh * g.oW;
+        const int c = g.f_kk.div(k), t = k - c * kk, dh = g.f_kw.div(t), dw = t - dh * g.kW;
         const int ih = oh * g.s - g.p + dh, iw = ow * g.s - g.p + dw;
         if ((unsigned)ih >= (unsigned)g.H || (unsigned)iw >= (unsigned)g.W) return 0.0f;
         return x[(((size_t)b * g.C + c) * g.H + ih) * g.W + iw];
@@ -78,7 +84,7 @@ struct ConvFwdF32 {
     __device__ float b(int k, int n) const { return w[(size_t)n * K + k]; }
     __device__ void store(int m, int n, float v) const {
         const int hw = g.oH * g.oW;
-        const int b = m / hw, r = m - b * hw;
+        const int b = g.f_ohw.div(m), r = m - b * hw;
         float o = v;
         if (relu) o = o > 0.0f ? o : 0.0f;
         y[((size_t)b * g.oC + n) * hw + r] = o;
@@ -104,8 +110,8 @@ struct ConvDgradF32 {
           M(B * H * W), N(C), K(oC * kH * kW) {}
     __device__ float a(int m, int k) const {
         const int hw = g.H * g.W, kk = g.kH * g.kW;
-        const int b = m / hw, r = m - b * hw, ih = r / g.W, iw = r - ih * g.W;
-        const int oc = k / kk, t = k - oc * kk, dh = t / g.kW, dw = t - dh * g.kW;
+        const int b = g.f_hw.div(m), r = m - b * hw, ih = g.f_w.div(r), iw = r - ih * g.W;
+        const int oc = g.f_kk.div(k), t = k - oc * kk, dh = g.f_kw.div(t), dw = t - dh * g.kW;
         const int ohn = ih + g.p - dh, own = iw + g.p - dw;
         if (ohn < 0 || own < 0) return 0.0f;
         if (g.s != 1 && (ohn % g.s || own % g.s)) return 0.0f;
@@ -115,12 +121,12 @@ struct ConvDgradF32 {
     }
     __device__ float b(int k, int n) const {
         const int kk = g.kH * g.kW;
-        const int oc = k / kk, t = k - oc * kk;
+        const int oc = g.f_kk.div(k), t = k - oc * kk;
         return w[((size_t)oc * g.C + n) * kk + t];
     }
     __device__ void store(int m, int n, float v) const {
         const int hw = g.H * g.W;
-        const int b = m / hw, r = m - b * hw;
+        const int b = g.f_hw.div(m), r = m - b * hw;
         const size_t at = ((size_t)b * g.C + n) * hw + r;
         if (mask) v = mask[at] > 0.0f ? v : 0.0f;
         dx[at] = v;
@@ -142,15 +148,15 @@ struct ConvWgradF32 {
           M(oC), N(C * kH * kW + 1), K(B * oH * oW) {}
     __device__ float a(int m, int k) const {
         const int hw = g.oH * g.oW;
-        const int b = k / hw, r = k - b * hw;
+        const int b = g.f_ohw.div(k), r = k - b * hw;
         return gout[((size_t)b * g.oC + m) * hw + r];
     }
     __device__ float b(int k, int n) const {
         const int kk = g.kH * g.kW;
         if (n == N - 1) return 1.0f;
         const int hw = g.oH * g.oW;
-        const int b = k / hw, r = k - b * hw, oh = r / g.oW, ow = r - oh * g.oW;
-        const int c = n / kk, t = n - c * kk, dh = t / g.kW, dwi = t - dh * g.kW;
+        const int b = g.f_ohw.div(k), r = k - b * hw, oh = g.f_ow.div(r), ow = r - oh * g.oW;
+        const int c = g.f_kk.div(n), t = n - c * kk, dh = g.f_kw.div(t), dwi = t - dh * g.kW;
         const int ih = oh * g.s - g.p + dh, iw = ow * g.s - g.p + dwi;
         if ((unsigned)ih >= (unsigned)g.H || (unsigned)iw >= (unsigned)g.W) return 0.0f;
         return x[(((size_t)b * g.C + c) * g.H + ih) * g.W + iw];

@@ -54,6 +54,13 @@ struct LmEngine {
 namespace {
 
 // ---------------------------------------------------------------- GEMM problems
+// Segment s of a 3-way operand list, by selects (a runtime index into the
+// parameter arrays would copy them to local memory).
+__device__ __forceinline__ const float *seg3(const float *const (&p)[3], int s) {
+    return s == 0 ? p[0] : s == 1 ? p[1] : p[2];
+}
+__device__ __forceinline__ float *seg3(float *const (&p)[3], int s) { return s == 0 ? p[0] : s == 1 ? p[1] : p[2]; }
+
 // Y[m, n] = sum_k X[m*ldx + k] W_s[k*sw + (n - s*sw)] + b_s[n - s*sw]  (s = n / sw)
 //           [+ R[m*ldy + n]] [relu]
 struct LinFwd {
@@ -65,10 +72,10 @@ struct LinFwd {
     static constexpr bool kAMFast = false, kBNFast = true, kExactOrder = false;
     __device__ float init(int, int) const { return 0.0f; }
     __device__ float a(int m, int k) const { return X[(size_t)m * ldx + k]; }
-    __device__ float b(int k, int n) const { const int s = n / sw; return W[s][(size_t)k * sw + (n - s * sw)]; }
+    __device__ float b(int k, int n) const { const int s = n / sw; return seg3(W, s)[(size_t)k * sw + (n - s * sw)]; }
     __device__ void store(int m, int n, float v) const {
         const int s = n / sw;
-        float o = v + Bv[s][n - s * sw];
+        float o = v + seg3(Bv, s)[n - s * sw];
         if (R) o += R[(size_t)m * ldy + n];
         if (relu) o = o > 0.0f ? o : 0.0f;
         Y[(size_t)m * ldy + n] = o;
@@ -84,7 +91,7 @@ struct LinDgrad {
     static constexpr bool kAMFast = false, kBNFast = false, kExactOrder = false;
     __device__ float init(int, int) const { return 0.0f; }
     __device__ float a(int m, int k) const { return dY[(size_t)m * ldy + k]; }
-    __device__ float b(int k, int n) const { const int s = k / sw; return W[s][(size_t)n * sw + (k - s * sw)]; }
+    __device__ float b(int k, int n) const { const int s = k / sw; return seg3(W, s)[(size_t)n * sw + (k - s * sw)]; }
     __device__ void store(int m, int n, float v) const {
         const size_t at = (size_t)m * ldx + n;
         if (mask && !(mask[at] > 0.0f)) v = 0.0f;
@@ -103,7 +110,7 @@ struct LinWgrad {
     __device__ float b(int k, int n) const { return dY[(size_t)k * ldy + n]; }
     __device__ void store(int m, int n, float v) const {
         const int s = n / sw;
-        dW[s][(size_t)m * sw + (n - s * sw)] = v;
+        seg3(dW, s)[(size_t)m * sw + (n - s * sw)] = v;
     }
 };
 

@@ -55,7 +55,8 @@ namespace {
 
 // ---------------------------------------------------------------- GEMM problems
 // Segment s of a 3-way operand list, by selects (a runtime index into the
-// parameter arrays would copy them to local memory).
+// parameter arrays would copy them to local memory).  Columns span at most
+// three segments of width sw, so s = (c >= sw) + (c >= 2 sw) needs no division.
 __device__ __forceinline__ const float *seg3(const float *const (&p)[3], int s) {
     return s == 0 ? p[0] : s == 1 ? p[1] : p[2];
 }
@@ -72,9 +73,9 @@ struct LinFwd {
     static constexpr bool kAMFast = false, kBNFast = true, kExactOrder = false;
     __device__ float init(int, int) const { return 0.0f; }
     __device__ float a(int m, int k) const { return X[(size_t)m * ldx + k]; }
-    __device__ float b(int k, int n) const { const int s = n / sw; return seg3(W, s)[(size_t)k * sw + (n - s * sw)]; }
+    __device__ float b(int k, int n) const { const int s = (n >= sw) + (n >= 2 * sw); return seg3(W, s)[(size_t)k * sw + (n - s * sw)]; }
     __device__ void store(int m, int n, float v) const {
-        const int s = n / sw;
+        const int s = (n >= sw) + (n >= 2 * sw);
         float o = v + seg3(Bv, s)[n - s * sw];
         if (R) o += R[(size_t)m * ldy + n];
         if (relu) o = o > 0.0f ? o : 0.0f;
@@ -91,7 +92,7 @@ struct LinDgrad {
     static constexpr bool kAMFast = false, kBNFast = false, kExactOrder = false;
     __device__ float init(int, int) const { return 0.0f; }
     __device__ float a(int m, int k) const { return dY[(size_t)m * ldy + k]; }
-    __device__ float b(int k, int n) const { const int s = k / sw; return seg3(W, s)[(size_t)n * sw + (k - s * sw)]; }
+    __device__ float b(int k, int n) const { const int s = (k >= sw) + (k >= 2 * sw); return seg3(W, s)[(size_t)n * sw + (k - s * sw)]; }
     __device__ void store(int m, int n, float v) const {
         const size_t at = (size_t)m * ldx + n;
         if (mask && !(mask[at] > 0.0f)) v = 0.0f;
@@ -109,7 +110,7 @@ struct LinWgrad {
     __device__ float a(int m, int k) const { return X[(size_t)k * ldx + m]; }
     __device__ float b(int k, int n) const { return dY[(size_t)k * ldy + n]; }
     __device__ void store(int m, int n, float v) const {
-        const int s = n / sw;
+        const int s = (n >= sw) + (n >= 2 * sw);
         seg3(dW, s)[(size_t)m * sw + (n - s * sw)] = v;
     }
 };

@@ -10,6 +10,9 @@
 //     implicit GEMMs on NCHW tensors (no im2col buffer),
 //   maxpool2d_batched_fwd_dev / _bwd_dev (native/cuda/pooling_batched.cu:
 //     61-116) and maxpool2d_fwd_dev / _bwd_dev (native/cuda/pooling.cu:67-124).
+#include <stdlib.h>
+#include <string.h>
+
 #include "conv_pool_f32.cuh"
 
 using namespace zb;
@@ -36,6 +39,164 @@ float *gemm_workspace(size_t floats) {
         g_ws_cap = floats;
     }
     return g_ws;
+}
+
+// Direct weight gradient of a 3x3 stride-1 convolution (fp32, NCHW), for
+// 16-channel x 32-filter tiles.  The reduction runs over the B*oH rows
+// (b, oh): each block takes a contiguous range of rows and, per row, stages
+// in shared memory the 32 filters' gradient rows gout[b][oc][oh][:] and the 16
+// channels' three input rows x[b][c][oh-p+kh][:] (zero-padded), then every
+// thread accumulates 2 filters x 1 channel x 9 taps along the row with a
+// sliding 3-wide window, 18 FMAs per 5 shared-memory loads.  The next row's
+// values are loaded into registers while the current row is computed.  Block
+// partials go to the split-K workspace in the layout of ConvWgradF32 ([split]
+// [oC][C*9 + 1], the last column the bias), which simt_gemm_reduce_kernel
+// sums in split order and stores (deterministic).
+constexpr int kDwOct = 32, kDwCt = 16, kDwMaxLoads = 24;
+
+struct DirectWgradArgs {
+    const float *x, *gout;
+    float *ws;
+    int B, C, H, W, oC, oH, oW, p;
+    int Wp, XS, NG, NX;              // padded row, channel stride in Xs, staged counts
+    int rows, splits, ctiles;
+    FastDiv f_ow, f_rowX, f_Wp, f_oH;  // oW, 3*Wp, Wp, oH
+};
+
+__global__ void __launch_bounds__(256) conv3x3_wgrad_direct_kernel(const __grid_constant__ DirectWgradArgs A) {
+    extern __shared__ float dsm[];
+    float *Gs = dsm, *Xs = dsm + kDwOct * A.oW;
+    const int tid = threadIdx.x;
+    const int z = blockIdx.x;
+    const int ct = blockIdx.y % A.ctiles, ot = blockIdx.y / A.ctiles;
+    const int c0 = ct * kDwCt, oc0 = ot * kDwOct;
+    const int cl = tid % kDwCt, ol = tid / kDwCt;   // channel, first of two filters (ol, ol + 16)
+    const long long r_lo = (long long)A.rows * z / A.splits, r_hi = (long long)A.rows * (z + 1) / A.splits;
+    const int nload = A.NG + A.NX;
+
+    float pre[kDwMaxLoads];
+    auto load_row = [&](int rr) {
+        const int b = A.f_oH.div(rr), oh = rr - b * A.oH;
+#pragma unroll
+        for (int i = 0; i < kDwMaxLoads; ++i) {
+            const int idx = tid + i * 256;
+            float v = 0.0f;
+            if (idx < A.NG) {
+                const int o = A.f_ow.div(idx), ow = idx - o * A.oW;
+                v = A.gout[(((size_t)b * A.oC + oc0 + o) * A.oH + oh) * A.oW + ow];
+            } else if (idx < nload) {
+                const int i2 = idx - A.NG;
+                const int c = A.f_rowX.div(i2), rem = i2 - c * 3 * A.Wp;
+                const int kh = A.f_Wp.div(rem), jp = rem - kh * A.Wp;
+                const int ih = oh - A.p + kh, iw = jp - A.p;
+                if ((unsigned)ih < (unsigned)A.H && (unsigned)iw < (unsigned)A.W)
+                    v = A.x[(((size_t)b * A.C + c0 + c) * A.H + ih) * A.W + iw];
+            }
+            pre[i] = v;
+        }
+    };
+    auto store_row = [&]() {
+#pragma unroll
+        for (int i = 0; i < kDwMaxLoads; ++i) {
+            const int idx = tid + i * 256;
+            if (idx < A.NG) {
+                Gs[idx] = pre[i];
+            } else if (idx < nload) {
+                const int i2 = idx - A.NG;
+                const int c = A.f_rowX.div(i2);
+                Xs[c * A.XS + (i2 - c * 3 * A.Wp)] = pre[i];
+            }
+        }
+    };
+
+    float acc[2][9];
+#pragma unroll
+    for (int o = 0; o < 2; ++o)
+#pragma unroll
+        for (int t = 0; t < 9; ++t) acc[o][t] = 0.0f;
+    float bacc[2] = {0.0f, 0.0f};
+    const bool do_bias = ct == 0 && cl == 0;
+
+    if (r_lo < r_hi) load_row((int)r_lo);
+    for (long long rr = r_lo; rr < r_hi; ++rr) {
+        __syncthreads();            // the previous row's reads of Gs / Xs are done
+        store_row();
+        __syncthreads();
+        if (rr + 1 < r_hi) load_row((int)rr + 1);
+        const float *g0 = Gs + ol * A.oW, *g1 = Gs + (ol + 16) * A.oW;
+        const float *xr = Xs + cl * A.XS;
+        float w[3][3];
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh) {
+            w[kh][1] = xr[kh * A.Wp];
+            w[kh][2] = xr[kh * A.Wp + 1];
+        }
+        for (int ow = 0; ow < A.oW; ++ow) {
+#pragma unroll
+            for (int kh = 0; kh < 3; ++kh) {
+                w[kh][0] = w[kh][1];
+                w[kh][1] = w[kh][2];
+                w[kh][2] = xr[kh * A.Wp + ow + 2];
+            }
+            const float ga = g0[ow], gb = g1[ow];
+#pragma unroll
+            for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+                for (int kw = 0; kw < 3; ++kw) {
+                    acc[0][kh * 3 + kw] = fmaf(ga, w[kh][kw], acc[0][kh * 3 + kw]);
+                    acc[1][kh * 3 + kw] = fmaf(gb, w[kh][kw], acc[1][kh * 3 + kw]);
+                }
+            if (do_bias) {
+                bacc[0] += ga;
+                bacc[1] += gb;
+            }
+        }
+    }
+    const int N = A.C * 9 + 1;
+#pragma unroll
+    for (int o = 0; o < 2; ++o) {
+        const int oc = oc0 + ol + 16 * o;
+        float *row = A.ws + ((size_t)z * A.oC + oc) * N;
+#pragma unroll
+        for (int t = 0; t < 9; ++t) row[(c0 + cl) * 9 + t] = acc[o][t];
+        if (do_bias) row[N - 1] = bacc[o];
+    }
+}
+
+int run_conv_wgrad(const ConvWgradF32 &pw, const char *what) {
+    const ConvGeom &g = pw.g;
+    static const bool force_gemm = [] {
+        const char *e = getenv("ZB_FP32_WGRAD");
+        return e && !strcmp(e, "gemm");
+    }();
+    const int Wp = g.W + 2 * g.p;
+    const int XS = (3 * Wp) | 1;   // odd channel stride: 16 channels on 16 banks
+    const int NG = kDwOct * g.oW, NX = kDwCt * 3 * Wp;
+    const size_t smem = (size_t)(NG + kDwCt * XS) * sizeof(float);
+    const bool fits = g.kH == 3 && g.kW == 3 && g.s == 1 && g.p >= 0 && g.p <= 2 && g.C % kDwCt == 0 &&
+                      g.oC % kDwOct == 0 && g.oW >= 1 && g.oH >= 1 && NG + NX <= kDwMaxLoads * 256 &&
+                      smem <= 48 * 1024 && (long long)g.B * g.oH < (1LL << 31);
+    if (force_gemm || !fits) return run_simt_gemm(pw, 0, what);
+    DirectWgradArgs A;
+    A.x = pw.x; A.gout = pw.gout;
+    A.B = g.B; A.C = g.C; A.H = g.H; A.W = g.W; A.oC = g.oC; A.oH = g.oH; A.oW = g.oW; A.p = g.p;
+    A.Wp = Wp; A.XS = XS; A.NG = NG; A.NX = NX;
+    A.rows = g.B * g.oH;
+    A.ctiles = g.C / kDwCt;
+    const int tiles = A.ctiles * (g.oC / kDwOct);
+    int splits = 4 * sm_count() / tiles;
+    if (splits < 1) splits = 1;
+    if (splits > A.rows) splits = A.rows > 0 ? A.rows : 1;
+    A.splits = splits;
+    A.f_ow = FastDiv(g.oW); A.f_rowX = FastDiv(3 * Wp); A.f_Wp = FastDiv(Wp); A.f_oH = FastDiv(g.oH);
+    A.ws = gemm_workspace((size_t)splits * pw.M * pw.N);
+    if (!A.ws) return fail(kBadHandle, "%s: weight-gradient workspace allocation failed", what);
+    conv3x3_wgrad_direct_kernel<<<dim3(splits, tiles), 256, smem, stream()>>>(A);
+    ZB_LAUNCH_CHECK(what);
+    simt_gemm_reduce_kernel<ConvWgradF32><<<grid_for((long long)pw.M * pw.N, 256), 256, 0, stream()>>>(pw, A.ws,
+                                                                                                      splits);
+    ZB_LAUNCH_CHECK(what);
+    return kOk;
 }
 
 // ---------------------------------------------------------------- pooling
@@ -126,7 +287,7 @@ int conv_bwd(int in_id, int w_id, int go_id, int gi_id, int gw_id, int gb_id, in
     int rc = run_simt_gemm(pd, 1, name);
     if (rc) return rc;
     ConvWgradF32 pw(x, go, gw, gb, B, C, H, W, oC, oH, oW, kH, kW, stride, pad);
-    return run_simt_gemm(pw, 0, name);
+    return run_conv_wgrad(pw, name);
 }
 
 int pool_fwd(int in_id, int out_id, int arg_id, int B, int C, int H, int W, int oH, int oW,

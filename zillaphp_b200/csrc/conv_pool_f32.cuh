@@ -167,4 +167,9 @@ struct ConvWgradF32 {
     }
 };
 
+// dW, db of a ConvWgradF32 problem: the direct kernel when the shape fits
+// (3x3, stride 1, C % 16 == 0, oC % 32 == 0, one row's operands in 24 loads
+// per thread), else the implicit GEMM.  ZB_FP32_WGRAD=gemm forces the GEMM.
+int run_conv_wgrad(const ConvWgradF32 &pw, const char *what);
+
 }  // namespace zb

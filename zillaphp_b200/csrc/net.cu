@@ -344,7 +344,7 @@ int fp32_backward(Net &n, const float *x) {
             }
             ConvWgradF32 pw(in, g, n.grads + s.poff, n.grads + s.poff + s.pn_w, B, s.C, s.H, s.W, s.oC,
                             s.oH, s.oW, 3, 3, 1, s.pad);
-            rc = run_simt_gemm(pw, 0, "net conv wgrad");
+            rc = run_conv_wgrad(pw, "net conv wgrad");
             break;
         }
         case kLinear: {

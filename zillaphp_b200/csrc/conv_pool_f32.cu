@@ -52,7 +52,7 @@ float *gemm_workspace(size_t floats) {
 // partials go to the split-K workspace in the layout of ConvWgradF32 ([split]
 // [oC][C*9 + 1], the last column the bias), which simt_gemm_reduce_kernel
 // sums in split order and stores (deterministic).
-constexpr int kDwOct = 32, kDwCt = 16, kDwMaxLoads = 24;
+constexpr int kDwOct = 32, kDwCt = 16, kDwMaxLoads = 16;
 
 struct DirectWgradArgs {
     const float *x, *gout;
@@ -63,7 +63,7 @@ struct DirectWgradArgs {
     FastDiv f_ow, f_rowX, f_Wp, f_oH;  // oW, 3*Wp, Wp, oH
 };
 
-__global__ void __launch_bounds__(256) conv3x3_wgrad_direct_kernel(const __grid_constant__ DirectWgradArgs A) {
+__global__ void __launch_bounds__(256, 3) conv3x3_wgrad_direct_kernel(const __grid_constant__ DirectWgradArgs A) {
     extern __shared__ float dsm[];
     float *Gs = dsm, *Xs = dsm + kDwOct * A.oW;
     const int tid = threadIdx.x;

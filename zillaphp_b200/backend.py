@@ -6,7 +6,7 @@ C function of the same name and raises ``RuntimeError("<fn> failed.")`` when it
 returns non-zero; ``bufferAlloc`` raises on a negative handle, ``bufferFree`` is
 a no-op for invalid handles.  Host arrays are numpy float32 arrays (PHP float
 arrays in the reference).  This is the interface the parity tests drive; a
-PHP host binds the same C functions through FFI::cdef (INTEGRATION.md).
+PHP host binds the same C functions through FFI::cdef.
 """
 from __future__ import annotations
 

@@ -39,7 +39,8 @@ def make(w, flat):
     return model, ag.Trainer(model, opt, ag.CrossEntropy())
 
 
-@pytest.mark.parametrize("name,batch", [("mlp_784_128_10", 8), ("cnn_1x8_pool_fc", 6), ("large_cnn", 2)])
+@pytest.mark.parametrize("name,batch", [("mlp_784_128_10", 8), ("cnn_1x8_pool_fc", 6), ("large_cnn", 2),
+                                        ("audio_kws_cnn", 2)])
 def test_bridge_steps_match_oracle_step(fake, name, batch):
     w = configs.WORKLOADS[name]
     p0 = synthetic.init_params(w, seed=21)

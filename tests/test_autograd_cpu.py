@@ -110,3 +110,13 @@ def test_buffers_are_recycled(fake):
     for _ in range(3):
         trainer.step(x.reshape(4, 1, 28, 28), y)
     assert len(fake.bufs) == live      # steady state: every temporary comes from the pool
+
+
+def test_buffer_returns_to_its_own_pool(fake):
+    """A tensor freed after the pool was replaced (another backend) does not
+    hand its handle to the new pool."""
+    t = ag.Tensor.from_numpy(np.ones(7, np.float32))
+    old = ag._POOL
+    ag._POOL = ag._Pool()
+    del t
+    assert old.free.get(7) and not ag._POOL.free

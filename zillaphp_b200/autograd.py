@@ -117,6 +117,7 @@ class Tensor:
         self.backward_fn = None
         self.op = "leaf"
         self._base = base            # a view keeps the tensor that owns the buffer alive
+        self._pool = _POOL           # the pool (and so the backend) the buffer belongs to
 
     # ---------------------------------------------------------------- creation
     @classmethod
@@ -140,7 +141,7 @@ class Tensor:
     def __del__(self):
         try:
             if self._base is None and self.buf > 0:
-                _POOL.put(self.size, self.buf)
+                self._pool.put(self.size, self.buf)
                 self.buf = 0
         except Exception:  # noqa: BLE001 (interpreter shutdown)
             pass

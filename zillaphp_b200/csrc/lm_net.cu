@@ -739,7 +739,7 @@ int lm_forward_cached(Net &n, const float *tokens, int count, float *logits) {
         return fail(kBadArg, "zilla_lm_forward_cached: sequence position %d exceeds max %d", e.cache_len + count, e.T);
     for (int i = 0; i < count; ++i) {   // Embedding::forward (src/NN/Layers/Embedding.php:44-48)
         const float t = tokens[i];
-        if (!isfinite(t) || (int)t < 0 || (int)t >= V)
+        if (!(t > -1.0f && t < (float)V))   // (int)t in [0, V); NaN fails both compares
             return fail(kBadArg, "zilla_lm_forward_cached: token id %g out of range [0, %d)", (double)t, V);
     }
     int rc;

@@ -140,7 +140,10 @@ int adam_update_dev(int w_id, int g_id, int m_id, int v_id, float lr, float beta
  * (code under a caller-owned memory pool or budget, or a host that only hands
  * over device pointers it already owns).  No counterpart in the reference.
  * Same arithmetic and the same outputs as softmax_ce_dev, on raw device
- * pointers and the caller's stream (NULL = the legacy default stream): dlogits
+ * pointers and the caller's stream.  NULL means the library's own stream (the
+ * one every *_dev op and zilla_set_stream use), so the call is ordered after
+ * the ops that produced the logits; with any other stream the caller orders
+ * it against the library's work (an event, or zilla_sync).  dlogits
  * = (softmax - onehot)/B, and the loss SUM over the rows is ADDED to *loss (the
  * caller zeroes it).  It calls no cudaMalloc, cudaFree or allocating library
  * routine: its per-row scratch is a file-scope static device array of 65536
@@ -230,7 +233,9 @@ int zilla_net_step_staged(int net, float *loss_sum, int update);
  * data parallelism over peer memory (each rank holds a slice of the state).
  * zilla_net_load reads such a file (or the reference's) into the net:
  * param_i required with matching shapes and dtype F32, adam_* optional;
- * -2 on a missing, malformed or mismatched file. */
+ * -2 on a missing, malformed or mismatched file, and while the net is
+ * attached for data parallelism over peer memory (detach, load the same file
+ * on every rank, attach again). */
 int zilla_net_save(int net, const char *path, int with_state);
 int zilla_net_load(int net, const char *path);
 

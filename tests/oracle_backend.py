@@ -44,6 +44,9 @@ class OracleBackend:
     def addDev(self, a, b, c, n):  # noqa: N802
         self.bufs[c][:n] = self.bufs[a][:n] + self.bufs[b][:n]
 
+    def mulDev(self, a, b, c, n):  # noqa: N802
+        self.bufs[c][:n] = self.bufs[a][:n] * self.bufs[b][:n]
+
     def scaleDev(self, x, s, n):  # noqa: N802
         self.bufs[x][:n] *= np.float32(s)
 

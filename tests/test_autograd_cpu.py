@@ -94,6 +94,27 @@ def test_gradient_accumulates_over_two_uses(fake):
     np.testing.assert_allclose(loss.item(), -np.log(p[np.arange(4), [0, 1, 2, 0]]).mean(), rtol=1e-6)
 
 
+def test_scaled_loss_scales_the_gradient(fake):
+    """loss.mul(k) before backward(): CrossEntropy's backward multiplies by the upstream
+    gradient g->item() (src/Loss/CrossEntropy.php:69-70), so every gradient scales by k."""
+    g = np.random.default_rng(3)
+    Wn = g.standard_normal((5, 4)).astype(np.float32)
+    xn = g.standard_normal((6, 5)).astype(np.float32)
+    t = [0, 1, 2, 3, 1, 0]
+    grads = []
+    for k in (1.0, 0.5, -3.0):
+        W = ag.Parameter(Wn)
+        z = ag.Tensor.from_numpy(xn).matmul(W)
+        loss = ag.CrossEntropy().forward(z, t)
+        root = loss if k == 1.0 else loss.mul(ag.Tensor.from_numpy(np.array([k], np.float32)))
+        root.backward()
+        grads.append(W.grad.numpy().copy())
+        if k != 1.0:
+            np.testing.assert_allclose(root.item(), k * loss.item(), rtol=1e-6)
+    np.testing.assert_allclose(grads[1], 0.5 * grads[0], rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(grads[2], -3.0 * grads[0], rtol=1e-6, atol=1e-7)
+
+
 def test_no_grad_records_nothing(fake):
     W = ag.Parameter(np.ones((3, 2), np.float32))
     with ag.no_grad():

@@ -75,3 +75,22 @@ def test_bridge_eval_matches_fused_forward():
     fused, _ = net.forward(x)
     net.close()
     assert npref.normwise(logits, fused) < 1e-5
+
+
+def test_scaled_loss_scales_the_gradient_on_device():
+    """loss.mul(k).backward() on the device ops: CrossEntropy's backward multiplies
+    (p - onehot) / B by the upstream gradient (src/Loss/CrossEntropy.php:69-70), so the
+    MLP's gradients are k times those of loss.backward(), checked against the oracle's
+    step gradients (1e-4 normwise, fp32 device arithmetic)."""
+    w, batch = configs.MLP, 64
+    p0 = synthetic.init_params(w, seed=8)
+    x, y = synthetic.batch(w, batch, seed=8)
+    ref = oracle.StepModel(w.spec(), batch, w.in_shape, kind="oracle")
+    ref.params[:] = p0
+    ref.step(x, y, opt=0, lr=0.0)
+    for k in (0.5, -2.0):
+        model = ag.sequential_from_spec(w.layers, w.in_shape)
+        model.load_flat(p0)
+        loss = ag.CrossEntropy().forward(model(ag.Tensor.from_numpy(x.reshape(batch, -1))), y)
+        loss.mul(ag.Tensor.from_numpy(np.array([k], np.float32))).backward()
+        assert npref.normwise(model.flat(grads=True), k * ref.grads) < 1e-4

@@ -25,8 +25,13 @@ Mirrors, with their semantics:
   Tensor::noGrad     :54-62
   CrossEntropy       src/Loss/CrossEntropy.php:18-85: the mean over the batch of
                      -log p_target; gradient (p - onehot) / B.  Computed by
-                     softmax_ce_dev in fp32 (the PHP class is float64 with a
-                     1e-12 clamp on p, which only matters for p < 1e-12)
+                     softmax_ce_dev in fp32, then scaled by the upstream gradient
+                     g->item() as :69-70 do.  The PHP class is float64 and clamps p
+                     at 1e-12 (:58); softmax_ce_dev has no clamp, so the loss of a
+                     row whose target probability is below 1e-12 (a logit gap
+                     above 27.6) keeps growing here where the reference's stops
+                     at 27.63 (the gradients are the same)
+  Tensor::mul        :1046-1054 mul_dev, same-shape operands only
   SGD / Adam         src/Optim/SGD.php:12-26, src/Optim/Adam.php:36-62
                      (sgd_update_dev; adam_update_dev with t counted per step)
   Conv2D / Linear / MaxPool2D / ReLU / Flatten / Sequential
@@ -198,6 +203,7 @@ class Tensor:
                     stack.append((i, False))
         if self.grad is None:
             self.grad = Tensor.from_numpy(np.ones(self.shape, np.float32))
+            self.grad.seed_one = True   # known to be 1 on the host: no device read needed
         for t in reversed(order):
             if t.backward_fn is not None and t.grad is not None:
                 t.backward_fn(t.grad)
@@ -331,6 +337,29 @@ class Tensor:
         return out._attach((self, other), "add", fn)
 
 
+    def mul(self, other: "Tensor") -> "Tensor":
+        """Elementwise product of two tensors of the same shape (Tensor::mul, :1046-1054, without
+        broadcasting): dA = g * B, dB = g * A."""
+        if other.shape != self.shape:
+            raise ValueError(f"mul: shapes {self.shape} and {other.shape} differ.")
+        be = backend()
+        out = Tensor.empty(self.shape)
+        be.mulDev(self.buf, other.buf, out.buf, self.size)
+        a, b = self, other
+
+        def fn(g: Tensor) -> None:
+            if a.requires_grad:
+                ga = Tensor.empty(a.shape)
+                be.mulDev(g.buf, b.buf, ga.buf, a.size)
+                a.accumulate_grad(ga)
+            if b.requires_grad:
+                gb = Tensor.empty(b.shape)
+                be.mulDev(g.buf, a.buf, gb.buf, b.size)
+                b.accumulate_grad(gb)
+
+        return out._attach((self, other), "mul", fn)
+
+
 class Parameter(Tensor):
     """src/NN/Parameter.php: a leaf tensor that requires gradients."""
 
@@ -451,8 +480,17 @@ class CrossEntropy:
         be.scaleDev(loss.buf, 1.0 / B, 1)                                  # the mean
         p = pred
 
-        def fn(g: Tensor) -> None:   # seed gradient 1 (a loss is the root of backward)
-            p.accumulate_grad(dlogits)
+        def fn(g: Tensor) -> None:
+            # CrossEntropy.php:69-70: the gradient is (p - onehot) * g->item() / batch.  The seed
+            # gradient of a loss that is the root of backward() is 1 and needs no device read.
+            s = 1.0 if getattr(g, "seed_one", False) else float(g.item())
+            if s == 1.0:
+                p.accumulate_grad(dlogits)
+                return
+            scaled = Tensor.empty(dlogits.shape)
+            be.copyDev(dlogits.buf, scaled.buf, dlogits.size)
+            be.scaleDev(scaled.buf, s, scaled.size)
+            p.accumulate_grad(scaled)
 
         return loss._attach((pred,), "cross_entropy", fn)
 

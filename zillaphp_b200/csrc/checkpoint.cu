@@ -217,6 +217,11 @@ int zilla_net_load(int id, const char *path) {
     Net *n = net_get(id);
     if (!n) return fail(kBadHandle, "zilla_net_load: unknown net %d", id);
     if (!path) return fail(kBadArg, "zilla_net_load: null path");
+    // attached over peer memory, the ranks' parameters are identical by construction and each
+    // rank holds only its slice of the Adam state: a load on some ranks would break both
+    if (n->peer.on)
+        return fail(kBadArg, "zilla_net_load: the net is attached for data parallelism over peer memory; "
+                             "detach first, load the same file on every rank, then attach");
     FILE *f = fopen(path, "rb");
     if (!f) return fail(kBadArg, "zilla_net_load: checkpoint not found: %s", path);
     std::vector<char> raw;

@@ -172,4 +172,10 @@ struct ConvWgradF32 {
 // per thread), else the implicit GEMM.  ZB_FP32_WGRAD=gemm forces the GEMM.
 int run_conv_wgrad(const ConvWgradF32 &pw, const char *what);
 
+// 2x2-style max-pool forward with the reference's tie rule and batched flat
+// argmax (conv_pool_f32.cu); shared by the *_dev entry points and the fp32 step.
+__global__ void maxpool_fwd_kernel(const float *__restrict__ in, float *__restrict__ out,
+                                   int *__restrict__ arg, int B, int C, int H, int W, int oH,
+                                   int oW, int kH, int kW, int s);
+
 }  // namespace zb

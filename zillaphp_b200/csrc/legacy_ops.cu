@@ -373,8 +373,10 @@ extern "C" int softmax_ce_noalloc(const float *logits, const float *targets, flo
                     B, kNoAllocMaxRows);
     if (B == 0) return kOk;
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-        return check_cuda("softmax_ce_noalloc: cudaGetDevice");
+    if (cudaGetDevice(&dev) != cudaSuccess) return check_cuda("softmax_ce_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices)
+        return fail(kBadArg, "softmax_ce_noalloc: device %d beyond the %d devices it keeps set-up for", dev,
+                    kMaxDevices);
     if (!g_noalloc_ptr[dev]) {   // set-up, once per device, with that device current
         double *p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress((void **)&p, g_noalloc_row_loss);
@@ -384,7 +386,9 @@ extern "C" int softmax_ce_noalloc(const float *logits, const float *targets, flo
         }
         g_noalloc_ptr[dev] = p;
     }
-    cudaStream_t s = (cudaStream_t)stream_handle;
+    // NULL: the library's own stream, so the call is ordered after the *_dev ops that produced
+    // the logits and before the ones that consume dlogits
+    cudaStream_t s = stream_handle ? (cudaStream_t)stream_handle : stream();
     // every row slot read by the sum is written first by the row kernel: nothing to clear
     softmax_ce_rows_kernel<<<grid_for((long long)B * 32, kThreads), kThreads, 0, s>>>(
         logits, targets, dlogits, g_noalloc_ptr[dev], B, C);

@@ -27,10 +27,6 @@ namespace zb {
 int launch_softmax_ce(const float *z, const float *y, float *dz, double *row_loss, float *loss,
                       int B, int C, bool zero_first);
 int launch_bias_grad(const float *dy, float *db, int B, int C);
-__global__ void maxpool_fwd_kernel(const float *__restrict__ in, float *__restrict__ out,
-                                   int *__restrict__ arg, int B, int C, int H, int W, int oH,
-                                   int oW, int kH, int kW, int s);
-
 namespace {
 
 std::map<int, Net *> g_nets;

@@ -461,9 +461,28 @@ def main():
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize()
 
+    # ---- data-parallel check, part 1: the first step's loss summed over the ranks
+    # against one GPU's forward over the whole global batch (same weights, same samples)
+    dp_check = None
+    if world > 1:
+        full_loss = None
+        if rank == 0:
+            xf, yf = synthetic.batch(w, w.batch, seed=1234, step=0)
+            ref_net = Net(w, batch=w.batch, precision=precision)
+            ref_net.set_params(synthetic.init_params(w))
+            _, full_loss = ref_net.forward(xf, yf)
+            ref_net.close()
+        barrier()
+
     launches0 = lib.zilla_launch_count()
     for s in range(args.warmup):
         net.step_dev(xs_dev[s % nb], ys_dev[s % nb], loss_id)
+        if s == 0 and world > 1:
+            first = np.empty(1, np.float32)
+            lib.zilla_buffer_download(loss_id, ctypes.cast(first.ctypes.data, native.FP), 1)
+            if rank == 0:
+                dp_check = {"first_step_loss_sum": float(first[0]), "full_batch_loss_sum_1gpu": float(full_loss),
+                            "rel_diff": abs(float(first[0]) - float(full_loss)) / abs(float(full_loss))}
     launches_warm = lib.zilla_launch_count()
     per_step_launches = (launches_warm - launches0) / max(args.warmup, 1)
     if args.graph:   # every input set runs once plain and once captured before the timed region
@@ -543,6 +562,16 @@ def main():
         dist.all_reduce(ms_e2e, op=dist.ReduceOp.MAX)
     e2e_value = w.batch * args.steps / (float(ms_e2e.item()) / 1e3)
 
+    # ---- data-parallel check, part 2: every rank's parameters after all the steps, bit
+    # for bit (a SHA-256 of the flat fp32 buffer), gathered on rank 0
+    import hashlib
+    digest = hashlib.sha256(net.params().tobytes()).hexdigest()
+    digests = [digest]
+    if world > 1:
+        digests = [None] * world
+        dist.all_gather_object(digests, digest)
+    ranks_identical = len(set(digests)) == 1
+
     if rank == 0:
         pk, pk_kind = peaks()
         roof, breakdown = roofline(w, b, breakdown_pass, args.steps, pk, pk_kind, precision,
@@ -574,12 +603,21 @@ def main():
             "segments_ms": breakdown,
             "cpu_baseline": cpu,
             "clocks": clocks,
+            "ranks_identical": ranks_identical,
+            "params_sha256": digests[0][:16],
+            "dp_check": dp_check,
         }
+        if dp_check is not None:
+            dp_check["tolerance"] = 2e-3
         print(json.dumps(line))
     net.close()
     lib.zilla_set_stream(None)
     if world > 1:
         dist.destroy_process_group()
+    if not ranks_identical:
+        raise SystemExit(f"data-parallel ranks diverged: parameter digests {sorted(set(digests))}")
+    if dp_check is not None and dp_check["rel_diff"] > dp_check["tolerance"]:
+        raise SystemExit(f"first data-parallel step's loss differs from the full-batch loss: {dp_check}")
 
 
 def main_autograd(args, w, stream, lib):

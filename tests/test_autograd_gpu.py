@@ -91,6 +91,7 @@ def test_scaled_loss_scales_the_gradient_on_device():
     for k in (0.5, -2.0):
         model = ag.sequential_from_spec(w.layers, w.in_shape)
         model.load_flat(p0)
-        loss = ag.CrossEntropy().forward(model(ag.Tensor.from_numpy(x.reshape(batch, -1))), y)
+        xin = ag.Tensor.from_numpy(x.reshape((batch,) + tuple(w.in_shape)))
+        loss = ag.CrossEntropy().forward(model(xin), y)
         loss.mul(ag.Tensor.from_numpy(np.array([k], np.float32))).backward()
         assert npref.normwise(model.flat(grads=True), k * ref.grads) < 1e-4

@@ -12,9 +12,10 @@ over NCCL before the identical update (global batch fixed: strong scaling).
 value  : global samples/s with inputs resident in HBM (CUDA events on the
          library's stream, max over ranks).
 e2e    : the same from pinned host buffers through zilla_net_stage_host +
-         zilla_net_step_staged: every step's x/y host->device copy and its loss
-         device->host read are inside the timed region (the copy of batch k+1
-         overlaps step k).
+         zilla_net_step_staged_deferred: every step's x/y host->device copy and
+         its loss device->host read (into pinned memory) are inside the timed
+         region; the copy of batch k+1 overlaps step k, and the host waits for
+         step k-1's loss while step k is queued.
 roofline: the dominant kernel group of the step (algorithmic FLOPs or bytes
          / its CUDA-event duration averaged over the timed steps) against
          MEASURED_PEAKS.json.
@@ -160,7 +161,8 @@ def stage_work(w: configs.Workload, batch: int) -> list[dict]:
 def tc_work(w: configs.Workload, b: int) -> list[dict]:
     """Kernel groups of the tensor-core engine in execution order (the labels
     zilla_net_timings reports): algorithmic FLOPs (2*M*N*K per contraction)
-    and compulsory bytes (bf16 activations, u8 pool codes, fp32 parameters)."""
+    and compulsory bytes (bf16 activations, u8 pool codes, fp32 parameters).
+    The kernel choices follow the engine's (tc_net.cu: tc_build)."""
     L = list(w.layers)
     c, h, wd = w.in_shape
     out = [{"label": "pack", "flops": 0, "bytes": 4 * configs.param_count(w)}]
@@ -184,56 +186,59 @@ def tc_work(w: configs.Workload, b: int) -> list[dict]:
         inb = b * ih * iw * a * (4 if k == 0 else 2)
         outb = b * (oh // 2) * (ow // 2) * o * 3 if pool else b * oh * ow * o * 2
         out.append({"label": "conv_fwd", "flops": f, "bytes": inb + outb, "name": f"conv{k + 1} fwd"})
-    (F, HD), (_, NC) = lin[0], lin[-1]
-    out.append({"label": "linear_fwd", "flops": 2 * b * F * HD, "bytes": 2 * (b * (F + HD) + F * HD),
-                "name": "fc1 fwd"})
-    out.append({"label": "softmax_ce", "flops": 6 * b * HD * NC, "bytes": 4 * b * HD, "name": "head"})
-    out.append({"label": "linear_bwd", "flops": 4 * b * F * HD, "bytes": 2 * (2 * b * F + 2 * b * HD + F * HD) + 4 * F * HD,
-                "name": "fc1 dX+dW"})
-    # the first conv's weight gradient is taken inside the next conv's fused
-    # backward when that one is 32 -> 64 on the unpooled, same-size first-conv output
     a0, o0, ih0, iw0, oh0, ow0, pool0 = convs[0]
+    if len(lin) == 2:   # hidden Linear + ReLU, then the classifier
+        (F, HD), (_, NC) = lin[0], lin[-1]
+        out.append({"label": "linear_fwd", "flops": 2 * b * F * HD, "bytes": 2 * (b * (F + HD) + F * HD),
+                    "name": "fc1 fwd"})
+        out.append({"label": "softmax_ce", "flops": 6 * b * HD * NC, "bytes": 4 * b * HD, "name": "head"})
+        out.append({"label": "linear_bwd", "flops": 4 * b * F * HD,
+                    "bytes": 2 * (2 * b * F + 2 * b * HD + F * HD) + 4 * F * HD, "name": "fc1 dX+dW"})
+    else:               # the classifier straight after the last pool
+        F, NC = lin[0]
+        out.append({"label": "softmax_ce", "flops": 4 * b * F * NC, "bytes": 2 * b * F * 2 + 4 * b * NC,
+                    "name": "head fwd+dX"})
+        out.append({"label": "linear_bwd", "flops": 2 * b * F * NC, "bytes": 2 * b * F + 4 * b * NC + 4 * F * NC,
+                    "name": "head dW"})
+    # the first conv's weight gradient is taken inside the next conv's fused backward
+    # when that one is 32 -> 64 on the unpooled, same-size first-conv output
     c1_fused = (len(convs) > 1 and convs[1][:2] == (32, 64) and o0 == 32 and not pool0 and (oh0, ow0) == (ih0, iw0)
                 and convs[1][3] + 2 <= 32 and (4 * convs[1][3]) % 16 == 0)
     for k in range(len(convs) - 1, -1, -1):
         a, o, ih, iw, oh, ow, pool = convs[k]
-        if k > 0:
-            # the 32 -> 64 fused backward, and the 64 -> 128 input- and weight-gradient kernels on
-            # halo tiles, build dY from the pooled gradient and the codes themselves
-            r = (128 // ow) & ~1
-            up = pool and oh % 2 == 0 and ow % 2 == 0 and (
-                ((a, o) == (32, 64) and k == 1 and not pool0 and iw + 2 <= 32) or
-                ((a, o) == (64, 128) and r >= 2 and r * (ow + 2) <= 128 and r * ow <= 128
-                 and (r // 2 + 2) * (ow // 2) * 8 <= 512))
-            if not up:
-                out.append({"label": "pool_bwd", "flops": 0,
-                            "bytes": b * ((oh // 2) * (ow // 2) * o * 3 + oh * ow * o * 2), "name": f"unpool{k + 1}"})
-            f = 2 * b * oh * ow * o * a * 9
-            if (a, o) == (32, 64) and k == 1 and c1_fused:
-                # one kernel: reads the pooled dY and its codes (or dY), X and the first conv's
-                # fp32 input; dY and dX stay on chip
-                dy_bytes = (oh // 2) * (ow // 2) * o * 3 if up else oh * ow * o * 2
+        if k == 0:
+            out.append({"label": "conv_wgrad", "flops": 2 * b * oh * ow * o * a * 9,
+                        "bytes": b * ((oh // 2) * (ow // 2) * o * 3 + ih * iw * 4 if pool0 else oh * ow * o * 2 + ih * iw * 4),
+                        "name": "unpool1+conv1 dW" if pool0 else "conv1 dW"})
+            break
+        f = 2 * b * oh * ow * o * a * 9
+        r = (128 // ow) & ~1
+        halo = r >= 2 and r * (ow + 2) <= 128
+        # 32 -> 64 on the unpooled first-conv output: one fused kernel (dX + dW, conv1 dW)
+        fused = (a, o) == (32, 64) and k == 1 and not pool0 and iw + 2 <= 32 and halo
+        up = pool and oh % 2 == 0 and ow % 2 == 0 and (
+            fused or ((a, o) == (64, 128) and halo and r * ow <= 128 and (r // 2 + 2) * (ow // 2) * 8 <= 512))
+        if not up:
+            out.append({"label": "pool_bwd", "flops": 0,
+                        "bytes": b * ((oh // 2) * (ow // 2) * o * 3 + oh * ow * o * 2), "name": f"unpool{k + 1}"})
+        dy_bytes = (oh // 2) * (ow // 2) * o * 3 if up else oh * ow * o * 2
+        if fused:
+            if c1_fused:   # reads the pooled dY and its codes (or dY), X and the first conv's fp32 input
                 out.append({"label": "conv_bwd", "flops": 2 * f + 2 * b * oh0 * ow0 * o0 * 9,
                             "bytes": b * (dy_bytes + ih * iw * a * 2 + ih0 * iw0 * 4),
                             "name": f"{'unpool2+' if up else ''}conv{k + 1} dX+dW, conv1 dW"})
                 break
-            if (a, o) == (32, 64):
-                # one kernel for both: reads dY and X once, writes dX
-                out.append({"label": "conv_bwd", "flops": 2 * f,
-                            "bytes": b * (oh * ow * o * 2 + ih * iw * a * 2 * 2), "name": f"conv{k + 1} dX+dW"})
-                continue
-            # input gradient: reads dY (or the pooled dY and its codes), writes dX (plus the
-            # ReLU mask of conv1's output for conv2)
-            dy_bytes = (oh // 2) * (ow // 2) * o * 3 if up else oh * ow * o * 2
-            pre = f"unpool{k + 1}+" if up else ""
-            out.append({"label": "conv_dgrad", "flops": f,
-                        "bytes": b * (dy_bytes + ih * iw * a * 2 * (2 if k == 1 else 1)),
-                        "name": f"{pre}conv{k + 1} dX"})
-            out.append({"label": "conv_wgrad", "flops": f, "bytes": b * (dy_bytes + ih * iw * a * 2),
-                        "name": f"{pre}conv{k + 1} dW"})
-        else:
-            out.append({"label": "conv_wgrad", "flops": 2 * b * oh * ow * o * a * 9,
-                        "bytes": b * (oh * ow * o * 2 + ih * iw * 4), "name": "conv1 dW"})
+            out.append({"label": "conv_bwd", "flops": 2 * f,
+                        "bytes": b * (dy_bytes + ih * iw * a * 2 * 2), "name": f"conv{k + 1} dX+dW"})
+            continue
+        # input gradient: reads dY (or the pooled dY and its codes), writes dX (plus the ReLU
+        # mask of the previous activation when it is an unpooled first-conv output)
+        pre = f"unpool{k + 1}+" if up else ""
+        mask = k == 1 and not pool0
+        out.append({"label": "conv_dgrad", "flops": f, "bytes": b * (dy_bytes + ih * iw * a * 2 * (2 if mask else 1)),
+                    "name": f"{pre}conv{k + 1} dX"})
+        out.append({"label": "conv_wgrad", "flops": f, "bytes": b * (dy_bytes + ih * iw * a * 2),
+                    "name": f"{pre}conv{k + 1} dW"})
     n = configs.param_count(w)
     out.append({"label": "adam" if w.optimizer == configs.ADAM else "sgd", "flops": 0,
                 "bytes": (28 if w.optimizer == configs.ADAM else 12) * n, "name": "optimizer"})
@@ -542,21 +547,28 @@ def main():
     value = w.batch * args.steps / (ms / 1e3)
 
     # ---- end to end from pinned host buffers: the next batch's host->device copy
-    # (zilla_net_stage_host) runs during the current step (zilla_net_step_staged,
-    # which returns after reading the loss back)
+    # (zilla_net_stage_host) runs during the current step, and every step's loss
+    # is read back into pinned host memory; zilla_net_step_staged_deferred hands
+    # the host the previous step's loss while the current one stays queued
     for _ in range(4 if args.graph else 1):   # warm-up: the staging slots (and their graphs) come into being
         net.stage_host(xs_host[0].numpy(), ys_host[0].numpy())
-        net.step_staged()
+        net.step_staged_deferred()
+    net.loss_flush()
     barrier()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
     net.stage_host(xs_host[0].numpy(), ys_host[0].numpy())
+    e2e_losses = []
     for s in range(args.steps):
         if s + 1 < args.steps:
             net.stage_host(xs_host[(s + 1) % nb].numpy(), ys_host[(s + 1) % nb].numpy())
-        net.step_staged()
+        prev = net.step_staged_deferred()
+        if prev is not None:
+            e2e_losses.append(prev)
     e3.record(stream)
+    e2e_losses.append(net.loss_flush())
     barrier()
+    assert len(e2e_losses) == args.steps and all(np.isfinite(e2e_losses))
     ms_e2e = torch.tensor([e2.elapsed_time(e3)], device="cuda")
     if world > 1:
         dist.all_reduce(ms_e2e, op=dist.ReduceOp.MAX)
@@ -732,7 +744,8 @@ def main_lm(args):
     if batch % world:
         raise SystemExit("global batch must divide by the number of GPUs")
     b = batch // world
-    net = LM(w, batch=b)
+    lm_precision = args.precision or 0   # 1: the blocks' Linear layers on TF32 tensor cores
+    net = LM(w, batch=b, precision=lm_precision)
     net.set_params(synthetic.lm_init_params(w))
     if world > 1:
         obj = [dp_unique_id() if rank == 0 else None]
@@ -856,7 +869,7 @@ def main_lm(args):
         print(json.dumps({
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "tf32" if lm_precision == 1 else "f32", "data": "synthetic",
             "config": {"workload": w.name, "global_batch": batch, "per_gpu_batch": b, "seq_len": w.seq,
                        "tokens_per_s": round(value * w.seq, 1),
                        "step_tflops": round(total_flops * world / (ms / args.steps * 1e-3) / 1e12, 3),

@@ -220,6 +220,18 @@ int zilla_net_step_host(int net, const float *x, const float *y, float *loss_sum
  * Typical loop: stage(0); for k: stage(k+1); step_staged(k). */
 int zilla_net_stage_host(int net, const float *x, const float *y);
 int zilla_net_step_staged(int net, float *loss_sum, int update);
+/* The staged step with a deferred loss read (no reference counterpart; the
+ * reference's Trainer::fitLoader reads each step's loss with a blocking
+ * item(), src/Training/Trainer.php:74-98).  zilla_net_step_staged_deferred
+ * runs the step on the oldest staged batch and enqueues the copy of its loss
+ * sum into pinned host memory, then waits only for the PREVIOUS deferred
+ * step: that step's loss sum goes to *prev_loss_sum with *has_prev = 1 (0 on
+ * the first call, or after a flush), while this step stays queued on the GPU.
+ * zilla_net_loss_flush waits for the last deferred step and returns its loss
+ * (*has = 0 when none is pending).  Typical loop: stage(0); for k: stage(k+1);
+ * step_staged_deferred(k) -> loss of k-1; after the loop, flush -> last loss. */
+int zilla_net_step_staged_deferred(int net, float *prev_loss_sum, int *has_prev, int update);
+int zilla_net_loss_flush(int net, float *loss_sum, int *has);
 
 /* Checkpoints: the net's parameters as a SafeTensors F32 file in the layout
  * ModelSerializer::save writes through SafeTensorsSerializer::save
@@ -303,6 +315,14 @@ int zilla_lm_create(int vocab, int dim, int heads, int layers, int max_seq, int 
  * reference throws RuntimeException / OutOfRangeException).  Uses the net's
  * current parameters; independent of the training step's buffers. */
 int zilla_lm_forward_cached(int net, const float *tokens, int count, float *logits);
+/* Arithmetic of the language model's Linear layers (no reference counterpart;
+ * the reference computes in float64 PHP): 0 = fp32 CUDA-core GEMMs (the
+ * default; matches the reference within 1e-4), 1 = TF32 tcgen05 tensor-core
+ * GEMMs for the blocks' Q/K/V, output, FFN projections and their input and
+ * weight gradients (fp32 operands read with a 10-bit mantissa, fp32
+ * accumulation; stated tolerance), with LayerNorm, attention, the head and
+ * the loss unchanged.  Needs batch*seq % 256 == 0 and dim, ffn % 128 == 0. */
+int zilla_lm_set_precision(int net, int precision);
 /* TransformerLM::newCache (TransformerLM.php:153-156): cache length 0. */
 int zilla_lm_cache_reset(int net);
 /* KVCache::$length: the number of cached positions (>= 0), or a negative status. */

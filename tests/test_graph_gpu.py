@@ -2,11 +2,18 @@
 for an input set, replay afterwards with the optimizer's arguments of each step.
 The replayed steps must leave parameters and losses bit-identical to plain
 steps (SGD and Adam, fp32 and bf16 engines), keep doing so across an optimizer
-change (which drops the graphs), and count their kernels as launches.
+change (which drops the graphs), and count their kernels as launches.  The
+graph runs of the fp32 configs are also held against the oracle's replay of
+the reference step sequence (losses within 1e-5, weights within 1e-4
+normwise), with the same optimizer change at step 4.
 """
+import os
+
 import numpy as np
 import pytest
 
+import npref
+import oracle
 from zillaphp_b200 import configs, native, synthetic
 from zillaphp_b200.net import Net
 
@@ -43,6 +50,13 @@ def test_graph_steps_match_plain_steps(name, precision, batch):
         assert la == lb, (la, lb)
         assert np.array_equal(a.params(), b.params()), "graph replays diverged from plain steps"
         assert na == nb, (na, nb)
+        if precision == 0:
+            threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else 1
+            ref = oracle.StepModel(w.spec(), batch, w.in_shape, nthreads=threads)
+            ref.params[:] = p0
+            rl = [ref.step(*batches[s % 2], w.optimizer, w.lr if s < 4 else w.lr * 0.5) for s in range(6)]
+            assert all(abs(g - r) <= 1e-5 * abs(r) for g, r in zip(lb, rl)), (lb, rl)
+            assert npref.normwise(b.params(), ref.params) < 1e-4
     finally:
         a.close()
         b.close()

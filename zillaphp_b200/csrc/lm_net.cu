@@ -21,8 +21,23 @@
 
 #include "conv_pool_f32.cuh"
 #include "net.cuh"
+#include "tc_gemm_tf32.cuh"
 
 namespace zb {
+
+// One Linear GEMM of the tensor-core step (precision 1): its TF32 tcgen05
+// problem, built once per net over the persistent activations and weights.
+//   kind 0 forward      Y = X W (+ b) (+ R) (relu)     A K-major, B MN-major
+//   kind 1 input grad   dX = dY W^T                    A K-major, B K-major
+//   kind 2 input grad   dX = (dY W^T) * (mask > 0)     (ReLU backward)
+//   kind 3 weight grad  dW = X^T dY, K split; the splits are summed in order
+//                       into dst[n / seg_w][m * seg_w + n % seg_w]
+struct LmTcGemm {
+    tc::GemmTf32Params p;
+    int kind = 0, grid = 0;
+    float *dst[3] = {nullptr, nullptr, nullptr};
+    int seg_w = 0;
+};
 
 int launch_softmax_ce(const float *z, const float *y, float *dz, double *row_loss, float *loss,
                       int B, int C, bool zero_first);
@@ -48,8 +63,14 @@ struct LmEngine {
     float *gx = nullptr, *gxm = nullptr, *gh = nullptr, *gxh = nullptr, *ginv = nullptr, *gqkv = nullptr,
           *gatt = nullptr, *gf1 = nullptr, *glog = nullptr, *gtok = nullptr;
     int cache_len = 0;
+    // tensor-core GEMMs (precision 1), per block: 0 qkv, 1 out proj, 2 fc1, 3 fc2 (forward);
+    // 4 fc2 dX, 5 fc1 dX, 6 out dX, 7 qkv dX; 8 fc2 dW, 9 fc1 dW, 10 out dW, 11 qkv dW
+    std::vector<LmTcGemm> tcg;
+    float *tc_partial = nullptr;   // weight-gradient split partials
+    const float *tc_params = nullptr, *tc_grads = nullptr;   // the buffers the plan was built over
     std::vector<void *> allocs;
 };
+constexpr int kLmTcPerBlock = 12;
 
 namespace {
 
@@ -567,6 +588,177 @@ int lm_build(Net &n, LmEngine &e) {
     return kOk;
 }
 
+// ---------------------------------------------------------------- tensor-core GEMMs (precision 1)
+// Sum of the K-split partials [splits][M][N] in split order, scattered into
+// the weight-gradient segments dst[n / seg_w] (row-major [M][seg_w]).
+__global__ void __launch_bounds__(256) lm_tc_reduce_kernel(const float *__restrict__ partial, int splits, int M, int N,
+                                                           float *d0, float *d1, float *d2, int seg_w) {
+    griddep_launch();
+    griddep_wait();
+    const long long MN = (long long)M * N;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < MN; i += (long long)gridDim.x * blockDim.x) {
+        float s = 0.0f;
+        for (int k = 0; k < splits; ++k) s += __ldcg(partial + (size_t)k * MN + i);
+        const int m = (int)(i / N), n = (int)(i % N), seg = n / seg_w;
+        float *d = seg == 0 ? d0 : seg == 1 ? d1 : d2;
+        d[(size_t)m * seg_w + (n - seg * seg_w)] = s;
+    }
+}
+
+template <bool AMN, bool BMN, int EPI>
+int launch_tf32(const tc::GemmTf32Params &p, int grid) {
+    constexpr int BN = 128, NS = 4;
+    using S = tc::GemmTf32Shape<BN, NS>;
+    auto kern = tc::gemm_tf32_kernel<BN, AMN, BMN, EPI, NS>;
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM) != cudaSuccess)
+            return check_cuda("lm tf32 gemm smem attribute");
+        attr = true;
+    }
+    launch_pdl(kern, dim3(grid), dim3(192), S::SMEM, p);
+    ZB_LAUNCH_CHECK("lm tf32 gemm");
+    return kOk;
+}
+
+int lm_tc_run(const LmEngine &e, const LmTcGemm &g) {
+    switch (g.kind) {
+    case 0: return launch_tf32<false, true, tc::kTfStore>(g.p, g.grid);
+    case 1: return launch_tf32<false, false, tc::kTfStore>(g.p, g.grid);
+    case 2: return launch_tf32<false, false, tc::kTfMask>(g.p, g.grid);
+    default: {
+        int rc = launch_tf32<true, true, tc::kTfPartial>(g.p, g.grid);
+        if (rc) return rc;
+        launch_pdl(lm_tc_reduce_kernel, dim3(grid_for((long long)g.p.M * g.p.N, 256, 4)), dim3(256), 0,
+                   (const float *)e.tc_partial, g.p.ksplit, g.p.M, g.p.N, g.dst[0], g.dst[1], g.dst[2], g.seg_w);
+        ZB_LAUNCH_CHECK("lm tf32 weight-gradient sum");
+        return kOk;
+    }
+    }
+}
+
+// 2D fp32 tensor maps, 128-byte swizzle: K-major {K (contiguous), rows}, box {32, box_rows};
+// MN-major {MN (contiguous), K rows}, box {32, 32}
+int fmap(CUtensorMap *m, const float *base, int inner, int outer, int box_outer) {
+    const uint64_t dims[2] = {(uint64_t)inner, (uint64_t)outer}, strides[1] = {(uint64_t)inner * 4};
+    const uint32_t box[2] = {32, (uint32_t)box_outer};
+    return tc::make_tmap_f32(m, base, 2, dims, strides, box, tc::kSw128);
+}
+
+// Forward: Y [M][ldo] = X [M][K] W_s [K][N_s] over nseg segments (n tile s = segment s when nseg > 1).
+int tc_fwd(LmTcGemm &g, const float *X, int M, int K, const float *const *W, int nseg, int Nseg, const float *const *bias,
+           const float *res, int ldr, bool relu, float *Y, int ldo) {
+    tc::GemmTf32Params &p = g.p;
+    int rc;
+    if ((rc = fmap(&p.a_map, X, K, M, 128))) return rc;
+    for (int s = 0; s < nseg; ++s)
+        if ((rc = fmap(&p.b_map[s], W[s], Nseg, K, 32))) return rc;
+    p.M = M; p.N = nseg * Nseg; p.K = K;
+    p.m_tiles = M / 128; p.n_tiles = p.N / 128; p.ksplit = 1; p.kper = K / 32;
+    p.nseg = nseg; p.b_seg_by_n = nseg > 1; p.seg_k = 0;
+    p.out = Y; p.ldo = ldo;
+    for (int s = 0; s < 3; ++s) p.bias[s] = s < nseg ? bias[s] : nullptr;
+    p.res = res; p.ldr = ldr; p.relu = relu;
+    g.kind = 0;
+    return kOk;
+}
+
+// Input gradient: dX [M][ldo] = sum_s dY[:, s*Kseg ..] W_s^T, W_s [N][Kseg] (the layer's [in][out]).
+int tc_dgrad(LmTcGemm &g, const float *dY, int M, int Kseg, int nseg, const float *const *W, int N, const float *mask,
+             float *dX) {
+    tc::GemmTf32Params &p = g.p;
+    int rc;
+    if ((rc = fmap(&p.a_map, dY, Kseg * nseg, M, 128))) return rc;
+    for (int s = 0; s < nseg; ++s)
+        if ((rc = fmap(&p.b_map[s], W[s], Kseg, N, 128))) return rc;
+    p.M = M; p.N = N; p.K = Kseg * nseg;
+    p.m_tiles = M / 128; p.n_tiles = N / 128; p.ksplit = 1; p.kper = p.K / 32;
+    p.nseg = nseg; p.b_seg_by_n = 0; p.seg_k = nseg > 1 ? Kseg : 0;
+    p.out = dX; p.ldo = N;
+    p.mask = mask; p.ldm = N;
+    g.kind = mask ? 2 : 1;
+    return kOk;
+}
+
+// Weight gradient: dW [M][N] = X^T dY over `rows` rows, X [rows][M], dY [rows][N]; the
+// summed result goes to dst[n / seg_w].
+int tc_wgrad(LmTcGemm &g, const float *X, int M, const float *dY, int N, int rows, float *const *dst, int seg_w) {
+    tc::GemmTf32Params &p = g.p;
+    int rc;
+    if ((rc = fmap(&p.a_map, X, M, rows, 32))) return rc;
+    if ((rc = fmap(&p.b_map[0], dY, N, rows, 32))) return rc;
+    p.M = M; p.N = N; p.K = rows;
+    p.m_tiles = M / 128; p.n_tiles = N / 128;
+    const int stages = rows / 32;
+    int ks = sm_count() / (p.m_tiles * p.n_tiles);
+    if (ks > stages / 8) ks = stages / 8;   // at least eight K stages per split
+    if (ks > 32) ks = 32;
+    if (ks < 1) ks = 1;
+    p.kper = (stages + ks - 1) / ks;
+    p.ksplit = (stages + p.kper - 1) / p.kper;
+    p.nseg = 1; p.b_seg_by_n = 0; p.seg_k = 0;
+    g.kind = 3;
+    for (int s = 0; s < 3; ++s) g.dst[s] = dst[s];
+    g.seg_w = seg_w;
+    return kOk;
+}
+
+// The plan over the net's buffers (after net_alloc_common: parameters and gradients exist).
+int lm_tc_build(Net &n, LmEngine &e) {
+    const int D = e.D, N = e.N, F = e.F, L = e.L;
+    if (N % 128 || D % 128 || F % 128 || N % 256)
+        return fail(kBadArg, "lm: tensor-core GEMMs need batch*seq %% 256 == 0 and dim, ffn %% 128 == 0 (%d, %d, %d)",
+                    N, D, F);
+    const float *Pm = n.params;
+    float *G = n.grads;
+    e.tc_params = Pm;
+    e.tc_grads = G;
+    size_t part = 0;
+    e.tcg.assign((size_t)L * kLmTcPerBlock, LmTcGemm());
+    int rc;
+    for (int l = 0; l < L; ++l) {
+        const auto &b = e.blk[l];
+        LmTcGemm *g = &e.tcg[(size_t)l * kLmTcPerBlock];
+        for (int j = 0; j < kLmTcPerBlock; ++j) g[j].p.err = device_error_word();
+        const float *Wqkv[3] = {Pm + b.qW, Pm + b.kW, Pm + b.vW}, *bqkv[3] = {Pm + b.qb, Pm + b.kb, Pm + b.vb};
+        const float *Wo[1] = {Pm + b.oW}, *bo[1] = {Pm + b.ob};
+        const float *W1[1] = {Pm + b.f1W}, *b1[1] = {Pm + b.f1b};
+        const float *W2[1] = {Pm + b.f2W}, *b2[1] = {Pm + b.f2b};
+        if ((rc = tc_fwd(g[0], e.h1[l], N, D, Wqkv, 3, D, bqkv, nullptr, 0, false, e.qkv[l], 3 * D)) ||
+            (rc = tc_fwd(g[1], e.att[l], N, D, Wo, 1, D, bo, e.x[l], D, false, e.xm[l], D)) ||
+            (rc = tc_fwd(g[2], e.h2[l], N, D, W1, 1, F, b1, nullptr, 0, true, e.f1[l], F)) ||
+            (rc = tc_fwd(g[3], e.f1[l], N, F, W2, 1, D, b2, e.xm[l], D, false, e.x[l + 1], D)))
+            return rc;
+        // input gradients: W [in][out] is B K-major over out
+        if ((rc = tc_dgrad(g[4], e.g, N, D, 1, W2, F, e.f1[l], e.df1)) ||
+            (rc = tc_dgrad(g[5], e.df1, N, F, 1, W1, D, nullptr, e.dh)) ||
+            (rc = tc_dgrad(g[6], e.gm, N, D, 1, Wo, D, nullptr, e.datt)) ||
+            (rc = tc_dgrad(g[7], e.dqkv, N, D, 3, Wqkv, D, nullptr, e.dh)))
+            return rc;
+        float *dW2[3] = {G + b.f2W, nullptr, nullptr}, *dW1[3] = {G + b.f1W, nullptr, nullptr};
+        float *dWo[3] = {G + b.oW, nullptr, nullptr}, *dWqkv[3] = {G + b.qW, G + b.kW, G + b.vW};
+        if ((rc = tc_wgrad(g[8], e.f1[l], F, e.g, D, N, dW2, D)) ||
+            (rc = tc_wgrad(g[9], e.h2[l], D, e.df1, F, N, dW1, F)) ||
+            (rc = tc_wgrad(g[10], e.att[l], D, e.gm, D, N, dWo, D)) ||
+            (rc = tc_wgrad(g[11], e.h1[l], D, e.dqkv, 3 * D, N, dWqkv, D)))
+            return rc;
+        for (int j = 0; j < kLmTcPerBlock; ++j) {
+            LmTcGemm &t = g[j];
+            const int tiles = t.p.m_tiles * t.p.n_tiles * t.p.ksplit;
+            t.grid = tiles < sm_count() ? tiles : sm_count();
+            if (t.kind == 3) {
+                t.p.partial = nullptr;   // set below, once the scratch exists
+                const size_t need = (size_t)t.p.ksplit * t.p.M * t.p.N;
+                if (need > part) part = need;
+            }
+        }
+    }
+    if ((rc = lalloc(e, &e.tc_partial, part))) return rc;
+    for (auto &t : e.tcg)
+        if (t.kind == 3) t.p.partial = e.tc_partial;
+    return kOk;
+}
+
 int attn_smem_fwd(int Ts, int dh) { return (int)((2 * (size_t)Ts * (dh + 1) + 32 * (dh + 1) + 32 * (size_t)Ts) * sizeof(float)); }
 int attn_smem_bwd(int Ts, int dh) { return (int)((4 * (size_t)Ts * (dh + 1) + (size_t)Ts * (Ts + 1)) * sizeof(float)); }
 
@@ -607,6 +799,11 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
     float *G = n.grads;
     const float scale = 1.0f / sqrtf((float)(D / e.H));
     int rc;
+    // precision 1: the Linear GEMMs of the blocks on TF32 tensor cores (the plan holds
+    // the parameter and gradient buffers it was built over)
+    const bool tcp = n.precision == 1 && !e.tcg.empty();
+    if (tcp && (G != e.tc_grads || Pm != e.tc_params))
+        return fail(kBadArg, "lm: tensor-core plan built over other parameter / gradient buffers");
     // ---- forward
     embed_fwd_kernel<<<grid_for((long long)N * D, 256, 8), 256, 0, stream()>>>(
         tokens, Pm + e.o_tok, Pm + e.o_pos, e.x[0], N, e.Ts, D, V, device_error_word());
@@ -614,10 +811,11 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
     prof_mark(n, "embed");
     for (int l = 0; l < L; ++l) {
         const auto &b = e.blk[l];
+        const LmTcGemm *tg = tcp ? &e.tcg[(size_t)l * kLmTcPerBlock] : nullptr;
         if ((rc = ln_fwd(e.x[l], Pm + b.ln1g, Pm + b.ln1b, e.h1[l], e.xh1[l], e.inv1[l], N, D))) return rc;
         LinFwd qkv{e.h1[l], nullptr, {Pm + b.qW, Pm + b.kW, Pm + b.vW}, {Pm + b.qb, Pm + b.kb, Pm + b.vb},
                    e.qkv[l], N, 3 * D, D, D, 3 * D, D, false};
-        if ((rc = run_simt_gemm(qkv, 1, "lm qkv"))) return rc;
+        if ((rc = tcp ? lm_tc_run(e, tg[0]) : run_simt_gemm(qkv, 1, "lm qkv"))) return rc;
         prof_mark(n, "ln1_qkv");
         attn_fwd_kernel<32><<<dim3(e.Bs * e.H, (e.Ts + 31) / 32), 128, attn_smem_fwd(e.Ts, 32), stream()>>>(
             e.qkv[l], e.P[l], e.att[l], e.Ts, e.H, D, scale);
@@ -625,14 +823,14 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
         prof_mark(n, "attn_fwd");
         LinFwd o{e.att[l], e.x[l], {Pm + b.oW, nullptr, nullptr}, {Pm + b.ob, nullptr, nullptr}, e.xm[l],
                  N, D, D, D, D, D, false};
-        if ((rc = run_simt_gemm(o, 1, "lm out proj"))) return rc;
+        if ((rc = tcp ? lm_tc_run(e, tg[1]) : run_simt_gemm(o, 1, "lm out proj"))) return rc;
         if ((rc = ln_fwd(e.xm[l], Pm + b.ln2g, Pm + b.ln2b, e.h2[l], e.xh2[l], e.inv2[l], N, D))) return rc;
         LinFwd f1{e.h2[l], nullptr, {Pm + b.f1W, nullptr, nullptr}, {Pm + b.f1b, nullptr, nullptr}, e.f1[l],
                   N, F, D, D, F, F, true};
-        if ((rc = run_simt_gemm(f1, 1, "lm fc1"))) return rc;
+        if ((rc = tcp ? lm_tc_run(e, tg[2]) : run_simt_gemm(f1, 1, "lm fc1"))) return rc;
         LinFwd f2{e.f1[l], e.xm[l], {Pm + b.f2W, nullptr, nullptr}, {Pm + b.f2b, nullptr, nullptr}, e.x[l + 1],
                   N, D, F, F, D, D, false};
-        if ((rc = run_simt_gemm(f2, 1, "lm fc2"))) return rc;
+        if ((rc = tcp ? lm_tc_run(e, tg[3]) : run_simt_gemm(f2, 1, "lm fc2"))) return rc;
         prof_mark(n, "oproj_ln2_ffn");
     }
     if ((rc = ln_fwd(e.x[L], Pm + e.o_lnf_g, Pm + e.o_lnf_b, e.hf, e.xhf, e.invf, N, D))) return rc;
@@ -653,34 +851,35 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
     prof_mark(n, "head_bwd");
     for (int l = L - 1; l >= 0; --l) {
         const auto &b = e.blk[l];
+        const LmTcGemm *tg = tcp ? &e.tcg[(size_t)l * kLmTcPerBlock] : nullptr;
         // FFN
         LinWgrad w2{e.f1[l], e.g, {G + b.f2W, nullptr, nullptr}, F, D, N, F, D, D};
-        if ((rc = run_simt_gemm(w2, 0, "lm fc2 dW"))) return rc;
+        if ((rc = tcp ? lm_tc_run(e, tg[8]) : run_simt_gemm(w2, 0, "lm fc2 dW"))) return rc;
         if ((rc = colsum(e.g, N, D, D, G + b.f2b))) return rc;
         LinDgrad d2{e.g, e.f1[l], {Pm + b.f2W, nullptr, nullptr}, e.df1, N, F, D, F, D, D};
-        if ((rc = run_simt_gemm(d2, 1, "lm fc2 dX"))) return rc;
+        if ((rc = tcp ? lm_tc_run(e, tg[4]) : run_simt_gemm(d2, 1, "lm fc2 dX"))) return rc;
         LinWgrad w1{e.h2[l], e.df1, {G + b.f1W, nullptr, nullptr}, D, F, N, D, F, F};
-        if ((rc = run_simt_gemm(w1, 0, "lm fc1 dW"))) return rc;
+        if ((rc = tcp ? lm_tc_run(e, tg[9]) : run_simt_gemm(w1, 0, "lm fc1 dW"))) return rc;
         if ((rc = colsum(e.df1, N, F, F, G + b.f1b))) return rc;
         LinDgrad d1{e.df1, nullptr, {Pm + b.f1W, nullptr, nullptr}, e.dh, N, D, F, D, F, F};
-        if ((rc = run_simt_gemm(d1, 1, "lm fc1 dX"))) return rc;
+        if ((rc = tcp ? lm_tc_run(e, tg[5]) : run_simt_gemm(d1, 1, "lm fc1 dX"))) return rc;
         if ((rc = ln_bwd(e, e.dh, e.xh2[l], e.inv2[l], Pm + b.ln2g, e.g, e.gm, G + b.ln2g, G + b.ln2b))) return rc;
         prof_mark(n, "ffn_ln2_bwd");
         // attention
         LinWgrad wo{e.att[l], e.gm, {G + b.oW, nullptr, nullptr}, D, D, N, D, D, D};
-        if ((rc = run_simt_gemm(wo, 0, "lm out dW"))) return rc;
+        if ((rc = tcp ? lm_tc_run(e, tg[10]) : run_simt_gemm(wo, 0, "lm out dW"))) return rc;
         if ((rc = colsum(e.gm, N, D, D, G + b.ob))) return rc;
         LinDgrad dout{e.gm, nullptr, {Pm + b.oW, nullptr, nullptr}, e.datt, N, D, D, D, D, D};
-        if ((rc = run_simt_gemm(dout, 1, "lm out dX"))) return rc;
+        if ((rc = tcp ? lm_tc_run(e, tg[6]) : run_simt_gemm(dout, 1, "lm out dX"))) return rc;
         attn_bwd_kernel<32><<<e.Bs * e.H, 256, attn_smem_bwd(e.Ts, 32), stream()>>>(e.qkv[l], e.P[l], e.datt,
                                                                                   e.dqkv, e.Ts, e.H, D, scale);
         ZB_LAUNCH_CHECK("lm attention backward");
         prof_mark(n, "oproj_attn_bwd");
         LinWgrad wq{e.h1[l], e.dqkv, {G + b.qW, G + b.kW, G + b.vW}, D, 3 * D, N, D, 3 * D, D};
-        if ((rc = run_simt_gemm(wq, 0, "lm qkv dW"))) return rc;
+        if ((rc = tcp ? lm_tc_run(e, tg[11]) : run_simt_gemm(wq, 0, "lm qkv dW"))) return rc;
         if ((rc = colsum(e.dqkv, N, 3 * D, D, G + b.qb, G + b.kb, G + b.vb))) return rc;
         LinDgrad dq{e.dqkv, nullptr, {Pm + b.qW, Pm + b.kW, Pm + b.vW}, e.dh, N, D, 3 * D, D, 3 * D, D};
-        if ((rc = run_simt_gemm(dq, 1, "lm qkv dX"))) return rc;
+        if ((rc = tcp ? lm_tc_run(e, tg[7]) : run_simt_gemm(dq, 1, "lm qkv dX"))) return rc;
         if ((rc = ln_bwd(e, e.dh, e.xh1[l], e.inv1[l], Pm + b.ln1g, e.gm, e.g, G + b.ln1g, G + b.ln1b))) return rc;
         prof_mark(n, "qkv_ln1_bwd");
     }
@@ -827,6 +1026,24 @@ extern "C" int zilla_lm_create(int vocab, int dim, int heads, int layers, int ma
         return rc;
     }
     return net_register(n);
+}
+
+extern "C" int zilla_lm_set_precision(int net, int precision) {
+    Net *n = net_get(net);
+    if (!n || !n->lm) return fail(kBadHandle, "zilla_lm_set_precision: %d is not a language model", net);
+    if (precision != 0 && precision != 1) return fail(kBadArg, "zilla_lm_set_precision: precision %d", precision);
+    if (precision == 1 && n->lm->tcg.empty()) {
+        cudaStreamSynchronize(stream());
+        int rc = lm_tc_build(*n, *n->lm);
+        if (rc) {
+            n->lm->tcg.clear();
+            return rc;
+        }
+    }
+    cudaStreamSynchronize(stream());
+    release_graphs(*n);   // captured steps carry the other kernels
+    n->precision = precision;
+    return check_cuda("zilla_lm_set_precision");
 }
 
 extern "C" int zilla_lm_cache_reset(int net) {

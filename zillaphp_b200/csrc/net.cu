@@ -195,6 +195,9 @@ void free_net(Net *n) {
         cudaStreamSynchronize(n->copy_stream);
         cudaStreamDestroy(n->copy_stream);
     }
+    for (int k = 0; k < 2; ++k)
+        if (n->ev_loss[k]) cudaEventDestroy(n->ev_loss[k]);
+    if (n->loss_host) cudaFreeHost(n->loss_host);
     if (n->tc) tc_destroy(*n);
     if (n->lm) lm_destroy(*n);
     for (auto &s : n->st) {
@@ -737,6 +740,51 @@ int zilla_net_step_staged(int id, float *loss_sum, int update) {
         if (cudaStreamSynchronize(stream()) != cudaSuccess) return check_cuda("zilla_net_step_staged");
     }
     return check_cuda("zilla_net_step_staged");
+}
+
+int zilla_net_step_staged_deferred(int id, float *prev_loss_sum, int *has_prev, int update) {
+    Net *n = net_get(id);
+    if (!n) return fail(kBadHandle, "zilla_net_step_staged_deferred: unknown net %d", id);
+    if (!prev_loss_sum || !has_prev) return fail(kBadArg, "zilla_net_step_staged_deferred: null output");
+    *has_prev = 0;
+    if (n->stage_count == 0) return fail(kBadArg, "zilla_net_step_staged_deferred: no batch staged");
+    if (!n->loss_host) {   // first use: two pinned loss slots and their events
+        if (cudaHostAlloc((void **)&n->loss_host, 2 * sizeof(float), cudaHostAllocDefault) != cudaSuccess)
+            return check_cuda("zilla_net_step_staged_deferred: pinned loss slots");
+        for (int k = 0; k < 2; ++k)
+            if (cudaEventCreateWithFlags(&n->ev_loss[k], cudaEventDisableTiming) != cudaSuccess)
+                return check_cuda("zilla_net_step_staged_deferred: events");
+    }
+    int rc = zilla_net_step_staged(id, nullptr, update);
+    if (rc) return rc;
+    // this step's loss sum goes to a pinned slot; the slot's previous content was handed out
+    const int k = n->loss_next;
+    cudaMemcpyAsync(n->loss_host + k, n->grads + n->nparams, sizeof(float), cudaMemcpyDeviceToHost, stream());
+    cudaEventRecord(n->ev_loss[k], stream());
+    n->loss_next ^= 1;
+    // hand out the previous step's loss: wait only for that step (this one stays queued)
+    if (n->loss_pending >= 0) {
+        if (cudaEventSynchronize(n->ev_loss[n->loss_pending]) != cudaSuccess)
+            return check_cuda("zilla_net_step_staged_deferred: previous step");
+        *prev_loss_sum = n->loss_host[n->loss_pending];
+        *has_prev = 1;
+    }
+    n->loss_pending = k;
+    return check_cuda("zilla_net_step_staged_deferred");
+}
+
+int zilla_net_loss_flush(int id, float *loss_sum, int *has) {
+    Net *n = net_get(id);
+    if (!n) return fail(kBadHandle, "zilla_net_loss_flush: unknown net %d", id);
+    if (!loss_sum || !has) return fail(kBadArg, "zilla_net_loss_flush: null output");
+    *has = 0;
+    if (n->loss_pending < 0) return kOk;
+    if (cudaEventSynchronize(n->ev_loss[n->loss_pending]) != cudaSuccess)
+        return check_cuda("zilla_net_loss_flush");
+    *loss_sum = n->loss_host[n->loss_pending];
+    *has = 1;
+    n->loss_pending = -1;
+    return kOk;
 }
 
 int zilla_net_inspect(int id, int index, char *name, int name_len, float *host, unsigned long n_floats) {

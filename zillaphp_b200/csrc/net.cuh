@@ -50,6 +50,12 @@ struct PeerState {
     std::vector<void *> opened;            // IPC mappings to close
     unsigned long long step = 0;           // peer steps taken
     long long lo = 0, hi = 0, chunk = 0;   // owned slice [lo, hi); slices of `chunk` floats
+    // two-phase steps: the late layers' part of the slice is exchanged and updated on a side
+    // stream while the backward of the early layers runs (peer_step_mid)
+    cudaStream_t side_stream = nullptr;
+    cudaEvent_t ev_mid = nullptr, ev_side = nullptr;
+    long long mid_off = -1;                // first parameter of the late layers this step (-1: one phase)
+    bool two_phase = true;                 // use peer_step_mid (ZB_PEER_TWO_PHASE=0 turns it off)
 };
 
 struct TcEngine;  // bf16 tensor-core engine (tc_net.cu)
@@ -85,6 +91,11 @@ struct Net {
     float *sx[2] = {nullptr, nullptr}, *sy[2] = {nullptr, nullptr};
     cudaEvent_t ev_staged[2] = {nullptr, nullptr}, ev_consumed[2] = {nullptr, nullptr};
     int stage_head = 0, stage_tail = 0, stage_count = 0;
+    // deferred loss reads (zilla_net_step_staged_deferred): two pinned host slots
+    float *loss_host = nullptr;
+    cudaEvent_t ev_loss[2] = {nullptr, nullptr};
+    int loss_next = 0;        // slot the next deferred step writes
+    int loss_pending = -1;    // slot holding a loss not yet handed to the caller (-1: none)
     // per-step CUDA graphs (zilla_net_set_graph): one per (x, y, update) on one rank
     bool graph_on = false;
     struct StepGraph {
@@ -143,5 +154,8 @@ int peer_detach(Net &n);                   // collective: gathers the Adam state
 void peer_release(Net &n);                 // local: unmaps and frees
 int peer_step_begin(Net &n);               // gradients of this step go to the exchange buffer
 int peer_step_end(Net &n);                 // exchange + update + wait for every rank's slice
+// Gradients [off, nparams] of this step are final: their part of the slice is exchanged and
+// updated on a side stream while the rest of the backward runs; no-op off the peer path.
+int peer_step_mid(Net &n, long long off);
 
 }  // namespace zb

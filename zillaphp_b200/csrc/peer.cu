@@ -51,13 +51,20 @@ struct PeerArgs {
     unsigned long long *my_flags;
     unsigned int *done;
     float *m, *v, *api_grads;
-    long long lo, hi, nparams;
+    long long lo, hi, nparams;                       // [lo, hi): the part of the slice this launch updates
     int world, rank, opt;                            // opt 2 = Adam, else SGD
+    int slot;                                        // flag word published / awaited: "gradients final"
+    int do_loss;                                     // this launch sums the loss slot
+    int written;                                     // the last block publishes "slice written" (slot 8)
     unsigned long long step;
     AdamArgs a;
     float lr, scale;
     int *err;
 };
+
+constexpr int kSlotFinalA = 0;   // gradients of the late layers (the first launch of a two-phase step)
+constexpr int kSlotFinalB = 1;   // gradients of the early layers (the second launch)
+constexpr int kSlotWritten = 8;  // this rank's whole slice of the step stored into every rank
 
 __device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -97,18 +104,22 @@ __device__ __forceinline__ void update_one(const PeerArgs &A, float &w, float g,
     else w = __fsub_rn(w, __fmul_rn(A.lr, __fmul_rn(g, A.scale)));   // as the SGD kernel: no FMA
 }
 
-__global__ void __launch_bounds__(256) peer_update_kernel(const __grid_constant__ PeerArgs A) {
+// 128-thread blocks: with 74 registers a block (10,240 registers) fits beside one CTA of the
+// fused conv backward (14 warps x 120 registers), so the first launch of a two-phase step runs
+// on the SMs that kernel occupies.
+__global__ void __launch_bounds__(128, 6) peer_update_kernel(const __grid_constant__ PeerArgs A) {
     __shared__ int ok;
     if (threadIdx.x < 32) {
-        // this rank's gradients (written by the kernels before this one) are final
-        if (threadIdx.x == 0) st_release_sys(A.my_flags, A.step);
-        const bool w = wait_peers(A, 0, A.step);
+        // this rank's gradients of the range (written by the kernels before this one) are final
+        if (threadIdx.x == 0) st_release_sys(A.my_flags + A.slot, A.step);
+        const bool w = wait_peers(A, A.slot, A.step);
         if (threadIdx.x == 0) ok = w;
     }
     __syncthreads();
     if (ok) {
         float *own = A.params[A.rank];
-        const long long b4 = A.lo >> 2, e4 = A.hi >> 2;   // float4 groups of [lo, hi) (lo is a multiple of 4)
+        // float4 groups inside [lo, hi); the < 4 elements before and after them are done singly
+        const long long b4 = (A.lo + 3) >> 2, e4 = A.hi >> 2;
         const long long stride = (long long)gridDim.x * blockDim.x;
         for (long long i4 = b4 + blockIdx.x * blockDim.x + threadIdx.x; i4 < e4; i4 += stride) {
             // all ranks' loads in flight together, then the sum in rank order
@@ -133,10 +144,12 @@ __global__ void __launch_bounds__(256) peer_update_kernel(const __grid_constant_
             for (int q = 0; q < kMaxPeers; ++q)
                 if (q < A.world) reinterpret_cast<float4 *>(A.params[q])[i4] = w;
         }
-        if (blockIdx.x == 0 && threadIdx.x < 4) {
-            // the slice's last elements past the float4 groups (fewer than 4)
-            const long long e = 4 * e4 + threadIdx.x;
-            if (e >= A.lo && e < A.hi) {
+        if (blockIdx.x == 0 && threadIdx.x < 8) {
+            // threads 0-3: [lo, min(4 b4, hi)); threads 4-7: [max(4 e4, 4 b4), hi)
+            const long long head_end = 4 * b4 < A.hi ? 4 * b4 : A.hi;
+            const long long tail_beg = 4 * e4 > 4 * b4 ? 4 * e4 : 4 * b4;
+            const long long e = threadIdx.x < 4 ? A.lo + threadIdx.x : tail_beg + (threadIdx.x - 4);
+            if (threadIdx.x < 4 ? e < head_end : e < A.hi) {
                 float g = __ldcg(A.ex[0] + e);
                 for (int q = 1; q < A.world; ++q) g += __ldcg(A.ex[q] + e);
                 float w = own[e], m = A.m[e], v = A.v[e];
@@ -147,7 +160,7 @@ __global__ void __launch_bounds__(256) peer_update_kernel(const __grid_constant_
                 for (int q = 0; q < A.world; ++q) A.params[q][e] = w;
             }
         }
-        if (blockIdx.x == 0 && threadIdx.x == 0) {
+        if (A.do_loss && blockIdx.x == 0 && threadIdx.x == 0) {
             float l = 0.0f;   // the loss slot: sum over the ranks
             for (int q = 0; q < A.world; ++q) l += __ldcg(A.ex[q] + A.nparams);
             A.api_grads[A.nparams] = l;
@@ -160,13 +173,13 @@ __global__ void __launch_bounds__(256) peer_update_kernel(const __grid_constant_
         if (atomicAdd(A.done, 1u) == gridDim.x - 1) {
             *A.done = 0;
             __threadfence_system();
-            if (ok) st_release_sys(A.my_flags + 8, A.step);
+            if (ok && A.written) st_release_sys(A.my_flags + kSlotWritten, A.step);
         }
     }
 }
 
 __global__ void peer_wait_kernel(const __grid_constant__ PeerArgs A) {
-    wait_peers(A, 8, A.step);   // one warp
+    wait_peers(A, kSlotWritten, A.step);   // one warp
 }
 
 #ifdef ZB_HAVE_NCCL
@@ -220,6 +233,13 @@ PeerArgs make_args(Net &n, unsigned long long step) {
 
 void peer_release(Net &n) {
     PeerState &P = n.peer;
+    if (P.side_stream) {
+        cudaStreamSynchronize(P.side_stream);
+        cudaStreamDestroy(P.side_stream);
+        cudaEventDestroy(P.ev_mid);
+        cudaEventDestroy(P.ev_side);
+        P.side_stream = nullptr;
+    }
     if (!P.flags && !P.ex[0] && P.opened.empty()) return;
     cudaStreamSynchronize(stream());
     for (void *p : P.opened) cudaIpcCloseMemHandle(p);
@@ -303,6 +323,9 @@ int peer_attach(Net &n) {
         peer_release(n);
         return kOk;
     }
+    // ZB_PEER_TWO_PHASE=0: one update kernel after the whole backward (no side stream)
+    const char *tp = getenv("ZB_PEER_TWO_PHASE");
+    P.two_phase = !(tp && tp[0] == '0');
     P.chunk = ((n.nparams + n.world - 1) / n.world + 3) / 4 * 4;
     P.lo = P.chunk * n.rank < n.nparams ? P.chunk * n.rank : n.nparams;
     P.hi = P.lo + P.chunk < n.nparams ? P.lo + P.chunk : n.nparams;
@@ -345,7 +368,47 @@ int peer_step_begin(Net &n) {
     PeerState &P = n.peer;
     P.step += 1;
     P.in_step = true;
+    P.mid_off = -1;
     n.grads = P.ex[P.step & 1];
+    return kOk;
+}
+
+namespace {
+
+int update_grid(long long count, int per_sm) {
+    const long long n4 = count / 4 + 2;
+    long long grid = (n4 + 127) / 128;
+    if (grid > (long long)sm_count() * per_sm) grid = (long long)sm_count() * per_sm;
+    return grid < 1 ? 1 : (int)grid;
+}
+
+}  // namespace
+
+int peer_step_mid(Net &n, long long off) {
+    PeerState &P = n.peer;
+    if (!P.on || !P.in_step || P.mid_off >= 0 || off <= 0 || off >= n.nparams || !P.two_phase) return kOk;
+    if (!P.side_stream) {   // first use: the side stream and its two events
+        if (cudaStreamCreateWithFlags(&P.side_stream, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&P.ev_mid, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&P.ev_side, cudaEventDisableTiming) != cudaSuccess)
+            return check_cuda("peer: side stream");
+    }
+    // gradients [off, nparams] (and the loss slot) of this step are final: exchange and update
+    // the part of this rank's slice above `off` on the side stream, while the backward goes on
+    if (cudaEventRecord(P.ev_mid, stream()) != cudaSuccess || cudaStreamWaitEvent(P.side_stream, P.ev_mid, 0) != cudaSuccess)
+        return check_cuda("peer: mid-step ordering");
+    P.mid_off = off;
+    PeerArgs A = make_args(n, P.step);
+    A.a = make_adam_args(n.lr, n.b1, n.b2, n.eps, n.t + 1, A.scale);
+    A.lo = P.lo > off ? P.lo : off;
+    A.hi = P.hi;
+    if (A.hi < A.lo) A.hi = A.lo;
+    A.slot = kSlotFinalA;
+    A.do_loss = 1;
+    A.written = 0;
+    peer_update_kernel<<<update_grid(A.hi - A.lo, 1), 128, 0, P.side_stream>>>(A);
+    ZB_LAUNCH_CHECK("peer update (late layers)");
+    if (cudaEventRecord(P.ev_side, P.side_stream) != cudaSuccess) return check_cuda("peer: side event");
     return kOk;
 }
 
@@ -356,11 +419,19 @@ int peer_step_end(Net &n) {
     n.t += 1;
     PeerArgs A = make_args(n, P.step);
     A.a = make_adam_args(n.lr, n.b1, n.b2, n.eps, n.t, A.scale);
-    const long long n4 = (P.hi - P.lo) / 4 + 1;
-    int grid = (int)((n4 + 255) / 256);
-    if (grid > sm_count() * 2) grid = sm_count() * 2;
-    if (grid < 1) grid = 1;
-    peer_update_kernel<<<grid, 256, 0, stream()>>>(A);
+    A.written = 1;
+    if (P.mid_off >= 0) {   // second phase: the early layers [0, mid_off) after the first one
+        if (cudaStreamWaitEvent(stream(), P.ev_side, 0) != cudaSuccess) return check_cuda("peer: join");
+        A.hi = P.hi < P.mid_off ? P.hi : P.mid_off;
+        if (A.hi < A.lo) A.hi = A.lo;
+        A.slot = kSlotFinalB;
+        A.do_loss = 0;
+        P.mid_off = -1;
+    } else {                // one phase: the whole slice
+        A.slot = kSlotFinalA;
+        A.do_loss = 1;
+    }
+    peer_update_kernel<<<update_grid(A.hi - A.lo, 2), 128, 0, stream()>>>(A);
     ZB_LAUNCH_CHECK("peer update");
     peer_wait_kernel<<<1, 32, 0, stream()>>>(A);
     ZB_LAUNCH_CHECK("peer wait");

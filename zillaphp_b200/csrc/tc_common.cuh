@@ -334,6 +334,11 @@ __device__ __forceinline__ bool elect_one() {
 // strides in bytes for dims 1..rank-1).  Returns 0 on success.
 int make_tmap_bf16(CUtensorMap *map, const void *base, int rank, const uint64_t *dims, const uint64_t *strides,
                    const uint32_t *box, Swizzle sw);
+// The same for an fp32 tensor, and for any element type.
+int make_tmap_f32(CUtensorMap *map, const void *base, int rank, const uint64_t *dims, const uint64_t *strides,
+                  const uint32_t *box, Swizzle sw);
+int make_tmap_typed(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, int rank, const uint64_t *dims,
+                    const uint64_t *strides, const uint32_t *box, Swizzle sw);
 
 }  // namespace tc
 }  // namespace zb

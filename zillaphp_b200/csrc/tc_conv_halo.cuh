@@ -115,7 +115,8 @@ struct ConvHaloShape {
         const int epi = POOL_STAGE > out_total ? POOL_STAGE : out_total;
         return 1024 + BTOTAL + NS * stage + SLACK + epi + BIAS_BYTES + BAR_BYTES;
     }
-    static_assert(CIN % 16 == 0 && SC % 16 == 0 && COUT % 32 == 0 && COUT <= 256, "unsupported conv channels");
+    static_assert(CIN % 16 == 0 && SC % 16 == 0 && COUT % 16 == 0 && COUT <= 256, "unsupported conv channels");
+    static_assert(!POOL || COUT % 32 == 0, "the pool epilogue works on 32-channel chunks");
     static_assert(CIN <= 64 || CIN % 64 == 0, "CIN above 64 must be a multiple of 64");
     static_assert(SC % CHUNK == 0 || CHUNK % SC == 0, "stage channels and weight chunks must nest");
 };
@@ -361,7 +362,9 @@ __global__ void __launch_bounds__(UP ? 448 : 320, UP ? 1 : 2) conv_halo_kernel(c
         const int etid = threadIdx.x - 64;      // 0..255
         const int r = row / p.Wp, c = row - r * p.Wp;
         const bool in_tile = (r < p.R) && (c < p.W);
-        constexpr int NCC = COUT / 32;
+        constexpr int NCC = COUT / 32;          // 32-column accumulator chunks (pool epilogue)
+        constexpr int CW = COUT % 32 == 0 ? 32 : 16;   // chunk width of the other epilogues
+        constexpr int NCW = COUT / CW;
         constexpr int OCT = COUT / 8;           // channel octets per pixel
         const int Wo = p.W >> 1, Ho = p.H >> 1;
         const int nitems = (p.R >> 1) * Wo * OCT;
@@ -385,7 +388,7 @@ __global__ void __launch_bounds__(UP ? 448 : 320, UP ? 1 : 2) conv_halo_kernel(c
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * COUT);
             const int h = h0 + r;
             const bool pix_ok = in_tile && (h < p.H);
-            if (grp >= NCC) {   // no chunk for this group (COUT = 32)
+            if (grp >= (EPI == kEpiPool ? NCC : NCW)) {   // no chunk for this group (COUT = 32, or 16)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -446,10 +449,11 @@ __global__ void __launch_bounds__(UP ? 448 : 320, UP ? 1 : 2) conv_halo_kernel(c
                 if constexpr (S::NSBUF == 2) sb ^= 1;
             } else {
 #pragma unroll 1
-                for (int cc = grp; cc < NCC; cc += 2) {
-                    float v[32];
-                    tmem_ld32(taddr + 32 * cc, v);
-                    if (cc + 2 >= NCC) {   // this group's last chunk: the accumulator is free
+                for (int cc = grp; cc < NCW; cc += 2) {
+                    float v[CW];
+                    if constexpr (CW == 32) tmem_ld32(taddr + 32 * cc, v);
+                    else tmem_ld16(taddr + 16 * cc, v);
+                    if (cc + 2 >= NCW) {   // this group's last chunk: the accumulator is free
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -458,9 +462,9 @@ __global__ void __launch_bounds__(UP ? 448 : 320, UP ? 1 : 2) conv_halo_kernel(c
                         if (!in_tile) continue;   // rows past H are clipped by the TMA store
                         if (p.mask && pix_ok) {
                             const uint4 *mk = reinterpret_cast<const uint4 *>(
-                                p.mask + (((size_t)b * p.H + h) * p.W + c) * COUT + 32 * cc);
+                                p.mask + (((size_t)b * p.H + h) * p.W + c) * COUT + CW * cc);
 #pragma unroll
-                            for (int q4 = 0; q4 < 4; ++q4) {
+                            for (int q4 = 0; q4 < CW / 8; ++q4) {
                                 uint4 m = __ldg(mk + q4);
                                 const __nv_bfloat16 *mb = reinterpret_cast<const __nv_bfloat16 *>(&m);
 #pragma unroll
@@ -473,9 +477,9 @@ __global__ void __launch_bounds__(UP ? 448 : 320, UP ? 1 : 2) conv_halo_kernel(c
                         constexpr int RB = COUT * 2;
                         constexpr uint32_t SWM = RB == 128 ? 7u : RB == 64 ? 3u : 1u;
                         uint8_t *tile_buf = reinterpret_cast<uint8_t *>(stage) + sb * p.out_tile_bytes;
-                        const uint32_t base_off = (uint32_t)((r * p.W + c) * RB + 64 * cc);
+                        const uint32_t base_off = (uint32_t)((r * p.W + c) * RB + 2 * CW * cc);
 #pragma unroll
-                        for (int q4 = 0; q4 < 4; ++q4) {
+                        for (int q4 = 0; q4 < CW / 8; ++q4) {
                             uint4 pk;
                             __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
 #pragma unroll
@@ -487,17 +491,17 @@ __global__ void __launch_bounds__(UP ? 448 : 320, UP ? 1 : 2) conv_halo_kernel(c
                         continue;
                     }
                     if (!pix_ok) continue;
-                    const size_t o = (((size_t)b * p.H + h) * p.W + c) * COUT + 32 * cc;
+                    const size_t o = (((size_t)b * p.H + h) * p.W + c) * COUT + CW * cc;
                     if constexpr (EPI == kEpiStore) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const float x = v[j] + __ldg(p.bias + 32 * cc + j);
+                        for (int j = 0; j < CW; ++j) {
+                            const float x = v[j] + __ldg(p.bias + CW * cc + j);
                             v[j] = x > 0.0f ? x : 0.0f;
                         }
                     } else if (p.mask) {
                         const uint4 *mk = reinterpret_cast<const uint4 *>(p.mask + o);
 #pragma unroll
-                        for (int q4 = 0; q4 < 4; ++q4) {
+                        for (int q4 = 0; q4 < CW / 8; ++q4) {
                             uint4 m = __ldg(mk + q4);
                             const __nv_bfloat16 *mb = reinterpret_cast<const __nv_bfloat16 *>(&m);
 #pragma unroll
@@ -507,7 +511,7 @@ __global__ void __launch_bounds__(UP ? 448 : 320, UP ? 1 : 2) conv_halo_kernel(c
                     }
                     uint4 *dst = reinterpret_cast<uint4 *>(p.out + o);
 #pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
+                    for (int q4 = 0; q4 < CW / 8; ++q4) {
                         uint4 pk;
                         __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
 #pragma unroll

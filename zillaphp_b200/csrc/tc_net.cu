@@ -44,8 +44,18 @@ namespace {
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 }
 
+int make_tmap_f32(CUtensorMap *map, const void *base, int rank, const uint64_t *dims, const uint64_t *strides,
+                  const uint32_t *box, Swizzle sw) {
+    return make_tmap_typed(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, rank, dims, strides, box, sw);
+}
+
 int make_tmap_bf16(CUtensorMap *map, const void *base, int rank, const uint64_t *dims, const uint64_t *strides,
                    const uint32_t *box, Swizzle sw) {
+    return make_tmap_typed(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, rank, dims, strides, box, sw);
+}
+
+int make_tmap_typed(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, int rank, const uint64_t *dims,
+                    const uint64_t *strides, const uint32_t *box, Swizzle sw) {
     if (!g_encode) {
         cudaDriverEntryPointQueryResult q;
         void *fn = nullptr;
@@ -64,7 +74,7 @@ int make_tmap_bf16(CUtensorMap *map, const void *base, int rank, const uint64_t 
                            : sw == kSw64 ? CU_TENSOR_MAP_SWIZZLE_64B
                            : sw == kSw32 ? CU_TENSOR_MAP_SWIZZLE_32B
                                          : CU_TENSOR_MAP_SWIZZLE_NONE;
-    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void *>(base), gd, gs,
+    CUresult r = g_encode(map, dtype, (cuuint32_t)rank, const_cast<void *>(base), gd, gs,
                           bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, s, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(kCudaError, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -82,6 +92,8 @@ using bf16 = __nv_bfloat16;
 //                 1 conv dgrad dst[t][ci][co] = W[co][ci][8-t]
 //                 2 linear W^T  dst[n][k]     = W[perm(k)][n]   (K-major forward B)
 //                 3 linear W    dst[k][n]     = W[perm(k)][n]   (K-major dgrad B)
+//                 4 classifier  dst[(k/8)*98 + (k%8)*NC + n] = W[perm(k)][n]  (direct head:
+//                   eight input rows of NC <= 12 bf16 per 196-byte group)
 // perm maps an NHWC flatten index of the previous activation to the NCHW
 // flatten index of the reference (src/Tensor/Tensor.php:958-981).
 struct PackJob {
@@ -103,6 +115,12 @@ __device__ __forceinline__ int nhwc_to_nchw(int k, int C, int H, int W) {
     return c * H * W + hw;
 }
 
+// Direct classifier head (Linear(F -> NC) right after the last pool): its bf16
+// weights in groups of eight input rows, 98 bf16 (196 bytes, 49 words) per
+// group.  Lane l of a warp reads group l + 32 j, so the 49-word pitch (odd)
+// spreads a warp's 32 reads over 32 banks.
+constexpr int kHeadGroup = 98;
+
 // bf16 conv weights in the tensor-core layouts (32-bit index math; the conv
 // weights are < 2^31 elements):
 //   kind 0 (forward): dst[(t*COUT + co)*CIN + ci] = W[co][ci][t]
@@ -115,6 +133,12 @@ __global__ void pack_kernel(PackJobs jobs) {
         const int n = (int)J.n;
         for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
             float v;
+            if (J.kind == 4) {   // i = k * NC + n over the classifier weight [F][NC]
+                const int n = i % J.b, k = i / J.b;
+                v = J.src[(size_t)nhwc_to_nchw(k, J.C, J.H, J.W) * J.b + n];
+                J.dst[(k >> 3) * kHeadGroup + (k & 7) * J.b + n] = __float2bfloat16_rn(v);
+                continue;
+            }
             if (J.kind == 0) {
                 const int ci = i % J.b, r = i / J.b, co = r % J.a, t = r / J.a;
                 v = J.src[(co * J.b + ci) * 9 + t];
@@ -340,8 +364,10 @@ __global__ void __launch_bounds__(256, 2) conv_first_fwd_img_kernel(const float 
 // and keeps 8 x 10 accumulators.  Lanes of a warp that share an octet are
 // combined by shuffles, warps in fixed order through shared memory: per-block
 // partials [block][COUT][10], summed later in block order.  Dynamic shared
-// memory: max((H+2p)(W+2p), 8*4*80) floats.
-template <int COUT>
+// memory: max((H+2p)(W+2p), 8*4*80) floats.  BIG: images past the 1024
+// elements the register stager holds (e.g. 64 x 101 spectrograms) are copied
+// into shared memory by a plain loop per image instead.
+template <int COUT, bool BIG = false>
 __global__ void __launch_bounds__(256, 2) conv_first_wgrad_kernel(const bf16 *__restrict__ dC,
                                                                const float *__restrict__ x,
                                                                float *__restrict__ partial, int B, int H, int W,
@@ -360,13 +386,24 @@ __global__ void __launch_bounds__(256, 2) conv_first_wgrad_kernel(const bf16 *__
 #pragma unroll
         for (int t = 0; t < 10; ++t) acc2[k][t] = make_float2(0.0f, 0.0f);
     ImageStager stg;
-    stg.init(H, W, pad);
-    if (blockIdx.x < B) stg.load(x + (size_t)blockIdx.x * H * W);
+    if constexpr (!BIG) {
+        stg.init(H, W, pad);
+        if (blockIdx.x < B) stg.load(x + (size_t)blockIdx.x * H * W);
+    }
     for (int b = blockIdx.x; b < B; b += gridDim.x) {
         __syncthreads();
-        stg.store(xs);
+        if constexpr (BIG) {
+            const float *xb = x + (size_t)b * H * W;
+            for (int i = threadIdx.x; i < PH * PW; i += 256) {
+                const int ih = i / PW - pad, iw = i - (i / PW) * PW - pad;
+                xs[i] = ((unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W) ? __ldg(xb + ih * W + iw) : 0.0f;
+            }
+        } else {
+            stg.store(xs);
+        }
         __syncthreads();
-        if (b + (int)gridDim.x < B) stg.load(x + (size_t)(b + gridDim.x) * H * W);
+        if constexpr (!BIG)
+            if (b + (int)gridDim.x < B) stg.load(x + (size_t)(b + gridDim.x) * H * W);
         const bf16 *gb = dC + (size_t)b * P * COUT + 8 * q;
         int oh = pl / oW, ow = pl - (pl / oW) * oW;
         for (int p0 = pl; p0 < P; p0 += U * LANES) {
@@ -662,12 +699,174 @@ __global__ void __launch_bounds__(256) head_fwd_kernel(const bf16 *__restrict__ 
     }
 }
 
+// Direct head: the classifier Linear (F -> NC, NC <= 12) on the flattened last
+// pooled activation a [B][F] (NHWC order, bf16), softmax cross-entropy and the
+// start of the backward, one warp per row:
+//   z = a W + b;  loss_r = -log softmax(z)[y];  dz = (p - onehot) / B
+//   dA = dz W^T -> bf16 [B][F]  (the pool's ReLU lives in the pool codes)
+// W comes packed in bf16 groups (kHeadGroup) and stays in shared memory
+// (F / 8 groups of 196 bytes: 147 KB at F = 6144).  Lane l owns the 8-input
+// groups l, l + 32, ... of the row: one 16-byte load of a per group.  dz goes
+// to global memory for the weight-gradient kernel; the block's bias-gradient
+// and loss partial is [NC + 1] (fixed warp order).  logits != null: the
+// evaluation forward (logits out, the loss partial only when y is given).
+template <int NC>
+__global__ void __launch_bounds__(256) head_direct_kernel(const bf16 *__restrict__ a, const bf16 *__restrict__ wq,
+                                                          const float *__restrict__ bias, const float *__restrict__ y,
+                                                          float *__restrict__ dz_out, bf16 *__restrict__ dA,
+                                                          float *__restrict__ logits, float *__restrict__ partial,
+                                                          int B, int F, float invB) {
+    extern __shared__ uint32_t sWq[];   // F / 8 groups of 49 words
+    __shared__ float sAcc[8][NC + 1];
+    __shared__ double sLoss[8];
+    griddep_launch();
+    griddep_wait();
+    const int G = F / 8;
+    for (int i = threadIdx.x; i < G * (kHeadGroup / 2); i += blockDim.x)
+        sWq[i] = reinterpret_cast<const uint32_t *>(wq)[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int GPL = G / 32;   // groups per lane
+    float gB[NC];
+#pragma unroll
+    for (int n = 0; n < NC; ++n) gB[n] = 0.0f;
+    double lsum = 0.0;
+    for (int r = blockIdx.x * 8 + warp; r < B; r += gridDim.x * 8) {
+        const uint4 *ar = reinterpret_cast<const uint4 *>(a + (size_t)r * F);
+        float z[NC];
+#pragma unroll
+        for (int n = 0; n < NC; ++n) z[n] = 0.0f;
+        for (int j = 0; j < GPL; ++j) {
+            const int g = lane + 32 * j;
+            const uint4 av = __ldg(ar + g);
+            const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+            const uint32_t *wg = sWq + g * (kHeadGroup / 2);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float ae = __uint_as_float(e & 1 ? aw[e >> 1] & 0xFFFF0000u : aw[e >> 1] << 16);
+#pragma unroll
+                for (int n = 0; n < NC; n += 2) {
+                    const uint32_t w2 = wg[(e * NC + n) >> 1];   // NC even: bf16 pairs (n, n + 1)
+                    z[n] = fmaf(ae, __uint_as_float(w2 << 16), z[n]);
+                    z[n + 1] = fmaf(ae, __uint_as_float(w2 & 0xFFFF0000u), z[n + 1]);
+                }
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < NC; ++n) {
+#pragma unroll
+            for (int o = 16; o; o >>= 1) z[n] += __shfl_xor_sync(0xffffffffu, z[n], o);
+            z[n] += bias[n];
+        }
+        if (logits && lane < NC) {
+            float zl = z[0];
+#pragma unroll
+            for (int n = 1; n < NC; ++n) if (lane == n) zl = z[n];
+            logits[(size_t)r * NC + lane] = zl;
+        }
+        if (!y) continue;
+        float mx = z[0];
+#pragma unroll
+        for (int n = 1; n < NC; ++n) mx = fmaxf(mx, z[n]);
+        float se = 0.0f;
+#pragma unroll
+        for (int n = 0; n < NC; ++n) se += expf(z[n] - mx);
+        const int t = (int)y[r];
+        float pt = 0.0f;
+#pragma unroll
+        for (int n = 0; n < NC; ++n) if (n == t) pt = expf(z[n] - mx) / se;
+        if (lane == 0) lsum += -(double)logf(pt);
+        if (logits) continue;
+        float dz[NC];
+#pragma unroll
+        for (int n = 0; n < NC; ++n) {
+            dz[n] = (expf(z[n] - mx) / se - (n == t ? 1.0f : 0.0f)) * invB;
+            gB[n] += dz[n];
+        }
+        if (lane < NC) {
+            float dl = dz[0];
+#pragma unroll
+            for (int n = 1; n < NC; ++n) if (lane == n) dl = dz[n];
+            dz_out[(size_t)r * NC + lane] = dl;
+        }
+        uint4 *dr = reinterpret_cast<uint4 *>(dA + (size_t)r * F);
+        for (int j = 0; j < GPL; ++j) {
+            const int g = lane + 32 * j;
+            const uint32_t *wg = sWq + g * (kHeadGroup / 2);
+            float o8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int n = 0; n < NC; n += 2) {
+                    const uint32_t w2 = wg[(e * NC + n) >> 1];
+                    acc = fmaf(dz[n], __uint_as_float(w2 << 16), acc);
+                    acc = fmaf(dz[n + 1], __uint_as_float(w2 & 0xFFFF0000u), acc);
+                }
+                o8[e] = acc;
+            }
+            uint4 pk;
+            __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h2[e] = __floats2bfloat162_rn(o8[2 * e], o8[2 * e + 1]);
+            dr[g] = pk;
+        }
+    }
+    if (!partial) return;
+    if (lane == 0) {
+#pragma unroll
+        for (int n = 0; n < NC; ++n) sAcc[warp][n] = gB[n];
+        sLoss[warp] = lsum;
+    }
+    __syncthreads();
+    if (threadIdx.x <= NC) {   // fixed warp order
+        float sacc = 0.0f;
+        double sl = 0.0;
+        for (int wv = 0; wv < 8; ++wv) {
+            if (threadIdx.x < NC) sacc += sAcc[wv][threadIdx.x];
+            else sl += sLoss[wv];
+        }
+        partial[(size_t)blockIdx.x * (NC + 1) + threadIdx.x] = threadIdx.x < NC ? sacc : (float)sl;
+    }
+}
+
+// Weight gradient of the direct head: dW[k][n] = sum_b a[b][k] dz[b][n] over a
+// slice of the batch, k in NHWC order.  Block = 64 inputs x a batch slice;
+// thread (k, n-group of NC / 4) keeps NC / 4 sums; a warp's 32 loads of a are
+// 64 contiguous bytes.  Partials [split][F][NC], summed in split order.
+template <int NC>
+__global__ void __launch_bounds__(256) head_direct_wgrad_kernel(const bf16 *__restrict__ a,
+                                                                const float *__restrict__ dz,
+                                                                float *__restrict__ partial, int B, int F,
+                                                                int splits) {
+    constexpr int NPT = NC / 4;   // classes per thread
+    griddep_launch();
+    griddep_wait();
+    const int kchunks = F / 64;
+    const int kc = blockIdx.x % kchunks, split = blockIdx.x / kchunks;
+    const int k = kc * 64 + (threadIdx.x & 63), n0 = (threadIdx.x >> 6) * NPT;
+    const int b0 = (int)((long long)B * split / splits), b1 = (int)((long long)B * (split + 1) / splits);
+    float acc[NPT];
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) acc[j] = 0.0f;
+    for (int b = b0; b < b1; ++b) {
+        const float av = __bfloat162float(a[(size_t)b * F + k]);
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) acc[j] = fmaf(av, __ldg(dz + (size_t)b * NC + n0 + j), acc[j]);
+    }
+    float *dst = partial + ((size_t)split * F + k) * NC + n0;
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) dst[j] = acc[j];
+}
+
 // Sums partial[s][i] over s in order and scatters into the gradient layout.
 // map 0: dst[i];  1 conv (M=COUT rows, N = 9*CIN, n = tap*CIN + ci) -> dst[(co*CIN+ci)*9+tap]
 //        2 conv (M = 9*CIN rows (tap*CIN+ci), N = COUT)  -> same dst layout
 //        3 linear (M = F rows in NHWC order, N = OUT)    -> dst[nchw(m)*OUT + n]
 //        4 head partial [HD*NC | NC | HD | 1] -> dW5, db5, db4, loss (four destinations)
 //        5 first conv [COUT][10] -> dW1[co*9+t], db1[co]
+//        6 fc1 forward split-K: relu(s + bias) -> bf16
+//        7 only the last element, into *dst4 (a loss behind zero partials)
 struct ReduceArgs {
     const float *partial;
     int splits;
@@ -816,6 +1015,7 @@ __device__ void r_store(const ReduceArgs &r, long long i, float s) {
         }
         case 5: { const int co = (int)(i / 10), t = (int)(i % 10); if (t < 9) r.dst[co * 9 + t] = s; else r.dst2[co] = s; break; }
         case 6: { const float x = s + r.bias[n]; r.out_bf16[i] = __float2bfloat16_rn(x > 0.0f ? x : 0.0f); break; }
+        case 7: if (i == r.n - 1) *r.dst4 = s; break;   // the last element only (a loss)
         }
     }
 }
@@ -889,6 +1089,12 @@ struct TcEngine {
     float *fc_fwd_partial = nullptr;   // [ksplit][B][HD] when the forward splits K
     float *head_partial = nullptr;
     int head_grid = 0;
+    // direct head: the classifier straight after the last pool (no hidden Linear)
+    bool direct_head = false;
+    bf16 *wq = nullptr;                  // packed classifier weights (kHeadGroup groups)
+    float *dz = nullptr;                 // [B][NC] logit gradients
+    int hdw_splits = 0;
+    float *hdw_partial = nullptr;        // [hdw_splits][F][NC]
     double *row_loss = nullptr;
     PackJobs pack{};
     std::vector<void *> allocs;
@@ -933,7 +1139,7 @@ int launch_conv(const ConvTcParams &p) {
 }
 
 bool conv_shape_supported(int cin, int cout) {
-    return (cin == 32 && cout == 64) || (cin == 64 && cout == 128);
+    return (cin == 16 && cout == 32) || (cin == 32 && cout == 64) || (cin == 64 && cout == 128);
 }
 
 template <int CIN, int COUT, int EPI, int NS, int KS, int OB = 2, bool UP = false>
@@ -968,9 +1174,11 @@ int launch_halo(const ConvHaloParams &p0, int up_grid = 0) {
 
 int run_conv_fwd(const ConvLayer &L) {
     if (L.halo) {
+        if (L.CIN == 16 && L.COUT == 32) return launch_halo<16, 32, tc::kEpiPool, 4, 1>(L.hfwd);
         if (L.CIN == 32 && L.COUT == 64) return launch_halo<32, 64, tc::kEpiPool, 3, 1>(L.hfwd);
         if (L.CIN == 64 && L.COUT == 128) return launch_halo<64, 128, tc::kEpiPool, 2, 1>(L.hfwd);
     }
+    if (L.CIN == 16) return fail(kBadArg, "tc engine: 16 -> 32 conv needs halo tiles (R * (W + 2) <= 128)");
     if (L.CIN == 32 && L.COUT == 64) return launch_conv<32, 64, tc::kEpiPool, 6>(L.fwd);
     if (L.CIN == 64 && L.COUT == 128) return launch_conv<64, 128, tc::kEpiPool, 6, true>(L.fwd);
     return fail(kBadArg, "tc engine: no forward conv kernel for %d->%d", L.CIN, L.COUT);
@@ -984,9 +1192,11 @@ int run_conv_dgrad(const ConvLayer &L, const bf16 *dp) {
         return launch_halo<128, 64, tc::kEpiDgrad, 3, 2, 1, true>(p, L.up_grid);
     }
     if (L.halo) {
+        if (L.CIN == 16 && L.COUT == 32) return launch_halo<32, 16, tc::kEpiDgrad, 3, 1, 2>(L.hdgrad);
         if (L.CIN == 32 && L.COUT == 64) return launch_halo<64, 32, tc::kEpiDgrad, 2, 1, 2>(L.hdgrad);
         if (L.CIN == 64 && L.COUT == 128) return launch_halo<128, 64, tc::kEpiDgrad, 3, 2, 1>(L.hdgrad);
     }
+    if (L.CIN == 16) return fail(kBadArg, "tc engine: 16 -> 32 conv needs halo tiles (R * (W + 2) <= 128)");
     if (L.CIN == 32 && L.COUT == 64) return launch_conv<64, 32, tc::kEpiDgrad, 4>(L.dgrad);
     if (L.CIN == 64 && L.COUT == 128) return launch_conv<128, 64, tc::kEpiDgrad, 4, true>(L.dgrad);
     return fail(kBadArg, "tc engine: no dgrad conv kernel for %d->%d", L.CIN, L.COUT);
@@ -1050,6 +1260,7 @@ int run_conv_bwd_fused(const ConvLayer &L, const float *x0, const bf16 *dp) {
 }
 
 int run_wgrad_halo(const ConvLayer &L) {
+    if (L.CIN == 16 && L.COUT == 32) return launch_wgrad_halo<16, 32, 1, 6>(L.whalo, L.whalo_grid);
     if (L.CIN == 32 && L.COUT == 64) return launch_wgrad_halo<32, 64, 1, 6>(L.whalo, L.whalo_grid);
     if (L.CIN == 64 && L.COUT == 128) return launch_wgrad_halo<64, 128, 2, 4>(L.whalo, L.whalo_grid);
     return fail(kBadArg, "tc engine: no halo weight-gradient kernel for %d->%d", L.CIN, L.COUT);
@@ -1164,11 +1375,14 @@ int tc_build(Net &n, TcEngine &e) {
     e.C1 = st[0].oC; e.H0 = st[0].H; e.W0 = st[0].W; e.pad1 = st[0].pad;
     e.H1 = st[0].oH; e.W1 = st[0].oW;
     if (e.C1 != 16 && e.C1 != 32) return fail(kBadArg, "tc engine: first conv must have 16 or 32 outputs");
-    if ((e.H0 + 2 * e.pad1) * (e.W0 + 2 * e.pad1) > kStageRegs * 256)
-        return fail(kBadArg, "tc engine: first-conv image too large (padded %d x %d)", e.H0 + 2 * e.pad1,
-                    e.W0 + 2 * e.pad1);
     i = 1;
     e.c1_pool = i < st.size() && st[i].kind == kPool;
+    {   // the unpooled forward stages the padded image in registers; the weight gradient in shared memory
+        const int padded = (e.H0 + 2 * e.pad1) * (e.W0 + 2 * e.pad1);
+        if ((!e.c1_pool && padded > kStageRegs * 256) || padded * (int)sizeof(float) > 48 * 1024)
+            return fail(kBadArg, "tc engine: first-conv image too large (padded %d x %d)", e.H0 + 2 * e.pad1,
+                        e.W0 + 2 * e.pad1);
+    }
     int C = e.C1, H = e.H1, W = e.W1;
     if (e.c1_pool) { H = st[i].oH; W = st[i].oW; ++i; }
     int rc;
@@ -1292,7 +1506,7 @@ int tc_build(Net &n, TcEngine &e) {
                 f.bias_partial = L.fbwd_bias_partial;
             }
         }
-        L.wg_halo = !L.fused_bwd && L.halo && L.CIN == 32 && L.COUT == 64;
+        L.wg_halo = !L.fused_bwd && L.halo && ((L.CIN == 32 && L.COUT == 64) || (L.CIN == 16 && L.COUT == 32));
         if (L.wg_halo) {
             WgradHaloParams &w = L.whalo;
             const int ngrp = L.COUT == 128 ? 2 : 1;
@@ -1322,6 +1536,9 @@ int tc_build(Net &n, TcEngine &e) {
             g.m_tiles = 3; g.M = L.COUT; g.N = 9 * L.CIN;
             g.splits = (sm_count() / 3) > 0 ? sm_count() / 3 : 1;
             L.wg_smem = tc::WgradTcShape<tc::kWgConvCo>::smem(g.kstage_rows);
+        } else if (L.CIN == 16 && L.wg_halo) {
+            L.wg_mode = -1;   // the halo weight gradient above; no per-tap fallback for 16 channels
+            g.m_tiles = 1; g.M = L.COUT; g.N = 9 * L.CIN; g.splits = 1;
         } else if (L.CIN == 32 && L.COUT == 64) {
             L.wg_mode = tc::kWgConvTap;
             if ((rc = nhwc_map(&g.a_map, prev, L.CIN, L.W, L.H, B, 32, L.W, L.R))) return rc;
@@ -1444,14 +1661,35 @@ int tc_build(Net &n, TcEngine &e) {
         return fail(kBadArg, "tc engine: the network must end with Linear(-> classes)");
     e.head_si = (int)i;
     e.NC = st[i].oC;
-    if (!e.has_hidden) return fail(kBadArg, "tc engine: a hidden Linear + ReLU before the classifier is required");
-    if (e.HD != 256 || e.NC != 10) return fail(kBadArg, "tc engine: head %d->%d not supported", e.HD, e.NC);
+    if (!e.has_hidden) {
+        // classifier on the flattened last pooled activation: packed bf16 weights in shared
+        // memory, logit gradients to global memory for the weight-gradient kernel
+        e.direct_head = true;
+        if (e.NC != 12 || e.F % 256 || (size_t)e.F / 8 * kHeadGroup * 2 > 200 * 1024)
+            return fail(kBadArg, "tc engine: classifier %d->%d after the last pool not supported", e.F, e.NC);
+        if ((rc = dalloc(e, &e.dflat, (size_t)B * e.F))) return rc;
+        if ((rc = dalloc(e, &e.wq, (size_t)e.F / 8 * kHeadGroup))) return rc;
+        if ((rc = dalloc(e, &e.dz, (size_t)B * e.NC))) return rc;
+        e.head_grid = (B + 7) / 8;
+        if (e.head_grid > sm_count()) e.head_grid = sm_count();
+        if ((rc = dalloc(e, &e.head_partial, (size_t)e.head_grid * (e.NC + 1)))) return rc;
+        // weight gradient: 64-input chunks x batch slices, about four blocks per SM
+        const int kchunks = e.F / 64;
+        e.hdw_splits = (sm_count() * 4 + kchunks - 1) / kchunks;
+        if (e.hdw_splits > B) e.hdw_splits = B;
+        if (e.hdw_splits < 1) e.hdw_splits = 1;
+        if ((rc = dalloc(e, &e.hdw_partial, (size_t)e.hdw_splits * e.F * e.NC))) return rc;
+    } else if (e.HD != 256 || e.NC != 10) {
+        return fail(kBadArg, "tc engine: head %d->%d not supported", e.HD, e.NC);
+    }
     // a row per warp up to two blocks per SM (small batches: the kernel is
     // latency-bound, so more SMs), then more rows per warp (the block set-up,
     // W staging and partial write, is the fixed cost; fewer partials to sum)
-    e.head_grid = (B + 7) / 8;
-    if (e.head_grid > sm_count() * 2) e.head_grid = sm_count() * 2;
-    if ((rc = dalloc(e, &e.head_partial, (size_t)e.head_grid * (e.HD * e.NC + e.NC + e.HD + 1)))) return rc;
+    if (!e.direct_head) {
+        e.head_grid = (B + 7) / 8;
+        if (e.head_grid > sm_count() * 2) e.head_grid = sm_count() * 2;
+        if ((rc = dalloc(e, &e.head_partial, (size_t)e.head_grid * (e.HD * e.NC + e.NC + e.HD + 1)))) return rc;
+    }
     if ((rc = dalloc(e, &e.row_loss, (size_t)B))) return rc;
     e.c1_wgrad_grid = sm_count() * 2;   // the resident blocks (two per SM): each walks whole images
     if (e.c1_wgrad_grid > B) e.c1_wgrad_grid = B;
@@ -1464,6 +1702,10 @@ int tc_build(Net &n, TcEngine &e) {
     // diagnostics
     e.views.push_back({"conv1.out", e.a1, (size_t)B * (e.c1_pool ? (e.H1 / 2) * (e.W1 / 2) : e.H1 * e.W1) * e.C1, 0});
     if (!e.c1_fused) e.views.push_back({"conv1.dC", e.dC1, (size_t)B * e.H1 * e.W1 * e.C1, 0});
+    if (e.c1_pool) {
+        e.views.push_back({"conv1.code", e.code1, (size_t)B * (e.H1 / 2) * (e.W1 / 2) * e.C1, 1});
+        e.views.push_back({"conv1.dP", e.dP1, (size_t)B * (e.H1 / 2) * (e.W1 / 2) * e.C1, 0});
+    }
     for (size_t k = 0; k < e.convs.size(); ++k) {
         const ConvLayer &L = e.convs[k];
         const std::string pre = "conv" + std::to_string(k + 2);
@@ -1475,11 +1717,17 @@ int tc_build(Net &n, TcEngine &e) {
         e.views.push_back({pre + ".wf", L.wf, (size_t)9 * L.CIN * L.COUT, 0});
         e.views.push_back({pre + ".wd", L.wd, (size_t)9 * L.CIN * L.COUT, 0});
     }
-    e.views.push_back({"hidden.out", e.a_hid, (size_t)B * e.HD, 0});
-    e.views.push_back({"hidden.dZ", e.dZ_hid, (size_t)B * e.HD, 0});
+    if (e.has_hidden) {
+        e.views.push_back({"hidden.out", e.a_hid, (size_t)B * e.HD, 0});
+        e.views.push_back({"hidden.dZ", e.dZ_hid, (size_t)B * e.HD, 0});
+    }
     e.views.push_back({"flat.d", e.dflat, (size_t)B * e.F, 0});
-    e.views.push_back({"hidden.wT", e.wT, (size_t)e.F * e.HD, 0});
-    e.views.push_back({"hidden.wP", e.wP, (size_t)e.F * e.HD, 0});
+    if (e.has_hidden) {
+        e.views.push_back({"hidden.wT", e.wT, (size_t)e.F * e.HD, 0});
+        e.views.push_back({"hidden.wP", e.wP, (size_t)e.F * e.HD, 0});
+    } else {
+        e.views.push_back({"head.dz", e.dz, (size_t)B * e.NC, 2});
+    }
     // conv weight packing jobs (the hidden Linear weight has its own kernel)
     PackJobs &pj = e.pack;
     pj.count = 0;
@@ -1488,6 +1736,8 @@ int tc_build(Net &n, TcEngine &e) {
         pj.j[pj.count++] = {0, n.params + s.poff, L.wf, L.COUT, L.CIN, 0, 0, 0, (long long)9 * L.CIN * L.COUT};
         pj.j[pj.count++] = {1, n.params + s.poff, L.wd, L.COUT, L.CIN, 0, 0, 0, (long long)9 * L.CIN * L.COUT};
     }
+    if (e.direct_head)   // the classifier weight [F][NC] in its grouped bf16 layout
+        pj.j[pj.count++] = {4, n.params + st[e.head_si].poff, e.wq, e.F, e.NC, e.fC, e.fH, e.fW, (long long)e.F * e.NC};
     return kOk;
 }
 
@@ -1500,7 +1750,7 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
     // ---- pack bf16 operands from the fp32 master
     launch_pdl(pack_kernel, dim3(sm_count()), dim3(256), 0, e.pack);
     ZB_LAUNCH_CHECK("pack");
-    {
+    if (e.has_hidden) {
         const float *W4 = n.params + st[e.hid_si].poff;
         launch_pdl(pack_fc_kernel, dim3((e.F + 31) / 32, (e.HD + 31) / 32), dim3(256), 0, W4, e.wP, e.wT, e.F, e.HD,
                    e.fC, e.fH, e.fW);
@@ -1515,7 +1765,7 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
         const int grid = grid_for(pix, 128, 8);
         const size_t xsm = (size_t)(e.H0 + 2 * e.pad1) * (e.W0 + 2 * e.pad1) * sizeof(float);
         const int gimg = B < sm_count() * 4 ? B : sm_count() * 4;
-        if ((e.H0 + 2 * e.pad1) * (e.W0 + 2 * e.pad1) > kStageRegs * 256)
+        if (!e.c1_pool && (e.H0 + 2 * e.pad1) * (e.W0 + 2 * e.pad1) > kStageRegs * 256)
             return fail(kBadArg, "tc engine: first-conv image too large (padded %d x %d)", e.H0 + 2 * e.pad1,
                         e.W0 + 2 * e.pad1);
         const bool same = e.pad1 == 1 && e.H1 == e.H0 && e.W1 == e.W0;   // 3x3, pad 1
@@ -1536,7 +1786,47 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
         if ((rc = run_conv_fwd(L))) return rc;
         prof_mark(n, "conv_fwd");
     }
-    if (e.fc_fwd.ksplit > 1) {
+    if (e.direct_head) {   // the classifier follows the last pool: forward, loss and dA in one kernel
+        const Stage &sf = st[e.head_si];
+        const int smem = e.F / 8 * kHeadGroup * 2;
+        static int attr = 0;
+        if (attr < smem) {
+            if (cudaFuncSetAttribute(head_direct_kernel<12>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+                return check_cuda("head_direct smem attribute");
+            attr = smem;
+        }
+        const bf16 *flat = e.convs.empty() ? e.a1 : e.convs.back().out;
+        float *gW = n.grads + sf.poff, *gb = gW + sf.pn_w;
+        launch_pdl(head_direct_kernel<12>, dim3(e.head_grid), dim3(256), smem, flat, e.wq, n.params + sf.poff + sf.pn_w,
+                   y, logits_out ? nullptr : e.dz, logits_out ? nullptr : e.dflat, logits_out,
+                   (logits_out && !(y && loss_out)) ? nullptr : e.head_partial, B, e.F, 1.0f / (float)B);
+        ZB_LAUNCH_CHECK("head direct");
+        if (logits_out) {
+            if (y && loss_out) {   // only the loss of the evaluation partials [NC zeros | loss] is kept
+                ReduceArgs r{e.head_partial, e.head_grid, e.NC + 1, 7, 0, e.NC, 0, 0, 0, 0, nullptr, nullptr, nullptr};
+                r.dst4 = loss_out;
+                if ((rc = reduce(r))) return rc;
+            }
+            prof_mark(n, "softmax_ce");
+            return kOk;
+        }
+        {   // classifier bias gradient and the loss sum (block partials, in block order)
+            ReduceArgs r{e.head_partial, e.head_grid, e.NC + 1, 4, 0, e.NC, 0, 0, 0, 0, nullptr, gb, nullptr};
+            r.dst4 = loss_out;
+            if ((rc = reduce(r))) return rc;
+        }
+        prof_mark(n, "softmax_ce");
+        launch_pdl(head_direct_wgrad_kernel<12>, dim3((e.F / 64) * e.hdw_splits), dim3(256), 0, flat, e.dz,
+                   e.hdw_partial, B, e.F, e.hdw_splits);
+        ZB_LAUNCH_CHECK("head direct weight gradient");
+        {
+            ReduceArgs r{e.hdw_partial, e.hdw_splits, (long long)e.F * e.NC, 3, e.F, e.NC, 0, e.fC, e.fH, e.fW,
+                         gW, nullptr, nullptr};
+            if ((rc = reduce(r))) return rc;
+        }
+        if ((rc = dp_bucket_ready(n, sf.poff))) return rc;
+        prof_mark(n, "linear_bwd");
+    } else if (e.fc_fwd.ksplit > 1) {
         if ((rc = launch_gemm<128, tc::kGemmPartial, 6>(e.fc_fwd))) return rc;
         ReduceArgs r{e.fc_fwd_partial, e.fc_fwd.ksplit, (long long)B * e.HD, 6, B, e.HD, 0, 0, 0, 0,
                      nullptr, nullptr, nullptr, e.fc_fwd.bias, e.a_hid};
@@ -1544,8 +1834,10 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
     } else if ((rc = launch_gemm<128, tc::kGemmBiasRelu, 6>(e.fc_fwd))) {
         return rc;
     }
-    prof_mark(n, "linear_fwd");
-    if (logits_out) {   // evaluation: classifier and loss only
+    if (!e.direct_head) prof_mark(n, "linear_fwd");
+    if (e.direct_head) {
+        // (the classifier, loss and its backward ran above)
+    } else if (logits_out) {   // evaluation: classifier and loss only
         const Stage &sf = st[e.head_si];
         launch_pdl(head_fwd_kernel<256, 10>, dim3(e.head_grid), dim3(256), 0, e.a_hid, n.params + sf.poff,
                    n.params + sf.poff + sf.pn_w, y, logits_out, (y && loss_out) ? e.head_partial : nullptr, B);
@@ -1557,7 +1849,8 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
         prof_mark(n, "softmax_ce");
         return kOk;
     }
-    // ---- head: classifier, loss, start of the backward
+    // ---- head: classifier, loss, start of the backward (hidden Linear + classifier)
+    if (!e.direct_head) {
     const Stage &sh = st[e.head_si];
     float *gW5 = n.grads + sh.poff, *gb5 = gW5 + sh.pn_w;
     const Stage &sd = st[e.hid_si];
@@ -1590,6 +1883,7 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
     // all-reduce (the bulk of the gradient bytes) overlaps the conv backward
     if ((rc = dp_bucket_ready(n, st[e.hid_si].poff))) return rc;
     prof_mark(n, "linear_bwd");
+    }
     // ---- conv stages backward (last to first)
     const bf16 *dpooled = e.dflat;   // gradient w.r.t. the last pooled output
     for (int li = (int)e.convs.size() - 1; li >= 0; --li) {
@@ -1607,6 +1901,9 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
             prof_mark(n, "pool_bwd");
         }
         if (L.fused_bwd) {
+            // data parallel over peer memory: the gradients of every later layer are final, so
+            // their exchange and update run on a side stream beside this kernel
+            if ((rc = peer_step_mid(n, s.poff + s.pn_w + s.pn_b))) return rc;
             if ((rc = run_conv_bwd_fused(L, x, dP))) return rc;
             // the kernel's partials: conv2 dW, conv2 db (UP), conv1 dW + db (C1)
             ReduceArgs jobs[3];
@@ -1671,8 +1968,11 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
         const int padded = (e.H0 + 2 * e.pad1) * (e.W0 + 2 * e.pad1);
         const size_t smem = (size_t)(padded > 8 * 4 * 80 ? padded : 8 * 4 * 80) * sizeof(float);
         if (smem > 48 * 1024) return fail(kBadArg, "tc engine: first-conv image too large for the weight-gradient kernel");
-        if (e.C1 == 32) conv_first_wgrad_kernel<32><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
-        else conv_first_wgrad_kernel<16><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
+        const bool big = padded > kStageRegs * 256;   // past the register stager: a plain copy per image
+        if (e.C1 == 32 && !big) conv_first_wgrad_kernel<32><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
+        else if (e.C1 == 32) conv_first_wgrad_kernel<32, true><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
+        else if (!big) conv_first_wgrad_kernel<16><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
+        else conv_first_wgrad_kernel<16, true><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
     }
     ZB_LAUNCH_CHECK("conv_first_wgrad");
     {

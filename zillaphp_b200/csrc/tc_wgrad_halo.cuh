@@ -20,7 +20,9 @@
 // and a slice of the images; it accumulates over all its tiles in TMEM and
 // writes one fp32 partial [split][COUT][9 * CIN] (its columns), which a
 // second kernel sums in split order (deterministic).  M = COUT: 128 uses all
-// TMEM lanes; 64 uses lanes 32q .. 32q + 15 of each quarter q.
+// TMEM lanes; 64 uses lanes 32q .. 32q + 15 of each quarter q.  COUT = 32 runs
+// as M = 64: the A (dY) part of each stage has 64 channel groups' room, the
+// upper four groups stay zero (never loaded), and their D rows are dropped.
 //
 // Warp roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer and TMEM
 // owner, warps 2-5 write the partial.  Every wait is bounded (tc_common.cuh).
@@ -42,6 +44,7 @@ struct WgradHaloParams {
 
 template <int CIN, int COUT, int NGRP, int NS>
 struct WgradHaloShape {
+    static constexpr int MP = COUT < 64 ? 64 : COUT;   // MMA M (COUT = 32: padded with zero rows)
     static constexpr int NTOT = 9 * CIN;
     static constexpr int NG = NTOT / NGRP;          // D columns per CTA
     static constexpr uint32_t TMEM_COLS = NG <= 32 ? 32 : NG <= 64 ? 64 : NG <= 128 ? 128 : NG <= 256 ? 256 : 512;
@@ -51,11 +54,11 @@ struct WgradHaloShape {
     static __host__ __device__ int dy_region(int R, int Wp) { return ksteps(R, Wp) * 16 * 16; }
     static __host__ __device__ int x_region(int HR) { return (HR * 16 + 127) / 128 * 128; }
     static __host__ __device__ int stage_bytes(int R, int Wp, int HR) {
-        return ((COUT / 8) * dy_region(R, Wp) + (CIN / 8) * x_region(HR) + 1023) / 1024 * 1024;
+        return ((MP / 8) * dy_region(R, Wp) + (CIN / 8) * x_region(HR) + 1023) / 1024 * 1024;
     }
     static __host__ __device__ int smem(int R, int Wp, int HR) { return 1024 + NS * stage_bytes(R, Wp, HR) + SLACK + BAR_BYTES; }
-    static_assert(COUT == 64 || COUT == 128, "MMA M must be 64 or 128");
-    static_assert(CIN % 32 == 0 && NTOT % NGRP == 0 && NG % 32 == 0 && NG <= 512, "column split");
+    static_assert(COUT == 32 || COUT == 64 || COUT == 128, "MMA M must be 64 or 128");
+    static_assert(CIN % 16 == 0 && NTOT % NGRP == 0 && NG % 16 == 0 && NG <= 512, "column split");
 };
 
 template <int CIN, int COUT, int NGRP, int NS>
@@ -80,7 +83,7 @@ __global__ void __launch_bounds__(192, 1) wgrad_halo_kernel(const __grid_constan
     const int ntiles = (k1 - k0) * p.tiles_per_img;
     const int n0 = grp * S::NG;
     const int KST = S::ksteps(p.R, p.Wp);
-    const int DYB = (COUT / 8) * p.dy_region;   // dY part of a stage
+    const int DYB = (S::MP / 8) * p.dy_region;   // dY part of a stage (groups past COUT stay zero)
 
     // rows that TMA never writes (dY rows past R*Wp, X group padding, the
     // slack) are zeroed once
@@ -152,7 +155,7 @@ __global__ void __launch_bounds__(192, 1) wgrad_halo_kernel(const __grid_constan
                         const int dh = tap / 3, dw = tap - 3 * dh;
                         const uint64_t bd = b_st + (uint64_t)(((lo - tap * CIN) / 8) * xr16) +
                                             (uint64_t)(dh * p.Wp + dw + 16 * k);
-                        const uint32_t idesc = idesc_bf16(COUT, hi - lo, true, true);
+                        const uint32_t idesc = idesc_bf16(S::MP, hi - lo, true, true);
                         mma_bf16(tmem_base + (uint32_t)(lo - n0), ad, bd, idesc, (t | k) != 0);
                     }
                 }
@@ -175,8 +178,8 @@ __global__ void __launch_bounds__(192, 1) wgrad_halo_kernel(const __grid_constan
         if (!*abort_flag) {
             tc_fence_after();
             // row of D held by this thread's TMEM lane (M = 64: lanes 32q .. 32q + 15)
-            const int m = COUT == 128 ? q * 32 + lane : q * 16 + lane;
-            const bool row_ok = COUT == 128 || lane < 16;
+            const int m = S::MP == 128 ? q * 32 + lane : q * 16 + lane;
+            const bool row_ok = (S::MP == 128 || lane < 16) && m < COUT;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16);
             float *part = p.partial + ((size_t)split * COUT + (row_ok ? m : 0)) * S::NTOT + n0;
             const bool empty_slice = ntiles == 0;
@@ -190,6 +193,18 @@ __global__ void __launch_bounds__(192, 1) wgrad_halo_kernel(const __grid_constan
                 for (int j = 0; j < 8; ++j)
                     d4[j] = empty_slice ? make_float4(0.0f, 0.0f, 0.0f, 0.0f)
                                         : make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            }
+            if constexpr (S::NG % 32 != 0) {   // the last 16 columns
+                constexpr int c16 = S::NG / 32 * 32;
+                float v[16];
+                tmem_ld16(taddr + c16, v);
+                if (row_ok) {
+                    float4 *d4 = reinterpret_cast<float4 *>(part + c16);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        d4[j] = empty_slice ? make_float4(0.0f, 0.0f, 0.0f, 0.0f)
+                                            : make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                }
             }
         }
     }

@@ -89,6 +89,8 @@ SIGNATURES: dict[str, tuple] = {
     "zilla_net_save": (I, [I, C.c_char_p, I]),
     "zilla_net_load": (I, [I, C.c_char_p]),
     "zilla_net_step_staged": (I, [I, FP, I]),
+    "zilla_net_step_staged_deferred": (I, [I, FP, IP, I]),
+    "zilla_net_loss_flush": (I, [I, FP, IP]),
     "zilla_net_profile": (I, [I, I]),
     "zilla_net_profile_segment": (I, [I, I]),
     "zilla_net_timings": (I, [I, C.c_char_p, I, FP, I]),
@@ -97,6 +99,7 @@ SIGNATURES: dict[str, tuple] = {
     "zilla_lm_create": (I, [I] * 8),
     "zilla_lm_forward_cached": (I, [I, FP, I, FP]),
     "zilla_lm_cache_reset": (I, [I]),
+    "zilla_lm_set_precision": (I, [I, I]),
     "zilla_lm_cache_length": (I, [I]),
     "zilla_dp_unique_id": (I, [C.c_char_p]),
     "zilla_dp_attach": (I, [I, I, I, C.c_char_p]),

@@ -84,6 +84,23 @@ class Net:
             staged.pop(0)
         return float(loss.value)
 
+    def step_staged_deferred(self, update: bool = True) -> float | None:
+        """Step on the oldest staged batch without waiting for its loss
+        (zilla_net_step_staged_deferred); returns the PREVIOUS deferred step's
+        loss sum, or None on the first call."""
+        loss, has = C.c_float(0.0), C.c_int(0)
+        self._check(self.lib.zilla_net_step_staged_deferred(self.id, C.byref(loss), C.byref(has), int(update)))
+        staged = getattr(self, "_staged", [])
+        if staged:
+            staged.pop(0)
+        return float(loss.value) if has.value else None
+
+    def loss_flush(self) -> float | None:
+        """The last deferred step's loss sum (zilla_net_loss_flush), or None."""
+        loss, has = C.c_float(0.0), C.c_int(0)
+        self._check(self.lib.zilla_net_loss_flush(self.id, C.byref(loss), C.byref(has)))
+        return float(loss.value) if has.value else None
+
     def forward(self, x: np.ndarray, y: np.ndarray | None = None) -> tuple[np.ndarray, float | None]:
         """Evaluation through zilla_net_forward: (logits [batch, classes], loss sum or None)."""
         lib, ids = self.lib, []
@@ -178,12 +195,12 @@ class LM(Net):
     (zilla_lm_create + zilla_net_step): x and y are the batch*seq token ids
     and next-token ids, as floats."""
 
-    def __init__(self, workload: LmWorkload, batch: int | None = None, seq: int | None = None):
+    def __init__(self, workload: LmWorkload, batch: int | None = None, seq: int | None = None, precision: int = 0):
         self.w = workload
         self.lib = native.load()
         self.batch = batch if batch is not None else workload.batch
         self.seq = seq if seq is not None else workload.seq
-        self.precision = 0
+        self.precision = precision
         w = workload
         self.id = self.lib.zilla_lm_create(w.vocab, w.dim, w.heads, w.layers, w.max_seq, w.ffn, self.batch,
                                            self.seq)
@@ -194,6 +211,8 @@ class LM(Net):
         self._check(self.lib.zilla_net_set_optimizer(self.id, w.optimizer, w.lr, b1, b2, eps))
         self.params_id = self.lib.zilla_net_params_id(self.id)
         self.grads_id = self.lib.zilla_net_grads_id(self.id)
+        if precision:   # TF32 tensor-core GEMMs for the blocks' Linear layers
+            self._check(self.lib.zilla_lm_set_precision(self.id, precision))
 
     def forward_cached(self, tokens) -> np.ndarray:
         """TransformerLM::forwardWithCache: logits [len(tokens), vocab] for the

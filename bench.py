@@ -185,7 +185,10 @@ def tc_work(w: configs.Workload, b: int) -> list[dict]:
         f = 2 * b * oh * ow * o * a * 9
         inb = b * ih * iw * a * (4 if k == 0 else 2)
         outb = b * (oh // 2) * (ow // 2) * o * 3 if pool else b * oh * ow * o * 2
-        out.append({"label": "conv_fwd", "flops": f, "bytes": inb + outb, "name": f"conv{k + 1} fwd"})
+        item = {"label": "conv_fwd", "flops": f, "bytes": inb + outb, "name": f"conv{k + 1} fwd"}
+        if k == 0:
+            item["bound"] = "hbm"   # one input channel: the output write bounds it
+        out.append(item)
     a0, o0, ih0, iw0, oh0, ow0, pool0 = convs[0]
     if len(lin) == 2:   # hidden Linear + ReLU, then the classifier
         (F, HD), (_, NC) = lin[0], lin[-1]
@@ -206,9 +209,10 @@ def tc_work(w: configs.Workload, b: int) -> list[dict]:
                 and convs[1][3] + 2 <= 32 and (4 * convs[1][3]) % 16 == 0)
     for k in range(len(convs) - 1, -1, -1):
         a, o, ih, iw, oh, ow, pool = convs[k]
-        if k == 0:
-            out.append({"label": "conv_wgrad", "flops": 2 * b * oh * ow * o * a * 9,
-                        "bytes": b * ((oh // 2) * (ow // 2) * o * 3 + ih * iw * 4 if pool0 else oh * ow * o * 2 + ih * iw * 4),
+        if k == 0:   # CUDA cores (one input channel): bound by the dC1 round trip, so HBM
+            dc1 = b * oh * ow * o * 2
+            out.append({"label": "conv_wgrad", "flops": 2 * b * oh * ow * o * a * 9, "bound": "hbm",
+                        "bytes": (b * (oh // 2) * (ow // 2) * o * 3 + 2 * dc1 if pool0 else dc1) + b * ih * iw * 4,
                         "name": "unpool1+conv1 dW" if pool0 else "conv1 dW"})
             break
         f = 2 * b * oh * ow * o * a * 9
@@ -288,7 +292,7 @@ def roofline(w, batch, seg_times: list[tuple[str, float]], steps: int, pk: dict,
         k_dom, ms = focus[0], sum(focus[1]) / len(focus[1])
     item = order[k_dom]
     breakdown = {f"{order[k].get('name', order[k]['label'])}#{k}": round(sum(v) / len(v), 4) for k, v in sorted(agg.items())}
-    if item["flops"] > 0:
+    if item["flops"] > 0 and item.get("bound") != "hbm":
         achieved = item["flops"] / (ms * 1e-3) / 1e12
         peak = pk.get("bf16_tflops_sustained" if ms > 50 else "bf16_tflops", 1590.0)
         r = {"bound": "tensor", "unit": "TFLOP/s", "achieved": round(achieved, 3), "peak": peak}

@@ -6,13 +6,12 @@ The Q/K/V, output and FFN projections and their input and weight gradients
 run as tcgen05 kind::tf32 GEMMs: the fp32 operands are read with a 10-bit
 mantissa (relative rounding 2^-11) and accumulated in fp32.  LayerNorm,
 attention, the head, the loss and Adam are the fp32 engine's.  Tolerances
-against the float64 oracle restatement (oracle/lm_oracle.py), stated for TF32:
-  loss sum            relative 2e-3
-  gradients           normwise 2e-2 over the whole flat buffer
-  three-step losses   relative 5e-3 against the oracle's own trajectory
-The same GEMMs are also checked one by one against float64 products of the
-step's own inputs through the fp32 engine: both precisions must agree on the
-loss within 2e-3 on the same batch.
+against the float64 oracle restatement (oracle/lm_oracle.py), stated for TF32,
+with the values measured on a B200 in brackets:
+  loss sum            relative 2e-4   [6.7e-6, 1.4e-5]
+  gradients           normwise 2e-2 over the whole flat buffer [5.7e-3, 9.6e-3]
+  three-step losses   relative 2e-4 against the oracle's own trajectory and
+                      against the fp32 engine's [2.0e-5]
 """
 import numpy as np
 import pytest
@@ -47,7 +46,7 @@ def test_tf32_step_against_oracle(batch, seq):
     lerr = abs(loss - rl) / abs(rl)
     gerr = npref.normwise(g, rg)
     print(f"tf32 LM {batch}x{seq}: loss rel {lerr:.2e}, gradients normwise {gerr:.2e}")
-    assert lerr < 2e-3, (loss, rl)
+    assert lerr < 2e-4, (loss, rl)
     assert gerr < 2e-2
 
 
@@ -74,5 +73,5 @@ def test_tf32_trajectory_and_fp32_agreement():
         for n in nets:
             n.close()
     print(f"tf32 trajectory: worst loss gap to the oracle {worst:.2e}, to the fp32 engine {worst32:.2e}")
-    assert worst < 5e-3
-    assert worst32 < 5e-3
+    assert worst < 2e-4
+    assert worst32 < 2e-4

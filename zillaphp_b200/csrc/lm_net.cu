@@ -68,6 +68,11 @@ struct LmEngine {
     std::vector<LmTcGemm> tcg;
     float *tc_partial = nullptr;   // weight-gradient split partials
     const float *tc_params = nullptr, *tc_grads = nullptr;   // the buffers the plan was built over
+    // The flat parameter layout (TransformerLM::parameters() order) puts the blocks' tensors at
+    // arbitrary float offsets; TMA and the 16-byte bias loads need 16-byte-aligned bases, so each
+    // step first copies the blocks' weights and biases into a shadow with every tensor aligned.
+    float *tc_shadow = nullptr;
+    std::vector<long long> shadow_src, shadow_dst, shadow_len;
     std::vector<void *> allocs;
 };
 constexpr int kLmTcPerBlock = 12;
@@ -637,12 +642,12 @@ int lm_tc_run(const LmEngine &e, const LmTcGemm &g) {
     }
 }
 
-// 2D fp32 tensor maps, 128-byte swizzle: K-major {K (contiguous), rows}, box {32, box_rows};
-// MN-major {MN (contiguous), K rows}, box {32, 32}
-int fmap(CUtensorMap *m, const float *base, int inner, int outer, int box_outer) {
+// 2D fp32 tensor maps: K-major {K (contiguous), rows}, box {32, box_rows}, 128-byte swizzle;
+// MN-major {MN (contiguous), K rows}, box {32, 32}, 128-byte swizzle over 32-byte atoms
+int fmap(CUtensorMap *m, const float *base, int inner, int outer, int box_outer, bool mn_major = false) {
     const uint64_t dims[2] = {(uint64_t)inner, (uint64_t)outer}, strides[1] = {(uint64_t)inner * 4};
     const uint32_t box[2] = {32, (uint32_t)box_outer};
-    return tc::make_tmap_f32(m, base, 2, dims, strides, box, tc::kSw128);
+    return tc::make_tmap_f32(m, base, 2, dims, strides, box, mn_major ? tc::kSw128B32 : tc::kSw128);
 }
 
 // Forward: Y [M][ldo] = X [M][K] W_s [K][N_s] over nseg segments (n tile s = segment s when nseg > 1).
@@ -652,7 +657,7 @@ int tc_fwd(LmTcGemm &g, const float *X, int M, int K, const float *const *W, int
     int rc;
     if ((rc = fmap(&p.a_map, X, K, M, 128))) return rc;
     for (int s = 0; s < nseg; ++s)
-        if ((rc = fmap(&p.b_map[s], W[s], Nseg, K, 32))) return rc;
+        if ((rc = fmap(&p.b_map[s], W[s], Nseg, K, 32, true))) return rc;
     p.M = M; p.N = nseg * Nseg; p.K = K;
     p.m_tiles = M / 128; p.n_tiles = p.N / 128; p.ksplit = 1; p.kper = K / 32;
     p.nseg = nseg; p.b_seg_by_n = nseg > 1; p.seg_k = 0;
@@ -685,8 +690,8 @@ int tc_dgrad(LmTcGemm &g, const float *dY, int M, int Kseg, int nseg, const floa
 int tc_wgrad(LmTcGemm &g, const float *X, int M, const float *dY, int N, int rows, float *const *dst, int seg_w) {
     tc::GemmTf32Params &p = g.p;
     int rc;
-    if ((rc = fmap(&p.a_map, X, M, rows, 32))) return rc;
-    if ((rc = fmap(&p.b_map[0], dY, N, rows, 32))) return rc;
+    if ((rc = fmap(&p.a_map, X, M, rows, 32, true))) return rc;
+    if ((rc = fmap(&p.b_map[0], dY, N, rows, 32, true))) return rc;
     p.M = M; p.N = N; p.K = rows;
     p.m_tiles = M / 128; p.n_tiles = N / 128;
     const int stages = rows / 32;
@@ -703,21 +708,70 @@ int tc_wgrad(LmTcGemm &g, const float *X, int M, const float *dY, int N, int row
     return kOk;
 }
 
+// Copies of the blocks' weights and biases into the aligned shadow: job j copies
+// len[j] floats from params + src[j] to shadow + dst[j] (blockIdx.y = job).
+struct ShadowJobs {
+    long long src[64], dst[64], len[64];
+};
+
+__global__ void __launch_bounds__(256) lm_shadow_kernel(const float *__restrict__ params, float *__restrict__ shadow,
+                                                        const __grid_constant__ ShadowJobs J) {
+    griddep_launch();
+    griddep_wait();
+    const int j = blockIdx.y;
+    const float *s = params + J.src[j];
+    float *d = shadow + J.dst[j];
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < J.len[j]; i += (long long)gridDim.x * blockDim.x)
+        d[i] = __ldg(s + i);
+}
+
+int lm_tc_shadow(const Net &n, const LmEngine &e) {
+    ShadowJobs J{};
+    const int nj = (int)e.shadow_src.size();
+    for (int j = 0; j < nj; ++j) { J.src[j] = e.shadow_src[j]; J.dst[j] = e.shadow_dst[j]; J.len[j] = e.shadow_len[j]; }
+    launch_pdl(lm_shadow_kernel, dim3(16, nj), dim3(256), 0, (const float *)n.params, e.tc_shadow, J);
+    ZB_LAUNCH_CHECK("lm weight shadow");
+    return kOk;
+}
+
 // The plan over the net's buffers (after net_alloc_common: parameters and gradients exist).
 int lm_tc_build(Net &n, LmEngine &e) {
     const int D = e.D, N = e.N, F = e.F, L = e.L;
     if (N % 128 || D % 128 || F % 128 || N % 256)
         return fail(kBadArg, "lm: tensor-core GEMMs need batch*seq %% 256 == 0 and dim, ffn %% 128 == 0 (%d, %d, %d)",
                     N, D, F);
-    const float *Pm = n.params;
+    if (L * 12 > 64) return fail(kBadArg, "lm: tensor-core GEMMs support up to 5 blocks");
+    e.tc_params = n.params;
+    e.tc_grads = n.grads;
     float *G = n.grads;
-    e.tc_params = Pm;
-    e.tc_grads = G;
-    size_t part = 0;
-    e.tcg.assign((size_t)L * kLmTcPerBlock, LmTcGemm());
-    int rc;
+    // the aligned shadow of every block weight and bias (each tensor at a multiple of 4 floats)
+    e.shadow_src.clear(); e.shadow_dst.clear(); e.shadow_len.clear();
+    long long sh = 0;
+    auto place = [&](long long src, long long len) {
+        e.shadow_src.push_back(src); e.shadow_dst.push_back(sh); e.shadow_len.push_back(len);
+        const long long at = sh;
+        sh += (len + 3) / 4 * 4;
+        return at;
+    };
+    std::vector<LmEngine::Blk> sb(L);   // shadow offsets of each block's tensors
     for (int l = 0; l < L; ++l) {
         const auto &b = e.blk[l];
+        LmEngine::Blk &o = sb[l];
+        o.qW = place(b.qW, (long long)D * D); o.qb = place(b.qb, D);
+        o.kW = place(b.kW, (long long)D * D); o.kb = place(b.kb, D);
+        o.vW = place(b.vW, (long long)D * D); o.vb = place(b.vb, D);
+        o.oW = place(b.oW, (long long)D * D); o.ob = place(b.ob, D);
+        o.f1W = place(b.f1W, (long long)D * F); o.f1b = place(b.f1b, F);
+        o.f2W = place(b.f2W, (long long)F * D); o.f2b = place(b.f2b, D);
+    }
+    int rc;
+    if ((rc = lalloc(e, &e.tc_shadow, (size_t)sh))) return rc;
+    const float *Pm = e.tc_shadow;
+    size_t part = 0;
+    e.tcg.assign((size_t)L * kLmTcPerBlock, LmTcGemm());
+    for (int l = 0; l < L; ++l) {
+        const auto &b = sb[l];        // operands: the shadow copies
+        const auto &bg = e.blk[l];    // gradient destinations: the flat layout
         LmTcGemm *g = &e.tcg[(size_t)l * kLmTcPerBlock];
         for (int j = 0; j < kLmTcPerBlock; ++j) g[j].p.err = device_error_word();
         const float *Wqkv[3] = {Pm + b.qW, Pm + b.kW, Pm + b.vW}, *bqkv[3] = {Pm + b.qb, Pm + b.kb, Pm + b.vb};
@@ -735,8 +789,8 @@ int lm_tc_build(Net &n, LmEngine &e) {
             (rc = tc_dgrad(g[6], e.gm, N, D, 1, Wo, D, nullptr, e.datt)) ||
             (rc = tc_dgrad(g[7], e.dqkv, N, D, 3, Wqkv, D, nullptr, e.dh)))
             return rc;
-        float *dW2[3] = {G + b.f2W, nullptr, nullptr}, *dW1[3] = {G + b.f1W, nullptr, nullptr};
-        float *dWo[3] = {G + b.oW, nullptr, nullptr}, *dWqkv[3] = {G + b.qW, G + b.kW, G + b.vW};
+        float *dW2[3] = {G + bg.f2W, nullptr, nullptr}, *dW1[3] = {G + bg.f1W, nullptr, nullptr};
+        float *dWo[3] = {G + bg.oW, nullptr, nullptr}, *dWqkv[3] = {G + bg.qW, G + bg.kW, G + bg.vW};
         if ((rc = tc_wgrad(g[8], e.f1[l], F, e.g, D, N, dW2, D)) ||
             (rc = tc_wgrad(g[9], e.h2[l], D, e.df1, F, N, dW1, F)) ||
             (rc = tc_wgrad(g[10], e.att[l], D, e.gm, D, N, dWo, D)) ||
@@ -804,6 +858,7 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
     const bool tcp = n.precision == 1 && !e.tcg.empty();
     if (tcp && (G != e.tc_grads || Pm != e.tc_params))
         return fail(kBadArg, "lm: tensor-core plan built over other parameter / gradient buffers");
+    if (tcp && (rc = lm_tc_shadow(n, e))) return rc;   // this step's weights, aligned for TMA
     // ---- forward
     embed_fwd_kernel<<<grid_for((long long)N * D, 256, 8), 256, 0, stream()>>>(
         tokens, Pm + e.o_tok, Pm + e.o_pos, e.x[0], N, e.Ts, D, V, device_error_word());

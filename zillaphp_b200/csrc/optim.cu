@@ -13,8 +13,15 @@
 
 namespace zb {
 
-__global__ void adam_kernel(float *__restrict__ w, const float *__restrict__ g,
-                            float *__restrict__ m, float *__restrict__ v, long long n, AdamArgs a) {
+// Each thread takes kAdamU float4 groups (i, i + stride, ...) per pass and
+// issues all their loads before any arithmetic, so 4 * kAdamU 16-byte loads
+// per thread are in flight; the launcher sizes the grid so that one pass
+// covers the buffer.
+constexpr int kAdamU = 2;
+
+__global__ void __launch_bounds__(256) adam_kernel(float *__restrict__ w, const float *__restrict__ g,
+                                                   float *__restrict__ m, float *__restrict__ v, long long n,
+                                                   AdamArgs a) {
     griddep_launch();
     griddep_wait();
     const long long stride = (long long)gridDim.x * blockDim.x;
@@ -23,18 +30,27 @@ __global__ void adam_kernel(float *__restrict__ w, const float *__restrict__ g,
     long long tail = 0;
     if (vec) {
         const long long n4 = n >> 2;
-        for (long long i = i0; i < n4; i += stride) {
-            float4 W = reinterpret_cast<float4 *>(w)[i];
-            const float4 G = reinterpret_cast<const float4 *>(g)[i];
-            float4 M = reinterpret_cast<float4 *>(m)[i];
-            float4 V = reinterpret_cast<float4 *>(v)[i];
-            adam_one(W.x, G.x, M.x, V.x, a);
-            adam_one(W.y, G.y, M.y, V.y, a);
-            adam_one(W.z, G.z, M.z, V.z, a);
-            adam_one(W.w, G.w, M.w, V.w, a);
-            reinterpret_cast<float4 *>(w)[i] = W;
-            reinterpret_cast<float4 *>(m)[i] = M;
-            reinterpret_cast<float4 *>(v)[i] = V;
+        float4 *w4 = reinterpret_cast<float4 *>(w), *m4 = reinterpret_cast<float4 *>(m), *v4 = reinterpret_cast<float4 *>(v);
+        const float4 *g4 = reinterpret_cast<const float4 *>(g);
+        for (long long base = i0; base < n4; base += stride * kAdamU) {
+            float4 W[kAdamU], G[kAdamU], M[kAdamU], V[kAdamU];
+#pragma unroll
+            for (int u = 0; u < kAdamU; ++u) {
+                const long long i = base + u * stride;
+                if (i < n4) { W[u] = w4[i]; G[u] = __ldcs(g4 + i); M[u] = m4[i]; V[u] = v4[i]; }
+            }
+#pragma unroll
+            for (int u = 0; u < kAdamU; ++u) {
+                const long long i = base + u * stride;
+                if (i >= n4) break;
+                adam_one(W[u].x, G[u].x, M[u].x, V[u].x, a);
+                adam_one(W[u].y, G[u].y, M[u].y, V[u].y, a);
+                adam_one(W[u].z, G[u].z, M[u].z, V[u].z, a);
+                adam_one(W[u].w, G[u].w, M[u].w, V[u].w, a);
+                w4[i] = W[u];
+                m4[i] = M[u];
+                v4[i] = V[u];
+            }
         }
         tail = n4 << 2;
     }
@@ -73,7 +89,8 @@ AdamArgs make_adam_args(float lr, float b1, float b2, float eps, int t, float gr
 
 int launch_adam(float *w, const float *g, float *m, float *v, long long n, const AdamArgs &a) {
     if (n <= 0) return kOk;
-    launch_pdl(adam_kernel, dim3(grid_for(n / 4 + 1, 256, 4)), dim3(256), 0, w, g, m, v, n, a);
+    // one pass: kAdamU float4 groups per thread (capped at 16 blocks per SM)
+    launch_pdl(adam_kernel, dim3(grid_for((n / 4 + kAdamU) / kAdamU, 256, 16)), dim3(256), 0, w, g, m, v, n, a);
     ZB_LAUNCH_CHECK("adam_update");
     return kOk;
 }

@@ -175,7 +175,9 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
 // ---------------------------------------------------------------- descriptors
 // Shared-memory matrix descriptor (tcgen05 format): start address, leading
 // and stride byte offsets (all >> 4), version 1, swizzle mode in bits 61-63.
-enum Swizzle : uint32_t { kSwNone = 0, kSw128 = 2, kSw64 = 4, kSw32 = 6 };
+// kSw128B32: the 128-byte swizzle over 32-byte atoms (4 rows of 128 B per atom), the
+// only shared-memory layout of an MN-major operand of 32-bit elements (tf32).
+enum Swizzle : uint32_t { kSwNone = 0, kSw128B32 = 1, kSw128 = 2, kSw64 = 4, kSw32 = 6 };
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes, Swizzle sw) {
     uint64_t d = 0;

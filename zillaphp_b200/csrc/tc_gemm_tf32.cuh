@@ -13,10 +13,13 @@
 //   B K-major  : B(k, n) = W[n][k]   input gradient (W^T)      box {32 k, BN n}
 //   B MN-major : B(k, n) = dY[k][n]  weight gradient
 // A K stage is 32 fp32 (one 128-byte swizzle row for K-major, 32 rows for
-// MN-major): four K8 MMAs of M = 128, N = BN.  The descriptors follow the
-// bf16 kernels (tc_gemm.cuh K-major, tc_wgrad.cuh MN-major) with the element
-// size doubled: a K8 step is 32 bytes along a K-major row, or 8 rows (1024
-// bytes) of an MN-major box; MN-major atoms of 32 elements sit 4 KB apart.
+// MN-major): four K8 MMAs of M = 128, N = BN.  K-major operands use the
+// 128-byte swizzle like the bf16 kernels (tc_gemm.cuh): a K8 step is 32 bytes
+// along a row.  MN-major operands of 32-bit elements have one valid layout,
+// the 128-byte swizzle over 32-byte atoms (TMA's 128B_ATOM_32B, descriptor
+// layout type 1): 128-byte rows of 32 MN elements, swizzled in groups of 4 K
+// rows (512 bytes, the SBO); a K8 step is 8 rows (1024 bytes), and the
+// 32-element MN atoms (one TMA box each) sit 4 KB apart (the LBO).
 //
 // Up to three B segments (the Q/K/V weights of one attention layer): with
 // b_seg_by_n the n tile t reads segment t (its N coordinates restart at 0);
@@ -182,9 +185,9 @@ __global__ void __launch_bounds__(192, 1) gemm_tf32_kernel(const __grid_constant
                     const uint32_t a0 = s0 + s * S::STAGE, b0 = a0 + S::ABYTES;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t ad = AMN ? smem_desc(a0 + kk * 1024, 4096, 1024, kSw128)
+                        const uint64_t ad = AMN ? smem_desc(a0 + kk * 1024, 4096, 512, kSw128B32)
                                                 : smem_desc(a0 + kk * 32, 16, 1024, kSw128);
-                        const uint64_t bd = BMN ? smem_desc(b0 + kk * 1024, 4096, 1024, kSw128)
+                        const uint64_t bd = BMN ? smem_desc(b0 + kk * 1024, 4096, 512, kSw128B32)
                                                 : smem_desc(b0 + kk * 32, 16, 1024, kSw128);
                         mma_tf32(d, ad, bd, IDESC, (k > kb) || kk != 0);
                     }

@@ -71,6 +71,7 @@ int make_tmap_typed(CUtensorMap *map, CUtensorMapDataType dtype, const void *bas
     for (int i = 0; i < rank; ++i) { gd[i] = dims[i]; bx[i] = box[i]; es[i] = 1; }
     for (int i = 0; i < rank - 1; ++i) gs[i] = strides[i];
     CUtensorMapSwizzle s = sw == kSw128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                           : sw == kSw128B32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
                            : sw == kSw64 ? CU_TENSOR_MAP_SWIZZLE_64B
                            : sw == kSw32 ? CU_TENSOR_MAP_SWIZZLE_32B
                                          : CU_TENSOR_MAP_SWIZZLE_NONE;
@@ -1958,17 +1959,17 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
     }
     // ---- first conv backward (dC1 written by the next conv's dgrad, masked)
     if (e.c1_fused) return kOk;   // taken by the next conv's fused backward kernel
-    if (e.c1_pool) {
-        const int G = e.C1 / 8, slots = 256 / G;
-        unpool_kernel<<<sm_count() * 4, slots * G, slots * G * 8 * sizeof(float), stream()>>>(
-            e.dP1, e.code1, e.dC1, e.c1_partial /*scratch*/, B, e.H1, e.W1, e.C1);
-        ZB_LAUNCH_CHECK("unpool first");
-    }
     {
         const int padded = (e.H0 + 2 * e.pad1) * (e.W0 + 2 * e.pad1);
         const size_t smem = (size_t)(padded > 8 * 4 * 80 ? padded : 8 * 4 * 80) * sizeof(float);
         if (smem > 48 * 1024) return fail(kBadArg, "tc engine: first-conv image too large for the weight-gradient kernel");
         const bool big = padded > kStageRegs * 256;   // past the register stager: a plain copy per image
+        if (e.c1_pool) {   // dC1 = unpool(dP1, codes): a separate pass (the kernel below is issue-bound)
+            const int G = e.C1 / 8, slots = 256 / G;
+            unpool_kernel<<<sm_count() * 4, slots * G, slots * G * 8 * sizeof(float), stream()>>>(
+                e.dP1, e.code1, e.dC1, e.c1_partial /*scratch*/, B, e.H1, e.W1, e.C1);
+            ZB_LAUNCH_CHECK("unpool first");
+        }
         if (e.C1 == 32 && !big) conv_first_wgrad_kernel<32><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
         else if (e.C1 == 32) conv_first_wgrad_kernel<32, true><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
         else if (!big) conv_first_wgrad_kernel<16><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);

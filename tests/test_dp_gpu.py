@@ -114,3 +114,21 @@ def test_two_gpu_bf16_step_matches_one_gpu():
     assert npref.normwise(two[0][0], one[0][0]) < 2e-2
     for got, want in zip(two[0][1], one[0][1]):
         assert abs(got - want) / abs(want) < 2e-2, (got, want)
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+@pytest.mark.timeout(600)
+def test_two_phase_exchange_equals_one_phase():
+    """ZB_PEER_TWO_PHASE=1 (the late layers' exchange and update on a side stream beside the
+    fused conv backward) does the same per-element arithmetic as the one-phase update: the
+    ranks' parameters and losses are bit-identical to the default step's."""
+    name, batch, steps = "large_cnn", 256, 3
+    one = _run(2, name, batch, 1, steps)
+    os.environ["ZB_PEER_TWO_PHASE"] = "1"
+    try:
+        two = _run(2, name, batch, 1, steps)
+    finally:
+        del os.environ["ZB_PEER_TWO_PHASE"]
+    assert np.array_equal(two[0][0], two[1][0]), "ranks diverged"
+    assert np.array_equal(two[0][0], one[0][0]), "two-phase update differs from one-phase"
+    assert two[0][1] == one[0][1], (two[0][1], one[0][1])

@@ -55,6 +55,7 @@ struct LmEngine {
     // gradients
     float *g = nullptr, *gm = nullptr, *dh = nullptr, *df1 = nullptr, *datt = nullptr, *dqkv = nullptr;
     float *ln_partial = nullptr;   // [ln_blocks][2D]
+    float *colsum_partial = nullptr;   // [kColsumChunks][widest gradient row]
     float *emb_partial = nullptr;  // [row chunks][V][D]
     int ln_blocks = 0;
     // generation (TransformerLM::forwardWithCache): per-layer K/V caches
@@ -76,6 +77,7 @@ struct LmEngine {
     std::vector<void *> allocs;
 };
 constexpr int kLmTcPerBlock = 12;
+constexpr int kColsumChunks = 296;   // row chunks of the two-stage column sums
 
 namespace {
 
@@ -228,101 +230,174 @@ __global__ void ln_bwd_kernel(const float *__restrict__ gout, const float *__res
 }
 
 // Sum of per-block partials [blocks][2D] into gamma / beta gradients.
-__global__ void sum_ln_partials_kernel(const float *__restrict__ partial, int blocks, int D,
-                                       float *__restrict__ dg, float *__restrict__ db) {
-    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < 2 * D; j += gridDim.x * blockDim.x) {
-        float s = 0.0f;
-        for (int b = 0; b < blocks; ++b) s += partial[(size_t)b * 2 * D + j];
-        if (j < D) dg[j] = s;
-        else db[j - D] = s;
+// out[j] = sum_b partial[b * n + j] for j < n, b < blocks, in a fixed order: a block takes 8
+// columns x 32 split lanes (lane l adds b = l, l + 32, ...), then the 32 lane sums of each
+// column are added in lane order.  Columns j < n0 go to o0[j], the rest to o1[j - n0]
+// (LayerNorm: dgamma | dbeta).
+__global__ void __launch_bounds__(256) sum_partials_kernel(const float *__restrict__ partial, int blocks, int n,
+                                                           int n0, float *__restrict__ o0, float *__restrict__ o1) {
+    __shared__ float red[32][9];
+    const int el = threadIdx.x & 7, sl = threadIdx.x >> 3;
+    const int j = blockIdx.x * 8 + el;
+    float s = 0.0f;
+    if (j < n)
+        for (int b = sl; b < blocks; b += 32) s += partial[(size_t)b * n + j];
+    red[sl][el] = s;
+    __syncthreads();
+    if (sl == 0 && j < n) {
+        float t = red[0][el];
+#pragma unroll
+        for (int l = 1; l < 32; ++l) t += red[l][el];
+        if (j < n0) o0[j] = t;
+        else o1[j - n0] = t;
     }
 }
 
-// Column sums over rows with a row stride: out_s[c] = sum_r dY[r*ld + s*sw + c].
-__global__ void colsum_kernel(const float *__restrict__ dY, int rows, int ld, int sw, float *o0, float *o1,
-                              float *o2) {
-    __shared__ float part[8][33];
+// Column sums over rows with a row stride, first stage: block (column tile, row chunk)
+// sums rows [r0, r1) of 32 columns (8 row lanes, combined in order) into
+// part[chunk][col]; sum_cols_kernel adds the chunks in order.
+__global__ void colsum_part_kernel(const float *__restrict__ dY, int rows, int ld, int chunks,
+                                   float *__restrict__ part) {
+    __shared__ float red[8][33];
     const int col = blockIdx.x * 32 + threadIdx.x;
+    const int r0 = (int)((long long)rows * blockIdx.y / chunks), r1 = (int)((long long)rows * (blockIdx.y + 1) / chunks);
     float acc = 0.0f;
     if (col < ld)
-        for (int r = threadIdx.y; r < rows; r += 8) acc += dY[(size_t)r * ld + col];
-    part[threadIdx.y][threadIdx.x] = acc;
+        for (int r = r0 + threadIdx.y; r < r1; r += 8) acc += dY[(size_t)r * ld + col];
+    red[threadIdx.y][threadIdx.x] = acc;
     __syncthreads();
     if (threadIdx.y == 0 && col < ld) {
-        float s = 0.0f;
+        float t = 0.0f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) s += part[k][threadIdx.x];
+        for (int k = 0; k < 8; ++k) t += red[k][threadIdx.x];
+        part[(size_t)blockIdx.y * ld + col] = t;
+    }
+}
+
+// Second stage: out_s[c] = sum over chunks of part[chunk][s * sw + c], chunks in order.
+__global__ void sum_cols_kernel(const float *__restrict__ part, int chunks, int ld, int sw, float *o0, float *o1,
+                                float *o2) {
+    __shared__ float red[32][9];
+    const int el = threadIdx.x & 7, sl = threadIdx.x >> 3;
+    const int col = blockIdx.x * 8 + el;
+    float s = 0.0f;
+    if (col < ld)
+        for (int b = sl; b < chunks; b += 32) s += part[(size_t)b * ld + col];
+    red[sl][el] = s;
+    __syncthreads();
+    if (sl == 0 && col < ld) {
+        float t = red[0][el];
+#pragma unroll
+        for (int l = 1; l < 32; ++l) t += red[l][el];
         const int seg = col / sw, c = col - seg * sw;
         float *o = seg == 0 ? o0 : seg == 1 ? o1 : o2;
-        o[c] = s;
+        o[c] = t;
     }
 }
 
 // Causal attention forward for one (sequence, head, block of 32 query rows),
 // head dim DH: S = q k^T * scale with -1e9 on future keys, P = row softmax
-// (written out for the backward), o = P v into the head's columns.
+// (written out for the backward), o = P v into the head's columns.  Scores and
+// o are 4 x 4 register tiles of one thread (float4 shared-memory rows: 8 loads
+// per 64 FMAs for the scores); keys after the block's last query row are never
+// used.  Shared memory: K, V [Tp][DH + 4], Q [32][DH + 4], S [32][Tp + 4].
 template <int DH>
 __global__ void __launch_bounds__(128) attn_fwd_kernel(const float *__restrict__ qkv, float *__restrict__ P,
                                                        float *__restrict__ out, int Ts, int H, int D, float scale) {
-    extern __shared__ float sm[];
+    static_assert(DH == 32, "head dimension 32: 8 column tiles of 4");
+    extern __shared__ __align__(16) float sm[];
     const int bh = blockIdx.x, b = bh / H, h = bh % H;
     const int i0 = blockIdx.y * 32;
     const int rows = min(32, Ts - i0);
     const int keys = min(Ts, i0 + 32);   // causal: keys after the last query row are never used
-    float *Ks = sm, *Vs = Ks + (size_t)Ts * (DH + 1), *Qs = Vs + (size_t)Ts * (DH + 1), *S = Qs + 32 * (DH + 1);
+    const int kp = (keys + 3) & ~3;      // keys rounded up to a tile of 4 (zero rows past `keys`)
+    const int Tp = (Ts + 3) & ~3, LD = DH + 4, SP = Tp + 4;
+    float *Ks = sm, *Vs = Ks + (size_t)Tp * LD, *Qs = Vs + (size_t)Tp * LD, *S = Qs + 32 * LD;
     const size_t ld = 3 * (size_t)D;
     const float *base = qkv + (size_t)b * Ts * ld + h * DH;
-    for (int i = threadIdx.x; i < keys * DH; i += blockDim.x) {
+    for (int i = threadIdx.x; i < kp * DH; i += blockDim.x) {
         const int j = i / DH, d = i % DH;
-        Ks[j * (DH + 1) + d] = base[(size_t)j * ld + D + d];
-        Vs[j * (DH + 1) + d] = base[(size_t)j * ld + 2 * D + d];
+        const bool in = j < keys;
+        Ks[j * LD + d] = in ? base[(size_t)j * ld + D + d] : 0.0f;
+        Vs[j * LD + d] = in ? base[(size_t)j * ld + 2 * D + d] : 0.0f;
     }
-    for (int i = threadIdx.x; i < rows * DH; i += blockDim.x) {
+    for (int i = threadIdx.x; i < 32 * DH; i += blockDim.x) {
         const int r = i / DH, d = i % DH;
-        Qs[r * (DH + 1) + d] = base[(size_t)(i0 + r) * ld + d];
+        Qs[r * LD + d] = r < rows ? base[(size_t)(i0 + r) * ld + d] : 0.0f;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < rows * keys; i += blockDim.x) {
-        const int r = i / keys, j = i % keys;
-        float s;
-        if (j > i0 + r) {
-            s = -1e9f;                      // maskedFill(-1e9)
-        } else {
-            s = 0.0f;
+    // scores: tile (4 rows, 4 keys), 8 row tiles x kp / 4 key tiles
+    const int kt = kp / 4;
+    for (int t = threadIdx.x; t < 8 * kt; t += blockDim.x) {
+        const int r0 = 4 * (t % 8), j0 = 4 * (t / 8);
+        float acc[4][4] = {};
 #pragma unroll
-            for (int d = 0; d < DH; ++d) s += Qs[r * (DH + 1) + d] * Ks[j * (DH + 1) + d];
-            s *= scale;
+        for (int d = 0; d < DH; d += 4) {
+            float4 qr[4], kr[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                qr[a] = *reinterpret_cast<const float4 *>(Qs + (r0 + a) * LD + d);
+                kr[a] = *reinterpret_cast<const float4 *>(Ks + (j0 + a) * LD + d);
+            }
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    acc[a][c] += qr[a].x * kr[c].x + qr[a].y * kr[c].y + qr[a].z * kr[c].z + qr[a].w * kr[c].w;
         }
-        S[r * Ts + j] = s;
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            float v[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) v[c] = (j0 + c > i0 + r0 + a) ? -1e9f : acc[a][c] * scale;   // maskedFill(-1e9)
+            *reinterpret_cast<float4 *>(S + (r0 + a) * SP + j0) = make_float4(v[0], v[1], v[2], v[3]);
+        }
     }
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int r = warp; r < rows; r += 4) {
         float mx = -INFINITY;
-        for (int j = lane; j < keys; j += 32) mx = fmaxf(mx, S[r * Ts + j]);
+        for (int j = lane; j < keys; j += 32) mx = fmaxf(mx, S[r * SP + j]);
 #pragma unroll
         for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         float sum = 0.0f;
         for (int j = lane; j < keys; j += 32) {
-            const float e = expf(S[r * Ts + j] - mx);
-            S[r * Ts + j] = e;
+            const float e = expf(S[r * SP + j] - mx);
+            S[r * SP + j] = e;
             sum += e;
         }
 #pragma unroll
         for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
         float *prow = P + ((size_t)bh * Ts + i0 + r) * Ts;
         for (int j = lane; j < Ts; j += 32) {
-            const float p = j < keys ? S[r * Ts + j] / sum : 0.0f;
-            if (j < keys) S[r * Ts + j] = p;
+            const float p = j < keys ? S[r * SP + j] / sum : 0.0f;
+            if (j < kp) S[r * SP + j] = p;   // zero past `keys`: the o tiles read up to kp
             prow[j] = p;
         }
     }
+    // rows of the block past Ts (the last block of a ragged length): zero, so o reads finite values
+    for (int i = threadIdx.x; i < (32 - rows) * kp; i += blockDim.x) S[(rows + i / kp) * SP + i % kp] = 0.0f;
     __syncthreads();
-    for (int i = threadIdx.x; i < rows * DH; i += blockDim.x) {
-        const int r = i / DH, d = i % DH;
-        float o = 0.0f;
-        for (int j = 0; j <= i0 + r; ++j) o += S[r * Ts + j] * Vs[j * (DH + 1) + d];
-        out[((size_t)b * Ts + i0 + r) * D + h * DH + d] = o;
+    // o[r][d] = sum_j P[r][j] v[j][d]: tile (4 rows, 4 d), 8 x 8 tiles
+    for (int t = threadIdx.x; t < 64; t += blockDim.x) {
+        const int r0 = 4 * (t % 8), d0 = 4 * (t / 8);
+        float acc[4][4] = {};
+        const int jend = min(kp, i0 + r0 + 4);   // causal: P is zero past each row's own position
+        for (int j = 0; j < jend; ++j) {
+            const float4 vv = *reinterpret_cast<const float4 *>(Vs + j * LD + d0);
+            const float vr[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                const float pv = S[(r0 + a) * SP + j];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[a][c] = fmaf(pv, vr[c], acc[a][c]);
+            }
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+            if (r0 + a < rows)
+                *reinterpret_cast<float4 *>(out + ((size_t)b * Ts + i0 + r0 + a) * D + h * DH + d0) =
+                    make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
     }
 }
 
@@ -400,71 +475,145 @@ __global__ void __launch_bounds__(128) attn_cached_kernel(const float *__restric
 }
 
 // Attention backward for one (sequence, head):
-//   dV = P^T dO;  dP = dO V^T;  dS = P (dP - rowsum(dP P)) * scale  (softmax and
-//   maskedFill backward: masked entries have P = 0);  dQ = dS K;  dK = dS^T Q.
+//   dV = P^T dO;  dP = dO V^T;  dS = P (dP - Dr) * scale  with Dr[r] = sum_j P[r][j] dP[r][j]
+//   (softmax and maskedFill backward: masked entries have P = 0);  dQ = dS K;  dK = dS^T Q.
+// Dr = dO[r] . O[r], O = P V the forward's output of this head (the same sum regrouped), so
+// no row reduction across threads is needed.  Every product is a 4 x 4 register tile of one
+// thread (float4 shared-memory reads along rows: 8 loads per 16 FMAs); only the causal lower
+// triangle of dS is computed (P is zero above the diagonal, so is dS).  Shared memory: Q, K,
+// V, dO [Tp][DH + 4] (Tp = Ts rounded up to 4, zero rows past Ts) and P / dS [Tp][Tp + 4].
 template <int DH>
 __global__ void __launch_bounds__(256) attn_bwd_kernel(const float *__restrict__ qkv, const float *__restrict__ P,
-                                                       const float *__restrict__ dO, float *__restrict__ dqkv,
-                                                       int Ts, int H, int D, float scale) {
-    extern __shared__ float sm[];
+                                                       const float *__restrict__ dO, const float *__restrict__ O,
+                                                       float *__restrict__ dqkv, int Ts, int H, int D, float scale) {
+    static_assert(DH == 32, "head dimension 32: 8 column tiles of 4");
+    extern __shared__ __align__(16) float sm[];
     const int bh = blockIdx.x, b = bh / H, h = bh % H;
-    const int LD = DH + 1;
-    float *Qs = sm, *Ks = Qs + Ts * LD, *Vs = Ks + Ts * LD, *Os = Vs + Ts * LD, *S = Os + Ts * LD;   // S: [Ts][Ts+1]
-    const int SL = Ts + 1;
+    const int Tp = (Ts + 3) & ~3, LD = DH + 4, SP = Tp + 4;
+    float *Qs = sm, *Ks = Qs + Tp * LD, *Vs = Ks + Tp * LD, *Gs = Vs + Tp * LD, *S = Gs + Tp * LD;
+    float *Dr = S + Tp * SP;   // [Tp]
     const size_t ld = 3 * (size_t)D;
     const float *base = qkv + (size_t)b * Ts * ld + h * DH;
-    for (int i = threadIdx.x; i < Ts * DH; i += blockDim.x) {
+    for (int i = threadIdx.x; i < Tp * DH; i += blockDim.x) {
         const int j = i / DH, d = i % DH;
-        Qs[j * LD + d] = base[(size_t)j * ld + d];
-        Ks[j * LD + d] = base[(size_t)j * ld + D + d];
-        Vs[j * LD + d] = base[(size_t)j * ld + 2 * D + d];
-        Os[j * LD + d] = dO[((size_t)b * Ts + j) * D + h * DH + d];
+        const bool in = j < Ts;
+        Qs[j * LD + d] = in ? base[(size_t)j * ld + d] : 0.0f;
+        Ks[j * LD + d] = in ? base[(size_t)j * ld + D + d] : 0.0f;
+        Vs[j * LD + d] = in ? base[(size_t)j * ld + 2 * D + d] : 0.0f;
+        Gs[j * LD + d] = in ? dO[((size_t)b * Ts + j) * D + h * DH + d] : 0.0f;
     }
     const float *Pb = P + (size_t)bh * Ts * Ts;
-    for (int i = threadIdx.x; i < Ts * Ts; i += blockDim.x) S[(i / Ts) * SL + (i % Ts)] = Pb[i];
-    __syncthreads();
-    float *gb = dqkv + (size_t)b * Ts * ld + h * DH;
-    // dV[j][d] = sum_{i >= j} P[i][j] dO[i][d]
-    for (int i = threadIdx.x; i < Ts * DH; i += blockDim.x) {
-        const int j = i / DH, d = i % DH;
-        float s = 0.0f;
-        for (int r = j; r < Ts; ++r) s += S[r * SL + j] * Os[r * LD + d];
-        gb[(size_t)j * ld + 2 * D + d] = s;
+    for (int i = threadIdx.x; i < Tp * Tp; i += blockDim.x) {
+        const int r = i / Tp, c = i % Tp;
+        S[r * SP + c] = (r < Ts && c <= r) ? Pb[(size_t)r * Ts + c] : 0.0f;
+    }
+    {   // Dr[r] = dO[r] . O[r], one warp per row
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        for (int r = warp; r < Tp; r += blockDim.x >> 5) {
+            float t = r < Ts ? dO[((size_t)b * Ts + r) * D + h * DH + lane] * O[((size_t)b * Ts + r) * D + h * DH + lane]
+                             : 0.0f;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+            if (lane == 0) Dr[r] = t;
+        }
     }
     __syncthreads();
-    // dS in place, one warp per row
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
-    for (int r = warp; r < Ts; r += warps) {
-        float dot = 0.0f;
-        float dp[8];   // Ts <= 256: at most 8 columns per lane
+    float *gb = dqkv + (size_t)b * Ts * ld + h * DH;
+    const int RT = Tp / 4;   // row tiles
+    // dV[j][d] = sum_{r >= j} P[r][j] dO[r][d]: tile (4 j, 4 d)
+    for (int t = threadIdx.x; t < RT * 8; t += blockDim.x) {
+        const int j0 = 4 * (t >> 3), d0 = 4 * (t & 7);
+        float acc[4][4] = {};
+        for (int r = j0; r < Tp; ++r) {
+            const float4 p = *reinterpret_cast<const float4 *>(S + r * SP + j0);
+            const float4 g = *reinterpret_cast<const float4 *>(Gs + r * LD + d0);
+            const float pv[4] = {p.x, p.y, p.z, p.w}, gv[4] = {g.x, g.y, g.z, g.w};
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const int j = lane + 32 * c;
-            dp[c] = 0.0f;
-            if (j <= r && j < Ts) {
-                float s = 0.0f;
+            for (int a = 0; a < 4; ++a)
 #pragma unroll
-                for (int d = 0; d < DH; ++d) s += Os[r * LD + d] * Vs[j * LD + d];
-                dp[c] = s;
-                dot += s * S[r * SL + j];
+                for (int c = 0; c < 4; ++c) acc[a][c] = fmaf(pv[a], gv[c], acc[a][c]);
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+            if (j0 + a < Ts)
+                *reinterpret_cast<float4 *>(gb + (size_t)(j0 + a) * ld + 2 * D + d0) =
+                    make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+    }
+    __syncthreads();
+    // dS[r][j] = P[r][j] (dP[r][j] - Dr[r]) scale, dP = dO V^T: tile (4 r, 4 j), j tile <= r tile,
+    // written over P (each thread reads and writes only its own tile)
+    const int ntri = RT * (RT + 1) / 2;
+    for (int t = threadIdx.x; t < ntri; t += blockDim.x) {
+        // lower-triangle tile t -> (rt, jt), jt <= rt
+        int rt = (int)((sqrtf(8.0f * t + 1.0f) - 1.0f) * 0.5f);
+        while ((rt + 1) * (rt + 2) / 2 <= t) ++rt;
+        while (rt * (rt + 1) / 2 > t) --rt;
+        const int jt = t - rt * (rt + 1) / 2;
+        const int r0 = 4 * rt, j0 = 4 * jt;
+        float acc[4][4] = {};
+#pragma unroll 4
+        for (int d = 0; d < DH; d += 4) {
+            float4 gr[4], vr[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                gr[a] = *reinterpret_cast<const float4 *>(Gs + (r0 + a) * LD + d);
+                vr[a] = *reinterpret_cast<const float4 *>(Vs + (j0 + a) * LD + d);
+            }
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    acc[a][c] += gr[a].x * vr[c].x + gr[a].y * vr[c].y + gr[a].z * vr[c].z + gr[a].w * vr[c].w;
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            float4 *sp = reinterpret_cast<float4 *>(S + (r0 + a) * SP + j0);
+            const float4 p = *sp;
+            const float dr = Dr[r0 + a];
+            *sp = make_float4(p.x * (acc[a][0] - dr) * scale, p.y * (acc[a][1] - dr) * scale,
+                              p.z * (acc[a][2] - dr) * scale, p.w * (acc[a][3] - dr) * scale);
+        }
+    }
+    __syncthreads();
+    // dQ[r][d] = sum_{j <= r} dS[r][j] K[j][d]: tile (4 r, 4 d)
+    for (int t = threadIdx.x; t < RT * 8; t += blockDim.x) {
+        const int r0 = 4 * (t >> 3), d0 = 4 * (t & 7);
+        float acc[4][4] = {};
+        const int jend = r0 + 4 < Tp ? r0 + 4 : Tp;
+        for (int j = 0; j < jend; ++j) {
+            const float4 k = *reinterpret_cast<const float4 *>(Ks + j * LD + d0);
+            const float kv[4] = {k.x, k.y, k.z, k.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                const float sv = S[(r0 + a) * SP + j];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[a][c] = fmaf(sv, kv[c], acc[a][c]);
             }
         }
 #pragma unroll
-        for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const int j = lane + 32 * c;
-            if (j < Ts) S[r * SL + j] = j <= r ? S[r * SL + j] * (dp[c] - dot) * scale : 0.0f;
-        }
+        for (int a = 0; a < 4; ++a)
+            if (r0 + a < Ts)
+                *reinterpret_cast<float4 *>(gb + (size_t)(r0 + a) * ld + d0) =
+                    make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < Ts * DH; i += blockDim.x) {
-        const int r = i / DH, d = i % DH;
-        float sq = 0.0f, sk = 0.0f;
-        for (int j = 0; j <= r; ++j) sq += S[r * SL + j] * Ks[j * LD + d];          // dQ[r]
-        for (int q = r; q < Ts; ++q) sk += S[q * SL + r] * Qs[q * LD + d];         // dK[r]
-        gb[(size_t)r * ld + d] = sq;
-        gb[(size_t)r * ld + D + d] = sk;
+    // dK[j][d] = sum_{r >= j} dS[r][j] Q[r][d]: tile (4 j, 4 d)
+    for (int t = threadIdx.x; t < RT * 8; t += blockDim.x) {
+        const int j0 = 4 * (t >> 3), d0 = 4 * (t & 7);
+        float acc[4][4] = {};
+        for (int r = j0; r < Tp; ++r) {
+            const float4 sr = *reinterpret_cast<const float4 *>(S + r * SP + j0);
+            const float4 q = *reinterpret_cast<const float4 *>(Qs + r * LD + d0);
+            const float sv[4] = {sr.x, sr.y, sr.z, sr.w}, qv[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[a][c] = fmaf(sv[a], qv[c], acc[a][c]);
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+            if (j0 + a < Ts)
+                *reinterpret_cast<float4 *>(gb + (size_t)(j0 + a) * ld + D + d0) =
+                    make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
     }
 }
 
@@ -534,13 +683,22 @@ int ln_bwd(LmEngine &e, const float *gout, const float *xh, const float *inv, co
     ln_bwd_kernel<<<e.ln_blocks, warps * 32, (size_t)warps * 2 * e.D * sizeof(float), stream()>>>(
         gout, xh, inv, gam, R, out, e.ln_partial, e.N, e.D);
     ZB_LAUNCH_CHECK("lm layernorm backward");
-    sum_ln_partials_kernel<<<(2 * e.D + 255) / 256, 256, 0, stream()>>>(e.ln_partial, e.ln_blocks, e.D, dg, db);
+    sum_partials_kernel<<<(2 * e.D + 7) / 8, 256, 0, stream()>>>(e.ln_partial, e.ln_blocks, 2 * e.D, e.D, dg, db);
     ZB_LAUNCH_CHECK("lm layernorm partials");
     return kOk;
 }
 
-int colsum(const float *dY, int rows, int ld, int sw, float *o0, float *o1 = nullptr, float *o2 = nullptr) {
-    colsum_kernel<<<(ld + 31) / 32, dim3(32, 8), 0, stream()>>>(dY, rows, ld, sw, o0, o1, o2);
+// Bias gradients: column sums of dY [rows][ld] in two fixed-order stages (row chunks over
+// about two blocks per SM, then the chunks in order), into segments of sw columns.
+int colsum(LmEngine &e, const float *dY, int rows, int ld, int sw, float *o0, float *o1 = nullptr, float *o2 = nullptr) {
+    const int tiles = (ld + 31) / 32;
+    int chunks = sm_count() * 2 / tiles;
+    if (chunks > rows / 32) chunks = rows / 32;
+    if (chunks > kColsumChunks) chunks = kColsumChunks;
+    if (chunks < 1) chunks = 1;
+    colsum_part_kernel<<<dim3(tiles, chunks), dim3(32, 8), 0, stream()>>>(dY, rows, ld, chunks, e.colsum_partial);
+    ZB_LAUNCH_CHECK("lm column sums (chunks)");
+    sum_cols_kernel<<<(ld + 7) / 8, 256, 0, stream()>>>(e.colsum_partial, chunks, ld, sw, o0, o1, o2);
     ZB_LAUNCH_CHECK("lm column sums");
     return kOk;
 }
@@ -590,6 +748,8 @@ int lm_build(Net &n, LmEngine &e) {
     e.ln_blocks = sm_count() * 2;
     if ((rc = lalloc(e, &e.ln_partial, (size_t)e.ln_blocks * 2 * D))) return rc;
     if ((rc = lalloc(e, &e.emb_partial, (size_t)((N + kEmbChunk - 1) / kEmbChunk) * V * D))) return rc;
+    const int widest = 3 * D > F ? (3 * D > V ? 3 * D : V) : (F > V ? F : V);
+    if ((rc = lalloc(e, &e.colsum_partial, (size_t)kColsumChunks * widest))) return rc;
     return kOk;
 }
 
@@ -813,8 +973,14 @@ int lm_tc_build(Net &n, LmEngine &e) {
     return kOk;
 }
 
-int attn_smem_fwd(int Ts, int dh) { return (int)((2 * (size_t)Ts * (dh + 1) + 32 * (dh + 1) + 32 * (size_t)Ts) * sizeof(float)); }
-int attn_smem_bwd(int Ts, int dh) { return (int)((4 * (size_t)Ts * (dh + 1) + (size_t)Ts * (Ts + 1)) * sizeof(float)); }
+int attn_smem_fwd(int Ts, int dh) {
+    const size_t Tp = (size_t)((Ts + 3) & ~3);
+    return (int)((2 * Tp * (dh + 4) + 32 * (size_t)(dh + 4) + 32 * (Tp + 4)) * sizeof(float));
+}
+int attn_smem_bwd(int Ts, int dh) {
+    const size_t Tp = (size_t)((Ts + 3) & ~3);
+    return (int)((4 * Tp * (dh + 4) + Tp * (Tp + 4) + Tp) * sizeof(float));
+}
 
 }  // namespace
 
@@ -898,7 +1064,7 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
     {
         LinWgrad wg{e.hf, n.dlogits, {G + e.o_head_W, nullptr, nullptr}, D, V, N, D, V, V};
         if ((rc = run_simt_gemm(wg, 0, "lm head dW"))) return rc;
-        if ((rc = colsum(n.dlogits, N, V, V, G + e.o_head_b))) return rc;
+        if ((rc = colsum(e, n.dlogits, N, V, V, G + e.o_head_b))) return rc;
         LinDgrad dg{n.dlogits, nullptr, {Pm + e.o_head_W, nullptr, nullptr}, e.dh, N, D, V, D, V, V};
         if ((rc = run_simt_gemm(dg, 1, "lm head dX"))) return rc;
         if ((rc = ln_bwd(e, e.dh, e.xhf, e.invf, Pm + e.o_lnf_g, nullptr, e.g, G + e.o_lnf_g, G + e.o_lnf_b))) return rc;
@@ -910,12 +1076,12 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
         // FFN
         LinWgrad w2{e.f1[l], e.g, {G + b.f2W, nullptr, nullptr}, F, D, N, F, D, D};
         if ((rc = tcp ? lm_tc_run(e, tg[8]) : run_simt_gemm(w2, 0, "lm fc2 dW"))) return rc;
-        if ((rc = colsum(e.g, N, D, D, G + b.f2b))) return rc;
+        if ((rc = colsum(e, e.g, N, D, D, G + b.f2b))) return rc;
         LinDgrad d2{e.g, e.f1[l], {Pm + b.f2W, nullptr, nullptr}, e.df1, N, F, D, F, D, D};
         if ((rc = tcp ? lm_tc_run(e, tg[4]) : run_simt_gemm(d2, 1, "lm fc2 dX"))) return rc;
         LinWgrad w1{e.h2[l], e.df1, {G + b.f1W, nullptr, nullptr}, D, F, N, D, F, F};
         if ((rc = tcp ? lm_tc_run(e, tg[9]) : run_simt_gemm(w1, 0, "lm fc1 dW"))) return rc;
-        if ((rc = colsum(e.df1, N, F, F, G + b.f1b))) return rc;
+        if ((rc = colsum(e, e.df1, N, F, F, G + b.f1b))) return rc;
         LinDgrad d1{e.df1, nullptr, {Pm + b.f1W, nullptr, nullptr}, e.dh, N, D, F, D, F, F};
         if ((rc = tcp ? lm_tc_run(e, tg[5]) : run_simt_gemm(d1, 1, "lm fc1 dX"))) return rc;
         if ((rc = ln_bwd(e, e.dh, e.xh2[l], e.inv2[l], Pm + b.ln2g, e.g, e.gm, G + b.ln2g, G + b.ln2b))) return rc;
@@ -923,16 +1089,16 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
         // attention
         LinWgrad wo{e.att[l], e.gm, {G + b.oW, nullptr, nullptr}, D, D, N, D, D, D};
         if ((rc = tcp ? lm_tc_run(e, tg[10]) : run_simt_gemm(wo, 0, "lm out dW"))) return rc;
-        if ((rc = colsum(e.gm, N, D, D, G + b.ob))) return rc;
+        if ((rc = colsum(e, e.gm, N, D, D, G + b.ob))) return rc;
         LinDgrad dout{e.gm, nullptr, {Pm + b.oW, nullptr, nullptr}, e.datt, N, D, D, D, D, D};
         if ((rc = tcp ? lm_tc_run(e, tg[6]) : run_simt_gemm(dout, 1, "lm out dX"))) return rc;
         attn_bwd_kernel<32><<<e.Bs * e.H, 256, attn_smem_bwd(e.Ts, 32), stream()>>>(e.qkv[l], e.P[l], e.datt,
-                                                                                  e.dqkv, e.Ts, e.H, D, scale);
+                                                                                  e.att[l], e.dqkv, e.Ts, e.H, D, scale);
         ZB_LAUNCH_CHECK("lm attention backward");
         prof_mark(n, "oproj_attn_bwd");
         LinWgrad wq{e.h1[l], e.dqkv, {G + b.qW, G + b.kW, G + b.vW}, D, 3 * D, N, D, 3 * D, D};
         if ((rc = tcp ? lm_tc_run(e, tg[11]) : run_simt_gemm(wq, 0, "lm qkv dW"))) return rc;
-        if ((rc = colsum(e.dqkv, N, 3 * D, D, G + b.qb, G + b.kb, G + b.vb))) return rc;
+        if ((rc = colsum(e, e.dqkv, N, 3 * D, D, G + b.qb, G + b.kb, G + b.vb))) return rc;
         LinDgrad dq{e.dqkv, nullptr, {Pm + b.qW, Pm + b.kW, Pm + b.vW}, e.dh, N, D, 3 * D, D, 3 * D, D};
         if ((rc = tcp ? lm_tc_run(e, tg[7]) : run_simt_gemm(dq, 1, "lm qkv dX"))) return rc;
         if ((rc = ln_bwd(e, e.dh, e.xh1[l], e.inv1[l], Pm + b.ln1g, e.gm, e.g, G + b.ln1g, G + b.ln1b))) return rc;

@@ -55,7 +55,7 @@ struct PeerState {
     cudaStream_t side_stream = nullptr;
     cudaEvent_t ev_mid = nullptr, ev_side = nullptr;
     long long mid_off = -1;                // first parameter of the late layers this step (-1: one phase)
-    bool two_phase = true;                 // use peer_step_mid (ZB_PEER_TWO_PHASE=0 turns it off)
+    bool two_phase = false;                // use peer_step_mid (ZB_PEER_TWO_PHASE=1 turns it on)
 };
 
 struct TcEngine;  // bf16 tensor-core engine (tc_net.cu)

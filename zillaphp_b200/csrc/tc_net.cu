@@ -357,6 +357,86 @@ __global__ void __launch_bounds__(256, 2) conv_first_fwd_img_kernel(const float 
     }
 }
 
+// First conv followed by a 2x2 max-pool, for images staged in shared memory: a
+// block walks whole images (the zero-padded image copied by a plain loop);
+// thread = (pooled window, 8-channel octet), octets fastest, so a warp writes
+// consecutive windows' channels as one contiguous run.  The window's 4 x 4 input
+// neighbourhood is read once for its four pixels; the octet's 72 weights and 8
+// biases live in registers as channel pairs, and each pair's four pixels are
+// summed with packed fp32x2 FMAs in the order of conv_first_fwd_kernel (bias,
+// then the taps ascending; each lane rounds like fmaf), then ReLU and the pool
+// with its rules (first maximum of the fp32 values, code = position | 4 when
+// positive): the same outputs and codes bit for bit.
+template <int COUT>
+__global__ void __launch_bounds__(256, 2) conv_first_pool_img_kernel(const float *__restrict__ x,
+                                                                  const float *__restrict__ w,
+                                                                  const float *__restrict__ bias,
+                                                                  bf16 *__restrict__ out, uint8_t *__restrict__ code,
+                                                                  int B, int H, int W, int pad) {
+    constexpr int NQ = COUT / 8;
+    constexpr int LANES = 256 / NQ;
+    extern __shared__ float xs[];
+    const int q = threadIdx.x % NQ, pl = threadIdx.x / NQ;
+    const int oH = H + 2 * pad - 2, oW = W + 2 * pad - 2;
+    const int pH = oH >> 1, pW = oW >> 1, NW = pH * pW;
+    const int PH = H + 2 * pad, PW = W + 2 * pad;
+    float2 wr2[4][9], br2[4];   // channel pairs (2k, 2k + 1) of the octet
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        br2[k] = make_float2(__ldg(bias + 8 * q + 2 * k), __ldg(bias + 8 * q + 2 * k + 1));
+#pragma unroll
+        for (int t = 0; t < 9; ++t)
+            wr2[k][t] = make_float2(__ldg(w + (8 * q + 2 * k) * 9 + t), __ldg(w + (8 * q + 2 * k + 1) * 9 + t));
+    }
+    for (int b = blockIdx.x; b < B; b += gridDim.x) {
+        __syncthreads();
+        const float *xb = x + (size_t)b * H * W;
+        for (int i = threadIdx.x; i < PH * PW; i += 256) {
+            const int ih = i / PW - pad, iw = i - (i / PW) * PW - pad;
+            xs[i] = ((unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W) ? __ldg(xb + ih * W + iw) : 0.0f;
+        }
+        __syncthreads();
+        for (int wi = pl; wi < NW; wi += LANES) {
+            const int ph = wi / pW, pw = wi - ph * pW;
+            const float *xr = xs + (2 * ph) * PW + 2 * pw;
+            float xv[4][4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) xv[r][c] = xr[r * PW + c];
+            uint4 pk;
+            __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
+            uint2 cp;
+            uint8_t *cb = reinterpret_cast<uint8_t *>(&cp);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                float2 best = make_float2(0.0f, 0.0f);
+                int px = 0, py = 0;
+#pragma unroll
+                for (int qq = 0; qq < 4; ++qq) {   // window position (kh, kw) = (qq >> 1, qq & 1)
+                    const int dy = qq >> 1, dx = qq & 1;
+                    float2 a = br2[k];
+#pragma unroll
+                    for (int t = 0; t < 9; ++t) {
+                        const float xt = xv[dy + t / 3][dx + t % 3];
+                        a = ffma2(make_float2(xt, xt), wr2[k][t], a);
+                    }
+                    a.x = a.x > 0.0f ? a.x : 0.0f;
+                    a.y = a.y > 0.0f ? a.y : 0.0f;
+                    if (qq == 0 || a.x > best.x) { best.x = a.x; px = qq; }
+                    if (qq == 0 || a.y > best.y) { best.y = a.y; py = qq; }
+                }
+                h2[k] = __floats2bfloat162_rn(best.x, best.y);
+                cb[2 * k] = (uint8_t)(px | (best.x > 0.0f ? 4 : 0));
+                cb[2 * k + 1] = (uint8_t)(py | (best.y > 0.0f ? 4 : 0));
+            }
+            const size_t o = ((size_t)b * NW + wi) * COUT + 8 * q;
+            *reinterpret_cast<uint4 *>(out + o) = pk;
+            *reinterpret_cast<uint2 *>(code + o) = cp;
+        }
+    }
+}
+
 // First-conv weight and bias gradient: dW[co][t] = sum_p dC[p][co] x[p + t],
 // db[co] = sum_p dC[p][co].  A block walks whole images: the image (with a
 // zero halo) is staged in shared memory; thread (pixel lane, channel octet)
@@ -464,6 +544,88 @@ __global__ void __launch_bounds__(256, 2) conv_first_wgrad_kernel(const bf16 *__
         float s = 0.0f;
         for (int wv = 0; wv < 8; ++wv) s += red[(wv * NQ + qq) * 80 + e * 10 + t];
         partial[(size_t)blockIdx.x * COUT * 10 + i] = s;
+    }
+}
+
+// First-conv weight and bias gradient when the conv is followed by a 2x2 max-pool:
+// dW[co][t] = sum_p dC[p][co] x[p + t] where dC = unpool(dP, codes) holds, per
+// window and channel, dP at the position the code names (and only when the
+// maximum was positive), zero at the other three.  So the sum runs over windows:
+// thread = (window lane, 8-channel octet): one 16-byte dP load and one 8-byte
+// code load per window, and for each routed channel the 3 x 3 patch of the
+// zero-padded image (staged in shared memory per image) at the routed pixel, 10
+// FMAs (9 taps + bias).  A quarter of the dense sum's FMAs and no full-size dC.
+// Partials as conv_first_wgrad_kernel: [block][COUT][10], lanes of an octet
+// combined by shuffles, warps in fixed order.
+template <int COUT>
+__global__ void __launch_bounds__(256, 2) conv_first_wgrad_pool_kernel(const bf16 *__restrict__ dP,
+                                                                    const uint8_t *__restrict__ code,
+                                                                    const float *__restrict__ x,
+                                                                    float *__restrict__ partial, int B, int H, int W,
+                                                                    int pad) {
+    constexpr int NQ = COUT / 8;
+    constexpr int LANES = 256 / NQ;
+    extern __shared__ float xs[];
+    const int q = threadIdx.x % NQ, pl = threadIdx.x / NQ;
+    const int oH = H + 2 * pad - 2, oW = W + 2 * pad - 2;
+    const int Ho = oH >> 1, Wo = oW >> 1, NW = Ho * Wo;
+    const int PH = H + 2 * pad, PW = W + 2 * pad;
+    float acc[8][10];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+#pragma unroll
+        for (int t = 0; t < 10; ++t) acc[e][t] = 0.0f;
+    for (int b = blockIdx.x; b < B; b += gridDim.x) {
+        __syncthreads();
+        const float *xb = x + (size_t)b * H * W;
+        for (int i = threadIdx.x; i < PH * PW; i += 256) {
+            const int ih = i / PW - pad, iw = i - (i / PW) * PW - pad;
+            xs[i] = ((unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W) ? __ldg(xb + ih * W + iw) : 0.0f;
+        }
+        __syncthreads();
+        const size_t ob = (size_t)b * NW * COUT + 8 * q;
+        for (int wi = pl; wi < NW; wi += LANES) {
+            const int ph = wi / Wo, pw = wi - ph * Wo;
+            const uint4 dv = __ldg(reinterpret_cast<const uint4 *>(dP + ob + (size_t)wi * COUT));
+            const uint2 cv = __ldg(reinterpret_cast<const uint2 *>(code + ob + (size_t)wi * COUT));
+            const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+            const uint32_t cw[2] = {cv.x, cv.y};
+            // window top-left in padded-image coordinates of the conv output pixel (2ph, 2pw):
+            // output pixel (oh, ow) reads padded rows oh .. oh + 2, columns ow .. ow + 2
+            const int base0 = (2 * ph) * PW + 2 * pw;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const uint32_t c = (cw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+                if (!(c & 4u)) continue;   // the window's maximum was not positive: no gradient
+                const float g = __uint_as_float(e & 1 ? dw[e >> 1] & 0xFFFF0000u : dw[e >> 1] << 16);
+                const float *xr = xs + base0 + (int)((c >> 1) & 1u) * PW + (int)(c & 1u);
+#pragma unroll
+                for (int t = 0; t < 9; ++t) acc[e][t] = fmaf(g, xr[(t / 3) * PW + (t % 3)], acc[e][t]);
+                acc[e][9] += g;
+            }
+        }
+    }
+    // lanes of a warp with the same octet: lane = window-slot * NQ + q
+#pragma unroll
+    for (int off = NQ; off < 32; off <<= 1)
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+#pragma unroll
+            for (int t = 0; t < 10; ++t) acc[e][t] += __shfl_xor_sync(0xffffffffu, acc[e][t], off);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float *red = xs;   // [8 warps][NQ][80]
+    if (lane < NQ)
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+#pragma unroll
+            for (int t = 0; t < 10; ++t) red[(warp * NQ + lane) * 80 + e * 10 + t] = acc[e][t];
+    __syncthreads();
+    for (int i = threadIdx.x; i < COUT * 10; i += blockDim.x) {   // i = co*10 + t, co = 8q + e
+        const int co = i / 10, t = i % 10, qq = co / 8, e = co % 8;
+        float sum = 0.0f;
+        for (int wv = 0; wv < 8; ++wv) sum += red[(wv * NQ + qq) * 80 + e * 10 + t];
+        partial[(size_t)blockIdx.x * COUT * 10 + i] = sum;
     }
 }
 
@@ -702,24 +864,70 @@ __global__ void __launch_bounds__(256) head_fwd_kernel(const bf16 *__restrict__ 
 
 // Direct head: the classifier Linear (F -> NC, NC <= 12) on the flattened last
 // pooled activation a [B][F] (NHWC order, bf16), softmax cross-entropy and the
-// start of the backward, one warp per row:
+// start of the backward:
 //   z = a W + b;  loss_r = -log softmax(z)[y];  dz = (p - onehot) / B
 //   dA = dz W^T -> bf16 [B][F]  (the pool's ReLU lives in the pool codes)
 // W comes packed in bf16 groups (kHeadGroup) and stays in shared memory
-// (F / 8 groups of 196 bytes: 147 KB at F = 6144).  Lane l owns the 8-input
-// groups l, l + 32, ... of the row: one 16-byte load of a per group.  dz goes
-// to global memory for the weight-gradient kernel; the block's bias-gradient
-// and loss partial is [NC + 1] (fixed warp order).  logits != null: the
-// evaluation forward (logits out, the loss partial only when y is given).
+// (F / 8 groups of 196 bytes: 147 KB at F = 6144), shared by the block's 16
+// warps.  A warp takes two rows at a time: lane l owns the 8-input groups l,
+// l + 32, ... of both, so each weight word read from shared memory serves two
+// rows, and the next group's two 16-byte loads of a are issued before the
+// current group's arithmetic.  dz goes to global memory for the weight-gradient
+// kernel; the block's bias-gradient and loss partial is [NC + 1] (fixed warp
+// order).  logits != null: the evaluation forward (logits out, the loss partial
+// only when y is given).
+constexpr int kHeadWarps = 16;
+
 template <int NC>
-__global__ void __launch_bounds__(256) head_direct_kernel(const bf16 *__restrict__ a, const bf16 *__restrict__ wq,
-                                                          const float *__restrict__ bias, const float *__restrict__ y,
-                                                          float *__restrict__ dz_out, bf16 *__restrict__ dA,
-                                                          float *__restrict__ logits, float *__restrict__ partial,
-                                                          int B, int F, float invB) {
+__device__ __forceinline__ void head_rows_fwd(const uint32_t *__restrict__ sWq, const uint4 *a0, const uint4 *a1,
+                                              bool two, int GPL, int lane, float (&z0)[NC], float (&z1)[NC]) {
+#pragma unroll
+    for (int n = 0; n < NC; ++n) { z0[n] = 0.0f; z1[n] = 0.0f; }
+    uint4 c0 = __ldg(a0 + lane), c1 = two ? __ldg(a1 + lane) : make_uint4(0, 0, 0, 0);
+    for (int j = 0; j < GPL; ++j) {
+        const int g = lane + 32 * j;
+        uint4 n0 = make_uint4(0, 0, 0, 0), n1 = make_uint4(0, 0, 0, 0);
+        if (j + 1 < GPL) {   // the next group's loads go out before this group's arithmetic
+            n0 = __ldg(a0 + g + 32);
+            if (two) n1 = __ldg(a1 + g + 32);
+        }
+        const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w}, w1[4] = {c1.x, c1.y, c1.z, c1.w};
+        const uint32_t *wg = sWq + g * (kHeadGroup / 2);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float x0 = __uint_as_float(e & 1 ? w0[e >> 1] & 0xFFFF0000u : w0[e >> 1] << 16);
+            const float x1 = __uint_as_float(e & 1 ? w1[e >> 1] & 0xFFFF0000u : w1[e >> 1] << 16);
+#pragma unroll
+            for (int n = 0; n < NC; n += 2) {
+                const uint32_t w2 = wg[(e * NC + n) >> 1];   // NC even: bf16 pairs (n, n + 1)
+                const float wa = __uint_as_float(w2 << 16), wb = __uint_as_float(w2 & 0xFFFF0000u);
+                z0[n] = fmaf(x0, wa, z0[n]);
+                z0[n + 1] = fmaf(x0, wb, z0[n + 1]);
+                z1[n] = fmaf(x1, wa, z1[n]);
+                z1[n + 1] = fmaf(x1, wb, z1[n + 1]);
+            }
+        }
+        c0 = n0;
+        c1 = n1;
+    }
+#pragma unroll
+    for (int n = 0; n < NC; ++n) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            z0[n] += __shfl_xor_sync(0xffffffffu, z0[n], o);
+            z1[n] += __shfl_xor_sync(0xffffffffu, z1[n], o);
+        }
+    }
+}
+
+template <int NC>
+__global__ void __launch_bounds__(kHeadWarps * 32) head_direct_kernel(
+    const bf16 *__restrict__ a, const bf16 *__restrict__ wq, const float *__restrict__ bias,
+    const float *__restrict__ y, float *__restrict__ dz_out, bf16 *__restrict__ dA, float *__restrict__ logits,
+    float *__restrict__ partial, int B, int F, float invB) {
     extern __shared__ uint32_t sWq[];   // F / 8 groups of 49 words
-    __shared__ float sAcc[8][NC + 1];
-    __shared__ double sLoss[8];
+    __shared__ float sAcc[kHeadWarps][NC + 1];
+    __shared__ double sLoss[kHeadWarps];
     griddep_launch();
     griddep_wait();
     const int G = F / 8;
@@ -732,85 +940,88 @@ __global__ void __launch_bounds__(256) head_direct_kernel(const bf16 *__restrict
 #pragma unroll
     for (int n = 0; n < NC; ++n) gB[n] = 0.0f;
     double lsum = 0.0;
-    for (int r = blockIdx.x * 8 + warp; r < B; r += gridDim.x * 8) {
-        const uint4 *ar = reinterpret_cast<const uint4 *>(a + (size_t)r * F);
-        float z[NC];
+    for (int r0 = 2 * (blockIdx.x * kHeadWarps + warp); r0 < B; r0 += 2 * gridDim.x * kHeadWarps) {
+        const bool two = r0 + 1 < B;
+        float z[2][NC];
+        head_rows_fwd<NC>(sWq, reinterpret_cast<const uint4 *>(a + (size_t)r0 * F),
+                          reinterpret_cast<const uint4 *>(a + (size_t)(r0 + (two ? 1 : 0)) * F), two, GPL, lane,
+                          z[0], z[1]);
+        float dz[2][NC];
 #pragma unroll
-        for (int n = 0; n < NC; ++n) z[n] = 0.0f;
-        for (int j = 0; j < GPL; ++j) {
-            const int g = lane + 32 * j;
-            const uint4 av = __ldg(ar + g);
-            const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
-            const uint32_t *wg = sWq + g * (kHeadGroup / 2);
+        for (int q = 0; q < 2; ++q) {
+            const int r = r0 + q;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float ae = __uint_as_float(e & 1 ? aw[e >> 1] & 0xFFFF0000u : aw[e >> 1] << 16);
+            for (int n = 0; n < NC; ++n) z[q][n] += bias[n];
+            if (q == 1 && !two) {
 #pragma unroll
-                for (int n = 0; n < NC; n += 2) {
-                    const uint32_t w2 = wg[(e * NC + n) >> 1];   // NC even: bf16 pairs (n, n + 1)
-                    z[n] = fmaf(ae, __uint_as_float(w2 << 16), z[n]);
-                    z[n + 1] = fmaf(ae, __uint_as_float(w2 & 0xFFFF0000u), z[n + 1]);
-                }
+                for (int n = 0; n < NC; ++n) dz[q][n] = 0.0f;
+                continue;
+            }
+            if (logits && lane < NC) {
+                float zl = z[q][0];
+#pragma unroll
+                for (int n = 1; n < NC; ++n) if (lane == n) zl = z[q][n];
+                logits[(size_t)r * NC + lane] = zl;
+            }
+#pragma unroll
+            for (int n = 0; n < NC; ++n) dz[q][n] = 0.0f;
+            if (!y) continue;
+            float mx = z[q][0];
+#pragma unroll
+            for (int n = 1; n < NC; ++n) mx = fmaxf(mx, z[q][n]);
+            float se = 0.0f;
+#pragma unroll
+            for (int n = 0; n < NC; ++n) se += expf(z[q][n] - mx);
+            const int t = (int)y[r];
+            float pt = 0.0f;
+#pragma unroll
+            for (int n = 0; n < NC; ++n) if (n == t) pt = expf(z[q][n] - mx) / se;
+            if (lane == 0) lsum += -(double)logf(pt);
+            if (logits) continue;
+#pragma unroll
+            for (int n = 0; n < NC; ++n) {
+                dz[q][n] = (expf(z[q][n] - mx) / se - (n == t ? 1.0f : 0.0f)) * invB;
+                gB[n] += dz[q][n];
+            }
+            if (lane < NC) {
+                float dl = dz[q][0];
+#pragma unroll
+                for (int n = 1; n < NC; ++n) if (lane == n) dl = dz[q][n];
+                dz_out[(size_t)r * NC + lane] = dl;
             }
         }
-#pragma unroll
-        for (int n = 0; n < NC; ++n) {
-#pragma unroll
-            for (int o = 16; o; o >>= 1) z[n] += __shfl_xor_sync(0xffffffffu, z[n], o);
-            z[n] += bias[n];
-        }
-        if (logits && lane < NC) {
-            float zl = z[0];
-#pragma unroll
-            for (int n = 1; n < NC; ++n) if (lane == n) zl = z[n];
-            logits[(size_t)r * NC + lane] = zl;
-        }
-        if (!y) continue;
-        float mx = z[0];
-#pragma unroll
-        for (int n = 1; n < NC; ++n) mx = fmaxf(mx, z[n]);
-        float se = 0.0f;
-#pragma unroll
-        for (int n = 0; n < NC; ++n) se += expf(z[n] - mx);
-        const int t = (int)y[r];
-        float pt = 0.0f;
-#pragma unroll
-        for (int n = 0; n < NC; ++n) if (n == t) pt = expf(z[n] - mx) / se;
-        if (lane == 0) lsum += -(double)logf(pt);
-        if (logits) continue;
-        float dz[NC];
-#pragma unroll
-        for (int n = 0; n < NC; ++n) {
-            dz[n] = (expf(z[n] - mx) / se - (n == t ? 1.0f : 0.0f)) * invB;
-            gB[n] += dz[n];
-        }
-        if (lane < NC) {
-            float dl = dz[0];
-#pragma unroll
-            for (int n = 1; n < NC; ++n) if (lane == n) dl = dz[n];
-            dz_out[(size_t)r * NC + lane] = dl;
-        }
-        uint4 *dr = reinterpret_cast<uint4 *>(dA + (size_t)r * F);
+        if (logits || !y) continue;
+        // dA = dz W^T for both rows: each weight word serves the two rows
+        uint4 *d0 = reinterpret_cast<uint4 *>(dA + (size_t)r0 * F);
+        uint4 *d1 = reinterpret_cast<uint4 *>(dA + (size_t)(r0 + 1) * F);
         for (int j = 0; j < GPL; ++j) {
             const int g = lane + 32 * j;
             const uint32_t *wg = sWq + g * (kHeadGroup / 2);
-            float o8[8];
+            float o0[8], o1[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-                float acc = 0.0f;
+                float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
                 for (int n = 0; n < NC; n += 2) {
                     const uint32_t w2 = wg[(e * NC + n) >> 1];
-                    acc = fmaf(dz[n], __uint_as_float(w2 << 16), acc);
-                    acc = fmaf(dz[n + 1], __uint_as_float(w2 & 0xFFFF0000u), acc);
+                    const float wa = __uint_as_float(w2 << 16), wb = __uint_as_float(w2 & 0xFFFF0000u);
+                    s0 = fmaf(dz[0][n], wa, s0);
+                    s0 = fmaf(dz[0][n + 1], wb, s0);
+                    s1 = fmaf(dz[1][n], wa, s1);
+                    s1 = fmaf(dz[1][n + 1], wb, s1);
                 }
-                o8[e] = acc;
+                o0[e] = s0;
+                o1[e] = s1;
             }
-            uint4 pk;
-            __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
+            uint4 p0, p1;
+            __nv_bfloat162 *h0 = reinterpret_cast<__nv_bfloat162 *>(&p0), *h1 = reinterpret_cast<__nv_bfloat162 *>(&p1);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) h2[e] = __floats2bfloat162_rn(o8[2 * e], o8[2 * e + 1]);
-            dr[g] = pk;
+            for (int e = 0; e < 4; ++e) {
+                h0[e] = __floats2bfloat162_rn(o0[2 * e], o0[2 * e + 1]);
+                h1[e] = __floats2bfloat162_rn(o1[2 * e], o1[2 * e + 1]);
+            }
+            d0[g] = p0;
+            if (two) d1[g] = p1;
         }
     }
     if (!partial) return;
@@ -823,7 +1034,7 @@ __global__ void __launch_bounds__(256) head_direct_kernel(const bf16 *__restrict
     if (threadIdx.x <= NC) {   // fixed warp order
         float sacc = 0.0f;
         double sl = 0.0;
-        for (int wv = 0; wv < 8; ++wv) {
+        for (int wv = 0; wv < kHeadWarps; ++wv) {
             if (threadIdx.x < NC) sacc += sAcc[wv][threadIdx.x];
             else sl += sLoss[wv];
         }
@@ -832,32 +1043,53 @@ __global__ void __launch_bounds__(256) head_direct_kernel(const bf16 *__restrict
 }
 
 // Weight gradient of the direct head: dW[k][n] = sum_b a[b][k] dz[b][n] over a
-// slice of the batch, k in NHWC order.  Block = 64 inputs x a batch slice;
-// thread (k, n-group of NC / 4) keeps NC / 4 sums; a warp's 32 loads of a are
-// 64 contiguous bytes.  Partials [split][F][NC], summed in split order.
+// batch slice, k in NHWC order.  Block = 512 inputs (thread: 2 consecutive
+// inputs, one 4-byte load per row, 2 x NC sums) x a batch slice whose dz rows
+// are staged in shared memory.  Partials [split][F][NC], summed in split order.
+constexpr int kHeadWgRows = 256;   // rows of dz staged per pass
+
 template <int NC>
 __global__ void __launch_bounds__(256) head_direct_wgrad_kernel(const bf16 *__restrict__ a,
                                                                 const float *__restrict__ dz,
                                                                 float *__restrict__ partial, int B, int F,
                                                                 int splits) {
-    constexpr int NPT = NC / 4;   // classes per thread
+    __shared__ float sdz[kHeadWgRows * NC];
     griddep_launch();
     griddep_wait();
-    const int kchunks = F / 64;
+    const int kchunks = F / 512;
     const int kc = blockIdx.x % kchunks, split = blockIdx.x / kchunks;
-    const int k = kc * 64 + (threadIdx.x & 63), n0 = (threadIdx.x >> 6) * NPT;
+    const int k = kc * 512 + 2 * threadIdx.x;
     const int b0 = (int)((long long)B * split / splits), b1 = (int)((long long)B * (split + 1) / splits);
-    float acc[NPT];
+    float acc[2][NC];
 #pragma unroll
-    for (int j = 0; j < NPT; ++j) acc[j] = 0.0f;
-    for (int b = b0; b < b1; ++b) {
-        const float av = __bfloat162float(a[(size_t)b * F + k]);
+    for (int e = 0; e < 2; ++e)
 #pragma unroll
-        for (int j = 0; j < NPT; ++j) acc[j] = fmaf(av, __ldg(dz + (size_t)b * NC + n0 + j), acc[j]);
+        for (int n = 0; n < NC; ++n) acc[e][n] = 0.0f;
+    for (int c0 = b0; c0 < b1; c0 += kHeadWgRows) {
+        const int rows = min(kHeadWgRows, b1 - c0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < rows * NC; i += blockDim.x) sdz[i] = dz[(size_t)c0 * NC + i];
+        __syncthreads();
+        const uint32_t *ar = reinterpret_cast<const uint32_t *>(a + (size_t)c0 * F + k);
+        uint32_t nxt = __ldg(ar);
+        for (int r = 0; r < rows; ++r) {
+            const uint32_t cur = nxt;
+            if (r + 1 < rows) nxt = __ldg(ar + (size_t)(r + 1) * (F / 2));
+            const float x0 = __uint_as_float(cur << 16), x1 = __uint_as_float(cur & 0xFFFF0000u);
+            const float *dr = sdz + r * NC;
+#pragma unroll
+            for (int n = 0; n < NC; ++n) {
+                const float d = dr[n];
+                acc[0][n] = fmaf(x0, d, acc[0][n]);
+                acc[1][n] = fmaf(x1, d, acc[1][n]);
+            }
+        }
     }
-    float *dst = partial + ((size_t)split * F + k) * NC + n0;
+    float *dst = partial + ((size_t)split * F + k) * NC;
 #pragma unroll
-    for (int j = 0; j < NPT; ++j) dst[j] = acc[j];
+    for (int e = 0; e < 2; ++e)
+#pragma unroll
+        for (int n = 0; n < NC; ++n) dst[e * NC + n] = acc[e][n];
 }
 
 // Sums partial[s][i] over s in order and scatters into the gradient layout.
@@ -1388,7 +1620,8 @@ int tc_build(Net &n, TcEngine &e) {
     if (e.c1_pool) { H = st[i].oH; W = st[i].oW; ++i; }
     int rc;
     if ((rc = dalloc(e, &e.a1, (size_t)B * H * W * C))) return rc;
-    if ((rc = dalloc(e, &e.dC1, (size_t)B * e.H1 * e.W1 * C))) return rc;
+    // the full-size first-conv gradient (a pooled first conv's weight gradient reads dP1 and the codes)
+    if ((rc = dalloc(e, &e.dC1, e.c1_pool ? (size_t)1 : (size_t)B * e.H1 * e.W1 * C))) return rc;
     if (e.c1_pool) {
         if ((rc = dalloc(e, &e.code1, (size_t)B * H * W * C))) return rc;
         if ((rc = dalloc(e, &e.dP1, (size_t)B * H * W * C))) return rc;
@@ -1666,17 +1899,17 @@ int tc_build(Net &n, TcEngine &e) {
         // classifier on the flattened last pooled activation: packed bf16 weights in shared
         // memory, logit gradients to global memory for the weight-gradient kernel
         e.direct_head = true;
-        if (e.NC != 12 || e.F % 256 || (size_t)e.F / 8 * kHeadGroup * 2 > 200 * 1024)
+        if (e.NC != 12 || e.F % 512 || (size_t)e.F / 8 * kHeadGroup * 2 > 200 * 1024)
             return fail(kBadArg, "tc engine: classifier %d->%d after the last pool not supported", e.F, e.NC);
         if ((rc = dalloc(e, &e.dflat, (size_t)B * e.F))) return rc;
         if ((rc = dalloc(e, &e.wq, (size_t)e.F / 8 * kHeadGroup))) return rc;
         if ((rc = dalloc(e, &e.dz, (size_t)B * e.NC))) return rc;
-        e.head_grid = (B + 7) / 8;
+        e.head_grid = (B + 2 * kHeadWarps - 1) / (2 * kHeadWarps);   // two rows per warp
         if (e.head_grid > sm_count()) e.head_grid = sm_count();
         if ((rc = dalloc(e, &e.head_partial, (size_t)e.head_grid * (e.NC + 1)))) return rc;
-        // weight gradient: 64-input chunks x batch slices, about four blocks per SM
-        const int kchunks = e.F / 64;
-        e.hdw_splits = (sm_count() * 4 + kchunks - 1) / kchunks;
+        // weight gradient: 512-input chunks x batch slices, about two blocks per SM
+        const int kchunks = e.F / 512;
+        e.hdw_splits = (sm_count() * 2 + kchunks - 1) / kchunks;
         if (e.hdw_splits > B) e.hdw_splits = B;
         if (e.hdw_splits < 1) e.hdw_splits = 1;
         if ((rc = dalloc(e, &e.hdw_partial, (size_t)e.hdw_splits * e.F * e.NC))) return rc;
@@ -1702,7 +1935,7 @@ int tc_build(Net &n, TcEngine &e) {
     if (e.c1_fused) e.convs.front().fbwd.c1_partial = e.c1_partial;
     // diagnostics
     e.views.push_back({"conv1.out", e.a1, (size_t)B * (e.c1_pool ? (e.H1 / 2) * (e.W1 / 2) : e.H1 * e.W1) * e.C1, 0});
-    if (!e.c1_fused) e.views.push_back({"conv1.dC", e.dC1, (size_t)B * e.H1 * e.W1 * e.C1, 0});
+    if (!e.c1_fused && !e.c1_pool) e.views.push_back({"conv1.dC", e.dC1, (size_t)B * e.H1 * e.W1 * e.C1, 0});
     if (e.c1_pool) {
         e.views.push_back({"conv1.code", e.code1, (size_t)B * (e.H1 / 2) * (e.W1 / 2) * e.C1, 1});
         e.views.push_back({"conv1.dP", e.dP1, (size_t)B * (e.H1 / 2) * (e.W1 / 2) * e.C1, 0});
@@ -1777,8 +2010,10 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
             launch_pdl(tc::conv_first_tc_kernel<32>, dim3(g), dim3(128), tc::ConvFirstTcShape<32>::SMEM, x, w1, b1,
                        e.a1, B, e.H0, e.W0, device_error_word());
         } else if (e.C1 == 32 && !e.c1_pool) conv_first_fwd_img_kernel<32><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
+        else if (e.C1 == 32 && xsm <= 48 * 1024) conv_first_pool_img_kernel<32><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
         else if (e.C1 == 32) conv_first_fwd_kernel<32, true><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
         else if (!e.c1_pool) conv_first_fwd_img_kernel<16><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
+        else if (xsm <= 48 * 1024) conv_first_pool_img_kernel<16><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
         else conv_first_fwd_kernel<16, true><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
         ZB_LAUNCH_CHECK("conv_first_fwd");
         prof_mark(n, "conv_fwd");
@@ -1798,7 +2033,7 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
         }
         const bf16 *flat = e.convs.empty() ? e.a1 : e.convs.back().out;
         float *gW = n.grads + sf.poff, *gb = gW + sf.pn_w;
-        launch_pdl(head_direct_kernel<12>, dim3(e.head_grid), dim3(256), smem, flat, e.wq, n.params + sf.poff + sf.pn_w,
+        launch_pdl(head_direct_kernel<12>, dim3(e.head_grid), dim3(kHeadWarps * 32), smem, flat, e.wq, n.params + sf.poff + sf.pn_w,
                    y, logits_out ? nullptr : e.dz, logits_out ? nullptr : e.dflat, logits_out,
                    (logits_out && !(y && loss_out)) ? nullptr : e.head_partial, B, e.F, 1.0f / (float)B);
         ZB_LAUNCH_CHECK("head direct");
@@ -1817,7 +2052,7 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
             if ((rc = reduce(r))) return rc;
         }
         prof_mark(n, "softmax_ce");
-        launch_pdl(head_direct_wgrad_kernel<12>, dim3((e.F / 64) * e.hdw_splits), dim3(256), 0, flat, e.dz,
+        launch_pdl(head_direct_wgrad_kernel<12>, dim3((e.F / 512) * e.hdw_splits), dim3(256), 0, flat, e.dz,
                    e.hdw_partial, B, e.F, e.hdw_splits);
         ZB_LAUNCH_CHECK("head direct weight gradient");
         {
@@ -1964,13 +2199,11 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
         const size_t smem = (size_t)(padded > 8 * 4 * 80 ? padded : 8 * 4 * 80) * sizeof(float);
         if (smem > 48 * 1024) return fail(kBadArg, "tc engine: first-conv image too large for the weight-gradient kernel");
         const bool big = padded > kStageRegs * 256;   // past the register stager: a plain copy per image
-        if (e.c1_pool) {   // dC1 = unpool(dP1, codes): a separate pass (the kernel below is issue-bound)
-            const int G = e.C1 / 8, slots = 256 / G;
-            unpool_kernel<<<sm_count() * 4, slots * G, slots * G * 8 * sizeof(float), stream()>>>(
-                e.dP1, e.code1, e.dC1, e.c1_partial /*scratch*/, B, e.H1, e.W1, e.C1);
-            ZB_LAUNCH_CHECK("unpool first");
+        if (e.c1_pool) {   // straight from the pooled gradient and the codes: no unpooled dC1
+            if (e.C1 == 32) conv_first_wgrad_pool_kernel<32><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dP1, e.code1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
+            else conv_first_wgrad_pool_kernel<16><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dP1, e.code1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
         }
-        if (e.C1 == 32 && !big) conv_first_wgrad_kernel<32><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
+        else if (e.C1 == 32 && !big) conv_first_wgrad_kernel<32><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
         else if (e.C1 == 32) conv_first_wgrad_kernel<32, true><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
         else if (!big) conv_first_wgrad_kernel<16><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
         else conv_first_wgrad_kernel<16, true><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);

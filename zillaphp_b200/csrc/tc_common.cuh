@@ -210,6 +210,38 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64
         : "memory");
 }
 
+// The same MMA with the A operand kept in the tensor core's collector buffer:
+// OP 0 (fill) reads A from shared memory and keeps it, OP 1 (use) takes A from
+// the buffer instead of shared memory, OP 2 (lastuse) takes it and releases
+// the buffer.  For a run of MMAs that share one A (same descriptor), issued
+// back to back by one thread.
+template <int OP>
+__device__ __forceinline__ void mma_bf16_ca(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            bool accumulate) {
+    static_assert(OP >= 0 && OP <= 2, "collector op");
+    if constexpr (OP == 0)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16.collector::a::fill [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
+            : "memory");
+    else if constexpr (OP == 1)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16.collector::a::use [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
+            : "memory");
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16.collector::a::lastuse [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
+            : "memory");
+}
+
 // Arrives on `bar` once all previously issued MMAs of this thread complete.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

@@ -38,10 +38,17 @@
 // an MN-major UMMA operand with K = pixels; the second epilogue warp group
 // builds the matching im2col tile of x (rows = pixels, 64 bf16: x_hi of the 9
 // taps, 1.0 for the bias, x_lo of the 9 taps at 16.., with x = x_hi + x_lo so the
-// fp32 input keeps its precision; 128-byte swizzle).  One elected epilogue
-// thread issues the R*W/16 MMAs D1[64][32] += im2col^T dX per tile (M = 64, N =
+// fp32 input keeps its precision; 128-byte swizzle).  Once both are staged
+// the epilogue marks the buffer ready, and the MMA thread, after the next
+// tile's MMAs, issues the R*W/16 MMAs D1[64][32] += im2col^T dX (M = 64, N =
 // 32); at the end D1's hi rows (+ bias) and lo rows go out as two [32][10]
 // partials per CTA, which the deterministic split reduction adds.
+//
+// The nine weight-gradient MMAs of a K16 step share A (the dY rows): the first
+// fills the tensor core's collector buffer with it and the other eight read it
+// from there, so shared memory serves A once per step instead of nine times.
+// Every MMA of the CTA comes from the one MMA thread, so nothing else is issued
+// between them.
 //
 // UP (dY is the max-unpool of the pooled gradient dP [B, H/2, W/2, CY] by the
 // pool codes [B, H/2, W/2, CY], byte = window position | 4 when routed): four
@@ -128,7 +135,8 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
     uint64_t *wg_full = wbar + 1;
     uint64_t *drain = wg_full + 1;
     uint64_t *c1_done = drain + 1;       // [2] (C1): the first-conv MMAs reading buffer i finished
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(c1_done + 2);
+    uint64_t *c1_ready = c1_done + 2;    // [2] (C1): buffer i's dX and im2col tiles are staged
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(c1_ready + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     int *armed = const_cast<int *>(abort_flag) + 1;   // [NS]
 
@@ -150,6 +158,8 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
         mbar_init(drain, 1);
         mbar_init(&c1_done[0], 1);
         mbar_init(&c1_done[1], 1);
+        mbar_init(&c1_ready[0], 1);
+        mbar_init(&c1_ready[1], 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -206,7 +216,25 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
                 const uint64_t dw_a0 = smem_desc(smem_u32(sA), 128, lbo, kSwNone);          // MN-major dY
                 const uint64_t dw_b0 = smem_desc(smem_u32(sA) + (uint32_t)p.x_off, 128, (uint32_t)p.region, kSwNone);
                 const uint32_t wp = (uint32_t)p.Wp;
+                // C1: the first conv's weight-gradient MMAs of the CTA's m-th tile, once the
+                // epilogue has staged buffer m & 1 (this thread issues every MMA of the CTA, so
+                // no other MMA lands inside a run that keeps A in the collector buffer)
+                auto issue_c1 = [&](int m) -> bool {
+                    const int b1 = m & 1;
+                    if (!mbar_wait(&c1_ready[b1], (uint32_t)((m >> 1) & 1), abort_flag, p.err, kErrAccWait)) return false;
+                    tc_fence_after();
+                    constexpr uint32_t IDESC_C1 = idesc_bf16(64, CX, true, true);
+                    const uint32_t xa = smem_u32(outbuf + b1 * OBUF + p.out_tile_bytes);
+                    const uint32_t db = smem_u32(outbuf + b1 * OBUF);
+                    const int ksteps = (p.R * p.W) / 16;
+                    for (int k = 0; k < ksteps; ++k)
+                        mma_bf16(tmem_base + (uint32_t)S::C1_COL0, smem_desc(xa + k * 2048, 16, 1024, kSw128),
+                                 smem_desc(db + k * 1024, 16, 512, kSw64), IDESC_C1, (m | k) != 0);
+                    mma_commit(&c1_done[b1]);
+                    return true;
+                };
                 int n = 0;
+                bool c1_ok = true;
                 for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x, ++n) {
                     if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1u, abort_flag, p.err, kErrAccWait)) break;
                     if (!mbar_wait(&full[s], ph, abort_flag, p.err, kErrFullWait)) break;
@@ -226,20 +254,32 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
                     }
                     mma_commit(&acc_full[acc]);
                     if (++acc == 2) { acc = 0; acc_ph ^= 1u; }
-                    // weight gradient: 8 K16 steps (128 pixel rows) x 9 taps
+                    // weight gradient: 8 K16 steps (128 pixel rows) x 9 taps; the 9 MMAs of a
+                    // K16 step share A (dY), which stays in the collector buffer after the
+                    // first, so shared memory serves it once instead of nine times
                     const uint64_t a_dy = dw_a0 + st16 + (uint64_t)(wp + 1);
 #pragma unroll 1
                     for (int k = 0; k < 8; ++k) {
 #pragma unroll
                         for (int tap = 0; tap < 9; ++tap) {
                             const int dh = tap / 3, dw = tap - 3 * dh;
-                            mma_bf16(tmem_base + (uint32_t)(S::WG_COL0 + tap * CX), a_dy + (uint64_t)(16 * k),
-                                     dw_b0 + st16 + (uint64_t)(dh * wp + dw + 16 * k), IDESC_DW, (n | k) != 0);
+                            const uint32_t dt = tmem_base + (uint32_t)(S::WG_COL0 + tap * CX);
+                            const uint64_t ad = a_dy + (uint64_t)(16 * k);
+                            const uint64_t bd = dw_b0 + st16 + (uint64_t)(dh * wp + dw + 16 * k);
+                            if (tap == 0) mma_bf16_ca<0>(dt, ad, bd, IDESC_DW, (n | k) != 0);
+                            else if (tap == 8) mma_bf16_ca<2>(dt, ad, bd, IDESC_DW, (n | k) != 0);
+                            else mma_bf16_ca<1>(dt, ad, bd, IDESC_DW, (n | k) != 0);
                         }
                     }
                     issued = true;
                     mma_commit(&empty[s]);
                     if (++s == NS) { s = 0; ph ^= 1u; }
+                    if constexpr (C1) {   // the previous tile's first-conv MMAs
+                        if (n > 0 && !(c1_ok = issue_c1(n - 1))) break;
+                    }
+                }
+                if constexpr (C1) {
+                    if (c1_ok && n > 0 && !*abort_flag) issue_c1(n - 1);   // the last tile's
                 }
             }
             if (issued) mma_commit(wg_full);
@@ -438,16 +478,9 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
             if (etid == 0) {
                 mbar_arrive(&empty[s]);   // this stage's mask reads are done
                 if (C1) {
-                    // D1[64][CX] += im2col^T (MN-major, 128-byte swizzle) x dX (MN-major, 64-byte swizzle)
-                    tc_fence_after();
-                    constexpr uint32_t IDESC_C1 = idesc_bf16(64, CX, true, true);
-                    const uint32_t xa = smem_u32(outbuf + sb * OBUF + p.out_tile_bytes);
-                    const uint32_t db = smem_u32(outbuf + sb * OBUF);
-                    const int ksteps = (p.R * p.W) / 16;
-                    for (int k = 0; k < ksteps; ++k)
-                        mma_bf16(tmem_base + (uint32_t)S::C1_COL0, smem_desc(xa + k * 2048, 16, 1024, kSw128),
-                                 smem_desc(db + k * 1024, 16, 512, kSw64), IDESC_C1, (n | k) != 0);
-                    mma_commit(&c1_done[sb]);
+                    // D1[64][CX] += im2col^T (MN-major, 128-byte swizzle) x dX (MN-major, 64-byte
+                    // swizzle): issued by the MMA thread once this buffer is marked staged
+                    mbar_arrive(&c1_ready[sb]);
                     c1_state |= 1u << sb;
                 } else {
                     tma_store_4d(&p.out_map, outbuf + sb * p.out_tile_bytes, 0, 0, h0, b);

@@ -1,7 +1,11 @@
-// tc_gemm.cuh -- K-major tcgen05 GEMM: D[m, n] = sum_k A[m][k] * B[n][k]
-// (bf16 operands, fp32 accumulation in TMEM), used for the Linear layers:
-//   forward          A = X [rows][in],     B = W^T [out][in]     -> Z [rows][out]
-//   input gradient   A = dZ [rows][out],   B = W [in][out]       -> dX [rows][in]
+// tc_gemm.cuh -- tcgen05 GEMM: D[m, n] = sum_k A[m][k] * B(k, n) (bf16
+// operands, fp32 accumulation in TMEM), used for the Linear layers:
+//   forward          A = X [rows][in],     B = W [in][out] (MN-major)  -> Z [rows][out]
+//   input gradient   A = dZ [rows][out],   B = W [in][out] (K-major)   -> dX [rows][in]
+// Both read the same packed bf16 copy of W: K-major B tiles are BN rows of 64
+// k (one box); MN-major B tiles are 64 k rows of BN, as BN / 64 boxes of
+// 64 x 64 (128-byte swizzle; 8-row groups 1024 B apart, 64-wide n blocks one
+// box apart).
 // Tiles of 128 x BN, K staged 64 elements (128 B, 128-byte swizzle) per TMA
 // box; persistent CTAs, warp-specialised (producer / MMA / 4 epilogue warps),
 // double-buffered TMEM accumulators.
@@ -27,7 +31,7 @@ enum GemmEpi { kGemmBiasRelu = 0, kGemmStore = 1, kGemmPartial = 2 };
 
 struct GemmTcParams {
     CUtensorMap a_map;   // 2D {K, M} bf16, box {64, 128}
-    CUtensorMap b_map;   // 2D {K, N} bf16, box {64, BN}
+    CUtensorMap b_map;   // 2D {K, N} bf16, box {64, BN}; MN-major: 2D {N, K}, box {64, 64}
     CUtensorMap out_map; // kGemmStore: 2D {N, M} bf16, box {32, 128}, 64-byte swizzle
     int M, N, K;         // N % BN == 0, K % 64 == 0
     int m_tiles, n_tiles;
@@ -49,8 +53,9 @@ struct GemmTcShape {
     static_assert(BN % 32 == 0 && BN <= 256, "BN");
 };
 
-template <int BN, int EPI, int NS>
+template <int BN, int EPI, int NS, bool BMN = false>
 __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ GemmTcParams p) {
+    static_assert(!BMN || BN % 64 == 0, "MN-major B tiles are whole 64-wide boxes");
     griddep_launch();
     using S = GemmTcShape<BN, NS>;
     extern __shared__ uint8_t smem_raw[];
@@ -65,7 +70,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
     int *armed = const_cast<int *>(abort_flag) + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    constexpr uint32_t IDESC = idesc_bf16(128, BN, false, false);
+    constexpr uint32_t IDESC = idesc_bf16(128, BN, false, BMN);
     const int mn_tiles = p.m_tiles * p.n_tiles;
     const int num_tiles = mn_tiles * p.ksplit;
     const int ksteps = p.K / 64;
@@ -101,7 +106,13 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                     armed[s] = (int)ph + 1;
                     uint8_t *st = sbase + s * S::STAGE;
                     tma_load_2d(st, &p.a_map, &full[s], k * 64, mt * 128);
-                    tma_load_2d(st + S::ABYTES, &p.b_map, &full[s], k * 64, nt * BN);
+                    if constexpr (BMN) {
+#pragma unroll
+                        for (int j = 0; j < BN / 64; ++j)
+                            tma_load_2d(st + S::ABYTES + j * 8192, &p.b_map, &full[s], nt * BN + j * 64, k * 64);
+                    } else {
+                        tma_load_2d(st + S::ABYTES, &p.b_map, &full[s], k * 64, nt * BN);
+                    }
                     if (++s == NS) { s = 0; ph ^= 1u; }
                 }
             }
@@ -128,7 +139,8 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                     const uint32_t a0 = s0 + s * S::STAGE, b0 = a0 + S::ABYTES;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        mma_bf16(d, smem_desc(a0 + kk * 32, 16, 1024, kSw128), smem_desc(b0 + kk * 32, 16, 1024, kSw128),
+                        mma_bf16(d, smem_desc(a0 + kk * 32, 16, 1024, kSw128),
+                                 BMN ? smem_desc(b0 + kk * 2048, 8192, 1024, kSw128) : smem_desc(b0 + kk * 32, 16, 1024, kSw128),
                                  IDESC, (k > kb) || kk != 0);
                     issued = true;
                     mma_commit(&empty[s]);

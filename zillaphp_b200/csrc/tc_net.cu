@@ -109,6 +109,8 @@ constexpr int kMaxPack = 8;
 struct PackJobs {
     PackJob j[kMaxPack];
     int count;
+    int conv_blocks;   // blocks [0, conv_blocks) take the jobs above; the rest pack `fc`
+    PackJob fc;        // the hidden Linear weight's rows (n = 0: none)
 };
 
 __device__ __forceinline__ int nhwc_to_nchw(int k, int C, int H, int W) {
@@ -126,13 +128,44 @@ constexpr int kHeadGroup = 98;
 // weights are < 2^31 elements):
 //   kind 0 (forward): dst[(t*COUT + co)*CIN + ci] = W[co][ci][t]
 //   kind 1 (dgrad)  : dst[(t*CIN + ci)*COUT + co] = W[co][ci][8 - t]   (flipped, transposed)
-__global__ void pack_kernel(PackJobs jobs) {
+// The bf16 copy of the hidden Linear weight W [F][N] (row-major over NCHW
+// features) that both of its GEMMs read (the forward as an MN-major operand,
+// the input gradient as a K-major one): wP[k'][n] = W[nchw(k')][n], k' the
+// NHWC feature index of the conv output.  Four consecutive n per thread: one
+// 16-byte load (N % 64 == 0; four loads if W is not 16-byte aligned), one
+// 8-byte store.  J: src W, dst wP, a = F, b = N, C/H/W the flatten geometry.
+__device__ __forceinline__ void pack_fc_rows(const PackJob &J, int block, int nblocks) {
+    const int n4 = J.b / 4;
+    const bool vec = (reinterpret_cast<uintptr_t>(J.src) & 15) == 0;
+    for (long long q = (long long)block * blockDim.x + threadIdx.x; q < (long long)J.a * n4;
+         q += (long long)nblocks * blockDim.x) {
+        const int k = (int)(q / n4), c4 = (int)(q % n4);
+        const float *src = J.src + (size_t)nhwc_to_nchw(k, J.C, J.H, J.W) * J.b + 4 * c4;
+        const float4 v = vec ? __ldg(reinterpret_cast<const float4 *>(src)) : make_float4(src[0], src[1], src[2], src[3]);
+        uint2 pk;
+        __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&pk);
+        h2[0] = __floats2bfloat162_rn(v.x, v.y);
+        h2[1] = __floats2bfloat162_rn(v.z, v.w);
+        reinterpret_cast<uint2 *>(J.dst + (size_t)k * J.b)[c4] = pk;
+    }
+}
+
+// Every bf16 operand copy of the step from the fp32 master weights, in one
+// launch: the conv weights in their forward / input-gradient layouts and the
+// direct classifier's grouped layout (blocks [0, conv_blocks)), and the hidden
+// Linear weight's rows (the other blocks).
+__global__ void __launch_bounds__(256) pack_kernel(const __grid_constant__ PackJobs jobs) {
     griddep_launch();
     griddep_wait();
+    if ((int)blockIdx.x >= jobs.conv_blocks) {
+        pack_fc_rows(jobs.fc, (int)blockIdx.x - jobs.conv_blocks, (int)gridDim.x - jobs.conv_blocks);
+        return;
+    }
+    const int stride = jobs.conv_blocks * blockDim.x;
     for (int ji = 0; ji < jobs.count; ++ji) {
-        const PackJob J = jobs.j[ji];
+        const PackJob &J = jobs.j[ji];
         const int n = (int)J.n;
-        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
             float v;
             if (J.kind == 4) {   // i = k * NC + n over the classifier weight [F][NC]
                 const int n = i % J.b, k = i / J.b;
@@ -149,34 +182,6 @@ __global__ void pack_kernel(PackJobs jobs) {
             }
             J.dst[i] = __float2bfloat16_rn(v);
         }
-    }
-}
-
-// The two bf16 copies of the hidden Linear weight W [F][N] (row-major over
-// NCHW features; k' is the NHWC feature index of the conv output):
-//   wP[k'][n] = W[nchw(k')][n]   (input-gradient GEMM operand)
-//   wT[n][k'] = W[nchw(k')][n]   (forward GEMM operand, K-major)
-// W is read once, in 32 x 32 tiles through shared memory, so the fp32 reads
-// and both bf16 writes are coalesced.
-__global__ void __launch_bounds__(256) pack_fc_kernel(const float *__restrict__ W, bf16 *__restrict__ wP,
-                                                      bf16 *__restrict__ dst, int F, int N, int C, int H, int Wd) {
-    __shared__ float tile[32][33];
-    griddep_launch();
-    griddep_wait();
-    const int k0 = blockIdx.x * 32, n0 = blockIdx.y * 32;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8
-    for (int r = ty; r < 32; r += 8) {
-        const int k = k0 + r;
-        if (k < F && n0 + tx < N) {
-            const float v = W[(size_t)nhwc_to_nchw(k, C, H, Wd) * N + n0 + tx];
-            tile[r][tx] = v;
-            wP[(size_t)k * N + n0 + tx] = __float2bfloat16_rn(v);
-        }
-    }
-    __syncthreads();
-    for (int r = ty; r < 32; r += 8) {
-        const int n = n0 + r;
-        if (n < N && k0 + tx < F) dst[(size_t)n * F + k0 + tx] = __float2bfloat16_rn(tile[tx][r]);
     }
 }
 
@@ -1172,9 +1177,10 @@ __global__ void __launch_bounds__(256) reduce_deep_kernel(ReduceArgs r) {
 
 // Several independent deep reductions in one launch: blocks [start[j],
 // start[j+1]) run job j exactly as reduce_deep_kernel would.
+constexpr int kMaxReduceJobs = 6;
 struct ReduceJobs {
-    ReduceArgs job[3];
-    int start[4];
+    ReduceArgs job[kMaxReduceJobs];
+    int start[kMaxReduceJobs + 1];
     int count;
 };
 
@@ -1207,6 +1213,54 @@ __global__ void __launch_bounds__(256) reduce_multi_kernel(const __grid_constant
             r_store(r, i, s);
         }
         __syncthreads();
+    }
+}
+
+// The same jobs, 128 elements per block when every job's length is a multiple
+// of 4: warp w sums splits w, w + 8, w + 16, ... in order, four consecutive
+// elements per lane (one 16-byte load: a warp reads 512 contiguous bytes of a
+// split, four splits in flight), then the eight warp sums of each element are
+// added in warp order (a fixed order: deterministic).
+__global__ void __launch_bounds__(256) reduce_multi4_kernel(const __grid_constant__ ReduceJobs J) {
+    griddep_launch();
+    griddep_wait();
+    int j = 0;
+    while (j + 1 < J.count && (int)blockIdx.x >= J.start[j + 1]) ++j;
+    const ReduceArgs &r = J.job[j];
+    __shared__ float4 part[8][32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const long long n4 = r.n >> 2;
+    const long long q = (long long)((int)blockIdx.x - J.start[j]) * 32 + lane;
+    float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (q < n4) {
+        const float4 *p = reinterpret_cast<const float4 *>(r.partial) + q;
+        int k = w;
+        for (; k + 24 < r.splits; k += 32) {
+            const float4 a = __ldcg(p + (size_t)k * n4), b = __ldcg(p + (size_t)(k + 8) * n4);
+            const float4 c = __ldcg(p + (size_t)(k + 16) * n4), d = __ldcg(p + (size_t)(k + 24) * n4);
+            s.x += a.x; s.y += a.y; s.z += a.z; s.w += a.w;
+            s.x += b.x; s.y += b.y; s.z += b.z; s.w += b.w;
+            s.x += c.x; s.y += c.y; s.z += c.z; s.w += c.w;
+            s.x += d.x; s.y += d.y; s.z += d.z; s.w += d.w;
+        }
+        for (; k < r.splits; k += 8) {
+            const float4 a = __ldcg(p + (size_t)k * n4);
+            s.x += a.x; s.y += a.y; s.z += a.z; s.w += a.w;
+        }
+    }
+    part[w][lane] = s;
+    __syncthreads();
+    if (w == 0 && q < n4) {
+        float4 t = part[0][lane];
+#pragma unroll
+        for (int l = 1; l < 8; ++l) {
+            const float4 u = part[l][lane];
+            t.x += u.x; t.y += u.y; t.z += u.z; t.w += u.w;
+        }
+        r_store(r, 4 * q, t.x);
+        r_store(r, 4 * q + 1, t.y);
+        r_store(r, 4 * q + 2, t.z);
+        r_store(r, 4 * q + 3, t.w);
     }
 }
 
@@ -1311,7 +1365,7 @@ struct TcEngine {
     // hidden Linear (tensor cores) and head
     bool has_hidden = false;
     int hid_si = 0, HD = 0, head_si = 0, NC = 0;
-    bf16 *wT = nullptr, *wP = nullptr;   // hidden Linear packed W^T [HD][F], W [F][HD]
+    bf16 *wP = nullptr;   // hidden Linear packed W [F][HD] (NHWC feature rows)
     bf16 *a_hid = nullptr;               // [B][HD]
     bf16 *dZ_hid = nullptr;              // [B][HD]
     bf16 *dflat = nullptr;               // gradient w.r.t. the flattened activation [B][F]
@@ -1330,6 +1384,7 @@ struct TcEngine {
     float *hdw_partial = nullptr;        // [hdw_splits][F][NC]
     double *row_loss = nullptr;
     PackJobs pack{};
+    int pack_grid = 0;
     std::vector<void *> allocs;
     // named intermediate tensors (zilla_net_inspect)
     struct View { std::string name; const void *p; size_t n; int kind; };   // kind 0 bf16, 1 u8, 2 f32
@@ -1517,6 +1572,7 @@ int launch_wgrad(const WgradTcParams &p, int grid, int smem) {
 // dp: the pooled gradient when the conv-co kernel builds dY itself (null: dY from the a map)
 int run_wgrad(const WgradTcParams &p0, int mode, int grid, int smem, const bf16 *dp = nullptr) {
     if (mode == tc::kWgLinear) return launch_wgrad<tc::kWgLinear>(p0, grid, smem);
+    if (mode == tc::kWgLinearN128) return launch_wgrad<tc::kWgLinearN128>(p0, grid, smem);
     if (mode == tc::kWgConvCo) {
         if (!dp) return launch_wgrad<tc::kWgConvCo>(p0, grid, smem);
         WgradTcParams p = p0;
@@ -1526,10 +1582,10 @@ int run_wgrad(const WgradTcParams &p0, int mode, int grid, int smem, const bf16 
     return launch_wgrad<tc::kWgConvTap>(p0, grid, smem);
 }
 
-template <int BN, int EPI, int NS>
+template <int BN, int EPI, int NS, bool BMN = false>
 int launch_gemm(const GemmTcParams &p) {
     using S = tc::GemmTcShape<BN, NS>;
-    auto kern = tc::gemm_tc_kernel<BN, EPI, NS>;
+    auto kern = tc::gemm_tc_kernel<BN, EPI, NS, BMN>;
     static bool attr = false;
     if (!attr) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM) != cudaSuccess)
@@ -1544,21 +1600,27 @@ int launch_gemm(const GemmTcParams &p) {
 
 // Deep reductions (many splits, short vectors) of one phase in one launch.
 int reduce_multi(const ReduceArgs *jobs, int count) {
+    if (count < 1 || count > kMaxReduceJobs) return fail(kBadArg, "reduce_multi: %d jobs", count);
     ReduceJobs J{};
     J.count = count;
+    bool vec = true;   // every partial vector a multiple of 4 long (16-byte aligned splits)
+    for (int j = 0; j < count; ++j)
+        vec = vec && jobs[j].n % 4 == 0 && (reinterpret_cast<uintptr_t>(jobs[j].partial) & 15) == 0;
     int total = 0;
     for (int j = 0; j < count; ++j) {
         J.job[j] = jobs[j];
         J.start[j] = total;
-        total += grid_for(jobs[j].n, 8, 16);
+        total += vec ? (int)((jobs[j].n / 4 + 31) / 32) : grid_for(jobs[j].n, 8, 16);
     }
     J.start[count] = total;
-    launch_pdl(reduce_multi_kernel, dim3(total), dim3(256), 0, J);
+    if (vec) launch_pdl(reduce_multi4_kernel, dim3(total), dim3(256), 0, J);
+    else launch_pdl(reduce_multi_kernel, dim3(total), dim3(256), 0, J);
     ZB_LAUNCH_CHECK("reduce_multi");
     return kOk;
 }
 
 int reduce(const ReduceArgs &r) {
+    if (r.splits >= 32 && r.n <= 131072 && r.n % 4 == 0) return reduce_multi(&r, 1);
     if (r.splits >= 32 && r.n <= 131072) {
         launch_pdl(reduce_deep_kernel, dim3(grid_for(r.n, 8, 16)), dim3(256), 0, r);   // 8 elements per block
     } else if (r.n % 4 == 0 && r.n >= 65536 && r.splits <= 16) {
@@ -1815,20 +1877,19 @@ int tc_build(Net &n, TcEngine &e) {
         e.HD = s.oC;
         if (e.F % 64 || e.HD % 64 || e.HD > 256)
             return fail(kBadArg, "tc engine: hidden Linear %d->%d not supported", e.F, e.HD);
-        if ((rc = dalloc(e, &e.wT, (size_t)e.F * e.HD))) return rc;
         if ((rc = dalloc(e, &e.wP, (size_t)e.F * e.HD))) return rc;
         if ((rc = dalloc(e, &e.a_hid, (size_t)B * e.HD))) return rc;
         if ((rc = dalloc(e, &e.dZ_hid, (size_t)B * e.HD))) return rc;
         if ((rc = dalloc(e, &e.dflat, (size_t)B * e.F))) return rc;
-        // forward: A = flattened activation [B][F], B = W^T [HD][F]
+        // forward: A = flattened activation [B][F], B = W [F][HD] (MN-major: 64 x 64 boxes)
         GemmTcParams &g = e.fc_fwd;
         {
             const uint64_t da[2] = {(uint64_t)e.F, (uint64_t)B}, sa[1] = {(uint64_t)e.F * 2};
             const uint32_t ba[2] = {64, 128};
             if ((rc = tc::make_tmap_bf16(&g.a_map, prev, 2, da, sa, ba, tc::kSw128))) return rc;
-            const uint64_t db[2] = {(uint64_t)e.F, (uint64_t)e.HD}, sb[1] = {(uint64_t)e.F * 2};
-            const uint32_t bb[2] = {64, 128};
-            if ((rc = tc::make_tmap_bf16(&g.b_map, e.wT, 2, db, sb, bb, tc::kSw128))) return rc;
+            const uint64_t db[2] = {(uint64_t)e.HD, (uint64_t)e.F}, sb[1] = {(uint64_t)e.HD * 2};
+            const uint32_t bb[2] = {64, 64};
+            if ((rc = tc::make_tmap_bf16(&g.b_map, e.wP, 2, db, sb, bb, tc::kSw128))) return rc;
         }
         // 128-wide N tiles; when the batch gives fewer tiles than SMs, split K
         // so that the tiles fill the SMs (fp32 partials, summed in split order)
@@ -1881,13 +1942,21 @@ int tc_build(Net &n, TcEngine &e) {
         if (e.HD != 256) return fail(kBadArg, "tc engine: hidden Linear width must be 256");
         w.mode = tc::kWgLinear; w.K_total = B; w.m_tiles = e.F / 128; w.M = e.F; w.N = e.HD;
         if (e.F % 128) return fail(kBadArg, "tc engine: Linear input %d not a multiple of 128", e.F);
-        w.splits = sm_count() / w.m_tiles;   // one wave: one CTA per SM fits
+        // one wave of one CTA per SM: two N halves per M tile when they fit, then K splits;
+        // a single split writes the gradient itself (no partials, no reduction)
+        w.n_tiles = w.m_tiles * 2 <= sm_count() ? 2 : 1;
+        w.splits = sm_count() / (w.m_tiles * w.n_tiles);
         if (w.splits < 1) w.splits = 1;
         if (w.splits > (B + 63) / 64) w.splits = (B + 63) / 64;
         w.kstage_rows = 64; w.err = device_error_word();
-        e.fc_wg_grid = w.m_tiles * w.splits;
-        e.fc_wg_smem = tc::WgradTcShape<tc::kWgLinear>::smem(64);
-        if ((rc = dalloc(e, &e.fc_partial, (size_t)w.splits * e.F * e.HD))) return rc;
+        w.oC = e.fC; w.oHW = e.fH * e.fW; w.out = nullptr;
+        e.fc_wg_grid = w.m_tiles * w.n_tiles * w.splits;
+        if (w.n_tiles == 2) w.mode = tc::kWgLinearN128;
+        e.fc_wg_smem = w.n_tiles == 2 ? tc::WgradTcShape<tc::kWgLinearN128>::smem(64)
+                                      : tc::WgradTcShape<tc::kWgLinear>::smem(64);
+        if (w.splits > 1) {
+            if ((rc = dalloc(e, &e.fc_partial, (size_t)w.splits * e.F * e.HD))) return rc;
+        }
         w.partial = e.fc_partial;
         ++i;
     }
@@ -1957,7 +2026,6 @@ int tc_build(Net &n, TcEngine &e) {
     }
     e.views.push_back({"flat.d", e.dflat, (size_t)B * e.F, 0});
     if (e.has_hidden) {
-        e.views.push_back({"hidden.wT", e.wT, (size_t)e.F * e.HD, 0});
         e.views.push_back({"hidden.wP", e.wP, (size_t)e.F * e.HD, 0});
     } else {
         e.views.push_back({"head.dz", e.dz, (size_t)B * e.NC, 2});
@@ -1972,6 +2040,13 @@ int tc_build(Net &n, TcEngine &e) {
     }
     if (e.direct_head)   // the classifier weight [F][NC] in its grouped bf16 layout
         pj.j[pj.count++] = {4, n.params + st[e.head_si].poff, e.wq, e.F, e.NC, e.fC, e.fH, e.fW, (long long)e.F * e.NC};
+    pj.conv_blocks = sm_count();
+    pj.fc = PackJob{};
+    e.pack_grid = pj.conv_blocks;
+    if (e.has_hidden) {
+        pj.fc = {5, n.params + st[e.hid_si].poff, e.wP, e.F, e.HD, e.fC, e.fH, e.fW, (long long)e.F * e.HD};
+        e.pack_grid += grid_for((long long)e.F * e.HD / 4, 256, 8);
+    }
     return kOk;
 }
 
@@ -1982,14 +2057,8 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
     auto &st = n.st;
     int rc;
     // ---- pack bf16 operands from the fp32 master
-    launch_pdl(pack_kernel, dim3(sm_count()), dim3(256), 0, e.pack);
+    launch_pdl(pack_kernel, dim3(e.pack_grid), dim3(256), 0, e.pack);
     ZB_LAUNCH_CHECK("pack");
-    if (e.has_hidden) {
-        const float *W4 = n.params + st[e.hid_si].poff;
-        launch_pdl(pack_fc_kernel, dim3((e.F + 31) / 32, (e.HD + 31) / 32), dim3(256), 0, W4, e.wP, e.wT, e.F, e.HD,
-                   e.fC, e.fH, e.fW);
-        ZB_LAUNCH_CHECK("pack transpose");
-    }
     prof_mark(n, "pack");
     // ---- forward
     const Stage &s1 = st[e.c1_si];
@@ -2063,11 +2132,11 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
         if ((rc = dp_bucket_ready(n, sf.poff))) return rc;
         prof_mark(n, "linear_bwd");
     } else if (e.fc_fwd.ksplit > 1) {
-        if ((rc = launch_gemm<128, tc::kGemmPartial, 6>(e.fc_fwd))) return rc;
+        if ((rc = launch_gemm<128, tc::kGemmPartial, 6, true>(e.fc_fwd))) return rc;
         ReduceArgs r{e.fc_fwd_partial, e.fc_fwd.ksplit, (long long)B * e.HD, 6, B, e.HD, 0, 0, 0, 0,
                      nullptr, nullptr, nullptr, e.fc_fwd.bias, e.a_hid};
         if ((rc = reduce(r))) return rc;
-    } else if ((rc = launch_gemm<128, tc::kGemmBiasRelu, 6>(e.fc_fwd))) {
+    } else if ((rc = launch_gemm<128, tc::kGemmBiasRelu, 6, true>(e.fc_fwd))) {
         return rc;
     }
     if (!e.direct_head) prof_mark(n, "linear_fwd");
@@ -2109,8 +2178,12 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
                          : launch_gemm<128, tc::kGemmStore, 4>(e.fc_dgrad);
         if (rc) return rc;
     }
-    if ((rc = run_wgrad(e.fc_wg, tc::kWgLinear, e.fc_wg_grid, e.fc_wg_smem))) return rc;
-    {
+    if (e.fc_wg.splits == 1) {   // the kernel writes the gradient itself
+        WgradTcParams w = e.fc_wg;
+        w.out = gW4;
+        if ((rc = run_wgrad(w, w.mode, e.fc_wg_grid, e.fc_wg_smem))) return rc;
+    } else {
+        if ((rc = run_wgrad(e.fc_wg, e.fc_wg.mode, e.fc_wg_grid, e.fc_wg_smem))) return rc;
         ReduceArgs r{e.fc_partial, e.fc_wg.splits, (long long)e.F * e.HD, 3, e.F, e.HD, 0, e.fC, e.fH, e.fW,
                      gW4, nullptr, nullptr};
         if ((rc = reduce(r))) return rc;
@@ -2122,6 +2195,12 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
     }
     // ---- conv stages backward (last to first)
     const bf16 *dpooled = e.dflat;   // gradient w.r.t. the last pooled output
+    // deep reductions of a layer whose partial sums nothing reads before the next fused
+    // backward kernel ends: they join that kernel's reduction launch (one launch fewer).
+    // Not while the data-parallel exchange starts beside the fused kernel: it needs them final.
+    ReduceArgs held[kMaxReduceJobs];
+    int nheld = 0;
+    const bool hold_ok = !(n.peer.on && n.peer.two_phase);
     for (int li = (int)e.convs.size() - 1; li >= 0; --li) {
         ConvLayer &L = e.convs[li];
         const Stage &s = st[L.si];
@@ -2142,8 +2221,10 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
             if ((rc = peer_step_mid(n, s.poff + s.pn_w + s.pn_b))) return rc;
             if ((rc = run_conv_bwd_fused(L, x, dP))) return rc;
             // the kernel's partials: conv2 dW, conv2 db (UP), conv1 dW + db (C1)
-            ReduceArgs jobs[3];
+            ReduceArgs jobs[kMaxReduceJobs];
             int nj = 0;
+            for (int j = 0; j < nheld; ++j) jobs[nj++] = held[j];
+            nheld = 0;
             jobs[nj++] = ReduceArgs{L.fbwd_partial, L.fbwd_grid, (long long)L.COUT * 9 * L.CIN, 1, L.COUT, 9 * L.CIN,
                                     L.CIN, 0, 0, 0, n.grads + s.poff, nullptr, nullptr};
             if (L.fbwd_up)
@@ -2183,7 +2264,10 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
                                      n.grads + s.poff + s.pn_w, nullptr, nullptr};
             bool deep = true;
             for (int j = 0; j < nj; ++j) deep = deep && jobs[j].splits >= 32 && jobs[j].n <= 131072;
-            if (deep) {
+            const bool next_fused = li > 0 && e.convs[li - 1].fused_bwd;
+            if (deep && hold_ok && next_fused) {
+                for (int j = 0; j < nj; ++j) held[nheld++] = jobs[j];
+            } else if (deep) {
                 if ((rc = reduce_multi(jobs, nj))) return rc;
             } else {
                 for (int j = 0; j < nj; ++j)

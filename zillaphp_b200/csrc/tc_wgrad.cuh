@@ -34,7 +34,10 @@
 namespace zb {
 namespace tc {
 
-enum WgMode { kWgLinear = 0, kWgConvCo = 1, kWgConvTap = 2 };
+enum WgMode { kWgLinear = 0, kWgConvCo = 1, kWgConvTap = 2, kWgLinearN128 = 3 };
+// kWgLinearN128: kWgLinear for CTAs that take half of N = 256 (n_tiles = 2): two
+// B boxes per stage, so six stages fit in shared memory instead of three
+constexpr bool wg_linear(int mode) { return mode == kWgLinear || mode == kWgLinearN128; }
 
 struct WgradTcParams {
     CUtensorMap a_map, b_map;
@@ -42,12 +45,15 @@ struct WgradTcParams {
     int K_total;          // linear: rows; conv: images
     int splits;           // CTAs along K
     int m_tiles;          // linear: M/128; conv-co: tap groups (3)
+    int n_tiles;          // linear: 1 (N = 256 per CTA) or 2 (two CTAs of N = 128); else 1
     int M, N;             // logical D (partial row / col extents)
     int H, W, R, tiles_per_img;   // conv geometry (K-stage = R rows of one image)
     int kstage_rows;      // rows (pixels) per K-stage, multiple of 16 after zero padding
     float *partial;       // [splits][M][N]
     const __nv_bfloat16 *dp;   // UP: pooled gradient [B, H/2, W/2, COUT]
     const uint8_t *up_code;    // UP: its pool codes
+    float *out;           // linear, one K split: the final gradient, rows in the layout below
+    int oC, oHW;          // linear: row m = hw * oC + c of the NHWC flatten goes to c * oHW + hw
     int *err;
 };
 
@@ -55,10 +61,10 @@ template <int MODE>
 struct WgradTcShape {
     // stage = A box slots + B box slots; a slot holds kpad = round16(kstage_rows)
     // k rows (the rows past kstage_rows stay zero)
-    static constexpr int A_BOXES = MODE == kWgLinear ? 2 : MODE == kWgConvCo ? 2 : 12;
+    static constexpr int A_BOXES = wg_linear(MODE) ? 2 : MODE == kWgConvCo ? 2 : 12;
     static constexpr int A_ROWB = MODE == kWgConvTap ? 64 : 128;
-    static constexpr int B_BOXES = MODE == kWgLinear ? 4 : MODE == kWgConvCo ? 3 : 1;
-    static constexpr int NS = MODE == kWgLinear ? 3 : 2;
+    static constexpr int B_BOXES = MODE == kWgLinear ? 4 : MODE == kWgLinearN128 ? 2 : MODE == kWgConvCo ? 3 : 1;
+    static constexpr int NS = MODE == kWgLinear ? 3 : MODE == kWgLinearN128 ? 6 : 2;
     static constexpr uint32_t TMEM_COLS = 256;
     static __host__ __device__ int kpad(int kr) { return (kr + 15) / 16 * 16; }
     static __host__ __device__ int abox(int kr) { return kpad(kr) * A_ROWB; }
@@ -96,12 +102,14 @@ __global__ void __launch_bounds__(UP ? 320 : 192, 1) wgrad_tc_kernel(const __gri
 
     // CTA -> (m tile / tap group, K split)
     const int mt = blockIdx.x % p.m_tiles;
-    const int split = blockIdx.x / p.m_tiles;
+    const int nt = wg_linear(MODE) ? (blockIdx.x / p.m_tiles) % p.n_tiles : 0;
+    const int split = wg_linear(MODE) ? blockIdx.x / (p.m_tiles * p.n_tiles) : blockIdx.x / p.m_tiles;
+    const int nb = wg_linear(MODE) ? 4 / p.n_tiles : 0;   // linear: 64-column B boxes per stage (<= B_BOXES)
     // K slices: linear splits whole 64-row stages, conv splits whole images
-    const int kunits = MODE == kWgLinear ? (p.K_total + 63) / 64 : p.K_total;
+    const int kunits = wg_linear(MODE) ? (p.K_total + 63) / 64 : p.K_total;
     const int k0 = (int)((long long)kunits * split / p.splits);
     const int k1 = (int)((long long)kunits * (split + 1) / p.splits);
-    const int nstages = MODE == kWgLinear ? (k1 - k0) : (k1 - k0) * p.tiles_per_img;
+    const int nstages = wg_linear(MODE) ? (k1 - k0) : (k1 - k0) * p.tiles_per_img;
 
     // zero the never-written tails of every box slot once (k rows kr..127)
     for (int i = threadIdx.x; i < S::NS * STAGE / 16; i += blockDim.x) {
@@ -141,11 +149,11 @@ __global__ void __launch_bounds__(UP ? 320 : 192, 1) wgrad_tc_kernel(const __gri
                 uint8_t *sa = sbase + s * STAGE;
                 uint8_t *sb = sa + S::A_BOXES * ABOX;
                 armed[s] = (int)ph + 1;
-                if constexpr (MODE == kWgLinear) {
+                if constexpr (wg_linear(MODE)) {
                     const int r0 = (k0 + st) * 64;
-                    mbar_arrive_expect_tx(&full[s], 2 * abox_bytes + 4 * bbox_bytes);
+                    mbar_arrive_expect_tx(&full[s], 2 * abox_bytes + nb * bbox_bytes);
                     for (int j = 0; j < 2; ++j) tma_load_2d(sa + j * ABOX, &p.a_map, &full[s], mt * 128 + j * 64, r0);
-                    for (int j = 0; j < 4; ++j) tma_load_2d(sb + j * BBOX, &p.b_map, &full[s], j * 64, r0);
+                    for (int j = 0; j < nb; ++j) tma_load_2d(sb + j * BBOX, &p.b_map, &full[s], (nt * nb + j) * 64, r0);
                 } else {
                     const int img = k0 + st / p.tiles_per_img;
                     const int h0 = (st % p.tiles_per_img) * p.R;
@@ -184,11 +192,11 @@ __global__ void __launch_bounds__(UP ? 320 : 192, 1) wgrad_tc_kernel(const __gri
                 const uint32_t a0 = s0 + s * STAGE, b0 = a0 + S::A_BOXES * ABOX;
                 for (int kk = 0; kk < kr16; ++kk) {
                     const bool accum = (st | kk) != 0;
-                    if constexpr (MODE == kWgLinear) {
-                        // A: 2 MN blocks of 64 at ABOX; B: 4 MN blocks of 64 at BBOX
+                    if constexpr (wg_linear(MODE)) {
+                        // A: 2 MN blocks of 64 at ABOX; B: nb MN blocks of 64 at BBOX
                         const uint64_t ad = smem_desc(a0 + kk * 2048, ABOX, 1024, kSw128);
                         const uint64_t bd = smem_desc(b0 + kk * 2048, BBOX, 1024, kSw128);
-                        mma_bf16(tmem_base, ad, bd, idesc_bf16(128, 256, true, true), accum);
+                        mma_bf16(tmem_base, ad, bd, idesc_bf16(128, 64 * nb, true, true), accum);
                     } else if constexpr (MODE == kWgConvCo) {
                         const uint64_t ad = smem_desc(a0 + kk * 2048, ABOX, 1024, kSw128);
                         const uint64_t bd = smem_desc(b0 + kk * 2048, BBOX, 1024, kSw128);
@@ -281,13 +289,18 @@ __global__ void __launch_bounds__(UP ? 320 : 192, 1) wgrad_tc_kernel(const __gri
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16);
             float *part = p.partial + (size_t)split * p.M * p.N;
             const bool empty_slice = nstages == 0;
-            if constexpr (MODE == kWgLinear) {
+            if constexpr (wg_linear(MODE)) {
                 const int m = mt * 128 + row;
+                // one K split: straight into the gradient (the NHWC flatten's row m is
+                // the NCHW row c * oHW + hw); else this split's partial
+                float *dst = p.out ? p.out + ((size_t)(m % p.oC) * p.oHW + m / p.oC) * p.N
+                                   : part + (size_t)m * p.N;
+                dst += nt * 64 * nb;
 #pragma unroll 1
-                for (int cc = 0; cc < 8; ++cc) {
+                for (int cc = 0; cc < 2 * nb; ++cc) {
                     float v[32];
                     tmem_ld32(taddr + 32 * cc, v);
-                    if (m < p.M) store_row32(part + (size_t)m * p.N + 32 * cc, v, empty_slice);
+                    if (m < p.M) store_row32(dst + 32 * cc, v, empty_slice);
                 }
             } else if constexpr (MODE == kWgConvCo) {
 #pragma unroll 1

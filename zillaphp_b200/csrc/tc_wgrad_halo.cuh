@@ -139,6 +139,7 @@ __global__ void __launch_bounds__(192, 1) wgrad_halo_kernel(const __grid_constan
             const uint64_t adesc0 = smem_desc(smem_u32(base), 128, (uint32_t)p.dy_region, kSwNone);
             const uint64_t bdesc0 = smem_desc(smem_u32(base) + (uint32_t)DYB, 128, (uint32_t)p.x_region, kSwNone);
             const uint32_t xr16 = (uint32_t)p.x_region >> 4;
+            const int t_first = n0 / CIN, t_last = min(8, (n0 + S::NG - 1) / CIN);   // taps with columns here
             for (int t = 0; t < ntiles; ++t) {
                 if (!mbar_wait(&full[s], ph, abort_flag, p.err, kErrFullWait)) break;
                 tc_fence_after();
@@ -156,7 +157,13 @@ __global__ void __launch_bounds__(192, 1) wgrad_halo_kernel(const __grid_constan
                         const uint64_t bd = b_st + (uint64_t)(((lo - tap * CIN) / 8) * xr16) +
                                             (uint64_t)(dh * p.Wp + dw + 16 * k);
                         const uint32_t idesc = idesc_bf16(S::MP, hi - lo, true, true);
-                        mma_bf16(tmem_base + (uint32_t)(lo - n0), ad, bd, idesc, (t | k) != 0);
+                        const uint32_t dt = tmem_base + (uint32_t)(lo - n0);
+                        // the taps of this CTA's columns share A (dY): it stays in the
+                        // collector buffer from the first MMA to the last
+                        if (t_first == t_last) mma_bf16(dt, ad, bd, idesc, (t | k) != 0);
+                        else if (tap == t_first) mma_bf16_ca<0>(dt, ad, bd, idesc, (t | k) != 0);
+                        else if (tap == t_last) mma_bf16_ca<2>(dt, ad, bd, idesc, (t | k) != 0);
+                        else mma_bf16_ca<1>(dt, ad, bd, idesc, (t | k) != 0);
                     }
                 }
                 issued = true;

@@ -21,6 +21,7 @@
 
 #include "conv_pool_f32.cuh"
 #include "net.cuh"
+#include "tc_attn_tf32.cuh"
 #include "tc_gemm_tf32.cuh"
 
 namespace zb {
@@ -74,6 +75,10 @@ struct LmEngine {
     // step first copies the blocks' weights and biases into a shadow with every tensor aligned.
     float *tc_shadow = nullptr;
     std::vector<long long> shadow_src, shadow_dst, shadow_len;
+    // attention on TF32 tensor cores (precision 1, head dim 32, sequence <= 128): per block
+    // the forward and backward problems and the score rows' max and exp-sum [B*H][T][2]
+    std::vector<tc::AttnTcParams> attn_f, attn_b;
+    std::vector<float *> attn_stats;
     std::vector<void *> allocs;
 };
 constexpr int kLmTcPerBlock = 12;
@@ -970,6 +975,44 @@ int lm_tc_build(Net &n, LmEngine &e) {
     if ((rc = lalloc(e, &e.tc_partial, part))) return rc;
     for (auto &t : e.tcg)
         if (t.kind == 3) t.p.partial = e.tc_partial;
+    // attention: one (sequence, head) per CTA when a sequence fits one 128-row tile
+    e.attn_f.clear(); e.attn_b.clear(); e.attn_stats.clear();
+    if (e.D / e.H == 32 && e.D % e.H == 0 && e.Ts <= 128) {
+        static bool attr = false;
+        if (!attr) {
+            if (cudaFuncSetAttribute(tc::attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     tc::kAttnFwdSmem) != cudaSuccess ||
+                cudaFuncSetAttribute(tc::attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     tc::kAttnBwdSmem) != cudaSuccess)
+                return check_cuda("lm: attention smem attribute");
+            attr = true;
+        }
+        const uint32_t box[2] = {32, 128};
+        const uint64_t dq[2] = {(uint64_t)3 * D, (uint64_t)N}, sq[1] = {(uint64_t)3 * D * 4};
+        const uint64_t dd[2] = {(uint64_t)D, (uint64_t)N}, sd[1] = {(uint64_t)D * 4};
+        for (int l = 0; l < L; ++l) {
+            float *st = nullptr;
+            if ((rc = lalloc(e, &st, (size_t)e.Bs * e.H * e.Ts * 2))) return rc;
+            tc::AttnTcParams a{};
+            if ((rc = tc::make_tmap_f32(&a.qkv_k, e.qkv[l], 2, dq, sq, box, tc::kSw128)) ||
+                (rc = tc::make_tmap_f32(&a.qkv_mn, e.qkv[l], 2, dq, sq, box, tc::kSw128B32)) ||
+                (rc = tc::make_tmap_f32(&a.do_k, e.datt, 2, dd, sd, box, tc::kSw128)) ||
+                (rc = tc::make_tmap_f32(&a.do_mn, e.datt, 2, dd, sd, box, tc::kSw128B32)))
+                return rc;
+            a.T = e.Ts; a.H = e.H; a.D = D;
+            a.scale = 1.0f / sqrtf((float)(D / e.H));
+            a.stats = st;
+            a.err = device_error_word();
+            tc::AttnTcParams f = a, bw = a;
+            f.out = e.att[l];
+            bw.O = e.att[l];
+            bw.dO = e.datt;
+            bw.out = e.dqkv;
+            e.attn_f.push_back(f);
+            e.attn_b.push_back(bw);
+            e.attn_stats.push_back(st);
+        }
+    }
     return kOk;
 }
 
@@ -1038,8 +1081,11 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
                    e.qkv[l], N, 3 * D, D, D, 3 * D, D, false};
         if ((rc = tcp ? lm_tc_run(e, tg[0]) : run_simt_gemm(qkv, 1, "lm qkv"))) return rc;
         prof_mark(n, "ln1_qkv");
-        attn_fwd_kernel<32><<<dim3(e.Bs * e.H, (e.Ts + 31) / 32), 128, attn_smem_fwd(e.Ts, 32), stream()>>>(
-            e.qkv[l], e.P[l], e.att[l], e.Ts, e.H, D, scale);
+        if (tcp && !e.attn_f.empty())
+            tc::attn_fwd_tc_kernel<<<e.Bs * e.H, 512, tc::kAttnFwdSmem, stream()>>>(e.attn_f[l]);
+        else
+            attn_fwd_kernel<32><<<dim3(e.Bs * e.H, (e.Ts + 31) / 32), 128, attn_smem_fwd(e.Ts, 32), stream()>>>(
+                e.qkv[l], e.P[l], e.att[l], e.Ts, e.H, D, scale);
         ZB_LAUNCH_CHECK("lm attention");
         prof_mark(n, "attn_fwd");
         LinFwd o{e.att[l], e.x[l], {Pm + b.oW, nullptr, nullptr}, {Pm + b.ob, nullptr, nullptr}, e.xm[l],
@@ -1092,8 +1138,11 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
         if ((rc = colsum(e, e.gm, N, D, D, G + b.ob))) return rc;
         LinDgrad dout{e.gm, nullptr, {Pm + b.oW, nullptr, nullptr}, e.datt, N, D, D, D, D, D};
         if ((rc = tcp ? lm_tc_run(e, tg[6]) : run_simt_gemm(dout, 1, "lm out dX"))) return rc;
-        attn_bwd_kernel<32><<<e.Bs * e.H, 256, attn_smem_bwd(e.Ts, 32), stream()>>>(e.qkv[l], e.P[l], e.datt,
-                                                                                  e.att[l], e.dqkv, e.Ts, e.H, D, scale);
+        if (tcp && !e.attn_b.empty())
+            tc::attn_bwd_tc_kernel<<<e.Bs * e.H, 512, tc::kAttnBwdSmem, stream()>>>(e.attn_b[l]);
+        else
+            attn_bwd_kernel<32><<<e.Bs * e.H, 256, attn_smem_bwd(e.Ts, 32), stream()>>>(e.qkv[l], e.P[l], e.datt,
+                                                                                      e.att[l], e.dqkv, e.Ts, e.H, D, scale);
         ZB_LAUNCH_CHECK("lm attention backward");
         prof_mark(n, "oproj_attn_bwd");
         LinWgrad wq{e.h1[l], e.dqkv, {G + b.qW, G + b.kW, G + b.vW}, D, 3 * D, N, D, 3 * D, D};

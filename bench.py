@@ -335,7 +335,7 @@ def lm_work(w: configs.LmWorkload, batch: int) -> list[dict]:
                  "name": f"block{l} out-proj+attention bwd"},
                 {"label": "qkv_ln1_bwd", "flops": 4 * N * D * 3 * D, "bytes": 4 * N * 8 * D,
                  "name": f"block{l} qkv+ln1 bwd"}]
-    out += [{"label": "embed_bwd", "flops": 0, "bytes": 4 * (N * (D + 1) + (V + w.max_seq) * D), "name": "embedding bwd"},
+    out += [{"label": "embed_bwd", "flops": 0, "bytes": 4 * (N * (D + 1) + (V + w.max_seq) * D), "name": "embedding bwd + the step's split sums"},
             {"label": "adam", "flops": 0, "bytes": 28 * configs.lm_param_count(w), "name": "optimizer"}]
     return out
 

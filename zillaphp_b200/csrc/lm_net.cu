@@ -43,6 +43,26 @@ struct LmTcGemm {
 int launch_softmax_ce(const float *z, const float *y, float *dz, double *row_loss, float *loss,
                       int B, int C, bool zero_first);
 
+// The step's split sums, deferred: every weight-gradient K split (tensor-core path), bias
+// column sum, LayerNorm parameter sum and embedding sum of the backward is queued as a job,
+// and the jobs run together in one launch at the end of the step, before the optimizer reads
+// the gradients.  Job: element i = m * N + n (i < M * N) is the sum over k < splits of
+// partial[k * stride + i], in a fixed order, stored to o[n / sw][m * sw + n % sw]; elements
+// i >= nvalid are stored as zero.
+constexpr int kMaxLmRed = 40;
+struct LmRedJob {
+    const float *partial;
+    long long stride, nvalid;
+    int splits, M, N, sw;
+    int vec;   // 16-byte loads: M * N, stride and nvalid multiples of 4, partial 16-byte aligned, sw % 4 == 0
+    float *o[3];
+};
+struct LmRedJobs {
+    LmRedJob j[kMaxLmRed];
+    int start[kMaxLmRed + 1];
+    int count;
+};
+
 struct LmEngine {
     int V = 0, D = 0, H = 0, L = 0, T = 0, F = 0, Bs = 0, Ts = 0, N = 0;
     long long o_tok = 0, o_pos = 0, o_lnf_g = 0, o_lnf_b = 0, o_head_W = 0, o_head_b = 0;
@@ -55,8 +75,6 @@ struct LmEngine {
     float *hf = nullptr, *xhf = nullptr, *invf = nullptr, *logits = nullptr;
     // gradients
     float *g = nullptr, *gm = nullptr, *dh = nullptr, *df1 = nullptr, *datt = nullptr, *dqkv = nullptr;
-    float *ln_partial = nullptr;   // [ln_blocks][2D]
-    float *colsum_partial = nullptr;   // [kColsumChunks][widest gradient row]
     float *emb_partial = nullptr;  // [row chunks][V][D]
     int ln_blocks = 0;
     // generation (TransformerLM::forwardWithCache): per-layer K/V caches
@@ -79,6 +97,11 @@ struct LmEngine {
     // the forward and backward problems and the score rows' max and exp-sum [B*H][T][2]
     std::vector<tc::AttnTcParams> attn_f, attn_b;
     std::vector<float *> attn_stats;
+    // deferred split sums: the queue of this step and the scratch of the column-sum and
+    // LayerNorm partials (a fresh region per call, reset every step)
+    std::vector<LmRedJob> red;
+    float *red_arena = nullptr;
+    size_t red_cap = 0, red_used = 0;
     std::vector<void *> allocs;
 };
 constexpr int kLmTcPerBlock = 12;
@@ -234,33 +257,9 @@ __global__ void ln_bwd_kernel(const float *__restrict__ gout, const float *__res
     }
 }
 
-// Sum of per-block partials [blocks][2D] into gamma / beta gradients.
-// out[j] = sum_b partial[b * n + j] for j < n, b < blocks, in a fixed order: a block takes 8
-// columns x 32 split lanes (lane l adds b = l, l + 32, ...), then the 32 lane sums of each
-// column are added in lane order.  Columns j < n0 go to o0[j], the rest to o1[j - n0]
-// (LayerNorm: dgamma | dbeta).
-__global__ void __launch_bounds__(256) sum_partials_kernel(const float *__restrict__ partial, int blocks, int n,
-                                                           int n0, float *__restrict__ o0, float *__restrict__ o1) {
-    __shared__ float red[32][9];
-    const int el = threadIdx.x & 7, sl = threadIdx.x >> 3;
-    const int j = blockIdx.x * 8 + el;
-    float s = 0.0f;
-    if (j < n)
-        for (int b = sl; b < blocks; b += 32) s += partial[(size_t)b * n + j];
-    red[sl][el] = s;
-    __syncthreads();
-    if (sl == 0 && j < n) {
-        float t = red[0][el];
-#pragma unroll
-        for (int l = 1; l < 32; ++l) t += red[l][el];
-        if (j < n0) o0[j] = t;
-        else o1[j - n0] = t;
-    }
-}
-
 // Column sums over rows with a row stride, first stage: block (column tile, row chunk)
 // sums rows [r0, r1) of 32 columns (8 row lanes, combined in order) into
-// part[chunk][col]; sum_cols_kernel adds the chunks in order.
+// part[chunk][col]; the step's deferred sums add the chunks in order.
 __global__ void colsum_part_kernel(const float *__restrict__ dY, int rows, int ld, int chunks,
                                    float *__restrict__ part) {
     __shared__ float red[8][33];
@@ -279,26 +278,6 @@ __global__ void colsum_part_kernel(const float *__restrict__ dY, int rows, int l
     }
 }
 
-// Second stage: out_s[c] = sum over chunks of part[chunk][s * sw + c], chunks in order.
-__global__ void sum_cols_kernel(const float *__restrict__ part, int chunks, int ld, int sw, float *o0, float *o1,
-                                float *o2) {
-    __shared__ float red[32][9];
-    const int el = threadIdx.x & 7, sl = threadIdx.x >> 3;
-    const int col = blockIdx.x * 8 + el;
-    float s = 0.0f;
-    if (col < ld)
-        for (int b = sl; b < chunks; b += 32) s += part[(size_t)b * ld + col];
-    red[sl][el] = s;
-    __syncthreads();
-    if (sl == 0 && col < ld) {
-        float t = red[0][el];
-#pragma unroll
-        for (int l = 1; l < 32; ++l) t += red[l][el];
-        const int seg = col / sw, c = col - seg * sw;
-        float *o = seg == 0 ? o0 : seg == 1 ? o1 : o2;
-        o[c] = t;
-    }
-}
 
 // Causal attention forward for one (sequence, head, block of 32 query rows),
 // head dim DH: S = q k^T * scale with -1e9 on future keys, P = row softmax
@@ -624,7 +603,9 @@ __global__ void __launch_bounds__(256) attn_bwd_kernel(const float *__restrict__
 
 // Embedding backward (the one-hot matmul's gradient, src/NN/Layers/Embedding.php:35-56),
 // in two fixed-order passes.  Pass 1: for each chunk of kEmbChunk rows,
-// part[chunk][v][d] = sum over the chunk's rows with token v of g[row][d].
+// part[chunk][v][d] = sum over the chunk's rows with token v of g[row][d].  Pass 2 (with
+// the step's deferred sums): dTok[v][d] = the chunk partials in chunk order, dPos[t][d] =
+// sum over sequences of g[b*T + t][d] (positions past the sequence length: zero).
 constexpr int kEmbChunk = 256;
 
 __global__ void __launch_bounds__(256) embed_tok_partial_kernel(const float *__restrict__ g,
@@ -644,24 +625,65 @@ __global__ void __launch_bounds__(256) embed_tok_partial_kernel(const float *__r
     part[((size_t)blockIdx.y * V + v) * D + d] = s;
 }
 
-// Pass 2: dTok[v][d] = sum of the chunk partials in chunk order; dPos[t][d] =
-// sum over sequences of g[b*T + t][d] (positions >= T are unused: zero).
-__global__ void embed_bwd_kernel(const float *__restrict__ g, const float *__restrict__ part,
-                                 float *__restrict__ dtok, float *__restrict__ dpos, int N, int Ts, int D, int V,
-                                 int Tmax, int chunks) {
-    const int Bs = N / Ts;
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (long long)(V + Tmax) * D;
-         i += (long long)gridDim.x * blockDim.x) {
-        const int row = (int)(i / D), d = (int)(i % D);
-        float s = 0.0f;
-        if (row < V) {
-            for (int c = 0; c < chunks; ++c) s += part[((size_t)c * V + row) * D + d];
-            dtok[(size_t)row * D + d] = s;
+// All queued split sums of a step in one launch: blocks [start[j], start[j+1]) take job j,
+// 128 elements per block (vec: 32 lanes x 4 consecutive elements, one 16-byte load per split)
+// or 32 (one element per lane); warp w adds splits w, w + 8, ... in order, then the eight warp
+// sums of each element are added in warp order (fixed order: deterministic).
+__global__ void __launch_bounds__(256) lm_reduce_all_kernel(const __grid_constant__ LmRedJobs J) {
+    int j = 0;
+    while (j + 1 < J.count && (int)blockIdx.x >= J.start[j + 1]) ++j;
+    const LmRedJob &r = J.j[j];
+    const int bx = (int)blockIdx.x - J.start[j];
+    __shared__ float4 part[8][32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const long long total = (long long)r.M * r.N;
+    const int per = r.vec ? 4 : 1;
+    const long long i = ((long long)bx * 32 + lane) * per;   // first element of this lane
+    float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (i < total && i < r.nvalid) {
+        if (r.vec) {
+            const float4 *p = reinterpret_cast<const float4 *>(r.partial + i);
+            const long long st4 = r.stride >> 2;
+            int k = w;
+            for (; k + 24 < r.splits; k += 32) {
+                const float4 a = __ldcg(p + (size_t)k * st4), b = __ldcg(p + (size_t)(k + 8) * st4);
+                const float4 c = __ldcg(p + (size_t)(k + 16) * st4), d = __ldcg(p + (size_t)(k + 24) * st4);
+                s.x += a.x; s.y += a.y; s.z += a.z; s.w += a.w;
+                s.x += b.x; s.y += b.y; s.z += b.z; s.w += b.w;
+                s.x += c.x; s.y += c.y; s.z += c.z; s.w += c.w;
+                s.x += d.x; s.y += d.y; s.z += d.z; s.w += d.w;
+            }
+            for (; k < r.splits; k += 8) {
+                const float4 a = __ldcg(p + (size_t)k * st4);
+                s.x += a.x; s.y += a.y; s.z += a.z; s.w += a.w;
+            }
         } else {
-            const int t = row - V;
-            if (t < Ts)
-                for (int bq = 0; bq < Bs; ++bq) s += g[((size_t)bq * Ts + t) * D + d];
-            dpos[(size_t)t * D + d] = s;   // positions >= T were not used: zero
+            const float *p = r.partial + i;
+            int k = w;
+            for (; k + 8 < r.splits; k += 16) {
+                const float a = __ldcg(p + (size_t)k * r.stride), b = __ldcg(p + (size_t)(k + 8) * r.stride);
+                s.x += a;
+                s.x += b;
+            }
+            if (k < r.splits) s.x += __ldcg(p + (size_t)k * r.stride);
+        }
+    }
+    part[w][lane] = s;
+    __syncthreads();
+    if (w == 0) {
+        float4 t = part[0][lane];
+#pragma unroll
+        for (int l = 1; l < 8; ++l) {
+            const float4 u = part[l][lane];
+            t.x += u.x; t.y += u.y; t.z += u.z; t.w += u.w;
+        }
+        const float v[4] = {t.x, t.y, t.z, t.w};
+        for (int e = 0; e < per; ++e) {
+            const long long ie = i + e;
+            if (ie >= total) break;
+            const int m = (int)(ie / r.N), n = (int)(ie % r.N), seg = n / r.sw;
+            float *o = seg == 0 ? r.o[0] : seg == 1 ? r.o[1] : r.o[2];
+            o[(size_t)m * r.sw + (n - seg * r.sw)] = ie < r.nvalid ? v[e] : 0.0f;
         }
     }
 }
@@ -682,30 +704,80 @@ int ln_fwd(const float *x, const float *g, const float *b, float *y, float *xh, 
     return kOk;
 }
 
+int red_push(LmEngine &e, const float *partial, long long stride, int splits, int M, int N, int sw, long long nvalid,
+             float *o0, float *o1, float *o2);
+float *red_take(LmEngine &e, size_t n);
+
+// LayerNorm backward; its dgamma | dbeta block partials join the step's deferred sums.
 int ln_bwd(LmEngine &e, const float *gout, const float *xh, const float *inv, const float *gam, const float *R,
            float *out, float *dg, float *db) {
     const int warps = 8;
+    float *part = red_take(e, (size_t)e.ln_blocks * 2 * e.D);
+    if (!part) return fail(kBadArg, "lm: split-sum scratch exhausted");
     ln_bwd_kernel<<<e.ln_blocks, warps * 32, (size_t)warps * 2 * e.D * sizeof(float), stream()>>>(
-        gout, xh, inv, gam, R, out, e.ln_partial, e.N, e.D);
+        gout, xh, inv, gam, R, out, part, e.N, e.D);
     ZB_LAUNCH_CHECK("lm layernorm backward");
-    sum_partials_kernel<<<(2 * e.D + 7) / 8, 256, 0, stream()>>>(e.ln_partial, e.ln_blocks, 2 * e.D, e.D, dg, db);
-    ZB_LAUNCH_CHECK("lm layernorm partials");
-    return kOk;
+    return red_push(e, part, 2 * e.D, e.ln_blocks, 1, 2 * e.D, e.D, 2 * e.D, dg, db, nullptr);
 }
 
 // Bias gradients: column sums of dY [rows][ld] in two fixed-order stages (row chunks over
-// about two blocks per SM, then the chunks in order), into segments of sw columns.
+// about two blocks per SM now, the chunks in order with the step's deferred sums), into
+// segments of sw columns.
 int colsum(LmEngine &e, const float *dY, int rows, int ld, int sw, float *o0, float *o1 = nullptr, float *o2 = nullptr) {
     const int tiles = (ld + 31) / 32;
     int chunks = sm_count() * 2 / tiles;
     if (chunks > rows / 32) chunks = rows / 32;
     if (chunks > kColsumChunks) chunks = kColsumChunks;
     if (chunks < 1) chunks = 1;
-    colsum_part_kernel<<<dim3(tiles, chunks), dim3(32, 8), 0, stream()>>>(dY, rows, ld, chunks, e.colsum_partial);
+    float *part = red_take(e, (size_t)chunks * ld);
+    if (!part) return fail(kBadArg, "lm: split-sum scratch exhausted");
+    colsum_part_kernel<<<dim3(tiles, chunks), dim3(32, 8), 0, stream()>>>(dY, rows, ld, chunks, part);
     ZB_LAUNCH_CHECK("lm column sums (chunks)");
-    sum_cols_kernel<<<(ld + 7) / 8, 256, 0, stream()>>>(e.colsum_partial, chunks, ld, sw, o0, o1, o2);
-    ZB_LAUNCH_CHECK("lm column sums");
+    return red_push(e, part, ld, chunks, 1, ld, sw, ld, o0, o1, o2);   // the chunks in order, deferred
+}
+
+// Runs every queued split sum (one launch) and empties the queue.
+int red_flush(LmEngine &e) {
+    if (e.red.empty()) return kOk;
+    LmRedJobs J{};
+    J.count = (int)e.red.size();
+    int total = 0;
+    for (int j = 0; j < J.count; ++j) {
+        J.j[j] = e.red[j];
+        J.start[j] = total;
+        const long long el = (long long)e.red[j].M * e.red[j].N;
+        total += (int)((el + (e.red[j].vec ? 128 : 32) - 1) / (e.red[j].vec ? 128 : 32));
+    }
+    J.start[J.count] = total;
+    e.red.clear();
+    lm_reduce_all_kernel<<<total, 256, 0, stream()>>>(J);
+    ZB_LAUNCH_CHECK("lm split sums");
     return kOk;
+}
+
+int red_push(LmEngine &e, const float *partial, long long stride, int splits, int M, int N, int sw, long long nvalid,
+             float *o0, float *o1 = nullptr, float *o2 = nullptr) {
+    if ((int)e.red.size() == kMaxLmRed) {
+        int rc = red_flush(e);
+        if (rc) return rc;
+    }
+    LmRedJob j{};
+    j.partial = partial; j.stride = stride; j.nvalid = nvalid;
+    j.splits = splits; j.M = M; j.N = N; j.sw = sw;
+    j.vec = ((long long)M * N) % 4 == 0 && stride % 4 == 0 && nvalid % 4 == 0 && sw % 4 == 0 && N % 4 == 0 &&
+            (reinterpret_cast<uintptr_t>(partial) & 15) == 0;
+    j.o[0] = o0; j.o[1] = o1; j.o[2] = o2;
+    e.red.push_back(j);
+    return kOk;
+}
+
+// A fresh 16-byte-aligned scratch region of n floats for this step's partials.
+float *red_take(LmEngine &e, size_t n) {
+    const size_t n4 = (n + 3) / 4 * 4;
+    if (e.red_used + n4 > e.red_cap) return nullptr;
+    float *p = e.red_arena + e.red_used;
+    e.red_used += n4;
+    return p;
 }
 
 int lm_build(Net &n, LmEngine &e) {
@@ -751,30 +823,16 @@ int lm_build(Net &n, LmEngine &e) {
         (rc = lalloc(e, &e.dqkv, 3 * ND)))
         return rc;
     e.ln_blocks = sm_count() * 2;
-    if ((rc = lalloc(e, &e.ln_partial, (size_t)e.ln_blocks * 2 * D))) return rc;
     if ((rc = lalloc(e, &e.emb_partial, (size_t)((N + kEmbChunk - 1) / kEmbChunk) * V * D))) return rc;
+    // per step: 4 column sums per block and the head's, 2 LayerNorms per block and the final one
     const int widest = 3 * D > F ? (3 * D > V ? 3 * D : V) : (F > V ? F : V);
-    if ((rc = lalloc(e, &e.colsum_partial, (size_t)kColsumChunks * widest))) return rc;
+    e.red_cap = (size_t)(4 * L + 1) * ((size_t)kColsumChunks * widest + 4) +
+                (size_t)(2 * L + 1) * ((size_t)e.ln_blocks * 2 * D + 4);
+    if ((rc = lalloc(e, &e.red_arena, e.red_cap))) return rc;
     return kOk;
 }
 
 // ---------------------------------------------------------------- tensor-core GEMMs (precision 1)
-// Sum of the K-split partials [splits][M][N] in split order, scattered into
-// the weight-gradient segments dst[n / seg_w] (row-major [M][seg_w]).
-__global__ void __launch_bounds__(256) lm_tc_reduce_kernel(const float *__restrict__ partial, int splits, int M, int N,
-                                                           float *d0, float *d1, float *d2, int seg_w) {
-    griddep_launch();
-    griddep_wait();
-    const long long MN = (long long)M * N;
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < MN; i += (long long)gridDim.x * blockDim.x) {
-        float s = 0.0f;
-        for (int k = 0; k < splits; ++k) s += __ldcg(partial + (size_t)k * MN + i);
-        const int m = (int)(i / N), n = (int)(i % N), seg = n / seg_w;
-        float *d = seg == 0 ? d0 : seg == 1 ? d1 : d2;
-        d[(size_t)m * seg_w + (n - seg * seg_w)] = s;
-    }
-}
-
 template <bool AMN, bool BMN, int EPI>
 int launch_tf32(const tc::GemmTf32Params &p, int grid) {
     constexpr int BN = 128, NS = 4;
@@ -791,18 +849,16 @@ int launch_tf32(const tc::GemmTf32Params &p, int grid) {
     return kOk;
 }
 
-int lm_tc_run(const LmEngine &e, const LmTcGemm &g) {
+int lm_tc_run(LmEngine &e, const LmTcGemm &g) {
     switch (g.kind) {
     case 0: return launch_tf32<false, true, tc::kTfStore>(g.p, g.grid);
     case 1: return launch_tf32<false, false, tc::kTfStore>(g.p, g.grid);
     case 2: return launch_tf32<false, false, tc::kTfMask>(g.p, g.grid);
-    default: {
+    default: {   // the K splits' partials (this GEMM's own region) join the step's deferred sums
         int rc = launch_tf32<true, true, tc::kTfPartial>(g.p, g.grid);
         if (rc) return rc;
-        launch_pdl(lm_tc_reduce_kernel, dim3(grid_for((long long)g.p.M * g.p.N, 256, 4)), dim3(256), 0,
-                   (const float *)e.tc_partial, g.p.ksplit, g.p.M, g.p.N, g.dst[0], g.dst[1], g.dst[2], g.seg_w);
-        ZB_LAUNCH_CHECK("lm tf32 weight-gradient sum");
-        return kOk;
+        return red_push(e, g.p.partial, (long long)g.p.M * g.p.N, g.p.ksplit, g.p.M, g.p.N, g.seg_w,
+                        (long long)g.p.M * g.p.N, g.dst[0], g.dst[1], g.dst[2]);
     }
     }
 }
@@ -934,6 +990,7 @@ int lm_tc_build(Net &n, LmEngine &e) {
     const float *Pm = e.tc_shadow;
     size_t part = 0;
     e.tcg.assign((size_t)L * kLmTcPerBlock, LmTcGemm());
+    std::vector<size_t> part_off(e.tcg.size(), 0);
     for (int l = 0; l < L; ++l) {
         const auto &b = sb[l];        // operands: the shadow copies
         const auto &bg = e.blk[l];    // gradient destinations: the flat layout
@@ -965,16 +1022,15 @@ int lm_tc_build(Net &n, LmEngine &e) {
             LmTcGemm &t = g[j];
             const int tiles = t.p.m_tiles * t.p.n_tiles * t.p.ksplit;
             t.grid = tiles < sm_count() ? tiles : sm_count();
-            if (t.kind == 3) {
-                t.p.partial = nullptr;   // set below, once the scratch exists
-                const size_t need = (size_t)t.p.ksplit * t.p.M * t.p.N;
-                if (need > part) part = need;
+            if (t.kind == 3) {   // its own partial region (summed at the end of the step)
+                part_off[(size_t)l * kLmTcPerBlock + j] = part;
+                part += ((size_t)t.p.ksplit * t.p.M * t.p.N + 3) / 4 * 4;
             }
         }
     }
     if ((rc = lalloc(e, &e.tc_partial, part))) return rc;
-    for (auto &t : e.tcg)
-        if (t.kind == 3) t.p.partial = e.tc_partial;
+    for (size_t k = 0; k < e.tcg.size(); ++k)
+        if (e.tcg[k].kind == 3) e.tcg[k].p.partial = e.tc_partial + part_off[k];
     // attention: one (sequence, head) per CTA when a sequence fits one 128-row tile
     e.attn_f.clear(); e.attn_b.clear(); e.attn_stats.clear();
     if (e.D / e.H == 32 && e.D % e.H == 0 && e.Ts <= 128) {
@@ -1068,6 +1124,8 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
     if (tcp && (G != e.tc_grads || Pm != e.tc_params))
         return fail(kBadArg, "lm: tensor-core plan built over other parameter / gradient buffers");
     if (tcp && (rc = lm_tc_shadow(n, e))) return rc;   // this step's weights, aligned for TMA
+    e.red.clear();       // (a step that failed part-way leaves nothing queued for the next)
+    e.red_used = 0;
     // ---- forward
     embed_fwd_kernel<<<grid_for((long long)N * D, 256, 8), 256, 0, stream()>>>(
         tokens, Pm + e.o_tok, Pm + e.o_pos, e.x[0], N, e.Ts, D, V, device_error_word());
@@ -1157,9 +1215,12 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
     embed_tok_partial_kernel<<<dim3((V * D + 255) / 256, chunks), 256, 0, stream()>>>(e.g, tokens, e.emb_partial,
                                                                                     N, D, V);
     ZB_LAUNCH_CHECK("lm embedding backward (partials)");
-    embed_bwd_kernel<<<grid_for((long long)(V + e.T) * D, 256, 8), 256, 0, stream()>>>(
-        e.g, e.emb_partial, G + e.o_tok, G + e.o_pos, N, e.Ts, D, V, e.T, chunks);
-    ZB_LAUNCH_CHECK("lm embedding backward");
+    // token rows: the chunk partials in order; positions: the sequences' rows in order (positions
+    // past the sequence length get zero)
+    if ((rc = red_push(e, e.emb_partial, (long long)V * D, chunks, 1, V * D, V * D, (long long)V * D, G + e.o_tok)) ||
+        (rc = red_push(e, e.g, (long long)e.Ts * D, N / e.Ts, 1, e.T * D, e.T * D, (long long)e.Ts * D, G + e.o_pos)))
+        return rc;
+    if ((rc = red_flush(e))) return rc;   // every split sum of the step, before the optimizer
     prof_mark(n, "embed_bwd");
     return kOk;
 }

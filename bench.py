@@ -494,37 +494,37 @@ def main():
                             "rel_diff": abs(float(first[0]) - float(full_loss)) / abs(float(full_loss))}
     launches_warm = lib.zilla_launch_count()
     per_step_launches = (launches_warm - launches0) / max(args.warmup, 1)
-    if args.graph:   # every input set runs once plain and once captured before the timed region
-        for s in range(2 * nb):
-            net.step_dev(xs_dev[s % nb], ys_dev[s % nb], loss_id)
 
-    # ---- the step's segments (an untimed profiled pass): the breakdown and the
-    # dominant group, whose two boundaries alone carry events in the timed region
+    # ---- the step's segments (an untimed profiled pass of plain steps, graphs or not): the
+    # breakdown and the dominant group, whose two boundaries alone carry events in the timed
+    # region (graph replay carries no events: the pass's time stands for it then)
     focus_seg, focus_label, breakdown_pass = None, None, []
-    if not args.graph:
-        net.profile(True)
-        for s in range(3):
+    net.profile(True)
+    for s in range(3):
+        net.step_dev(xs_dev[s % nb], ys_dev[s % nb], loss_id)
+    breakdown_pass = net.timings()
+    net.profile(False)
+    if rank == 0:
+        r0, _ = roofline(w, b, breakdown_pass, 3, {}, "", precision)
+        k_dom = r0["group"] if r0 else None
+    else:
+        k_dom = None
+    if world > 1:
+        obj = [k_dom]
+        dist.broadcast_object_list(obj, src=0)
+        k_dom = obj[0]
+    if k_dom is not None and not args.graph:   # index of that group in the unfiltered segment list
+        seen = 0
+        for j, (lab, _) in enumerate(breakdown_pass):
+            if lab == "allreduce":
+                continue
+            if seen == k_dom:
+                focus_seg, focus_label = j, lab
+                break
+            seen += 1
+    if args.graph:   # every input set (and exchange buffer) runs once plain and once captured first
+        for s in range(4 * nb):
             net.step_dev(xs_dev[s % nb], ys_dev[s % nb], loss_id)
-        breakdown_pass = net.timings()
-        net.profile(False)
-        if rank == 0:
-            r0, _ = roofline(w, b, breakdown_pass, 3, {}, "", precision)
-            k_dom = r0["group"] if r0 else None
-        else:
-            k_dom = None
-        if world > 1:
-            obj = [k_dom]
-            dist.broadcast_object_list(obj, src=0)
-            k_dom = obj[0]
-        if k_dom is not None:   # index of that group in the unfiltered segment list of one step
-            seen = 0
-            for j, (lab, _) in enumerate(breakdown_pass):
-                if lab == "allreduce":
-                    continue
-                if seen == k_dom:
-                    focus_seg, focus_label = j, lab
-                    break
-                seen += 1
 
     # ---- device-resident timed region
     if focus_seg is not None:
@@ -595,6 +595,8 @@ def main():
         if roof and focus_seg is not None:
             roof["timing"] = (f"CUDA events at the two boundaries of this group only, every timed step "
                               f"({len(focus_ms)} launches); segments_ms from an untimed profiled pass of 3 steps")
+        elif roof:
+            roof["timing"] = "an untimed profiled pass of 3 plain steps (graph replay carries no events)"
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             r = cpu_reference(w, sample=64, min_seconds=10.0, max_steps=50)

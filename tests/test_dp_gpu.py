@@ -28,7 +28,7 @@ def _gpus() -> int:
         return 0
 
 
-def _rank(rank, world, name, batch, precision, steps, uid_q, out_q):
+def _rank(rank, world, name, batch, precision, steps, uid_q, out_q, graph=False):
     sys.path[:0] = [ROOT, os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")]
     import torch
     torch.cuda.set_device(rank)
@@ -47,6 +47,8 @@ def _rank(rank, world, name, batch, precision, steps, uid_q, out_q):
             else:
                 uid = uid_q.get(timeout=60)
             net.dp_attach(rank, world, uid)
+        if graph:
+            net.set_graph(True)
         losses = []
         for s in range(steps):
             x, y = synthetic.batch(w, batch, seed=21, step=s)
@@ -58,11 +60,11 @@ def _rank(rank, world, name, batch, precision, steps, uid_q, out_q):
         out_q.put((rank, None, None, repr(e)))
 
 
-def _run(world, name, batch, precision, steps):
+def _run(world, name, batch, precision, steps, graph=False):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     uid_q, out_q = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, name, batch, precision, steps, uid_q, out_q))
+    procs = [ctx.Process(target=_rank, args=(r, world, name, batch, precision, steps, uid_q, out_q, graph))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -132,3 +134,18 @@ def test_two_phase_exchange_equals_one_phase():
     assert np.array_equal(two[0][0], two[1][0]), "ranks diverged"
     assert np.array_equal(two[0][0], one[0][0]), "two-phase update differs from one-phase"
     assert two[0][1] == one[0][1], (two[0][1], one[0][1])
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+@pytest.mark.timeout(600)
+def test_peer_step_graphs_equal_plain_steps():
+    """zilla_net_set_graph under data parallelism: each step's kernels, the peer-memory exchange
+    and update among them, are captured per exchange buffer (step parity) and replayed with the
+    step's number and Adam arguments.  Six steps (two plain, two captured, two replayed per
+    parity) leave both ranks bit-identical to the plain run's parameters and losses."""
+    name, batch, steps = "large_cnn", 256, 6
+    plain = _run(2, name, batch, 1, steps)
+    graph = _run(2, name, batch, 1, steps, graph=True)
+    assert np.array_equal(graph[0][0], graph[1][0]), "ranks diverged"
+    assert np.array_equal(graph[0][0], plain[0][0]), "graph replay differs from the plain steps"
+    assert graph[0][1] == plain[0][1], (graph[0][1], plain[0][1])

@@ -454,32 +454,41 @@ void release_graphs(Net &n) {
 // second captures the step on the library stream and launches the graph,
 // later calls only refresh the optimizer's arguments and launch it.
 static int run_step(Net &n, const float *x, const float *y, int update) {
-    if (!n.graph_on || n.world > 1 || n.profile || n.peer.on) return run_step_body(n, x, y, update);
+    // data parallel: only the one-phase peer-memory step is captured (its exchange and update
+    // are two kernels of the step; the NCCL path and the two-phase side stream are not)
+    const bool peer = n.peer.on && update;
+    if (!n.graph_on || n.profile || (n.world > 1 && !(peer && !n.peer.two_phase)))
+        return run_step_body(n, x, y, update);
+    const int parity = peer ? (int)((n.peer.step + 1) & 1) : 0;   // the exchange buffer this step writes
     Net::StepGraph *g = nullptr;
     for (auto &e : n.graphs)
-        if (e.x == x && e.y == y && e.update == update) g = &e;
+        if (e.x == x && e.y == y && e.update == update && e.parity == parity) g = &e;
     if (!g) {
         if (n.graphs.size() >= 16) return run_step_body(n, x, y, update);
         n.graphs.emplace_back();
         g = &n.graphs.back();
-        g->x = x; g->y = y; g->update = update;
+        g->x = x; g->y = y; g->update = update; g->parity = parity;
     }
     if (g->runs++ == 0) return run_step_body(n, x, y, update);
     if (!g->exec) {
         const int t0 = n.t;
+        const unsigned long long s0 = n.peer.step;
         const unsigned long long l0 = zilla_launch_count();
         n.captured_opt = nullptr;
+        n.peer.cap_update = n.peer.cap_wait = nullptr;
         if (cudaStreamBeginCapture(stream(), cudaStreamCaptureModeRelaxed) != cudaSuccess)
             return check_cuda("net: graph capture");
         int rc = run_step_body(n, x, y, update);
         cudaGraph_t graph = nullptr;
         const cudaError_t ce = cudaStreamEndCapture(stream(), &graph);
         cudaGraphExec_t exec = nullptr;
-        if (!rc && ce == cudaSuccess && graph && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess &&
-            (!update || n.captured_opt)) {
+        const bool nodes = !update || (peer ? (n.peer.cap_update && n.peer.cap_wait) : n.captured_opt != nullptr);
+        if (!rc && ce == cudaSuccess && graph && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess && nodes) {
             g->graph = graph;
             g->exec = exec;
-            g->opt_node = update ? n.captured_opt : nullptr;
+            g->opt_node = update && !peer ? n.captured_opt : nullptr;
+            g->upd_node = peer ? n.peer.cap_update : nullptr;
+            g->wait_node = peer ? n.peer.cap_wait : nullptr;
             g->nkern = (unsigned)(zilla_launch_count() - l0);
             if (cudaGraphLaunch(exec, stream()) != cudaSuccess) return check_cuda("net: graph launch");
             return check_cuda("net: graph");
@@ -491,10 +500,15 @@ static int run_step(Net &n, const float *x, const float *y, int update) {
         release_graphs(n);
         n.graph_on = false;
         n.t = t0;
+        n.peer.step = s0;
+        if (n.peer.in_step) n.grads = n.peer.api_grads, n.peer.in_step = false;
         if (rc) return rc;
         return run_step_body(n, x, y, update);
     }
-    if (update) {
+    if (peer) {   // this step's step number and Adam arguments for the exchange and update kernels
+        int rc = peer_graph_args(n, g->exec, g->upd_node, g->wait_node);
+        if (rc) return rc;
+    } else if (update) {
         n.t += 1;
         if (n.opt == 2) {   // this step's Adam arguments (the bias corrections change with t)
             float *w = n.params, *m = n.m, *v = n.v;

@@ -56,6 +56,9 @@ struct PeerState {
     cudaEvent_t ev_mid = nullptr, ev_side = nullptr;
     long long mid_off = -1;                // first parameter of the late layers this step (-1: one phase)
     bool two_phase = false;                // use peer_step_mid (ZB_PEER_TWO_PHASE=1 turns it on)
+    // graph capture of a step: the update and wait kernels' nodes (their step number and Adam
+    // arguments change every replay)
+    cudaGraphNode_t cap_update = nullptr, cap_wait = nullptr;
 };
 
 struct TcEngine;  // bf16 tensor-core engine (tc_net.cu)
@@ -104,6 +107,8 @@ struct Net {
         cudaGraph_t graph = nullptr;          // kept: its optimizer node updates the exec
         cudaGraphExec_t exec = nullptr;
         cudaGraphNode_t opt_node = nullptr;   // the optimizer kernel (Adam's arguments change every step)
+        int parity = 0;                       // peer steps: the exchange buffer (step parity) it was captured on
+        cudaGraphNode_t upd_node = nullptr, wait_node = nullptr;   // peer steps: the update and wait kernels
         unsigned nkern = 0;                   // kernels per replay (launch counter)
     };
     std::vector<StepGraph> graphs;
@@ -157,5 +162,8 @@ int peer_step_end(Net &n);                 // exchange + update + wait for every
 // Gradients [off, nparams] of this step are final: their part of the slice is exchanged and
 // updated on a side stream while the rest of the backward runs; no-op off the peer path.
 int peer_step_mid(Net &n, long long off);
+// A captured peer step replayed: advances the step count and Adam's t as the step
+// would, and gives the graph's update and wait kernels this step's arguments.
+int peer_graph_args(Net &n, cudaGraphExec_t exec, cudaGraphNode_t upd, cudaGraphNode_t wt);
 
 }  // namespace zb

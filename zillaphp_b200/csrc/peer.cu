@@ -233,6 +233,7 @@ PeerArgs make_args(Net &n, unsigned long long step) {
 
 void peer_release(Net &n) {
     PeerState &P = n.peer;
+    release_graphs(n);   // captured steps hold the peers' buffers
     if (P.side_stream) {
         cudaStreamSynchronize(P.side_stream);
         cudaStreamDestroy(P.side_stream);
@@ -255,6 +256,7 @@ int peer_attach(Net &n) {
     const bool want = !(env && env[0] == '0') && n.precision == 1 && !n.lm && n.world > 1 && n.world <= kMaxPeers;
     // every rank takes the same branch: the decision only depends on values equal on all ranks
     if (!want) return kOk;
+    release_graphs(n);   // steps captured before the attach write the registry gradients
     PeerState &P = n.peer;
     P.api_grads = n.grads;
     const size_t gbytes = (size_t)(n.nparams + 1) * sizeof(float);
@@ -377,6 +379,16 @@ int peer_step_begin(Net &n) {
 
 namespace {
 
+// The node of the kernel just launched when the library stream is being captured, else null.
+cudaGraphNode_t captured_node() {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream(), &cs) != cudaSuccess || cs != cudaStreamCaptureStatusActive) return nullptr;
+    const cudaGraphNode_t *deps = nullptr;
+    size_t nd = 0;
+    if (cudaStreamGetCaptureInfo(stream(), &cs, nullptr, nullptr, &deps, &nd) != cudaSuccess || nd != 1) return nullptr;
+    return deps[0];
+}
+
 int update_grid(long long count, int per_sm) {
     const long long n4 = count / 4 + 2;
     long long grid = (n4 + 127) / 128;
@@ -435,8 +447,31 @@ int peer_step_end(Net &n) {
     }
     peer_update_kernel<<<update_grid(A.hi - A.lo, 2), 128, 0, stream()>>>(A);
     ZB_LAUNCH_CHECK("peer update");
+    P.cap_update = captured_node();
     peer_wait_kernel<<<1, 32, 0, stream()>>>(A);
     ZB_LAUNCH_CHECK("peer wait");
+    P.cap_wait = captured_node();
+    return kOk;
+}
+
+int peer_graph_args(Net &n, cudaGraphExec_t exec, cudaGraphNode_t upd, cudaGraphNode_t wt) {
+    PeerState &P = n.peer;
+    if (!P.on || P.two_phase || !upd || !wt) return fail(kBadArg, "peer: no captured one-phase step");
+    P.step += 1;   // as peer_step_begin and peer_step_end would
+    n.t += 1;
+    PeerArgs A = make_args(n, P.step);
+    A.a = make_adam_args(n.lr, n.b1, n.b2, n.eps, n.t, A.scale);
+    A.written = 1;
+    A.slot = kSlotFinalA;
+    A.do_loss = 1;
+    void *args[1] = {&A};
+    for (cudaGraphNode_t node : {upd, wt}) {
+        cudaKernelNodeParams kp{};
+        if (cudaGraphKernelNodeGetParams(node, &kp) != cudaSuccess) return check_cuda("peer: graph node");
+        kp.kernelParams = args;
+        kp.extra = nullptr;
+        if (cudaGraphExecKernelNodeSetParams(exec, node, &kp) != cudaSuccess) return check_cuda("peer: graph arguments");
+    }
     return kOk;
 }
 

@@ -1143,124 +1143,84 @@ __global__ void __launch_bounds__(256) reduce_partials_kernel(ReduceArgs r) {
     }
 }
 
-// Many splits of a short vector (bias and small weight gradients: hundreds of
-// partials of <= 64K floats): block = 8 consecutive elements x 32 split lanes;
-// lane l sums splits l, l+32, ... in order, then the 32 lane sums of each
-// element are added in lane order (fixed order: deterministic).
-__global__ void __launch_bounds__(256) reduce_deep_kernel(ReduceArgs r) {
-    griddep_launch();
-    griddep_wait();
-    __shared__ float part[32][9];
-    const int el = threadIdx.x & 7, sl = threadIdx.x >> 3;
-    for (long long base = (long long)blockIdx.x * 8; base < r.n; base += (long long)gridDim.x * 8) {
-        const long long i = base + el;
-        float s0 = 0.0f, s1 = 0.0f;
-        if (i < r.n) {
-            int k = sl;
-            for (; k + 32 < r.splits; k += 64) {   // two independent chains per lane
-                s0 += r.partial[(size_t)k * r.n + i];
-                s1 += r.partial[(size_t)(k + 32) * r.n + i];
-            }
-            if (k < r.splits) s0 += r.partial[(size_t)k * r.n + i];
-        }
-        part[sl][el] = s0 + s1;
-        __syncthreads();
-        if (sl == 0 && i < r.n) {
-            float s = part[0][el];
-#pragma unroll
-            for (int l = 1; l < 32; ++l) s += part[l][el];
-            r_store(r, i, s);
-        }
-        __syncthreads();
-    }
-}
-
-// Several independent deep reductions in one launch: blocks [start[j],
-// start[j+1]) run job j exactly as reduce_deep_kernel would.
+// Several independent split sums of one phase in one launch: blocks [start[j],
+// start[j+1]) take job j.
 constexpr int kMaxReduceJobs = 6;
 struct ReduceJobs {
     ReduceArgs job[kMaxReduceJobs];
     int start[kMaxReduceJobs + 1];
+    int vec[kMaxReduceJobs];   // reduce_multi4_kernel: 1 = 128 elements per block (16-byte loads), 0 = 32
     int count;
 };
 
-__global__ void __launch_bounds__(256) reduce_multi_kernel(const __grid_constant__ ReduceJobs J) {
-    griddep_launch();
-    griddep_wait();
-    int j = 0;
-    while (j + 1 < J.count && (int)blockIdx.x >= J.start[j + 1]) ++j;
-    const ReduceArgs &r = J.job[j];
-    const int bx = (int)blockIdx.x - J.start[j], gx = J.start[j + 1] - J.start[j];
-    __shared__ float part[32][9];
-    const int el = threadIdx.x & 7, sl = threadIdx.x >> 3;
-    for (long long base = (long long)bx * 8; base < r.n; base += (long long)gx * 8) {
-        const long long i = base + el;
-        float s0 = 0.0f, s1 = 0.0f;
-        if (i < r.n) {
-            int k = sl;
-            for (; k + 32 < r.splits; k += 64) {
-                s0 += r.partial[(size_t)k * r.n + i];
-                s1 += r.partial[(size_t)(k + 32) * r.n + i];
-            }
-            if (k < r.splits) s0 += r.partial[(size_t)k * r.n + i];
-        }
-        part[sl][el] = s0 + s1;
-        __syncthreads();
-        if (sl == 0 && i < r.n) {
-            float s = part[0][el];
-#pragma unroll
-            for (int l = 1; l < 32; ++l) s += part[l][el];
-            r_store(r, i, s);
-        }
-        __syncthreads();
-    }
-}
-
-// The same jobs, 128 elements per block when every job's length is a multiple
-// of 4: warp w sums splits w, w + 8, w + 16, ... in order, four consecutive
-// elements per lane (one 16-byte load: a warp reads 512 contiguous bytes of a
-// split, four splits in flight), then the eight warp sums of each element are
-// added in warp order (a fixed order: deterministic).
+// Eight split lanes per block: warp w sums splits w, w + 8,
+// w + 16, ... in order, then the eight warp sums of each element are added in
+// warp order (a fixed order: deterministic).  A job whose length is a multiple
+// of 4 (16-byte aligned splits) takes 128 elements per block, four consecutive
+// per lane (one 16-byte load: a warp reads 512 contiguous bytes of a split,
+// four splits in flight); any other job 32, one per lane.
 __global__ void __launch_bounds__(256) reduce_multi4_kernel(const __grid_constant__ ReduceJobs J) {
     griddep_launch();
     griddep_wait();
     int j = 0;
     while (j + 1 < J.count && (int)blockIdx.x >= J.start[j + 1]) ++j;
     const ReduceArgs &r = J.job[j];
+    const bool vec = J.vec[j] != 0;
     __shared__ float4 part[8][32];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const long long n4 = r.n >> 2;
-    const long long q = (long long)((int)blockIdx.x - J.start[j]) * 32 + lane;
+    const long long bx = (int)blockIdx.x - J.start[j];
     float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (q < n4) {
-        const float4 *p = reinterpret_cast<const float4 *>(r.partial) + q;
-        int k = w;
-        for (; k + 24 < r.splits; k += 32) {
-            const float4 a = __ldcg(p + (size_t)k * n4), b = __ldcg(p + (size_t)(k + 8) * n4);
-            const float4 c = __ldcg(p + (size_t)(k + 16) * n4), d = __ldcg(p + (size_t)(k + 24) * n4);
-            s.x += a.x; s.y += a.y; s.z += a.z; s.w += a.w;
-            s.x += b.x; s.y += b.y; s.z += b.z; s.w += b.w;
-            s.x += c.x; s.y += c.y; s.z += c.z; s.w += c.w;
-            s.x += d.x; s.y += d.y; s.z += d.z; s.w += d.w;
+    if (vec) {
+        const long long n4 = r.n >> 2, q = bx * 32 + lane;
+        if (q < n4) {
+            const float4 *p = reinterpret_cast<const float4 *>(r.partial) + q;
+            int k = w;
+            for (; k + 24 < r.splits; k += 32) {
+                const float4 a = __ldcg(p + (size_t)k * n4), b = __ldcg(p + (size_t)(k + 8) * n4);
+                const float4 c = __ldcg(p + (size_t)(k + 16) * n4), d = __ldcg(p + (size_t)(k + 24) * n4);
+                s.x += a.x; s.y += a.y; s.z += a.z; s.w += a.w;
+                s.x += b.x; s.y += b.y; s.z += b.z; s.w += b.w;
+                s.x += c.x; s.y += c.y; s.z += c.z; s.w += c.w;
+                s.x += d.x; s.y += d.y; s.z += d.z; s.w += d.w;
+            }
+            for (; k < r.splits; k += 8) {
+                const float4 a = __ldcg(p + (size_t)k * n4);
+                s.x += a.x; s.y += a.y; s.z += a.z; s.w += a.w;
+            }
         }
-        for (; k < r.splits; k += 8) {
-            const float4 a = __ldcg(p + (size_t)k * n4);
-            s.x += a.x; s.y += a.y; s.z += a.z; s.w += a.w;
+    } else {
+        const long long i = bx * 32 + lane;
+        if (i < r.n) {
+            const float *p = r.partial + i;
+            int k = w;
+            for (; k + 8 < r.splits; k += 16) {
+                const float a = __ldcg(p + (size_t)k * r.n), b = __ldcg(p + (size_t)(k + 8) * r.n);
+                s.x += a;
+                s.x += b;
+            }
+            if (k < r.splits) s.x += __ldcg(p + (size_t)k * r.n);
         }
     }
     part[w][lane] = s;
     __syncthreads();
-    if (w == 0 && q < n4) {
+    if (w == 0) {
         float4 t = part[0][lane];
 #pragma unroll
         for (int l = 1; l < 8; ++l) {
             const float4 u = part[l][lane];
             t.x += u.x; t.y += u.y; t.z += u.z; t.w += u.w;
         }
-        r_store(r, 4 * q, t.x);
-        r_store(r, 4 * q + 1, t.y);
-        r_store(r, 4 * q + 2, t.z);
-        r_store(r, 4 * q + 3, t.w);
+        if (vec) {
+            const long long q = bx * 32 + lane;
+            if (q < (r.n >> 2)) {
+                r_store(r, 4 * q, t.x);
+                r_store(r, 4 * q + 1, t.y);
+                r_store(r, 4 * q + 2, t.z);
+                r_store(r, 4 * q + 3, t.w);
+            }
+        } else if (bx * 32 + lane < r.n) {
+            r_store(r, bx * 32 + lane, t.x);
+        }
     }
 }
 
@@ -1603,27 +1563,23 @@ int reduce_multi(const ReduceArgs *jobs, int count) {
     if (count < 1 || count > kMaxReduceJobs) return fail(kBadArg, "reduce_multi: %d jobs", count);
     ReduceJobs J{};
     J.count = count;
-    bool vec = true;   // every partial vector a multiple of 4 long (16-byte aligned splits)
-    for (int j = 0; j < count; ++j)
-        vec = vec && jobs[j].n % 4 == 0 && (reinterpret_cast<uintptr_t>(jobs[j].partial) & 15) == 0;
     int total = 0;
     for (int j = 0; j < count; ++j) {
         J.job[j] = jobs[j];
         J.start[j] = total;
-        total += vec ? (int)((jobs[j].n / 4 + 31) / 32) : grid_for(jobs[j].n, 8, 16);
+        // 16-byte loads: a partial vector a multiple of 4 long (16-byte aligned splits)
+        J.vec[j] = jobs[j].n % 4 == 0 && (reinterpret_cast<uintptr_t>(jobs[j].partial) & 15) == 0;
+        total += (int)(J.vec[j] ? (jobs[j].n / 4 + 31) / 32 : (jobs[j].n + 31) / 32);
     }
     J.start[count] = total;
-    if (vec) launch_pdl(reduce_multi4_kernel, dim3(total), dim3(256), 0, J);
-    else launch_pdl(reduce_multi_kernel, dim3(total), dim3(256), 0, J);
+    launch_pdl(reduce_multi4_kernel, dim3(total), dim3(256), 0, J);
     ZB_LAUNCH_CHECK("reduce_multi");
     return kOk;
 }
 
 int reduce(const ReduceArgs &r) {
-    if (r.splits >= 32 && r.n <= 131072 && r.n % 4 == 0) return reduce_multi(&r, 1);
-    if (r.splits >= 32 && r.n <= 131072) {
-        launch_pdl(reduce_deep_kernel, dim3(grid_for(r.n, 8, 16)), dim3(256), 0, r);   // 8 elements per block
-    } else if (r.n % 4 == 0 && r.n >= 65536 && r.splits <= 16) {
+    if (r.splits >= 32 && r.n <= 131072) return reduce_multi(&r, 1);   // many splits of a short vector
+    if (r.n % 4 == 0 && r.n >= 65536 && r.splits <= 16) {
         launch_pdl(reduce_wide_kernel, dim3(grid_for(r.n / 4, 256, 8)), dim3(256), 0, r);
     } else {
         launch_pdl(reduce_partials_kernel, dim3(grid_for(r.n, 32, 8)), dim3(256), 0, r);   // 32 elements per block
@@ -2154,6 +2110,12 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
         prof_mark(n, "softmax_ce");
         return kOk;
     }
+    // Deep reductions whose partial sums nothing reads before the next fused backward kernel
+    // ends join that kernel's reduction launch (fewer launches).  Not while the data-parallel
+    // exchange starts beside the fused kernel: it needs them final.
+    ReduceArgs held[kMaxReduceJobs];
+    int nheld = 0;
+    const bool hold_ok = !(n.peer.on && n.peer.two_phase);
     // ---- head: classifier, loss, start of the backward (hidden Linear + classifier)
     if (!e.direct_head) {
     const Stage &sh = st[e.head_si];
@@ -2163,11 +2125,15 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
     launch_pdl(head_kernel<256, 10>, dim3(e.head_grid), dim3(256), 0, e.a_hid, n.params + sh.poff,
                n.params + sh.poff + sh.pn_w, y, e.dZ_hid, e.row_loss, e.head_partial, B, 1.0f / (float)B);
     ZB_LAUNCH_CHECK("head");
-    {   // fc2 dW, db, fc1 db and the loss sum (the blocks' partials, in block order)
+    {   // fc2 dW, db, fc1 db and the loss sum (the blocks' partials, in block order): nothing reads
+        // them before the optimizer unless an all-reduce bucket or the mid-step exchange takes them
+        // first, so they join the fused phase's reduction launch
         ReduceArgs r{e.head_partial, e.head_grid, (long long)e.HD * e.NC + e.NC + e.HD + 1, 4, e.HD, e.NC, 0, 0, 0, 0,
                      gW5, gb5, gb4};
         r.dst4 = loss_out;
-        if ((rc = reduce(r))) return rc;
+        const bool hold_head = hold_ok && (n.world <= 1 || n.peer.in_step) && r.splits >= 32 && r.n <= 131072;
+        if (hold_head) held[nheld++] = r;
+        else if ((rc = reduce(r))) return rc;
     }
     prof_mark(n, "softmax_ce");
     // ---- hidden Linear backward
@@ -2195,12 +2161,6 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
     }
     // ---- conv stages backward (last to first)
     const bf16 *dpooled = e.dflat;   // gradient w.r.t. the last pooled output
-    // deep reductions of a layer whose partial sums nothing reads before the next fused
-    // backward kernel ends: they join that kernel's reduction launch (one launch fewer).
-    // Not while the data-parallel exchange starts beside the fused kernel: it needs them final.
-    ReduceArgs held[kMaxReduceJobs];
-    int nheld = 0;
-    const bool hold_ok = !(n.peer.on && n.peer.two_phase);
     for (int li = (int)e.convs.size() - 1; li >= 0; --li) {
         ConvLayer &L = e.convs[li];
         const Stage &s = st[L.si];
@@ -2265,7 +2225,7 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
             bool deep = true;
             for (int j = 0; j < nj; ++j) deep = deep && jobs[j].splits >= 32 && jobs[j].n <= 131072;
             const bool next_fused = li > 0 && e.convs[li - 1].fused_bwd;
-            if (deep && hold_ok && next_fused) {
+            if (deep && hold_ok && next_fused && nheld + nj + 3 <= kMaxReduceJobs) {
                 for (int j = 0; j < nj; ++j) held[nheld++] = jobs[j];
             } else if (deep) {
                 if ((rc = reduce_multi(jobs, nj))) return rc;
@@ -2276,6 +2236,8 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
         }
         prof_mark(n, "conv_wgrad");
     }
+    if (nheld && (rc = reduce_multi(held, nheld))) return rc;   // (no fused layer took them)
+    nheld = 0;
     // ---- first conv backward (dC1 written by the next conv's dgrad, masked)
     if (e.c1_fused) return kOk;   // taken by the next conv's fused backward kernel
     {

@@ -19,12 +19,20 @@
 // memory, so a stage is released only when both its MMAs and the epilogue's
 // mask reads are done (two arrivals).
 //
-// TMEM: the input gradient in two 128 x CX accumulators (double-buffered: the
+// The input gradient runs as Z[i][dw][ci] = sum_dh sum_co dY[i + dh*Wp][co]
+// Wd[dh][dw][ci][co]: per kernel row dh and K16 step, three MMAs (dw = 0, 1, 2;
+// N = CX each) share one A descriptor, kept in the tensor core's collector
+// buffer, so shared memory serves the dY operand 12 times per tile instead of
+// 36; the epilogue adds dX[i] = Z[i][0] + Z[i+1][1] + Z[i+2][2] with warp
+// shuffles (a warp is one tile row, and the columns c + dw of a real output
+// stay inside it).
+//
+// TMEM: the input gradient in two 128 x 3*CX accumulators (double-buffered: the
 // epilogue of tile i overlaps the MMAs of tile i+1), the weight gradient in one
 // 64-row x 9*CX accumulator that stays for the CTA's whole run (M = CY = 64:
-// rows 16q .. 16q+15 in lanes 32q .. 32q+15).  At the end each CTA writes its
-// weight-gradient partial [cta][CY][9*CX]; a second kernel sums them in CTA
-// order (deterministic).
+// rows 16q .. 16q+15 in lanes 32q .. 32q+15), the first conv's in CX columns:
+// 512 in all.  At the end each CTA writes its weight-gradient partial
+// [cta][CY][9*CX]; a second kernel sums them in CTA order (deterministic).
 //
 // Warp roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer and TMEM
 // owner, warps 2-9 epilogue (input gradient: staged bf16 tile + TMA store, as
@@ -96,8 +104,9 @@ struct ConvBwdFusedShape {
     static constexpr int WROWB = CY * 2;                 // dgrad weight row: 128 B (CY = 64)
     static constexpr int WBLK = CX * WROWB;              // one tap
     static constexpr int WTOTAL = 9 * WBLK;
-    static constexpr uint32_t TMEM_COLS = 512;           // 2 * CX + NTOT <= 512
-    static constexpr int WG_COL0 = 2 * CX;                // weight-gradient columns start
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr int ZCOLS = 3 * CX;                  // one input-gradient accumulator: Z[i][dw][ci]
+    static constexpr int WG_COL0 = 2 * ZCOLS;             // weight-gradient columns start
     static constexpr int C1_COL0 = WG_COL0 + 9 * CX;      // first-conv weight-gradient columns (C1)
     static constexpr int SLACK = 1024;
     static constexpr int BAR_BYTES = 256;
@@ -111,7 +120,7 @@ struct ConvBwdFusedShape {
         return 1024 + WTOTAL + NS * stage_bytes(R, Wp) + SLACK + 2 * (out_tile_bytes(R, W) + x9_bytes(R, W)) + BAR_BYTES;
     }
     static_assert(CY == 64 && CX == 32, "built for the 32 -> 64 conv: M = 64 weight gradient, N = 32 input gradient");
-    static_assert(2 * CX + NTOT + (C1 ? CX : 0) <= 512, "TMEM columns");
+    static_assert(2 * ZCOLS + NTOT + (C1 ? CX : 0) <= 512, "TMEM columns");
 };
 
 template <int CX, int CY, int NS, bool C1 = false, bool UP = false>
@@ -240,17 +249,26 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
                     if (!mbar_wait(&full[s], ph, abort_flag, p.err, kErrFullWait)) break;
                     tc_fence_after();
                     const uint64_t st16 = (uint64_t)((uint32_t)(s * STAGE) >> 4);
-                    // input gradient: 9 taps x CY/16 K16 steps into acc
-                    const uint32_t d = tmem_base + (uint32_t)(acc * CX);
+                    // input gradient: Z[i][dw][ci] = sum_dh dY[i + dh*Wp] Wd[dh][dw] (3 kernel rows x
+                    // CY/16 K16 steps x the 3 columns dw, N = CX each); the three MMAs of a (dh, K16)
+                    // step share A, which stays in the collector buffer.  The epilogue forms
+                    // dX[i] = sum_dw Z[i + dw][dw] (a shift along the tile row).
+                    const uint32_t d = tmem_base + (uint32_t)(acc * S::ZCOLS);
 #pragma unroll
-                    for (int tap = 0; tap < 9; ++tap) {
-                        const int dh = tap / 3, dw = tap - 3 * dh;
-                        const uint64_t a_tap = dx_a0 + st16 + (uint64_t)(dh * wp + dw);
+                    for (int dh = 0; dh < 3; ++dh) {
+                        const uint64_t a_dh = dx_a0 + st16 + (uint64_t)(dh * wp);
 #pragma unroll
-                        for (int k = 0; k < CY / 16; ++k)
-                            mma_bf16(d, a_tap + (uint64_t)(2 * k * reg16),
-                                     dx_b0 + (uint64_t)((uint32_t)(tap * S::WBLK + k * 32) >> 4), IDESC_DX,
-                                     (tap | k) != 0);
+                        for (int k = 0; k < CY / 16; ++k) {
+                            const uint64_t ad = a_dh + (uint64_t)(2 * k * reg16);
+#pragma unroll
+                            for (int dw = 0; dw < 3; ++dw) {
+                                const uint64_t bd = dx_b0 + (uint64_t)((uint32_t)((dh * 3 + dw) * S::WBLK + k * 32) >> 4);
+                                const uint32_t dt = d + (uint32_t)(dw * CX);
+                                if (dw == 0) mma_bf16_ca<0>(dt, ad, bd, IDESC_DX, (dh | k) != 0);
+                                else if (dw == 1) mma_bf16_ca<1>(dt, ad, bd, IDESC_DX, (dh | k) != 0);
+                                else mma_bf16_ca<2>(dt, ad, bd, IDESC_DX, (dh | k) != 0);
+                            }
+                        }
                     }
                     mma_commit(&acc_full[acc]);
                     if (++acc == 2) { acc = 0; acc_ph ^= 1u; }
@@ -412,10 +430,18 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
             named_bar_sync(1, 256);
             if (*abort_flag) break;
             tc_fence_after();
-            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * CX);
-            if (grp == 0) {   // CX = 32: one 32-column chunk, taken by the first group
-                float v[32];
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * S::ZCOLS);
+            if (grp == 0) {   // CX = 32: dX = Z[.][0] + Z[. + 1][1] + Z[. + 2][2], taken by the first group
+                // lane = tile column (Wp = 32: a warp is one tile row); columns c + dw of a real
+                // output (c < W <= 30) stay inside the row
+                float v[32], z[32];
                 tmem_ld32(taddr, v);
+                tmem_ld32(taddr + CX, z);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += __shfl_down_sync(0xffffffffu, z[j], 1);
+                tmem_ld32(taddr + 2 * CX, z);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += __shfl_down_sync(0xffffffffu, z[j], 2);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acc_empty[acc]);

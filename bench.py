@@ -1,13 +1,15 @@
 """Training-step throughput of the ZillaPHP hot path on B200 (samples/s).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload large_cnn] [--precision 0|1]
+                    [--workload large_cnn] [--precision 0|1] [--no-graph]
 
 One step = forward + backward + optimizer update of the whole global batch
 (large_cnn: 8192 samples of 1x28x28, Conv/ReLU/Pool x3 + Linear x2, Adam),
 through the fused-step C-ABI (zilla_net_step).  Under torchrun each rank
-trains its 1/N shard and the library all-reduces the flat gradient buffer
-over NCCL before the identical update (global batch fixed: strong scaling).
+trains its 1/N shard; the ranks exchange their gradients over NVLink peer
+memory (the update kernel of each rank sums and updates its slice) before the
+next step (global batch fixed: strong scaling).  Each step is replayed from a
+CUDA graph (zilla_net_set_graph) unless --no-graph.
 
 value  : global samples/s with inputs resident in HBM (CUDA events on the
          library's stream, max over ranks).
@@ -17,8 +19,9 @@ e2e    : the same from pinned host buffers through zilla_net_stage_host +
          region; the copy of batch k+1 overlaps step k, and the host waits for
          step k-1's loss while step k is queued.
 roofline: the dominant kernel group of the step (algorithmic FLOPs or bytes
-         / its CUDA-event duration averaged over the timed steps) against
-         MEASURED_PEAKS.json.
+         / its CUDA-event duration) against MEASURED_PEAKS.json: averaged over
+         the timed steps with --no-graph (events at the group's two boundaries
+         only), else over an untimed profiled pass of 3 plain steps.
 cpu_baseline: the reference's own CPU library (native/cpu/*.c built with its
          flags + OpenBLAS) driven through the reference step sequence on a
          bounded sample, rank 0, N=1 only.
@@ -383,13 +386,17 @@ def main():
     ap.add_argument("--precision", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--graph", action="store_true",
-                    help="replay each step from a CUDA graph (zilla_net_set_graph); the timed region then "
-                         "runs without per-segment events, so no roofline")
+                    help="replay each step from a CUDA graph (zilla_net_set_graph): the default; the "
+                         "roofline's group time then comes from an untimed profiled pass of plain steps")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch every step's kernels from the host (events at the dominant group's "
+                         "boundaries in the timed region)")
     ap.add_argument("--autograd", action="store_true",
                     help="time the batched autograd bridge (Tensor/Sequential/Trainer, one device call per op)")
     ap.add_argument("--batch", type=int, default=None,
                     help="global batch override (small cases for ncu captures; default: the workload's)")
     args = ap.parse_args()
+    args.graph = not args.no_graph
     if args.workload == configs.TRANSFORMER_LM.name:
         return main_lm(args)
     w = configs.WORKLOADS[args.workload]

@@ -136,6 +136,13 @@ int zilla_check_device(void);
 int adam_update_dev(int w_id, int g_id, int m_id, int v_id, float lr, float beta1, float beta2,
                     float eps, int t, int n);
 
+/* The loss of the PHP CrossEntropy (src/Loss/CrossEntropy.php:56-59), which
+ * clamps each row's target probability at 1e-12 before the log: loss +=
+ * sum_rows -log(max(p_t, 1e-12)).  dlogits = (p - onehot)/B as softmax_ce_dev.
+ * The native softmax_ce_dev has no clamp; this serves the Tensor / autograd
+ * layer, whose rows can reach p_t < 1e-12 (a logit gap above 27.6). */
+int softmax_ce_clamped_dev(int logits_id, int targets_id, int dlogits_id, int loss_id, int B, int C);
+
 /* softmax_ce_dev for callers that cannot let a library allocate device memory
  * (code under a caller-owned memory pool or budget, or a host that only hands
  * over device pointers it already owns).  No counterpart in the reference.

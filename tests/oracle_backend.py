@@ -107,6 +107,16 @@ class OracleBackend:
         self.bufs[dl][:B * C] = g.ravel()
         self.bufs[loss][0] = s
 
+    def softmaxCeClampedDev(self, z, t, dl, loss, B, C):  # noqa: N802
+        """CrossEntropy.php:56-59 in float64: the rows' -log(max(p_t, 1e-12)); softmax_ce_dev's gradient."""
+        zz = self._b(z, B * C, (B, C)).astype(np.float64)
+        tt = self._b(t, B).astype(np.int64)
+        g, _ = oracle.softmax_ce_dev(self._b(z, B * C, (B, C)), self._b(t, B), loss0=0.0)
+        p = np.exp(zz - zz.max(axis=1, keepdims=True))
+        p /= p.sum(axis=1, keepdims=True)
+        self.bufs[dl][:B * C] = g.ravel()
+        self.bufs[loss][0] = np.float32(float(self.bufs[loss][0]) + float(-np.log(np.maximum(p[np.arange(B), tt], 1e-12)).sum()))
+
     def sgdUpdateDev(self, w, g, lr, n):  # noqa: N802
         self.bufs[w][:n] = oracle.sgd_update_dev(self._b(w, n), self._b(g, n), lr)
 

@@ -60,7 +60,8 @@ def test_host_side_errors(lib):
     lib.zilla_buffer_free(-3)          # idempotent no-op
     lib.zilla_buffer_free(77)
     for rc in (lib.relu_dev(77, 78, 10), lib.matmul_dev(1, 2, 3, 4, 5, 6),
-               lib.softmax_ce_dev(1, 2, 3, 4, 8, 10), lib.conv2d_batched_fwd_dev(*([5] * 15)),
+               lib.softmax_ce_dev(1, 2, 3, 4, 8, 10), lib.softmax_ce_clamped_dev(1, 2, 3, 4, 8, 10),
+               lib.conv2d_batched_fwd_dev(*([5] * 15)),
                lib.maxpool2d_batched_bwd_dev(1, 2, 3, 4, 5, 6, 7), lib.adam_update_dev(1, 2, 3, 4, 1e-3, .9, .999, 1e-8, 1, 8)):
         assert rc == -1
     buf = np.zeros(4, np.float32)

@@ -52,6 +52,13 @@ def test_bridge_steps_match_oracle_step(fake, name, batch):
         x4 = x.reshape((batch,) + tuple(w.in_shape))
         rl = ref.step(x, y, opt=w.optimizer, lr=w.lr)
         bl = trainer.step(x4, y)
+        # the step sequence's loss is softmax_ce_dev's (no clamp); CrossEntropy clamps p_t at
+        # 1e-12 (CrossEntropy.php:58), so where a row falls below it the bar is that loss
+        z = ref.output(len(w.layers) - 1, batch * w.classes).reshape(batch, w.classes).astype(np.float64)
+        pz = np.exp(z - z.max(1, keepdims=True))
+        pt = (pz / pz.sum(1, keepdims=True))[np.arange(batch), y.astype(np.int64)]
+        if (pt < 1e-12).any():   # CrossEntropy's loss (float64, as the PHP class) from the same logits
+            rl = float(-np.log(np.maximum(pt, 1e-12)).sum())
         assert abs(bl * batch - rl) <= 1e-6 * abs(rl), (step, bl * batch, rl)
         assert npref.normwise(model.flat(grads=True), ref.grads) < 1e-6
         assert npref.normwise(model.flat(), ref.params) < 1e-6
@@ -113,6 +120,25 @@ def test_scaled_loss_scales_the_gradient(fake):
             np.testing.assert_allclose(root.item(), k * loss.item(), rtol=1e-6)
     np.testing.assert_allclose(grads[1], 0.5 * grads[0], rtol=1e-6, atol=1e-7)
     np.testing.assert_allclose(grads[2], -3.0 * grads[0], rtol=1e-6, atol=1e-7)
+
+
+def test_cross_entropy_clamps_the_target_probability(fake):
+    """CrossEntropy.php:58 takes -log(max(p, 1e-12)): a row whose target logit trails by 100
+    (p_t ~ 4e-44) adds 27.631 to the sum, not 100; the gradient is unclamped (p - onehot) / B."""
+    zn = np.array([[0.0, 100.0, 0.0], [1.0, 2.0, 3.0]], np.float32)
+    t = [0, 2]
+    z = ag.Parameter(zn)
+    loss = ag.CrossEntropy().forward(z, t)
+    loss.backward()
+    zz = zn.astype(np.float64)
+    p = np.exp(zz - zz.max(1, keepdims=True))
+    p /= p.sum(1, keepdims=True)
+    want = -np.log(np.maximum(p[np.arange(2), t], 1e-12)).mean()
+    np.testing.assert_allclose(loss.item(), want, rtol=1e-6)
+    assert abs(loss.item() - (-np.log(1e-12) - np.log(p[1, 2])) / 2) < 1e-4
+    g = p.copy()
+    g[np.arange(2), t] -= 1
+    np.testing.assert_allclose(z.grad.numpy(), g / 2, atol=1e-7)
 
 
 def test_no_grad_records_nothing(fake):

@@ -253,3 +253,32 @@ def test_stft_and_hann(be):
     win = 0.5 - 0.5 * np.cos(2 * np.pi * np.arange(64) / 63)
     ref0 = np.abs(np.fft.rfft(x[:64] * win))
     np.testing.assert_allclose(mag[:, 0], ref0, atol=1e-3)
+
+
+def test_softmax_ce_clamped_matches_cross_entropy_php(be):
+    """softmax_ce_clamped_dev: the loss of CrossEntropy.php:56-59, -log(max(p_t, 1e-12)) per
+    row, on rows with and without a target probability below 1e-12; the gradient equals
+    softmax_ce_dev's (p - onehot) / B bit for bit."""
+    rng = np.random.default_rng(5)
+    B, C = 64, 10
+    z = rng.standard_normal((B, C)).astype(np.float32)
+    t = rng.integers(0, C, B).astype(np.float32)
+    z[::4, :] *= 40.0                          # every fourth row: logit gaps far past 27.6
+    zi, ti = put(be, z), put(be, t)
+    d1, d2 = be.bufferAlloc(B * C), be.bufferAlloc(B * C)
+    l1, l2 = put(be, np.zeros(1)), put(be, np.zeros(1))
+    be.softmaxCeDev(zi, ti, d1, l1, B, C)
+    be.softmaxCeClampedDev(zi, ti, d2, l2, B, C)
+    g1, g2 = get(be, d1, B * C), get(be, d2, B * C)
+    loss1, loss2 = float(get(be, l1, 1)[0]), float(get(be, l2, 1)[0])
+    for i in (zi, ti, d1, d2, l1, l2):
+        be.bufferFree(i)
+    zz = z.astype(np.float64)
+    p = np.exp(zz - zz.max(1, keepdims=True))
+    p /= p.sum(1, keepdims=True)
+    pt = p[np.arange(B), t.astype(np.int64)]
+    assert (pt < 1e-12).sum() >= 4
+    want = float(-np.log(np.maximum(pt, 1e-12)).sum())
+    assert abs(loss2 - want) / want < 1e-5, (loss2, want)
+    assert loss1 > loss2                        # the unclamped rows count more
+    assert np.array_equal(g1, g2)

@@ -24,13 +24,10 @@ Mirrors, with their semantics:
   Tensor::relu       :1140-1154 relu_fwd_dev (mask) / relu_bwd_dev
   Tensor::noGrad     :54-62
   CrossEntropy       src/Loss/CrossEntropy.php:18-85: the mean over the batch of
-                     -log p_target; gradient (p - onehot) / B.  Computed by
-                     softmax_ce_dev in fp32, then scaled by the upstream gradient
-                     g->item() as :69-70 do.  The PHP class is float64 and clamps p
-                     at 1e-12 (:58); softmax_ce_dev has no clamp, so the loss of a
-                     row whose target probability is below 1e-12 (a logit gap
-                     above 27.6) keeps growing here where the reference's stops
-                     at 27.63 (the gradients are the same)
+                     -log max(p_target, 1e-12) (:58); gradient (p - onehot) / B.
+                     Computed by softmax_ce_clamped_dev in fp32 (the PHP class is
+                     float64), then scaled by the upstream gradient g->item() as
+                     :69-70 do
   Tensor::mul        :1046-1054 mul_dev, same-shape operands only
   SGD / Adam         src/Optim/SGD.php:12-26, src/Optim/Adam.php:36-62
                      (sgd_update_dev; adam_update_dev with t counted per step)
@@ -476,7 +473,7 @@ class CrossEntropy:
         dlogits = Tensor.empty((B, Cn))
         loss = Tensor.zeros((1,))
         be = backend()
-        be.softmaxCeDev(pred.buf, y.buf, dlogits.buf, loss.buf, B, Cn)   # loss SUM, dlogits = (p - 1hot)/B
+        be.softmaxCeClampedDev(pred.buf, y.buf, dlogits.buf, loss.buf, B, Cn)   # loss SUM (p_t >= 1e-12), dlogits = (p - 1hot)/B
         be.scaleDev(loss.buf, 1.0 / B, 1)                                  # the mean
         p = pred
 

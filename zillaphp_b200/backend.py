@@ -111,6 +111,10 @@ class B200Backend:
     def softmaxCeDev(self, logitsId, targetsId, dlogitsId, lossId, B, C_):  # noqa: N802,N803
         self._check(self.ffi.softmax_ce_dev(logitsId, targetsId, dlogitsId, lossId, B, C_), "softmax_ce_dev")
 
+    def softmaxCeClampedDev(self, logitsId, targetsId, dlogitsId, lossId, B, C_):  # noqa: N802,N803
+        self._check(self.ffi.softmax_ce_clamped_dev(logitsId, targetsId, dlogitsId, lossId, B, C_),
+                    "softmax_ce_clamped_dev")
+
     def biasGradDev(self, dyId, dbId, B, C_):  # noqa: N802,N803
         self._check(self.ffi.bias_grad_dev(dyId, dbId, B, C_), "bias_grad_dev")
 

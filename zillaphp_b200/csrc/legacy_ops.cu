@@ -91,9 +91,11 @@ __global__ void scale_kernel(float *__restrict__ x, float s, long long n) {
 // row order (deterministic, unlike the reference's float atomicAdd at
 // native/cuda/training_ops.cu:141) and adds the total to *loss as the CPU
 // reference does (native/cpu/training_ops.c:171,204).
+// floor > 0: each row's loss is -log(max(p_target, floor)) (CrossEntropy.php's clamp);
+// floor = 0 is softmax_ce_dev's plain -log(p_target).
 __global__ void softmax_ce_rows_kernel(const float *__restrict__ z, const float *__restrict__ tgt,
                                        float *__restrict__ dz, double *__restrict__ row_loss,
-                                       int B, int C) {
+                                       int B, int C, float floor = 0.0f) {
     const int warps = blockDim.x >> 5;
     const int lane = threadIdx.x & 31;
     const float inv = 1.0f / (float)B;
@@ -114,7 +116,7 @@ __global__ void softmax_ce_rows_kernel(const float *__restrict__ z, const float 
         }
         if (lane == 0) {
             const float pt = (t >= 0 && t < C) ? expf(row[t] - mx) / s : 0.0f;
-            row_loss[r] = -(double)logf(pt);
+            row_loss[r] = -(double)logf(floor > 0.0f ? fmaxf(pt, floor) : pt);
         }
     }
 }
@@ -440,21 +442,30 @@ int relu_bwd_dev(int dy_id, int mask_id, int dx_id, int n) {
     return binary_dev<Bin::Mul>(dy_id, mask_id, dx_id, n, "relu_bwd_dev");
 }
 
-int softmax_ce_dev(int logits_id, int targets_id, int dlogits_id, int loss_id, int B, int C) {
+static int softmax_ce_rows(int logits_id, int targets_id, int dlogits_id, int loss_id, int B, int C, float floor,
+                           const char *name) {
     float *z = ptr(logits_id), *t = ptr(targets_id), *dz = ptr(dlogits_id), *loss = ptr(loss_id);
-    if (!z || !t || !dz || !loss) return fail(kBadHandle, "softmax_ce_dev: invalid handle");
-    if (B < 0 || C <= 0) return fail(kBadArg, "softmax_ce_dev: bad sizes");
+    if (!z || !t || !dz || !loss) return fail(kBadHandle, "%s: invalid handle", name);
+    if (B < 0 || C <= 0) return fail(kBadArg, "%s: bad sizes", name);
     if (B == 0) return kOk;
     double *rl = row_loss_scratch((size_t)B);
-    if (!rl) return fail(kBadHandle, "softmax_ce_dev: scratch allocation failed");
-    const int warps = kThreads / 32;
+    if (!rl) return fail(kBadHandle, "%s: scratch allocation failed", name);
     softmax_ce_rows_kernel<<<grid_for((long long)B * 32, kThreads), kThreads, 0, stream()>>>(
-        z, t, dz, rl, B, C);
-    ZB_LAUNCH_CHECK("softmax_ce_dev");
-    (void)warps;
+        z, t, dz, rl, B, C, floor);
+    ZB_LAUNCH_CHECK(name);
     sum_rows_into_loss_kernel<<<1, kThreads, 0, stream()>>>(rl, B, loss);
-    ZB_LAUNCH_CHECK("softmax_ce_dev(sum)");
+    ZB_LAUNCH_CHECK(name);
     return kOk;
+}
+
+int softmax_ce_dev(int logits_id, int targets_id, int dlogits_id, int loss_id, int B, int C) {
+    return softmax_ce_rows(logits_id, targets_id, dlogits_id, loss_id, B, C, 0.0f, "softmax_ce_dev");
+}
+
+// The loss of CrossEntropy::forward (src/Loss/CrossEntropy.php:56-59): -log(max(p, 1e-12)) per
+// row; the gradient is softmax_ce_dev's.
+int softmax_ce_clamped_dev(int logits_id, int targets_id, int dlogits_id, int loss_id, int B, int C) {
+    return softmax_ce_rows(logits_id, targets_id, dlogits_id, loss_id, B, C, 1e-12f, "softmax_ce_clamped_dev");
 }
 
 int bias_grad_dev(int dy_id, int db_id, int B, int C) {

@@ -73,6 +73,7 @@ SIGNATURES: dict[str, tuple] = {
     "zilla_launch_count": (C.c_ulonglong, []),
     "zilla_check_device": (I, []),
     "adam_update_dev": (I, [I, I, I, I, F, F, F, F, I, I]),
+    "softmax_ce_clamped_dev": (I, [I, I, I, I, I, I]),
     "softmax_ce_noalloc": (I, [VP, VP, VP, VP, I, I, VP]),
     "zilla_net_create": (I, [IP, I, I, I, I, I, I]),
     "zilla_net_destroy": (I, [I]),

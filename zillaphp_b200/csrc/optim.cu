@@ -14,10 +14,11 @@
 namespace zb {
 
 // Each thread takes kAdamU float4 groups (i, i + stride, ...) per pass and
-// issues all their loads before any arithmetic, so 4 * kAdamU 16-byte loads
-// per thread are in flight; the launcher sizes the grid so that one pass
-// covers the buffer.
-constexpr int kAdamU = 2;
+// issues all their loads before any arithmetic; the launcher sizes the grid so
+// that one pass covers the buffer.  One group per thread (1,662 blocks for the
+// large CNN's 1.7 M parameters) measured 14.4 us cold against 16.3 us for two
+// groups and 20.5 us for four: more threads in flight beat more loads per thread.
+constexpr int kAdamU = 1;
 
 __global__ void __launch_bounds__(256) adam_kernel(float *__restrict__ w, const float *__restrict__ g,
                                                    float *__restrict__ m, float *__restrict__ v, long long n,

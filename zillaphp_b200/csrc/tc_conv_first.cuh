@@ -34,8 +34,8 @@ template <int CO>
 struct ConvFirstTcShape {
     static constexpr int ABYTES = 4 * 128 * 16;   // 4 K chunks x 128 rows x 16 B
     static constexpr int BBYTES = 4 * CO * 16;
-    static constexpr int OBYTES = 128 * CO * 2;   // staged output tile
-    static constexpr int SMEM = 1024 + ABYTES + BBYTES + OBYTES + 64;
+    static constexpr int OBYTES = 128 * CO * 2;   // one staged output tile
+    static constexpr int SMEM = 1024 + ABYTES + BBYTES + 2 * OBYTES + 64;   // two output buffers
     static constexpr uint32_t TMEM_COLS = 32;
     static_assert(CO == 32, "one 32-column TMEM accumulator");
 };
@@ -62,7 +62,7 @@ __global__ void __launch_bounds__(128, 8) conv_first_tc_kernel(const float *__re
     uint8_t *sA = base;
     uint8_t *sB = sA + S::ABYTES;
     uint8_t *sO = sB + S::BBYTES;
-    uint64_t *mma_done = reinterpret_cast<uint64_t *>(sO + S::OBYTES);
+    uint64_t *mma_done = reinterpret_cast<uint64_t *>(sO + 2 * S::OBYTES);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     const int m = threadIdx.x, warp = m >> 5;
@@ -122,7 +122,8 @@ __global__ void __launch_bounds__(128, 8) conv_first_tc_kernel(const float *__re
     long long tile = blockIdx.x;
     if (tile < ntiles) load_taps(tile, xt);
     uint32_t ph = 0;
-    for (; tile < ntiles; tile += gridDim.x) {
+    int ob = 0;   // output buffer of this tile (two, so one tile's copy overlaps the next tile)
+    for (; tile < ntiles; tile += gridDim.x, ob ^= 1) {
         // im2col row m of this tile
         {
             const bool ok = tile * 128 + m < npix;
@@ -144,7 +145,7 @@ __global__ void __launch_bounds__(128, 8) conv_first_tc_kernel(const float *__re
         }
         fence_proxy_async_smem();
         tc_fence_before();
-        if (m == 0) bulk_wait_read<0>();   // the previous tile's copy has read the staged output
+        if (m == 0) bulk_wait_read<1>();   // the copy of two tiles ago has read this tile's output buffer
         __syncthreads();   // row writes visible; the previous tile's TMEM reads are done
         if (m == 0) {
             tc_fence_after();
@@ -177,14 +178,14 @@ __global__ void __launch_bounds__(128, 8) conv_first_tc_kernel(const float *__re
             if (q4 == 1) val = pk[1];
             if (q4 == 2) val = pk[2];
             if (q4 == 3) val = pk[3];
-            *reinterpret_cast<uint4 *>(sO + m * (CO * 2) + q4 * 16) = val;
+            *reinterpret_cast<uint4 *>(sO + ob * S::OBYTES + m * (CO * 2) + q4 * 16) = val;
         }
         fence_proxy_async_smem();
         __syncthreads();
         if (m == 0) {
             const long long p0 = tile * 128;
             const long long np = npix - p0 < 128 ? npix - p0 : 128;
-            bulk_store(out + p0 * CO, sO, (uint32_t)(np * CO * 2));
+            bulk_store(out + p0 * CO, sO + ob * S::OBYTES, (uint32_t)(np * CO * 2));
             bulk_commit();
         }
     }

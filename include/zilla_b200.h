@@ -260,12 +260,15 @@ int zilla_net_load(int net, const char *path);
 
 /* Per-step CUDA graphs (no reference counterpart; the reference launches
  * about 30 FFI calls per step, examples/mnist_cnn_gpu_v2.php:183-264).
- * enable != 0: on one rank and without profiling, the first step for given
- * inputs (x, y buffers and update flag) runs as is, the second is captured
- * into a CUDA graph and launched, later ones replay it with the optimizer's
- * arguments of the step; up to 16 input sets per net.  Results are those of
- * the plain step, bit for bit.  zilla_net_set_optimizer drops the graphs.
- * enable = 0 drops them and returns to plain launches. */
+ * enable != 0: without profiling, the first step for given inputs (x, y
+ * buffers and update flag) runs as is, the second is captured into a CUDA
+ * graph and launched, later ones replay it with the optimizer's arguments of
+ * the step; up to 16 input sets per net.  On one rank, or under the
+ * peer-memory data-parallel step (one graph per input set and exchange
+ * buffer, the exchange and update kernels given each step's number and Adam
+ * arguments); the NCCL path runs plain.  Results are those of the plain step,
+ * bit for bit.  zilla_net_set_optimizer, zilla_dp_attach and zilla_dp_detach
+ * drop the graphs.  enable = 0 drops them and returns to plain launches. */
 int zilla_net_set_graph(int net, int enable);
 
 /* Device timing of the step's segments (instrumentation).  With profiling

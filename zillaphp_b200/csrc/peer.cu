@@ -346,6 +346,7 @@ int peer_detach(Net &n) {
 #ifdef ZB_HAVE_NCCL
     PeerState &P = n.peer;
     if (!P.on) return kOk;
+    release_graphs(n);   // captured steps hold the peers' mappings
     // the Adam moments of each slice live on its owner: every rank gets all of them
     for (int q = 0; q < n.world; ++q) {
         const long long lo = P.chunk * q < n.nparams ? P.chunk * q : n.nparams;

@@ -257,24 +257,130 @@ __global__ void ln_bwd_kernel(const float *__restrict__ gout, const float *__res
     }
 }
 
-// Column sums over rows with a row stride, first stage: block (column tile, row chunk)
-// sums rows [r0, r1) of 32 columns (8 row lanes, combined in order) into
-// part[chunk][col]; the step's deferred sums add the chunks in order.
-__global__ void colsum_part_kernel(const float *__restrict__ dY, int rows, int ld, int chunks,
-                                   float *__restrict__ part) {
-    __shared__ float red[8][33];
-    const int col = blockIdx.x * 32 + threadIdx.x;
-    const int r0 = (int)((long long)rows * blockIdx.y / chunks), r1 = (int)((long long)rows * (blockIdx.y + 1) / chunks);
-    float acc = 0.0f;
-    if (col < ld)
-        for (int r = r0 + threadIdx.y; r < r1; r += 8) acc += dY[(size_t)r * ld + col];
-    red[threadIdx.y][threadIdx.x] = acc;
-    __syncthreads();
-    if (threadIdx.y == 0 && col < ld) {
-        float t = 0.0f;
+// ln_bwd_kernel for D = 32 KD: lane l keeps columns l + 32 k (k < KD) of gamma and
+// of its warp's dgamma / dbeta sums in registers, and loads the next row's g, xhat
+// and R while it finishes the current one.  Same arithmetic and order as above.
+template <int KD>
+__global__ void __launch_bounds__(256) ln_bwd_reg_kernel(const float *__restrict__ gout, const float *__restrict__ xhat,
+                                                         const float *__restrict__ inv, const float *__restrict__ gam,
+                                                         const float *__restrict__ R, float *__restrict__ out,
+                                                         float *__restrict__ partial, int N) {
+    constexpr int D = 32 * KD;
+    __shared__ float red[8][2 * D];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float gm[KD], dgam[KD], dbet[KD];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) t += red[k][threadIdx.x];
-        part[(size_t)blockIdx.y * ld + col] = t;
+    for (int k = 0; k < KD; ++k) { gm[k] = gam[lane + 32 * k]; dgam[k] = 0.0f; dbet[k] = 0.0f; }
+    const int stride = gridDim.x * 8;
+    int r = blockIdx.x * 8 + warp;
+    float g[KD], xh[KD], rr[KD], iv = 0.0f;
+    auto load = [&](int row) {
+        iv = inv[row];
+#pragma unroll
+        for (int k = 0; k < KD; ++k) {
+            g[k] = __ldcs(gout + (size_t)row * D + lane + 32 * k);
+            xh[k] = __ldcs(xhat + (size_t)row * D + lane + 32 * k);
+            rr[k] = R ? __ldcs(R + (size_t)row * D + lane + 32 * k) : 0.0f;
+        }
+    };
+    if (r < N) load(r);
+    for (; r < N; r += stride) {
+        float cg[KD], cx[KD], cr[KD];
+#pragma unroll
+        for (int k = 0; k < KD; ++k) { cg[k] = g[k]; cx[k] = xh[k]; cr[k] = rr[k]; }
+        const float is = iv;
+        if (r + stride < N) load(r + stride);
+        float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+        for (int k = 0; k < KD; ++k) {
+            const float gx = cg[k] * gm[k];
+            s1 += gx;
+            s2 += gx * cx[k];
+            dgam[k] += cg[k] * cx[k];
+            dbet[k] += cg[k];
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+            s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        }
+#pragma unroll
+        for (int k = 0; k < KD; ++k) {
+            const float gx = cg[k] * gm[k];
+            float d = is / D * (D * gx - s1 - cx[k] * s2);
+            if (R) d += cr[k];
+            out[(size_t)r * D + lane + 32 * k] = d;
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < KD; ++k) { red[warp][lane + 32 * k] = dgam[k]; red[warp][D + lane + 32 * k] = dbet[k]; }
+    __syncthreads();
+    for (int j = threadIdx.x; j < 2 * D; j += blockDim.x) {
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) s += red[w][j];
+        partial[(size_t)blockIdx.x * 2 * D + j] = s;
+    }
+}
+
+// Column sums over rows with a row stride, first stage: block (column tile, row chunk)
+// sums rows [r0, r1) of 128 (or 32) columns (8 row lanes, combined in order) into
+// part[chunk][col]; the step's deferred sums add the chunks in order.
+template <bool VEC>
+__global__ void __launch_bounds__(256) colsum_part_kernel(const float *__restrict__ dY, int rows, int ld, int chunks,
+                                                          float *__restrict__ part) {
+    // VEC: lane x takes 4 consecutive columns (one 16-byte load per row), a block 128
+    // columns; else one column per lane, 32 per block.  Row lane y adds rows r0 + y,
+    // r0 + y + 8, ... in order, four loads in flight; the 8 row lanes are then added
+    // in order (fixed order: deterministic).
+    constexpr int PER = VEC ? 4 : 1;
+    __shared__ float red[8][32 * PER + 1];
+    const int col = (blockIdx.x * 32 + threadIdx.x) * PER;
+    const int r0 = (int)((long long)rows * blockIdx.y / chunks), r1 = (int)((long long)rows * (blockIdx.y + 1) / chunks);
+    float acc[PER];
+#pragma unroll
+    for (int e = 0; e < PER; ++e) acc[e] = 0.0f;
+    if (col < ld) {
+        int r = r0 + threadIdx.y;
+        for (; r + 24 < r1; r += 32) {
+            float v[4][PER];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float *src = dY + (size_t)(r + 8 * u) * ld + col;
+                if constexpr (VEC) {
+                    const float4 q = __ldcs(reinterpret_cast<const float4 *>(src));
+                    v[u][0] = q.x; v[u][1 % PER] = q.y; v[u][2 % PER] = q.z; v[u][3 % PER] = q.w;
+                } else {
+                    v[u][0] = __ldcs(src);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int e = 0; e < PER; ++e) acc[e] += v[u][e];
+        }
+        for (; r < r1; r += 8) {
+            const float *src = dY + (size_t)r * ld + col;
+            if constexpr (VEC) {
+                const float4 q = __ldcs(reinterpret_cast<const float4 *>(src));
+                acc[0] += q.x; acc[1 % PER] += q.y; acc[2 % PER] += q.z; acc[3 % PER] += q.w;
+            } else {
+                acc[0] += __ldcs(src);
+            }
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < PER; ++e) red[threadIdx.y][threadIdx.x * PER + e] = acc[e];
+    __syncthreads();
+    const int t = threadIdx.y * 32 + threadIdx.x;   // one output column per thread
+    if (t < 32 * PER) {
+        const int c = blockIdx.x * 32 * PER + t;
+        if (c < ld) {
+            float s = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) s += red[k][t];
+            part[(size_t)blockIdx.y * ld + c] = s;
+        }
     }
 }
 
@@ -606,8 +712,44 @@ __global__ void __launch_bounds__(256) attn_bwd_kernel(const float *__restrict__
 // part[chunk][v][d] = sum over the chunk's rows with token v of g[row][d].  Pass 2 (with
 // the step's deferred sums): dTok[v][d] = the chunk partials in chunk order, dPos[t][d] =
 // sum over sequences of g[b*T + t][d] (positions past the sequence length: zero).
-constexpr int kEmbChunk = 256;
+constexpr int kEmbChunk = 64;
 
+// Pass 1 when a chunk's [V][D] sums fit in shared memory: thread d walks the chunk's
+// rows in order, eight rows' loads in flight, and adds g[row][d] into sums[token][d]
+// (a thread owns column d of every token, so nothing races); then the block writes its
+// [V][D] partial.  Token ids outside [0, V) add nothing.
+__global__ void __launch_bounds__(128) embed_tok_rows_kernel(const float *__restrict__ g,
+                                                             const float *__restrict__ tokens,
+                                                             float *__restrict__ part, int N, int D, int V) {
+    extern __shared__ float sums[];   // [V][D]
+    for (int i = threadIdx.x; i < V * D; i += blockDim.x) sums[i] = 0.0f;
+    __syncthreads();
+    const int r0 = blockIdx.x * kEmbChunk, r1 = min(N, r0 + kEmbChunk);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        int r = r0;
+        for (; r + 8 <= r1; r += 8) {
+            float v[8];
+            int t[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                t[u] = (int)__ldg(tokens + r + u);
+                v[u] = __ldcs(g + (size_t)(r + u) * D + d);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if ((unsigned)t[u] < (unsigned)V) sums[t[u] * D + d] += v[u];
+        }
+        for (; r < r1; ++r) {
+            const int t = (int)__ldg(tokens + r);
+            if ((unsigned)t < (unsigned)V) sums[t * D + d] += g[(size_t)r * D + d];
+        }
+    }
+    __syncthreads();
+    float *dst = part + (size_t)blockIdx.x * V * D;
+    for (int i = threadIdx.x; i < V * D; i += blockDim.x) dst[i] = sums[i];
+}
+
+// Pass 1 for a vocabulary too large for that: thread (v, d) scans the chunk's ids.
 __global__ void __launch_bounds__(256) embed_tok_partial_kernel(const float *__restrict__ g,
                                                                 const float *__restrict__ tokens,
                                                                 float *__restrict__ part, int N, int D, int V) {
@@ -714,8 +856,11 @@ int ln_bwd(LmEngine &e, const float *gout, const float *xh, const float *inv, co
     const int warps = 8;
     float *part = red_take(e, (size_t)e.ln_blocks * 2 * e.D);
     if (!part) return fail(kBadArg, "lm: split-sum scratch exhausted");
-    ln_bwd_kernel<<<e.ln_blocks, warps * 32, (size_t)warps * 2 * e.D * sizeof(float), stream()>>>(
-        gout, xh, inv, gam, R, out, part, e.N, e.D);
+    if (e.D == 128)
+        ln_bwd_reg_kernel<4><<<e.ln_blocks, warps * 32, 0, stream()>>>(gout, xh, inv, gam, R, out, part, e.N);
+    else
+        ln_bwd_kernel<<<e.ln_blocks, warps * 32, (size_t)warps * 2 * e.D * sizeof(float), stream()>>>(
+            gout, xh, inv, gam, R, out, part, e.N, e.D);
     ZB_LAUNCH_CHECK("lm layernorm backward");
     return red_push(e, part, 2 * e.D, e.ln_blocks, 1, 2 * e.D, e.D, 2 * e.D, dg, db, nullptr);
 }
@@ -724,14 +869,16 @@ int ln_bwd(LmEngine &e, const float *gout, const float *xh, const float *inv, co
 // about two blocks per SM now, the chunks in order with the step's deferred sums), into
 // segments of sw columns.
 int colsum(LmEngine &e, const float *dY, int rows, int ld, int sw, float *o0, float *o1 = nullptr, float *o2 = nullptr) {
-    const int tiles = (ld + 31) / 32;
+    const bool vec = ld % 4 == 0 && (reinterpret_cast<uintptr_t>(dY) & 15) == 0;
+    const int tiles = vec ? (ld + 127) / 128 : (ld + 31) / 32;
     int chunks = sm_count() * 2 / tiles;
     if (chunks > rows / 32) chunks = rows / 32;
     if (chunks > kColsumChunks) chunks = kColsumChunks;
     if (chunks < 1) chunks = 1;
     float *part = red_take(e, (size_t)chunks * ld);
     if (!part) return fail(kBadArg, "lm: split-sum scratch exhausted");
-    colsum_part_kernel<<<dim3(tiles, chunks), dim3(32, 8), 0, stream()>>>(dY, rows, ld, chunks, part);
+    if (vec) colsum_part_kernel<true><<<dim3(tiles, chunks), dim3(32, 8), 0, stream()>>>(dY, rows, ld, chunks, part);
+    else colsum_part_kernel<false><<<dim3(tiles, chunks), dim3(32, 8), 0, stream()>>>(dY, rows, ld, chunks, part);
     ZB_LAUNCH_CHECK("lm column sums (chunks)");
     return red_push(e, part, ld, chunks, 1, ld, sw, ld, o0, o1, o2);   // the chunks in order, deferred
 }
@@ -1212,8 +1359,12 @@ int lm_step(Net &n, const float *tokens, const float *targets, float *loss_out) 
         prof_mark(n, "qkv_ln1_bwd");
     }
     const int chunks = (N + kEmbChunk - 1) / kEmbChunk;
-    embed_tok_partial_kernel<<<dim3((V * D + 255) / 256, chunks), 256, 0, stream()>>>(e.g, tokens, e.emb_partial,
-                                                                                    N, D, V);
+    const size_t emb_smem = (size_t)V * D * sizeof(float);
+    if (emb_smem <= 48 * 1024)
+        embed_tok_rows_kernel<<<chunks, 128, emb_smem, stream()>>>(e.g, tokens, e.emb_partial, N, D, V);
+    else
+        embed_tok_partial_kernel<<<dim3((V * D + 255) / 256, chunks), 256, 0, stream()>>>(e.g, tokens, e.emb_partial,
+                                                                                        N, D, V);
     ZB_LAUNCH_CHECK("lm embedding backward (partials)");
     // token rows: the chunk partials in order; positions: the sequences' rows in order (positions
     // past the sequence length get zero)

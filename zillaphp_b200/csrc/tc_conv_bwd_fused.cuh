@@ -20,12 +20,14 @@
 // mask reads are done (two arrivals).
 //
 // The input gradient runs as Z[i][dw][ci] = sum_dh sum_co dY[i + dh*Wp][co]
-// Wd[dh][dw][ci][co]: per kernel row dh and K16 step, three MMAs (dw = 0, 1, 2;
-// N = CX each) share one A descriptor, kept in the tensor core's collector
-// buffer, so shared memory serves the dY operand 12 times per tile instead of
-// 36; the epilogue adds dX[i] = Z[i][0] + Z[i+1][1] + Z[i+2][2] with warp
-// shuffles (a warp is one tile row, and the columns c + dw of a real output
-// stay inside it).
+// Wd[dh][dw][ci][co]: per kernel row dh and K16 step, ONE MMA with N = 3 * CX
+// (the weight blocks of taps (dh, 0), (dh, 1), (dh, 2) lie back to back in
+// shared memory, so one B descriptor covers the three columns dw), 12 MMAs
+// per tile instead of 36 with N = CX; the epilogue adds
+// dX[i] = Z[i][0] + Z[i+1][1] + Z[i+2][2] with warp shuffles (a warp is one
+// tile row, and the columns c + dw of a real output stay inside it).  The
+// MMAs come from one thread, whose issue rate bounds this kernel, so fewer,
+// wider MMAs are what count.
 //
 // TMEM: the input gradient in two 128 x 3*CX accumulators (double-buffered: the
 // epilogue of tile i overlaps the MMAs of tile i+1), the weight gradient in one
@@ -150,7 +152,7 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
     int *armed = const_cast<int *>(abort_flag) + 1;   // [NS]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    constexpr uint32_t IDESC_DX = idesc_bf16(128, CX, false, false);
+    constexpr uint32_t IDESC_DX = idesc_bf16(128, 3 * CX, false, false);   // N = the three columns dw
     constexpr uint32_t IDESC_DW = idesc_bf16(CY, CX, true, true);
     const int my_tiles = p.num_tiles > (int)blockIdx.x ? (p.num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
@@ -250,8 +252,9 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
                     tc_fence_after();
                     const uint64_t st16 = (uint64_t)((uint32_t)(s * STAGE) >> 4);
                     // input gradient: Z[i][dw][ci] = sum_dh dY[i + dh*Wp] Wd[dh][dw] (3 kernel rows x
-                    // CY/16 K16 steps x the 3 columns dw, N = CX each); the three MMAs of a (dh, K16)
-                    // step share A, which stays in the collector buffer.  The epilogue forms
+                    // CY/16 K16 steps).  The weight blocks of taps (dh, 0..2) lie back to back in
+                    // shared memory, so one MMA with N = 3 * CX takes all three columns dw into
+                    // accumulator columns dw * CX + ci.  The epilogue forms
                     // dX[i] = sum_dw Z[i + dw][dw] (a shift along the tile row).
                     const uint32_t d = tmem_base + (uint32_t)(acc * S::ZCOLS);
 #pragma unroll
@@ -260,14 +263,8 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
 #pragma unroll
                         for (int k = 0; k < CY / 16; ++k) {
                             const uint64_t ad = a_dh + (uint64_t)(2 * k * reg16);
-#pragma unroll
-                            for (int dw = 0; dw < 3; ++dw) {
-                                const uint64_t bd = dx_b0 + (uint64_t)((uint32_t)((dh * 3 + dw) * S::WBLK + k * 32) >> 4);
-                                const uint32_t dt = d + (uint32_t)(dw * CX);
-                                if (dw == 0) mma_bf16_ca<0>(dt, ad, bd, IDESC_DX, (dh | k) != 0);
-                                else if (dw == 1) mma_bf16_ca<1>(dt, ad, bd, IDESC_DX, (dh | k) != 0);
-                                else mma_bf16_ca<2>(dt, ad, bd, IDESC_DX, (dh | k) != 0);
-                            }
+                            const uint64_t bd = dx_b0 + (uint64_t)((uint32_t)(dh * 3 * S::WBLK + k * 32) >> 4);
+                            mma_bf16(d, ad, bd, IDESC_DX, (dh | k) != 0);
                         }
                     }
                     mma_commit(&acc_full[acc]);

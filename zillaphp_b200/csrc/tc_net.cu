@@ -15,6 +15,7 @@
 //   -> fc1 dX, fc1 dW -> unpool3 -> conv3 dX, conv3 dW -> unpool2
 //   -> conv2 dX (x ReLU mask of conv1) , conv2 dW -> conv1 dW -> Adam/SGD
 #include <math.h>
+#include <algorithm>
 #include <string.h>
 
 #include <string>
@@ -109,7 +110,7 @@ constexpr int kMaxPack = 8;
 struct PackJobs {
     PackJob j[kMaxPack];
     int count;
-    int conv_blocks;   // blocks [0, conv_blocks) take the jobs above; the rest pack `fc`
+    int conv_blocks;   // pack_kernel's grid: conv_blocks for the jobs above + blocks for `fc`
     PackJob fc;        // the hidden Linear weight's rows (n = 0: none)
 };
 
@@ -134,11 +135,10 @@ constexpr int kHeadGroup = 98;
 // NHWC feature index of the conv output.  Four consecutive n per thread: one
 // 16-byte load (N % 64 == 0; four loads if W is not 16-byte aligned), one
 // 8-byte store.  J: src W, dst wP, a = F, b = N, C/H/W the flatten geometry.
-__device__ __forceinline__ void pack_fc_rows(const PackJob &J, int block, int nblocks) {
+__device__ __forceinline__ void pack_fc_rows(const PackJob &J, long long t, long long nt) {
     const int n4 = J.b / 4;
     const bool vec = (reinterpret_cast<uintptr_t>(J.src) & 15) == 0;
-    for (long long q = (long long)block * blockDim.x + threadIdx.x; q < (long long)J.a * n4;
-         q += (long long)nblocks * blockDim.x) {
+    for (long long q = t; q < (long long)J.a * n4; q += nt) {
         const int k = (int)(q / n4), c4 = (int)(q % n4);
         const float *src = J.src + (size_t)nhwc_to_nchw(k, J.C, J.H, J.W) * J.b + 4 * c4;
         const float4 v = vec ? __ldg(reinterpret_cast<const float4 *>(src)) : make_float4(src[0], src[1], src[2], src[3]);
@@ -150,22 +150,15 @@ __device__ __forceinline__ void pack_fc_rows(const PackJob &J, int block, int nb
     }
 }
 
-// Every bf16 operand copy of the step from the fp32 master weights, in one
-// launch: the conv weights in their forward / input-gradient layouts and the
-// direct classifier's grouped layout (blocks [0, conv_blocks)), and the hidden
-// Linear weight's rows (the other blocks).
-__global__ void __launch_bounds__(256) pack_kernel(const __grid_constant__ PackJobs jobs) {
-    griddep_launch();
-    griddep_wait();
-    if ((int)blockIdx.x >= jobs.conv_blocks) {
-        pack_fc_rows(jobs.fc, (int)blockIdx.x - jobs.conv_blocks, (int)gridDim.x - jobs.conv_blocks);
-        return;
-    }
-    const int stride = jobs.conv_blocks * blockDim.x;
+// Every bf16 operand copy of the step from the fp32 master weights: the conv
+// weights in their forward / input-gradient layouts, the direct classifier's
+// grouped layout, and the hidden Linear weight's rows.  Thread t of nt takes
+// elements t, t + nt, ... of each job.
+__device__ __forceinline__ void pack_span(const PackJobs &jobs, long long t, long long nt) {
     for (int ji = 0; ji < jobs.count; ++ji) {
         const PackJob &J = jobs.j[ji];
-        const int n = (int)J.n;
-        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        for (long long ii = t; ii < J.n; ii += nt) {
+            const int i = (int)ii;
             float v;
             if (J.kind == 4) {   // i = k * NC + n over the classifier weight [F][NC]
                 const int n = i % J.b, k = i / J.b;
@@ -174,16 +167,33 @@ __global__ void __launch_bounds__(256) pack_kernel(const __grid_constant__ PackJ
                 continue;
             }
             if (J.kind == 0) {
-                const int ci = i % J.b, r = i / J.b, co = r % J.a, t = r / J.a;
-                v = J.src[(co * J.b + ci) * 9 + t];
+                const int ci = i % J.b, r = i / J.b, co = r % J.a, tp = r / J.a;
+                v = J.src[(co * J.b + ci) * 9 + tp];
             } else {
-                const int co = i % J.a, r = i / J.a, ci = r % J.b, t = r / J.b;
-                v = J.src[(co * J.b + ci) * 9 + (8 - t)];
+                const int co = i % J.a, r = i / J.a, ci = r % J.b, tp = r / J.b;
+                v = J.src[(co * J.b + ci) * 9 + (8 - tp)];
             }
             J.dst[i] = __float2bfloat16_rn(v);
         }
     }
+    if (jobs.fc.n) pack_fc_rows(jobs.fc, t, nt);
 }
+
+// The packing as a launch of its own (engines whose first conv is not the
+// tensor-core kernel, which otherwise does it: PackWork).
+__global__ void __launch_bounds__(256) pack_kernel(const __grid_constant__ PackJobs jobs) {
+    griddep_launch();
+    griddep_wait();
+    pack_span(jobs, (long long)blockIdx.x * blockDim.x + threadIdx.x, (long long)gridDim.x * blockDim.x);
+}
+
+// The packing as side work of the first conv's tensor-core kernel: its CTAs
+// run it once before their tiles, so it costs no launch of its own (the conv
+// reads the fp32 weights; every reader of the bf16 copies runs after it).
+struct PackWork {
+    PackJobs jobs;
+    __device__ void operator()(long long t, long long nt) const { pack_span(jobs, t, nt); }
+};
 
 // First conv (CIN = 1, 3x3, stride 1, pad P) + bias + ReLU on CUDA cores,
 // NHWC bf16 output; with `pool`, 2x2 max-pool + codes instead (same rules as
@@ -711,11 +721,17 @@ __global__ void unpool_kernel(const bf16 *__restrict__ dP, const uint8_t *__rest
 //   dA = dz W^T times (a > 0) (ReLU of the previous Linear) -> bf16
 // Block partials (fixed warp order): dW [Hd][NC], db [NC], dbPrev [Hd], and
 // the block's loss sum (one more element, summed by the same reduction).
-template <int HD, int NC>
-__global__ void __launch_bounds__(256) head_kernel(const bf16 *__restrict__ a, const float *__restrict__ Wt,
+// With SPLIT the previous Linear split its K: a[r][k] is taken here as
+// bf16(relu(sum_s fpart[s][r][k] + fbias[k])), the splits added in order from
+// split 0 (the split-K reduction's own arithmetic, so the values are the same),
+// and written to `a` for later readers.
+template <int HD, int NC, bool SPLIT = false>
+__global__ void __launch_bounds__(256) head_kernel(bf16 *__restrict__ a, const float *__restrict__ Wt,
                                                    const float *__restrict__ bias, const float *__restrict__ y,
                                                    bf16 *__restrict__ dA, double *__restrict__ row_loss,
-                                                   float *__restrict__ partial, int B, float invB) {
+                                                   float *__restrict__ partial, int B, float invB,
+                                                   const float *__restrict__ fpart, int ksplit,
+                                                   const float *__restrict__ fbias) {
     constexpr int KPL = HD / 32;   // inputs per lane
     __shared__ float sW[HD * NC];
     __shared__ float sAcc[HD * NC + NC + HD];
@@ -739,8 +755,31 @@ __global__ void __launch_bounds__(256) head_kernel(const bf16 *__restrict__ a, c
     for (int n = 0; n < NC; ++n) gB[n] = 0.0f;
     for (int r = blockIdx.x * 8 + warp; r < B; r += gridDim.x * 8) {
         float av[KPL];
+        if constexpr (SPLIT) {
+            const float *pr = fpart + (size_t)r * HD + lane;
+            const size_t sstride = (size_t)B * HD;
 #pragma unroll
-        for (int j = 0; j < KPL; ++j) av[j] = __bfloat162float(a[(size_t)r * HD + lane + 32 * j]);
+            for (int j = 0; j < KPL; ++j) av[j] = __ldcs(pr + 32 * j);
+#pragma unroll 4
+            for (int sp = 1; sp < ksplit; ++sp) {
+                float v[KPL];
+#pragma unroll
+                for (int j = 0; j < KPL; ++j) v[j] = __ldcs(pr + sp * sstride + 32 * j);
+#pragma unroll
+                for (int j = 0; j < KPL; ++j) av[j] += v[j];
+            }
+#pragma unroll
+            for (int j = 0; j < KPL; ++j) {
+                const int k = lane + 32 * j;
+                const float x = av[j] + fbias[k];
+                const bf16 h = __float2bfloat16_rn(x > 0.0f ? x : 0.0f);
+                a[(size_t)r * HD + k] = h;
+                av[j] = __bfloat162float(h);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < KPL; ++j) av[j] = __bfloat162float(a[(size_t)r * HD + lane + 32 * j]);
+        }
         float z[NC];
 #pragma unroll
         for (int n = 0; n < NC; ++n) {
@@ -1158,7 +1197,8 @@ struct ReduceJobs {
 // warp order (a fixed order: deterministic).  A job whose length is a multiple
 // of 4 (16-byte aligned splits) takes 128 elements per block, four consecutive
 // per lane (one 16-byte load: a warp reads 512 contiguous bytes of a split,
-// four splits in flight); any other job 32, one per lane.
+// eight splits in flight while at least 64 remain, then four); any other job
+// 32, one per lane.  The adds run in split order either way.
 __global__ void __launch_bounds__(256) reduce_multi4_kernel(const __grid_constant__ ReduceJobs J) {
     griddep_launch();
     griddep_wait();
@@ -1175,6 +1215,13 @@ __global__ void __launch_bounds__(256) reduce_multi4_kernel(const __grid_constan
         if (q < n4) {
             const float4 *p = reinterpret_cast<const float4 *>(r.partial) + q;
             int k = w;
+            for (; k + 56 < r.splits; k += 64) {   // eight loads in flight per lane
+                float4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = __ldcg(p + (size_t)(k + 8 * u) * n4);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) { s.x += v[u].x; s.y += v[u].y; s.z += v[u].z; s.w += v[u].w; }
+            }
             for (; k + 24 < r.splits; k += 32) {
                 const float4 a = __ldcg(p + (size_t)k * n4), b = __ldcg(p + (size_t)(k + 8) * n4);
                 const float4 c = __ldcg(p + (size_t)(k + 16) * n4), d = __ldcg(p + (size_t)(k + 24) * n4);
@@ -1563,13 +1610,17 @@ int reduce_multi(const ReduceArgs *jobs, int count) {
     if (count < 1 || count > kMaxReduceJobs) return fail(kBadArg, "reduce_multi: %d jobs", count);
     ReduceJobs J{};
     J.count = count;
+    // the deepest job first: its blocks (the longest) start in the first wave
+    int order[kMaxReduceJobs];
+    for (int j = 0; j < count; ++j) order[j] = j;
+    std::stable_sort(order, order + count, [&](int a, int b) { return jobs[a].splits > jobs[b].splits; });
     int total = 0;
     for (int j = 0; j < count; ++j) {
-        J.job[j] = jobs[j];
+        J.job[j] = jobs[order[j]];
         J.start[j] = total;
         // 16-byte loads: a partial vector a multiple of 4 long (16-byte aligned splits)
-        J.vec[j] = jobs[j].n % 4 == 0 && (reinterpret_cast<uintptr_t>(jobs[j].partial) & 15) == 0;
-        total += (int)(J.vec[j] ? (jobs[j].n / 4 + 31) / 32 : (jobs[j].n + 31) / 32);
+        J.vec[j] = J.job[j].n % 4 == 0 && (reinterpret_cast<uintptr_t>(J.job[j].partial) & 15) == 0;
+        total += (int)(J.vec[j] ? (J.job[j].n / 4 + 31) / 32 : (J.job[j].n + 31) / 32);
     }
     J.start[count] = total;
     launch_pdl(reduce_multi4_kernel, dim3(total), dim3(256), 0, J);
@@ -1986,7 +2037,7 @@ int tc_build(Net &n, TcEngine &e) {
     } else {
         e.views.push_back({"head.dz", e.dz, (size_t)B * e.NC, 2});
     }
-    // conv weight packing jobs (the hidden Linear weight has its own kernel)
+    // bf16 weight packing jobs (the hidden Linear weight's rows: `fc`)
     PackJobs &pj = e.pack;
     pj.count = 0;
     for (auto &L : e.convs) {
@@ -2012,9 +2063,13 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
     const int B = e.B;
     auto &st = n.st;
     int rc;
-    // ---- pack bf16 operands from the fp32 master
-    launch_pdl(pack_kernel, dim3(e.pack_grid), dim3(256), 0, e.pack);
-    ZB_LAUNCH_CHECK("pack");
+    // ---- pack bf16 operands from the fp32 master: inside the first conv's kernel when that is
+    // the tensor-core one (the "pack" group is then empty), else a launch of its own
+    const bool c1_tc = e.C1 == 32 && !e.c1_pool && e.pad1 == 1 && e.H1 == e.H0 && e.W1 == e.W0;
+    if (!c1_tc) {
+        launch_pdl(pack_kernel, dim3(e.pack_grid), dim3(256), 0, e.pack);
+        ZB_LAUNCH_CHECK("pack");
+    }
     prof_mark(n, "pack");
     // ---- forward
     const Stage &s1 = st[e.c1_si];
@@ -2027,13 +2082,12 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
         if (!e.c1_pool && (e.H0 + 2 * e.pad1) * (e.W0 + 2 * e.pad1) > kStageRegs * 256)
             return fail(kBadArg, "tc engine: first-conv image too large (padded %d x %d)", e.H0 + 2 * e.pad1,
                         e.W0 + 2 * e.pad1);
-        const bool same = e.pad1 == 1 && e.H1 == e.H0 && e.W1 == e.W0;   // 3x3, pad 1
-        if (e.C1 == 32 && !e.c1_pool && same) {
-            // tensor cores: one 128 x 32 x 32 MMA per 128 output pixels
+        if (c1_tc) {   // 3x3, pad 1, same size
+            // tensor cores: one 128 x 32 x 32 MMA per 128 output pixels; the CTAs also pack
             const long long tiles = (pix + 127) / 128;
             const int g = tiles < (long long)sm_count() * 8 ? (int)tiles : sm_count() * 8;
-            launch_pdl(tc::conv_first_tc_kernel<32>, dim3(g), dim3(128), tc::ConvFirstTcShape<32>::SMEM, x, w1, b1,
-                       e.a1, B, e.H0, e.W0, device_error_word());
+            launch_pdl(tc::conv_first_tc_kernel<32, PackWork>, dim3(g), dim3(128), tc::ConvFirstTcShape<32>::SMEM, x,
+                       w1, b1, e.a1, B, e.H0, e.W0, device_error_word(), PackWork{e.pack});
         } else if (e.C1 == 32 && !e.c1_pool) conv_first_fwd_img_kernel<32><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
         else if (e.C1 == 32 && xsm <= 48 * 1024) conv_first_pool_img_kernel<32><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
         else if (e.C1 == 32) conv_first_fwd_kernel<32, true><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
@@ -2089,9 +2143,11 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
         prof_mark(n, "linear_bwd");
     } else if (e.fc_fwd.ksplit > 1) {
         if ((rc = launch_gemm<128, tc::kGemmPartial, 6, true>(e.fc_fwd))) return rc;
-        ReduceArgs r{e.fc_fwd_partial, e.fc_fwd.ksplit, (long long)B * e.HD, 6, B, e.HD, 0, 0, 0, 0,
-                     nullptr, nullptr, nullptr, e.fc_fwd.bias, e.a_hid};
-        if ((rc = reduce(r))) return rc;
+        if (logits_out) {   // (a training step's head kernel sums the splits itself)
+            ReduceArgs r{e.fc_fwd_partial, e.fc_fwd.ksplit, (long long)B * e.HD, 6, B, e.HD, 0, 0, 0, 0,
+                         nullptr, nullptr, nullptr, e.fc_fwd.bias, e.a_hid};
+            if ((rc = reduce(r))) return rc;
+        }
     } else if ((rc = launch_gemm<128, tc::kGemmBiasRelu, 6, true>(e.fc_fwd))) {
         return rc;
     }
@@ -2122,8 +2178,14 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
     float *gW5 = n.grads + sh.poff, *gb5 = gW5 + sh.pn_w;
     const Stage &sd = st[e.hid_si];
     float *gW4 = n.grads + sd.poff, *gb4 = gW4 + sd.pn_w;
-    launch_pdl(head_kernel<256, 10>, dim3(e.head_grid), dim3(256), 0, e.a_hid, n.params + sh.poff,
-               n.params + sh.poff + sh.pn_w, y, e.dZ_hid, e.row_loss, e.head_partial, B, 1.0f / (float)B);
+    if (e.fc_fwd.ksplit > 1)   // the hidden Linear's split-K sum, bias and ReLU in the head
+        launch_pdl(head_kernel<256, 10, true>, dim3(e.head_grid), dim3(256), 0, e.a_hid, n.params + sh.poff,
+                   n.params + sh.poff + sh.pn_w, y, e.dZ_hid, e.row_loss, e.head_partial, B, 1.0f / (float)B,
+                   (const float *)e.fc_fwd_partial, e.fc_fwd.ksplit, (const float *)e.fc_fwd.bias);
+    else
+        launch_pdl(head_kernel<256, 10>, dim3(e.head_grid), dim3(256), 0, e.a_hid, n.params + sh.poff,
+                   n.params + sh.poff + sh.pn_w, y, e.dZ_hid, e.row_loss, e.head_partial, B, 1.0f / (float)B,
+                   (const float *)nullptr, 0, (const float *)nullptr);
     ZB_LAUNCH_CHECK("head");
     {   // fc2 dW, db, fc1 db and the loss sum (the blocks' partials, in block order): nothing reads
         // them before the optimizer unless an all-reduce bucket or the mid-step exchange takes them

@@ -771,7 +771,7 @@ __global__ void __launch_bounds__(256) embed_tok_partial_kernel(const float *__r
 // 128 elements per block (vec: 32 lanes x 4 consecutive elements, one 16-byte load per split)
 // or 32 (one element per lane); warp w adds splits w, w + 8, ... in order, then the eight warp
 // sums of each element are added in warp order (fixed order: deterministic).
-__global__ void __launch_bounds__(256) lm_reduce_all_kernel(const __grid_constant__ LmRedJobs J) {
+__global__ void __launch_bounds__(256, 4) lm_reduce_all_kernel(const __grid_constant__ LmRedJobs J) {
     int j = 0;
     while (j + 1 < J.count && (int)blockIdx.x >= J.start[j + 1]) ++j;
     const LmRedJob &r = J.j[j];

@@ -715,136 +715,166 @@ __global__ void unpool_kernel(const bf16 *__restrict__ dP, const uint8_t *__rest
     }
 }
 
+// A head block's partial: dW [Hd][NC], db [NC], dbPrev [Hd], the loss, then zeros up to a
+// multiple of 4 floats (16-byte aligned rows for the split reduction's vector loads).
+__host__ __device__ constexpr int head_pstride(int HD, int NC) { return (HD * NC + NC + HD + 1 + 3) / 4 * 4; }
+
 // Head: last Linear (Hd -> NC, NC <= 32) + softmax cross-entropy + the start
 // of the backward, one warp per row:
 //   z = a W + b;  loss_r = -log softmax(z)[y];  dz = (p - onehot)/B
 //   dA = dz W^T times (a > 0) (ReLU of the previous Linear) -> bf16
-// Block partials (fixed warp order): dW [Hd][NC], db [NC], dbPrev [Hd], and
-// the block's loss sum (one more element, summed by the same reduction).
+// The rows' a and dz are staged in shared memory, kHeadRpw rows per warp at a
+// time; after each such chunk thread k adds, over the chunk's rows in order
+// (warp 0's rows first), dW[k][n] += a[k] dz[n], dA[k] = (a[k] > 0) sum_n dz[n] W[k][n]
+// (written out, and added into dbPrev[k]) and, for k < NC, db[k] += dz[k].  So no
+// thread holds more than NC + 2 accumulators.  Block partial: dW [Hd][NC], db [NC],
+// dbPrev [Hd] and the block's loss sum (warps in order).
 // With SPLIT the previous Linear split its K: a[r][k] is taken here as
 // bf16(relu(sum_s fpart[s][r][k] + fbias[k])), the splits added in order from
 // split 0 (the split-K reduction's own arithmetic, so the values are the same),
 // and written to `a` for later readers.
+constexpr int kHeadRpw = 4;
 template <int HD, int NC, bool SPLIT = false>
-__global__ void __launch_bounds__(256) head_kernel(bf16 *__restrict__ a, const float *__restrict__ Wt,
-                                                   const float *__restrict__ bias, const float *__restrict__ y,
-                                                   bf16 *__restrict__ dA, double *__restrict__ row_loss,
-                                                   float *__restrict__ partial, int B, float invB,
-                                                   const float *__restrict__ fpart, int ksplit,
-                                                   const float *__restrict__ fbias) {
+__global__ void __launch_bounds__(256, 2) head_kernel(bf16 *__restrict__ a, const float *__restrict__ Wt,
+                                                      const float *__restrict__ bias, const float *__restrict__ y,
+                                                      bf16 *__restrict__ dA, double *__restrict__ row_loss,
+                                                      float *__restrict__ partial, int B, float invB,
+                                                      const float *__restrict__ fpart, int ksplit,
+                                                      const float *__restrict__ fbias) {
+    static_assert(HD == 256, "one thread per input of the previous Linear");
     constexpr int KPL = HD / 32;   // inputs per lane
+    constexpr int SLOTS = 8 * kHeadRpw;
     __shared__ float sW[HD * NC];
-    __shared__ float sAcc[HD * NC + NC + HD];
-    __shared__ double sLoss;
+    __shared__ bf16 sA[SLOTS][HD];
+    __shared__ float sDz[SLOTS][NC];
+    __shared__ double sLoss[8];
     griddep_launch();
     griddep_wait();
     for (int i = threadIdx.x; i < HD * NC; i += blockDim.x) sW[i] = Wt[i];
-    for (int i = threadIdx.x; i < HD * NC + NC + HD; i += blockDim.x) sAcc[i] = 0.0f;
-    if (threadIdx.x == 0) sLoss = 0.0;
     double lsum = 0.0;   // lane 0: this warp's rows' loss
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float gW[KPL][NC], gB[NC], gP[KPL];
+    const int t = threadIdx.x;   // the post-pass: input k = t
+    float gW[NC], gP = 0.0f, gB = 0.0f;
 #pragma unroll
-    for (int j = 0; j < KPL; ++j) {
-        gP[j] = 0.0f;
+    for (int n = 0; n < NC; ++n) gW[n] = 0.0f;
+    const long long step = (long long)gridDim.x * 8;
+    for (long long base = (long long)blockIdx.x * 8; base < B; base += step * kHeadRpw) {
+        // row loop: this warp's rows base + warp + i * step, i < kHeadRpw
+        for (int i = 0; i < kHeadRpw; ++i) {
+            const long long rr = base + warp + i * step;
+            const int slot = warp * kHeadRpw + i;
+            if (rr >= B) {
+                if (lane < NC) sDz[slot][lane] = 0.0f;
 #pragma unroll
-        for (int n = 0; n < NC; ++n) gW[j][n] = 0.0f;
-    }
+                for (int j = 0; j < KPL; ++j) sA[slot][lane + 32 * j] = __float2bfloat16_rn(0.0f);
+                continue;
+            }
+            const int r = (int)rr;
+            float av[KPL];
+            if constexpr (SPLIT) {
+                const float *pr = fpart + (size_t)r * HD + lane;
+                const size_t sstride = (size_t)B * HD;
 #pragma unroll
-    for (int n = 0; n < NC; ++n) gB[n] = 0.0f;
-    for (int r = blockIdx.x * 8 + warp; r < B; r += gridDim.x * 8) {
-        float av[KPL];
-        if constexpr (SPLIT) {
-            const float *pr = fpart + (size_t)r * HD + lane;
-            const size_t sstride = (size_t)B * HD;
-#pragma unroll
-            for (int j = 0; j < KPL; ++j) av[j] = __ldcs(pr + 32 * j);
+                for (int j = 0; j < KPL; ++j) av[j] = __ldcs(pr + 32 * j);
 #pragma unroll 4
-            for (int sp = 1; sp < ksplit; ++sp) {
-                float v[KPL];
+                for (int sp = 1; sp < ksplit; ++sp) {
+                    float v[KPL];
 #pragma unroll
-                for (int j = 0; j < KPL; ++j) v[j] = __ldcs(pr + sp * sstride + 32 * j);
+                    for (int j = 0; j < KPL; ++j) v[j] = __ldcs(pr + sp * sstride + 32 * j);
 #pragma unroll
-                for (int j = 0; j < KPL; ++j) av[j] += v[j];
+                    for (int j = 0; j < KPL; ++j) av[j] += v[j];
+                }
+#pragma unroll
+                for (int j = 0; j < KPL; ++j) {
+                    const int k = lane + 32 * j;
+                    const float x = av[j] + fbias[k];
+                    const bf16 h = __float2bfloat16_rn(x > 0.0f ? x : 0.0f);
+                    a[(size_t)r * HD + k] = h;
+                    sA[slot][k] = h;
+                    av[j] = __bfloat162float(h);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < KPL; ++j) {
+                    const bf16 h = a[(size_t)r * HD + lane + 32 * j];
+                    sA[slot][lane + 32 * j] = h;
+                    av[j] = __bfloat162float(h);
+                }
             }
-#pragma unroll
-            for (int j = 0; j < KPL; ++j) {
-                const int k = lane + 32 * j;
-                const float x = av[j] + fbias[k];
-                const bf16 h = __float2bfloat16_rn(x > 0.0f ? x : 0.0f);
-                a[(size_t)r * HD + k] = h;
-                av[j] = __bfloat162float(h);
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < KPL; ++j) av[j] = __bfloat162float(a[(size_t)r * HD + lane + 32 * j]);
-        }
-        float z[NC];
-#pragma unroll
-        for (int n = 0; n < NC; ++n) {
-            float s = 0.0f;
-#pragma unroll
-            for (int j = 0; j < KPL; ++j) s = fmaf(av[j], sW[(lane + 32 * j) * NC + n], s);
-#pragma unroll
-            for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-            z[n] = s + bias[n];
-        }
-        float mx = z[0];
-#pragma unroll
-        for (int n = 1; n < NC; ++n) mx = fmaxf(mx, z[n]);
-        float se = 0.0f;
-#pragma unroll
-        for (int n = 0; n < NC; ++n) se += expf(z[n] - mx);
-        const int t = (int)y[r];
-        float dz[NC];
-#pragma unroll
-        for (int n = 0; n < NC; ++n) {
-            const float p = expf(z[n] - mx) / se;
-            dz[n] = (p - (n == t ? 1.0f : 0.0f)) * invB;
-            gB[n] += dz[n];
-        }
-        if (lane == 0) {
-            float pt = 0.0f;
-#pragma unroll
-            for (int n = 0; n < NC; ++n) if (n == t) pt = expf(z[n] - mx) / se;
-            row_loss[r] = -(double)logf(pt);
-            lsum += -(double)logf(pt);
-        }
-#pragma unroll
-        for (int j = 0; j < KPL; ++j) {
-            const int k = lane + 32 * j;
-            float g = 0.0f;
+            float z[NC];
 #pragma unroll
             for (int n = 0; n < NC; ++n) {
-                g = fmaf(dz[n], sW[k * NC + n], g);
-                gW[j][n] = fmaf(av[j], dz[n], gW[j][n]);
+                float s = 0.0f;
+#pragma unroll
+                for (int j = 0; j < KPL; ++j) s = fmaf(av[j], sW[(lane + 32 * j) * NC + n], s);
+#pragma unroll
+                for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+                z[n] = s + bias[n];
             }
-            g = av[j] > 0.0f ? g : 0.0f;
-            gP[j] += g;
-            dA[(size_t)r * HD + k] = __float2bfloat16_rn(g);
-        }
-    }
-    for (int wv = 0; wv < 8; ++wv) {   // fixed warp order
-        if (warp == wv) {
+            float mx = z[0];
 #pragma unroll
-            for (int j = 0; j < KPL; ++j) {
-                const int k = lane + 32 * j;
+            for (int n = 1; n < NC; ++n) mx = fmaxf(mx, z[n]);
+            float se = 0.0f;
 #pragma unroll
-                for (int n = 0; n < NC; ++n) sAcc[k * NC + n] += gW[j][n];
-                sAcc[HD * NC + NC + k] += gP[j];
+            for (int n = 0; n < NC; ++n) se += expf(z[n] - mx);
+            const int tg = (int)y[r];
+            float dz[NC];
+#pragma unroll
+            for (int n = 0; n < NC; ++n) {
+                const float p = expf(z[n] - mx) / se;
+                dz[n] = (p - (n == tg ? 1.0f : 0.0f)) * invB;
+            }
+            if (lane < NC) {
+                float v = dz[0];
+#pragma unroll
+                for (int n = 1; n < NC; ++n) if (n == lane) v = dz[n];
+                sDz[slot][lane] = v;
             }
             if (lane == 0) {
+                float pt = 0.0f;
 #pragma unroll
-                for (int n = 0; n < NC; ++n) sAcc[HD * NC + n] += gB[n];
-                sLoss += lsum;
+                for (int n = 0; n < NC; ++n) if (n == tg) pt = expf(z[n] - mx) / se;
+                row_loss[r] = -(double)logf(pt);
+                lsum += -(double)logf(pt);
             }
         }
         __syncthreads();
+        // post-pass over the chunk's rows in slot order (rows past B hold zeros): thread t
+        // takes input k = t of every row, and writes the row's dA[k] (coalesced rows)
+        float wk[NC];
+#pragma unroll
+        for (int n = 0; n < NC; ++n) wk[n] = sW[t * NC + n];
+        for (int sl = 0; sl < SLOTS; ++sl) {
+            const float av = __bfloat162float(sA[sl][t]);
+            float g = 0.0f;
+#pragma unroll
+            for (int n = 0; n < NC; ++n) {
+                const float d = sDz[sl][n];
+                gW[n] = fmaf(av, d, gW[n]);
+                g = fmaf(d, wk[n], g);
+            }
+            g = av > 0.0f ? g : 0.0f;
+            gP += g;
+            if (t < NC) gB += sDz[sl][t];
+            const long long rr = base + (sl / kHeadRpw) + (long long)(sl % kHeadRpw) * step;
+            if (rr < B) dA[(size_t)rr * HD + t] = __float2bfloat16_rn(g);
+        }
+        __syncthreads();
     }
-    float *dst = partial + (size_t)blockIdx.x * (HD * NC + NC + HD + 1);
-    for (int i = threadIdx.x; i < HD * NC + NC + HD; i += blockDim.x) dst[i] = sAcc[i];
-    if (threadIdx.x == 0) dst[HD * NC + NC + HD] = (float)sLoss;
+    if (lane == 0) sLoss[warp] = lsum;
+    __syncthreads();
+    float *dst = partial + (size_t)blockIdx.x * head_pstride(HD, NC);
+#pragma unroll
+    for (int n = 0; n < NC; ++n) dst[t * NC + n] = gW[n];
+    if (t < NC) dst[HD * NC + t] = gB;
+    dst[HD * NC + NC + t] = gP;
+    if (t == 0) {
+        double ls = 0.0;
+        for (int w = 0; w < 8; ++w) ls += sLoss[w];
+        dst[HD * NC + NC + HD] = (float)ls;
+    }
+    for (int i = HD * NC + NC + HD + 1 + t; i < head_pstride(HD, NC); i += blockDim.x) dst[i] = 0.0f;
 }
 
 // Forward-only classifier (evaluation): one warp per row, fp32 logits
@@ -1140,7 +1170,7 @@ __global__ void __launch_bounds__(256) head_direct_wgrad_kernel(const bf16 *__re
 // map 0: dst[i];  1 conv (M=COUT rows, N = 9*CIN, n = tap*CIN + ci) -> dst[(co*CIN+ci)*9+tap]
 //        2 conv (M = 9*CIN rows (tap*CIN+ci), N = COUT)  -> same dst layout
 //        3 linear (M = F rows in NHWC order, N = OUT)    -> dst[nchw(m)*OUT + n]
-//        4 head partial [HD*NC | NC | HD | 1] -> dW5, db5, db4, loss (four destinations)
+//        4 head partial [HD*NC | NC | HD | 1 | padding] -> dW5, db5, db4, loss (four destinations)
 //        5 first conv [COUT][10] -> dW1[co*9+t], db1[co]
 //        6 fc1 forward split-K: relu(s + bias) -> bf16
 //        7 only the last element, into *dst4 (a loss behind zero partials)
@@ -1199,7 +1229,7 @@ struct ReduceJobs {
 // per lane (one 16-byte load: a warp reads 512 contiguous bytes of a split,
 // eight splits in flight while at least 64 remain, then four); any other job
 // 32, one per lane.  The adds run in split order either way.
-__global__ void __launch_bounds__(256) reduce_multi4_kernel(const __grid_constant__ ReduceJobs J) {
+__global__ void __launch_bounds__(256, 4) reduce_multi4_kernel(const __grid_constant__ ReduceJobs J) {
     griddep_launch();
     griddep_wait();
     int j = 0;
@@ -1240,6 +1270,13 @@ __global__ void __launch_bounds__(256) reduce_multi4_kernel(const __grid_constan
         if (i < r.n) {
             const float *p = r.partial + i;
             int k = w;
+            for (; k + 56 < r.splits; k += 64) {   // eight loads in flight per lane
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = __ldcg(p + (size_t)(k + 8 * u) * r.n);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) s.x += v[u];
+            }
             for (; k + 8 < r.splits; k += 16) {
                 const float a = __ldcg(p + (size_t)k * r.n), b = __ldcg(p + (size_t)(k + 8) * r.n);
                 s.x += a;
@@ -1304,7 +1341,7 @@ __device__ void r_store(const ReduceArgs &r, long long i, float s) {
             if (i < hdnc) r.dst[i] = s;
             else if (i < hdnc + r.N) r.dst2[i - hdnc] = s;
             else if (i < hdnc + r.N + r.M) r.dst3[i - hdnc - r.N] = s;
-            else *r.dst4 = s;
+            else if (i == hdnc + r.N + r.M) *r.dst4 = s;   // (the elements after it are padding)
             break;
         }
         case 5: { const int co = (int)(i / 10), t = (int)(i % 10); if (t < 9) r.dst[co * 9 + t] = s; else r.dst2[co] = s; break; }
@@ -1998,7 +2035,7 @@ int tc_build(Net &n, TcEngine &e) {
     if (!e.direct_head) {
         e.head_grid = (B + 7) / 8;
         if (e.head_grid > sm_count() * 2) e.head_grid = sm_count() * 2;
-        if ((rc = dalloc(e, &e.head_partial, (size_t)e.head_grid * (e.HD * e.NC + e.NC + e.HD + 1)))) return rc;
+        if ((rc = dalloc(e, &e.head_partial, (size_t)e.head_grid * head_pstride(e.HD, e.NC)))) return rc;
     }
     if ((rc = dalloc(e, &e.row_loss, (size_t)B))) return rc;
     e.c1_wgrad_grid = sm_count() * 2;   // the resident blocks (two per SM): each walks whole images
@@ -2190,7 +2227,7 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
     {   // fc2 dW, db, fc1 db and the loss sum (the blocks' partials, in block order): nothing reads
         // them before the optimizer unless an all-reduce bucket or the mid-step exchange takes them
         // first, so they join the fused phase's reduction launch
-        ReduceArgs r{e.head_partial, e.head_grid, (long long)e.HD * e.NC + e.NC + e.HD + 1, 4, e.HD, e.NC, 0, 0, 0, 0,
+        ReduceArgs r{e.head_partial, e.head_grid, (long long)head_pstride(e.HD, e.NC), 4, e.HD, e.NC, 0, 0, 0, 0,
                      gW5, gb5, gb4};
         r.dst4 = loss_out;
         const bool hold_head = hold_ok && (n.world <= 1 || n.peer.in_step) && r.splits >= 32 && r.n <= 131072;

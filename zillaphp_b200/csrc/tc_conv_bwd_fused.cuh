@@ -54,9 +54,15 @@
 // 32); at the end D1's hi rows (+ bias) and lo rows go out as two [32][10]
 // partials per CTA, which the deterministic split reduction adds.
 //
-// The nine weight-gradient MMAs of a K16 step share A (the dY rows): the first
-// fills the tensor core's collector buffer with it and the other eight read it
-// from there, so shared memory serves A once per step instead of nine times.
+// X is loaded three times per stage, the copies one and two columns further
+// on (TMA boxes starting at columns -1, 0, +1; zero fill outside the image),
+// at a uniform pitch after the first: so one MN-major B descriptor with N =
+// 3 * CX starting at kernel row dh covers the taps (dh, 0), (dh, 1), (dh, 2),
+// and the weight gradient takes 3 MMAs (M = CY, N = 96) per K16 step instead
+// of 9 (N = CX), into accumulator columns (dh * 3 + dw) * CX + ci.
+// The three weight-gradient MMAs of a K16 step share A (the dY rows): the first
+// fills the tensor core's collector buffer with it and the other two read it
+// from there, so shared memory serves A once per step instead of three times.
 // Every MMA of the CTA comes from the one MMA thread, so nothing else is issued
 // between them.
 //
@@ -103,6 +109,7 @@ struct ConvBwdFusedShape {
     static constexpr int THREADS = UP ? 448 : 320;
     static constexpr int NTOT = 9 * CX;
     static constexpr int DYG = CY / 8, XG = CX / 8;
+    static constexpr int XCOPY = 3;                      // X at column offsets 0, +1, +2
     static constexpr int WROWB = CY * 2;                 // dgrad weight row: 128 B (CY = 64)
     static constexpr int WBLK = CX * WROWB;              // one tap
     static constexpr int WTOTAL = 9 * WBLK;
@@ -115,7 +122,7 @@ struct ConvBwdFusedShape {
     static __host__ __device__ int region(int R, int Wp) { return ((R + 2) * Wp * 16 + 127) / 128 * 128; }
     static __host__ __device__ int dy_region(int R, int Wp) { return region(R, Wp) + (UP ? 16 : 0); }
     static __host__ __device__ int x_off(int R, int Wp) { return (DYG * dy_region(R, Wp) + 127) / 128 * 128; }
-    static __host__ __device__ int stage_bytes(int R, int Wp) { return (x_off(R, Wp) + XG * region(R, Wp) + 1023) / 1024 * 1024; }
+    static __host__ __device__ int stage_bytes(int R, int Wp) { return (x_off(R, Wp) + XCOPY * XG * region(R, Wp) + 1023) / 1024 * 1024; }
     static __host__ __device__ int out_tile_bytes(int R, int W) { return (R * W * CX * 2 + 1023) / 1024 * 1024; }
     static __host__ __device__ int x9_bytes(int R, int W) { return C1 ? (R * W * 128 + 1023) / 1024 * 1024 : 0; }
     static __host__ __device__ int smem(int R, int Wp, int W) {
@@ -153,7 +160,7 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr uint32_t IDESC_DX = idesc_bf16(128, 3 * CX, false, false);   // N = the three columns dw
-    constexpr uint32_t IDESC_DW = idesc_bf16(CY, CX, true, true);
+    constexpr uint32_t IDESC_DW = idesc_bf16(CY, 3 * CX, true, true);   // N = the taps (dh, 0..2)
     const int my_tiles = p.num_tiles > (int)blockIdx.x ? (p.num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
     for (int i = threadIdx.x; i < (NS * STAGE + S::SLACK) / 16; i += blockDim.x)
@@ -190,7 +197,7 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
             prefetch_tmap(&p.out_map);
             mbar_arrive_expect_tx(wbar, S::WTOTAL);
             for (int t = 0; t < 9; ++t) tma_load_3d(sW + t * S::WBLK, &p.w_map, wbar, 0, 0, t);
-            const uint32_t tx = (uint32_t)(((UP ? 0 : S::DYG) + S::XG) * (p.R + 2) * p.Wp * 16);
+            const uint32_t tx = (uint32_t)(((UP ? 0 : S::DYG) + S::XCOPY * S::XG) * (p.R + 2) * p.Wp * 16);
             int s = 0;
             uint32_t ph = 0;
             for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
@@ -203,8 +210,10 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
                 if (!UP)
                     for (int g = 0; g < S::DYG; ++g)
                         tma_load_4d(st + g * p.dy_region, &p.dy_map, &full[s], 8 * g, -1, h0 - 1, b);
-                for (int g = 0; g < S::XG; ++g)
-                    tma_load_4d(st + p.x_off + g * p.region, &p.x_map, &full[s], 8 * g, -1, h0 - 1, b);
+                for (int c = 0; c < S::XCOPY; ++c)   // X, then the copies one and two columns on
+                    for (int g = 0; g < S::XG; ++g)
+                        tma_load_4d(st + p.x_off + (c * S::XG + g) * p.region, &p.x_map, &full[s], 8 * g, c - 1,
+                                    h0 - 1, b);
                 if (++s == NS) { s = 0; ph ^= 1u; }
             }
             if (*abort_flag) {
@@ -269,21 +278,21 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
                     }
                     mma_commit(&acc_full[acc]);
                     if (++acc == 2) { acc = 0; acc_ph ^= 1u; }
-                    // weight gradient: 8 K16 steps (128 pixel rows) x 9 taps; the 9 MMAs of a
+                    // weight gradient: 8 K16 steps (128 pixel rows) x 3 kernel rows (N = the three
+                    // taps of the row, from the X copies); the 3 MMAs of a
                     // K16 step share A (dY), which stays in the collector buffer after the
                     // first, so shared memory serves it once instead of nine times
                     const uint64_t a_dy = dw_a0 + st16 + (uint64_t)(wp + 1);
 #pragma unroll 1
                     for (int k = 0; k < 8; ++k) {
+                        const uint64_t ad = a_dy + (uint64_t)(16 * k);
 #pragma unroll
-                        for (int tap = 0; tap < 9; ++tap) {
-                            const int dh = tap / 3, dw = tap - 3 * dh;
-                            const uint32_t dt = tmem_base + (uint32_t)(S::WG_COL0 + tap * CX);
-                            const uint64_t ad = a_dy + (uint64_t)(16 * k);
-                            const uint64_t bd = dw_b0 + st16 + (uint64_t)(dh * wp + dw + 16 * k);
-                            if (tap == 0) mma_bf16_ca<0>(dt, ad, bd, IDESC_DW, (n | k) != 0);
-                            else if (tap == 8) mma_bf16_ca<2>(dt, ad, bd, IDESC_DW, (n | k) != 0);
-                            else mma_bf16_ca<1>(dt, ad, bd, IDESC_DW, (n | k) != 0);
+                        for (int dh = 0; dh < 3; ++dh) {
+                            const uint32_t dt = tmem_base + (uint32_t)(S::WG_COL0 + dh * 3 * CX);
+                            const uint64_t bd = dw_b0 + st16 + (uint64_t)(dh * wp + 16 * k);
+                            if (dh == 0) mma_bf16_ca<0>(dt, ad, bd, IDESC_DW, (n | k) != 0);
+                            else if (dh == 1) mma_bf16_ca<1>(dt, ad, bd, IDESC_DW, (n | k) != 0);
+                            else mma_bf16_ca<2>(dt, ad, bd, IDESC_DW, (n | k) != 0);
                         }
                     }
                     issued = true;

@@ -1557,8 +1557,8 @@ int launch_wgrad_halo(const WgradHaloParams &p0, int grid) {
 
 template <bool C1, bool UP>
 int launch_conv_bwd_fused(const ConvLayer &L, const float *x0, const bf16 *dp) {
-    using S = tc::ConvBwdFusedShape<32, 64, 3, C1, UP>;
-    auto kern = tc::conv_bwd_fused_kernel<32, 64, 3, C1, UP>;
+    using S = tc::ConvBwdFusedShape<32, 64, 2, C1, UP>;   // two stages: each holds X three times
+    auto kern = tc::conv_bwd_fused_kernel<32, 64, 2, C1, UP>;
     ConvBwdFusedParams p = L.fbwd;
     p.region = S::region(p.R, p.Wp);
     p.dy_region = S::dy_region(p.R, p.Wp);

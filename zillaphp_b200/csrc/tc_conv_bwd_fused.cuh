@@ -279,9 +279,9 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
                     mma_commit(&acc_full[acc]);
                     if (++acc == 2) { acc = 0; acc_ph ^= 1u; }
                     // weight gradient: 8 K16 steps (128 pixel rows) x 3 kernel rows (N = the three
-                    // taps of the row, from the X copies); the 3 MMAs of a
-                    // K16 step share A (dY), which stays in the collector buffer after the
-                    // first, so shared memory serves it once instead of nine times
+                    // taps of the row, from the X copies); the 3 MMAs of a K16 step share A (dY),
+                    // which stays in the collector buffer after the first, so shared memory
+                    // serves it once instead of three times
                     const uint64_t a_dy = dw_a0 + st16 + (uint64_t)(wp + 1);
 #pragma unroll 1
                     for (int k = 0; k < 8; ++k) {
@@ -322,23 +322,33 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
         float bsum[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) bsum[e] = 0.0f;
+        // an item's window (pooled row prow of the tile's four, column pw) and its halo offset do
+        // not depend on the tile: worked out once (wi = prow * Wo + pw)
+        int wi_[4], prow_[4], soff_[4];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            const int i = bt + 128 * m;
+            wi_[m] = i >> 3;
+            prow_[m] = i < nitems ? wi_[m] / Wo : -2;   // -2: no item
+            const int pw = wi_[m] - (i < nitems ? prow_[m] : 0) * Wo;
+            soff_[m] = ((2 * prow_[m] - 1) * p.Wp + 2 * pw + 1) * 16;   // halo row 2 prow - 1, column 2 pw + 1
+        }
         int s = 0;
         uint32_t ph = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
             const int b = tile / p.tiles_per_img;
             const int h0 = (tile - b * p.tiles_per_img) * p.R;
             // this tile's dP and code loads go out before the stage wait
+            const long long wbase = ((long long)b * Ho + (h0 >> 1) - 1) * Wo;   // window (phr = h0/2 - 1, 0)
             uint4 pv[4];
             uint2 cd[4];
 #pragma unroll
             for (int m = 0; m < 4; ++m) {
-                const int i = bt + 128 * m;
-                const int wi = i >> 3, prow = wi / Wo, pw = wi - prow * Wo;
-                const int phr = (h0 >> 1) - 1 + prow;   // pooled row
+                const int phr = (h0 >> 1) - 1 + prow_[m];   // pooled row
                 pv[m] = make_uint4(0, 0, 0, 0);
                 cd[m] = make_uint2(0, 0);
-                if (i < nitems && (unsigned)phr < (unsigned)Ho) {
-                    const size_t o = (((size_t)b * Ho + phr) * Wo + pw) * CY + 8 * g;
+                if (prow_[m] >= 0 && (unsigned)phr < (unsigned)Ho) {
+                    const size_t o = (size_t)(wbase + wi_[m]) * CY + 8 * g;
                     pv[m] = __ldg(reinterpret_cast<const uint4 *>(p.dp + o));
                     cd[m] = __ldg(reinterpret_cast<const uint2 *>(p.code + o));
                 }
@@ -347,9 +357,8 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
             uint8_t *st = sA + s * STAGE + g * p.dy_region;
 #pragma unroll
             for (int m = 0; m < 4; ++m) {
-                const int i = bt + 128 * m;
-                if (i >= nitems) continue;
-                const int wi = i >> 3, prow = wi / Wo, pw = wi - prow * Wo;
+                const int prow = prow_[m];
+                if (prow < 0) continue;
                 // selector nibbles = the 8 codes (values 0..7)
                 const uint32_t t0 = cd[m].x | (cd[m].x >> 4), t1 = cd[m].y | (cd[m].y >> 4);
                 const uint32_t sel0 = (t0 & 0xFFu) | ((t0 >> 8) & 0xFF00u);
@@ -360,7 +369,7 @@ __global__ void __launch_bounds__(UP ? 448 : 320, 1) conv_bwd_fused_kernel(const
                 for (int kh = 0; kh < 2; ++kh) {
                     const int hr = hr0 + kh;
                     if (hr < 0 || hr > p.R + 1) continue;
-                    uint8_t *rowp = st + (hr * p.Wp + 2 * pw + 1) * 16;
+                    uint8_t *rowp = st + soff_[m] + kh * p.Wp * 16;
 #pragma unroll
                     for (int kw = 0; kw < 2; ++kw)
                         *reinterpret_cast<uint4 *>(rowp + kw * 16) =

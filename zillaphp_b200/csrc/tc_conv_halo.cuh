@@ -269,20 +269,28 @@ __global__ void __launch_bounds__(UP ? 448 : 320, UP ? 1 : 2) conv_halo_kernel(c
         for (int kb = 0; kb < KS; ++kb)
 #pragma unroll
             for (int e = 0; e < 8; ++e) bsum[kb][e] = 0.0f;
+        // an item's window (pooled row prow of the tile's, column pw) does not depend on the
+        // tile or the stage: worked out once (window index (bt + 128 m) / NC8 = prow * Wo + pw;
+        // prow -2: no item)
+        int prow_[4];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            const int i = bt + 128 * m;
+            prow_[m] = i < nitems ? (i / S::NC8) / Wo : -2;
+        }
         // this thread's dP and code loads of stage kb of `tile` (zero past the image / the tiles)
         auto load_stage = [&](int tile, int kb, uint4 (&pv)[4], uint2 (&cd)[4]) {
             const int b = tile / p.tiles_per_img;
             const int h0 = (tile - b * p.tiles_per_img) * p.R;
             const int ch = (kb * S::NC8 + g) * 8;
+            const long long wbase = ((long long)b * Ho + (h0 >> 1) - 1) * Wo;   // window (h0/2 - 1, 0)
 #pragma unroll
             for (int m = 0; m < 4; ++m) {
-                const int i = bt + 128 * m;
-                const int wi = i / S::NC8, prow = wi / Wo, pw = wi - prow * Wo;
-                const int phr = (h0 >> 1) - 1 + prow;
+                const int phr = (h0 >> 1) - 1 + prow_[m];
                 pv[m] = make_uint4(0, 0, 0, 0);
                 cd[m] = make_uint2(0, 0);
-                if (tile < p.num_tiles && i < nitems && (unsigned)phr < (unsigned)Ho) {
-                    const size_t o = (((size_t)b * Ho + phr) * Wo + pw) * CIN + ch;
+                if (tile < p.num_tiles && prow_[m] >= 0 && (unsigned)phr < (unsigned)Ho) {
+                    const size_t o = (size_t)(wbase + (bt + 128 * m) / S::NC8) * CIN + ch;
                     pv[m] = __ldg(reinterpret_cast<const uint4 *>(p.dp + o));
                     cd[m] = __ldg(reinterpret_cast<const uint2 *>(p.up_code + o));
                 }
@@ -303,9 +311,8 @@ __global__ void __launch_bounds__(UP ? 448 : 320, UP ? 1 : 2) conv_halo_kernel(c
                 uint8_t *st = sA + s * STAGE + g * p.region;
 #pragma unroll
                 for (int m = 0; m < 4; ++m) {
-                    const int i = bt + 128 * m;
-                    if (i >= nitems) continue;
-                    const int wi = i / S::NC8, prow = wi / Wo, pw = wi - prow * Wo;
+                    const int prow = prow_[m], pw = (bt + 128 * m) / S::NC8 - prow * Wo;
+                    if (prow < 0) continue;
                     const uint32_t t0 = cd[m].x | (cd[m].x >> 4), t1 = cd[m].y | (cd[m].y >> 4);
                     const uint32_t sel0 = (t0 & 0xFFu) | ((t0 >> 8) & 0xFF00u);
                     const uint32_t sel1 = (t1 & 0xFFu) | ((t1 >> 8) & 0xFF00u);
@@ -368,6 +375,15 @@ __global__ void __launch_bounds__(UP ? 448 : 320, UP ? 1 : 2) conv_halo_kernel(c
         constexpr int OCT = COUT / 8;           // channel octets per pixel
         const int Wo = p.W >> 1, Ho = p.H >> 1;
         const int nitems = (p.R >> 1) * Wo * OCT;
+        // pool items etid and etid + 256 (thread = (window, channel octet)): their window's
+        // pooled row and column within the tile, worked out once (later items, if any, per tile)
+        int ipr[2], ipc[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int wi = (etid + 256 * j) / OCT;
+            ipr[j] = wi / Wo;
+            ipc[j] = wi - ipr[j] * Wo;
+        }
         __nv_bfloat16 *sbuf = reinterpret_cast<__nv_bfloat16 *>(stage);
         int acc = 0, sb = 0;
         uint32_t acc_ph = 0;
@@ -419,9 +435,17 @@ __global__ void __launch_bounds__(UP ? 448 : 320, UP ? 1 : 2) conv_halo_kernel(c
                 }
                 named_bar_sync(2, 256);
                 // thread = (window, channel octet), octets fastest: four pixels x 8 channels
-                for (int idx = etid; idx < nitems; idx += 256) {
-                    const int wi = idx / OCT, o = idx - wi * OCT;
-                    const int pr = wi / Wo, pc = wi - pr * Wo;
+                for (int idx = etid, j = 0; idx < nitems; idx += 256, ++j) {
+                    const int o = idx % OCT;
+                    int pr, pc;
+                    if (j < 2) {
+                        pr = j == 0 ? ipr[0] : ipr[1];
+                        pc = j == 0 ? ipc[0] : ipc[1];
+                    } else {
+                        const int wi = idx / OCT;
+                        pr = wi / Wo;
+                        pc = wi - pr * Wo;
+                    }
                     const int ho = (h0 >> 1) + pr;
                     if (ho >= Ho) continue;
                     const int r0 = (2 * pr) * p.Wp + 2 * pc;

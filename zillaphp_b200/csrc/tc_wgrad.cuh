@@ -228,19 +228,27 @@ __global__ void __launch_bounds__(UP ? 320 : 192, 1) wgrad_tc_kernel(const __gri
         const int o = bt & 15;              // channel octet (of 16) of every item of this thread
         const int Ho = p.H >> 1, Wo = p.W >> 1;
         const int nitems = (p.R >> 1) * Wo * 16;
+        // an item's window (pooled row prow of the stage's, column pw) does not depend on the
+        // stage: worked out once (wi = prow * Wo + pw; prow -1: no item)
+        int wi_[4], prow_[4];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            const int i = bt + 128 * m;
+            wi_[m] = i >> 4;
+            prow_[m] = i < nitems ? wi_[m] / Wo : -1;
+        }
         // this thread's dP and code loads of stage st (zero past the image)
         auto load_stage = [&](int st, uint4 (&pv)[4], uint2 (&cd)[4]) {
             const int img = k0 + st / p.tiles_per_img;
             const int h0 = (st % p.tiles_per_img) * p.R;
+            const long long wbase = ((long long)img * Ho + (h0 >> 1)) * Wo;   // window (h0/2, 0)
 #pragma unroll
             for (int m = 0; m < 4; ++m) {
-                const int i = bt + 128 * m;
-                const int wi = i >> 4, prow = wi / Wo, pw = wi - prow * Wo;
-                const int phr = (h0 >> 1) + prow;
+                const int phr = (h0 >> 1) + prow_[m];
                 pv[m] = make_uint4(0, 0, 0, 0);
                 cd[m] = make_uint2(0, 0);
-                if (st < nstages && i < nitems && phr < Ho) {
-                    const size_t off = (((size_t)img * Ho + phr) * Wo + pw) * 128 + 8 * o;
+                if (st < nstages && prow_[m] >= 0 && phr < Ho) {
+                    const size_t off = (size_t)(wbase + wi_[m]) * 128 + 8 * o;
                     pv[m] = __ldg(reinterpret_cast<const uint4 *>(p.dp + off));
                     cd[m] = __ldg(reinterpret_cast<const uint2 *>(p.up_code + off));
                 }
@@ -257,9 +265,8 @@ __global__ void __launch_bounds__(UP ? 320 : 192, 1) wgrad_tc_kernel(const __gri
             uint8_t *sa = sbase + s * STAGE + (o >> 3) * ABOX;   // box of channels 64 (o / 8) ..
 #pragma unroll
             for (int m = 0; m < 4; ++m) {
-                const int i = bt + 128 * m;
-                if (i >= nitems) continue;
-                const int wi = i >> 4, prow = wi / Wo, pw = wi - prow * Wo;
+                const int prow = prow_[m], pw = wi_[m] - prow * Wo;
+                if (prow < 0) continue;
                 const uint32_t t0 = cd[m].x | (cd[m].x >> 4), t1 = cd[m].y | (cd[m].y >> 4);
                 const uint32_t sel0 = (t0 & 0xFFu) | ((t0 >> 8) & 0xFF00u);
                 const uint32_t sel1 = (t1 & 0xFFu) | ((t1 >> 8) & 0xFF00u);

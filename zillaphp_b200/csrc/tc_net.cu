@@ -276,6 +276,24 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
 // global-load latency overlaps the compute.
 constexpr int kStageRegs = 4;
 
+// Asynchronous staging of one image into a zero-padded shared-memory buffer:
+// element i of the [H][W] image goes to ((i / W) + pad) * (W + 2 pad) + (i % W) + pad
+// by a 4-byte cp.async (the halo is never written, so it stays zero).  The
+// coordinates advance by 256 elements per step (no division in the loop).
+__device__ __forceinline__ void stage_image_async(float *buf, const float *__restrict__ xb, int H, int W, int pad) {
+    const int PW = W + 2 * pad;
+    int ih = (int)threadIdx.x / W, iw = (int)threadIdx.x - ih * W;
+    const int dh = 256 / W, dw = 256 - dh * W;
+    for (int i = threadIdx.x; i < H * W; i += 256) {
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(buf + (ih + pad) * PW + iw + pad);
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(xb + i) : "memory");
+        ih += dh;
+        iw += dw;
+        if (iw >= W) { iw -= W; ++ih; }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
 struct ImageStager {
     int off[kStageRegs];
     float v[kStageRegs];
@@ -390,7 +408,7 @@ __global__ void __launch_bounds__(256, 2) conv_first_pool_img_kernel(const float
                                                                   int B, int H, int W, int pad) {
     constexpr int NQ = COUT / 8;
     constexpr int LANES = 256 / NQ;
-    extern __shared__ float xs[];
+    extern __shared__ float xbuf[];   // two zero-padded images: the next one lands while this one is used
     const int q = threadIdx.x % NQ, pl = threadIdx.x / NQ;
     const int oH = H + 2 * pad - 2, oW = W + 2 * pad - 2;
     const int pH = oH >> 1, pW = oW >> 1, NW = pH * pW;
@@ -403,14 +421,19 @@ __global__ void __launch_bounds__(256, 2) conv_first_pool_img_kernel(const float
         for (int t = 0; t < 9; ++t)
             wr2[k][t] = make_float2(__ldg(w + (8 * q + 2 * k) * 9 + t), __ldg(w + (8 * q + 2 * k + 1) * 9 + t));
     }
-    for (int b = blockIdx.x; b < B; b += gridDim.x) {
+    const int NPX = PH * PW;
+    for (int i = threadIdx.x; i < 2 * NPX; i += 256) xbuf[i] = 0.0f;
+    __syncthreads();
+    if ((int)blockIdx.x < B) stage_image_async(xbuf, x + (size_t)blockIdx.x * H * W, H, W, pad);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    int it = 0;
+    for (int b = blockIdx.x; b < B; b += gridDim.x, ++it) {
+        const int nb = b + (int)gridDim.x;
+        if (nb < B) stage_image_async(xbuf + ((it + 1) & 1) * NPX, x + (size_t)nb * H * W, H, W, pad);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");   // this image's copies are done
         __syncthreads();
-        const float *xb = x + (size_t)b * H * W;
-        for (int i = threadIdx.x; i < PH * PW; i += 256) {
-            const int ih = i / PW - pad, iw = i - (i / PW) * PW - pad;
-            xs[i] = ((unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W) ? __ldg(xb + ih * W + iw) : 0.0f;
-        }
-        __syncthreads();
+        const float *xs = xbuf + (it & 1) * NPX;
         for (int wi = pl; wi < NW; wi += LANES) {
             const int ph = wi / pW, pw = wi - ph * pW;
             const float *xr = xs + (2 * ph) * PW + 2 * pw;
@@ -449,7 +472,9 @@ __global__ void __launch_bounds__(256, 2) conv_first_pool_img_kernel(const float
             *reinterpret_cast<uint4 *>(out + o) = pk;
             *reinterpret_cast<uint2 *>(code + o) = cp;
         }
+        __syncthreads();   // every thread is done with this buffer before it is refilled
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // First-conv weight and bias gradient: dW[co][t] = sum_p dC[p][co] x[p + t],
@@ -580,7 +605,7 @@ __global__ void __launch_bounds__(256, 2) conv_first_wgrad_pool_kernel(const bf1
                                                                     int pad) {
     constexpr int NQ = COUT / 8;
     constexpr int LANES = 256 / NQ;
-    extern __shared__ float xs[];
+    extern __shared__ float xbuf[];   // two zero-padded images: the next one lands while this one is used
     const int q = threadIdx.x % NQ, pl = threadIdx.x / NQ;
     const int oH = H + 2 * pad - 2, oW = W + 2 * pad - 2;
     const int Ho = oH >> 1, Wo = oW >> 1, NW = Ho * Wo;
@@ -590,14 +615,19 @@ __global__ void __launch_bounds__(256, 2) conv_first_wgrad_pool_kernel(const bf1
     for (int e = 0; e < 8; ++e)
 #pragma unroll
         for (int t = 0; t < 10; ++t) acc[e][t] = 0.0f;
-    for (int b = blockIdx.x; b < B; b += gridDim.x) {
+    const int NPX = PH * PW;
+    for (int i = threadIdx.x; i < 2 * NPX; i += 256) xbuf[i] = 0.0f;
+    __syncthreads();
+    if ((int)blockIdx.x < B) stage_image_async(xbuf, x + (size_t)blockIdx.x * H * W, H, W, pad);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    int it = 0;
+    for (int b = blockIdx.x; b < B; b += gridDim.x, ++it) {
+        const int nb = b + (int)gridDim.x;
+        if (nb < B) stage_image_async(xbuf + ((it + 1) & 1) * NPX, x + (size_t)nb * H * W, H, W, pad);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");   // this image's copies are done
         __syncthreads();
-        const float *xb = x + (size_t)b * H * W;
-        for (int i = threadIdx.x; i < PH * PW; i += 256) {
-            const int ih = i / PW - pad, iw = i - (i / PW) * PW - pad;
-            xs[i] = ((unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W) ? __ldg(xb + ih * W + iw) : 0.0f;
-        }
-        __syncthreads();
+        const float *xs = xbuf + (it & 1) * NPX;
         const size_t ob = (size_t)b * NW * COUT + 8 * q;
         for (int wi = pl; wi < NW; wi += LANES) {
             const int ph = wi / Wo, pw = wi - ph * Wo;
@@ -619,7 +649,9 @@ __global__ void __launch_bounds__(256, 2) conv_first_wgrad_pool_kernel(const bf1
                 acc[e][9] += g;
             }
         }
+        __syncthreads();   // every thread is done with this buffer before it is refilled
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     // lanes of a warp with the same octet: lane = window-slot * NQ + q
 #pragma unroll
     for (int off = NQ; off < 32; off <<= 1)
@@ -629,7 +661,7 @@ __global__ void __launch_bounds__(256, 2) conv_first_wgrad_pool_kernel(const bf1
             for (int t = 0; t < 10; ++t) acc[e][t] += __shfl_xor_sync(0xffffffffu, acc[e][t], off);
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float *red = xs;   // [8 warps][NQ][80]
+    float *red = xbuf;   // [8 warps][NQ][80]
     if (lane < NQ)
 #pragma unroll
         for (int e = 0; e < 8; ++e)
@@ -2094,6 +2126,21 @@ int tc_build(Net &n, TcEngine &e) {
     return kOk;
 }
 
+// Dynamic shared memory above the default 48 KB for `kern` (set once per kernel and size;
+// kernels of the same signature are told apart by their address).
+template <class K>
+int allow_smem(K *kern, size_t bytes) {
+    static std::vector<std::pair<const void *, size_t>> allowed;
+    if (bytes <= 48 * 1024) return kOk;
+    for (const auto &a : allowed)
+        if (a.first == (const void *)kern && bytes <= a.second) return kOk;
+    if (bytes > 227 * 1024) return fail(kBadArg, "tc engine: %zu bytes of shared memory needed", bytes);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
+        return check_cuda("dynamic shared memory attribute");
+    allowed.push_back({(const void *)kern, bytes});
+    return kOk;
+}
+
 // One training step, or (logits_out != null) the forward pass only: logits
 // [B][classes] fp32 and, with y, the loss sum; no gradients, no update.
 int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out, float *logits_out = nullptr) {
@@ -2126,10 +2173,16 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
             launch_pdl(tc::conv_first_tc_kernel<32, PackWork>, dim3(g), dim3(128), tc::ConvFirstTcShape<32>::SMEM, x,
                        w1, b1, e.a1, B, e.H0, e.W0, device_error_word(), PackWork{e.pack});
         } else if (e.C1 == 32 && !e.c1_pool) conv_first_fwd_img_kernel<32><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
-        else if (e.C1 == 32 && xsm <= 48 * 1024) conv_first_pool_img_kernel<32><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
+        else if (e.C1 == 32 && xsm <= 48 * 1024) {   // two image buffers
+            if ((rc = allow_smem(conv_first_pool_img_kernel<32>, 2 * xsm))) return rc;
+            conv_first_pool_img_kernel<32><<<gimg, 256, 2 * xsm, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
+        }
         else if (e.C1 == 32) conv_first_fwd_kernel<32, true><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
         else if (!e.c1_pool) conv_first_fwd_img_kernel<16><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, B, e.H0, e.W0, e.pad1);
-        else if (xsm <= 48 * 1024) conv_first_pool_img_kernel<16><<<gimg, 256, xsm, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
+        else if (xsm <= 48 * 1024) {
+            if ((rc = allow_smem(conv_first_pool_img_kernel<16>, 2 * xsm))) return rc;
+            conv_first_pool_img_kernel<16><<<gimg, 256, 2 * xsm, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
+        }
         else conv_first_fwd_kernel<16, true><<<grid, 128, 0, stream()>>>(x, w1, b1, e.a1, e.code1, B, e.H0, e.W0, e.pad1);
         ZB_LAUNCH_CHECK("conv_first_fwd");
         prof_mark(n, "conv_fwd");
@@ -2345,8 +2398,15 @@ int tc_run(Net &n, TcEngine &e, const float *x, const float *y, float *loss_out,
         if (smem > 48 * 1024) return fail(kBadArg, "tc engine: first-conv image too large for the weight-gradient kernel");
         const bool big = padded > kStageRegs * 256;   // past the register stager: a plain copy per image
         if (e.c1_pool) {   // straight from the pooled gradient and the codes: no unpooled dC1
-            if (e.C1 == 32) conv_first_wgrad_pool_kernel<32><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dP1, e.code1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
-            else conv_first_wgrad_pool_kernel<16><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dP1, e.code1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
+            // two image buffers (the reduction reuses the first)
+            const size_t psmem = (size_t)(2 * padded > 8 * 4 * 80 ? 2 * padded : 8 * 4 * 80) * sizeof(float);
+            if (e.C1 == 32) {
+                if ((rc = allow_smem(conv_first_wgrad_pool_kernel<32>, psmem))) return rc;
+                conv_first_wgrad_pool_kernel<32><<<e.c1_wgrad_grid, 256, psmem, stream()>>>(e.dP1, e.code1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
+            } else {
+                if ((rc = allow_smem(conv_first_wgrad_pool_kernel<16>, psmem))) return rc;
+                conv_first_wgrad_pool_kernel<16><<<e.c1_wgrad_grid, 256, psmem, stream()>>>(e.dP1, e.code1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
+            }
         }
         else if (e.C1 == 32 && !big) conv_first_wgrad_kernel<32><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);
         else if (e.C1 == 32) conv_first_wgrad_kernel<32, true><<<e.c1_wgrad_grid, 256, smem, stream()>>>(e.dC1, x, e.c1_partial, B, e.H0, e.W0, e.pad1);

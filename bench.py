@@ -797,6 +797,8 @@ def main_lm(args):
     lm_precision = args.precision or 0   # 1: the blocks' Linear layers on TF32 tensor cores
     net = LM(w, batch=b, precision=lm_precision)
     net.set_params(synthetic.lm_init_params(w))
+    if args.graph:
+        net.set_graph(True)
     if world > 1:
         obj = [dp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
@@ -955,7 +957,7 @@ def main_lm(args):
             "config": {"workload": w.name, "global_batch": batch, "per_gpu_batch": b, "seq_len": w.seq,
                        "tokens_per_s": round(value * w.seq, 1),
                        "step_tflops": round(total_flops * world / (ms / args.steps * 1e-3) / 1e12, 3),
-                       "parallelism": f"dp{world}",
+                       "parallelism": f"dp{world}", "cuda_graph": bool(args.graph),
                        "l2": "8 distinct token batches rotated; per-step activations (~300 MB) exceed the 126 MB L2",
                        "notes": w.notes},
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(b * w.seq * 8),

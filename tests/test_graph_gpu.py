@@ -15,7 +15,7 @@ import pytest
 import npref
 import oracle
 from zillaphp_b200 import configs, native, synthetic
-from zillaphp_b200.net import Net
+from zillaphp_b200.net import LM, Net
 
 pytestmark = pytest.mark.gpu
 
@@ -57,6 +57,40 @@ def test_graph_steps_match_plain_steps(name, precision, batch):
             rl = [ref.step(*batches[s % 2], w.optimizer, w.lr if s < 4 else w.lr * 0.5) for s in range(6)]
             assert all(abs(g - r) <= 1e-5 * abs(r) for g, r in zip(lb, rl)), (lb, rl)
             assert npref.normwise(b.params(), ref.params) < 1e-4
+    finally:
+        a.close()
+        b.close()
+
+
+@pytest.mark.parametrize("precision", [0, 1])
+def test_lm_graph_steps_match_plain_steps(precision):
+    """The language model's step replayed from a graph: losses, parameters and launch
+    counts equal to plain steps over six steps of two alternating token batches."""
+    w = configs.TRANSFORMER_LM
+    batch, seq = 8, 64
+    p0 = synthetic.lm_init_params(w, seed=13, perturb=0.1)
+    batches = [synthetic.lm_batch(w, batch, seq, seed=13, step=s) for s in range(2)]
+    lib = native.load()
+    a, b = LM(w, batch=batch, seq=seq, precision=precision), LM(w, batch=batch, seq=seq, precision=precision)
+    try:
+        a.set_params(p0)
+        b.set_params(p0)
+        b.set_graph(True)
+        la, lb, na, nb = [], [], [], []
+        for s in range(6):
+            tok, tgt = batches[s % 2]
+            c0 = lib.zilla_launch_count()
+            la.append(a.step_host(tok, tgt))
+            c1 = lib.zilla_launch_count()
+            lb.append(b.step_host(tok, tgt))
+            c2 = lib.zilla_launch_count()
+            na.append(c1 - c0)
+            nb.append(c2 - c1)
+        a.device_status()
+        b.device_status()
+        assert la == lb, (la, lb)
+        assert np.array_equal(a.params(), b.params()), "graph replays diverged from plain steps"
+        assert na == nb, (na, nb)
     finally:
         a.close()
         b.close()

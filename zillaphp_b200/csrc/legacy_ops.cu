@@ -128,7 +128,15 @@ __global__ void sum_rows_into_loss_kernel(const double *__restrict__ row_loss, i
     // contiguous chunk per thread, chunks combined in thread order
     const int per = (B + blockDim.x - 1) / blockDim.x;
     const int b0 = threadIdx.x * per, b1 = min(B, b0 + per);
-    for (int r = b0; r < b1; ++r) acc += row_loss[r];
+    int r = b0;
+    for (; r + 8 <= b1; r += 8) {   // eight loads in flight, added in row order
+        double v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = row_loss[r + u];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc += v[u];
+    }
+    for (; r < b1; ++r) acc += row_loss[r];
     part[threadIdx.x] = acc;
     __syncthreads();
     if (threadIdx.x == 0) {

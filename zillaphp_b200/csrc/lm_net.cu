@@ -1096,8 +1096,17 @@ __global__ void __launch_bounds__(256) lm_shadow_kernel(const float *__restrict_
 int lm_tc_shadow(const Net &n, const LmEngine &e) {
     ShadowJobs J{};
     const int nj = (int)e.shadow_src.size();
-    for (int j = 0; j < nj; ++j) { J.src[j] = e.shadow_src[j]; J.dst[j] = e.shadow_dst[j]; J.len[j] = e.shadow_len[j]; }
-    launch_pdl(lm_shadow_kernel, dim3(16, nj), dim3(256), 0, (const float *)n.params, e.tc_shadow, J);
+    long long longest = 0;
+    for (int j = 0; j < nj; ++j) {
+        J.src[j] = e.shadow_src[j]; J.dst[j] = e.shadow_dst[j]; J.len[j] = e.shadow_len[j];
+        if (J.len[j] > longest) longest = J.len[j];
+    }
+    // about two elements per thread of the longest tensor: each thread's loads are a
+    // dependent chain of latencies, so the width of the grid sets the time
+    long long bx = (longest + 511) / 512;
+    if (bx > 128) bx = 128;
+    if (bx < 1) bx = 1;
+    launch_pdl(lm_shadow_kernel, dim3((unsigned)bx, nj), dim3(256), 0, (const float *)n.params, e.tc_shadow, J);
     ZB_LAUNCH_CHECK("lm weight shadow");
     return kOk;
 }
